@@ -1,0 +1,165 @@
+"""Python binding of the B200 C ABI (include/nnb.h), loaded with ctypes.
+
+The library is the in-tree ``libnnb.so`` built by :mod:`nnb._build`. There is no fallback: if the
+library is missing, or the process has no sm_100 GPU, every call raises. Device buffers are
+``torch`` CUDA tensors (torch is used for allocation and streams only); every compute call goes
+through one ``nnb_*`` entry point of the C ABI.
+
+Errors follow the reference's conventions: a shape mismatch raises :class:`TensorShapeError`
+(nn::TensorShapeError, include/nn/tensor.hpp:70), a bad argument raises ``ValueError``
+(std::invalid_argument), and CUDA or device failures raise :class:`NnbError`.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import re
+
+_PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libnnb.so"
+HEADER = _PKG.parent.parent / "include" / "nnb.h"
+
+NNB_OK, NNB_ERR_INVALID, NNB_ERR_CUDA, NNB_ERR_UNSUPPORTED, NNB_ERR_DEVICE, NNB_ERR_SHAPE = range(6)
+MATH_FP32X3, MATH_TF32 = 0, 1
+
+
+class NnbError(RuntimeError):
+    """A CUDA, device or support failure reported by the library."""
+
+
+class TensorShapeError(ValueError):
+    """Shapes of the operands do not agree (the reference's nn::TensorShapeError)."""
+
+
+_lib = None
+
+_c = ctypes
+_sz = _c.c_size_t
+_p = _c.c_void_p
+_i = _c.c_int
+
+# argument types of every entry point, in header order
+_SIGS = {
+    "nnb_version": ([], _c.c_char_p),
+    "nnb_last_error": ([], _c.c_char_p),
+    "nnb_set_math_mode": ([_i], _i),
+    "nnb_get_math_mode": ([], _i),
+    "nnb_device_error": ([_p], _i),
+    "nnb_trace_enable": ([_i], None),
+    "nnb_trace_reset": ([], None),
+    "nnb_trace_query": ([_i, _c.POINTER(_c.c_double), _c.POINTER(_c.c_longlong)], _i),
+    "nnb_launch_count": ([], _c.c_longlong),
+    "nnb_sgemm": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i], _i),
+    "nnb_sgemm_ex": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
+    "nnb_sgemm_strided_batched": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz,
+                                   _sz, _i, _i], _i),
+}
+
+
+def header_symbols() -> list[str]:
+    """Names of every function declared in include/nnb.h."""
+    text = HEADER.read_text()
+    return re.findall(r"NNB_API\s+[\w\s\*]*?\b(nnb_\w+)\s*\(", text)
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libnnb.so once; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise NnbError(f"{LIB_PATH} is missing: build it with __graft_entry__.build()")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (args, res) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().nnb_last_error().decode()
+
+
+def check(status: int) -> None:
+    """Raises the reference-style exception for a non-OK status."""
+    if status == NNB_OK:
+        return
+    msg = last_error()
+    if status == NNB_ERR_SHAPE:
+        raise TensorShapeError(msg)
+    if status == NNB_ERR_INVALID:
+        raise ValueError(msg)
+    raise NnbError(f"status {status}: {msg}")
+
+
+def _stream_ptr(stream) -> int | None:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def _ptr(t) -> int | None:
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    return t.data_ptr()
+
+
+def set_math_mode(mode: int) -> None:
+    check(lib().nnb_set_math_mode(mode))
+
+
+def get_math_mode() -> int:
+    return lib().nnb_get_math_mode()
+
+
+def device_error(stream=None) -> int:
+    return lib().nnb_device_error(_stream_ptr(stream))
+
+
+TRACE_GEMM, TRACE_PACK, TRACE_AUX, TRACE_ROWWISE, TRACE_ATTENTION, TRACE_CONV = range(6)
+
+
+def trace_enable(on: bool = True) -> None:
+    lib().nnb_trace_enable(int(on))
+
+
+def trace_reset() -> None:
+    lib().nnb_trace_reset()
+
+
+def trace_query(kind: int) -> tuple[float, int]:
+    """(total device ms, launches) of one kernel kind since the last reset."""
+    ms, n = ctypes.c_double(), ctypes.c_longlong()
+    check(lib().nnb_trace_query(kind, ctypes.byref(ms), ctypes.byref(n)))
+    return ms.value, n.value
+
+
+def launch_count() -> int:
+    return lib().nnb_launch_count()
+
+
+def sgemm(trans_a: bool, trans_b: bool, m: int, n: int, k: int, a, lda: int, b, ldb: int, c, ldc: int,
+          accumulate: bool, math_mode: int | None = None, stream=None) -> None:
+    """nn::kernels::sgemm (include/nn/kernels/gemm.hpp:57) on device buffers through nnb_sgemm[_ex]."""
+    s = _stream_ptr(stream)
+    if math_mode is None:
+        st = lib().nnb_sgemm(s, int(trans_a), int(trans_b), m, n, k, _ptr(a), lda, _ptr(b), ldb, _ptr(c), ldc,
+                             int(accumulate))
+    else:
+        st = lib().nnb_sgemm_ex(s, int(trans_a), int(trans_b), m, n, k, _ptr(a), lda, _ptr(b), ldb, _ptr(c),
+                                ldc, int(accumulate), math_mode)
+    check(st)
+
+
+def sgemm_strided_batched(trans_a: bool, trans_b: bool, m: int, n: int, k: int, a, lda: int, stride_a: int,
+                          b, ldb: int, stride_b: int, c, ldc: int, stride_c: int, batch: int,
+                          accumulate: bool, math_mode: int = MATH_FP32X3, stream=None) -> None:
+    check(lib().nnb_sgemm_strided_batched(_stream_ptr(stream), int(trans_a), int(trans_b), m, n, k, _ptr(a), lda,
+                                          stride_a, _ptr(b), ldb, stride_b, _ptr(c), ldc, stride_c, batch,
+                                          int(accumulate), math_mode))

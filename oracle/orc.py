@@ -1,0 +1,148 @@
+"""ctypes loader for the CPU checkers. TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's cpu_baseline / reference legs import this
+module. It exposes:
+
+- :data:`orc` -- ``liborc.so``, this directory's restatement of the reference algorithms
+  (orc_gemm.c, orc_ops.c, orc_gen.cpp);
+- :func:`ref` -- ``_ref/libnnref.so``, the reference library compiled from its own sources
+  (``None`` when it was not built), through ref_shim.cpp's C-ABI.
+
+Helpers return numpy arrays; the problem builders mirror tests/test_kernels.cpp:68-86 of the
+reference.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+ORC_PATH = HERE / "liborc.so"
+REF_PATH = HERE / "_ref" / "libnnref.so"
+SENTINEL = np.float32(1e30)
+
+_c = ctypes
+_sz, _p, _i, _u32, _f, _d = _c.c_size_t, _c.c_void_p, _c.c_int, _c.c_uint32, _c.c_float, _c.c_double
+
+_ORC_SIGS = {
+    "orc_sgemm_f32": [_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i],
+    "orc_sgemm_f64": [_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _p],
+    "orc_magnitude": [_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _p],
+    "orc_sgemm_f64_sample": [_i, _i, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _p, _p, _sz, _p, _p],
+    "orc_fill_uniform": [_u32, _sz, _f, _f, _p],
+    "orc_fill_normal": [_u32, _sz, _f, _f, _p],
+    "orc_fill_int": [_u32, _sz, _c.c_int64, _c.c_int64, _p],
+    "orc_make_problem": [_i, _i, _sz, _sz, _sz, _sz, _u32, _p, _p, _p],
+}
+
+_REF_SIGS = {
+    "ref_sgemm": ([_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i], None),
+    "ref_sgemm_portable": ([_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i], None),
+    "ref_reference_sgemm": ([_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i], None),
+    "ref_sgemm_uses_avx2": ([], _i),
+    "ref_num_threads": ([], _sz),
+    "ref_set_threads": ([_sz], None),
+    "ref_matmul": ([_sz, _sz, _sz, _sz, _p, _p, _p], None),
+    "ref_time_matmul": ([_sz, _sz, _sz, _p, _p, _i], _d),
+}
+
+
+def _load(path, sigs):
+    L = ctypes.CDLL(str(path))
+    for name, spec in sigs.items():
+        fn = getattr(L, name, None)
+        if fn is None:
+            continue
+        if isinstance(spec, tuple):
+            fn.argtypes, fn.restype = spec
+        else:
+            fn.argtypes, fn.restype = spec, None
+    return L
+
+
+orc = _load(ORC_PATH, _ORC_SIGS)
+_ref = None
+
+
+def ref():
+    """The reference library built from its sources, or None if oracle/_ref was not built."""
+    global _ref
+    if _ref is None and REF_PATH.exists():
+        _ref = _load(REF_PATH, _REF_SIGS)
+    return _ref
+
+
+def ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+# ---- generators -------------------------------------------------------------------------------
+
+def uniform(seed: int, n: int, lo: float = -1.0, hi: float = 1.0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    orc.orc_fill_uniform(seed, n, lo, hi, ptr(out))
+    return out
+
+
+def normal(seed: int, n: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    orc.orc_fill_normal(seed, n, mean, std, ptr(out))
+    return out
+
+
+def integers(seed: int, n: int, lo: int, hi: int) -> np.ndarray:
+    out = np.empty(n, np.int64)
+    orc.orc_fill_int(seed, n, lo, hi, ptr(out))
+    return out
+
+
+class Problem:
+    """One GEMM problem laid out like test_kernels.cpp:68-86 (padding = 1e30f)."""
+
+    def __init__(self, ta, tb, m, n, k, pad, seed):
+        self.ta, self.tb, self.m, self.n, self.k = bool(ta), bool(tb), m, n, k
+        a_rows, a_cols = (k, m) if ta else (m, k)
+        b_rows, b_cols = (n, k) if tb else (k, n)
+        self.lda, self.ldb, self.ldc = a_cols + pad, b_cols + pad, n + pad
+        self.a = np.empty(max(a_rows * self.lda, 1), np.float32)
+        self.b = np.empty(max(b_rows * self.ldb, 1), np.float32)
+        self.c = np.empty(max(m * self.ldc, 1), np.float32)
+        orc.orc_make_problem(int(ta), int(tb), m, n, k, pad, seed, ptr(self.a), ptr(self.b), ptr(self.c))
+
+    def args(self):
+        return (int(self.ta), int(self.tb), self.m, self.n, self.k, ptr(self.a), self.lda, ptr(self.b), self.ldb)
+
+
+# ---- GEMM oracles -----------------------------------------------------------------------------
+
+def sgemm_f32(p: Problem, c: np.ndarray, accumulate: bool) -> np.ndarray:
+    """tests/reference_gemm.hpp's fp32 loop (restated in orc_gemm.c) on a copy of c."""
+    out = c.copy()
+    orc.orc_sgemm_f32(*p.args(), ptr(out), p.ldc, int(accumulate))
+    return out
+
+
+def sgemm_f64(p: Problem, c: np.ndarray, accumulate: bool) -> np.ndarray:
+    """fp64 evaluation, m x n."""
+    out = np.empty(max(p.m * p.n, 1), np.float64)
+    orc.orc_sgemm_f64(*p.args(), ptr(c), p.ldc, int(accumulate), ptr(out))
+    return out[: p.m * p.n].reshape(p.m, p.n)
+
+
+def magnitude(p: Problem, c: np.ndarray, accumulate: bool) -> np.ndarray:
+    """test_kernels.cpp:101-109 in fp64, m x n."""
+    out = np.empty(max(p.m * p.n, 1), np.float64)
+    orc.orc_magnitude(*p.args(), ptr(c), p.ldc, int(accumulate), ptr(out))
+    return out[: p.m * p.n].reshape(p.m, p.n)
+
+
+def sgemm_f64_sample(ta, tb, k, a, lda, b, ldb, c, ldc, accumulate, rows, cols):
+    rows = np.ascontiguousarray(rows, np.int64)
+    cols = np.ascontiguousarray(cols, np.int64)
+    val = np.empty(len(rows), np.float64)
+    mag = np.empty(len(rows), np.float64)
+    orc.orc_sgemm_f64_sample(int(ta), int(tb), k, ptr(a), lda, ptr(b), ldb, ptr(c) if c is not None else None,
+                             ldc, int(accumulate), ptr(rows), ptr(cols), len(rows), ptr(val), ptr(mag))
+    return val, mag

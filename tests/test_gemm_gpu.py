@@ -1,0 +1,201 @@
+"""Parity of the sm_100a GEMM (nnb_sgemm*, through the C ABI) with the fp64 oracle.
+
+Re-expresses the reference's kernel tests (tests/test_kernels.cpp) for the GPU build:
+sizes {1,7,33,257}^3 x trans flags x accumulate (:157-167), past each CPU block size
+(:169-178), zero-size dimensions (:180-201), wide leading dimensions with sentinel padding
+(:203-209), Inf/NaN propagation (:211-231) and determinism (:333-341). Tolerances:
+3xTF32 |got - want| <= max(1e-5 * sum|a*b|, 1e-6) (the reference test's own bound, tighter than
+1e-5*sqrt(K)); TF32 5e-3 * sum|a*b|.
+"""
+import itertools
+
+import numpy as np
+import pytest
+
+import nnb
+from oracle import orc
+
+pytestmark = pytest.mark.gpu
+
+SIZES = [1, 7, 33, 257]
+MODES = [(nnb.MATH_FP32X3, 1e-5), (nnb.MATH_TF32, 5e-3)]
+
+
+def run_gpu(torch, p, acc, mode, a=None, b=None, c=None):
+    dev = torch.device("cuda")
+    da = torch.from_numpy(p.a if a is None else a).to(dev)
+    db = torch.from_numpy(p.b if b is None else b).to(dev)
+    dc = torch.from_numpy((p.c if c is None else c).copy()).to(dev)
+    nnb.sgemm(p.ta, p.tb, p.m, p.n, p.k, da, p.lda, db, p.ldb, dc, p.ldc, acc, math_mode=mode)
+    out = dc.cpu().numpy()
+    assert nnb.device_error() == 0
+    return out
+
+
+def check(p, got, acc, rel):
+    want = orc.sgemm_f64(p, p.c, acc)
+    mag = orc.magnitude(p, p.c, acc)
+    full = got[: p.m * p.ldc].reshape(p.m, p.ldc) if p.m else np.zeros((0, p.ldc), np.float32)
+    # padding columns untouched, no sentinel leaked into the result
+    assert np.all(full[:, p.n:] == orc.SENTINEL)
+    g = full[:, : p.n].astype(np.float64)
+    nan_w, nan_g = np.isnan(want), np.isnan(g)
+    assert np.array_equal(nan_w, nan_g), "NaN positions differ"
+    inf = np.isinf(want) | np.isinf(g)
+    assert np.array_equal(g[inf], want[inf]), "Inf values differ"
+    fin = ~(nan_w | inf)
+    assert np.all(np.abs(g[fin]) < 1e29)
+    err = np.abs(g[fin] - want[fin])
+    bound = np.maximum(rel * mag[fin], 1e-6)
+    bad = err > bound
+    assert not bad.any(), f"{bad.sum()} elements out of tolerance; worst ratio {(err / bound).max():.3g}"
+
+
+@pytest.mark.parametrize("mode,rel", MODES)
+def test_sizes_and_flags(cuda, mode, rel):
+    seed = 4000
+    for ta, tb, acc in itertools.product((0, 1), repeat=3):
+        for m, n, k in itertools.product(SIZES, repeat=3):
+            p = orc.Problem(ta, tb, m, n, k, 0, seed)
+            seed += 1
+            check(p, run_gpu(cuda, p, acc, mode), acc, rel)
+
+
+@pytest.mark.parametrize("mode,rel", MODES)
+def test_past_block_sizes_and_wide_ld(cuda, mode, rel):
+    seed = 1000
+    cases = [(101, 7, 33), (7, 33, 261), (7, 1029, 33), (7, 1029, 261), (129, 257, 17), (300, 300, 512)]
+    for ta, tb, acc in itertools.product((0, 1), repeat=3):
+        for m, n, k in cases:
+            p = orc.Problem(ta, tb, m, n, k, 0, seed)
+            seed += 1
+            check(p, run_gpu(cuda, p, acc, mode), acc, rel)
+        p = orc.Problem(ta, tb, 7, 33, 33, 3, seed)
+        seed += 1
+        check(p, run_gpu(cuda, p, acc, mode), acc, rel)
+
+
+def test_zero_size_dimensions(cuda):
+    """test_kernels.cpp:180-201: only the m x n region is written; k == 0 stores 0 or keeps C."""
+    torch = cuda
+    for m, n, k in [(0, 5, 4), (3, 0, 4), (3, 5, 0)]:
+        for acc in (0, 1):
+            ldc = 6
+            a = torch.ones(16, device="cuda")
+            b = torch.ones(32, device="cuda")
+            c = torch.full((4 * ldc,), float(orc.SENTINEL), device="cuda")
+            cv = c.view(4, ldc)
+            cv[:m, :n] = 2.0
+            nnb.sgemm(False, False, m, n, k, a, k if k else 1, b, n if n else 1, c, ldc, acc)
+            got = c.cpu().numpy().reshape(4, ldc)
+            for i in range(4):
+                for j in range(ldc):
+                    inside = i < m and j < n
+                    want = (2.0 if acc else 0.0) if inside else orc.SENTINEL
+                    assert got[i, j] == want
+                    if inside and not acc:
+                        assert not np.signbit(got[i, j])
+
+
+@pytest.mark.parametrize("mode,rel", MODES)
+def test_inf_nan_propagate_like_reference(cuda, mode, rel):
+    seed = 3000
+    for ta, tb, acc in itertools.product((0, 1), repeat=3):
+        p = orc.Problem(ta, tb, 7, 33, 17, 0, seed)
+        seed += 1
+        p.a[2 if ta else 2 * p.lda] = np.inf
+        for j in range(p.n):
+            p.b[j * p.ldb if tb else j] = (1.0, -1.0, 0.0)[j % 3]
+        p.b[3 * p.ldb + 5 if tb else 5 * p.ldb + 3] = np.nan
+        got = run_gpu(cuda, p, acc, mode)
+        loop = orc.sgemm_f32(p, p.c, acc)
+        assert np.array_equal(np.isnan(got), np.isnan(loop))
+        inf = np.isinf(loop)
+        assert np.array_equal(got[inf], loop[inf])
+        check(p, got, acc, rel)
+
+
+def test_deterministic(cuda):
+    """test_kernels.cpp:333-341: the same call twice gives the same bytes."""
+    for acc in (0, 1):
+        for mode, _ in MODES:
+            p = orc.Problem(0, 1, 101, 75, 300, 2, 5000)
+            g1 = run_gpu(cuda, p, acc, mode)
+            g2 = run_gpu(cuda, p, acc, mode)
+            assert g1.tobytes() == g2.tobytes()
+
+
+def test_config1_matmul_512(cuda):
+    """512^3, A then B from mt19937(0) U[-1,1], against the fp64 oracle."""
+    torch = cuda
+    n = 512
+    ab = orc.uniform(0, 2 * n * n)
+    a, b = ab[: n * n], ab[n * n:]
+    c = np.zeros(n * n, np.float32)
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    dc = torch.from_numpy(c).cuda()
+    nnb.sgemm(False, False, n, n, n, da, n, db, n, dc, n, False)
+    got = dc.cpu().numpy().reshape(n, n).astype(np.float64)
+    p = orc.Problem(0, 0, 1, 1, 1, 0, 0)   # reuse the oracle entry points on explicit buffers
+    p.m = p.n = p.k = n
+    p.lda = p.ldb = p.ldc = n
+    p.a, p.b, p.c = a, b, c
+    want = orc.sgemm_f64(p, c, False)
+    mag = orc.magnitude(p, c, False)
+    assert np.all(np.abs(got - want) <= 1e-5 * mag)
+    # the north-star bound, relative error normalised by sum|a*b|
+    assert (np.abs(got - want) / mag).max() <= 1e-5 * np.sqrt(n)
+
+
+def test_strided_batched_matches_single(cuda):
+    torch = cuda
+    rng = np.random.default_rng(7)
+    for ta, tb in itertools.product((0, 1), repeat=2):
+        batch, m, n, k = 5, 70, 90, 130
+        a = rng.standard_normal((batch, k, m) if ta else (batch, m, k)).astype(np.float32)
+        b = rng.standard_normal((batch, n, k) if tb else (batch, k, n)).astype(np.float32)
+        da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        dc = torch.zeros(batch, m, n, device="cuda")
+        lda, ldb = (m if ta else k), (k if tb else n)
+        nnb.sgemm_strided_batched(ta, tb, m, n, k, da, lda, a[0].size, db, ldb, b[0].size, dc, n, m * n, batch,
+                                  False)
+        for i in range(batch):
+            one = torch.zeros(m, n, device="cuda")
+            nnb.sgemm(ta, tb, m, n, k, da[i], lda, db[i], ldb, one, n, False, math_mode=nnb.MATH_FP32X3)
+            assert torch.equal(one, dc[i])
+        # broadcast B (stride 0)
+        dc2 = torch.zeros(batch, m, n, device="cuda")
+        nnb.sgemm_strided_batched(ta, tb, m, n, k, da, lda, a[0].size, db[0], ldb, 0, dc2, n, m * n, batch, False)
+        for i in range(batch):
+            one = torch.zeros(m, n, device="cuda")
+            nnb.sgemm(ta, tb, m, n, k, da[i], lda, db[0], ldb, one, n, False, math_mode=nnb.MATH_FP32X3)
+            assert torch.equal(one, dc2[i])
+
+
+def test_large_sampled(cuda):
+    """2048^3 and a ragged 3000 x 2500 x 1800, N(0,1): sampled rows/columns against fp64."""
+    torch = cuda
+    for (m, n, k), seed in (((2048, 2048, 2048), 41), ((3000, 2500, 1800), 42)):
+        a = orc.normal(seed, m * k)
+        b = orc.normal(seed + 100, k * n)
+        da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        for mode, rel in MODES:
+            dc = torch.zeros(m * n, device="cuda")
+            nnb.sgemm(False, False, m, n, k, da, k, db, n, dc, n, False, math_mode=mode)
+            got = dc.cpu().numpy().reshape(m, n)
+            rows = np.r_[0, m - 1, np.arange(0, m, 97)].repeat(8)
+            cols = np.tile(np.r_[0, n - 1, 131, 255, 256, n // 2, n - 2, 1], len(rows) // 8)
+            val, mag = orc.sgemm_f64_sample(0, 0, k, a, k, b, n, None, n, 0, rows, cols)
+            err = np.abs(got[rows, cols] - val)
+            assert np.all(err <= rel * mag), (m, n, k, mode, (err / mag).max())
+
+
+def test_argument_errors(cuda):
+    torch = cuda
+    a = torch.zeros(64, device="cuda")
+    with pytest.raises(ValueError):
+        nnb.sgemm(False, False, 4, 4, 4, a, 3, a, 4, a, 4, False)   # lda < k
+    with pytest.raises(ValueError):
+        nnb.sgemm(False, False, 4, 4, 4, a, 4, a, 4, a, 3, False)   # ldc < n
+    with pytest.raises(ValueError):
+        nnb.sgemm(False, False, 4, 4, 4, None, 4, a, 4, a, 4, False)
