@@ -1,0 +1,407 @@
+#!/usr/bin/env python
+"""Headline benchmark: fp32-accurate (3xTF32) GEMM TFLOP/s on B200, BASELINE config 4 at 8192^3.
+
+One "step" is one M = N = K = 8192 fp32 GEMM C = A.B (A, B ~ N(0,1)) in 3xTF32 mode through the
+library's C ABI (nnb_sgemm: pack/split kernels + the tcgen05 GEMM kernel). With N GPUs
+(torchrun, one rank per GPU) the 8192 rows of A are split into N contiguous bands, every rank
+holds all of B, computes its band of C, and the bands are gathered to GPU 0 with NCCL each step
+(total work fixed: strong scaling). Inputs are 256 MiB per operand, larger than the 126 MB L2,
+so no flush is needed between steps.
+
+Keys beyond the base contract:
+  roofline      the GEMM kernel's fp32-algorithmic TFLOP/s (2*M*N*K per launch / its average
+                event-timed duration) against the 3xTF32 ceiling = measured dense bf16 peak / 2
+                (TF32 rate) / 3 (three MMAs per fp32 product);
+  cpu_baseline  the reference's own AVX2 sgemm (built from its sources into oracle/_ref) on all
+                host cores, on a 1024-row band of the same problem;
+  e2e           the same GEMM through the public API from pinned host buffers: H2D of A (band)
+                and B, the GEMM, D2H of C, every step.
+`python bench.py --impl reference` times the reference's CPU sgemm alone (see run_reference).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import pathlib
+import signal
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "nn-cpp_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "fp32-accurate GEMM TFLOP/s"
+UNIT = "TFLOP/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+CPU_SAMPLE_ROWS = 1024
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("nnb", "reference"), default="nnb")
+    ap.add_argument("--size", type=int, default=8192, help="M = N = K")
+    ap.add_argument("--mode", choices=("fp32x3", "tf32"), default="fp32x3")
+    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        d = json.loads(path.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {**FALLBACK_PEAKS, "bf16_tflops_sustained": None, "source": "fallback"}
+
+
+def load_traffic(workload: str):
+    """DRAM bytes per launch of the GEMM kernel from the committed ncu summary (or None)."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    d = json.loads(path.read_text())
+    return d.get(workload)
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 100 ms while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.2)
+        self.proc.send_signal(signal.SIGTERM)
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                rows.append({"sm": float(f[1]), "max": float(f[2]), "power": float(f[3]),
+                             "hw_slowdown": f[5], "hw_thermal_slowdown": f[6],
+                             "sw_thermal_slowdown": f[7], "sw_power_cap": f[8]})
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        peak_power = max(r["power"] for r in rows)
+        loaded = [r for r in rows if r["power"] >= 0.5 * peak_power] or rows
+        reasons = sorted({k for r in loaded for k in ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                                      "sw_power_cap") if r[k].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded), "sm_max_mhz": max(r["max"] for r in rows),
+                "reasons": reasons, "samples": len(loaded), "power_w_max": peak_power}
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU side: the reference's own sgemm (oracle/_ref) or, if that was not built, the oracle port
+# ---------------------------------------------------------------------------------------------
+
+class CpuGemm:
+    """The reference's own sgemm (oracle/_ref) on row bands of the size^3 problem.
+
+    Inputs are drawn once (mt19937 N(0,1)); a sample is one call on a `rows` x size x size band.
+    Without the reference build, the oracle's single-thread triple loop stands in ("port").
+    """
+
+    def __init__(self, size: int):
+        import numpy as np
+        from oracle import orc
+
+        self.np, self.orc, self.size = np, orc, size
+        self.ref = orc.ref()
+        self.cores = os.cpu_count() or 1
+        self.kind = "reference" if self.ref is not None else "port"
+        if self.ref is not None:
+            self.ref.ref_set_threads(self.cores)
+            self.max_rows = size
+        else:
+            self.cores = 1
+            self.max_rows = 64
+        self.b = orc.normal(2, size * size)
+        self.a = orc.normal(1, self.max_rows * size)
+        self.c = np.empty(self.max_rows * size, np.float32)
+
+    def time_band(self, rows: int, reps: int) -> float:
+        """Median seconds of one rows x size x size product."""
+        rows = max(1, min(rows, self.max_rows))
+        o, n = self.orc, self.size
+        if self.ref is not None:
+            return self.ref.ref_time_sgemm(rows, n, n, o.ptr(self.a), o.ptr(self.b), o.ptr(self.c), reps)
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            o.orc.orc_sgemm_f32(0, 0, rows, n, n, o.ptr(self.a), n, o.ptr(self.b), n, o.ptr(self.c), n, 0)
+            ts.append(time.perf_counter() - t0)
+        return statistics.median(ts)
+
+    def rows_for(self, seconds: float) -> int:
+        """Band height whose product takes about `seconds` (probed with a small band)."""
+        probe = min(64, self.max_rows)
+        t = self.time_band(probe, 1)
+        rows = int(probe * seconds / max(t, 1e-6)) // 64 * 64
+        return max(64 if self.ref is not None else 1, min(rows, self.max_rows))
+
+    def describe(self, rows: int, reps: int) -> str:
+        who = ("nn::kernels::sgemm (reference v2.0.0 built from its sources, AVX2/FMA)" if self.ref is not None
+               else "the oracle's fp32 triple loop (reference build absent)")
+        return (f"{who} on a {rows} x {self.size} x {self.size} row band of the {self.size}^3 problem, "
+                f"{self.cores} threads, median of {reps}")
+
+
+def cpu_baseline(size: int):
+    """10-30 s of reference CPU work on the host cores (rank 0, N = 1 only)."""
+    cg = CpuGemm(size)
+    rows = cg.rows_for(4.0)
+    reps = 3
+    sec = cg.time_band(rows, reps)
+    return {"value": 2.0 * rows * size * size / sec / 1e12, "unit": UNIT, "cores": cg.cores, "kind": cg.kind,
+            "sample": cg.describe(rows, reps)}
+
+
+def run_reference(args, rank: int):
+    """--impl reference: the reference's CPU sgemm on the host cores, same metric and config.
+
+    Each step is one row band of the size^3 product sized to about 0.2 s, so that
+    warmup + steps stays within about a minute. Only rank 0 runs; other ranks exit at once.
+    """
+    if rank != 0:
+        return
+    size = args.size
+    cg = CpuGemm(size)
+    rows = cg.rows_for(0.2)
+    for _ in range(args.warmup):
+        cg.time_band(rows, 1)
+    secs = [cg.time_band(rows, 1) for _ in range(args.steps)]
+    sec = statistics.median(secs)
+    value = 2.0 * rows * size * size / sec / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) from mt19937",
+        "config": {"workload": f"config 4: square fp32 GEMM M=N=K={size}, each step a {rows}-row band",
+                   "l2": "inputs larger than L2"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cg.cores, "kind": cg.kind,
+                         "sample": cg.describe(rows, args.steps)},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------------
+
+def run_nnb(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    import nnb
+
+    size = args.size
+    mode = nnb.MATH_FP32X3 if args.mode == "fp32x3" else nnb.MATH_TF32
+    if size % (128 * world) != 0:
+        raise SystemExit(f"--size {size} must split into {world} bands of whole 128-row tiles")
+    rows = size // world
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000)
+    b = torch.randn(size, size, device=dev, generator=gen)
+    gen.manual_seed(2000 + rank)
+    a = torch.randn(rows, size, device=dev, generator=gen)
+    c = torch.empty(rows, size, device=dev)
+    gathered = [torch.empty(rows, size, device=dev) for _ in range(world)] if (world > 1 and rank == 0) else None
+
+    def gemm():
+        nnb.sgemm(False, False, rows, size, size, a, size, b, size, c, size, False, math_mode=mode)
+
+    def step():
+        gemm()
+        if world > 1:
+            dist.gather(c, gathered, dst=0)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if nnb.device_error() != 0:
+        raise SystemExit("device error during warm-up")
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    nnb.trace_reset()
+    nnb.trace_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    nnb.trace_enable(False)
+    launches = nnb.launch_count()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    gemm_ms_total, gemm_launches = nnb.trace_query(nnb.TRACE_GEMM)
+    pack_ms_total, _ = nnb.trace_query(nnb.TRACE_PACK)
+    kernel_ms = gemm_ms_total / max(gemm_launches, 1)
+    stats = torch.tensor([ms, kernel_ms, pack_ms_total / args.steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms_max, kernel_ms_max, pack_ms_max = stats.tolist()
+
+    # compute-only timing (no gather): the GEMM step alone
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(min(args.steps, 50)):
+        gemm()
+    e1.record()
+    torch.cuda.synchronize()
+    comp = torch.tensor([e0.elapsed_time(e1) / min(args.steps, 50)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(comp, op=dist.ReduceOp.MAX)
+
+    # end to end through the public API from pinned host memory
+    a_h = a.cpu().pin_memory()
+    b_h = b.cpu().pin_memory()
+    c_h = torch.empty(rows, size).pin_memory()
+    e2e_steps = max(1, args.e2e_steps)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        a.copy_(a_h, non_blocking=True)
+        b.copy_(b_h, non_blocking=True)
+        gemm()
+        c_h.copy_(c, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+
+    # cuBLAS TF32 on the same operands: a measured TF32 tensor-core reference point (rank 0, N = 1)
+    cublas_tf32 = None
+    if world == 1:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        for _ in range(3):
+            torch.matmul(a, b, out=c)
+        e0.record()
+        for _ in range(20):
+            torch.matmul(a, b, out=c)
+        e1.record()
+        torch.cuda.synchronize()
+        torch.backends.cuda.matmul.allow_tf32 = False
+        cublas_tf32 = 2.0 * rows * size * size / (e0.elapsed_time(e1) / 20 * 1e-3) / 1e12
+
+    if rank != 0:
+        return
+    flops = 2.0 * size ** 3
+    value = flops / (ms_max * 1e-3) / 1e12
+    peaks = load_peaks()
+    mmas = 3 if mode == nnb.MATH_FP32X3 else 1
+    # the GEMM runs back to back for about a second under the 1 kW cap: the sustained figure applies
+    bf16_peak = peaks["bf16_tflops_sustained"] or peaks["bf16_tflops"]
+    peak_kind = "sustained" if peaks["bf16_tflops_sustained"] else "burst"
+    peak = bf16_peak / 2.0 / mmas
+    achieved = 2.0 * rows * size * size / (kernel_ms_max * 1e-3) / 1e12
+    workload = f"gemm_{size}_{args.mode}"
+    traffic = load_traffic(workload)
+    if traffic is not None:
+        traffic = traffic * (rows / size)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "tf32x3" if mode == nnb.MATH_FP32X3 else "tf32",
+        "data": "synthetic N(0,1) (torch generator, fixed seeds)",
+        "config": {"workload": f"config 4: square fp32 GEMM M=N=K={size}, {args.mode}, "
+                               f"M-row-block sharded over {world} GPU(s), C gathered to GPU 0",
+                   "parallelism": f"m-rows x{world}", "l2": "inputs larger than L2 (256 MiB per operand), no flush",
+                   "math_mode": args.mode},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
+                     "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "gemm_tc_kernel", "kernel_ms": kernel_ms_max,
+                     "peak_basis": f"{peaks['source']} dense bf16 {peak_kind} {bf16_peak} TFLOP/s / 2 (TF32 rate)"
+                                   f" / {mmas} (MMAs per fp32 product)",
+                     "frac_of_burst_peak": achieved / (peaks["bf16_tflops"] / 2.0 / mmas),
+                     "cublas_tf32_tflops": cublas_tf32},
+        "pack_ms_per_step": pack_ms_max,
+        "ms_per_step_compute_only": comp.item(),
+        "e2e": {"value": flops / (e2e.item() * 1e-3) / 1e12, "unit": UNIT,
+                "h2d_bytes_per_step": int((rows * size + size * size) * 4 * world),
+                "d2h_bytes_per_step": int(rows * size * 4 * world)},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(size)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_nnb(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -46,6 +46,7 @@ _REF_SIGS = {
     "ref_set_threads": ([_sz], None),
     "ref_matmul": ([_sz, _sz, _sz, _sz, _p, _p, _p], None),
     "ref_time_matmul": ([_sz, _sz, _sz, _p, _p, _i], _d),
+    "ref_time_sgemm": ([_sz, _sz, _sz, _p, _p, _p, _i], _d),
 }
 
 

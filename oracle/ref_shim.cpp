@@ -81,4 +81,22 @@ double ref_time_matmul(size_t m, size_t k, size_t n, const float* a, const float
 	return s.empty() ? 0.0 : s[s.size() / 2];
 }
 
+/*
+ * Median seconds of `reps` calls (after one untimed call) of nn::kernels::sgemm(false, false, m, n,
+ * k, a, k, b, n, c, n, false): the reference's lowest seam (gemm.hpp:57) on row-major operands.
+ */
+double ref_time_sgemm(size_t m, size_t n, size_t k, const float* a, const float* b, float* c, int reps) {
+	nn::kernels::sgemm(false, false, m, n, k, a, k, b, n, c, n, false);
+	std::vector<double> t;
+	for (int r = 0; r < reps; ++r) {
+		auto t0 = std::chrono::steady_clock::now();
+		nn::kernels::sgemm(false, false, m, n, k, a, k, b, n, c, n, false);
+		auto t1 = std::chrono::steady_clock::now();
+		t.push_back(std::chrono::duration<double>(t1 - t0).count());
+	}
+	for (size_t i = 1; i < t.size(); ++i)
+		for (size_t j = i; j > 0 && t[j - 1] > t[j]; --j) std::swap(t[j - 1], t[j]);
+	return t.empty() ? 0.0 : t[t.size() / 2];
+}
+
 }  // extern "C"
