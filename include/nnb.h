@@ -108,6 +108,31 @@ NNB_API nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int tran
 		size_t stride_b, float* c, size_t ldc, size_t stride_c, size_t batch, int accumulate,
 		int math_mode);
 
+/*
+ * nnb_sgemm_ex for callers that cannot allocate device memory. This entry point has no
+ * counterpart in the reference (nn-cpp has no GPU and no allocator boundary); it exists for hosts
+ * that must not enter the CUDA allocator on the call path: an application that has already handed
+ * all device memory to its own arena, a latency-critical loop where cudaMalloc's device-wide
+ * synchronisation (or a memory-pool growth) is not acceptable, or an embedding whose allocator is
+ * not ours to call. The caller still passes A, B and C; the packed operands and flags go into a
+ * fixed 32 MiB device array that every GPU loading this library holds until the process exits.
+ *
+ * - Limit: (roundup(m,128) + roundup(n,256)) * roundup(k,16) * S * 4 bytes of packed operands plus
+ *   a few KB of flags must fit in 32 MiB (S = 2 in NNB_MATH_FP32X3, 1 in NNB_MATH_TF32); e.g.
+ *   1024 x 1024 x 1024 in 3xTF32 uses 16 MiB. Larger calls return NNB_ERR_UNSUPPORTED and
+ *   enqueue nothing.
+ * - The first call on a device (with that device current) looks up the array's device address and
+ *   sets kernel attributes; make that first call before any stream capture.
+ * - All calls share the array, which keeps the last call's contents; the flags that must start at
+ *   zero are cleared on the stream by every call. Calls that overlap on the GPU race on the array:
+ *   order them (one stream, or events) yourself.
+ * - No cudaMalloc/cudaFree or other allocating routine is called. A bounded wait that expires in this
+ *   entry point's kernels is recorded in a device word of its own, not in nnb_device_error.
+ */
+NNB_API nnb_status nnb_sgemm_noalloc(void* stream, int trans_a, int trans_b, size_t m, size_t n,
+		size_t k, const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc,
+		int accumulate, int math_mode);
+
 #ifdef __cplusplus
 }
 #endif

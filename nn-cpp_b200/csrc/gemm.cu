@@ -519,3 +519,159 @@ nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int trans_b, siz
 }
 
 }  // extern "C"
+
+// =============================================================================================
+// Allocation-free GEMM entry point (nnb_sgemm_noalloc)
+//
+// Some callers of this library cannot allocate device memory on the call path: a host that has
+// already handed every byte of the GPU to its own arena, a real-time loop that must not enter the
+// driver's allocator (cudaMalloc synchronises the device and cudaMallocAsync can grow a pool at an
+// unpredictable moment), or a host whose allocator hooks are off limits. For them this entry point
+// runs the same pack and tcgen05 kernels as nnb_sgemm_ex, with the packed operands and flags in a
+// fixed, file-scope device array instead of scratch from the memory pool.
+//
+// - The array holds kNoAllocScratchBytes (32 MiB). Every GPU that loads this library keeps it
+//   until the process exits.
+// - The first call on a device, with that device current, looks up the array's device address
+//   (cudaGetSymbolAddress) and sets the kernels' shared-memory limit. Make that first call before
+//   any stream capture.
+// - All calls share the array and it keeps the last call's contents; the non-finite flags that must
+//   start at zero are cleared on the stream at every call. Calls that overlap on the GPU (different
+//   streams, or different host threads, without ordering between them) race on the array.
+// - Calls needing more scratch than the array holds are rejected with NNB_ERR_UNSUPPORTED before
+//   anything is enqueued.
+// =============================================================================================
+
+#include <mutex>
+
+namespace nnb {
+namespace gemm {
+
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ int g_noalloc_error;
+
+struct NoAllocDevice {
+	bool ready = false;
+	unsigned char* scratch = nullptr;   // device address of g_noalloc_scratch on this device
+	int* error = nullptr;               // device address of g_noalloc_error on this device
+	int sm_count = 0;
+};
+
+static NoAllocDevice g_noalloc_devices[64];
+static std::mutex g_noalloc_mutex;
+
+// Once per device, with that device current: resolve the array's device address (in host code
+// the symbol itself is only a host-side stand-in) and set the kernels' shared-memory limit.
+static nnb_status noalloc_setup(NoAllocDevice** out) {
+	int dev = 0;
+	NNB_CUDA_TRY(cudaGetDevice(&dev));
+	if (dev < 0 || dev >= 64) return fail(NNB_ERR_UNSUPPORTED, "sgemm_noalloc: device index %d out of range", dev);
+	std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+	NoAllocDevice& d = g_noalloc_devices[dev];
+	if (!d.ready) {
+		int major = 0, sms = 0;
+		NNB_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+		if (major != 10) return fail(NNB_ERR_UNSUPPORTED, "sgemm_noalloc: device %d is not sm_100", dev);
+		NNB_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+		void* scratch = nullptr;
+		void* error = nullptr;
+		cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
+		if (e != cudaSuccess) return cuda_status(e, "sgemm_noalloc: cudaGetSymbolAddress(scratch)");
+		e = cudaGetSymbolAddress(&error, g_noalloc_error);
+		if (e != cudaSuccess) return cuda_status(e, "sgemm_noalloc: cudaGetSymbolAddress(error word)");
+		NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+			Cfg<1>::kSmemBytes));
+		NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+			Cfg<0>::kSmemBytes));
+		d.scratch = static_cast<unsigned char*>(scratch);
+		d.error = static_cast<int*>(error);
+		d.sm_count = sms;
+		d.ready = true;
+	}
+	*out = &d;
+	return NNB_OK;
+}
+
+template <int kSplit>
+static nnb_status launch_noalloc(cudaStream_t s, const NoAllocDevice* dev, int ta, int tb, long long m,
+		long long n, long long k, const float* a, long long lda, const float* b, long long ldb, float* c,
+		long long ldc, int acc) {
+	constexpr int S = Cfg<kSplit>::S;
+	const long long Mp = round_up(m, kBM), Np = round_up(n, kBN), Kp = round_up(k, kBK);
+	const long long KB = Kp / kBK;
+	const long long rows_a = Mp * KB * S, rows_b = Np * KB * S;
+	const size_t bytes_a = (size_t)rows_a * kBK * 4, bytes_b = (size_t)rows_b * kBK * 4;
+	const size_t flag_ints = (size_t)(Mp + Np + 1);
+	const size_t off_b = round_up(bytes_a, 1024), off_f = off_b + round_up(bytes_b, 1024);
+	const size_t total = off_f + flag_ints * sizeof(int);
+	if (total > kNoAllocScratchBytes)
+		return fail(NNB_ERR_UNSUPPORTED,
+			"sgemm_noalloc: %lld x %lld x %lld needs %zu bytes of scratch; the static buffer holds %zu "
+			"(packed operands take (roundup(m,128) + roundup(n,256)) * roundup(k,16) * %d * 4 bytes)",
+			m, n, k, total, kNoAllocScratchBytes, S);
+	float* pa = reinterpret_cast<float*>(dev->scratch);
+	float* pb = reinterpret_cast<float*>(dev->scratch + off_b);
+	int* flags_a = reinterpret_cast<int*>(dev->scratch + off_f);
+	int* flags_b = flags_a + Mp;
+	int* any = flags_b + Np;
+
+	NNB_CUDA_TRY(cudaMemsetAsync(flags_a, 0, flag_ints * sizeof(int), s));
+	dim3 ga((unsigned)(Mp / 32), (unsigned)((Kp + 63) / 64), 1);
+	pack_kernel<kSplit><<<ga, 256, 0, s>>>(a, lda, 0, ta, (int)m, (int)k, (int)Mp, (int)KB, pa, flags_a, any);
+	dim3 gb((unsigned)(Np / 32), (unsigned)((Kp + 63) / 64), 1);
+	pack_kernel<kSplit><<<gb, 256, 0, s>>>(b, ldb, 0, !tb, (int)n, (int)k, (int)Np, (int)KB, pb, flags_b, any);
+	NNB_CUDA_TRY(cudaGetLastError());
+
+	CUtensorMap tma, tmb;
+	NNB_TRY(encode_tiled_2d(&tma, pa, kBK, (uint64_t)rows_a, kBK * 4, kBK, kPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
+	NNB_TRY(encode_tiled_2d(&tmb, pb, kBK, (uint64_t)rows_b, kBK * 4, kBK, kPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
+
+	Params p;
+	p.M = (int)m; p.N = (int)n; p.K = (int)k; p.KB = (int)KB;
+	p.tiles_m = (int)(Mp / kBM); p.tiles_n = (int)(Np / kBN); p.batch = 1;
+	p.a_batched = 0; p.b_batched = 0;
+	p.Mp = (int)Mp; p.Np = (int)Np;
+	p.C = c; p.ldc = ldc; p.stride_c = 0; p.accumulate = acc;
+	p.any_nonfinite = any; p.flags_a = flags_a; p.flags_b = flags_b;
+	p.A = a; p.lda = lda; p.stride_a = 0; p.B = b; p.ldb = ldb; p.stride_b = 0;
+	p.ta = ta; p.tb = tb; p.err = dev->error;
+	const long long tiles = (Mp / kBM) * (Np / kBN);
+	const int grid = (int)std::min<long long>(tiles, dev->sm_count);
+	gemm_tc_kernel<kSplit><<<grid, kThreads, Cfg<kSplit>::kSmemBytes, s>>>(tma, tmb, p);
+	return cuda_status(cudaGetLastError(), "sgemm_noalloc: gemm launch");
+}
+
+}  // namespace gemm
+}  // namespace nnb
+
+extern "C" nnb_status nnb_sgemm_noalloc(void* stream, int trans_a, int trans_b, size_t m, size_t n,
+		size_t k, const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc,
+		int accumulate, int math_mode) {
+	using namespace nnb;
+	using namespace nnb::gemm;
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const int ta = trans_a != 0, tb = trans_b != 0, acc = accumulate != 0;
+	if (math_mode != NNB_MATH_FP32X3 && math_mode != NNB_MATH_TF32)
+		return fail(NNB_ERR_INVALID, "sgemm_noalloc: unknown math mode %d", math_mode);
+	if (m == 0 || n == 0) return NNB_OK;
+	if (!c) return fail(NNB_ERR_INVALID, "sgemm_noalloc: C is null");
+	if (ldc < n) return fail(NNB_ERR_INVALID, "sgemm_noalloc: ldc %zu < n %zu", ldc, n);
+	const size_t lim = (size_t)1 << 30;
+	if (m > lim || n > lim || k > lim) return fail(NNB_ERR_UNSUPPORTED, "sgemm_noalloc: dimension above 2^30");
+	NoAllocDevice* dev = nullptr;
+	NNB_TRY(noalloc_setup(&dev));
+	if (k == 0) {
+		if (acc) return NNB_OK;
+		dim3 g((unsigned)std::min<size_t>((m * n + 255) / 256, 4096), 1, 1);
+		zero_fill_kernel<<<g, 256, 0, s>>>(c, (long long)ldc, 0, (int)m, (int)n);
+		return cuda_status(cudaGetLastError(), "sgemm_noalloc: zero fill launch");
+	}
+	if (!a || !b) return fail(NNB_ERR_INVALID, "sgemm_noalloc: A or B is null");
+	if (lda < (ta ? m : k)) return fail(NNB_ERR_INVALID, "sgemm_noalloc: lda %zu too small", lda);
+	if (ldb < (tb ? k : n)) return fail(NNB_ERR_INVALID, "sgemm_noalloc: ldb %zu too small", ldb);
+	if (math_mode == NNB_MATH_FP32X3)
+		return launch_noalloc<1>(s, dev, ta, tb, m, n, k, a, lda, b, ldb, c, ldc, acc);
+	return launch_noalloc<0>(s, dev, ta, tb, m, n, k, a, lda, b, ldb, c, ldc, acc);
+}

@@ -53,6 +53,7 @@ _SIGS = {
     "nnb_sgemm_ex": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
     "nnb_sgemm_strided_batched": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz,
                                    _sz, _i, _i], _i),
+    "nnb_sgemm_noalloc": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
 }
 
 
