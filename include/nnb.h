@@ -108,6 +108,118 @@ NNB_API nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int tran
 		size_t stride_b, float* c, size_t ldc, size_t stride_c, size_t batch, int accumulate,
 		int math_mode);
 
+/* ---- linear (replaces Value linear, include/nn/autograd/ops.hpp:304; src/autograd/ops.cpp:714-745)
+ *
+ * "first" flags follow Value::grad_accum (src/autograd/value.cpp:60-64): 1 stores the value (+0),
+ * 0 adds it to what the buffer holds. A NULL gradient output is skipped.
+ */
+
+/* y[M, n] = x[M, K] · w[n, K]^T + bias[n] (bias added in the GEMM epilogue). */
+NNB_API nnb_status nnb_linear_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
+		const float* bias, float* y);
+/* dx (+)= g·w, dw (+)= g^T·x, db (+)= column sums of g (fixed chunked order: serial within 256-row
+ * chunks, then over chunks; the reference's serial order whenever M <= 256). */
+NNB_API nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const float* g, const float* x,
+		const float* w, float* dx, int dx_first, float* dw, int dw_first, float* db, int db_first);
+/* out[j] (+)= sum_r g[r][j] in the order above (Tensor::sum(0), src/tensor.cpp:422-455). */
+NNB_API nnb_status nnb_column_sum(void* stream, size_t rows, size_t cols, const float* g, float* out, int first);
+
+/* ---- normalisation ------------------------------------------------------------------------ */
+
+/* layernorm over the last axis (ops.hpp:130; ops.cpp:1003-1032): x is R rows of D; mean and
+ * inv_std (R each) are saved for the backward pass. */
+NNB_API nnb_status nnb_layernorm_fwd(void* stream, size_t R, size_t D, const float* x, const float* gamma,
+		const float* beta, float eps, float* y, float* mean, float* inv_std);
+/* layernorm backward (ops.cpp:1033-1076). */
+NNB_API nnb_status nnb_layernorm_bwd(void* stream, size_t R, size_t D, const float* g, const float* x,
+		const float* gamma, const float* mean, const float* inv_std, float* dx, int dx_first, float* dgamma,
+		int dgamma_first, float* dbeta, int dbeta_first);
+/* Training-mode batchnorm over [N, C, S] (ops.hpp:114; ops.cpp:900-961): per-channel statistics with
+ * the reference's fp64 sums of 8-lane partials; fuse_relu folds a ReLU and writes its 1-byte alive
+ * mask; mean, var (biased) and inv_std (C each) are written. */
+NNB_API nnb_status nnb_batchnorm_fwd(void* stream, size_t N, size_t C, size_t S, const float* x,
+		const float* weight, const float* bias, float eps, int fuse_relu, float* y, unsigned char* alive,
+		float* mean, float* var, float* inv_std);
+/* batchnorm backward (ops.cpp:963-1000); alive = the forward's mask when the ReLU was folded, else NULL. */
+NNB_API nnb_status nnb_batchnorm_bwd(void* stream, size_t N, size_t C, size_t S, const float* g, const float* x,
+		const float* weight, const float* mean, const float* inv_std, const unsigned char* alive, float* dx,
+		int dx_first, float* dweight, int dweight_first, float* dbias, int dbias_first);
+
+/* ---- attention (replaces Value attention, ops.hpp:324; ops.cpp:1183-1296) ------------------ */
+
+/* q [N, Tq, D], k/v [N, Tk, D], heads | D; key_padding_mask [N, Tk] (0 = padded) or NULL;
+ * causal needs Tq == Tk. out [N, Tq, D]; probs [N, heads, Tq, Tk] is kept for the backward pass. */
+NNB_API nnb_status nnb_attention_fwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* q, const float* k, const float* v, const float* key_padding_mask, int causal, float* out,
+		float* probs);
+NNB_API nnb_status nnb_attention_bwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* g, const float* q, const float* k, const float* v, const float* probs,
+		const float* key_padding_mask, int causal, float* dq, int dq_first, float* dk, int dk_first, float* dv,
+		int dv_first);
+/* masked_softmax_row over [N, H, Tq, Tk] scores in place (ops.cpp:1183-1204), and its backward
+ * turning dL/dP into dL/dS in place (ops.cpp:1216-1224). */
+NNB_API nnb_status nnb_masked_softmax_fwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk, float* scores,
+		const float* key_padding_mask, int causal, float scale);
+NNB_API nnb_status nnb_masked_softmax_bwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk,
+		const float* probs, float* grad, const float* key_padding_mask, int causal, float scale);
+
+/* ---- convolution (replaces conv2d / conv2d_relu, ops.hpp:402; ops.cpp:1345-1472) ------------ */
+
+/* x [N, Cin, H, W], weight [Cout, Cin, kh, kw], bias [Cout] -> y [N, Cout, ho, wo];
+ * fuse_relu = conv2d_relu with its 1-byte alive mask (same layout as y). */
+NNB_API nnb_status nnb_conv2d_fwd(void* stream, size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh,
+		size_t kw, int stride, int padding, const float* x, const float* weight, const float* bias, int fuse_relu,
+		float* y, unsigned char* alive);
+NNB_API nnb_status nnb_conv2d_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh,
+		size_t kw, int stride, int padding, const float* grad, const float* x, const float* weight,
+		const unsigned char* alive, float* dx, int dx_first, float* dweight, int dweight_first, float* dbias,
+		int dbias_first);
+
+/* ---- support ops on the configs' paths ----------------------------------------------------- */
+
+/* relu (ops.cpp:775-793) */
+NNB_API nnb_status nnb_relu_fwd(void* stream, size_t n, const float* x, float* y);
+NNB_API nnb_status nnb_relu_bwd(void* stream, size_t n, const float* x, const float* g, float* dx, int dx_first);
+/* tanh-GELU (ops.cpp:451-481, kernels::tanh_inplace src/kernels/vmath.cpp:117): tanh_saved gets the
+ * tanh for the backward pass; the backward recomputes it when tanh_saved is NULL. */
+NNB_API nnb_status nnb_gelu_fwd(void* stream, size_t n, const float* x, float* y, float* tanh_saved);
+NNB_API nnb_status nnb_gelu_bwd(void* stream, size_t n, const float* x, const float* tanh_saved, const float* g,
+		float* dx, int dx_first);
+/* y = a + b, b repeated every b_period elements (add with a broadcast leading axis, ops.cpp:331). */
+NNB_API nnb_status nnb_add_fwd(void* stream, size_t n, const float* a, const float* b, size_t b_period, float* y);
+/* dst (+)= src or (-)= src with the grad_accum convention (ops.cpp:77-92, add_to_grad). */
+NNB_API nnb_status nnb_accumulate(void* stream, size_t n, const float* src, float* dst, int first, int negate);
+/* maxpool2d (ops.cpp:1609-1705): argmax = offset inside the plane, first maximum wins. */
+NNB_API nnb_status nnb_maxpool2d_fwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel,
+		size_t stride, const float* x, float* y, uint32_t* argmax);
+NNB_API nnb_status nnb_maxpool2d_bwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel,
+		size_t stride, const float* g, const uint32_t* argmax, float* dx, int dx_first);
+/* cross_entropy_loss (ops.cpp:1774-1840) over logits [N, C], targets (device int64) [N]; loss and
+ * norm are device scalars (norm = N, the divisor of the backward scale). An out-of-range target
+ * makes the loss NaN and sets the device error word (the reference throws TensorIndexError). */
+NNB_API nnb_status nnb_cross_entropy_fwd(void* stream, size_t N, size_t C, const float* logits,
+		const int64_t* targets, float* softmax, float* loss, float* norm);
+NNB_API nnb_status nnb_cross_entropy_bwd(void* stream, size_t N, size_t C, const float* softmax,
+		const int64_t* targets, const float* grad_loss, const float* norm, float* dlogits, int first);
+/* sequence_cross_entropy (ops.cpp:1908-1979) over P positions of V logits with ignore_index and
+ * label smoothing; norm = 1/count of non-ignored positions (device scalar). */
+NNB_API nnb_status nnb_sequence_ce_fwd(void* stream, size_t P, size_t V, const float* logits,
+		const int64_t* targets, int64_t ignore_index, float label_smoothing, float* softmax, float* loss,
+		float* norm);
+NNB_API nnb_status nnb_sequence_ce_bwd(void* stream, size_t P, size_t V, const float* softmax,
+		const int64_t* targets, int64_t ignore_index, float label_smoothing, const float* grad_loss,
+		const float* norm, float* dlogits, int first);
+/* embedding (ops.cpp:1991-2015): out[i] = weight[ids[i]]; backward adds g rows into dweight in
+ * token order per row (deterministic, no float atomics); V <= 40000 for the backward. */
+NNB_API nnb_status nnb_embedding_fwd(void* stream, size_t V, size_t D, const float* weight, const int64_t* ids,
+		size_t count, float* out);
+NNB_API nnb_status nnb_embedding_bwd(void* stream, size_t V, size_t D, const int64_t* ids, size_t count,
+		const float* g, float* dweight);
+/* One AdamW step on one parameter (src/optim/adamw.cpp:15-24 then src/optim/adam.cpp:24-43);
+ * step counts from 1 (the value of Adam::t_ after its increment). */
+NNB_API nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float* g, float* m, float* v, float lr,
+		float beta1, float beta2, float eps, float weight_decay, long long step);
+
 /*
  * nnb_sgemm_ex for callers that cannot allocate device memory. This entry point has no
  * counterpart in the reference (nn-cpp has no GPU and no allocator boundary); it exists for hosts

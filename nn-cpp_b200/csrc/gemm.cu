@@ -3,23 +3,27 @@
 //
 // Pack (the counterpart of pack_a / pack_b, src/kernels/gemm.cpp:79,126): op(A) and op(B)^T are
 // rewritten, whatever their transpose flag and leading dimension, into K-major "panels" of
-// 128 rows x 16 floats (8 KB, contiguous), zero-padded to whole panels. In 3xTF32 mode each
-// value x is stored twice, as hi = tf32(x) and lo = tf32(x - hi) (the split-precision method of
+// 128 (or 64) rows x 16 floats, contiguous, zero-padded to whole panels. In 3xTF32 mode each value
+// x is stored twice, as hi = tf32(x) and lo = tf32(x - hi) (the split-precision method of
 // Ootomo & Yokota, 2022), so C = Ahi*Bhi + Ahi*Blo + Alo*Bhi carries about 21 mantissa bits.
 // Rows holding Inf or NaN are flagged; the epilogue recomputes the IEEE result of those
 // elements (+-Inf or NaN) so non-finite inputs propagate exactly as the reference's fp32 loop.
 //
 // Main kernel, one CTA per SM, 6 warps:
 //   warp 0     TMA producer: each stage = the A panels (hi[,lo]) of a 128-row tile and the B
-//              panels of a 256-column tile for one 16-wide k-block, 64-byte swizzled;
-//   warp 1     MMA issuer: tcgen05.mma.kind::tf32 128x256x8 into a TMEM accumulator, two
-//              accumulators (512 TMEM columns) so the epilogue of tile i overlaps tile i+1;
-//   warps 2-5  epilogue: tcgen05.ld -> (C +) acc -> global, with bounds checks.
+//              panels of a BN-column tile (BN = 64, 128 or 256) for one 16-wide k-block,
+//              64-byte swizzled;
+//   warp 1     MMA issuer: tcgen05.mma.kind::tf32 128xBNx8 into a TMEM accumulator, two
+//              accumulators so the epilogue of tile i overlaps tile i+1;
+//   warps 2-5  epilogue: tcgen05.ld -> (+bias, ReLU/GELU) -> (C +) -> global, bounds-checked.
 // There is no split-K and the k order is fixed, so every element of C is produced by the same
 // sequence of operations whatever the grid size, the number of GPUs or the M-shard it sits in.
 #include <algorithm>
+#include <mutex>
 
+#include "nnb_gemm.h"
 #include "nnb_internal.h"
+#include "nnb_math.cuh"
 #include "nnb_ptx.cuh"
 #include "nnb_trace.h"
 
@@ -27,40 +31,52 @@ namespace nnb {
 namespace gemm {
 
 constexpr int kBM = 128;                 // rows of C per tile (MMA M)
-constexpr int kBN = 256;                 // columns of C per tile (MMA N)
 constexpr int kBK = 16;                  // floats of depth per pipeline stage (one 64 B row)
-constexpr int kPanelRows = 128;          // rows per packed panel
-constexpr int kPanelFloats = kPanelRows * kBK;
-constexpr int kPanelBytes = kPanelFloats * 4;   // 8 KB
+constexpr int kAPanelRows = 128;         // rows per packed panel of A
 constexpr int kGroupM = 16;              // tiles of M walked together for L2 reuse of B
 constexpr int kThreads = 192;
+constexpr int kSmemBudget = 200 * 1024;  // dynamic shared memory for the stage ring
 
-template <int kSplit>
+__host__ __device__ constexpr int b_panel_rows(int bn) { return bn < 128 ? bn : 128; }
+
+template <int kSplit, int kBN>
 struct Cfg {
 	static constexpr int S = kSplit ? 2 : 1;                 // hi[, lo]
-	static constexpr int kABytes = S * kBM * kBK * 4;        // 16 KB / 8 KB
-	static constexpr int kBBytes = S * kBN * kBK * 4;        // 32 KB / 16 KB
+	static constexpr int kABytes = S * kBM * kBK * 4;
+	static constexpr int kBPartBytes = kBN * kBK * 4;        // one part (hi or lo) of the B tile
+	static constexpr int kBBytes = S * kBPartBytes;
 	static constexpr int kStageBytes = kABytes + kBBytes;
-	static constexpr int kStages = kSplit ? 4 : 8;
+	static constexpr int kStagesRaw = kSmemBudget / kStageBytes;
+	static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
 	static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+	static constexpr int kTmemCols = 2 * kBN;                // two accumulators
+	static constexpr int kBPanelRows = b_panel_rows(kBN);
+	static constexpr int kBPanels = kBN / kBPanelRows;
 };
 
 struct Params {
 	int M, N, K, KB;
-	int tiles_m, tiles_n, batch;
+	int tiles_m, tiles_n;
+	int batch, batch_inner;
 	int a_batched, b_batched;        // 0: operand shared by every batch entry
 	int Mp, Np;                      // padded row counts of the packed operands
 	float* C;
-	long long ldc, stride_c;
+	long long ldc, sc_outer, sc_inner;
 	int accumulate;
-	// Exact IEEE handling of non-finite inputs
+	// epilogue
+	const float* bias;
+	int bias_mode, act;
+	unsigned char* mask;
+	float* pre;
+	long long ld_aux, s_aux_outer, s_aux_inner;
+	// exact IEEE handling of non-finite inputs
 	const int* any_nonfinite;
 	const int* flags_a;              // [a_batches][Mp]
 	const int* flags_b;              // [b_batches][Np]
 	const float* A;
-	long long lda, stride_a;
+	long long lda, sa_outer, sa_inner;
 	const float* B;
-	long long ldb, stride_b;
+	long long ldb, sb_outer, sb_inner;
 	int ta, tb;
 	int* err;
 };
@@ -83,16 +99,17 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 }
 
 // One block: 32 rows x 64 depth of op(X) (X stored rows x K, or K x rows when trans), written
-// as 4 k-blocks of the packed panel layout. grid = (Rp/32, ceil(Kp/64), batches).
+// as 4 k-blocks of the packed panel layout with `panel_rows`-row panels.
+// grid = (Rp/32, ceil(Kp/64), batch entries); entry e reads X + (e / inner)*s_outer + (e % inner)*s_inner.
 template <int kSplit>
 __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, long long ldx,
-		long long stride_x, int trans, int R, int K, int Rp, int KB, float* __restrict__ out,
-		int* __restrict__ flags, int* __restrict__ any_flag) {
+		long long s_outer, long long s_inner, int inner, int trans, int R, int K, int Rp, int KB,
+		int panel_rows, float* __restrict__ out, int* __restrict__ flags, int* __restrict__ any_flag) {
 	constexpr int S = kSplit ? 2 : 1;
 	__shared__ float tile[32][65];
 	const int t = threadIdx.x;
-	const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 64, bi = blockIdx.z;
-	const float* Xb = X + (long long)bi * stride_x;
+	const int r0 = blockIdx.x * 32, k0 = blockIdx.y * 64, e = blockIdx.z;
+	const float* Xb = X + (long long)(e / inner) * s_outer + (long long)(e % inner) * s_inner;
 	if (!trans) {
 		const int kk = t & 63, rr = t >> 6;
 #pragma unroll
@@ -109,15 +126,16 @@ __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, 
 		}
 	}
 	__syncthreads();
-	const int e = 2 * t;                 // element pair inside a 32 x 16 k-block slab
-	const int rl = e >> 4, kl = e & 15;
-	const long long batch_off = (long long)bi * Rp * KB * 16 * S;
+	const int q = 2 * t;                 // element pair inside a 32 x 16 k-block slab
+	const int rl = q >> 4, kl = q & 15;
+	const long long batch_off = (long long)e * Rp * KB * 16 * S;
+	const int panel_floats = panel_rows * 16;
 	bool bad = false;
 #pragma unroll
 	for (int w = 0; w < 4; ++w) {
 		const int kb = (k0 >> 4) + w;
 		if (kb >= KB) break;
-		float x0 = tile[rl][w * 16 + kl], x1 = tile[rl][w * 16 + kl + 1];
+		const float x0 = tile[rl][w * 16 + kl], x1 = tile[rl][w * 16 + kl + 1];
 		const bool f0 = isfinite(x0), f1 = isfinite(x1);
 		bad |= !(f0 && f1);
 		float h0, l0, h1, l1;
@@ -129,13 +147,13 @@ __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, 
 			h1 = to_tf32(f1 ? x1 : 0.0f);
 			l0 = l1 = 0.0f;
 		}
-		const long long panel = ((long long)(r0 / kPanelRows) * KB + kb) * S;
-		float* dst = out + batch_off + panel * kPanelFloats + (r0 % kPanelRows) * 16 + e;
+		const long long panel = ((long long)(r0 / panel_rows) * KB + kb) * S;
+		float* dst = out + batch_off + panel * panel_floats + (r0 % panel_rows) * 16 + q;
 		*reinterpret_cast<float2*>(dst) = make_float2(h0, h1);
-		if (kSplit) *reinterpret_cast<float2*>(dst + kPanelFloats) = make_float2(l0, l1);
+		if (kSplit) *reinterpret_cast<float2*>(dst + panel_floats) = make_float2(l0, l1);
 	}
 	if (bad) {
-		atomicOr(flags + (long long)bi * Rp + r0 + rl, 1);
+		atomicOr(flags + (long long)e * Rp + r0 + rl, 1);
 		atomicOr(any_flag, 1);
 	}
 }
@@ -156,11 +174,15 @@ __device__ __forceinline__ void tile_coords(int t, const Params& p, int& bi, int
 	nt = in / gsz;
 }
 
+__device__ __forceinline__ long long batch_offset(int bi, int inner, long long s_outer, long long s_inner) {
+	return (long long)(bi / inner) * s_outer + (long long)(bi % inner) * s_inner;
+}
+
 // IEEE value of sum_p op(A)(i,p)*op(B)(p,j) for an element whose row or column holds Inf/NaN:
 // NaN if any product is NaN or both infinities occur, else the infinity that occurs.
 __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, int j, float v) {
-	const float* A = p.A + (p.a_batched ? (long long)bi * p.stride_a : 0);
-	const float* B = p.B + (p.b_batched ? (long long)bi * p.stride_b : 0);
+	const float* A = p.A + batch_offset(bi, p.batch_inner, p.sa_outer, p.sa_inner);
+	const float* B = p.B + batch_offset(bi, p.batch_inner, p.sb_outer, p.sb_inner);
 	bool nan = false, pinf = false, ninf = false;
 	for (int q = 0; q < p.K; ++q) {
 		const float a = p.ta ? A[(long long)q * p.lda + i] : A[(long long)i * p.lda + q];
@@ -175,10 +197,10 @@ __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, i
 	return v;
 }
 
-template <int kSplit>
+template <int kSplit, int kBN>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
 		const __grid_constant__ CUtensorMap tm_b, const Params p) {
-	using C = Cfg<kSplit>;
+	using C = Cfg<kSplit, kBN>;
 	constexpr int S = C::S;
 	constexpr int kStages = C::kStages;
 	extern __shared__ uint8_t smem_raw[];
@@ -203,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 		tma_prefetch_desc(&tm_b);
 	}
 	if (warp == 1) {
-		tmem_alloc(smem_u32(&tmem_base_sh), 512);
+		tmem_alloc(smem_u32(&tmem_base_sh), C::kTmemCols);
 		tmem_relinquish();
 	}
 	tc_fence_before();
@@ -213,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 	volatile int* abort_flag = &abort_sh;
 
 	const int num_tiles = p.batch * p.tiles_m * p.tiles_n;
-	const int a_panels = p.Mp / kPanelRows, b_panels = p.Np / kPanelRows;
+	const int a_panels = p.Mp / kAPanelRows, b_panels = p.Np / C::kBPanelRows;
 
 	if (warp == 0) {
 		if (lane == 0) {
@@ -233,16 +255,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 					const uint32_t fb = smem_u32(&full_bar[stage]);
 					mbar_arrive_expect_tx(fb, C::kStageBytes);
 					const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
-					const int ya = (int)((((long long)ab * a_panels + mt) * p.KB + kb) * S * kPanelRows);
+					const int ya = (int)((((long long)ab * a_panels + mt) * p.KB + kb) * S * kAPanelRows);
 #pragma unroll
-					for (int s = 0; s < S; ++s) tma_load_2d(base + s * kPanelBytes, &tm_a, fb, 0, ya + s * kPanelRows);
+					for (int s = 0; s < S; ++s)
+						tma_load_2d(base + s * (kAPanelRows * kBK * 4), &tm_a, fb, 0, ya + s * kAPanelRows);
 #pragma unroll
-					for (int q = 0; q < 2; ++q) {
-						const int yb = (int)((((long long)bb * b_panels + 2 * nt + q) * p.KB + kb) * S * kPanelRows);
+					for (int q = 0; q < C::kBPanels; ++q) {
+						const long long panel = (long long)bb * b_panels + (long long)nt * C::kBPanels + q;
+						const int yb = (int)((panel * p.KB + kb) * S * C::kBPanelRows);
 #pragma unroll
 						for (int s = 0; s < S; ++s)
-							tma_load_2d(base + C::kABytes + s * (kBN * kBK * 4) + q * kPanelBytes, &tm_b, fb, 0,
-								yb + s * kPanelRows);
+							tma_load_2d(base + C::kABytes + s * C::kBPartBytes + q * (C::kBPanelRows * kBK * 4), &tm_b,
+								fb, 0, yb + s * C::kBPanelRows);
 					}
 					if (++stage == kStages) {
 						stage = 0;
@@ -280,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 						const uint64_t b_hi = smem_desc_k_sw64(base + C::kABytes + off);
 						const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
 						if (kSplit) {
-							const uint64_t a_lo = smem_desc_k_sw64(base + kPanelBytes + off);
-							const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + kBN * kBK * 4 + off);
+							const uint64_t a_lo = smem_desc_k_sw64(base + kAPanelRows * kBK * 4 + off);
+							const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
 							mma_tf32(d_tmem, a_lo, b_hi, idesc, first);
 							mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
 							mma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
@@ -303,7 +327,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 		// ---------------------------------- epilogue ----------------------------------
 		const int quad = warp & 3;                 // TMEM lanes this warp may access
 		const int row = quad * 32 + lane;
-		const bool vec_ok = (p.ldc % 4 == 0) && (p.stride_c % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+		const bool vec_ok = p.act == kActNone && (p.ldc % 4 == 0) && (p.sc_outer % 4 == 0) &&
+			(p.sc_inner % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
 		int it = 0;
 		for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
 			const int buf = it & 1;
@@ -314,10 +339,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 			tile_coords(t, p, bi, mt, nt);
 			const int gm = mt * kBM + row;
 			const bool row_ok = gm < p.M;
-			float* crow = p.C + (long long)bi * p.stride_c + (long long)gm * p.ldc;
+			float* crow = p.C + batch_offset(bi, p.batch_inner, p.sc_outer, p.sc_inner) + (long long)gm * p.ldc;
+			const long long aux_row = batch_offset(bi, p.batch_inner, p.s_aux_outer, p.s_aux_inner) + (long long)gm * p.ld_aux;
 			const bool fix = *p.any_nonfinite != 0;
 			const bool row_bad = fix && row_ok && p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0;
 			const int* fcol = p.flags_b + (long long)(p.b_batched ? bi : 0) * p.Np;
+			const float row_bias = (p.bias_mode == kBiasRow && row_ok) ? p.bias[gm] : 0.0f;
 #pragma unroll 1
 			for (int ch = 0; ch < kBN / 32; ++ch) {
 				const int gn0 = nt * kBN + ch * 32;
@@ -336,6 +363,34 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 						if (gn < p.N && (row_bad || fcol[gn] != 0)) v[j] = nonfinite_result(p, bi, gm, gn, v[j]);
 					}
 				}
+#pragma unroll
+				for (int j = 0; j < 32; ++j) v[j] = v[j] + 0.0f;
+				if (p.bias_mode == kBiasRow) {
+#pragma unroll
+					for (int j = 0; j < 32; ++j) v[j] = v[j] + row_bias;
+				} else if (p.bias_mode == kBiasCol) {
+#pragma unroll
+					for (int j = 0; j < 32; ++j) {
+						const int gn = gn0 + j;
+						v[j] = v[j] + (gn < p.N ? __ldg(p.bias + gn) : 0.0f);
+					}
+				}
+				if (p.act == kActRelu) {
+#pragma unroll
+					for (int j = 0; j < 32; ++j) {
+						const int gn = gn0 + j;
+						const bool alive = v[j] > 0.0f;
+						v[j] = alive ? v[j] : 0.0f;
+						if (gn < p.N) p.mask[aux_row + gn] = alive ? 1 : 0;
+					}
+				} else if (p.act == kActGelu) {
+#pragma unroll
+					for (int j = 0; j < 32; ++j) {
+						const int gn = gn0 + j;
+						if (gn < p.N) p.pre[aux_row + gn] = v[j];
+						v[j] = gelu_fwd(v[j], tanh_one(gelu_tanh_arg(v[j])));
+					}
+				}
 				if (vec_ok && gn0 + 32 <= p.N) {
 					float4* c4 = reinterpret_cast<float4*>(crow + gn0);
 #pragma unroll
@@ -344,8 +399,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 						if (p.accumulate) {
 							const float4 c = c4[j];
 							o.x = c.x + o.x; o.y = c.y + o.y; o.z = c.z + o.z; o.w = c.w + o.w;
-						} else {
-							o.x += 0.0f; o.y += 0.0f; o.z += 0.0f; o.w += 0.0f;
 						}
 						c4[j] = o;
 					}
@@ -353,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {
 						const int gn = gn0 + j;
-						if (gn < p.N) crow[gn] = p.accumulate ? crow[gn] + v[j] : v[j] + 0.0f;
+						if (gn < p.N) crow[gn] = p.accumulate ? crow[gn] + v[j] : v[j];
 					}
 				}
 			}
@@ -368,13 +421,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 	if (warp == 1) {
 		__syncwarp();
 		tc_fence_after();
-		tmem_dealloc(tmem_base, 512);
+		tmem_dealloc(tmem_base, C::kTmemCols);
 	}
 }
 
 // Zero fill of an m x n region per batch entry: the k == 0 product (gemm.cpp:346-348).
-__global__ void zero_fill_kernel(float* c, long long ldc, long long stride_c, int m, int n) {
-	float* cb = c + (long long)blockIdx.z * stride_c;
+__global__ void zero_fill_kernel(float* c, long long ldc, long long s_outer, long long s_inner, int inner,
+		int m, int n) {
+	float* cb = c + (long long)(blockIdx.z / inner) * s_outer + (long long)(blockIdx.z % inner) * s_inner;
 	for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < (long long)m * n;
 			idx += (long long)gridDim.x * blockDim.x) {
 		const long long i = idx / n, j = idx - i * n;
@@ -382,130 +436,199 @@ __global__ void zero_fill_kernel(float* c, long long ldc, long long stride_c, in
 	}
 }
 
+// ---------------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------------
+
 inline long long round_up(long long x, long long a) { return (x + a - 1) / a * a; }
 
+// Column tile: the widest of 256 / 128 / 64 whose padding waste is within 12.5 % of the least.
+static int choose_bn(long long n) {
+	const long long best = std::min({round_up(n, 256), round_up(n, 128), round_up(n, 64)});
+	for (int bn : {256, 128, 64})
+		if (round_up(n, bn) * 8 <= best * 9) return bn;
+	return 64;
+}
+
+static bool g_attr_set[64][2][3];
+static std::mutex g_attr_mutex;
+
+template <int kSplit, int kBN>
+static nnb_status set_smem_attr(int dev) {
+	const int bi = kBN == 64 ? 0 : kBN == 128 ? 1 : 2;
+	std::lock_guard<std::mutex> lock(g_attr_mutex);
+	if (g_attr_set[dev & 63][kSplit][bi]) return NNB_OK;
+	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+		Cfg<kSplit, kBN>::kSmemBytes));
+	g_attr_set[dev & 63][kSplit][bi] = true;
+	return NNB_OK;
+}
+
+// Scratch layout of one product: packed A, packed B, then the non-finite flags.
+struct Plan {
+	int S, bn, b_panel_rows;
+	long long Mp, Np, Kp, KB, entries, a_entries, b_entries;
+	long long rows_a, rows_b;                 // packed 16-float rows of each operand
+	size_t off_b, off_f, flag_ints, total;
+};
+
+static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0) {
+	pl.S = d.mode == NNB_MATH_FP32X3 ? 2 : 1;
+	pl.bn = force_bn ? force_bn : choose_bn(d.n);
+	pl.b_panel_rows = b_panel_rows(pl.bn);
+	pl.Mp = round_up(d.m, kBM);
+	pl.Np = round_up(d.n, pl.bn);
+	pl.Kp = round_up(d.k, kBK);
+	pl.KB = pl.Kp / kBK;
+	pl.entries = d.batch_outer * d.batch_inner;
+	pl.a_entries = (d.sa_outer || d.sa_inner) ? pl.entries : 1;
+	pl.b_entries = (d.sb_outer || d.sb_inner) ? pl.entries : 1;
+	pl.rows_a = pl.a_entries * pl.Mp * pl.KB * pl.S;
+	pl.rows_b = pl.b_entries * pl.Np * pl.KB * pl.S;
+	if (pl.rows_a > INT32_MAX || pl.rows_b > INT32_MAX)
+		return fail(NNB_ERR_UNSUPPORTED, "gemm: operands too large for one launch (packed rows %lld, %lld)",
+			pl.rows_a, pl.rows_b);
+	if (pl.entries > 65535) return fail(NNB_ERR_UNSUPPORTED, "gemm: more than 65535 batch entries");
+	if (pl.entries * (pl.Mp / kBM) * (pl.Np / pl.bn) > INT32_MAX) return fail(NNB_ERR_UNSUPPORTED, "gemm: too many tiles");
+	const size_t bytes_a = (size_t)pl.rows_a * kBK * 4, bytes_b = (size_t)pl.rows_b * kBK * 4;
+	pl.flag_ints = (size_t)(pl.a_entries * pl.Mp + pl.b_entries * pl.Np + 1);
+	pl.off_b = round_up(bytes_a, 1024);
+	pl.off_f = pl.off_b + round_up(bytes_b, 1024);
+	pl.total = pl.off_f + pl.flag_ints * sizeof(int);
+	return NNB_OK;
+}
+
+template <int kSplit, int kBN>
+static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
+		unsigned char* ws, bool traced) {
+	using Cf = Cfg<kSplit, kBN>;
+	float* pa = reinterpret_cast<float*>(ws);
+	float* pb = reinterpret_cast<float*>(ws + pl.off_b);
+	int* flags_a = reinterpret_cast<int*>(ws + pl.off_f);
+	int* flags_b = flags_a + pl.a_entries * pl.Mp;
+	int* any = flags_b + pl.b_entries * pl.Np;
+	const int inner = (int)d.batch_inner;
+
+	NNB_CUDA_TRY(cudaMemsetAsync(flags_a, 0, pl.flag_ints * sizeof(int), s));
+	dim3 ga((unsigned)(pl.Mp / 32), (unsigned)((pl.Kp + 63) / 64), (unsigned)pl.a_entries);
+	dim3 gb((unsigned)(pl.Np / 32), (unsigned)((pl.Kp + 63) / 64), (unsigned)pl.b_entries);
+	{
+		TraceScope ts(s, kTracePack, traced);
+		pack_kernel<kSplit><<<ga, 256, 0, s>>>(d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, (int)d.m, (int)d.k,
+			(int)pl.Mp, (int)pl.KB, kAPanelRows, pa, flags_a, any);
+	}
+	{
+		TraceScope ts(s, kTracePack, traced);
+		pack_kernel<kSplit><<<gb, 256, 0, s>>>(d.b, d.ldb, d.sb_outer, d.sb_inner, inner, !d.tb, (int)d.n, (int)d.k,
+			(int)pl.Np, (int)pl.KB, Cf::kBPanelRows, pb, flags_b, any);
+	}
+	NNB_CUDA_TRY(cudaGetLastError());
+
+	CUtensorMap tma, tmb;
+	NNB_TRY(encode_tiled_2d(&tma, pa, kBK, (uint64_t)pl.rows_a, kBK * 4, kBK, kAPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
+	NNB_TRY(encode_tiled_2d(&tmb, pb, kBK, (uint64_t)pl.rows_b, kBK * 4, kBK, Cf::kBPanelRows,
+		CU_TENSOR_MAP_SWIZZLE_64B));
+
+	Params p;
+	p.M = (int)d.m; p.N = (int)d.n; p.K = (int)d.k; p.KB = (int)pl.KB;
+	p.tiles_m = (int)(pl.Mp / kBM); p.tiles_n = (int)(pl.Np / kBN);
+	p.batch = (int)pl.entries; p.batch_inner = inner;
+	p.a_batched = pl.a_entries > 1; p.b_batched = pl.b_entries > 1;
+	p.Mp = (int)pl.Mp; p.Np = (int)pl.Np;
+	p.C = d.c; p.ldc = d.ldc; p.sc_outer = d.sc_outer; p.sc_inner = d.sc_inner; p.accumulate = d.accumulate;
+	p.bias = d.epi.bias; p.bias_mode = d.epi.bias_mode; p.act = d.epi.act;
+	p.mask = d.epi.mask; p.pre = d.epi.pre;
+	p.ld_aux = d.epi.ld_aux; p.s_aux_outer = d.epi.s_aux_outer; p.s_aux_inner = d.epi.s_aux_inner;
+	p.any_nonfinite = any; p.flags_a = flags_a; p.flags_b = flags_b;
+	p.A = d.a; p.lda = d.lda; p.sa_outer = d.sa_outer; p.sa_inner = d.sa_inner;
+	p.B = d.b; p.ldb = d.ldb; p.sb_outer = d.sb_outer; p.sb_inner = d.sb_inner;
+	p.ta = d.ta; p.tb = d.tb; p.err = err;
+
+	NNB_TRY((set_smem_attr<kSplit, kBN>(dev)));
+	const long long tiles = pl.entries * p.tiles_m * p.tiles_n;
+	const int grid = (int)std::min<long long>(tiles, sm_count);
+	{
+		TraceScope ts(s, kTraceGemm, traced);
+		gemm_tc_kernel<kSplit, kBN><<<grid, kThreads, Cf::kSmemBytes, s>>>(tma, tmb, p);
+	}
+	return cuda_status(cudaGetLastError(), "gemm launch");
+}
+
 template <int kSplit>
-nnb_status launch(cudaStream_t s, const DeviceState* dev, int ta, int tb, long long m, long long n,
-		long long k, const float* a, long long lda, long long sa, const float* b, long long ldb,
-		long long sb, float* c, long long ldc, long long sc, long long batch, int acc) {
-	using Cf = Cfg<kSplit>;
-	constexpr int S = Cf::S;
-	const long long Mp = round_up(m, kBM), Np = round_up(n, kBN), Kp = round_up(k, kBK);
-	const long long KB = Kp / kBK;
-	const long long a_b = sa ? batch : 1, b_b = sb ? batch : 1;
-	const long long rows_a = a_b * Mp * KB * S, rows_b = b_b * Np * KB * S;   // packed 16-float rows
-	if (rows_a > INT32_MAX || rows_b > INT32_MAX)
-		return fail(NNB_ERR_UNSUPPORTED, "sgemm: operands too large for one launch (packed rows %lld, %lld)",
-			rows_a, rows_b);
-	const long long tiles = batch * (Mp / kBM) * (Np / kBN);
-	if (tiles > INT32_MAX) return fail(NNB_ERR_UNSUPPORTED, "sgemm: too many tiles");
+static nnb_status dispatch_bn(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
+		unsigned char* ws, bool traced) {
+	if (pl.bn == 256) return launch_main<kSplit, 256>(s, dev, sm_count, err, d, pl, ws, traced);
+	if (pl.bn == 128) return launch_main<kSplit, 128>(s, dev, sm_count, err, d, pl, ws, traced);
+	return launch_main<kSplit, 64>(s, dev, sm_count, err, d, pl, ws, traced);
+}
 
-	const size_t bytes_a = (size_t)rows_a * kBK * 4, bytes_b = (size_t)rows_b * kBK * 4;
-	const size_t flag_ints = (size_t)(a_b * Mp + b_b * Np + 1);
-	const size_t off_b = round_up(bytes_a, 1024), off_f = off_b + round_up(bytes_b, 1024);
-	const size_t total = off_f + flag_ints * sizeof(int);
+static nnb_status validate(const GemmDesc& d) {
+	if (d.mode != NNB_MATH_FP32X3 && d.mode != NNB_MATH_TF32) return fail(NNB_ERR_INVALID, "gemm: unknown math mode %d", d.mode);
+	if (d.m < 0 || d.n < 0 || d.k < 0 || d.batch_outer < 0 || d.batch_inner < 1) return fail(NNB_ERR_INVALID, "gemm: negative size");
+	if (d.m == 0 || d.n == 0 || d.batch_outer == 0) return NNB_OK;
+	if (!d.c) return fail(NNB_ERR_INVALID, "gemm: C is null");
+	if (d.ldc < d.n) return fail(NNB_ERR_INVALID, "gemm: ldc %lld < n %lld", d.ldc, d.n);
+	const long long lim = 1ll << 30;
+	if (d.m > lim || d.n > lim || d.k > lim || d.batch_outer * d.batch_inner > lim)
+		return fail(NNB_ERR_UNSUPPORTED, "gemm: dimension above 2^30");
+	if (d.k > 0) {
+		if (!d.a || !d.b) return fail(NNB_ERR_INVALID, "gemm: A or B is null");
+		if (d.lda < (d.ta ? d.m : d.k)) return fail(NNB_ERR_INVALID, "gemm: lda %lld too small", d.lda);
+		if (d.ldb < (d.tb ? d.k : d.n)) return fail(NNB_ERR_INVALID, "gemm: ldb %lld too small", d.ldb);
+	}
+	if (d.epi.bias_mode != kBiasNone && !d.epi.bias) return fail(NNB_ERR_INVALID, "gemm: bias is null");
+	if (d.epi.act == kActRelu && !d.epi.mask) return fail(NNB_ERR_INVALID, "gemm: relu mask is null");
+	if (d.epi.act == kActGelu && !d.epi.pre) return fail(NNB_ERR_INVALID, "gemm: gelu pre-activation is null");
+	if ((d.epi.act != kActNone || d.epi.bias_mode != kBiasNone) && d.k == 0)
+		return fail(NNB_ERR_UNSUPPORTED, "gemm: fused epilogue with k == 0");
+	return NNB_OK;
+}
+
+}  // namespace gemm
+
+nnb_status gemm_run(cudaStream_t s, const GemmDesc& d) {
+	using namespace gemm;
+	NNB_TRY(validate(d));
+	if (d.m == 0 || d.n == 0 || d.batch_outer == 0) return NNB_OK;
+	DeviceState* dev = nullptr;
+	NNB_TRY(device_state(&dev));
+	if (d.k == 0) {
+		if (d.accumulate) return NNB_OK;
+		const long long entries = d.batch_outer * d.batch_inner;
+		dim3 g((unsigned)std::min<long long>((d.m * d.n + 255) / 256, 4096), 1, (unsigned)entries);
+		TraceScope ts(s, kTraceAux);
+		zero_fill_kernel<<<g, 256, 0, s>>>(d.c, d.ldc, d.sc_outer, d.sc_inner, (int)d.batch_inner, (int)d.m, (int)d.n);
+		return cuda_status(cudaGetLastError(), "zero fill launch");
+	}
+	Plan pl;
+	NNB_TRY(make_plan(d, pl));
 	void* ws = nullptr;
-	NNB_TRY(scratch_alloc(&ws, total, s));
-	float* pa = static_cast<float*>(ws);
-	float* pb = reinterpret_cast<float*>(static_cast<char*>(ws) + off_b);
-	int* flags = reinterpret_cast<int*>(static_cast<char*>(ws) + off_f);
-	int* flags_a = flags;
-	int* flags_b = flags + a_b * Mp;
-	int* any = flags + a_b * Mp + b_b * Np;
-
-	nnb_status st = NNB_OK;
-	do {
-		if ((st = cuda_status(cudaMemsetAsync(flags, 0, flag_ints * sizeof(int), s), "memset flags")) != NNB_OK) break;
-		dim3 ga((unsigned)(Mp / 32), (unsigned)((Kp + 63) / 64), (unsigned)a_b);
-		{
-			TraceScope ts(s, kTracePack);
-			pack_kernel<kSplit><<<ga, 256, 0, s>>>(a, lda, sa, ta, (int)m, (int)k, (int)Mp, (int)KB, pa, flags_a, any);
-		}
-		dim3 gb((unsigned)(Np / 32), (unsigned)((Kp + 63) / 64), (unsigned)b_b);
-		{
-			TraceScope ts(s, kTracePack);
-			pack_kernel<kSplit><<<gb, 256, 0, s>>>(b, ldb, sb, !tb, (int)n, (int)k, (int)Np, (int)KB, pb, flags_b, any);
-		}
-		if ((st = cuda_status(cudaGetLastError(), "pack launch")) != NNB_OK) break;
-
-		CUtensorMap tma, tmb;
-		if ((st = encode_tiled_2d(&tma, pa, kBK, (uint64_t)rows_a, kBK * 4, kBK, kPanelRows,
-				CU_TENSOR_MAP_SWIZZLE_64B)) != NNB_OK) break;
-		if ((st = encode_tiled_2d(&tmb, pb, kBK, (uint64_t)rows_b, kBK * 4, kBK, kPanelRows,
-				CU_TENSOR_MAP_SWIZZLE_64B)) != NNB_OK) break;
-
-		Params p;
-		p.M = (int)m; p.N = (int)n; p.K = (int)k; p.KB = (int)KB;
-		p.tiles_m = (int)(Mp / kBM); p.tiles_n = (int)(Np / kBN); p.batch = (int)batch;
-		p.a_batched = sa != 0; p.b_batched = sb != 0;
-		p.Mp = (int)Mp; p.Np = (int)Np;
-		p.C = c; p.ldc = ldc; p.stride_c = sc; p.accumulate = acc;
-		p.any_nonfinite = any; p.flags_a = flags_a; p.flags_b = flags_b;
-		p.A = a; p.lda = lda; p.stride_a = sa; p.B = b; p.ldb = ldb; p.stride_b = sb;
-		p.ta = ta; p.tb = tb; p.err = dev->error_word;
-
-		static bool attr_set[64][2] = {};
-		if (!attr_set[dev->device & 63][kSplit]) {
-			if ((st = cuda_status(cudaFuncSetAttribute(gemm_tc_kernel<kSplit>,
-					cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::kSmemBytes), "smem attribute")) != NNB_OK) break;
-			attr_set[dev->device & 63][kSplit] = true;
-		}
-		const int grid = (int)std::min<long long>(tiles, dev->sm_count);
-		{
-			TraceScope ts(s, kTraceGemm);
-			gemm_tc_kernel<kSplit><<<grid, kThreads, Cf::kSmemBytes, s>>>(tma, tmb, p);
-		}
-		st = cuda_status(cudaGetLastError(), "gemm launch");
-	} while (0);
+	NNB_TRY(scratch_alloc(&ws, pl.total, s));
+	nnb_status st = d.mode == NNB_MATH_FP32X3
+		? dispatch_bn<1>(s, dev->device, dev->sm_count, dev->error_word, d, pl, static_cast<unsigned char*>(ws), true)
+		: dispatch_bn<0>(s, dev->device, dev->sm_count, dev->error_word, d, pl, static_cast<unsigned char*>(ws), true);
 	nnb_status st2 = scratch_free(ws, s);
 	return st != NNB_OK ? st : st2;
 }
 
-nnb_status sgemm_entry(void* stream, int ta, int tb, size_t m, size_t n, size_t k, const float* a,
-		size_t lda, size_t sa, const float* b, size_t ldb, size_t sb, float* c, size_t ldc,
-		size_t sc, size_t batch, int acc, int mode) {
-	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	if (mode != NNB_MATH_FP32X3 && mode != NNB_MATH_TF32)
-		return fail(NNB_ERR_INVALID, "sgemm: unknown math mode %d", mode);
-	if (m == 0 || n == 0 || batch == 0) return NNB_OK;
-	if (!c) return fail(NNB_ERR_INVALID, "sgemm: C is null");
-	if (ldc < n) return fail(NNB_ERR_INVALID, "sgemm: ldc %zu < n %zu", ldc, n);
-	const size_t lim = (size_t)1 << 30;
-	if (m > lim || n > lim || k > lim || batch > lim)
-		return fail(NNB_ERR_UNSUPPORTED, "sgemm: dimension above 2^30");
-	DeviceState* dev = nullptr;
-	NNB_TRY(device_state(&dev));
-	if (k == 0) {
-		if (acc) return NNB_OK;
-		dim3 g((unsigned)std::min<size_t>((m * n + 255) / 256, 4096), 1, (unsigned)batch);
-		TraceScope ts(s, kTraceAux);
-		zero_fill_kernel<<<g, 256, 0, s>>>(c, (long long)ldc, (long long)sc, (int)m, (int)n);
-		return cuda_status(cudaGetLastError(), "zero fill launch");
-	}
-	if (!a || !b) return fail(NNB_ERR_INVALID, "sgemm: A or B is null");
-	if (lda < (ta ? m : k)) return fail(NNB_ERR_INVALID, "sgemm: lda %zu too small", lda);
-	if (ldb < (tb ? k : n)) return fail(NNB_ERR_INVALID, "sgemm: ldb %zu too small", ldb);
-	if (mode == NNB_MATH_FP32X3)
-		return launch<1>(s, dev, ta, tb, m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc, batch, acc);
-	return launch<0>(s, dev, ta, tb, m, n, k, a, lda, sa, b, ldb, sb, c, ldc, sc, batch, acc);
-}
-
-}  // namespace gemm
 }  // namespace nnb
 
 extern "C" {
 
 nnb_status nnb_sgemm(void* stream, int trans_a, int trans_b, size_t m, size_t n, size_t k,
 		const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc, int accumulate) {
-	return nnb::gemm::sgemm_entry(stream, trans_a != 0, trans_b != 0, m, n, k, a, lda, 0, b, ldb, 0, c,
-		ldc, 0, 1, accumulate != 0, nnb::math_mode());
+	return nnb_sgemm_ex(stream, trans_a, trans_b, m, n, k, a, lda, b, ldb, c, ldc, accumulate, nnb::math_mode());
 }
 
 nnb_status nnb_sgemm_ex(void* stream, int trans_a, int trans_b, size_t m, size_t n, size_t k,
 		const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc, int accumulate,
 		int math_mode) {
-	return nnb::gemm::sgemm_entry(stream, trans_a != 0, trans_b != 0, m, n, k, a, lda, 0, b, ldb, 0, c,
-		ldc, 0, 1, accumulate != 0, math_mode);
+	nnb::GemmDesc d;
+	d.ta = trans_a != 0; d.tb = trans_b != 0;
+	d.m = (long long)m; d.n = (long long)n; d.k = (long long)k;
+	d.a = a; d.lda = (long long)lda; d.b = b; d.ldb = (long long)ldb; d.c = c; d.ldc = (long long)ldc;
+	d.accumulate = accumulate != 0; d.mode = math_mode;
+	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
 }
 
 nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int trans_b, size_t m, size_t n,
@@ -514,8 +637,14 @@ nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int trans_b, siz
 		int math_mode) {
 	if (batch > 1 && stride_c == 0)
 		return nnb::fail(NNB_ERR_INVALID, "sgemm_strided_batched: stride_c must be nonzero for batch > 1");
-	return nnb::gemm::sgemm_entry(stream, trans_a != 0, trans_b != 0, m, n, k, a, lda, stride_a, b, ldb,
-		stride_b, c, ldc, stride_c, batch, accumulate != 0, math_mode);
+	nnb::GemmDesc d;
+	d.ta = trans_a != 0; d.tb = trans_b != 0;
+	d.m = (long long)m; d.n = (long long)n; d.k = (long long)k;
+	d.a = a; d.lda = (long long)lda; d.b = b; d.ldb = (long long)ldb; d.c = c; d.ldc = (long long)ldc;
+	d.batch_outer = (long long)batch;
+	d.sa_outer = (long long)stride_a; d.sb_outer = (long long)stride_b; d.sc_outer = (long long)stride_c;
+	d.accumulate = accumulate != 0; d.mode = math_mode;
+	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
 }
 
 }  // extern "C"
@@ -539,10 +668,9 @@ nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int trans_b, siz
 //   start at zero are cleared on the stream at every call. Calls that overlap on the GPU (different
 //   streams, or different host threads, without ordering between them) race on the array.
 // - Calls needing more scratch than the array holds are rejected with NNB_ERR_UNSUPPORTED before
-//   anything is enqueued.
+//   anything is enqueued. The column tile is always 256 wide here, so the limit is exactly the
+//   one stated in include/nnb.h.
 // =============================================================================================
-
-#include <mutex>
 
 namespace nnb {
 namespace gemm {
@@ -564,10 +692,11 @@ static std::mutex g_noalloc_mutex;
 
 // Once per device, with that device current: resolve the array's device address (in host code
 // the symbol itself is only a host-side stand-in) and set the kernels' shared-memory limit.
-static nnb_status noalloc_setup(NoAllocDevice** out) {
+static nnb_status noalloc_setup(NoAllocDevice** out, int* dev_out) {
 	int dev = 0;
 	NNB_CUDA_TRY(cudaGetDevice(&dev));
 	if (dev < 0 || dev >= 64) return fail(NNB_ERR_UNSUPPORTED, "sgemm_noalloc: device index %d out of range", dev);
+	*dev_out = dev;
 	std::lock_guard<std::mutex> lock(g_noalloc_mutex);
 	NoAllocDevice& d = g_noalloc_devices[dev];
 	if (!d.ready) {
@@ -581,10 +710,8 @@ static nnb_status noalloc_setup(NoAllocDevice** out) {
 		if (e != cudaSuccess) return cuda_status(e, "sgemm_noalloc: cudaGetSymbolAddress(scratch)");
 		e = cudaGetSymbolAddress(&error, g_noalloc_error);
 		if (e != cudaSuccess) return cuda_status(e, "sgemm_noalloc: cudaGetSymbolAddress(error word)");
-		NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-			Cfg<1>::kSmemBytes));
-		NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-			Cfg<0>::kSmemBytes));
+		NNB_TRY((set_smem_attr<1, 256>(dev)));
+		NNB_TRY((set_smem_attr<0, 256>(dev)));
 		d.scratch = static_cast<unsigned char*>(scratch);
 		d.error = static_cast<int*>(error);
 		d.sm_count = sms;
@@ -592,55 +719,6 @@ static nnb_status noalloc_setup(NoAllocDevice** out) {
 	}
 	*out = &d;
 	return NNB_OK;
-}
-
-template <int kSplit>
-static nnb_status launch_noalloc(cudaStream_t s, const NoAllocDevice* dev, int ta, int tb, long long m,
-		long long n, long long k, const float* a, long long lda, const float* b, long long ldb, float* c,
-		long long ldc, int acc) {
-	constexpr int S = Cfg<kSplit>::S;
-	const long long Mp = round_up(m, kBM), Np = round_up(n, kBN), Kp = round_up(k, kBK);
-	const long long KB = Kp / kBK;
-	const long long rows_a = Mp * KB * S, rows_b = Np * KB * S;
-	const size_t bytes_a = (size_t)rows_a * kBK * 4, bytes_b = (size_t)rows_b * kBK * 4;
-	const size_t flag_ints = (size_t)(Mp + Np + 1);
-	const size_t off_b = round_up(bytes_a, 1024), off_f = off_b + round_up(bytes_b, 1024);
-	const size_t total = off_f + flag_ints * sizeof(int);
-	if (total > kNoAllocScratchBytes)
-		return fail(NNB_ERR_UNSUPPORTED,
-			"sgemm_noalloc: %lld x %lld x %lld needs %zu bytes of scratch; the static buffer holds %zu "
-			"(packed operands take (roundup(m,128) + roundup(n,256)) * roundup(k,16) * %d * 4 bytes)",
-			m, n, k, total, kNoAllocScratchBytes, S);
-	float* pa = reinterpret_cast<float*>(dev->scratch);
-	float* pb = reinterpret_cast<float*>(dev->scratch + off_b);
-	int* flags_a = reinterpret_cast<int*>(dev->scratch + off_f);
-	int* flags_b = flags_a + Mp;
-	int* any = flags_b + Np;
-
-	NNB_CUDA_TRY(cudaMemsetAsync(flags_a, 0, flag_ints * sizeof(int), s));
-	dim3 ga((unsigned)(Mp / 32), (unsigned)((Kp + 63) / 64), 1);
-	pack_kernel<kSplit><<<ga, 256, 0, s>>>(a, lda, 0, ta, (int)m, (int)k, (int)Mp, (int)KB, pa, flags_a, any);
-	dim3 gb((unsigned)(Np / 32), (unsigned)((Kp + 63) / 64), 1);
-	pack_kernel<kSplit><<<gb, 256, 0, s>>>(b, ldb, 0, !tb, (int)n, (int)k, (int)Np, (int)KB, pb, flags_b, any);
-	NNB_CUDA_TRY(cudaGetLastError());
-
-	CUtensorMap tma, tmb;
-	NNB_TRY(encode_tiled_2d(&tma, pa, kBK, (uint64_t)rows_a, kBK * 4, kBK, kPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
-	NNB_TRY(encode_tiled_2d(&tmb, pb, kBK, (uint64_t)rows_b, kBK * 4, kBK, kPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
-
-	Params p;
-	p.M = (int)m; p.N = (int)n; p.K = (int)k; p.KB = (int)KB;
-	p.tiles_m = (int)(Mp / kBM); p.tiles_n = (int)(Np / kBN); p.batch = 1;
-	p.a_batched = 0; p.b_batched = 0;
-	p.Mp = (int)Mp; p.Np = (int)Np;
-	p.C = c; p.ldc = ldc; p.stride_c = 0; p.accumulate = acc;
-	p.any_nonfinite = any; p.flags_a = flags_a; p.flags_b = flags_b;
-	p.A = a; p.lda = lda; p.stride_a = 0; p.B = b; p.ldb = ldb; p.stride_b = 0;
-	p.ta = ta; p.tb = tb; p.err = dev->error;
-	const long long tiles = (Mp / kBM) * (Np / kBN);
-	const int grid = (int)std::min<long long>(tiles, dev->sm_count);
-	gemm_tc_kernel<kSplit><<<grid, kThreads, Cfg<kSplit>::kSmemBytes, s>>>(tma, tmb, p);
-	return cuda_status(cudaGetLastError(), "sgemm_noalloc: gemm launch");
 }
 
 }  // namespace gemm
@@ -652,26 +730,30 @@ extern "C" nnb_status nnb_sgemm_noalloc(void* stream, int trans_a, int trans_b, 
 	using namespace nnb;
 	using namespace nnb::gemm;
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	const int ta = trans_a != 0, tb = trans_b != 0, acc = accumulate != 0;
-	if (math_mode != NNB_MATH_FP32X3 && math_mode != NNB_MATH_TF32)
-		return fail(NNB_ERR_INVALID, "sgemm_noalloc: unknown math mode %d", math_mode);
-	if (m == 0 || n == 0) return NNB_OK;
-	if (!c) return fail(NNB_ERR_INVALID, "sgemm_noalloc: C is null");
-	if (ldc < n) return fail(NNB_ERR_INVALID, "sgemm_noalloc: ldc %zu < n %zu", ldc, n);
-	const size_t lim = (size_t)1 << 30;
-	if (m > lim || n > lim || k > lim) return fail(NNB_ERR_UNSUPPORTED, "sgemm_noalloc: dimension above 2^30");
-	NoAllocDevice* dev = nullptr;
-	NNB_TRY(noalloc_setup(&dev));
-	if (k == 0) {
-		if (acc) return NNB_OK;
-		dim3 g((unsigned)std::min<size_t>((m * n + 255) / 256, 4096), 1, 1);
-		zero_fill_kernel<<<g, 256, 0, s>>>(c, (long long)ldc, 0, (int)m, (int)n);
+	GemmDesc d;
+	d.ta = trans_a != 0; d.tb = trans_b != 0;
+	d.m = (long long)m; d.n = (long long)n; d.k = (long long)k;
+	d.a = a; d.lda = (long long)lda; d.b = b; d.ldb = (long long)ldb; d.c = c; d.ldc = (long long)ldc;
+	d.accumulate = accumulate != 0; d.mode = math_mode;
+	NNB_TRY(validate(d));
+	if (d.m == 0 || d.n == 0) return NNB_OK;
+	NoAllocDevice* nd = nullptr;
+	int dev = 0;
+	NNB_TRY(noalloc_setup(&nd, &dev));
+	if (d.k == 0) {
+		if (d.accumulate) return NNB_OK;
+		dim3 g((unsigned)std::min<long long>((d.m * d.n + 255) / 256, 4096), 1, 1);
+		zero_fill_kernel<<<g, 256, 0, s>>>(d.c, d.ldc, 0, 0, 1, (int)d.m, (int)d.n);
 		return cuda_status(cudaGetLastError(), "sgemm_noalloc: zero fill launch");
 	}
-	if (!a || !b) return fail(NNB_ERR_INVALID, "sgemm_noalloc: A or B is null");
-	if (lda < (ta ? m : k)) return fail(NNB_ERR_INVALID, "sgemm_noalloc: lda %zu too small", lda);
-	if (ldb < (tb ? k : n)) return fail(NNB_ERR_INVALID, "sgemm_noalloc: ldb %zu too small", ldb);
-	if (math_mode == NNB_MATH_FP32X3)
-		return launch_noalloc<1>(s, dev, ta, tb, m, n, k, a, lda, b, ldb, c, ldc, acc);
-	return launch_noalloc<0>(s, dev, ta, tb, m, n, k, a, lda, b, ldb, c, ldc, acc);
+	Plan pl;
+	NNB_TRY(make_plan(d, pl, 256));
+	if (pl.total > kNoAllocScratchBytes)
+		return fail(NNB_ERR_UNSUPPORTED,
+			"sgemm_noalloc: %lld x %lld x %lld needs %zu bytes of scratch; the static buffer holds %zu "
+			"(packed operands take (roundup(m,128) + roundup(n,256)) * roundup(k,16) * %d * 4 bytes)",
+			d.m, d.n, d.k, pl.total, kNoAllocScratchBytes, pl.S);
+	if (d.mode == NNB_MATH_FP32X3)
+		return launch_main<1, 256>(s, dev, nd->sm_count, nd->error, d, pl, nd->scratch, false);
+	return launch_main<0, 256>(s, dev, nd->sm_count, nd->error, d, pl, nd->scratch, false);
 }

@@ -1,0 +1,50 @@
+// nnb_gemm.h -- the library-internal GEMM interface used by every op built on the tensor-core
+// GEMM (linear, attention, convolution, batched matmul).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "../../include/nnb.h"
+
+namespace nnb {
+
+enum GemmBias : int { kBiasNone = 0, kBiasCol = 1, kBiasRow = 2 };
+enum GemmAct : int { kActNone = 0, kActRelu = 1, kActGelu = 2 };
+
+// What the epilogue does to each element v = sum_p op(A)(i,p) op(B)(p,j) before it is stored:
+//   v = v + 0                 (so a zero result is +0, as the reference's zero-started sums)
+//   v = v + bias[j] or bias[i]              (bias_mode)
+//   relu: alive = v > 0, v = alive ? v : 0, mask(i,j) = alive
+//   gelu: pre(i,j) = v, v = 0.5 v (1 + tanh_one(k (v + c v^3)))
+//   C(i,j) = accumulate ? C(i,j) + v : v
+struct GemmEpilogue {
+	const float* bias = nullptr;
+	int bias_mode = kBiasNone;
+	int act = kActNone;
+	unsigned char* mask = nullptr;      // relu alive flags, same (i, j) layout as C with ld_aux
+	float* pre = nullptr;               // gelu pre-activation, same (i, j) layout as C with ld_aux
+	long long ld_aux = 0, s_aux_outer = 0, s_aux_inner = 0;
+};
+
+// C_e = op(A_e) op(B_e) for batch entries e = (o, i), o < batch_outer, i < batch_inner, where
+// X_e = x + o * sx_outer + i * sx_inner (floats). A zero stride shares the operand.
+struct GemmDesc {
+	int ta = 0, tb = 0;
+	long long m = 0, n = 0, k = 0;
+	const float* a = nullptr;
+	long long lda = 0;
+	const float* b = nullptr;
+	long long ldb = 0;
+	float* c = nullptr;
+	long long ldc = 0;
+	long long batch_outer = 1, batch_inner = 1;
+	long long sa_outer = 0, sa_inner = 0, sb_outer = 0, sb_inner = 0, sc_outer = 0, sc_inner = 0;
+	int accumulate = 0;
+	int mode = NNB_MATH_FP32X3;
+	GemmEpilogue epi;
+};
+
+// Validates and enqueues the product (pack kernels + one persistent tensor-core kernel).
+nnb_status gemm_run(cudaStream_t s, const GemmDesc& d);
+
+}  // namespace nnb

@@ -1,0 +1,21 @@
+// nnb_ops.h -- library-internal helpers shared between the op translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "../../include/nnb.h"
+
+namespace nnb {
+
+// out[j] (+)= sum over rows of g[r][j] in the fixed chunked order of ops_linear.cu.
+nnb_status colsum(cudaStream_t s, const float* g, long long rows, long long cols, float* out, int first);
+
+// Elementwise ceiling for 1-D grids: enough blocks for n items, at most 148 * 64 blocks.
+inline unsigned grid_for(long long n, int threads) {
+	long long b = (n + threads - 1) / threads;
+	if (b < 1) b = 1;
+	if (b > 148 * 64) b = 148 * 64;
+	return (unsigned)b;
+}
+
+}  // namespace nnb

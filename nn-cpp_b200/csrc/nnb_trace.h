@@ -18,7 +18,9 @@ enum TraceKind : int {
 
 class TraceScope {
 public:
-	TraceScope(cudaStream_t s, int kind);
+	// enabled = false: the scope does nothing at all (no event, no count), for entry points that
+	// must not create CUDA objects.
+	TraceScope(cudaStream_t s, int kind, bool enabled = true);
 	~TraceScope();
 	TraceScope(const TraceScope&) = delete;
 	TraceScope& operator=(const TraceScope&) = delete;

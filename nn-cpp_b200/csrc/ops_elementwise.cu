@@ -1,0 +1,574 @@
+// ops_elementwise.cu -- the support ops the CNN and transformer configs need so that nothing on
+// their path runs on the host: relu, gelu, residual add / gradient accumulation, maxpool2d,
+// cross_entropy_loss, sequence_cross_entropy, embedding and the AdamW step.
+//
+// Each kernel keeps the reference's expression and, where the reference's order of operations is
+// sequential per output element, that order too, so relu, gelu (Cephes tanh), add, maxpool2d,
+// embedding (forward and backward) and AdamW give the reference's bits on the same inputs.
+// The loss ops use CUDA's expf/logf and a fixed warp-tree order for the row sums, so they agree
+// within tolerance rather than bit for bit.
+#include <cmath>
+
+#include "nnb_internal.h"
+#include "nnb_math.cuh"
+#include "nnb_ops.h"
+#include "nnb_trace.h"
+
+namespace nnb {
+
+namespace {
+
+constexpr int kDevBadIndex = 16;   // device error word: a target or token id outside its range
+
+#define GRID_STRIDE(i, n) \
+	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (n); i += (long long)gridDim.x * blockDim.x)
+
+__global__ void relu_fwd_kernel(long long n, const float* __restrict__ x, float* __restrict__ y) {
+	GRID_STRIDE(i, n) y[i] = x[i] > 0.0f ? x[i] : 0.0f;          // ops.cpp:780
+}
+
+__global__ void relu_bwd_kernel(long long n, const float* __restrict__ x, const float* __restrict__ g,
+		float* __restrict__ dx, int first) {
+	GRID_STRIDE(i, n) {
+		const float v = x[i] > 0.0f ? g[i] : 0.0f;                  // ops.cpp:790
+		dx[i] = first ? v + 0.0f : dx[i] + v;
+	}
+}
+
+__global__ void gelu_fwd_kernel(long long n, const float* __restrict__ x, float* __restrict__ y,
+		float* __restrict__ th) {
+	GRID_STRIDE(i, n) {
+		const float t = tanh_one(gelu_tanh_arg(x[i]));            // ops.cpp:462-464
+		th[i] = t;
+		y[i] = gelu_fwd(x[i], t);
+	}
+}
+
+// th may be null: the tanh is then recomputed from x (same bits as the saved one)
+__global__ void gelu_bwd_kernel(long long n, const float* __restrict__ x, const float* __restrict__ th,
+		const float* __restrict__ g, float* __restrict__ dx, int first) {
+	GRID_STRIDE(i, n) {
+		const float t = th ? th[i] : tanh_one(gelu_tanh_arg(x[i]));
+		const float v = gelu_bwd(g[i], x[i], t);                  // ops.cpp:474-477
+		dx[i] = first ? v + 0.0f : dx[i] + v;
+	}
+}
+
+// y = a + b with b broadcast along the leading axis when b_period < n (b has b_period elements)
+__global__ void add_kernel(long long n, const float* __restrict__ a, const float* __restrict__ b, long long b_period,
+		float* __restrict__ y) {
+	GRID_STRIDE(i, n) y[i] = a[i] + b[i % b_period];
+}
+
+// the grad_accum convention (ops.cpp:67-73): first stores src + 0, otherwise adds; negate subtracts
+__global__ void accumulate_kernel(long long n, const float* __restrict__ src, float* __restrict__ dst, int first,
+		int negate) {
+	GRID_STRIDE(i, n) {
+		if (negate) dst[i] = first ? 0.0f - src[i] : dst[i] - src[i];
+		else dst[i] = first ? src[i] + 0.0f : dst[i] + src[i];
+	}
+}
+
+// ---------------------------------------------------------------------------------------------
+// maxpool2d (ops.cpp:1609-1705): first maximum wins, offset 0 when nothing beats -inf
+// ---------------------------------------------------------------------------------------------
+
+__global__ void maxpool_fwd_kernel(long long planes, int H, int W, int k, int stride, int ho, int wo,
+		const float* __restrict__ x, float* __restrict__ y, uint32_t* __restrict__ arg) {
+	GRID_STRIDE(i, planes * ho * wo) {
+		const long long p = i / ((long long)ho * wo);
+		const int oh = (int)((i / wo) % ho), ow = (int)(i % wo);
+		const float* plane = x + p * (long long)H * W;
+		float best = -INFINITY;
+		uint32_t at = 0;
+		for (int ph = 0; ph < k; ++ph) {
+			const int r = oh * stride + ph;
+			for (int pw = 0; pw < k; ++pw) {
+				const int c = ow * stride + pw;
+				const float v = plane[(long long)r * W + c];
+				if (v > best) {
+					best = v;
+					at = (uint32_t)(r * W + c);
+				}
+			}
+		}
+		y[i] = best;
+		arg[i] = at;
+	}
+}
+
+// Gather form of the reference's scatter `plane[arg[i]] += g[i]` in output order: each input
+// element adds, in increasing output index, the gradients of the windows whose argmax it is.
+__global__ void maxpool_bwd_kernel(long long planes, int H, int W, int k, int stride, int ho, int wo,
+		const float* __restrict__ g, const uint32_t* __restrict__ arg, float* __restrict__ dx, int first) {
+	GRID_STRIDE(i, planes * (long long)H * W) {
+		const long long p = i / ((long long)H * W);
+		const int off = (int)(i % ((long long)H * W));
+		const int r = off / W, c = off % W;
+		// windows (oh, ow) with oh*stride <= r < oh*stride + k
+		const int oh_lo = r >= k ? (r - k) / stride + 1 : 0, oh_hi = min(ho - 1, r / stride);
+		const int ow_lo = c >= k ? (c - k) / stride + 1 : 0, ow_hi = min(wo - 1, c / stride);
+		float acc = first ? 0.0f : dx[i];
+		const long long obase = p * (long long)ho * wo;
+		for (int oh = oh_lo; oh <= oh_hi; ++oh)
+			for (int ow = ow_lo; ow <= ow_hi; ++ow) {
+				const long long o = obase + (long long)oh * wo + ow;
+				if (arg[o] == (uint32_t)off) acc += g[o];
+			}
+		dx[i] = acc;
+	}
+}
+
+// ---------------------------------------------------------------------------------------------
+// Cross entropy over rows (ops.cpp:1774-1840) and sequences (ops.cpp:1908-1979)
+// ---------------------------------------------------------------------------------------------
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+	return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+	return v;
+}
+
+// One warp per row: softmax row and the row's loss (ignored rows: loss 0, softmax untouched).
+// label smoothing ls: loss = (1-ls)*nll + ls*mean_nll (ls = 0 for cross_entropy_loss).
+__global__ void ce_rows_kernel(long long rows, int C, const float* __restrict__ logits,
+		const int64_t* __restrict__ targets, int64_t ignore_index, int use_ignore, float ls,
+		float* __restrict__ softmax, float* __restrict__ row_loss, int* __restrict__ valid, int* err) {
+	const int lane = threadIdx.x & 31;
+	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+	if (r >= rows) return;
+	const int64_t t = targets[r];
+	if (use_ignore && t == ignore_index) {
+		if (lane == 0) {
+			row_loss[r] = 0.0f;
+			valid[r] = 0;
+		}
+		return;
+	}
+	if (t < 0 || t >= C) {
+		if (lane == 0) {
+			row_loss[r] = __int_as_float(0x7fc00000);
+			valid[r] = 0;
+			atomicCAS(err, 0, kDevBadIndex);
+		}
+		return;
+	}
+	const float* row = logits + r * C;
+	float m = -INFINITY;
+	for (int c = lane; c < C; c += 32) m = fmaxf(m, row[c]);
+	m = warp_max(m);
+	float se = 0.0f;
+	for (int c = lane; c < C; c += 32) se += expf(row[c] - m);
+	se = warp_sum(se);
+	const float lse = logf(se);
+	float* sm = softmax + r * C;
+	float mean_nll = 0.0f;
+	const float inv_c = 1.0f / (float)C;
+	for (int c = lane; c < C; c += 32) {
+		const float lp = row[c] - m - lse;
+		sm[c] = expf(lp);
+		mean_nll -= lp * inv_c;
+	}
+	mean_nll = warp_sum(mean_nll);
+	if (lane == 0) {
+		const float nll = -(row[t] - m - lse);
+		row_loss[r] = ls == 0.0f ? nll : (1.0f - ls) * nll + ls * mean_nll;
+		valid[r] = 1;
+	}
+}
+
+// loss = sum(row_loss) / count in fixed order: 256 threads sum contiguous slices serially
+// (fp64 for sequences, as the reference; fp32 otherwise), then thread 0 sums the slices in order.
+// norm: the backward scale's divisor N (rows) or multiplier 1/count (sequences)
+__global__ void ce_total_kernel(long long rows, const float* __restrict__ row_loss, const int* __restrict__ valid,
+		int as_double, float* __restrict__ loss, float* __restrict__ norm) {
+	__shared__ double part_d[256];
+	__shared__ float part_f[256];
+	__shared__ long long part_n[256];
+	const int t = threadIdx.x;
+	const long long per = (rows + 255) / 256, r0 = t * per, r1 = min(rows, r0 + per);
+	double sd = 0.0;
+	float sf = 0.0f;
+	long long cnt = 0;
+	for (long long r = r0; r < r1; ++r) {
+		sd += (double)row_loss[r];
+		sf += row_loss[r];
+		cnt += valid[r];
+	}
+	part_d[t] = sd;
+	part_f[t] = sf;
+	part_n[t] = cnt;
+	__syncthreads();
+	if (t == 0) {
+		double td = 0.0;
+		float tf = 0.0f;
+		long long tn = 0;
+		for (int i = 0; i < 256; ++i) {
+			td += part_d[i];
+			tf += part_f[i];
+			tn += part_n[i];
+		}
+		if (as_double) {
+			*loss = tn ? (float)(td / (double)tn) : __int_as_float(0x7fc00000);
+			*norm = tn ? 1.0f / (float)tn : 0.0f;
+		} else {
+			*loss = tf / (float)rows;
+			*norm = (float)rows;
+		}
+	}
+}
+
+// dlogits (+)= (softmax - ls/C - [c == t](1 - ls)) * scale (ignored rows: 0), where
+// scale = grad_loss / N for rows (ops.cpp:1830) and grad_loss * (1/count) for sequences (ops.cpp:1968)
+__global__ void ce_bwd_kernel(long long rows, int C, const float* __restrict__ softmax,
+		const int64_t* __restrict__ targets, int64_t ignore_index, int use_ignore, float ls,
+		const float* __restrict__ grad_loss, const float* __restrict__ norm, float* __restrict__ dlogits,
+		int first) {
+	const float scale = use_ignore ? grad_loss[0] * norm[0] : grad_loss[0] / norm[0];
+	GRID_STRIDE(i, rows * (long long)C) {
+		const long long r = i / C;
+		const int c = (int)(i % C);
+		const int64_t t = targets[r];
+		float v = 0.0f;
+		if (!(use_ignore && t == ignore_index) && t >= 0 && t < C) {
+			if (ls == 0.0f && !use_ignore) {
+				v = (c == t ? softmax[i] - 1.0f : softmax[i]) * scale;            // ops.cpp:1835
+			} else {
+				float q = softmax[i] - ls / (float)C;                             // ops.cpp:1972-1974
+				if (c == t) q -= 1.0f - ls;
+				v = q * scale;
+			}
+		}
+		dlogits[i] = first ? v + 0.0f : dlogits[i] + v;
+	}
+}
+
+// ---------------------------------------------------------------------------------------------
+// embedding (ops.cpp:1991-2015)
+// ---------------------------------------------------------------------------------------------
+
+__global__ void embedding_fwd_kernel(long long count, int V, int D, const float* __restrict__ w,
+		const int64_t* __restrict__ ids, float* __restrict__ out, int* err) {
+	GRID_STRIDE(i, count * (long long)D) {
+		const long long tok = i / D;
+		const int d = (int)(i % D);
+		const int64_t id = ids[tok];
+		if (id < 0 || id >= V) {
+			out[i] = __int_as_float(0x7fc00000);
+			if (d == 0) atomicCAS(err, 0, kDevBadIndex);
+		} else {
+			out[i] = w[id * D + d];
+		}
+	}
+}
+
+constexpr int kEmbChunk = 1024;
+
+// hist[chunk][v] = tokens of id v in chunk
+__global__ void embedding_hist_kernel(long long count, int V, const int64_t* __restrict__ ids, int* __restrict__ hist) {
+	GRID_STRIDE(i, count) {
+		const int64_t id = ids[i];
+		if (id >= 0 && id < V) atomicAdd(&hist[(i / kEmbChunk) * V + id], 1);
+	}
+}
+
+// start[v][chunk] = position of the first token of (id v, chunk) in the id-major, token-order
+// layout, id_begin[v] = first position of id v. One block of 1024 threads: per-thread totals of a
+// slice of ids, an integer scan across threads (exact in any order), then the per-chunk starts.
+__global__ void __launch_bounds__(1024) embedding_scan_kernel(int V, int chunks, const int* __restrict__ hist,
+		int* __restrict__ start, int* __restrict__ id_begin) {
+	__shared__ int part[1024];
+	const int t = threadIdx.x;
+	const int per = (V + 1023) / 1024, v0 = min(V, t * per), v1 = min(V, v0 + per);
+	int tot = 0;
+	for (int v = v0; v < v1; ++v)
+		for (int c = 0; c < chunks; ++c) tot += hist[(long long)c * V + v];
+	part[t] = tot;
+	__syncthreads();
+	for (int off = 1; off < 1024; off <<= 1) {
+		const int x = t >= off ? part[t - off] : 0;
+		__syncthreads();
+		part[t] += x;
+		__syncthreads();
+	}
+	int pos = t ? part[t - 1] : 0;
+	for (int v = v0; v < v1; ++v) {
+		id_begin[v] = pos;
+		for (int c = 0; c < chunks; ++c) {
+			start[(long long)v * chunks + c] = pos;
+			pos += hist[(long long)c * V + v];
+		}
+	}
+	if (t == 1023) id_begin[V] = part[1023];
+}
+
+// Stable placement: block c copies its chunk's ids and the V slot counters into shared memory,
+// then one thread walks the chunk's tokens in order, so tokens of one id keep their order.
+__global__ void embedding_place_kernel(long long count, int V, int chunks, const int64_t* __restrict__ ids,
+		const int* __restrict__ start, int* __restrict__ order) {
+	extern __shared__ int slots[];
+	__shared__ int sid[kEmbChunk];
+	const long long c = blockIdx.x, t0 = c * kEmbChunk, t1 = min(count, t0 + kEmbChunk);
+	for (int v = threadIdx.x; v < V; v += blockDim.x) slots[v] = start[(long long)v * chunks + c];
+	for (long long t = t0 + threadIdx.x; t < t1; t += blockDim.x) {
+		const int64_t id = ids[t];
+		sid[t - t0] = (id >= 0 && id < V) ? (int)id : -1;
+	}
+	__syncthreads();
+	if (threadIdx.x != 0) return;
+	for (long long t = t0; t < t1; ++t) {
+		const int id = sid[t - t0];
+		if (id < 0) continue;
+		order[slots[id]++] = (int)t;
+	}
+}
+
+// dweight[v][d] += g[t][d] for the tokens t of id v in token order (ops.cpp:2012-2013)
+__global__ void embedding_bwd_kernel(int V, int D, const int* __restrict__ id_begin, const int* __restrict__ order,
+		const float* __restrict__ g, float* __restrict__ dw) {
+	GRID_STRIDE(i, (long long)V * D) {
+		const int v = (int)(i / D), d = (int)(i % D);
+		const int b = id_begin[v], e = id_begin[v + 1];
+		if (b == e) continue;
+		float acc = dw[i];
+		for (int k = b; k < e; ++k) acc += g[(long long)order[k] * D + d];
+		dw[i] = acc;
+	}
+}
+
+// ---------------------------------------------------------------------------------------------
+// AdamW (src/optim/adamw.cpp:15-24 then src/optim/adam.cpp:24-43)
+// ---------------------------------------------------------------------------------------------
+
+__global__ void adamw_kernel(long long n, float* __restrict__ w, const float* __restrict__ g, float* __restrict__ m,
+		float* __restrict__ v, float shrink, float lr, float b1, float b2, float eps, float c1, float c2) {
+	GRID_STRIDE(k, n) {
+		float wk = w[k] * shrink;
+		const float gk = g[k];
+		const float mk = b1 * m[k] + (1.0f - b1) * gk;
+		const float vk = b2 * v[k] + (1.0f - b2) * gk * gk;
+		m[k] = mk;
+		v[k] = vk;
+		wk -= lr * (mk / c1) / (sqrtf(vk / c2) + eps);
+		w[k] = wk;
+	}
+}
+
+}  // namespace
+
+}  // namespace nnb
+
+using nnb::grid_for;
+
+extern "C" {
+
+#define NNB_LAUNCH(kind, grid, block, kernel, ...)                 \
+	do {                                                           \
+		nnb::TraceScope nnb_ts_(s, nnb::kind);                     \
+		kernel<<<grid, block, 0, s>>>(__VA_ARGS__);                \
+	} while (0)
+
+nnb_status nnb_relu_fwd(void* stream, size_t n, const float* x, float* y) {
+	if (n == 0) return NNB_OK;
+	if (!x || !y) return nnb::fail(NNB_ERR_INVALID, "relu_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::relu_fwd_kernel, (long long)n, x, y);
+	return nnb::cuda_status(cudaGetLastError(), "relu_fwd launch");
+}
+
+nnb_status nnb_relu_bwd(void* stream, size_t n, const float* x, const float* g, float* dx, int dx_first) {
+	if (n == 0) return NNB_OK;
+	if (!x || !g || !dx) return nnb::fail(NNB_ERR_INVALID, "relu_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::relu_bwd_kernel, (long long)n, x, g, dx, dx_first);
+	return nnb::cuda_status(cudaGetLastError(), "relu_bwd launch");
+}
+
+nnb_status nnb_gelu_fwd(void* stream, size_t n, const float* x, float* y, float* tanh_saved) {
+	if (n == 0) return NNB_OK;
+	if (!x || !y || !tanh_saved) return nnb::fail(NNB_ERR_INVALID, "gelu_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::gelu_fwd_kernel, (long long)n, x, y, tanh_saved);
+	return nnb::cuda_status(cudaGetLastError(), "gelu_fwd launch");
+}
+
+nnb_status nnb_gelu_bwd(void* stream, size_t n, const float* x, const float* tanh_saved, const float* g, float* dx,
+		int dx_first) {
+	if (n == 0) return NNB_OK;
+	if (!x || !g || !dx) return nnb::fail(NNB_ERR_INVALID, "gelu_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::gelu_bwd_kernel, (long long)n, x, tanh_saved, g, dx, dx_first);
+	return nnb::cuda_status(cudaGetLastError(), "gelu_bwd launch");
+}
+
+nnb_status nnb_add_fwd(void* stream, size_t n, const float* a, const float* b, size_t b_period, float* y) {
+	if (n == 0) return NNB_OK;
+	if (!a || !b || !y) return nnb::fail(NNB_ERR_INVALID, "add_fwd: null pointer");
+	if (b_period == 0 || n % b_period != 0) return nnb::fail(NNB_ERR_SHAPE, "add_fwd: %zu is not a multiple of %zu", n, b_period);
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::add_kernel, (long long)n, a, b, (long long)b_period, y);
+	return nnb::cuda_status(cudaGetLastError(), "add_fwd launch");
+}
+
+nnb_status nnb_accumulate(void* stream, size_t n, const float* src, float* dst, int first, int negate) {
+	if (n == 0) return NNB_OK;
+	if (!src || !dst) return nnb::fail(NNB_ERR_INVALID, "accumulate: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::accumulate_kernel, (long long)n, src, dst, first, negate);
+	return nnb::cuda_status(cudaGetLastError(), "accumulate launch");
+}
+
+nnb_status nnb_maxpool2d_fwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel, size_t stride,
+		const float* x, float* y, uint32_t* argmax) {
+	if (kernel == 0 || stride == 0 || kernel > H || kernel > W) return nnb::fail(NNB_ERR_SHAPE, "maxpool2d: bad window");
+	if ((unsigned long long)H * W > 0xffffffffull) return nnb::fail(NNB_ERR_SHAPE, "maxpool2d: plane too large");
+	const long long ho = (long long)(H - kernel) / stride + 1, wo = (long long)(W - kernel) / stride + 1;
+	const long long planes = (long long)N * C;
+	if (planes == 0) return NNB_OK;
+	if (!x || !y || !argmax) return nnb::fail(NNB_ERR_INVALID, "maxpool2d_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(planes * ho * wo, 256), 256, nnb::maxpool_fwd_kernel, planes, (int)H, (int)W,
+		(int)kernel, (int)stride, (int)ho, (int)wo, x, y, argmax);
+	return nnb::cuda_status(cudaGetLastError(), "maxpool2d_fwd launch");
+}
+
+nnb_status nnb_maxpool2d_bwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel, size_t stride,
+		const float* g, const uint32_t* argmax, float* dx, int dx_first) {
+	if (kernel == 0 || stride == 0 || kernel > H || kernel > W) return nnb::fail(NNB_ERR_SHAPE, "maxpool2d: bad window");
+	const long long ho = (long long)(H - kernel) / stride + 1, wo = (long long)(W - kernel) / stride + 1;
+	const long long planes = (long long)N * C;
+	if (planes == 0) return NNB_OK;
+	if (!g || !argmax || !dx) return nnb::fail(NNB_ERR_INVALID, "maxpool2d_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(planes * H * W, 256), 256, nnb::maxpool_bwd_kernel, planes, (int)H, (int)W,
+		(int)kernel, (int)stride, (int)ho, (int)wo, g, argmax, dx, dx_first);
+	return nnb::cuda_status(cudaGetLastError(), "maxpool2d_bwd launch");
+}
+
+// Shared body of the two cross-entropy forwards. `scratch` must hold rows floats + rows ints.
+static nnb_status ce_forward(cudaStream_t s, long long rows, int C, const float* logits, const int64_t* targets,
+		int64_t ignore_index, int use_ignore, float ls, int as_double, float* softmax, float* loss, float* norm) {
+	nnb::DeviceState* dev = nullptr;
+	NNB_TRY(nnb::device_state(&dev));
+	void* ws = nullptr;
+	NNB_TRY(nnb::scratch_alloc(&ws, rows * (sizeof(float) + sizeof(int)), s));
+	float* row_loss = static_cast<float*>(ws);
+	int* valid = reinterpret_cast<int*>(row_loss + rows);
+	const long long threads = rows * 32;
+	NNB_LAUNCH(kTraceRowwise, (unsigned)((threads + 255) / 256), 256, nnb::ce_rows_kernel, rows, C, logits, targets,
+		ignore_index, use_ignore, ls, softmax, row_loss, valid, dev->error_word);
+	NNB_LAUNCH(kTraceRowwise, 1, 256, nnb::ce_total_kernel, rows, row_loss, valid, as_double, loss, norm);
+	nnb_status st = nnb::cuda_status(cudaGetLastError(), "cross entropy launch");
+	nnb_status st2 = nnb::scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+nnb_status nnb_cross_entropy_fwd(void* stream, size_t N, size_t C, const float* logits, const int64_t* targets,
+		float* softmax, float* loss, float* norm) {
+	if (N == 0 || C == 0) return nnb::fail(NNB_ERR_SHAPE, "cross_entropy: empty logits");
+	if (!logits || !targets || !softmax || !loss || !norm) return nnb::fail(NNB_ERR_INVALID, "cross_entropy_fwd: null pointer");
+	return ce_forward(static_cast<cudaStream_t>(stream), (long long)N, (int)C, logits, targets, 0, 0, 0.0f, 0, softmax,
+		loss, norm);
+}
+
+nnb_status nnb_cross_entropy_bwd(void* stream, size_t N, size_t C, const float* softmax, const int64_t* targets,
+		const float* grad_loss, const float* norm, float* dlogits, int first) {
+	if (N == 0 || C == 0) return NNB_OK;
+	if (!softmax || !targets || !grad_loss || !norm || !dlogits)
+		return nnb::fail(NNB_ERR_INVALID, "cross_entropy_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long n = (long long)N * C;
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::ce_bwd_kernel, (long long)N, (int)C, softmax, targets, 0, 0,
+		0.0f, grad_loss, norm, dlogits, first);
+	return nnb::cuda_status(cudaGetLastError(), "cross_entropy_bwd launch");
+}
+
+nnb_status nnb_sequence_ce_fwd(void* stream, size_t P, size_t V, const float* logits, const int64_t* targets,
+		int64_t ignore_index, float label_smoothing, float* softmax, float* loss, float* norm) {
+	if (P == 0 || V == 0) return nnb::fail(NNB_ERR_SHAPE, "sequence_cross_entropy: empty logits");
+	if (!(label_smoothing >= 0.0f && label_smoothing < 1.0f))
+		return nnb::fail(NNB_ERR_INVALID, "sequence_cross_entropy: label_smoothing must be in [0, 1)");
+	if (!logits || !targets || !softmax || !loss || !norm) return nnb::fail(NNB_ERR_INVALID, "sequence_ce_fwd: null pointer");
+	return ce_forward(static_cast<cudaStream_t>(stream), (long long)P, (int)V, logits, targets, ignore_index, 1,
+		label_smoothing, 1, softmax, loss, norm);
+}
+
+nnb_status nnb_sequence_ce_bwd(void* stream, size_t P, size_t V, const float* softmax, const int64_t* targets,
+		int64_t ignore_index, float label_smoothing, const float* grad_loss, const float* norm, float* dlogits,
+		int first) {
+	if (P == 0 || V == 0) return NNB_OK;
+	if (!softmax || !targets || !grad_loss || !norm || !dlogits)
+		return nnb::fail(NNB_ERR_INVALID, "sequence_ce_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long n = (long long)P * V;
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::ce_bwd_kernel, (long long)P, (int)V, softmax, targets,
+		ignore_index, 1, label_smoothing, grad_loss, norm, dlogits, first);
+	return nnb::cuda_status(cudaGetLastError(), "sequence_ce_bwd launch");
+}
+
+nnb_status nnb_embedding_fwd(void* stream, size_t V, size_t D, const float* weight, const int64_t* ids, size_t count,
+		float* out) {
+	if (count == 0 || D == 0) return NNB_OK;
+	if (!weight || !ids || !out) return nnb::fail(NNB_ERR_INVALID, "embedding_fwd: null pointer");
+	nnb::DeviceState* dev = nullptr;
+	NNB_TRY(nnb::device_state(&dev));
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for((long long)count * D, 256), 256, nnb::embedding_fwd_kernel, (long long)count,
+		(int)V, (int)D, weight, ids, out, dev->error_word);
+	return nnb::cuda_status(cudaGetLastError(), "embedding_fwd launch");
+}
+
+nnb_status nnb_embedding_bwd(void* stream, size_t V, size_t D, const int64_t* ids, size_t count, const float* g,
+		float* dweight) {
+	if (count == 0 || D == 0 || V == 0) return NNB_OK;
+	if (!ids || !g || !dweight) return nnb::fail(NNB_ERR_INVALID, "embedding_bwd: null pointer");
+	if (V > 40000) return nnb::fail(NNB_ERR_UNSUPPORTED, "embedding_bwd: vocabulary above 40000 rows");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long chunks = ((long long)count + nnb::kEmbChunk - 1) / nnb::kEmbChunk;
+	const size_t hist_n = (size_t)(chunks * V);
+	void* ws = nullptr;
+	NNB_TRY(nnb::scratch_alloc(&ws, (2 * hist_n + V + 1 + count) * sizeof(int), s));
+	int* hist = static_cast<int*>(ws);
+	int* start = hist + hist_n;
+	int* id_begin = start + hist_n;
+	int* order = id_begin + V + 1;
+	nnb_status st = nnb::cuda_status(cudaMemsetAsync(hist, 0, hist_n * sizeof(int), s), "embedding_bwd memset");
+	if (st == NNB_OK) {
+		NNB_LAUNCH(kTraceAux, grid_for((long long)count, 256), 256, nnb::embedding_hist_kernel, (long long)count, (int)V,
+			ids, hist);
+		NNB_LAUNCH(kTraceAux, 1, 1024, nnb::embedding_scan_kernel, (int)V, (int)chunks, hist, start, id_begin);
+		{
+			nnb::TraceScope ts(s, nnb::kTraceAux);
+			nnb::embedding_place_kernel<<<(unsigned)chunks, 256, V * sizeof(int), s>>>((long long)count, (int)V,
+				(int)chunks, ids, start, order);
+		}
+		NNB_LAUNCH(kTraceRowwise, grid_for((long long)V * D, 256), 256, nnb::embedding_bwd_kernel, (int)V, (int)D,
+			id_begin, order, g, dweight);
+		st = nnb::cuda_status(cudaGetLastError(), "embedding_bwd launch");
+	}
+	nnb_status st2 = nnb::scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float* g, float* m, float* v, float lr, float beta1,
+		float beta2, float eps, float weight_decay, long long step) {
+	if (n == 0) return NNB_OK;
+	if (!w || !g || !m || !v) return nnb::fail(NNB_ERR_INVALID, "adamw_step: null pointer");
+	if (step < 1) return nnb::fail(NNB_ERR_INVALID, "adamw_step: step counts from 1");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	// host scalars exactly as Adam::step computes them (adam.cpp:25-27) and AdamW::step (adamw.cpp:16)
+	const float c1 = 1.0f - std::pow(beta1, static_cast<float>(step));
+	const float c2 = 1.0f - std::pow(beta2, static_cast<float>(step));
+	const float shrink = 1.0f - lr * weight_decay;
+	NNB_LAUNCH(kTraceRowwise, grid_for((long long)n, 256), 256, nnb::adamw_kernel, (long long)n, w, g, m, v, shrink, lr,
+		beta1, beta2, eps, c1, c2);
+	return nnb::cuda_status(cudaGetLastError(), "adamw launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,122 @@
+// ops_linear.cu -- `linear` (src/autograd/ops.cpp:714-745) and the column reduction its bias
+// gradient needs.
+//
+// Forward: one GEMM Y = X W^T with the bias added in the epilogue (acc + 0, then + b[j]: the
+// reference's sgemm store followed by `out += b[j]`, ops.cpp:725-730).
+// Backward: dX (+)= G W and dW (+)= G^T X are GEMMs with accumulate = !first (ops.cpp:737,741);
+// db (+)= the column sums of G.
+//
+// Column sums: the reference reduces the rows of G one after another per column
+// (Tensor::sum(0), src/tensor.cpp:422-455). A strictly serial column sum would leave a GPU with
+// one thread per column, so it is split into chunks of kColChunk rows, each summed serially from
+// +0 in row order, and the chunk partials are then summed serially in chunk order. The order
+// depends only on the number of rows, never on the launch, and with at most kColChunk rows it is
+// the reference's order exactly.
+#include "nnb_gemm.h"
+#include "nnb_internal.h"
+#include "nnb_ops.h"
+#include "nnb_trace.h"
+
+namespace nnb {
+
+namespace {
+
+constexpr int kColChunk = 256;
+
+// partial[c][j] = sum over rows [c*kColChunk, ...) of g[r][j], serial from +0.
+__global__ void colsum_partial_kernel(const float* __restrict__ g, long long rows, long long cols,
+		float* __restrict__ partial) {
+	const long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	const long long c = blockIdx.y;
+	if (j >= cols) return;
+	const long long r0 = c * kColChunk, r1 = min(rows, r0 + kColChunk);
+	float s = 0.0f;
+	for (long long r = r0; r < r1; ++r) s += g[r * cols + j];
+	partial[c * cols + j] = s;
+}
+
+// out[j] = (first ? 0 : out[j]) + sum_c partial[c][j] (serial from +0 in chunk order).
+__global__ void colsum_final_kernel(const float* __restrict__ partial, long long chunks, long long cols,
+		float* __restrict__ out, int first) {
+	const long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	if (j >= cols) return;
+	float s = 0.0f;
+	for (long long c = 0; c < chunks; ++c) s += partial[c * cols + j];
+	out[j] = first ? s + 0.0f : out[j] + s;
+}
+
+}  // namespace
+
+nnb_status colsum(cudaStream_t s, const float* g, long long rows, long long cols, float* out, int first) {
+	if (cols == 0) return NNB_OK;
+	if (rows == 0) {
+		if (first) NNB_CUDA_TRY(cudaMemsetAsync(out, 0, cols * sizeof(float), s));
+		return NNB_OK;
+	}
+	const long long chunks = (rows + kColChunk - 1) / kColChunk;
+	if (chunks > 65535) return fail(NNB_ERR_UNSUPPORTED, "column sum over more than %lld rows", 65535ll * kColChunk);
+	void* ws = nullptr;
+	NNB_TRY(scratch_alloc(&ws, chunks * cols * sizeof(float), s));
+	float* partial = static_cast<float*>(ws);
+	const unsigned bx = (unsigned)((cols + 127) / 128);
+	{
+		TraceScope ts(s, kTraceRowwise);
+		colsum_partial_kernel<<<dim3(bx, (unsigned)chunks), 128, 0, s>>>(g, rows, cols, partial);
+	}
+	{
+		TraceScope ts(s, kTraceRowwise);
+		colsum_final_kernel<<<bx, 128, 0, s>>>(partial, chunks, cols, out, first);
+	}
+	nnb_status st = cuda_status(cudaGetLastError(), "column sum launch");
+	nnb_status st2 = scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+}  // namespace nnb
+
+extern "C" {
+
+nnb_status nnb_linear_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
+		const float* bias, float* y) {
+	if (M == 0 || n == 0) return NNB_OK;
+	if (!x || !w || !bias || !y) return nnb::fail(NNB_ERR_INVALID, "linear_fwd: null pointer");
+	if (K == 0) return nnb::fail(NNB_ERR_SHAPE, "linear_fwd: zero input features");
+	nnb::GemmDesc d;
+	d.ta = 0; d.tb = 1;
+	d.m = (long long)M; d.n = (long long)n; d.k = (long long)K;
+	d.a = x; d.lda = (long long)K; d.b = w; d.ldb = (long long)K; d.c = y; d.ldc = (long long)n;
+	d.mode = nnb::math_mode();
+	d.epi.bias = bias; d.epi.bias_mode = nnb::kBiasCol;
+	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
+}
+
+nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const float* g, const float* x,
+		const float* w, float* dx, int dx_first, float* dw, int dw_first, float* db, int db_first) {
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	if (!g || !x || !w) return nnb::fail(NNB_ERR_INVALID, "linear_bwd: null input");
+	const int mode = nnb::math_mode();
+	if (dx) {   // dX = G W: [M, n] x [n, K]
+		nnb::GemmDesc d;
+		d.m = (long long)M; d.n = (long long)K; d.k = (long long)n;
+		d.a = g; d.lda = (long long)n; d.b = w; d.ldb = (long long)K; d.c = dx; d.ldc = (long long)K;
+		d.accumulate = !dx_first; d.mode = mode;
+		NNB_TRY(nnb::gemm_run(s, d));
+	}
+	if (dw) {   // dW = G^T X: [n, M] x [M, K]
+		nnb::GemmDesc d;
+		d.ta = 1;
+		d.m = (long long)n; d.n = (long long)K; d.k = (long long)M;
+		d.a = g; d.lda = (long long)n; d.b = x; d.ldb = (long long)K; d.c = dw; d.ldc = (long long)K;
+		d.accumulate = !dw_first; d.mode = mode;
+		NNB_TRY(nnb::gemm_run(s, d));
+	}
+	if (db) NNB_TRY(nnb::colsum(s, g, (long long)M, (long long)n, db, db_first));
+	return NNB_OK;
+}
+
+nnb_status nnb_column_sum(void* stream, size_t rows, size_t cols, const float* g, float* out, int first) {
+	if (cols && (!g || !out)) return nnb::fail(NNB_ERR_INVALID, "column_sum: null pointer");
+	return nnb::colsum(static_cast<cudaStream_t>(stream), g, (long long)rows, (long long)cols, out, first);
+}
+
+}  // extern "C"

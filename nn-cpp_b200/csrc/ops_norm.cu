@@ -1,0 +1,391 @@
+// ops_norm.cu -- `layernorm` (src/autograd/ops.cpp:1003-1078) and training-mode `batchnorm`
+// (ops.cpp:900-1001), forward and backward.
+//
+// LayerNorm: one warp per row. Each lane sums a strided slice of the row serially and a fixed
+// xor-shuffle tree combines the 32 partials, so every lane holds the same bits and the result
+// depends only on D. mean and 1/std are kept per row for the backward pass, as the reference
+// keeps them. dgamma/dbeta are column sums over rows in the fixed chunked order of
+// ops_linear.cu (serial within 256-row chunks, then over chunks).
+//
+// BatchNorm: the reference's statistics are reproduced bit for bit: per (sample, channel) an
+// 8-lane fp32 partial sum over the plane (lane_sum / lane_sq / lane_dot, ops.cpp:804-898), then
+// per channel an fp64 sum of those partials in sample order; the normalisation, the folded ReLU
+// with its 1-byte alive mask, and the backward formulas use the reference's expressions with
+// correctly rounded operations only (no FMA contraction).
+#include "nnb_internal.h"
+#include "nnb_ops.h"
+#include "nnb_trace.h"
+
+namespace nnb {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+	return v;
+}
+
+// ---------------------------------------------------------------------------------------------
+// LayerNorm
+// ---------------------------------------------------------------------------------------------
+
+__global__ void layernorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+		const float* __restrict__ beta, float eps, long long R, int D, float* __restrict__ y,
+		float* __restrict__ mean, float* __restrict__ inv_std) {
+	const int lane = threadIdx.x & 31;
+	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+	if (r >= R) return;
+	const float* row = x + r * D;
+	float s = 0.0f;
+	for (int j = lane; j < D; j += 32) s += row[j];
+	s = warp_sum(s);
+	const float mu = s / (float)D;
+	float q = 0.0f;
+	for (int j = lane; j < D; j += 32) {
+		const float d = row[j] - mu;
+		q += d * d;
+	}
+	q = warp_sum(q);
+	const float inv = 1.0f / sqrtf(q / (float)D + eps);
+	float* o = y + r * D;
+	for (int j = lane; j < D; j += 32) o[j] = (row[j] - mu) * inv * gamma[j] + beta[j];
+	if (lane == 0) {
+		mean[r] = mu;
+		inv_std[r] = inv;
+	}
+}
+
+__global__ void layernorm_bwd_dx_kernel(const float* __restrict__ g, const float* __restrict__ x,
+		const float* __restrict__ gamma, const float* __restrict__ mean, const float* __restrict__ inv_std,
+		long long R, int D, float* __restrict__ dx, int first) {
+	const int lane = threadIdx.x & 31;
+	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+	if (r >= R) return;
+	const float mu = mean[r], inv = inv_std[r];
+	const float* gr = g + r * D;
+	const float* xr = x + r * D;
+	float a = 0.0f, b = 0.0f;
+	for (int j = lane; j < D; j += 32) {
+		const float dxhat = gr[j] * gamma[j];
+		a += dxhat;
+		b += dxhat * ((xr[j] - mu) * inv);
+	}
+	a = warp_sum(a);
+	b = warp_sum(b);
+	const float k = inv / (float)D, fd = (float)D;
+	float* o = dx + r * D;
+	for (int j = lane; j < D; j += 32) {
+		const float dxhat = gr[j] * gamma[j];
+		const float v = k * (fd * dxhat - a - ((xr[j] - mu) * inv) * b);
+		o[j] = first ? v + 0.0f : o[j] + v;
+	}
+}
+
+constexpr int kChunk = 256;
+
+// Chunk partials of sum_r g*xhat (dgamma) and sum_r g (dbeta), serial within the chunk.
+__global__ void layernorm_bwd_param_partial(const float* __restrict__ g, const float* __restrict__ x,
+		const float* __restrict__ mean, const float* __restrict__ inv_std, long long R, int D,
+		float* __restrict__ pg, float* __restrict__ pb) {
+	const int j = blockIdx.x * blockDim.x + threadIdx.x;
+	const long long c = blockIdx.y;
+	if (j >= D) return;
+	const long long r0 = c * kChunk, r1 = min(R, r0 + kChunk);
+	float sg = 0.0f, sb = 0.0f;
+	for (long long r = r0; r < r1; ++r) {
+		const float gv = g[r * D + j];
+		sg += gv * ((x[r * D + j] - mean[r]) * inv_std[r]);
+		sb += gv;
+	}
+	pg[c * D + j] = sg;
+	pb[c * D + j] = sb;
+}
+
+__global__ void layernorm_bwd_param_final(const float* __restrict__ pg, const float* __restrict__ pb,
+		long long chunks, int D, float* __restrict__ dgamma, int dg_first, float* __restrict__ dbeta, int db_first) {
+	const int j = blockIdx.x * blockDim.x + threadIdx.x;
+	if (j >= D) return;
+	float sg = 0.0f, sb = 0.0f;
+	for (long long c = 0; c < chunks; ++c) {
+		sg += pg[c * D + j];
+		sb += pb[c * D + j];
+	}
+	if (dgamma) dgamma[j] = dg_first ? sg + 0.0f : dgamma[j] + sg;
+	if (dbeta) dbeta[j] = db_first ? sb + 0.0f : dbeta[j] + sb;
+}
+
+// ---------------------------------------------------------------------------------------------
+// BatchNorm (training statistics)
+// ---------------------------------------------------------------------------------------------
+
+// ops.cpp:804-812
+__device__ __forceinline__ float lane_sum(const float* p, long long n) {
+	float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+	long long i = 0;
+	for (; i + 8 <= n; i += 8)
+#pragma unroll
+		for (int k = 0; k < 8; ++k) a[k] += p[i + k];
+	float t = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+	for (; i < n; ++i) t += p[i];
+	return t;
+}
+
+// ops.cpp:824-835
+__device__ __forceinline__ float lane_sq(const float* p, long long n, float mu) {
+	float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+	long long i = 0;
+	for (; i + 8 <= n; i += 8)
+#pragma unroll
+		for (int k = 0; k < 8; ++k) {
+			const float d = p[i + k] - mu;
+			a[k] += d * d;
+		}
+	float t = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+	for (; i < n; ++i) t += (p[i] - mu) * (p[i] - mu);
+	return t;
+}
+
+// lane_sum of g (masked by `alive` when given) and lane_dot of g with (x - mu): ops.cpp:848-898
+__device__ __forceinline__ void lane_sum_dot(const float* g, const unsigned char* alive, const float* x,
+		long long n, float mu, float& sum_out, float& dot_out) {
+	float a[8] = {0, 0, 0, 0, 0, 0, 0, 0}, b[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+	long long i = 0;
+	for (; i + 8 <= n; i += 8)
+#pragma unroll
+		for (int k = 0; k < 8; ++k) {
+			const float gv = alive ? (alive[i + k] ? g[i + k] : 0.0f) : g[i + k];
+			a[k] += gv;
+			b[k] += gv * (x[i + k] - mu);
+		}
+	float t = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+	float u = ((b[0] + b[1]) + (b[2] + b[3])) + ((b[4] + b[5]) + (b[6] + b[7]));
+	for (; i < n; ++i) {
+		const float gv = alive ? (alive[i] ? g[i] : 0.0f) : g[i];
+		t += gv;
+		u += gv * (x[i] - mu);
+	}
+	sum_out = t;
+	dot_out = u;
+}
+
+// part[n*C + c] = lane_sum (pass 0) or lane_sq around mean[c] (pass 1) of plane (n, c)
+__global__ void bn_plane_kernel(const float* __restrict__ x, long long N, long long C, long long S,
+		const float* __restrict__ mean, int pass, float* __restrict__ part) {
+	const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	if (idx >= N * C) return;
+	const long long c = idx % C;
+	const float* p = x + idx * S;
+	part[idx] = pass == 0 ? lane_sum(p, S) : lane_sq(p, S, mean[c]);
+}
+
+// per channel: double sum of the plane partials in sample order; pass 0 -> mean, pass 1 -> var, inv_std
+__global__ void bn_channel_kernel(const float* __restrict__ part, long long N, long long C, long long M,
+		float eps, int pass, float* __restrict__ mean, float* __restrict__ var, float* __restrict__ inv_std) {
+	const long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	if (c >= C) return;
+	double s = 0.0;
+	for (long long n = 0; n < N; ++n) s += (double)part[n * C + c];
+	const float v = (float)(s / (double)M);
+	if (pass == 0) {
+		mean[c] = v;
+	} else {
+		var[c] = v;
+		inv_std[c] = 1.0f / sqrtf(v + eps);
+	}
+}
+
+__global__ void bn_apply_kernel(const float* __restrict__ x, long long N, long long C, long long S,
+		const float* __restrict__ w, const float* __restrict__ b, const float* __restrict__ mean,
+		const float* __restrict__ inv_std, float* __restrict__ y, unsigned char* __restrict__ alive) {
+	const long long total = N * C * S;
+	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+			i += (long long)gridDim.x * blockDim.x) {
+		const long long c = (i / S) % C;
+		const float scale = w[c] * inv_std[c];
+		const float v = (x[i] - mean[c]) * scale + b[c];
+		if (alive) {
+			alive[i] = v > 0.0f;
+			y[i] = v > 0.0f ? v : 0.0f;
+		} else {
+			y[i] = v;
+		}
+	}
+}
+
+__global__ void bn_bwd_plane_kernel(const float* __restrict__ g, const unsigned char* __restrict__ alive,
+		const float* __restrict__ x, long long N, long long C, long long S, const float* __restrict__ mean,
+		float* __restrict__ psum, float* __restrict__ pdot) {
+	const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	if (idx >= N * C) return;
+	const long long c = idx % C, base = idx * S;
+	float su, du;
+	lane_sum_dot(g + base, alive ? alive + base : nullptr, x + base, S, mean[c], su, du);
+	psum[idx] = su;
+	pdot[idx] = du;
+}
+
+// per channel: sdy, sdg in fp64 (sample order); db/dw update; scalars for the dx pass
+__global__ void bn_bwd_channel_kernel(const float* __restrict__ psum, const float* __restrict__ pdot,
+		long long N, long long C, const float* __restrict__ inv_std, float* __restrict__ dw, int dw_first,
+		float* __restrict__ db, int db_first, float* __restrict__ a_out, float* __restrict__ b_out) {
+	const long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	if (c >= C) return;
+	double sdy = 0.0, sdg = 0.0;
+	for (long long n = 0; n < N; ++n) {
+		sdy += (double)psum[n * C + c];
+		sdg += (double)pdot[n * C + c];
+	}
+	const double sdyx = sdg * (double)inv_std[c];
+	if (db) db[c] = db_first ? (float)sdy + 0.0f : db[c] + (float)sdy;
+	if (dw) dw[c] = dw_first ? (float)sdyx + 0.0f : dw[c] + (float)sdyx;
+	a_out[c] = (float)sdy;
+	b_out[c] = (float)sdyx;
+}
+
+__global__ void bn_bwd_dx_kernel(const float* __restrict__ g, const unsigned char* __restrict__ alive,
+		const float* __restrict__ x, long long N, long long C, long long S, const float* __restrict__ w,
+		const float* __restrict__ mean, const float* __restrict__ inv_std, const float* __restrict__ a_c,
+		const float* __restrict__ b_c, float* __restrict__ dx, int first) {
+	const long long total = N * C * S;
+	const float fm = (float)(N * S);
+	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+			i += (long long)gridDim.x * blockDim.x) {
+		const long long c = (i / S) % C;
+		const float mu = mean[c], inv = inv_std[c];
+		const float k = w[c] * inv / fm;
+		const float gv = alive ? (alive[i] ? g[i] : 0.0f) : g[i];
+		const float v = k * (fm * gv - a_c[c] - ((x[i] - mu) * inv) * b_c[c]);
+		dx[i] = first ? v + 0.0f : dx[i] + v;
+	}
+}
+
+}  // namespace
+
+}  // namespace nnb
+
+extern "C" {
+
+nnb_status nnb_layernorm_fwd(void* stream, size_t R, size_t D, const float* x, const float* gamma,
+		const float* beta, float eps, float* y, float* mean, float* inv_std) {
+	if (R == 0) return NNB_OK;
+	if (D == 0) return nnb::fail(NNB_ERR_SHAPE, "layernorm: empty rows");
+	if (!x || !gamma || !beta || !y || !mean || !inv_std) return nnb::fail(NNB_ERR_INVALID, "layernorm_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long threads = (long long)R * 32;
+	nnb::TraceScope ts(s, nnb::kTraceRowwise);
+	nnb::layernorm_fwd_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, gamma, beta, eps, (long long)R,
+		(int)D, y, mean, inv_std);
+	return nnb::cuda_status(cudaGetLastError(), "layernorm_fwd launch");
+}
+
+nnb_status nnb_layernorm_bwd(void* stream, size_t R, size_t D, const float* g, const float* x, const float* gamma,
+		const float* mean, const float* inv_std, float* dx, int dx_first, float* dgamma, int dgamma_first,
+		float* dbeta, int dbeta_first) {
+	if (R == 0 || D == 0) return NNB_OK;
+	if (!g || !x || !gamma || !mean || !inv_std) return nnb::fail(NNB_ERR_INVALID, "layernorm_bwd: null input");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	if (dx) {
+		const long long threads = (long long)R * 32;
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::layernorm_bwd_dx_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(g, x, gamma, mean, inv_std,
+			(long long)R, (int)D, dx, dx_first);
+		NNB_CUDA_TRY(cudaGetLastError());
+	}
+	if (dgamma || dbeta) {
+		const long long chunks = ((long long)R + nnb::kChunk - 1) / nnb::kChunk;
+		if (chunks > 65535) return nnb::fail(NNB_ERR_UNSUPPORTED, "layernorm_bwd: too many rows");
+		void* ws = nullptr;
+		NNB_TRY(nnb::scratch_alloc(&ws, 2 * chunks * D * sizeof(float), s));
+		float* pg = static_cast<float*>(ws);
+		float* pb = pg + chunks * D;
+		const unsigned bx = (unsigned)((D + 127) / 128);
+		{
+			nnb::TraceScope ts(s, nnb::kTraceRowwise);
+			nnb::layernorm_bwd_param_partial<<<dim3(bx, (unsigned)chunks), 128, 0, s>>>(g, x, mean, inv_std,
+				(long long)R, (int)D, pg, pb);
+		}
+		{
+			nnb::TraceScope ts(s, nnb::kTraceRowwise);
+			nnb::layernorm_bwd_param_final<<<bx, 128, 0, s>>>(pg, pb, chunks, (int)D, dgamma, dgamma_first, dbeta,
+				dbeta_first);
+		}
+		nnb_status st = nnb::cuda_status(cudaGetLastError(), "layernorm_bwd launch");
+		nnb_status st2 = nnb::scratch_free(ws, s);
+		NNB_TRY(st);
+		NNB_TRY(st2);
+	}
+	return NNB_OK;
+}
+
+nnb_status nnb_batchnorm_fwd(void* stream, size_t N, size_t C, size_t S, const float* x, const float* weight,
+		const float* bias, float eps, int fuse_relu, float* y, unsigned char* alive, float* mean, float* var,
+		float* inv_std) {
+	if (N == 0 || C == 0) return nnb::fail(NNB_ERR_SHAPE, "batchnorm: empty batch or no channels");
+	if (!x || !weight || !bias || !y || !mean || !var || !inv_std || (fuse_relu && !alive))
+		return nnb::fail(NNB_ERR_INVALID, "batchnorm_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long NC = (long long)N * C, M = (long long)N * S;
+	void* ws = nullptr;
+	NNB_TRY(nnb::scratch_alloc(&ws, NC * sizeof(float), s));
+	float* part = static_cast<float*>(ws);
+	const unsigned gp = (unsigned)((NC + 127) / 128), gc = (unsigned)((C + 127) / 128);
+	{
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_plane_kernel<<<gp, 128, 0, s>>>(x, N, C, S, nullptr, 0, part);
+	}
+	{
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_channel_kernel<<<gc, 128, 0, s>>>(part, N, C, M, eps, 0, mean, var, inv_std);
+	}
+	{
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_plane_kernel<<<gp, 128, 0, s>>>(x, N, C, S, mean, 1, part);
+	}
+	{
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_channel_kernel<<<gc, 128, 0, s>>>(part, N, C, M, eps, 1, mean, var, inv_std);
+	}
+	{
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_apply_kernel<<<nnb::grid_for(NC * S, 256), 256, 0, s>>>(x, N, C, S, weight, bias, mean, inv_std, y,
+			fuse_relu ? alive : nullptr);
+	}
+	nnb_status st = nnb::cuda_status(cudaGetLastError(), "batchnorm_fwd launch");
+	nnb_status st2 = nnb::scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+nnb_status nnb_batchnorm_bwd(void* stream, size_t N, size_t C, size_t S, const float* g, const float* x,
+		const float* weight, const float* mean, const float* inv_std, const unsigned char* alive, float* dx,
+		int dx_first, float* dweight, int dweight_first, float* dbias, int dbias_first) {
+	if (N == 0 || C == 0) return NNB_OK;
+	if (!g || !x || !weight || !mean || !inv_std) return nnb::fail(NNB_ERR_INVALID, "batchnorm_bwd: null input");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long NC = (long long)N * C;
+	void* ws = nullptr;
+	NNB_TRY(nnb::scratch_alloc(&ws, (2 * NC + 2 * C) * sizeof(float), s));
+	float* psum = static_cast<float*>(ws);
+	float* pdot = psum + NC;
+	float* a_c = pdot + NC;
+	float* b_c = a_c + C;
+	{
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_bwd_plane_kernel<<<(unsigned)((NC + 127) / 128), 128, 0, s>>>(g, alive, x, N, C, S, mean, psum, pdot);
+	}
+	{
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_bwd_channel_kernel<<<(unsigned)((C + 127) / 128), 128, 0, s>>>(psum, pdot, N, C, inv_std, dweight,
+			dweight_first, dbias, dbias_first, a_c, b_c);
+	}
+	if (dx) {
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_bwd_dx_kernel<<<nnb::grid_for(NC * S, 256), 256, 0, s>>>(g, alive, x, N, C, S, weight, mean, inv_std,
+			a_c, b_c, dx, dx_first);
+	}
+	nnb_status st = nnb::cuda_status(cudaGetLastError(), "batchnorm_bwd launch");
+	nnb_status st2 = nnb::scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+}  // extern "C"

@@ -55,7 +55,8 @@ void drain_locked() {
 
 }  // namespace
 
-TraceScope::TraceScope(cudaStream_t s, int kind) : s_(s), kind_(kind) {
+TraceScope::TraceScope(cudaStream_t s, int kind, bool enabled) : s_(s), kind_(kind) {
+	if (!enabled) return;
 	g_launches.fetch_add(1, std::memory_order_relaxed);
 	if (!g_on.load(std::memory_order_relaxed)) return;
 	std::lock_guard<std::mutex> lock(g_mu);

@@ -37,6 +37,7 @@ _c = ctypes
 _sz = _c.c_size_t
 _p = _c.c_void_p
 _i = _c.c_int
+_f = _c.c_float
 
 # argument types of every entry point, in header order
 _SIGS = {
@@ -54,6 +55,34 @@ _SIGS = {
     "nnb_sgemm_strided_batched": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz,
                                    _sz, _i, _i], _i),
     "nnb_sgemm_noalloc": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
+    "nnb_linear_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
+    "nnb_linear_bwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
+    "nnb_column_sum": ([_p, _sz, _sz, _p, _p, _i], _i),
+    "nnb_layernorm_fwd": ([_p, _sz, _sz, _p, _p, _p, _f, _p, _p, _p], _i),
+    "nnb_layernorm_bwd": ([_p, _sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
+    "nnb_batchnorm_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _f, _i, _p, _p, _p, _p, _p], _i),
+    "nnb_batchnorm_bwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
+    "nnb_attention_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _p], _i),
+    "nnb_attention_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _p, _i], _i),
+    "nnb_masked_softmax_fwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _i, _f], _i),
+    "nnb_masked_softmax_bwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _f], _i),
+    "nnb_conv2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _i, _p, _p], _i),
+    "nnb_conv2d_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
+    "nnb_relu_fwd": ([_p, _sz, _p, _p], _i),
+    "nnb_relu_bwd": ([_p, _sz, _p, _p, _p, _i], _i),
+    "nnb_gelu_fwd": ([_p, _sz, _p, _p, _p], _i),
+    "nnb_gelu_bwd": ([_p, _sz, _p, _p, _p, _p, _i], _i),
+    "nnb_add_fwd": ([_p, _sz, _p, _p, _sz, _p], _i),
+    "nnb_accumulate": ([_p, _sz, _p, _p, _i, _i], _i),
+    "nnb_maxpool2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p], _i),
+    "nnb_maxpool2d_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _i], _i),
+    "nnb_cross_entropy_fwd": ([_p, _sz, _sz, _p, _p, _p, _p, _p], _i),
+    "nnb_cross_entropy_bwd": ([_p, _sz, _sz, _p, _p, _p, _p, _p, _i], _i),
+    "nnb_sequence_ce_fwd": ([_p, _sz, _sz, _p, _p, _c.c_int64, _f, _p, _p, _p], _i),
+    "nnb_sequence_ce_bwd": ([_p, _sz, _sz, _p, _p, _c.c_int64, _f, _p, _p, _p, _i], _i),
+    "nnb_embedding_fwd": ([_p, _sz, _sz, _p, _p, _sz, _p], _i),
+    "nnb_embedding_bwd": ([_p, _sz, _sz, _p, _sz, _p, _p], _i),
+    "nnb_adamw_step": ([_p, _sz, _p, _p, _p, _p, _f, _f, _f, _f, _f, _c.c_longlong], _i),
 }
 
 

@@ -35,6 +35,30 @@ _ORC_SIGS = {
     "orc_fill_normal": [_u32, _sz, _f, _f, _p],
     "orc_fill_int": [_u32, _sz, _c.c_int64, _c.c_int64, _p],
     "orc_make_problem": [_i, _i, _sz, _sz, _sz, _sz, _u32, _p, _p, _p],
+    "orc_gelu_fwd": [_sz, _p, _p, _p],
+    "orc_gelu_bwd": [_sz, _p, _p, _p, _p, _i],
+    "orc_relu_fwd": [_sz, _p, _p],
+    "orc_relu_bwd": [_sz, _p, _p, _p, _i],
+    "orc_colsum": [_sz, _sz, _p, _p, _i],
+    "orc_linear_fwd": [_sz, _sz, _sz, _p, _p, _p, _p],
+    "orc_linear_bwd": [_sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _i, _p, _i],
+    "orc_layernorm_fwd": [_sz, _sz, _p, _p, _p, _f, _p, _p, _p],
+    "orc_layernorm_bwd": [_sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i],
+    "orc_batchnorm_fwd": [_sz, _sz, _sz, _p, _p, _p, _f, _i, _p, _p, _p, _p, _p],
+    "orc_batchnorm_bwd": [_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i],
+    "orc_attention_fwd": [_sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _p],
+    "orc_attention_bwd": [_sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _p, _i],
+    "orc_conv2d_fwd": [_sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _p, _p],
+    "orc_conv2d_bwd": [_sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i],
+    "orc_maxpool2d_fwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p],
+    "orc_maxpool2d_bwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _i],
+    "orc_cross_entropy_fwd": [_sz, _sz, _p, _p, _p, _p],
+    "orc_cross_entropy_bwd": [_sz, _sz, _p, _p, _f, _p, _i],
+    "orc_sequence_ce_fwd": [_sz, _sz, _p, _p, _c.c_int64, _f, _p, _p],
+    "orc_sequence_ce_bwd": [_sz, _sz, _p, _p, _c.c_int64, _f, _f, _sz, _p, _i],
+    "orc_embedding_fwd": [_sz, _p, _p, _sz, _p],
+    "orc_embedding_bwd": [_sz, _p, _sz, _p, _p],
+    "orc_adamw_step": [_sz, _p, _p, _p, _p, _f, _f, _f, _f, _f, _c.c_longlong],
 }
 
 _REF_SIGS = {
@@ -47,6 +71,19 @@ _REF_SIGS = {
     "ref_matmul": ([_sz, _sz, _sz, _sz, _p, _p, _p], None),
     "ref_time_matmul": ([_sz, _sz, _sz, _p, _p, _i], _d),
     "ref_time_sgemm": ([_sz, _sz, _sz, _p, _p, _p, _i], _d),
+    "ref_linear": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _p], None),
+    "ref_layernorm": ([_sz, _sz, _p, _p, _p, _f, _p, _p, _p, _p, _p], None),
+    "ref_batchnorm": ([_sz, _sz, _sz, _p, _p, _p, _f, _i, _p, _p, _p, _p, _p, _p, _p], None),
+    "ref_attention": ([_sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p], None),
+    "ref_conv2d": ([_sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _i, _p, _p, _p, _p, _p], None),
+    "ref_maxpool2d": ([_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
+    "ref_gelu": ([_sz, _p, _p, _p, _p], None),
+    "ref_relu": ([_sz, _p, _p, _p, _p], None),
+    "ref_tanh_inplace": ([_p, _sz], None),
+    "ref_cross_entropy": ([_sz, _sz, _p, _p, _f, _p, _p], None),
+    "ref_sequence_ce": ([_sz, _sz, _sz, _p, _p, _i, _f, _f, _p, _p], None),
+    "ref_embedding": ([_sz, _sz, _p, _p, _sz, _p, _p, _p], None),
+    "ref_adamw": ([_sz, _p, _p, _f, _f, _f, _f, _f, _i], None),
 }
 
 
@@ -64,6 +101,8 @@ def _load(path, sigs):
 
 
 orc = _load(ORC_PATH, _ORC_SIGS)
+orc.orc_tanh_one.argtypes, orc.orc_tanh_one.restype = [_f], _f
+orc.orc_exp_one.argtypes, orc.orc_exp_one.restype = [_f], _f
 _ref = None
 
 
@@ -75,8 +114,13 @@ def ref():
     return _ref
 
 
-def ptr(a: np.ndarray) -> int:
-    return a.ctypes.data
+def ptr(a) -> int | None:
+    """Address of a numpy array's data (None passes through as a NULL pointer)."""
+    return None if a is None else a.ctypes.data
+
+
+def zeros(*shape, dtype=np.float32):
+    return np.zeros(shape, dtype)
 
 
 # ---- generators -------------------------------------------------------------------------------

@@ -8,7 +8,11 @@
  * reference: every function forwards to the reference's public API so that Python (ctypes)
  * can run it on the same host buffers the CUDA path sees.
  */
+#include "nn/autograd/ops.hpp"
+#include "nn/autograd/value.hpp"
 #include "nn/kernels/gemm.hpp"
+#include "nn/kernels/vmath.hpp"
+#include "nn/optim/adamw.hpp"
 #include "nn/kernels/parallel.hpp"
 #include "nn/tensor.hpp"
 #include "reference_gemm.hpp"   // the reference's own test oracle, tests/reference_gemm.hpp
@@ -17,6 +21,40 @@
 #include <cstddef>
 #include <cstring>
 #include <vector>
+
+namespace {
+
+using nn::Tensor;
+using nn::Value;
+
+size_t count_of(const std::vector<size_t>& shape) {
+	size_t n = 1;
+	for (size_t d : shape) n *= d;
+	return n;
+}
+
+Tensor tensor(std::vector<size_t> shape, const float* p) {
+	const size_t n = count_of(shape);
+	return Tensor(std::move(shape), std::vector<float>(p, p + n));
+}
+
+Value leaf(std::vector<size_t> shape, const float* p) { return Value::leaf(tensor(std::move(shape), p), true); }
+
+void copy_out(const Tensor& t, float* dst) {
+	if (dst) std::memcpy(dst, t.data().data(), t.size() * sizeof(float));
+}
+
+// Runs a node's backward rule once with the given upstream gradient (the leaves' gradients start
+// at zero, so every contribution lands as 0 + term).
+void backward_with(const Value& out, const float* g) { out.impl()->backward_fn(tensor(out.data().shape(), g)); }
+
+Tensor ids_tensor(std::vector<size_t> shape, const int64_t* ids) {
+	std::vector<float> v(count_of(shape));
+	for (size_t i = 0; i < v.size(); ++i) v[i] = static_cast<float>(ids[i]);
+	return Tensor(std::move(shape), std::move(v));
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -97,6 +135,133 @@ double ref_time_sgemm(size_t m, size_t n, size_t k, const float* a, const float*
 	for (size_t i = 1; i < t.size(); ++i)
 		for (size_t j = i; j > 0 && t[j - 1] > t[j]; --j) std::swap(t[j - 1], t[j]);
 	return t.empty() ? 0.0 : t[t.size() / 2];
+}
+
+/* ---- the reference's autograd ops, forward then one backward with upstream gradient g ---- */
+
+void ref_linear(size_t M, size_t K, size_t n, const float* x, const float* w, const float* b, const float* g,
+		float* y, float* dx, float* dw, float* db) {
+	Value X = leaf({M, K}, x), W = leaf({n, K}, w), B = leaf({n}, b);
+	Value Y = nn::linear(X, W, B);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+	copy_out(W.grad(), dw);
+	copy_out(B.grad(), db);
+}
+
+void ref_layernorm(size_t R, size_t D, const float* x, const float* gm, const float* bt, float eps, const float* g,
+		float* y, float* dx, float* dg, float* db) {
+	Value X = leaf({R, D}, x), G = leaf({D}, gm), B = leaf({D}, bt);
+	Value Y = nn::layernorm(X, G, B, eps);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+	copy_out(G.grad(), dg);
+	copy_out(B.grad(), db);
+}
+
+void ref_batchnorm(size_t N, size_t C, size_t S, const float* x, const float* w, const float* b, float eps,
+		int fuse_relu, const float* g, float* y, float* mean, float* var, float* dx, float* dw, float* db) {
+	Value X = leaf({N, C, S}, x), W = leaf({C}, w), B = leaf({C}, b);
+	Tensor mo({1}), vo({1});
+	Value Y = nn::batchnorm(X, W, B, eps, &mo, &vo, fuse_relu != 0);
+	copy_out(Y.data(), y);
+	copy_out(mo, mean);
+	copy_out(vo, var);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+	copy_out(W.grad(), dw);
+	copy_out(B.grad(), db);
+}
+
+void ref_attention(size_t N, size_t Tq, size_t Tk, size_t D, size_t heads, const float* q, const float* k,
+		const float* v, const float* pad, int causal, const float* g, float* out, float* dq, float* dk, float* dv) {
+	Value Q = leaf({N, Tq, D}, q), K = leaf({N, Tk, D}, k), V = leaf({N, Tk, D}, v);
+	Tensor mask = pad ? tensor({N, Tk}, pad) : Tensor({0});
+	Value O = nn::attention(Q, K, V, heads, mask, causal != 0);
+	copy_out(O.data(), out);
+	backward_with(O, g);
+	copy_out(Q.grad(), dq);
+	copy_out(K.grad(), dk);
+	copy_out(V.grad(), dv);
+}
+
+void ref_conv2d(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh, size_t kw, int stride,
+		int padding, const float* x, const float* w, const float* b, int fuse_relu, const float* g, float* y, float* dx,
+		float* dw, float* db) {
+	Value X = leaf({N, Cin, H, W}, x), Wt = leaf({Cout, Cin, kh, kw}, w), B = leaf({Cout}, b);
+	Value Y = fuse_relu ? nn::conv2d_relu(X, Wt, B, stride, padding) : nn::conv2d(X, Wt, B, stride, padding);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+	copy_out(Wt.grad(), dw);
+	copy_out(B.grad(), db);
+}
+
+void ref_maxpool2d(size_t N, size_t C, size_t H, size_t W, size_t k, size_t stride, const float* x, const float* g,
+		float* y, float* dx) {
+	Value X = leaf({N, C, H, W}, x);
+	Value Y = nn::maxpool2d(X, k, stride);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+}
+
+void ref_gelu(size_t n, const float* x, const float* g, float* y, float* dx) {
+	Value X = leaf({n}, x);
+	Value Y = nn::gelu(X);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+}
+
+void ref_relu(size_t n, const float* x, const float* g, float* y, float* dx) {
+	Value X = leaf({n}, x);
+	Value Y = nn::relu(X);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+}
+
+void ref_tanh_inplace(float* x, size_t n) { nn::kernels::tanh_inplace(x, n); }
+
+void ref_cross_entropy(size_t N, size_t C, const float* logits, const int64_t* targets, float grad_loss, float* loss,
+		float* dlogits) {
+	Value L = leaf({N, C}, logits);
+	Value out = nn::cross_entropy_loss(L, ids_tensor({N}, targets));
+	copy_out(out.data(), loss);
+	backward_with(out, &grad_loss);
+	copy_out(L.grad(), dlogits);
+}
+
+void ref_sequence_ce(size_t N, size_t T, size_t V, const float* logits, const int64_t* targets, int ignore_index,
+		float ls, float grad_loss, float* loss, float* dlogits) {
+	Value L = leaf({N, T, V}, logits);
+	Value out = nn::sequence_cross_entropy(L, ids_tensor({N, T}, targets), ignore_index, ls);
+	copy_out(out.data(), loss);
+	backward_with(out, &grad_loss);
+	copy_out(L.grad(), dlogits);
+}
+
+void ref_embedding(size_t V, size_t D, const float* w, const int64_t* ids, size_t count, const float* g, float* out,
+		float* dw) {
+	Value Wt = leaf({V, D}, w);
+	Value Y = nn::embedding(Wt, ids_tensor({count}, ids));
+	copy_out(Y.data(), out);
+	backward_with(Y, g);
+	copy_out(Wt.grad(), dw);
+}
+
+/* `steps` AdamW steps on one parameter with the same gradient each step; w updated in place */
+void ref_adamw(size_t n, float* w, const float* g, float lr, float b1, float b2, float eps, float wd, int steps) {
+	Value P = leaf({n}, w);
+	nn::AdamW opt({P}, lr, b1, b2, eps, wd);
+	for (int s = 0; s < steps; ++s) {
+		std::memcpy(P.grad().data().data(), g, n * sizeof(float));
+		opt.step();
+	}
+	copy_out(P.data(), w);
 }
 
 }  // extern "C"
