@@ -117,6 +117,11 @@ NNB_API nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int tran
 /* y[M, n] = x[M, K] · w[n, K]^T + bias[n] (bias added in the GEMM epilogue). */
 NNB_API nnb_status nnb_linear_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
 		const float* bias, float* y);
+/* gelu(linear(x, w, bias)) as one GEMM with the GELU in its epilogue (the transformer's fc1 followed
+ * by gelu, ops.cpp:451-466): y = gelu(pre), pre = x·w^T + bias is kept for the backward pass
+ * (nnb_gelu_bwd with tanh_saved = NULL recomputes the tanh from pre, bit for bit). */
+NNB_API nnb_status nnb_linear_gelu_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
+		const float* bias, float* y, float* pre);
 /* dx (+)= g·w, dw (+)= g^T·x, db (+)= column sums of g (fixed chunked order: serial within 256-row
  * chunks, then over chunks; the reference's serial order whenever M <= 256). */
 NNB_API nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const float* g, const float* x,

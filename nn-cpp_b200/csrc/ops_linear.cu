@@ -90,6 +90,21 @@ nnb_status nnb_linear_fwd(void* stream, size_t M, size_t K, size_t n, const floa
 	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
 }
 
+nnb_status nnb_linear_gelu_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
+		const float* bias, float* y, float* pre) {
+	if (M == 0 || n == 0) return NNB_OK;
+	if (!x || !w || !bias || !y || !pre) return nnb::fail(NNB_ERR_INVALID, "linear_gelu_fwd: null pointer");
+	if (K == 0) return nnb::fail(NNB_ERR_SHAPE, "linear_gelu_fwd: zero input features");
+	nnb::GemmDesc d;
+	d.ta = 0; d.tb = 1;
+	d.m = (long long)M; d.n = (long long)n; d.k = (long long)K;
+	d.a = x; d.lda = (long long)K; d.b = w; d.ldb = (long long)K; d.c = y; d.ldc = (long long)n;
+	d.mode = nnb::math_mode();
+	d.epi.bias = bias; d.epi.bias_mode = nnb::kBiasCol;
+	d.epi.act = nnb::kActGelu; d.epi.pre = pre; d.epi.ld_aux = (long long)n;
+	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
+}
+
 nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const float* g, const float* x,
 		const float* w, float* dx, int dx_first, float* dw, int dw_first, float* db, int db_first) {
 	cudaStream_t s = static_cast<cudaStream_t>(stream);

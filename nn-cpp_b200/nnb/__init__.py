@@ -56,6 +56,7 @@ _SIGS = {
                                    _sz, _i, _i], _i),
     "nnb_sgemm_noalloc": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
     "nnb_linear_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
+    "nnb_linear_gelu_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p], _i),
     "nnb_linear_bwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
     "nnb_column_sum": ([_p, _sz, _sz, _p, _p, _i], _i),
     "nnb_layernorm_fwd": ([_p, _sz, _sz, _p, _p, _p, _f, _p, _p, _p], _i),
