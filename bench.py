@@ -233,11 +233,12 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
 
     import nnb
 
+    from nnb.parallel import gather_rows, row_bands
+
     size = args.size
     mode = nnb.MATH_FP32X3 if args.mode == "fp32x3" else nnb.MATH_TF32
-    if size % (128 * world) != 0:
-        raise SystemExit(f"--size {size} must split into {world} bands of whole 128-row tiles")
-    rows = size // world
+    bands = row_bands(size, world)
+    rows = bands[rank][1] - bands[rank][0]
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     gen = torch.Generator(device=dev)
@@ -246,7 +247,6 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     gen.manual_seed(2000 + rank)
     a = torch.randn(rows, size, device=dev, generator=gen)
     c = torch.empty(rows, size, device=dev)
-    gathered = [torch.empty(rows, size, device=dev) for _ in range(world)] if (world > 1 and rank == 0) else None
 
     def gemm():
         nnb.sgemm(False, False, rows, size, size, a, size, b, size, c, size, False, math_mode=mode)
@@ -254,7 +254,7 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     def step():
         gemm()
         if world > 1:
-            dist.gather(c, gathered, dst=0)
+            gather_rows(c, bands, dst=0)
 
     def barrier():
         if world > 1:

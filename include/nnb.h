@@ -108,6 +108,18 @@ NNB_API nnb_status nnb_sgemm_strided_batched(void* stream, int trans_a, int tran
 		size_t stride_b, float* c, size_t ldc, size_t stride_c, size_t batch, int accumulate,
 		int math_mode);
 
+/* ---- batched Tensor matmul (replaces nn::matmul, include/nn/tensor.hpp:475,491; src/tensor.cpp:571-641) */
+
+/*
+ * a (a_ndim axes, a_shape) times b (b_ndim axes), both dense row-major on the device, with the
+ * reference's rules: a batched a (not transposed) times a 2-D b is folded into one product over all
+ * of a's rows; otherwise the batch axes broadcast numpy-style and each output matrix is one product.
+ * out_shape (room for 16 axes) and out_ndim receive the result shape; with c == NULL only the shape
+ * is computed. Mismatched inner sizes or batch axes return NNB_ERR_SHAPE (TensorShapeError).
+ */
+NNB_API nnb_status nnb_matmul(void* stream, const float* a, const int64_t* a_shape, int a_ndim, const float* b,
+		const int64_t* b_shape, int b_ndim, int trans_a, int trans_b, float* c, int64_t* out_shape, int* out_ndim);
+
 /* ---- linear (replaces Value linear, include/nn/autograd/ops.hpp:304; src/autograd/ops.cpp:714-745)
  *
  * "first" flags follow Value::grad_accum (src/autograd/value.cpp:60-64): 1 stores the value (+0),

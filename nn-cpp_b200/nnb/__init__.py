@@ -55,6 +55,7 @@ _SIGS = {
     "nnb_sgemm_strided_batched": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz,
                                    _sz, _i, _i], _i),
     "nnb_sgemm_noalloc": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
+    "nnb_matmul": ([_p, _p, _p, _i, _p, _p, _i, _i, _i, _p, _p, _p], _i),
     "nnb_linear_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
     "nnb_linear_gelu_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p], _i),
     "nnb_linear_bwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
@@ -186,6 +187,23 @@ def sgemm(trans_a: bool, trans_b: bool, m: int, n: int, k: int, a, lda: int, b, 
         st = lib().nnb_sgemm_ex(s, int(trans_a), int(trans_b), m, n, k, _ptr(a), lda, _ptr(b), ldb, _ptr(c),
                                 ldc, int(accumulate), math_mode)
     check(st)
+
+
+def matmul(a, b, trans_a: bool = False, trans_b: bool = False, stream=None):
+    """nn::matmul (src/tensor.cpp:571-641) on torch CUDA tensors; returns a new CUDA tensor."""
+    import torch
+    a, b = a.contiguous(), b.contiguous()
+    ash = (ctypes.c_int64 * a.dim())(*a.shape)
+    bsh = (ctypes.c_int64 * b.dim())(*b.shape)
+    osh = (ctypes.c_int64 * 16)()
+    ond = ctypes.c_int()
+    s = _stream_ptr(stream)
+    check(lib().nnb_matmul(s, a.data_ptr(), ash, a.dim(), b.data_ptr(), bsh, b.dim(), int(trans_a), int(trans_b),
+                           None, osh, ctypes.byref(ond)))
+    out = torch.empty(tuple(osh[: ond.value]), device=a.device, dtype=torch.float32)
+    check(lib().nnb_matmul(s, a.data_ptr(), ash, a.dim(), b.data_ptr(), bsh, b.dim(), int(trans_a), int(trans_b),
+                           out.data_ptr(), osh, ctypes.byref(ond)))
+    return out
 
 
 def sgemm_strided_batched(trans_a: bool, trans_b: bool, m: int, n: int, k: int, a, lda: int, stride_a: int,

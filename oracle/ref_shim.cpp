@@ -137,6 +137,23 @@ double ref_time_sgemm(size_t m, size_t n, size_t k, const float* a, const float*
 	return t.empty() ? 0.0 : t[t.size() / 2];
 }
 
+/*
+ * nn::matmul(a, b, trans_a, trans_b) (tensor.cpp:571) on N-D tensors; c receives the result
+ * (sized by the caller). Returns 0, or 1 when the reference throws a shape error.
+ */
+int ref_matmul_nd(const float* a, const int64_t* as, int an, const float* b, const int64_t* bs, int bn, int ta,
+		int tb, float* c) {
+	try {
+		std::vector<size_t> sa(as, as + an), sb(bs, bs + bn);
+		Tensor A = tensor(sa, a), B = tensor(sb, b);
+		Tensor C = nn::matmul(A, B, ta != 0, tb != 0);
+		copy_out(C, c);
+		return 0;
+	} catch (const std::exception&) {
+		return 1;
+	}
+}
+
 /* ---- the reference's autograd ops, forward then one backward with upstream gradient g ---- */
 
 void ref_linear(size_t M, size_t K, size_t n, const float* x, const float* w, const float* b, const float* g,

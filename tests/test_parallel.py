@@ -1,0 +1,118 @@
+"""Host logic of the sharded GEMM: band partition and gather (CPU, gloo, world size 2), and on two or
+more GPUs (NCCL) the bitwise identity of the sharded product with the single-GPU one.
+
+The reference's analogue is thread-count invariance (tests/test_kernels.cpp:343-380): here the
+number of GPUs plays the role of the thread count.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+from nnb.parallel import row_bands
+
+
+def test_row_bands_cover_rows_in_whole_tiles():
+    for m in (1, 127, 128, 1000, 8192, 16384):
+        for world in (1, 2, 3, 4, 8):
+            bands = row_bands(m, world)
+            assert len(bands) == world
+            assert bands[0][0] == 0 and bands[-1][1] == m
+            for (s0, e0), (s1, _) in zip(bands, bands[1:]):
+                assert e0 == s1
+            nonempty = [(s, e) for s, e in bands if e > s]
+            for s, e in nonempty:
+                assert s % 128 == 0
+            for s, e in nonempty[:-1]:
+                assert (e - s) % 128 == 0
+    assert row_bands(8192, 8) == [(i * 1024, (i + 1) * 1024) for i in range(8)]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_worker(rank, world, port, m, n, k, out_dir):
+    import torch
+    import torch.distributed as dist
+
+    from nnb.parallel import gather_rows, row_bands
+    from oracle import orc
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        a = orc.uniform(7, m * k).reshape(m, k)
+        b = orc.uniform(8, k * n).reshape(k, n)
+        bands = row_bands(m, world)
+        s, e = bands[rank]
+        band = np.zeros((e - s, n), np.float32)
+        if e > s:
+            orc.orc.orc_sgemm_f32(0, 0, e - s, n, k, orc.ptr(np.ascontiguousarray(a[s:e])), k, orc.ptr(b), n,
+                                  orc.ptr(band), n, 0)
+        full = gather_rows(torch.from_numpy(band), bands)
+        if rank == 0:
+            np.save(os.path.join(out_dir, "gathered.npy"), full.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_rows_gloo_world2(tmp_path):
+    """Two CPU ranks each compute a band with the oracle's fp32 loop; the gathered matrix is bitwise
+    the single-process product."""
+    from oracle import orc
+
+    m, n, k = 300, 40, 33                       # bands of 256 and 44 rows: unequal heights
+    mp.start_processes(_gloo_worker, args=(2, _free_port(), m, n, k, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    got = np.load(tmp_path / "gathered.npy")
+    a = orc.uniform(7, m * k).reshape(m, k)
+    b = orc.uniform(8, k * n).reshape(k, n)
+    want = np.zeros((m, n), np.float32)
+    orc.orc.orc_sgemm_f32(0, 0, m, n, k, orc.ptr(a), k, orc.ptr(b), n, orc.ptr(want), n, 0)
+    assert got.tobytes() == want.tobytes()
+
+
+def _nccl_worker(rank, world, port, m, n, k, mode, out_dir):
+    import torch
+    import torch.distributed as dist
+
+    import nnb
+    from nnb.parallel import gather_rows, row_bands
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        g = torch.Generator(device="cuda").manual_seed(5)
+        a = torch.randn(m, k, device="cuda", generator=g)
+        b = torch.randn(k, n, device="cuda", generator=g)
+        bands = row_bands(m, world)
+        s, e = bands[rank]
+        band = torch.empty(e - s, n, device="cuda")
+        nnb.sgemm(False, False, e - s, n, k, a[s:e], k, b, n, band, n, False, math_mode=mode)
+        full = gather_rows(band, bands)
+        if rank == 0:
+            single = torch.empty(m, n, device="cuda")
+            nnb.sgemm(False, False, m, n, k, a, k, b, n, single, n, False, math_mode=mode)
+            np.save(os.path.join(out_dir, f"eq_{mode}.npy"), np.array([bool(torch.equal(full, single))]))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", [0, 1])
+def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode):
+    torch = cuda
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    m, n, k = 1000, 700, 900
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), m, n, k, mode, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    assert bool(np.load(tmp_path / f"eq_{mode}.npy")[0])
