@@ -586,6 +586,88 @@ static nnb_status validate(const GemmDesc& d) {
 
 }  // namespace gemm
 
+namespace gemm {
+
+// Depth cut (the counterpart of the reference's `blocked`, src/kernels/gemm.cpp:453-485): a product
+// whose output has too few tiles to occupy the machine but a long depth -- a weight gradient, a
+// 512 x 512 output summed over tens of thousands of rows -- is computed as P products over
+// consecutive depth pieces into separate buffers, which one kernel then adds in piece order. P
+// depends only on (m, n, k): it is planned for a fixed 148-SM machine, never for the device, the
+// grid or the number of GPUs, so the result is the same wherever it runs.
+constexpr long long kCutSMs = 148;
+constexpr long long kCutMinDepth = 1024;
+
+static int depth_pieces(const GemmDesc& d) {
+	if (d.batch_outer * d.batch_inner != 1 || d.epi.bias_mode != kBiasNone || d.epi.act != kActNone) return 1;
+	const int bn = choose_bn(d.n);
+	const long long tiles = ((d.m + kBM - 1) / kBM) * ((d.n + bn - 1) / bn);
+	if (tiles * 2 > kCutSMs) return 1;
+	const long long p = std::min<long long>(d.k / kCutMinDepth, (kCutSMs + tiles - 1) / tiles);
+	return p >= 2 ? (int)p : 1;
+}
+
+// c = (accumulate ? c : 0) + (((part_0 + part_1) + part_2) + ...), part_p an m x n slab
+__global__ void depth_sum_kernel(const float* __restrict__ part, int pieces, long long m, long long n,
+		float* __restrict__ c, long long ldc, int accumulate) {
+	const long long mn = m * n;
+	for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < mn;
+			idx += (long long)gridDim.x * blockDim.x) {
+		float acc = part[idx];
+		for (int p = 1; p < pieces; ++p) acc += part[p * mn + idx];
+		const long long i = idx / n, j = idx - i * n;
+		float* dst = c + i * ldc + j;
+		*dst = accumulate ? *dst + acc : acc + 0.0f;
+	}
+}
+
+static nnb_status gemm_direct(cudaStream_t s, const DeviceState* dev, const GemmDesc& d) {
+	Plan pl;
+	NNB_TRY(make_plan(d, pl));
+	void* ws = nullptr;
+	NNB_TRY(scratch_alloc(&ws, pl.total, s));
+	nnb_status st = d.mode == NNB_MATH_FP32X3
+		? dispatch_bn<1>(s, dev->device, dev->sm_count, dev->error_word, d, pl, static_cast<unsigned char*>(ws), true)
+		: dispatch_bn<0>(s, dev->device, dev->sm_count, dev->error_word, d, pl, static_cast<unsigned char*>(ws), true);
+	nnb_status st2 = scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+static nnb_status gemm_depth_cut(cudaStream_t s, const DeviceState* dev, const GemmDesc& d, int pieces) {
+	const long long kp = round_up((d.k + pieces - 1) / pieces, kBK);
+	pieces = (int)((d.k + kp - 1) / kp);
+	const long long full = d.k / kp;                      // pieces of exactly kp
+	const long long mn = d.m * d.n;
+	void* ws = nullptr;
+	NNB_TRY(scratch_alloc(&ws, (size_t)pieces * mn * sizeof(float), s));
+	float* part = static_cast<float*>(ws);
+	const long long a_step = d.ta ? kp * d.lda : kp, b_step = d.tb ? kp : kp * d.ldb;
+	nnb_status st = NNB_OK;
+	do {
+		GemmDesc e = d;
+		e.k = kp; e.c = part; e.ldc = d.n; e.accumulate = 0;
+		e.batch_outer = full; e.batch_inner = 1;
+		e.sa_outer = a_step; e.sb_outer = b_step; e.sc_outer = mn;
+		if ((st = gemm_direct(s, dev, e)) != NNB_OK) break;
+		if (full < pieces) {                                 // the shorter last piece
+			GemmDesc t = d;
+			t.k = d.k - full * kp;
+			t.a = d.a + full * a_step; t.b = d.b + full * b_step;
+			t.c = part + full * mn; t.ldc = d.n; t.accumulate = 0;
+			if ((st = gemm_direct(s, dev, t)) != NNB_OK) break;
+		}
+		const unsigned blocks = (unsigned)std::min<long long>((mn + 255) / 256, 148 * 16);
+		{
+			TraceScope ts(s, kTraceAux);
+			depth_sum_kernel<<<blocks, 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc, d.accumulate);
+		}
+		st = cuda_status(cudaGetLastError(), "depth sum launch");
+	} while (0);
+	nnb_status st2 = scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+}  // namespace gemm
+
 nnb_status gemm_run(cudaStream_t s, const GemmDesc& d) {
 	using namespace gemm;
 	NNB_TRY(validate(d));
@@ -600,15 +682,9 @@ nnb_status gemm_run(cudaStream_t s, const GemmDesc& d) {
 		zero_fill_kernel<<<g, 256, 0, s>>>(d.c, d.ldc, d.sc_outer, d.sc_inner, (int)d.batch_inner, (int)d.m, (int)d.n);
 		return cuda_status(cudaGetLastError(), "zero fill launch");
 	}
-	Plan pl;
-	NNB_TRY(make_plan(d, pl));
-	void* ws = nullptr;
-	NNB_TRY(scratch_alloc(&ws, pl.total, s));
-	nnb_status st = d.mode == NNB_MATH_FP32X3
-		? dispatch_bn<1>(s, dev->device, dev->sm_count, dev->error_word, d, pl, static_cast<unsigned char*>(ws), true)
-		: dispatch_bn<0>(s, dev->device, dev->sm_count, dev->error_word, d, pl, static_cast<unsigned char*>(ws), true);
-	nnb_status st2 = scratch_free(ws, s);
-	return st != NNB_OK ? st : st2;
+	const int pieces = depth_pieces(d);
+	if (pieces > 1) return gemm_depth_cut(s, dev, d, pieces);
+	return gemm_direct(s, dev, d);
 }
 
 }  // namespace nnb

@@ -199,3 +199,25 @@ def test_argument_errors(cuda):
         nnb.sgemm(False, False, 4, 4, 4, a, 4, a, 4, a, 3, False)   # ldc < n
     with pytest.raises(ValueError):
         nnb.sgemm(False, False, 4, 4, 4, None, 4, a, 4, a, 4, False)
+
+
+@pytest.mark.parametrize("mode,rel", MODES)
+def test_depth_cut_small_output_long_depth(cuda, mode, rel):
+    """Few output tiles and a long depth take the fixed-order depth cut (the reference's
+    gemm.cpp:453-485 counterpart): still within tolerance, ragged last piece, accumulate, Inf/NaN."""
+    torch = cuda
+    for (ta, tb, m, n, k, acc), seed in zip([(1, 0, 64, 96, 4096, 0), (0, 1, 100, 50, 5000, 1), (1, 0, 512, 512, 9000, 0)],
+                                            (601, 602, 603)):
+        p = orc.Problem(ta, tb, m, n, k, 0, seed)
+        check(p, run_gpu(torch, p, acc, mode), acc, rel)
+        g1 = run_gpu(torch, p, acc, mode)
+        g2 = run_gpu(torch, p, acc, mode)
+        assert g1.tobytes() == g2.tobytes()
+    p = orc.Problem(0, 0, 7, 33, 4100, 0, 604)
+    p.a[2 * p.lda + 4099] = np.inf                    # in the last depth piece
+    p.b[1000 * p.ldb + 5] = np.nan
+    got = run_gpu(torch, p, 0, mode)
+    loop = orc.sgemm_f32(p, p.c, 0)
+    assert np.array_equal(np.isnan(got), np.isnan(loop))
+    inf = np.isinf(loop)
+    assert np.array_equal(got[inf], loop[inf])
