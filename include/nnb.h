@@ -202,6 +202,8 @@ NNB_API nnb_status nnb_relu_bwd(void* stream, size_t n, const float* x, const fl
 NNB_API nnb_status nnb_gelu_fwd(void* stream, size_t n, const float* x, float* y, float* tanh_saved);
 NNB_API nnb_status nnb_gelu_bwd(void* stream, size_t n, const float* x, const float* tanh_saved, const float* g,
 		float* dx, int dx_first);
+/* y[0..n) = value (Tensor(shape, fill) / Tensor::zeros, include/nn/tensor.hpp:147,354). */
+NNB_API nnb_status nnb_fill(void* stream, size_t n, float value, float* y);
 /* y = a + b, b repeated every b_period elements (add with a broadcast leading axis, ops.cpp:331). */
 NNB_API nnb_status nnb_add_fwd(void* stream, size_t n, const float* a, const float* b, size_t b_period, float* y);
 /* dst (+)= src or (-)= src with the grad_accum convention (ops.cpp:77-92, add_to_grad). */
@@ -226,12 +228,13 @@ NNB_API nnb_status nnb_sequence_ce_fwd(void* stream, size_t P, size_t V, const f
 NNB_API nnb_status nnb_sequence_ce_bwd(void* stream, size_t P, size_t V, const float* softmax,
 		const int64_t* targets, int64_t ignore_index, float label_smoothing, const float* grad_loss,
 		const float* norm, float* dlogits, int first);
-/* embedding (ops.cpp:1991-2015): out[i] = weight[ids[i]]; backward adds g rows into dweight in
- * token order per row (deterministic, no float atomics); V <= 40000 for the backward. */
+/* embedding (ops.cpp:1991-2015): out[i] = weight[ids[i]]; the backward adds g rows into dweight in
+ * token order per row (deterministic, no float atomics), starting from 0 when first != 0 and from
+ * dweight's contents otherwise; V <= 40000 for the backward. */
 NNB_API nnb_status nnb_embedding_fwd(void* stream, size_t V, size_t D, const float* weight, const int64_t* ids,
 		size_t count, float* out);
 NNB_API nnb_status nnb_embedding_bwd(void* stream, size_t V, size_t D, const int64_t* ids, size_t count,
-		const float* g, float* dweight);
+		const float* g, float* dweight, int first);
 /* One AdamW step on one parameter (src/optim/adamw.cpp:15-24 then src/optim/adam.cpp:24-43);
  * step counts from 1 (the value of Adam::t_ after its increment). */
 NNB_API nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float* g, float* m, float* v, float lr,

@@ -54,6 +54,10 @@ __global__ void gelu_bwd_kernel(long long n, const float* __restrict__ x, const 
 	}
 }
 
+__global__ void fill_kernel(long long n, float value, float* __restrict__ y) {
+	GRID_STRIDE(i, n) y[i] = value;
+}
+
 // y = a + b with b broadcast along the leading axis when b_period < n (b has b_period elements)
 __global__ void add_kernel(long long n, const float* __restrict__ a, const float* __restrict__ b, long long b_period,
 		float* __restrict__ y) {
@@ -329,14 +333,18 @@ __global__ void embedding_place_kernel(long long count, int V, int chunks, const
 	}
 }
 
-// dweight[v][d] += g[t][d] for the tokens t of id v in token order (ops.cpp:2012-2013)
+// dweight[v][d] (+)= g[t][d] for the tokens t of id v in token order (ops.cpp:2012-2013); with
+// first set the row starts from 0, as the reference's zero-on-demand grad() does
 __global__ void embedding_bwd_kernel(int V, int D, const int* __restrict__ id_begin, const int* __restrict__ order,
-		const float* __restrict__ g, float* __restrict__ dw) {
+		const float* __restrict__ g, float* __restrict__ dw, int first) {
 	GRID_STRIDE(i, (long long)V * D) {
 		const int v = (int)(i / D), d = (int)(i % D);
 		const int b = id_begin[v], e = id_begin[v + 1];
-		if (b == e) continue;
-		float acc = dw[i];
+		if (b == e) {
+			if (first) dw[i] = 0.0f;
+			continue;
+		}
+		float acc = first ? 0.0f : dw[i];
 		for (int k = b; k < e; ++k) acc += g[(long long)order[k] * D + d];
 		dw[i] = acc;
 	}
@@ -405,6 +413,14 @@ nnb_status nnb_gelu_bwd(void* stream, size_t n, const float* x, const float* tan
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::gelu_bwd_kernel, (long long)n, x, tanh_saved, g, dx, dx_first);
 	return nnb::cuda_status(cudaGetLastError(), "gelu_bwd launch");
+}
+
+nnb_status nnb_fill(void* stream, size_t n, float value, float* y) {
+	if (n == 0) return NNB_OK;
+	if (!y) return nnb::fail(NNB_ERR_INVALID, "fill: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceAux, grid_for(n, 256), 256, nnb::fill_kernel, (long long)n, value, y);
+	return nnb::cuda_status(cudaGetLastError(), "fill launch");
 }
 
 nnb_status nnb_add_fwd(void* stream, size_t n, const float* a, const float* b, size_t b_period, float* y) {
@@ -525,8 +541,12 @@ nnb_status nnb_embedding_fwd(void* stream, size_t V, size_t D, const float* weig
 }
 
 nnb_status nnb_embedding_bwd(void* stream, size_t V, size_t D, const int64_t* ids, size_t count, const float* g,
-		float* dweight) {
-	if (count == 0 || D == 0 || V == 0) return NNB_OK;
+		float* dweight, int first) {
+	if (D == 0 || V == 0) return NNB_OK;
+	if (count == 0) {
+		if (first && dweight) NNB_CUDA_TRY(cudaMemsetAsync(dweight, 0, V * D * sizeof(float), static_cast<cudaStream_t>(stream)));
+		return NNB_OK;
+	}
 	if (!ids || !g || !dweight) return nnb::fail(NNB_ERR_INVALID, "embedding_bwd: null pointer");
 	if (V > 40000) return nnb::fail(NNB_ERR_UNSUPPORTED, "embedding_bwd: vocabulary above 40000 rows");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -549,7 +569,7 @@ nnb_status nnb_embedding_bwd(void* stream, size_t V, size_t D, const int64_t* id
 				(int)chunks, ids, start, order);
 		}
 		NNB_LAUNCH(kTraceRowwise, grid_for((long long)V * D, 256), 256, nnb::embedding_bwd_kernel, (int)V, (int)D,
-			id_begin, order, g, dweight);
+			id_begin, order, g, dweight, first);
 		st = nnb::cuda_status(cudaGetLastError(), "embedding_bwd launch");
 	}
 	nnb_status st2 = nnb::scratch_free(ws, s);

@@ -74,6 +74,7 @@ _SIGS = {
     "nnb_relu_bwd": ([_p, _sz, _p, _p, _p, _i], _i),
     "nnb_gelu_fwd": ([_p, _sz, _p, _p, _p], _i),
     "nnb_gelu_bwd": ([_p, _sz, _p, _p, _p, _p, _i], _i),
+    "nnb_fill": ([_p, _sz, _f, _p], _i),
     "nnb_add_fwd": ([_p, _sz, _p, _p, _sz, _p], _i),
     "nnb_accumulate": ([_p, _sz, _p, _p, _i, _i], _i),
     "nnb_maxpool2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p], _i),
@@ -83,7 +84,7 @@ _SIGS = {
     "nnb_sequence_ce_fwd": ([_p, _sz, _sz, _p, _p, _c.c_int64, _f, _p, _p, _p], _i),
     "nnb_sequence_ce_bwd": ([_p, _sz, _sz, _p, _p, _c.c_int64, _f, _p, _p, _p, _i], _i),
     "nnb_embedding_fwd": ([_p, _sz, _sz, _p, _p, _sz, _p], _i),
-    "nnb_embedding_bwd": ([_p, _sz, _sz, _p, _sz, _p, _p], _i),
+    "nnb_embedding_bwd": ([_p, _sz, _sz, _p, _sz, _p, _p, _i], _i),
     "nnb_adamw_step": ([_p, _sz, _p, _p, _p, _p, _f, _f, _f, _f, _f, _c.c_longlong], _i),
 }
 

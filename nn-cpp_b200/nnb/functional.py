@@ -1,0 +1,302 @@
+"""Differentiable ops over the C ABI, mirroring nn's autograd ops (include/nn/autograd/ops.hpp).
+
+Each function runs the forward kernel(s), returns a Value, and installs a backward rule that
+calls the matching backward entry point with the grad_accum `first` flag of every parent that
+needs a gradient. Names and argument meaning follow the reference; shape errors raise
+nnb.TensorShapeError as the reference throws TensorShapeError.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import TensorShapeError, check, lib
+from .autograd import Value, empty
+
+
+def _s():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need(v: Value) -> bool:
+    return v.requires_grad
+
+
+# ---- linear (ops.cpp:714-745) -------------------------------------------------------------------
+
+def linear(x: Value, weight: Value, bias: Value) -> Value:
+    xs, ws = x.shape, weight.shape
+    if len(xs) < 2 or len(ws) != 2 or xs[-1] != ws[1] or bias.shape != (ws[0],):
+        raise TensorShapeError("linear: shapes do not agree")
+    n, K = ws
+    M = x.data.numel() // K
+    y = empty(xs[:-1] + (n,))
+    check(lib().nnb_linear_fwd(_s(), M, K, n, _p(x.data), _p(weight.data), _p(bias.data), _p(y)))
+
+    def backward(g):
+        dx, fx = x.grad_accum() if _need(x) else (None, 0)
+        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
+        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
+        check(lib().nnb_linear_bwd(_s(), M, K, n, _p(g), _p(x.data), _p(weight.data), _p(dx), fx, _p(dw), fw,
+                                   _p(db), fb))
+
+    return Value.node(y, (x, weight, bias), backward)
+
+
+def linear_gelu(x: Value, weight: Value, bias: Value) -> Value:
+    """gelu(linear(x, w, b)) as one GEMM with the GELU in its epilogue (same bits as the two ops)."""
+    xs, ws = x.shape, weight.shape
+    if len(xs) < 2 or len(ws) != 2 or xs[-1] != ws[1] or bias.shape != (ws[0],):
+        raise TensorShapeError("linear: shapes do not agree")
+    n, K = ws
+    M = x.data.numel() // K
+    y = empty(xs[:-1] + (n,))
+    pre = empty(xs[:-1] + (n,))
+    check(lib().nnb_linear_gelu_fwd(_s(), M, K, n, _p(x.data), _p(weight.data), _p(bias.data), _p(y), _p(pre)))
+
+    def backward(g):
+        dpre = empty(pre.shape)
+        check(lib().nnb_gelu_bwd(_s(), pre.numel(), _p(pre), None, _p(g), _p(dpre), 1))
+        dx, fx = x.grad_accum() if _need(x) else (None, 0)
+        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
+        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
+        check(lib().nnb_linear_bwd(_s(), M, K, n, _p(dpre), _p(x.data), _p(weight.data), _p(dx), fx, _p(dw), fw,
+                                   _p(db), fb))
+
+    return Value.node(y, (x, weight, bias), backward)
+
+
+# ---- elementwise ------------------------------------------------------------------------------
+
+def add(a: Value, b: Value) -> Value:
+    """a + b for equal shapes, or b broadcast over a's leading axes (b's shape a suffix of a's)."""
+    if a.shape != b.shape and (len(b.shape) > len(a.shape) or a.shape[len(a.shape) - len(b.shape):] != b.shape):
+        raise TensorShapeError("add: shapes do not broadcast")
+    y = empty(a.shape)
+    check(lib().nnb_add_fwd(_s(), a.data.numel(), _p(a.data), _p(b.data), b.data.numel(), _p(y)))
+    same = a.shape == b.shape
+
+    def backward(g):
+        if _need(a):
+            da, f = a.grad_accum()
+            check(lib().nnb_accumulate(_s(), g.numel(), _p(g), _p(da), f, 0))
+        if _need(b):
+            db, f = b.grad_accum()
+            if same:
+                check(lib().nnb_accumulate(_s(), g.numel(), _p(g), _p(db), f, 0))
+            else:   # sum over the broadcast leading axes (sum_to_shape, ops.cpp:35-53)
+                rows = g.numel() // b.data.numel()
+                check(lib().nnb_column_sum(_s(), rows, b.data.numel(), _p(g), _p(db), f))
+
+    return Value.node(y, (a, b), backward)
+
+
+def relu(x: Value) -> Value:
+    y = empty(x.shape)
+    check(lib().nnb_relu_fwd(_s(), x.data.numel(), _p(x.data), _p(y)))
+
+    def backward(g):
+        dx, f = x.grad_accum()
+        check(lib().nnb_relu_bwd(_s(), g.numel(), _p(x.data), _p(g), _p(dx), f))
+
+    return Value.node(y, (x,), backward)
+
+
+def gelu(x: Value) -> Value:
+    y, th = empty(x.shape), empty(x.shape)
+    check(lib().nnb_gelu_fwd(_s(), x.data.numel(), _p(x.data), _p(y), _p(th)))
+
+    def backward(g):
+        dx, f = x.grad_accum()
+        check(lib().nnb_gelu_bwd(_s(), g.numel(), _p(x.data), _p(th), _p(g), _p(dx), f))
+
+    return Value.node(y, (x,), backward)
+
+
+def reshape(x: Value, shape) -> Value:
+    shape = tuple(shape)
+    n = 1
+    for d in shape:
+        n *= d
+    if n != x.data.numel():
+        raise TensorShapeError("reshape: element count differs")
+    y = x.data.view(shape)
+
+    def backward(g):
+        dx, f = x.grad_accum()
+        check(lib().nnb_accumulate(_s(), g.numel(), _p(g), _p(dx), f, 0))
+
+    return Value.node(y, (x,), backward)
+
+
+# ---- normalisation ------------------------------------------------------------------------------
+
+def layernorm(x: Value, gamma: Value, beta: Value, eps: float) -> Value:
+    D = x.shape[-1] if x.shape else 0
+    if not x.shape or gamma.shape != (D,) or beta.shape != (D,):
+        raise TensorShapeError("layernorm: shapes do not agree")
+    R = x.data.numel() // D
+    y, mean, inv = empty(x.shape), empty((R,)), empty((R,))
+    check(lib().nnb_layernorm_fwd(_s(), R, D, _p(x.data), _p(gamma.data), _p(beta.data), ctypes.c_float(eps), _p(y),
+                                  _p(mean), _p(inv)))
+
+    def backward(g):
+        dx, fx = x.grad_accum() if _need(x) else (None, 0)
+        dg, fg = gamma.grad_accum() if _need(gamma) else (None, 0)
+        db, fb = beta.grad_accum() if _need(beta) else (None, 0)
+        check(lib().nnb_layernorm_bwd(_s(), R, D, _p(g), _p(x.data), _p(gamma.data), _p(mean), _p(inv), _p(dx), fx,
+                                      _p(dg), fg, _p(db), fb))
+
+    return Value.node(y, (x, gamma, beta), backward)
+
+
+def batchnorm(x: Value, weight: Value, bias: Value, eps: float, fuse_relu: bool = False) -> Value:
+    if len(x.shape) < 2:
+        raise TensorShapeError("batchnorm: needs N and C axes")
+    N, C = x.shape[0], x.shape[1]
+    S = x.data.numel() // max(1, N * C)
+    y = empty(x.shape)
+    alive = empty(x.shape, dtype=torch.uint8) if fuse_relu else None
+    mean, var, inv = empty((C,)), empty((C,)), empty((C,))
+    check(lib().nnb_batchnorm_fwd(_s(), N, C, S, _p(x.data), _p(weight.data), _p(bias.data), ctypes.c_float(eps),
+                                  int(fuse_relu), _p(y), _p(alive), _p(mean), _p(var), _p(inv)))
+
+    def backward(g):
+        dx, fx = x.grad_accum() if _need(x) else (None, 0)
+        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
+        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
+        check(lib().nnb_batchnorm_bwd(_s(), N, C, S, _p(g), _p(x.data), _p(weight.data), _p(mean), _p(inv), _p(alive),
+                                      _p(dx), fx, _p(dw), fw, _p(db), fb))
+
+    out = Value.node(y, (x, weight, bias), backward)
+    out.name = "batchnorm"
+    return out
+
+
+# ---- attention (ops.cpp:1226-1296) --------------------------------------------------------------
+
+def attention(q: Value, k: Value, v: Value, heads: int, key_padding_mask: torch.Tensor | None = None,
+              causal: bool = False) -> Value:
+    qs, ks = q.shape, k.shape
+    if len(qs) != 3 or len(ks) != 3 or v.shape != ks or qs[0] != ks[0] or qs[2] != ks[2]:
+        raise TensorShapeError("attention: shapes do not agree")
+    N, Tq, D = qs
+    Tk = ks[1]
+    out, probs = empty((N, Tq, D)), empty((N, heads, Tq, Tk))
+    check(lib().nnb_attention_fwd(_s(), N, Tq, Tk, D, heads, _p(q.data), _p(k.data), _p(v.data),
+                                  _p(key_padding_mask), int(causal), _p(out), _p(probs)))
+
+    def backward(g):
+        # fetched in the reference's order (v, q, k: ops.cpp:1273-1275)
+        dv, fv = v.grad_accum() if _need(v) else (None, 0)
+        dq, fq = q.grad_accum() if _need(q) else (None, 0)
+        dk, fk = k.grad_accum() if _need(k) else (None, 0)
+        check(lib().nnb_attention_bwd(_s(), N, Tq, Tk, D, heads, _p(g), _p(q.data), _p(k.data), _p(v.data),
+                                      _p(probs), _p(key_padding_mask), int(causal), _p(dq), fq, _p(dk), fk, _p(dv),
+                                      fv))
+
+    return Value.node(out, (q, k, v), backward)
+
+
+# ---- convolution and pooling ---------------------------------------------------------------------
+
+def conv2d(x: Value, weight: Value, bias: Value, stride: int, padding: int, fuse_relu: bool = False) -> Value:
+    if len(x.shape) != 4 or len(weight.shape) != 4:
+        raise TensorShapeError("conv2d: needs 4-D input and weight")
+    N, Cin, H, W = x.shape
+    Cout, wc, kh, kw = weight.shape
+    if wc != Cin or bias.shape != (Cout,):
+        raise TensorShapeError("conv2d: channels do not agree")
+    if stride <= 0 or padding < 0 or kh > H + 2 * padding or kw > W + 2 * padding:
+        raise TensorShapeError("conv2d: bad window")
+    ho, wo = (H + 2 * padding - kh) // stride + 1, (W + 2 * padding - kw) // stride + 1
+    y = empty((N, Cout, ho, wo))
+    alive = empty((N, Cout, ho, wo), dtype=torch.uint8) if fuse_relu else None
+    check(lib().nnb_conv2d_fwd(_s(), N, Cin, H, W, Cout, kh, kw, stride, padding, _p(x.data), _p(weight.data),
+                               _p(bias.data), int(fuse_relu), _p(y), _p(alive)))
+
+    def backward(g):
+        dx, fx = x.grad_accum() if _need(x) else (None, 0)
+        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
+        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
+        check(lib().nnb_conv2d_bwd(_s(), N, Cin, H, W, Cout, kh, kw, stride, padding, _p(g), _p(x.data),
+                                   _p(weight.data), _p(alive), _p(dx), fx, _p(dw), fw, _p(db), fb))
+
+    return Value.node(y, (x, weight, bias), backward)
+
+
+def conv2d_relu(x: Value, weight: Value, bias: Value, stride: int, padding: int) -> Value:
+    return conv2d(x, weight, bias, stride, padding, fuse_relu=True)
+
+
+def maxpool2d(x: Value, kernel_size: int, stride: int) -> Value:
+    if len(x.shape) != 4 or kernel_size == 0 or stride == 0:
+        raise TensorShapeError("maxpool2d: bad input")
+    N, C, H, W = x.shape
+    if kernel_size > H or kernel_size > W:
+        raise TensorShapeError("maxpool2d: window larger than the input")
+    ho, wo = (H - kernel_size) // stride + 1, (W - kernel_size) // stride + 1
+    y = empty((N, C, ho, wo))
+    arg = empty((N, C, ho, wo), dtype=torch.int32)
+    check(lib().nnb_maxpool2d_fwd(_s(), N, C, H, W, kernel_size, stride, _p(x.data), _p(y), _p(arg)))
+
+    def backward(g):
+        dx, f = x.grad_accum()
+        check(lib().nnb_maxpool2d_bwd(_s(), N, C, H, W, kernel_size, stride, _p(g), _p(arg), _p(dx), f))
+
+    return Value.node(y, (x,), backward)
+
+
+# ---- embedding and losses -----------------------------------------------------------------------
+
+def embedding(weight: Value, ids: torch.Tensor) -> Value:
+    """ids: a CUDA int64 tensor of any shape; returns ids.shape + (D,) (ops.cpp:1991-2015)."""
+    if len(weight.shape) != 2:
+        raise TensorShapeError("embedding: weight must be 2-D")
+    V, D = weight.shape
+    cnt = ids.numel()
+    out = empty(tuple(ids.shape) + (D,))
+    check(lib().nnb_embedding_fwd(_s(), V, D, _p(weight.data), _p(ids), cnt, _p(out)))
+
+    def backward(g):
+        dw, f = weight.grad_accum()
+        check(lib().nnb_embedding_bwd(_s(), V, D, _p(ids), cnt, _p(g), _p(dw), f))
+
+    return Value.node(out, (weight,), backward)
+
+
+def cross_entropy_loss(logits: Value, targets: torch.Tensor) -> Value:
+    if len(logits.shape) != 2 or targets.dim() != 1 or targets.numel() != logits.shape[0]:
+        raise TensorShapeError("cross_entropy_loss: shapes do not agree")
+    N, C = logits.shape
+    sm, loss, norm = empty((N, C)), empty((1,)), empty((1,))
+    check(lib().nnb_cross_entropy_fwd(_s(), N, C, _p(logits.data), _p(targets), _p(sm), _p(loss), _p(norm)))
+
+    def backward(g):
+        dl, f = logits.grad_accum()
+        check(lib().nnb_cross_entropy_bwd(_s(), N, C, _p(sm), _p(targets), _p(g), _p(norm), _p(dl), f))
+
+    return Value.node(loss, (logits,), backward)
+
+
+def sequence_cross_entropy(logits: Value, targets: torch.Tensor, ignore_index: int = -100,
+                           label_smoothing: float = 0.0) -> Value:
+    if len(logits.shape) != 3 or tuple(targets.shape) != logits.shape[:2]:
+        raise TensorShapeError("sequence_cross_entropy: shapes do not agree")
+    N, T, V = logits.shape
+    P = N * T
+    sm, loss, norm = empty((P, V)), empty((1,)), empty((1,))
+    check(lib().nnb_sequence_ce_fwd(_s(), P, V, _p(logits.data), _p(targets), ignore_index,
+                                    ctypes.c_float(label_smoothing), _p(sm), _p(loss), _p(norm)))
+
+    def backward(g):
+        dl, f = logits.grad_accum()
+        check(lib().nnb_sequence_ce_bwd(_s(), P, V, _p(sm), _p(targets), ignore_index, ctypes.c_float(label_smoothing),
+                                        _p(g), _p(norm), _p(dl), f))
+
+    return Value.node(loss, (logits,), backward)

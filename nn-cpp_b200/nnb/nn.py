@@ -1,0 +1,294 @@
+"""Modules and the AdamW optimizer on the device, mirroring nn-cpp's nn modules (include/nn/nn/*.hpp)
+and optimizer (include/nn/optim/adamw.hpp).
+
+Structure, forward composition, parameter names and their order (named_parameters) follow the
+reference, so a checkpoint or a parameter list maps one to one:
+  Linear            src/nn/linear.cpp:18-26          weight [out, in], bias [out]
+  LayerNorm         src/nn/layernorm.cpp             gamma, beta
+  Embedding         src/nn/embedding.cpp             weight [V, D]
+  PositionalEncoding (sinusoidal) src/nn/positional.cpp:15-38
+  MultiHeadAttention src/nn/attention.cpp:15-48      q., k., v., o. (dropout 0: the fused attention op)
+  TransformerBlock  src/nn/transformer.cpp:37-55     ln1., attn., ln2., fc1., fc2.  (pre-LN)
+  Transformer       src/nn/transformer.cpp:66-90     embed., pos., blocks.<i>., ln_f., head.
+  Conv2d / Sequential (folds Conv2d + ReLU into conv2d_relu, src/nn/sequential.cpp:16-28)
+Initial values are drawn on the host from a seeded numpy generator with the reference's
+distributions (U(+-1/sqrt(fan_in)) weights, zero biases, LayerNorm gamma 1 / beta 0) and uploaded;
+to reproduce the reference's own numbers the tests load the same values into both.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import check, lib
+from . import functional as F
+from .autograd import Value
+
+
+def _param(array: np.ndarray, device) -> Value:
+    return Value.leaf(torch.from_numpy(np.ascontiguousarray(array, np.float32)).to(device), True)
+
+
+class Module:
+    def named_parameters(self) -> list[tuple[str, Value]]:
+        return []
+
+    def parameters(self) -> list[Value]:
+        return [p for _, p in self.named_parameters()]
+
+    def zero_grad(self) -> None:
+        for p in self.parameters():
+            p.zero_grad()
+
+    def load_parameters(self, arrays) -> None:
+        """Copies host arrays (in named_parameters order) into the parameters."""
+        params = self.parameters()
+        if len(arrays) != len(params):
+            raise ValueError("parameter count differs")
+        for p, a in zip(params, arrays):
+            t = torch.from_numpy(np.ascontiguousarray(a, np.float32).reshape(p.shape))
+            p.data.copy_(t, non_blocking=False)
+
+    def __call__(self, x):
+        return self.forward(x)
+
+
+class Linear(Module):
+    def __init__(self, in_features: int, out_features: int, rng: np.random.Generator, device):
+        lim = 1.0 / math.sqrt(in_features)
+        self.weight = _param(rng.uniform(-lim, lim, (out_features, in_features)), device)
+        self.bias = _param(np.zeros(out_features), device)
+
+    def forward(self, x: Value) -> Value:
+        return F.linear(x, self.weight, self.bias)
+
+    def named_parameters(self):
+        return [("weight", self.weight), ("bias", self.bias)]
+
+
+class LayerNorm(Module):
+    def __init__(self, dim: int, device, eps: float = 1e-5):
+        self.eps = eps
+        self.gamma = _param(np.ones(dim), device)
+        self.beta = _param(np.zeros(dim), device)
+
+    def forward(self, x: Value) -> Value:
+        return F.layernorm(x, self.gamma, self.beta, self.eps)
+
+    def named_parameters(self):
+        return [("gamma", self.gamma), ("beta", self.beta)]
+
+
+class Embedding(Module):
+    def __init__(self, num: int, dim: int, rng: np.random.Generator, device):
+        lim = 1.0 / math.sqrt(dim)
+        self.weight = _param(rng.uniform(-lim, lim, (num, dim)), device)
+
+    def forward(self, ids: torch.Tensor) -> Value:
+        return F.embedding(self.weight, ids)
+
+    def named_parameters(self):
+        return [("weight", self.weight)]
+
+
+def sinusoidal_table(max_len: int, dim: int) -> np.ndarray:
+    """positional.cpp:15-24: angle = pos / 10000^((c - c%2)/dim), sin on even c, cos on odd, in double."""
+    t = np.zeros((max_len, dim), np.float32)
+    for pos in range(max_len):
+        for c in range(dim):
+            angle = float(pos) / math.pow(10000.0, float(c - c % 2) / float(dim))
+            t[pos, c] = math.sin(angle) if c % 2 == 0 else math.cos(angle)
+    return t
+
+
+class PositionalEncoding(Module):
+    def __init__(self, max_len: int, dim: int, device):
+        self.max_len, self.dim = max_len, dim
+        self.pe = Value.leaf(torch.from_numpy(sinusoidal_table(max_len, dim)).to(device), False)
+
+    def forward(self, x: Value) -> Value:
+        if len(x.shape) != 3 or x.shape[1] > self.max_len or x.shape[2] != self.dim:
+            raise ValueError("PositionalEncoding: bad input shape")
+        return F.add(x, Value.leaf(self.pe.data[: x.shape[1]], False))
+
+
+class MultiHeadAttention(Module):
+    def __init__(self, dim: int, heads: int, causal: bool, rng, device):
+        if heads == 0 or dim % heads:
+            raise ValueError("MultiHeadAttention: dim must be divisible by heads")
+        self.heads, self.causal = heads, causal
+        self.q = Linear(dim, dim, rng, device)
+        self.k = Linear(dim, dim, rng, device)
+        self.v = Linear(dim, dim, rng, device)
+        self.o = Linear(dim, dim, rng, device)
+
+    def forward(self, x: Value) -> Value:
+        return self.o(F.attention(self.q(x), self.k(x), self.v(x), self.heads, None, self.causal))
+
+    def named_parameters(self):
+        out = []
+        for name, m in (("q.", self.q), ("k.", self.k), ("v.", self.v), ("o.", self.o)):
+            out += [(name + n, p) for n, p in m.named_parameters()]
+        return out
+
+
+class TransformerBlock(Module):
+    """x + attn(ln1(x)), then + fc2(gelu(fc1(ln2(.)))) (transformer.cpp:41-44); dropout 0 is the identity,
+    and fc1 + gelu run as one GEMM with the GELU in its epilogue."""
+
+    def __init__(self, dim: int, heads: int, mlp_ratio: int, causal: bool, rng, device):
+        self.ln1 = LayerNorm(dim, device)
+        self.attn = MultiHeadAttention(dim, heads, causal, rng, device)
+        self.ln2 = LayerNorm(dim, device)
+        self.fc1 = Linear(dim, mlp_ratio * dim, rng, device)
+        self.fc2 = Linear(mlp_ratio * dim, dim, rng, device)
+
+    def forward(self, x: Value) -> Value:
+        h = F.add(x, self.attn(self.ln1(x)))
+        return F.add(h, self.fc2(F.linear_gelu(self.ln2(h), self.fc1.weight, self.fc1.bias)))
+
+    def named_parameters(self):
+        out = []
+        for name, m in (("ln1.", self.ln1), ("attn.", self.attn), ("ln2.", self.ln2), ("fc1.", self.fc1),
+                        ("fc2.", self.fc2)):
+            out += [(name + n, p) for n, p in m.named_parameters()]
+        return out
+
+
+@dataclass
+class TransformerConfig:
+    """include/nn/nn/transformer.hpp:36-46 (sinusoidal positions, dropout 0)."""
+    vocab_size: int
+    dim: int
+    heads: int
+    layers: int
+    max_len: int
+    mlp_ratio: int = 4
+    causal: bool = True
+
+
+class Transformer(Module):
+    def __init__(self, c: TransformerConfig, seed: int = 0, device=None):
+        if c.dim == 0 or c.heads == 0 or c.mlp_ratio == 0 or c.dim % c.heads:
+            raise ValueError("Transformer: dim must be non-zero and divisible by heads")
+        if c.vocab_size == 0 or c.layers == 0 or c.max_len == 0:
+            raise ValueError("Transformer: sizes must be non-zero")
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        rng = np.random.default_rng(seed)
+        self.config = c
+        self.embed = Embedding(c.vocab_size, c.dim, rng, device)
+        self.pos = PositionalEncoding(c.max_len, c.dim, device)
+        self.blocks = [TransformerBlock(c.dim, c.heads, c.mlp_ratio, c.causal, rng, device) for _ in range(c.layers)]
+        self.ln_f = LayerNorm(c.dim, device)
+        self.head = Linear(c.dim, c.vocab_size, rng, device)
+
+    def forward(self, ids: torch.Tensor) -> Value:
+        h = self.pos(self.embed(ids))
+        for b in self.blocks:
+            h = b(h)
+        return self.head(self.ln_f(h))
+
+    def named_parameters(self):
+        out = [("embed." + n, p) for n, p in self.embed.named_parameters()]
+        for i, b in enumerate(self.blocks):
+            out += [(f"blocks.{i}." + n, p) for n, p in b.named_parameters()]
+        out += [("ln_f." + n, p) for n, p in self.ln_f.named_parameters()]
+        out += [("head." + n, p) for n, p in self.head.named_parameters()]
+        return out
+
+
+class Conv2d(Module):
+    def __init__(self, cin: int, cout: int, k: int, stride: int, padding: int, rng, device):
+        lim = 1.0 / math.sqrt(cin * k * k)
+        self.stride, self.padding = stride, padding
+        self.weight = _param(rng.uniform(-lim, lim, (cout, cin, k, k)), device)
+        self.bias = _param(np.zeros(cout), device)
+
+    def forward(self, x: Value) -> Value:
+        return F.conv2d(x, self.weight, self.bias, self.stride, self.padding)
+
+    def forward_relu(self, x: Value) -> Value:
+        return F.conv2d_relu(x, self.weight, self.bias, self.stride, self.padding)
+
+    def named_parameters(self):
+        return [("weight", self.weight), ("bias", self.bias)]
+
+
+class ReLU(Module):
+    def forward(self, x):
+        return F.relu(x)
+
+
+class MaxPool2d(Module):
+    def __init__(self, k: int, stride: int):
+        self.k, self.stride = k, stride
+
+    def forward(self, x):
+        return F.maxpool2d(x, self.k, self.stride)
+
+
+class Flatten(Module):
+    def forward(self, x):
+        return F.reshape(x, (x.shape[0], int(np.prod(x.shape[1:]))))
+
+
+class Sequential(Module):
+    """Runs layers in order; a Conv2d followed by a ReLU runs as one conv2d_relu (sequential.cpp:16-28)."""
+
+    def __init__(self, *layers):
+        self.layers = list(layers)
+
+    def forward(self, x):
+        i = 0
+        while i < len(self.layers):
+            layer = self.layers[i]
+            if isinstance(layer, Conv2d) and i + 1 < len(self.layers) and isinstance(self.layers[i + 1], ReLU):
+                x = layer.forward_relu(x)
+                i += 2
+                continue
+            x = layer(x)
+            i += 1
+        return x
+
+    def named_parameters(self):
+        out = []
+        for i, layer in enumerate(self.layers):
+            out += [(f"{i}.{n}", p) for n, p in layer.named_parameters()]
+        return out
+
+
+class AdamW:
+    """Decoupled weight decay then Adam (src/optim/adamw.cpp:15-24, src/optim/adam.cpp:24-43), one
+    fused kernel per parameter; the moment buffers start at zero."""
+
+    def __init__(self, params, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=1e-2):
+        self.params = list(params)
+        self.lr, self.beta1, self.beta2, self.eps, self.weight_decay = lr, beta1, beta2, eps, weight_decay
+        s = torch.cuda.current_stream().cuda_stream
+        self.m, self.v = [], []
+        for p in self.params:
+            for buf in (self.m, self.v):
+                t = torch.empty_like(p.data)
+                check(lib().nnb_fill(s, t.numel(), 0.0, t.data_ptr()))
+                buf.append(t)
+        self.t = 0
+
+    def zero_grad(self):
+        for p in self.params:
+            p.zero_grad()
+
+    def step(self):
+        import ctypes
+        self.t += 1
+        s = torch.cuda.current_stream().cuda_stream
+        for p, m, v in zip(self.params, self.m, self.v):
+            if p.grad_fresh:     # nothing reached this parameter: its gradient is all zeros
+                check(lib().nnb_fill(s, p.grad.numel(), 0.0, p.grad.data_ptr()))
+                p.grad_fresh = False
+            check(lib().nnb_adamw_step(s, p.data.numel(), p.data.data_ptr(), p.grad.data_ptr(), m.data_ptr(),
+                                       v.data_ptr(), ctypes.c_float(self.lr), ctypes.c_float(self.beta1),
+                                       ctypes.c_float(self.beta2), ctypes.c_float(self.eps),
+                                       ctypes.c_float(self.weight_decay), self.t))

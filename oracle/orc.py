@@ -72,6 +72,9 @@ _REF_SIGS = {
     "ref_time_matmul": ([_sz, _sz, _sz, _p, _p, _i], _d),
     "ref_time_sgemm": ([_sz, _sz, _sz, _p, _p, _p, _i], _d),
     "ref_matmul_nd": ([_p, _p, _i, _p, _p, _i, _i, _i, _p], _i),
+    "ref_transformer_train": ([_sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _f, _f, _i, _p, _p, _p],
+                              _c.c_longlong),
+    "ref_cnn_fwd_bwd": ([_sz, _p, _p, _p, _p, _p, _p], None),
     "ref_linear": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _p], None),
     "ref_layernorm": ([_sz, _sz, _p, _p, _p, _f, _p, _p, _p, _p, _p], None),
     "ref_batchnorm": ([_sz, _sz, _sz, _p, _p, _p, _f, _i, _p, _p, _p, _p, _p, _p, _p], None),

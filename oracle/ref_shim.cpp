@@ -12,6 +12,8 @@
 #include "nn/autograd/value.hpp"
 #include "nn/kernels/gemm.hpp"
 #include "nn/kernels/vmath.hpp"
+#include "nn/nn/sequential.hpp"
+#include "nn/nn/transformer.hpp"
 #include "nn/optim/adamw.hpp"
 #include "nn/kernels/parallel.hpp"
 #include "nn/tensor.hpp"
@@ -279,6 +281,88 @@ void ref_adamw(size_t n, float* w, const float* g, float lr, float b1, float b2,
 		opt.step();
 	}
 	copy_out(P.data(), w);
+}
+
+/*
+ * Builds nn::Transformer (src/nn/transformer.cpp) with the given parameters (flat, in
+ * named_parameters order), then runs `steps` training steps on one batch: zero_grad, forward,
+ * sequence_cross_entropy, backward, AdamW step. losses[s] gets each step's loss, grads the first
+ * step's gradients (flat), params_out the parameters after the last step. Returns the number of
+ * parameter floats, or -1 if the sizes do not match.
+ */
+long long ref_transformer_train(size_t vocab, size_t dim, size_t heads, size_t layers, size_t max_len, size_t N,
+		size_t T, const float* params_in, const int64_t* ids, const int64_t* targets, float lr, float wd, int steps,
+		float* losses, float* grads, float* params_out) {
+	nn::TransformerConfig c{vocab, dim, heads, layers, max_len};
+	nn::Transformer model(c);
+	std::vector<std::pair<std::string, Value>> named = model.named_parameters();
+	size_t off = 0;
+	for (auto& p : named) {
+		Tensor& d = p.second.data();
+		std::memcpy(d.data().data(), params_in + off, d.size() * sizeof(float));
+		off += d.size();
+	}
+	nn::AdamW opt(model.parameters(), lr, 0.9f, 0.999f, 1e-8f, wd);
+	Value idv = Value::leaf(ids_tensor({N, T}, ids), false);
+	Tensor tg = ids_tensor({N, T}, targets);
+	for (int st = 0; st < steps; ++st) {
+		opt.zero_grad();
+		Value logits = model.forward(idv);
+		Value loss = nn::sequence_cross_entropy(logits, tg);
+		loss.backward();
+		losses[st] = loss.data().data()[0];
+		if (st == 0 && grads) {
+			size_t g = 0;
+			for (auto& p : named) {
+				Tensor& gr = p.second.grad();
+				std::memcpy(grads + g, gr.data().data(), gr.size() * sizeof(float));
+				g += gr.size();
+			}
+		}
+		opt.step();
+	}
+	size_t o = 0;
+	for (auto& p : named) {
+		Tensor& d = p.second.data();
+		std::memcpy(params_out + o, d.data().data(), d.size() * sizeof(float));
+		o += d.size();
+	}
+	return static_cast<long long>(off);
+}
+
+/*
+ * The config-2 CNN (conv2d_relu 1->32, maxpool 2, conv2d_relu 32->64, maxpool 2, flatten,
+ * linear 3136->128, relu, linear 128->10, cross_entropy_loss) composed from the reference's ops,
+ * as Sequential runs it (src/nn/sequential.cpp:16-28): one forward and backward. params and grads
+ * are flat in order conv1.w, conv1.b, conv2.w, conv2.b, fc1.w, fc1.b, fc2.w, fc2.b.
+ */
+void ref_cnn_fwd_bwd(size_t N, const float* x, const int64_t* labels, const float* params, float* loss,
+		float* logits_out, float* grads) {
+	const std::vector<std::vector<size_t>> shapes = {{32, 1, 3, 3}, {32}, {64, 32, 3, 3}, {64}, {128, 3136}, {128},
+		{10, 128}, {10}};
+	std::vector<Value> P;
+	size_t off = 0;
+	for (const auto& sh : shapes) {
+		P.push_back(leaf(sh, params + off));
+		off += count_of(sh);
+	}
+	Value X = Value::leaf(tensor({N, 1, 28, 28}, x), false);
+	Value h = nn::conv2d_relu(X, P[0], P[1], 1, 1);
+	h = nn::maxpool2d(h, 2, 2);
+	h = nn::conv2d_relu(h, P[2], P[3], 1, 1);
+	h = nn::maxpool2d(h, 2, 2);
+	h = nn::reshape(h, {N, 3136});
+	h = nn::relu(nn::linear(h, P[4], P[5]));
+	Value logits = nn::linear(h, P[6], P[7]);
+	Value L = nn::cross_entropy_loss(logits, ids_tensor({N}, labels));
+	L.backward();
+	copy_out(L.data(), loss);
+	copy_out(logits.data(), logits_out);
+	size_t g = 0;
+	for (const Value& p : P) {
+		copy_out(p.grad(), grads + g);
+		g += p.data().size();
+	}
 }
 
 }  // extern "C"

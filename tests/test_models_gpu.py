@@ -1,0 +1,173 @@
+"""End-to-end training steps on the GPU against the reference's own modules.
+
+- Transformer (config 5's architecture at a small size): nnb's Transformer + AdamW and the
+  reference's nn::Transformer + nn::AdamW (oracle/_ref) start from the same parameters and train on
+  the same batch; losses, first-step gradients and the parameters after three steps agree to fp32
+  tolerance. Training twice gives the same bits (tests/test_transformer.cpp:464), and the
+  virtual-shard data-parallel step gives the same bits whatever the shard placement.
+- CNN (config 2, full size): the Sequential conv/pool/linear stack and cross entropy, one forward and
+  backward, against the reference's ops composed the same way.
+"""
+import numpy as np
+import pytest
+
+from oracle import orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _flat(model):
+    return np.concatenate([p.data.cpu().numpy().ravel() for p in model.parameters()])
+
+
+def _flat_grads(model):
+    return np.concatenate([p.grad.cpu().numpy().ravel() for p in model.parameters()])
+
+
+def _close(got, want, rel):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    scale = np.abs(want).max()
+    err = np.abs(got - want).max()
+    assert err <= rel * scale, f"max err {err:.3e} vs scale {scale:.3e}"
+
+
+def _batch(torch, vocab, N, T, seed):
+    ids = orc.integers(seed, N * (T + 1), 0, vocab - 1).reshape(N, T + 1)
+    x, y = ids[:, :T].copy(), ids[:, 1:].copy()          # next-token targets
+    return x, y, torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()
+
+
+def _train(torch, cfg, x_d, y_d, steps, lr, wd, shards=1, seed=3):
+    from nnb.nn import AdamW, Transformer
+    from nnb.train import ShardedTrainer
+
+    model = Transformer(cfg, seed=seed)
+    opt = AdamW(model.parameters(), lr=lr, weight_decay=wd)
+    tr = ShardedTrainer(model, opt, shards=shards)
+    losses, grads = [], None
+    for s in range(steps):
+        loss = tr.step(x_d, y_d)
+        losses.append(float(loss.cpu()[0]))
+        if s == 0:
+            grads = tr.reduced.cpu().numpy().copy()
+    return model, losses, grads
+
+
+def test_transformer_training_matches_reference(cuda):
+    torch = cuda
+    ref = orc.ref()
+    if ref is None:
+        pytest.skip("reference library not built (oracle/_ref)")
+    from nnb.nn import Transformer, TransformerConfig
+
+    cfg = TransformerConfig(vocab_size=64, dim=32, heads=4, layers=2, max_len=16)
+    N, T, steps, lr, wd = 4, 16, 3, 1e-2, 1e-2
+    x, y, x_d, y_d = _batch(torch, 64, N, T, 90)
+    init = _flat(Transformer(cfg, seed=3))
+    model, losses, grads = _train(torch, cfg, x_d, y_d, steps, lr, wd, shards=1, seed=3)
+
+    r_losses = np.zeros(steps, np.float32)
+    r_grads = np.zeros_like(init)
+    r_params = np.zeros_like(init)
+    n = ref.ref_transformer_train(64, 32, 4, 2, 16, N, T, orc.ptr(init), orc.ptr(x), orc.ptr(y), lr, wd, steps,
+                                  orc.ptr(r_losses), orc.ptr(r_grads), orc.ptr(r_params))
+    assert n == init.size
+    np.testing.assert_allclose(losses, r_losses, rtol=1e-5)
+    _close(grads, r_grads, 1e-4)
+    # Adam moves an element whose gradient is rounding noise by about +-lr per step whatever the
+    # noise's size, so the parameters after the steps are compared as: all within the Adam step
+    # bound (2 lr per step), and all but a sliver (elements with near-zero gradients) to 1e-5.
+    got = _flat(model).astype(np.float64)
+    err = np.abs(got - r_params)
+    assert err.max() <= 2 * lr * steps
+    tight = err <= 1e-5 * np.abs(r_params).max()
+    assert tight.mean() > 0.995, tight.mean()
+    assert losses[-1] < losses[0]
+
+
+def test_transformer_training_deterministic_and_shard_invariant(cuda):
+    torch = cuda
+    from nnb.nn import TransformerConfig
+
+    cfg = TransformerConfig(vocab_size=96, dim=64, heads=4, layers=2, max_len=32)
+    _, _, x_d, y_d = _batch(torch, 96, 8, 32, 91)
+    m1, l1, _ = _train(torch, cfg, x_d, y_d, 2, 3e-3, 1e-2, shards=8)
+    m2, l2, _ = _train(torch, cfg, x_d, y_d, 2, 3e-3, 1e-2, shards=8)
+    assert _flat(m1).tobytes() == _flat(m2).tobytes()
+    assert l1 == l2
+    # the same 8 shards, owned as if by ranks 0..3 of a 4-GPU job, each gathered: emulate one rank at a time
+    from nnb.nn import AdamW, Transformer
+    from nnb.train import ShardedTrainer
+
+    m3 = Transformer(cfg, seed=3)
+    opt = AdamW(m3.parameters(), lr=3e-3, weight_decay=1e-2)
+    trainers = [ShardedTrainer(m3, opt, shards=8, world=4, rank=r) for r in range(4)]
+    s = torch.cuda.current_stream().cuda_stream
+    import nnb
+    for _ in range(2):
+        full = torch.empty(8, trainers[0].total, device="cuda")
+        losses = torch.empty(8, device="cuda")
+        for r, tr in enumerate(trainers):    # each "rank" computes its two shards
+            B, per = x_d.shape[0], x_d.shape[0] // 8
+            from nnb import functional as F
+            for j, sh in enumerate(tr.owned):
+                tr._point_grads(tr.shard_grads[j])
+                logits = m3(x_d[sh * per:(sh + 1) * per])
+                loss = F.sequence_cross_entropy(logits, y_d[sh * per:(sh + 1) * per])
+                loss.backward(tr.seed)
+                full[sh].copy_(tr.shard_grads[j])
+                losses[sh] = loss.data[0]
+        t0 = trainers[0]
+        nnb.check(nnb.lib().nnb_column_sum(s, 8, t0.total, full.data_ptr(), t0.reduced.data_ptr(), 1))
+        t0._point_grads(t0.reduced)
+        for p in t0.params:
+            p.grad_fresh = False
+        opt.step()
+    assert _flat(m3).tobytes() == _flat(m1).tobytes()
+
+
+def test_cnn_forward_backward_matches_reference(cuda):
+    torch = cuda
+    ref = orc.ref()
+    if ref is None:
+        pytest.skip("reference library not built (oracle/_ref)")
+    import nnb.functional as F
+    from nnb.autograd import Value
+    from nnb.nn import Conv2d, Flatten, Linear, MaxPool2d, ReLU, Sequential
+
+    rng = np.random.default_rng(5)
+    dev = torch.device("cuda")
+    net = Sequential(Conv2d(1, 32, 3, 1, 1, rng, dev), ReLU(), MaxPool2d(2, 2), Conv2d(32, 64, 3, 1, 1, rng, dev),
+                     ReLU(), MaxPool2d(2, 2), Flatten(), Linear(3136, 128, rng, dev), ReLU(), Linear(128, 10, rng, dev))
+    N = 64
+    x = orc.uniform(50, N * 784, 0.0, 1.0).reshape(N, 1, 28, 28)
+    labels = orc.integers(51, N, 0, 9)
+    params = np.concatenate([p.data.cpu().numpy().ravel() for p in net.parameters()])
+    net.zero_grad()
+    logits = net(Value.leaf(torch.from_numpy(x).cuda(), False))
+    loss = F.cross_entropy_loss(logits, torch.from_numpy(labels).cuda())
+    loss.backward()
+    grads = np.concatenate([p.grad.cpu().numpy().ravel() for p in net.parameters()])
+
+    r_loss, r_logits, r_grads = np.zeros(1, np.float32), np.zeros((N, 10), np.float32), np.zeros_like(params)
+    ref.ref_cnn_fwd_bwd(N, orc.ptr(x), orc.ptr(labels), orc.ptr(params), orc.ptr(r_loss), orc.ptr(r_logits),
+                        orc.ptr(r_grads))
+    _close(logits.data.cpu().numpy(), r_logits, 1e-4)     # logits are small sums of larger terms
+    np.testing.assert_allclose(float(loss.data.cpu()[0]), float(r_loss[0]), rtol=1e-5)
+    # The forward agrees to fp32 GEMM accuracy (the 3xTF32 product's error grows with the depth,
+    # about 2e-5 of fc1's output at K = 3136), which is enough to move a handful of the 8192 ReLU
+    # decisions after fc1 that sit within ~5e-6 of zero; each moved decision routes a gradient g
+    # instead of 0 and shifts every gradient upstream of it by about 2% of its norm. The gradients
+    # are therefore compared by relative norm against the reference (the exact backward, with
+    # shared masks, is checked op by op in tests/test_ops_gpu.py), and the last layer, which no
+    # ReLU decision precedes in the backward pass, element by element.
+    off = 0
+    names = [n for n, _ in net.named_parameters()]
+    for name, p in zip(names, net.parameters()):
+        n = p.data.numel()
+        g, r = grads[off:off + n].astype(np.float64), r_grads[off:off + n].astype(np.float64)
+        off += n
+        rel = np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)
+        assert rel <= 6e-2, (name, rel)
+        if name.startswith("9."):                  # the last Linear layer
+            _close(g, r, 2e-3)

@@ -324,7 +324,15 @@ def test_embedding_bitwise(cuda):
     out = torch.empty(cnt, D, device="cuda")
     dw = dev(torch, dw_init)
     ok(lib().nnb_embedding_fwd(S(torch), V, D, tw.data_ptr(), ti.data_ptr(), cnt, out.data_ptr()))
-    ok(lib().nnb_embedding_bwd(S(torch), V, D, ti.data_ptr(), cnt, tg.data_ptr(), dw.data_ptr()))
+    ok(lib().nnb_embedding_bwd(S(torch), V, D, ti.data_ptr(), cnt, tg.data_ptr(), dw.data_ptr(), 0))
+    assert_bits(host(dw), dw_o)
+    # first: rows start from zero (ids 100.. get no token, so they become exactly 0)
+    dz = orc.zeros(V, D)
+    O.orc_embedding_bwd(D, P(ids), cnt, P(g), P(dz))
+    ok(lib().nnb_embedding_bwd(S(torch), V, D, ti.data_ptr(), cnt, tg.data_ptr(), dw.data_ptr(), 1))
+    assert_bits(host(dw), dz)
+    dw = dev(torch, dw_init)
+    ok(lib().nnb_embedding_bwd(S(torch), V, D, ti.data_ptr(), cnt, tg.data_ptr(), dw.data_ptr(), 0))
     assert_bits(host(out), out_o)
     assert_bits(host(dw), dw_o)
 
