@@ -53,6 +53,10 @@ def parse_args():
     ap.add_argument("--mode", choices=("fp32x3", "tf32"), default="fp32x3")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("all", "gemm", "transformer"), default="all",
+                    help="gemm: config 4 only; transformer: config 5 only; all: config 4 line with config 5 inside")
+    ap.add_argument("--t-steps", type=int, default=10, help="timed transformer steps")
+    ap.add_argument("--t-warmup", type=int, default=3)
     return ap.parse_args()
 
 
@@ -336,6 +340,11 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
         torch.backends.cuda.matmul.allow_tf32 = False
         cublas_tf32 = 2.0 * rows * size * size / (e0.elapsed_time(e1) / 20 * 1e-3) / 1e12
 
+    transformer = None
+    if args.workload == "all":
+        del a, b, c, a_h, b_h, c_h
+        torch.cuda.empty_cache()
+        transformer = run_transformer(args.t_steps, args.t_warmup, rank, world, local_rank)
     if rank != 0:
         return
     flops = 2.0 * size ** 3
@@ -375,9 +384,100 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
         "gpu_launches": int(launches),
         "clocks": clk,
     }
+    if transformer is not None:
+        line["transformer"] = transformer
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(size)
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------
+# Config 5: transformer training step (tokens/s)
+# ---------------------------------------------------------------------------------------------
+
+T5 = dict(vocab_size=4096, dim=512, heads=8, layers=4, max_len=512, batch=64, seq=512)
+# algorithmic work per step (causal-effective attention): 88.08 MFLOP/token of matmuls (forward +
+# backward) and 6.30 MFLOP/token of attention over 32768 tokens
+T5_FLOP_PER_STEP = 3.093e12
+
+
+def run_transformer(steps: int, warmup: int, rank: int, world: int, local_rank: int, group=None):
+    """One config-5 step = forward, sequence cross entropy, backward and AdamW on the global batch
+    of 64 x 512 tokens, cut into 8 virtual shards spread over the ranks (nnb.train)."""
+    import torch
+
+    import nnb
+    from nnb.nn import AdamW, Transformer, TransformerConfig
+    from nnb.train import ShardedTrainer
+
+    dev = torch.device("cuda", local_rank)
+    cfg = TransformerConfig(T5["vocab_size"], T5["dim"], T5["heads"], T5["layers"], T5["max_len"])
+    model = Transformer(cfg, seed=0, device=dev)
+    opt = AdamW(model.parameters(), lr=3e-4, weight_decay=1e-2)
+    tr = ShardedTrainer(model, opt, shards=8, world=world, rank=rank, group=group)
+    g = torch.Generator().manual_seed(11)
+    ids_h = torch.randint(0, T5["vocab_size"], (T5["batch"], T5["seq"] + 1), generator=g)
+    x_h = ids_h[:, :-1].contiguous().pin_memory()
+    y_h = ids_h[:, 1:].contiguous().pin_memory()
+    x_d, y_d = x_h.to(dev), y_h.to(dev)
+    loss_h = torch.empty(1).pin_memory()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(warmup):
+        tr.step(x_d, y_d)
+    torch.cuda.synchronize()
+    first_loss = float(tr.loss.cpu()[0])
+    nnb.trace_reset()
+    nnb.trace_enable(True)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        tr.step(x_d, y_d)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    nnb.trace_enable(False)
+    launches = nnb.launch_count()
+    kinds = {name: nnb.trace_query(k) for name, k in (("gemm", nnb.TRACE_GEMM), ("pack", nnb.TRACE_PACK),
+                                                      ("rowwise", nnb.TRACE_ROWWISE), ("attention", nnb.TRACE_ATTENTION),
+                                                      ("aux", nnb.TRACE_AUX))}
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+    # end to end: ids and targets from pinned host memory every step, the loss read back every step
+    e0.record()
+    for _ in range(steps):
+        x_d.copy_(x_h, non_blocking=True)
+        y_d.copy_(y_h, non_blocking=True)
+        loss = tr.step(x_d, y_d)
+        loss_h.copy_(loss, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    tokens = T5["batch"] * T5["seq"]
+    ms_v = ms.item()
+    return {
+        "metric": "transformer train tokens/s", "value": tokens / (ms_v * 1e-3), "unit": "tokens/s",
+        "ms_per_step": ms_v, "steps": steps, "warmup": warmup, "scaling": "strong",
+        "config": {"workload": "config 5: 4 pre-LN blocks, d 512, 8 heads, FFN 2048 GELU, vocab 4096, seq 512, "
+                               "global batch 64, sequence CE, AdamW 3e-4",
+                   "parallelism": f"data parallel x{world}, 8 virtual shards, fixed-order gradient sum",
+                   "math_mode": "fp32x3"},
+        "algorithmic_tflops": T5_FLOP_PER_STEP / (ms_v * 1e-3) / 1e12,
+        "loss_after_warmup": first_loss, "loss_final": float(tr.loss.cpu()[0]),
+        "kernel_ms_per_step": {k: v[0] / steps for k, v in kinds.items()},
+        "gpu_launches": int(launches),
+        "e2e": {"value": tokens / (e2e.item() * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": int(x_h.numel() * 8 * 2), "d2h_bytes_per_step": 4},
+    }
 
 
 def main():
@@ -396,7 +496,14 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_nnb(args, rank, world, local_rank)
+        if args.workload == "transformer":
+            t = run_transformer(args.t_steps, args.t_warmup, rank, world, local_rank)
+            if rank == 0:
+                t.update({"n_gpus": world, "higher_is_better": True, "vs_baseline": None, "dtype": "tf32x3",
+                          "data": "synthetic token ids (torch generator, fixed seed)"})
+                print(json.dumps(t), flush=True)
+        else:
+            run_nnb(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -138,6 +138,15 @@ NNB_API nnb_status nnb_linear_gelu_fwd(void* stream, size_t M, size_t K, size_t 
  * chunks, then over chunks; the reference's serial order whenever M <= 256). */
 NNB_API nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const float* g, const float* x,
 		const float* w, float* dx, int dx_first, float* dw, int dw_first, float* db, int db_first);
+/* nnb_linear_bwd whose weight and bias gradients are kept per group: the M rows are `groups`
+ * consecutive groups, and group z's dW (n x K) and db (n) are computed from its rows only (one
+ * batched launch) into dw + z*dw_stride and db + z*db_stride (a stride of 0 packs the groups
+ * back to back). dx covers all rows. The data-parallel step uses one group per virtual shard so
+ * that the shard sum can be taken in a fixed order. No reference counterpart: the reference has no
+ * distributed training. */
+NNB_API nnb_status nnb_linear_bwd_grouped(void* stream, size_t M, size_t K, size_t n, size_t groups, const float* g,
+		const float* x, const float* w, float* dx, int dx_first, float* dw, size_t dw_stride, int dw_first, float* db,
+		size_t db_stride, int db_first);
 /* out[j] (+)= sum_r g[r][j] in the order above (Tensor::sum(0), src/tensor.cpp:422-455). */
 NNB_API nnb_status nnb_column_sum(void* stream, size_t rows, size_t cols, const float* g, float* out, int first);
 
@@ -151,6 +160,11 @@ NNB_API nnb_status nnb_layernorm_fwd(void* stream, size_t R, size_t D, const flo
 NNB_API nnb_status nnb_layernorm_bwd(void* stream, size_t R, size_t D, const float* g, const float* x,
 		const float* gamma, const float* mean, const float* inv_std, float* dx, int dx_first, float* dgamma,
 		int dgamma_first, float* dbeta, int dbeta_first);
+/* layernorm backward with dgamma/dbeta kept per group of R/groups consecutive rows, group z at
+ * dgamma + z*dgamma_stride (0: back to back); see nnb_linear_bwd_grouped. */
+NNB_API nnb_status nnb_layernorm_bwd_grouped(void* stream, size_t R, size_t D, size_t groups, const float* g,
+		const float* x, const float* gamma, const float* mean, const float* inv_std, float* dx, int dx_first,
+		float* dgamma, size_t dgamma_stride, int dgamma_first, float* dbeta, size_t dbeta_stride, int dbeta_first);
 /* Training-mode batchnorm over [N, C, S] (ops.hpp:114; ops.cpp:900-961): per-channel statistics with
  * the reference's fp64 sums of 8-lane partials; fuse_relu folds a ReLU and writes its 1-byte alive
  * mask; mean, var (biased) and inv_std (C each) are written. */
@@ -204,6 +218,8 @@ NNB_API nnb_status nnb_gelu_bwd(void* stream, size_t n, const float* x, const fl
 		float* dx, int dx_first);
 /* y[0..n) = value (Tensor(shape, fill) / Tensor::zeros, include/nn/tensor.hpp:147,354). */
 NNB_API nnb_status nnb_fill(void* stream, size_t n, float value, float* y);
+/* y = alpha * x (Tensor scale, src/tensor.cpp:558-566). */
+NNB_API nnb_status nnb_scale(void* stream, size_t n, float alpha, const float* x, float* y);
 /* y = a + b, b repeated every b_period elements (add with a broadcast leading axis, ops.cpp:331). */
 NNB_API nnb_status nnb_add_fwd(void* stream, size_t n, const float* a, const float* b, size_t b_period, float* y);
 /* dst (+)= src or (-)= src with the grad_accum convention (ops.cpp:77-92, add_to_grad). */
@@ -235,6 +251,10 @@ NNB_API nnb_status nnb_embedding_fwd(void* stream, size_t V, size_t D, const flo
 		size_t count, float* out);
 NNB_API nnb_status nnb_embedding_bwd(void* stream, size_t V, size_t D, const int64_t* ids, size_t count,
 		const float* g, float* dweight, int first);
+/* embedding backward per group of count/groups consecutive ids, group z into
+ * dweight + z*dweight_stride (0: V*D). */
+NNB_API nnb_status nnb_embedding_bwd_grouped(void* stream, size_t V, size_t D, size_t groups, const int64_t* ids,
+		size_t count, const float* g, float* dweight, size_t dweight_stride, int first);
 /* One AdamW step on one parameter (src/optim/adamw.cpp:15-24 then src/optim/adam.cpp:24-43);
  * step counts from 1 (the value of Adam::t_ after its increment). */
 NNB_API nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float* g, float* m, float* v, float lr,

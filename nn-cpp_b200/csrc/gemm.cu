@@ -589,27 +589,28 @@ static nnb_status validate(const GemmDesc& d) {
 namespace gemm {
 
 // Depth cut (the counterpart of the reference's `blocked`, src/kernels/gemm.cpp:453-485): a product
-// whose output has too few tiles to occupy the machine but a long depth -- a weight gradient, a
-// 512 x 512 output summed over tens of thousands of rows -- is computed as P products over
-// consecutive depth pieces into separate buffers, which one kernel then adds in piece order. P
-// depends only on (m, n, k): it is planned for a fixed 148-SM machine, never for the device, the
-// grid or the number of GPUs, so the result is the same wherever it runs.
-constexpr long long kCutSMs = 148;
+// with a long depth relative to its output width -- a weight gradient, a 512 x 512 output summed over
+// thousands of rows -- is computed as P products over consecutive depth pieces into separate buffers,
+// which one kernel then adds in piece order. P is planned from (n, k) alone: never from m, the batch,
+// the device, the grid or the number of GPUs. A row of C therefore gets the same sequence of
+// operations however many rows the call has, which keeps row-sharded products (and the data-parallel
+// training step) bitwise identical at any GPU count.
 constexpr long long kCutMinDepth = 1024;
+constexpr long long kCutMaxPieces = 32;
 
 static int depth_pieces(const GemmDesc& d) {
-	if (d.batch_outer * d.batch_inner != 1 || d.epi.bias_mode != kBiasNone || d.epi.act != kActNone) return 1;
-	const int bn = choose_bn(d.n);
-	const long long tiles = ((d.m + kBM - 1) / kBM) * ((d.n + bn - 1) / bn);
-	if (tiles * 2 > kCutSMs) return 1;
-	const long long p = std::min<long long>(d.k / kCutMinDepth, (kCutSMs + tiles - 1) / tiles);
+	if (d.batch_inner != 1 || d.epi.bias_mode != kBiasNone || d.epi.act != kActNone) return 1;
+	const long long p = std::min<long long>(kCutMaxPieces, d.k / std::max<long long>(kCutMinDepth, 4 * d.n));
 	return p >= 2 ? (int)p : 1;
 }
 
-// c = (accumulate ? c : 0) + (((part_0 + part_1) + part_2) + ...), part_p an m x n slab
+// c_e = (accumulate ? c_e : 0) + (((part_e0 + part_e1) + part_e2) + ...), part_ep an m x n slab;
+// entry e = blockIdx.y, c_e = c + e * sc
 __global__ void depth_sum_kernel(const float* __restrict__ part, int pieces, long long m, long long n,
-		float* __restrict__ c, long long ldc, int accumulate) {
+		float* __restrict__ c, long long ldc, long long sc, int accumulate) {
 	const long long mn = m * n;
+	part += (long long)blockIdx.y * pieces * mn;
+	c += (long long)blockIdx.y * sc;
 	for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < mn;
 			idx += (long long)gridDim.x * blockDim.x) {
 		float acc = part[idx];
@@ -636,29 +637,35 @@ static nnb_status gemm_depth_cut(cudaStream_t s, const DeviceState* dev, const G
 	const long long kp = round_up((d.k + pieces - 1) / pieces, kBK);
 	pieces = (int)((d.k + kp - 1) / kp);
 	const long long full = d.k / kp;                      // pieces of exactly kp
-	const long long mn = d.m * d.n;
+	const long long mn = d.m * d.n, E = d.batch_outer;
+	if (E > 65535) return fail(NNB_ERR_UNSUPPORTED, "gemm: more than 65535 batch entries");
 	void* ws = nullptr;
-	NNB_TRY(scratch_alloc(&ws, (size_t)pieces * mn * sizeof(float), s));
+	NNB_TRY(scratch_alloc(&ws, (size_t)E * pieces * mn * sizeof(float), s));
 	float* part = static_cast<float*>(ws);
 	const long long a_step = d.ta ? kp * d.lda : kp, b_step = d.tb ? kp : kp * d.ldb;
 	nnb_status st = NNB_OK;
 	do {
-		GemmDesc e = d;
+		GemmDesc e = d;                                     // entries x full pieces, two-level batch
 		e.k = kp; e.c = part; e.ldc = d.n; e.accumulate = 0;
-		e.batch_outer = full; e.batch_inner = 1;
-		e.sa_outer = a_step; e.sb_outer = b_step; e.sc_outer = mn;
+		e.batch_outer = E; e.batch_inner = full;
+		e.sa_outer = d.sa_outer; e.sa_inner = a_step;
+		e.sb_outer = d.sb_outer; e.sb_inner = b_step;
+		e.sc_outer = (long long)pieces * mn; e.sc_inner = mn;
 		if ((st = gemm_direct(s, dev, e)) != NNB_OK) break;
-		if (full < pieces) {                                 // the shorter last piece
+		if (full < pieces) {                                 // the shorter last piece of every entry
 			GemmDesc t = d;
 			t.k = d.k - full * kp;
 			t.a = d.a + full * a_step; t.b = d.b + full * b_step;
 			t.c = part + full * mn; t.ldc = d.n; t.accumulate = 0;
+			t.batch_outer = E; t.batch_inner = 1;
+			t.sc_outer = (long long)pieces * mn;
 			if ((st = gemm_direct(s, dev, t)) != NNB_OK) break;
 		}
 		const unsigned blocks = (unsigned)std::min<long long>((mn + 255) / 256, 148 * 16);
 		{
 			TraceScope ts(s, kTraceAux);
-			depth_sum_kernel<<<blocks, 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc, d.accumulate);
+			depth_sum_kernel<<<dim3(blocks, (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc, d.sc_outer,
+				d.accumulate);
 		}
 		st = cuda_status(cudaGetLastError(), "depth sum launch");
 	} while (0);

@@ -9,6 +9,9 @@ namespace nnb {
 
 // out[j] (+)= sum over rows of g[r][j] in the fixed chunked order of ops_linear.cu.
 nnb_status colsum(cudaStream_t s, const float* g, long long rows, long long cols, float* out, int first);
+// The same per group of rows/groups consecutive rows: out[z*out_stride + j] (+)= sum over group z's rows.
+nnb_status colsum_grouped(cudaStream_t s, const float* g, long long rows, long long cols, long long groups, float* out,
+		long long out_stride, int first);
 
 // Elementwise ceiling for 1-D grids: enough blocks for n items, at most 148 * 64 blocks.
 inline unsigned grid_for(long long n, int threads) {

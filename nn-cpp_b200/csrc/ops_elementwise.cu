@@ -58,6 +58,10 @@ __global__ void fill_kernel(long long n, float value, float* __restrict__ y) {
 	GRID_STRIDE(i, n) y[i] = value;
 }
 
+__global__ void scale_kernel(long long n, float alpha, const float* __restrict__ x, float* __restrict__ y) {
+	GRID_STRIDE(i, n) y[i] = x[i] * alpha;                      // Tensor scale, src/tensor.cpp:558-566
+}
+
 // y = a + b with b broadcast along the leading axis when b_period < n (b has b_period elements)
 __global__ void add_kernel(long long n, const float* __restrict__ a, const float* __restrict__ b, long long b_period,
 		float* __restrict__ y) {
@@ -423,6 +427,14 @@ nnb_status nnb_fill(void* stream, size_t n, float value, float* y) {
 	return nnb::cuda_status(cudaGetLastError(), "fill launch");
 }
 
+nnb_status nnb_scale(void* stream, size_t n, float alpha, const float* x, float* y) {
+	if (n == 0) return NNB_OK;
+	if (!x || !y) return nnb::fail(NNB_ERR_INVALID, "scale: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::scale_kernel, (long long)n, alpha, x, y);
+	return nnb::cuda_status(cudaGetLastError(), "scale launch");
+}
+
 nnb_status nnb_add_fwd(void* stream, size_t n, const float* a, const float* b, size_t b_period, float* y) {
 	if (n == 0) return NNB_OK;
 	if (!a || !b || !y) return nnb::fail(NNB_ERR_INVALID, "add_fwd: null pointer");
@@ -574,6 +586,17 @@ nnb_status nnb_embedding_bwd(void* stream, size_t V, size_t D, const int64_t* id
 	}
 	nnb_status st2 = nnb::scratch_free(ws, s);
 	return st != NNB_OK ? st : st2;
+}
+
+nnb_status nnb_embedding_bwd_grouped(void* stream, size_t V, size_t D, size_t groups, const int64_t* ids, size_t count,
+		const float* g, float* dweight, size_t dweight_stride, int first) {
+	if (groups == 0 || count % groups != 0)
+		return nnb::fail(NNB_ERR_SHAPE, "embedding_bwd_grouped: %zu ids in %zu groups", count, groups);
+	const size_t per = count / groups;
+	for (size_t z = 0; z < groups; ++z)
+		NNB_TRY(nnb_embedding_bwd(stream, V, D, ids + z * per, per, g + z * per * D,
+			dweight + z * (dweight_stride ? dweight_stride : V * D), first));
+	return NNB_OK;
 }
 
 nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float* g, float* m, float* v, float lr, float beta1,

@@ -23,49 +23,61 @@ namespace {
 
 constexpr int kColChunk = 256;
 
-// partial[c][j] = sum over rows [c*kColChunk, ...) of g[r][j], serial from +0.
+// partial[z][c][j] = sum over rows [c*kColChunk, ...) of group z of g[r][j], serial from +0.
 __global__ void colsum_partial_kernel(const float* __restrict__ g, long long rows, long long cols,
 		float* __restrict__ partial) {
 	const long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-	const long long c = blockIdx.y;
+	const long long c = blockIdx.y, chunks = gridDim.y, z = blockIdx.z;
 	if (j >= cols) return;
+	const float* gz = g + z * rows * cols;
 	const long long r0 = c * kColChunk, r1 = min(rows, r0 + kColChunk);
 	float s = 0.0f;
-	for (long long r = r0; r < r1; ++r) s += g[r * cols + j];
-	partial[c * cols + j] = s;
+	for (long long r = r0; r < r1; ++r) s += gz[r * cols + j];
+	partial[(z * chunks + c) * cols + j] = s;
 }
 
-// out[j] = (first ? 0 : out[j]) + sum_c partial[c][j] (serial from +0 in chunk order).
+// out[z*out_stride + j] = (first ? 0 : out[..]) + sum_c partial[z][c][j] (serial from +0 in chunk order).
 __global__ void colsum_final_kernel(const float* __restrict__ partial, long long chunks, long long cols,
-		float* __restrict__ out, int first) {
+		float* __restrict__ out, long long out_stride, int first) {
 	const long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	const long long z = blockIdx.y;
 	if (j >= cols) return;
+	const float* pz = partial + z * chunks * cols;
 	float s = 0.0f;
-	for (long long c = 0; c < chunks; ++c) s += partial[c * cols + j];
-	out[j] = first ? s + 0.0f : out[j] + s;
+	for (long long c = 0; c < chunks; ++c) s += pz[c * cols + j];
+	float* o = out + z * out_stride + j;
+	*o = first ? s + 0.0f : *o + s;
 }
 
 }  // namespace
 
 nnb_status colsum(cudaStream_t s, const float* g, long long rows, long long cols, float* out, int first) {
-	if (cols == 0) return NNB_OK;
+	return colsum_grouped(s, g, rows, cols, 1, out, cols, first);
+}
+
+nnb_status colsum_grouped(cudaStream_t s, const float* g, long long rows, long long cols, long long groups, float* out,
+		long long out_stride, int first) {
+	if (cols == 0 || groups == 0) return NNB_OK;
+	if (rows % groups != 0) return fail(NNB_ERR_SHAPE, "column sum: %lld rows do not split into %lld groups", rows, groups);
+	rows /= groups;                                   // rows per group
 	if (rows == 0) {
-		if (first) NNB_CUDA_TRY(cudaMemsetAsync(out, 0, cols * sizeof(float), s));
+		if (first)
+			for (long long z = 0; z < groups; ++z) NNB_CUDA_TRY(cudaMemsetAsync(out + z * out_stride, 0, cols * sizeof(float), s));
 		return NNB_OK;
 	}
 	const long long chunks = (rows + kColChunk - 1) / kColChunk;
-	if (chunks > 65535) return fail(NNB_ERR_UNSUPPORTED, "column sum over more than %lld rows", 65535ll * kColChunk);
+	if (chunks > 65535 || groups > 65535) return fail(NNB_ERR_UNSUPPORTED, "column sum too large for one launch");
 	void* ws = nullptr;
-	NNB_TRY(scratch_alloc(&ws, chunks * cols * sizeof(float), s));
+	NNB_TRY(scratch_alloc(&ws, groups * chunks * cols * sizeof(float), s));
 	float* partial = static_cast<float*>(ws);
 	const unsigned bx = (unsigned)((cols + 127) / 128);
 	{
 		TraceScope ts(s, kTraceRowwise);
-		colsum_partial_kernel<<<dim3(bx, (unsigned)chunks), 128, 0, s>>>(g, rows, cols, partial);
+		colsum_partial_kernel<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 128, 0, s>>>(g, rows, cols, partial);
 	}
 	{
 		TraceScope ts(s, kTraceRowwise);
-		colsum_final_kernel<<<bx, 128, 0, s>>>(partial, chunks, cols, out, first);
+		colsum_final_kernel<<<dim3(bx, (unsigned)groups), 128, 0, s>>>(partial, chunks, cols, out, out_stride, first);
 	}
 	nnb_status st = cuda_status(cudaGetLastError(), "column sum launch");
 	nnb_status st2 = scratch_free(ws, s);
@@ -126,6 +138,38 @@ nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const floa
 		NNB_TRY(nnb::gemm_run(s, d));
 	}
 	if (db) NNB_TRY(nnb::colsum(s, g, (long long)M, (long long)n, db, db_first));
+	return NNB_OK;
+}
+
+nnb_status nnb_linear_bwd_grouped(void* stream, size_t M, size_t K, size_t n, size_t groups, const float* g,
+		const float* x, const float* w, float* dx, int dx_first, float* dw, size_t dw_stride, int dw_first, float* db,
+		size_t db_stride, int db_first) {
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	if (!g || !x || !w) return nnb::fail(NNB_ERR_INVALID, "linear_bwd_grouped: null input");
+	if (groups == 0 || M % groups != 0) return nnb::fail(NNB_ERR_SHAPE, "linear_bwd_grouped: %zu rows in %zu groups", M, groups);
+	const int mode = nnb::math_mode();
+	const long long Mg = (long long)(M / groups);
+	if (dx) {   // dX = G W over all rows
+		nnb::GemmDesc d;
+		d.m = (long long)M; d.n = (long long)K; d.k = (long long)n;
+		d.a = g; d.lda = (long long)n; d.b = w; d.ldb = (long long)K; d.c = dx; d.ldc = (long long)K;
+		d.accumulate = !dx_first; d.mode = mode;
+		NNB_TRY(nnb::gemm_run(s, d));
+	}
+	if (dw) {   // dW_z = G_z^T X_z per group z, one batched launch (depth-cut per group)
+		nnb::GemmDesc d;
+		d.ta = 1;
+		d.m = (long long)n; d.n = (long long)K; d.k = Mg;
+		d.a = g; d.lda = (long long)n; d.b = x; d.ldb = (long long)K; d.c = dw; d.ldc = (long long)K;
+		d.batch_outer = (long long)groups;
+		d.sa_outer = Mg * (long long)n; d.sb_outer = Mg * (long long)K;
+		d.sc_outer = dw_stride ? (long long)dw_stride : (long long)n * K;
+		d.accumulate = !dw_first; d.mode = mode;
+		NNB_TRY(nnb::gemm_run(s, d));
+	}
+	if (db)
+		NNB_TRY(nnb::colsum_grouped(s, g, (long long)M, (long long)n, (long long)groups, db,
+			db_stride ? (long long)db_stride : (long long)n, db_first));
 	return NNB_OK;
 }
 

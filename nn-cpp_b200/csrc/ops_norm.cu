@@ -84,35 +84,39 @@ __global__ void layernorm_bwd_dx_kernel(const float* __restrict__ g, const float
 
 constexpr int kChunk = 256;
 
-// Chunk partials of sum_r g*xhat (dgamma) and sum_r g (dbeta), serial within the chunk.
+// Chunk partials of sum_r g*xhat (dgamma) and sum_r g (dbeta), serial within the chunk; group z
+// (blockIdx.z) covers rows [z*R, (z+1)*R).
 __global__ void layernorm_bwd_param_partial(const float* __restrict__ g, const float* __restrict__ x,
 		const float* __restrict__ mean, const float* __restrict__ inv_std, long long R, int D,
 		float* __restrict__ pg, float* __restrict__ pb) {
 	const int j = blockIdx.x * blockDim.x + threadIdx.x;
-	const long long c = blockIdx.y;
+	const long long c = blockIdx.y, chunks = gridDim.y, z = blockIdx.z;
 	if (j >= D) return;
-	const long long r0 = c * kChunk, r1 = min(R, r0 + kChunk);
+	const long long base = z * R;
+	const long long r0 = base + c * kChunk, r1 = base + min(R, (c + 1) * kChunk);
 	float sg = 0.0f, sb = 0.0f;
 	for (long long r = r0; r < r1; ++r) {
 		const float gv = g[r * D + j];
 		sg += gv * ((x[r * D + j] - mean[r]) * inv_std[r]);
 		sb += gv;
 	}
-	pg[c * D + j] = sg;
-	pb[c * D + j] = sb;
+	pg[(z * chunks + c) * D + j] = sg;
+	pb[(z * chunks + c) * D + j] = sb;
 }
 
 __global__ void layernorm_bwd_param_final(const float* __restrict__ pg, const float* __restrict__ pb,
-		long long chunks, int D, float* __restrict__ dgamma, int dg_first, float* __restrict__ dbeta, int db_first) {
+		long long chunks, int D, float* __restrict__ dgamma, long long dg_stride, int dg_first,
+		float* __restrict__ dbeta, long long db_stride, int db_first) {
 	const int j = blockIdx.x * blockDim.x + threadIdx.x;
+	const long long z = blockIdx.y;
 	if (j >= D) return;
 	float sg = 0.0f, sb = 0.0f;
 	for (long long c = 0; c < chunks; ++c) {
-		sg += pg[c * D + j];
-		sb += pb[c * D + j];
+		sg += pg[(z * chunks + c) * D + j];
+		sb += pb[(z * chunks + c) * D + j];
 	}
-	if (dgamma) dgamma[j] = dg_first ? sg + 0.0f : dgamma[j] + sg;
-	if (dbeta) dbeta[j] = db_first ? sb + 0.0f : dbeta[j] + sb;
+	if (dgamma) dgamma[z * dg_stride + j] = dg_first ? sg + 0.0f : dgamma[z * dg_stride + j] + sg;
+	if (dbeta) dbeta[z * db_stride + j] = db_first ? sb + 0.0f : dbeta[z * db_stride + j] + sb;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -279,11 +283,12 @@ nnb_status nnb_layernorm_fwd(void* stream, size_t R, size_t D, const float* x, c
 	return nnb::cuda_status(cudaGetLastError(), "layernorm_fwd launch");
 }
 
-nnb_status nnb_layernorm_bwd(void* stream, size_t R, size_t D, const float* g, const float* x, const float* gamma,
-		const float* mean, const float* inv_std, float* dx, int dx_first, float* dgamma, int dgamma_first,
-		float* dbeta, int dbeta_first) {
+nnb_status nnb_layernorm_bwd_grouped(void* stream, size_t R, size_t D, size_t groups, const float* g, const float* x,
+		const float* gamma, const float* mean, const float* inv_std, float* dx, int dx_first, float* dgamma,
+		size_t dgamma_stride, int dgamma_first, float* dbeta, size_t dbeta_stride, int dbeta_first) {
 	if (R == 0 || D == 0) return NNB_OK;
 	if (!g || !x || !gamma || !mean || !inv_std) return nnb::fail(NNB_ERR_INVALID, "layernorm_bwd: null input");
+	if (groups == 0 || R % groups != 0) return nnb::fail(NNB_ERR_SHAPE, "layernorm_bwd: %zu rows in %zu groups", R, groups);
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	if (dx) {
 		const long long threads = (long long)R * 32;
@@ -293,22 +298,24 @@ nnb_status nnb_layernorm_bwd(void* stream, size_t R, size_t D, const float* g, c
 		NNB_CUDA_TRY(cudaGetLastError());
 	}
 	if (dgamma || dbeta) {
-		const long long chunks = ((long long)R + nnb::kChunk - 1) / nnb::kChunk;
-		if (chunks > 65535) return nnb::fail(NNB_ERR_UNSUPPORTED, "layernorm_bwd: too many rows");
+		const long long Rg = (long long)(R / groups);
+		const long long chunks = (Rg + nnb::kChunk - 1) / nnb::kChunk;
+		if (chunks > 65535 || groups > 65535) return nnb::fail(NNB_ERR_UNSUPPORTED, "layernorm_bwd: too many rows");
 		void* ws = nullptr;
-		NNB_TRY(nnb::scratch_alloc(&ws, 2 * chunks * D * sizeof(float), s));
+		NNB_TRY(nnb::scratch_alloc(&ws, 2 * groups * chunks * D * sizeof(float), s));
 		float* pg = static_cast<float*>(ws);
-		float* pb = pg + chunks * D;
+		float* pb = pg + groups * chunks * D;
 		const unsigned bx = (unsigned)((D + 127) / 128);
 		{
 			nnb::TraceScope ts(s, nnb::kTraceRowwise);
-			nnb::layernorm_bwd_param_partial<<<dim3(bx, (unsigned)chunks), 128, 0, s>>>(g, x, mean, inv_std,
-				(long long)R, (int)D, pg, pb);
+			nnb::layernorm_bwd_param_partial<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 128, 0, s>>>(g, x, mean,
+				inv_std, Rg, (int)D, pg, pb);
 		}
 		{
 			nnb::TraceScope ts(s, nnb::kTraceRowwise);
-			nnb::layernorm_bwd_param_final<<<bx, 128, 0, s>>>(pg, pb, chunks, (int)D, dgamma, dgamma_first, dbeta,
-				dbeta_first);
+			nnb::layernorm_bwd_param_final<<<dim3(bx, (unsigned)groups), 128, 0, s>>>(pg, pb, chunks, (int)D, dgamma,
+				dgamma_stride ? (long long)dgamma_stride : (long long)D, dgamma_first, dbeta,
+				dbeta_stride ? (long long)dbeta_stride : (long long)D, dbeta_first);
 		}
 		nnb_status st = nnb::cuda_status(cudaGetLastError(), "layernorm_bwd launch");
 		nnb_status st2 = nnb::scratch_free(ws, s);
@@ -316,6 +323,13 @@ nnb_status nnb_layernorm_bwd(void* stream, size_t R, size_t D, const float* g, c
 		NNB_TRY(st2);
 	}
 	return NNB_OK;
+}
+
+nnb_status nnb_layernorm_bwd(void* stream, size_t R, size_t D, const float* g, const float* x, const float* gamma,
+		const float* mean, const float* inv_std, float* dx, int dx_first, float* dgamma, int dgamma_first,
+		float* dbeta, int dbeta_first) {
+	return nnb_layernorm_bwd_grouped(stream, R, D, 1, g, x, gamma, mean, inv_std, dx, dx_first, dgamma, D, dgamma_first,
+		dbeta, D, dbeta_first);
 }
 
 nnb_status nnb_batchnorm_fwd(void* stream, size_t N, size_t C, size_t S, const float* x, const float* weight,

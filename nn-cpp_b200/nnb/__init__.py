@@ -75,6 +75,10 @@ _SIGS = {
     "nnb_gelu_fwd": ([_p, _sz, _p, _p, _p], _i),
     "nnb_gelu_bwd": ([_p, _sz, _p, _p, _p, _p, _i], _i),
     "nnb_fill": ([_p, _sz, _f, _p], _i),
+    "nnb_scale": ([_p, _sz, _f, _p, _p], _i),
+    "nnb_linear_bwd_grouped": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _sz, _i, _p, _sz, _i], _i),
+    "nnb_layernorm_bwd_grouped": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _sz, _i, _p, _sz, _i], _i),
+    "nnb_embedding_bwd_grouped": ([_p, _sz, _sz, _sz, _p, _sz, _p, _p, _sz, _i], _i),
     "nnb_add_fwd": ([_p, _sz, _p, _p, _sz, _p], _i),
     "nnb_accumulate": ([_p, _sz, _p, _p, _i, _i], _i),
     "nnb_maxpool2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p], _i),

@@ -64,8 +64,11 @@ class Value:
 
     # -- gradient access -----------------------------------------------------------------------
     def grad_accum(self) -> tuple[torch.Tensor, int]:
-        """The gradient buffer and whether this contribution is the first (store) or not (add)."""
-        if self.grad is None or self.grad.shape != self.data.shape:
+        """The gradient buffer and whether this contribution is the first (store) or not (add).
+
+        A parameter's buffer may be a per-group view set by the data-parallel step (nnb.train); it is
+        used as given."""
+        if self.grad is None:
             self.grad = torch.empty_like(self.data)
             self.grad_fresh = True
         first = 1 if self.grad_fresh else 0

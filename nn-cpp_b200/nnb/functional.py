@@ -7,6 +7,7 @@ nnb.TensorShapeError as the reference throws TensorShapeError.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 
 import torch
@@ -27,6 +28,29 @@ def _need(v: Value) -> bool:
     return v.requires_grad
 
 
+# Parameter-gradient groups: with n > 1 the rows of every op's batch are n consecutive groups (the
+# data-parallel step's virtual shards) and each parameter's gradient buffer is a [n, size] view; the
+# ops then write one gradient per group (the *_grouped entry points).
+_GROUPS = 1
+
+
+@contextlib.contextmanager
+def param_groups(n: int):
+    global _GROUPS
+    old, _GROUPS = _GROUPS, n
+    try:
+        yield
+    finally:
+        _GROUPS = old
+
+
+def _gstride(buf, param: Value) -> int:
+    """Elements between consecutive groups' gradients in a parameter's gradient buffer."""
+    if buf is None:
+        return 0
+    return buf.stride(0) if buf.dim() == 2 and buf.shape[0] == _GROUPS and _GROUPS > 1 else param.data.numel()
+
+
 # ---- linear (ops.cpp:714-745) -------------------------------------------------------------------
 
 def linear(x: Value, weight: Value, bias: Value) -> Value:
@@ -39,13 +63,21 @@ def linear(x: Value, weight: Value, bias: Value) -> Value:
     check(lib().nnb_linear_fwd(_s(), M, K, n, _p(x.data), _p(weight.data), _p(bias.data), _p(y)))
 
     def backward(g):
-        dx, fx = x.grad_accum() if _need(x) else (None, 0)
-        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
-        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
-        check(lib().nnb_linear_bwd(_s(), M, K, n, _p(g), _p(x.data), _p(weight.data), _p(dx), fx, _p(dw), fw,
-                                   _p(db), fb))
+        _linear_backward(g, x, weight, bias, M, K, n)
 
     return Value.node(y, (x, weight, bias), backward)
+
+
+def _linear_backward(g, x, weight, bias, M, K, n):
+    dx, fx = x.grad_accum() if _need(x) else (None, 0)
+    dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
+    db, fb = bias.grad_accum() if _need(bias) else (None, 0)
+    if _GROUPS > 1:
+        check(lib().nnb_linear_bwd_grouped(_s(), M, K, n, _GROUPS, _p(g), _p(x.data), _p(weight.data), _p(dx), fx,
+                                           _p(dw), _gstride(dw, weight), fw, _p(db), _gstride(db, bias), fb))
+    else:
+        check(lib().nnb_linear_bwd(_s(), M, K, n, _p(g), _p(x.data), _p(weight.data), _p(dx), fx, _p(dw), fw,
+                                   _p(db), fb))
 
 
 def linear_gelu(x: Value, weight: Value, bias: Value) -> Value:
@@ -62,11 +94,7 @@ def linear_gelu(x: Value, weight: Value, bias: Value) -> Value:
     def backward(g):
         dpre = empty(pre.shape)
         check(lib().nnb_gelu_bwd(_s(), pre.numel(), _p(pre), None, _p(g), _p(dpre), 1))
-        dx, fx = x.grad_accum() if _need(x) else (None, 0)
-        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
-        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
-        check(lib().nnb_linear_bwd(_s(), M, K, n, _p(dpre), _p(x.data), _p(weight.data), _p(dx), fx, _p(dw), fw,
-                                   _p(db), fb))
+        _linear_backward(dpre, x, weight, bias, M, K, n)
 
     return Value.node(y, (x, weight, bias), backward)
 
@@ -149,8 +177,9 @@ def layernorm(x: Value, gamma: Value, beta: Value, eps: float) -> Value:
         dx, fx = x.grad_accum() if _need(x) else (None, 0)
         dg, fg = gamma.grad_accum() if _need(gamma) else (None, 0)
         db, fb = beta.grad_accum() if _need(beta) else (None, 0)
-        check(lib().nnb_layernorm_bwd(_s(), R, D, _p(g), _p(x.data), _p(gamma.data), _p(mean), _p(inv), _p(dx), fx,
-                                      _p(dg), fg, _p(db), fb))
+        check(lib().nnb_layernorm_bwd_grouped(_s(), R, D, _GROUPS, _p(g), _p(x.data), _p(gamma.data), _p(mean), _p(inv),
+                                              _p(dx), fx, _p(dg), _gstride(dg, gamma), fg, _p(db), _gstride(db, beta),
+                                              fb))
 
     return Value.node(y, (x, gamma, beta), backward)
 
@@ -265,7 +294,11 @@ def embedding(weight: Value, ids: torch.Tensor) -> Value:
 
     def backward(g):
         dw, f = weight.grad_accum()
-        check(lib().nnb_embedding_bwd(_s(), V, D, _p(ids), cnt, _p(g), _p(dw), f))
+        if _GROUPS > 1:
+            check(lib().nnb_embedding_bwd_grouped(_s(), V, D, _GROUPS, _p(ids), cnt, _p(g), _p(dw), _gstride(dw, weight),
+                                                  f))
+        else:
+            check(lib().nnb_embedding_bwd(_s(), V, D, _p(ids), cnt, _p(g), _p(dw), f))
 
     return Value.node(out, (weight,), backward)
 
@@ -285,7 +318,9 @@ def cross_entropy_loss(logits: Value, targets: torch.Tensor) -> Value:
 
 
 def sequence_cross_entropy(logits: Value, targets: torch.Tensor, ignore_index: int = -100,
-                           label_smoothing: float = 0.0) -> Value:
+                           label_smoothing: float = 0.0, grad_norm: torch.Tensor | None = None) -> Value:
+    """grad_norm: a device scalar used by the backward pass in place of 1/(positions counted here),
+    e.g. 1/(positions of the global batch) when this call sees one rank's part of it."""
     if len(logits.shape) != 3 or tuple(targets.shape) != logits.shape[:2]:
         raise TensorShapeError("sequence_cross_entropy: shapes do not agree")
     N, T, V = logits.shape
@@ -297,6 +332,6 @@ def sequence_cross_entropy(logits: Value, targets: torch.Tensor, ignore_index: i
     def backward(g):
         dl, f = logits.grad_accum()
         check(lib().nnb_sequence_ce_bwd(_s(), P, V, _p(sm), _p(targets), ignore_index, ctypes.c_float(label_smoothing),
-                                        _p(g), _p(norm), _p(dl), f))
+                                        _p(g), _p(norm if grad_norm is None else grad_norm), _p(dl), f))
 
     return Value.node(loss, (logits,), backward)

@@ -87,43 +87,47 @@ def test_transformer_training_matches_reference(cuda):
 
 def test_transformer_training_deterministic_and_shard_invariant(cuda):
     torch = cuda
-    from nnb.nn import TransformerConfig
+    import nnb
+    from nnb import functional as F
+    from nnb.nn import AdamW, Transformer, TransformerConfig
+    from nnb.train import ShardedTrainer
 
     cfg = TransformerConfig(vocab_size=96, dim=64, heads=4, layers=2, max_len=32)
     _, _, x_d, y_d = _batch(torch, 96, 8, 32, 91)
-    m1, l1, _ = _train(torch, cfg, x_d, y_d, 2, 3e-3, 1e-2, shards=8)
+    m1, l1, g1 = _train(torch, cfg, x_d, y_d, 2, 3e-3, 1e-2, shards=8)
     m2, l2, _ = _train(torch, cfg, x_d, y_d, 2, 3e-3, 1e-2, shards=8)
     assert _flat(m1).tobytes() == _flat(m2).tobytes()
     assert l1 == l2
-    # the same 8 shards, owned as if by ranks 0..3 of a 4-GPU job, each gathered: emulate one rank at a time
-    from nnb.nn import AdamW, Transformer
-    from nnb.train import ShardedTrainer
-
+    # The first step's reduced gradient, recomputed as 4 ranks of 2 shards each would (each "rank"
+    # runs its own rows with 2 parameter-gradient groups), gathered and summed in shard order: the
+    # same bits as the single-rank step (this is the data-parallel step at 4 GPUs, one rank at a time)
     m3 = Transformer(cfg, seed=3)
     opt = AdamW(m3.parameters(), lr=3e-3, weight_decay=1e-2)
-    trainers = [ShardedTrainer(m3, opt, shards=8, world=4, rank=r) for r in range(4)]
+    trs = [ShardedTrainer(m3, opt, shards=8, world=4, rank=r) for r in range(4)]
+    norm = torch.tensor([1.0 / x_d.numel()], device="cuda")
+    gathered = torch.empty(8, trs[0].total, device="cuda")
+    for r, tr in enumerate(trs):
+        tr._point_grads(tr.shard_grads)
+        with F.param_groups(2):
+            logits = m3(x_d[2 * r:2 * r + 2])
+            loss = F.sequence_cross_entropy(logits, y_d[2 * r:2 * r + 2], grad_norm=norm)
+            loss.backward()
+        gathered[2 * r:2 * r + 2].copy_(tr.shard_grads)
+    reduced = torch.empty(trs[0].total, device="cuda")
     s = torch.cuda.current_stream().cuda_stream
-    import nnb
-    for _ in range(2):
-        full = torch.empty(8, trainers[0].total, device="cuda")
-        losses = torch.empty(8, device="cuda")
-        for r, tr in enumerate(trainers):    # each "rank" computes its two shards
-            B, per = x_d.shape[0], x_d.shape[0] // 8
-            from nnb import functional as F
-            for j, sh in enumerate(tr.owned):
-                tr._point_grads(tr.shard_grads[j])
-                logits = m3(x_d[sh * per:(sh + 1) * per])
-                loss = F.sequence_cross_entropy(logits, y_d[sh * per:(sh + 1) * per])
-                loss.backward(tr.seed)
-                full[sh].copy_(tr.shard_grads[j])
-                losses[sh] = loss.data[0]
-        t0 = trainers[0]
-        nnb.check(nnb.lib().nnb_column_sum(s, 8, t0.total, full.data_ptr(), t0.reduced.data_ptr(), 1))
-        t0._point_grads(t0.reduced)
-        for p in t0.params:
-            p.grad_fresh = False
-        opt.step()
-    assert _flat(m3).tobytes() == _flat(m1).tobytes()
+    nnb.check(nnb.lib().nnb_column_sum(s, 8, trs[0].total, gathered.data_ptr(), reduced.data_ptr(), 1))
+    assert reduced.cpu().numpy().tobytes() == g1.tobytes()
+    # and as 8 ranks of one shard each (the ungrouped path)
+    m4 = Transformer(cfg, seed=3)
+    tr8 = [ShardedTrainer(m4, AdamW(m4.parameters()), shards=8, world=8, rank=r) for r in range(8)]
+    for r, tr in enumerate(tr8):
+        tr._point_grads(tr.shard_grads)
+        logits = m4(x_d[r:r + 1])
+        loss = F.sequence_cross_entropy(logits, y_d[r:r + 1], grad_norm=norm)
+        loss.backward()
+        gathered[r:r + 1].copy_(tr.shard_grads)
+    nnb.check(nnb.lib().nnb_column_sum(s, 8, trs[0].total, gathered.data_ptr(), reduced.data_ptr(), 1))
+    assert reduced.cpu().numpy().tobytes() == g1.tobytes()
 
 
 def test_cnn_forward_backward_matches_reference(cuda):

@@ -116,3 +116,50 @@ def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode):
     mp.start_processes(_nccl_worker, args=(world, _free_port(), m, n, k, mode, str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")
     assert bool(np.load(tmp_path / f"eq_{mode}.npy")[0])
+
+
+def _dp_worker(rank, world, port, out_dir):
+    import torch
+    import torch.distributed as dist
+
+    from nnb.nn import AdamW, Transformer, TransformerConfig
+    from nnb.train import ShardedTrainer
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    try:
+        cfg = TransformerConfig(vocab_size=128, dim=64, heads=4, layers=2, max_len=64)
+        g = torch.Generator().manual_seed(3)
+        ids = torch.randint(0, 128, (8, 65), generator=g)
+        x, y = ids[:, :-1].contiguous().cuda(), ids[:, 1:].contiguous().cuda()
+        model = Transformer(cfg, seed=4)
+        tr = ShardedTrainer(model, AdamW(model.parameters(), lr=3e-3), shards=8, world=world, rank=rank)
+        for _ in range(2):
+            tr.step(x, y)
+        flat = torch.cat([p.data.reshape(-1) for p in model.parameters()])
+        if rank == 0:
+            ref_model = Transformer(cfg, seed=4)
+            ref_tr = ShardedTrainer(ref_model, AdamW(ref_model.parameters(), lr=3e-3), shards=8)
+            for _ in range(2):
+                ref_tr.step(x, y)
+            ref_flat = torch.cat([p.data.reshape(-1) for p in ref_model.parameters()])
+            np.save(os.path.join(out_dir, "dp_eq.npy"), np.array([bool(torch.equal(flat, ref_flat))]))
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_data_parallel_step_bitwise_equal_to_single_gpu(cuda, tmp_path):
+    """Two training steps of the virtual-shard data-parallel step on 2 (or 4) GPUs give the same
+    weights, bit for bit, as on one GPU."""
+    torch = cuda
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    if 8 % world:
+        world = 2
+    mp.start_processes(_dp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    assert bool(np.load(tmp_path / "dp_eq.npy")[0])
