@@ -53,8 +53,8 @@ def parse_args():
     ap.add_argument("--mode", choices=("fp32x3", "tf32"), default="fp32x3")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("all", "gemm", "transformer"), default="all",
-                    help="gemm: config 4 only; transformer: config 5 only; all: config 4 line with config 5 inside")
+    ap.add_argument("--workload", choices=("all", "gemm", "transformer", "cnn", "attention"), default="all",
+                    help="one config alone, or all: the config 4 line with configs 2, 3 and 5 inside")
     ap.add_argument("--t-steps", type=int, default=10, help="timed transformer steps")
     ap.add_argument("--t-warmup", type=int, default=3)
     return ap.parse_args()
@@ -345,6 +345,10 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
         del a, b, c, a_h, b_h, c_h
         torch.cuda.empty_cache()
         transformer = run_transformer(args.t_steps, args.t_warmup, rank, world, local_rank)
+        if world == 1:
+            transformer["cnn"] = run_cnn(20, 3, local_rank)
+            transformer["attention"] = run_attention(10, 3, local_rank)
+            transformer["matmul512"] = run_matmul512(local_rank)
     if rank != 0:
         return
     flops = 2.0 * size ** 3
@@ -385,9 +389,14 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
         "clocks": clk,
     }
     if transformer is not None:
+        for key in ("cnn", "attention", "matmul512"):
+            if key in transformer:
+                line[key] = transformer.pop(key)
         line["transformer"] = transformer
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(size)
+        if args.workload == "all":
+            line["cpu_baselines_other_configs"] = cpu_baselines()
     print(json.dumps(line), flush=True)
 
 
@@ -480,6 +489,182 @@ def run_transformer(steps: int, warmup: int, rank: int, world: int, local_rank: 
     }
 
 
+# ---------------------------------------------------------------------------------------------
+# Config 2 (CNN forward + backward) and config 3 (causal attention forward + backward)
+# ---------------------------------------------------------------------------------------------
+
+CNN_FLOP_PER_STEP = 1.60e9            # conv1 28.9 M + conv2 462.4 M + fc 51.6 M forward, ~2x that backward
+ATTN_FLOP_PER_STEP = 6.468e9          # causal-effective forward + backward, B32 H8 T256 Dh64
+
+
+def _time_steps(torch, fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_cnn(steps: int, warmup: int, local_rank: int):
+    """Config 2: conv2d_relu 1->32, maxpool, conv2d_relu 32->64, maxpool, flatten, linear 3136->128,
+    relu, linear 128->10, cross entropy; forward + backward on a batch of 64 (one GPU: replicas only)."""
+    import numpy as np
+    import torch
+
+    import nnb
+    import nnb.functional as F
+    from nnb.autograd import Value
+    from nnb.nn import Conv2d, Flatten, Linear, MaxPool2d, ReLU, Sequential
+
+    dev = torch.device("cuda", local_rank)
+    rng = np.random.default_rng(2)
+    net = Sequential(Conv2d(1, 32, 3, 1, 1, rng, dev), ReLU(), MaxPool2d(2, 2), Conv2d(32, 64, 3, 1, 1, rng, dev),
+                     ReLU(), MaxPool2d(2, 2), Flatten(), Linear(3136, 128, rng, dev), ReLU(), Linear(128, 10, rng, dev))
+    g = torch.Generator().manual_seed(4)
+    x = torch.rand(64, 1, 28, 28, generator=g).to(dev)
+    y = torch.randint(0, 10, (64,), generator=g).to(dev)
+
+    def step():
+        net.zero_grad()
+        loss = F.cross_entropy_loss(net(Value.leaf(x, False)), y)
+        loss.backward()
+
+    from nnb.graph import GraphedStep
+
+    nnb.trace_reset()
+    eager = _time_steps(torch, step, steps, warmup)
+    launches = nnb.launch_count() / (steps + warmup)
+    ms = _time_steps(torch, GraphedStep(step), steps, warmup)
+    return {"metric": "CNN fwd+bwd ms/step", "value": ms, "unit": "ms", "higher_is_better": False,
+            "config": {"workload": "config 2: CNN 1x28x28 batch 64, conv2d_relu x2, maxpool x2, linear x2, CE",
+                       "dispatch": "CUDA graph replay of the whole step"},
+            "eager_ms": eager, "algorithmic_gflops": CNN_FLOP_PER_STEP / (ms * 1e-3) / 1e9,
+            "launches_per_step": launches}
+
+
+def run_attention(steps: int, warmup: int, local_rank: int):
+    """Config 3: causal attention forward + backward, q/k/v [32, 256, 512], 8 heads, N(0,1)."""
+    import torch
+
+    import nnb
+
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(6)
+    N, T, D, H = 32, 256, 512, 8
+    q, k, v, go = (torch.randn(N, T, D, device=dev, generator=g) for _ in range(4))
+    out, probs = torch.empty(N, T, D, device=dev), torch.empty(N, H, T, T, device=dev)
+    dq, dk, dv = (torch.empty(N, T, D, device=dev) for _ in range(3))
+    L = nnb.lib()
+
+    def step():
+        s = torch.cuda.current_stream().cuda_stream
+        nnb.check(L.nnb_attention_fwd(s, N, T, T, D, H, q.data_ptr(), k.data_ptr(), v.data_ptr(), None, 1,
+                                      out.data_ptr(), probs.data_ptr()))
+        nnb.check(L.nnb_attention_bwd(s, N, T, T, D, H, go.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                      probs.data_ptr(), None, 1, dq.data_ptr(), 1, dk.data_ptr(), 1, dv.data_ptr(), 1))
+
+    from nnb.graph import GraphedStep
+
+    eager = _time_steps(torch, step, steps, warmup)
+    ms = _time_steps(torch, GraphedStep(step), steps, warmup)
+    return {"metric": "causal attention fwd+bwd ms/step", "value": ms, "unit": "ms", "higher_is_better": False,
+            "config": {"workload": "config 3: B32 H8 T256 Dh64 causal, fwd + bwd", "dispatch": "CUDA graph replay"},
+            "eager_ms": eager, "algorithmic_tflops_causal": ATTN_FLOP_PER_STEP / (ms * 1e-3) / 1e12}
+
+
+def run_matmul512(local_rank: int):
+    """Config 1: C = A.B, M = N = K = 512, A then B from U[-1, 1], through nn::matmul's counterpart
+    nnb_matmul (launch-bound: one pack pair and one tensor-core launch)."""
+    import ctypes
+
+    import torch
+
+    import nnb
+
+    dev = torch.device("cuda", local_rank)
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.rand(512, 512, device=dev, generator=g) * 2 - 1
+    b = torch.rand(512, 512, device=dev, generator=g) * 2 - 1
+    c = torch.empty(512, 512, device=dev)
+    sh = (ctypes.c_int64 * 2)(512, 512)
+    osh, ond = (ctypes.c_int64 * 16)(), ctypes.c_int()
+    L = nnb.lib()
+
+    def step():
+        nnb.check(L.nnb_matmul(torch.cuda.current_stream().cuda_stream, a.data_ptr(), sh, 2, b.data_ptr(), sh, 2, 0,
+                               0, c.data_ptr(), osh, ctypes.byref(ond)))
+
+    from nnb.graph import GraphedStep
+
+    eager = _time_steps(torch, step, 200, 20)
+    ms = _time_steps(torch, GraphedStep(step), 200, 20)
+    return {"metric": "matmul 512^3 TFLOP/s", "value": 2 * 512 ** 3 / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "us_per_call": ms * 1e3, "eager_us_per_call": eager * 1e3,
+            "config": {"workload": "config 1: nn::matmul 512^3 fp32 (3xTF32)", "dispatch": "CUDA graph replay"}}
+
+
+def cpu_baselines(cores: int | None = None):
+    """The reference's own CPU code (oracle/_ref) on the host cores for configs 1, 2, 3 and 5, each a
+    bounded sample (a few seconds)."""
+    import numpy as np
+
+    from oracle import orc
+
+    ref = orc.ref()
+    if ref is None:
+        return {"unavailable": "reference library not built"}
+    cores = cores or os.cpu_count() or 1
+    ref.ref_set_threads(cores)
+    out = {"cores": cores, "kind": "reference"}
+    P = orc.ptr
+    # config 1
+    ab = orc.uniform(0, 2 * 512 * 512)
+    sec = ref.ref_time_matmul(512, 512, 512, P(ab[:512 * 512]), P(ab[512 * 512:]), 50)
+    out["config1_matmul512_tflops"] = 2 * 512 ** 3 / sec / 1e12
+    # config 2
+    N = 64
+    x = orc.uniform(50, N * 784, 0.0, 1.0)
+    labels = orc.integers(51, N, 0, 9)
+    sizes = [32 * 9, 32, 64 * 288, 64, 128 * 3136, 128, 1280, 10]
+    params = np.concatenate([orc.uniform(60 + i, n, -0.05, 0.05) for i, n in enumerate(sizes)])
+    loss, logits, grads = np.zeros(1, np.float32), np.zeros((N, 10), np.float32), np.zeros_like(params)
+    ts = []
+    for _ in range(4):
+        t0 = time.perf_counter()
+        ref.ref_cnn_fwd_bwd(N, P(x), P(labels), P(params), P(loss), P(logits), P(grads))
+        ts.append(time.perf_counter() - t0)
+    out["config2_cnn_ms_per_step"] = statistics.median(ts[1:]) * 1e3
+    # config 3 (full size)
+    Na, T, D, H = 32, 256, 512, 8
+    q, k, v, g = (orc.normal(70 + i, Na * T * D) for i in range(4))
+    o, dq, dk, dv = (np.zeros(Na * T * D, np.float32) for _ in range(4))
+    ts = []
+    for _ in range(2):
+        t0 = time.perf_counter()
+        ref.ref_attention(Na, T, T, D, H, P(q), P(k), P(v), None, 1, P(g), P(o), P(dq), P(dk), P(dv))
+        ts.append(time.perf_counter() - t0)
+    out["config3_attention_ms_per_step"] = min(ts) * 1e3
+    # config 5 on 8 of the 64 sequences (one virtual shard), one training step
+    cfg = (4096, 512, 8, 4, 512)
+    n_params = 16808960
+    prm = orc.uniform(80, n_params, -0.04, 0.04)
+    ids = orc.integers(81, 8 * 513, 0, 4095).reshape(8, 513)
+    xi, yi = np.ascontiguousarray(ids[:, :512]), np.ascontiguousarray(ids[:, 1:])
+    losses, prm_out = np.zeros(1, np.float32), np.zeros_like(prm)
+    t0 = time.perf_counter()
+    n = ref.ref_transformer_train(*cfg, 8, 512, P(prm), P(xi), P(yi), 3e-4, 1e-2, 1, P(losses), None, P(prm_out))
+    sec = time.perf_counter() - t0
+    out["config5_transformer_tokens_per_s"] = 8 * 512 / sec if n == n_params else None
+    out["sample"] = ("config 1: 50 calls; config 2: 3 steps after 1; config 3: best of 2 full fwd+bwd; config 5: "
+                     "one AdamW step on 8 of the 64 sequences (4096 tokens)")
+    return out
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -496,7 +681,11 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload == "transformer":
+        if args.workload in ("cnn", "attention"):
+            if rank == 0:
+                fn = run_cnn if args.workload == "cnn" else run_attention
+                print(json.dumps(fn(max(args.t_steps, 10), args.t_warmup, local_rank)), flush=True)
+        elif args.workload == "transformer":
             t = run_transformer(args.t_steps, args.t_warmup, rank, world, local_rank)
             if rank == 0:
                 t.update({"n_gpus": world, "higher_is_better": True, "vs_baseline": None, "dtype": "tf32x3",

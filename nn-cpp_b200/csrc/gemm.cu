@@ -158,6 +158,109 @@ __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, 
 	}
 }
 
+// Vectorised pack for X stored rows x K (K contiguous) with 16-byte aligned rows and K % 4 == 0:
+// every thread moves float4 groups straight from X into the panels (4 consecutive k of one row are
+// 16 contiguous bytes in both layouts). grid = (blocks, batch entries), grid-stride over Rp * KB * 4.
+template <int kSplit>
+__global__ void __launch_bounds__(256) pack_rows_vec_kernel(const float* __restrict__ X, long long ldx,
+		long long s_outer, long long s_inner, int inner, int R, int K, int Rp, int KB, int panel_rows,
+		float* __restrict__ out, int* __restrict__ flags, int* __restrict__ any_flag) {
+	constexpr int S = kSplit ? 2 : 1;
+	const int e = blockIdx.y;
+	const float* Xb = X + (long long)(e / inner) * s_outer + (long long)(e % inner) * s_inner;
+	const long long K4 = (long long)KB * 4, total = (long long)Rp * K4;
+	const long long batch_off = (long long)e * Rp * KB * 16 * S;
+	const int panel_floats = panel_rows * 16;
+	for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+			idx += (long long)gridDim.x * blockDim.x) {
+		const int r = (int)(idx / K4), q = (int)(idx - (long long)r * K4), k = q * 4;
+		float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+		if (r < R && k < K) v = __ldg(reinterpret_cast<const float4*>(Xb + (long long)r * ldx + k));
+		const bool ok = isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+		if (!ok) {
+			atomicOr(flags + (long long)e * Rp + r, 1);
+			atomicOr(any_flag, 1);
+			v.x = isfinite(v.x) ? v.x : 0.0f;
+			v.y = isfinite(v.y) ? v.y : 0.0f;
+			v.z = isfinite(v.z) ? v.z : 0.0f;
+			v.w = isfinite(v.w) ? v.w : 0.0f;
+		}
+		float4 h, l;
+		if (kSplit) {
+			split_tf32(v.x, h.x, l.x);
+			split_tf32(v.y, h.y, l.y);
+			split_tf32(v.z, h.z, l.z);
+			split_tf32(v.w, h.w, l.w);
+		} else {
+			h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+		}
+		const int kb = q >> 2;
+		const long long panel = ((long long)(r / panel_rows) * KB + kb) * S;
+		float* dst = out + batch_off + panel * panel_floats + (r % panel_rows) * 16 + (q & 3) * 4;
+		*reinterpret_cast<float4*>(dst) = h;
+		if (kSplit) *reinterpret_cast<float4*>(dst + panel_floats) = l;
+	}
+}
+
+// Vectorised pack for X stored K x rows (rows contiguous) with 16-byte aligned k-rows and R % 4 == 0:
+// a 64-row x 32-depth tile is read with float4 loads along the rows, transposed in shared memory,
+// and written as float4 groups of 4 consecutive k. grid = (Rp/64, ceil(Kp/32), batch entries).
+template <int kSplit>
+__global__ void __launch_bounds__(256) pack_cols_vec_kernel(const float* __restrict__ X, long long ldx,
+		long long s_outer, long long s_inner, int inner, int R, int K, int Rp, int KB, int panel_rows,
+		float* __restrict__ out, int* __restrict__ flags, int* __restrict__ any_flag) {
+	constexpr int S = kSplit ? 2 : 1;
+	__shared__ float tile[64][33];
+	const int t = threadIdx.x;
+	const int r0 = blockIdx.x * 64, k0 = blockIdx.y * 32, e = blockIdx.z;
+	const float* Xb = X + (long long)(e / inner) * s_outer + (long long)(e % inner) * s_inner;
+#pragma unroll
+	for (int i = 0; i < 2; ++i) {
+		const int f = t + 256 * i;                // float4 index in the 32 x 16 float4 tile
+		const int kk = f >> 4, r4 = (f & 15) * 4;
+		const int gk = k0 + kk, gr = r0 + r4;
+		float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+		if (gk < K && gr < R) v = __ldg(reinterpret_cast<const float4*>(Xb + (long long)gk * ldx + gr));
+		tile[r4][kk] = v.x;
+		tile[r4 + 1][kk] = v.y;
+		tile[r4 + 2][kk] = v.z;
+		tile[r4 + 3][kk] = v.w;
+	}
+	__syncthreads();
+	const long long batch_off = (long long)e * Rp * KB * 16 * S;
+	const int panel_floats = panel_rows * 16;
+#pragma unroll
+	for (int i = 0; i < 2; ++i) {
+		const int f = t + 256 * i;                // (row, k-quad) pairs: 64 rows x 8 quads
+		const int rl = f >> 3, q = f & 7;
+		const int gr = r0 + rl, k = k0 + q * 4, kb = k >> 4;
+		if (kb >= KB) continue;
+		float4 v = make_float4(tile[rl][q * 4], tile[rl][q * 4 + 1], tile[rl][q * 4 + 2], tile[rl][q * 4 + 3]);
+		const bool ok = isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+		if (!ok) {
+			atomicOr(flags + (long long)e * Rp + gr, 1);
+			atomicOr(any_flag, 1);
+			v.x = isfinite(v.x) ? v.x : 0.0f;
+			v.y = isfinite(v.y) ? v.y : 0.0f;
+			v.z = isfinite(v.z) ? v.z : 0.0f;
+			v.w = isfinite(v.w) ? v.w : 0.0f;
+		}
+		float4 h, l;
+		if (kSplit) {
+			split_tf32(v.x, h.x, l.x);
+			split_tf32(v.y, h.y, l.y);
+			split_tf32(v.z, h.z, l.z);
+			split_tf32(v.w, h.w, l.w);
+		} else {
+			h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
+		}
+		const long long panel = ((long long)(gr / panel_rows) * KB + kb) * S;
+		float* dst = out + batch_off + panel * panel_floats + (gr % panel_rows) * 16 + (k & 15);
+		*reinterpret_cast<float4*>(dst) = h;
+		if (kSplit) *reinterpret_cast<float4*>(dst + panel_floats) = l;
+	}
+}
+
 // ---------------------------------------------------------------------------------------------
 // Main kernel
 // ---------------------------------------------------------------------------------------------
@@ -498,6 +601,30 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0) {
 	return NNB_OK;
 }
 
+// Packs one operand with the fastest kernel its layout allows (16-byte aligned rows and a multiple of
+// 4 along the contiguous axis: float4 paths; anything else: the scalar tile kernel).
+template <int kSplit>
+static void launch_pack(cudaStream_t s, const float* X, long long ldx, long long s_outer, long long s_inner, int inner,
+		int trans, long long R, long long K, long long Rp, long long KB, int panel_rows, long long entries, float* out,
+		int* flags, int* any) {
+	const bool base16 = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
+	const bool strides4 = ldx % 4 == 0 && s_outer % 4 == 0 && s_inner % 4 == 0;
+	if (!trans && base16 && strides4 && K % 4 == 0) {
+		const long long work = Rp * KB * 4;
+		const unsigned blocks = (unsigned)std::max<long long>(1, std::min<long long>((work + 255) / 256, 148 * 16));
+		pack_rows_vec_kernel<kSplit><<<dim3(blocks, (unsigned)entries), 256, 0, s>>>(X, ldx, s_outer, s_inner, inner,
+			(int)R, (int)K, (int)Rp, (int)KB, panel_rows, out, flags, any);
+	} else if (trans && base16 && strides4 && R % 4 == 0) {
+		dim3 g((unsigned)(Rp / 64), (unsigned)((KB * 16 + 31) / 32), (unsigned)entries);
+		pack_cols_vec_kernel<kSplit><<<g, 256, 0, s>>>(X, ldx, s_outer, s_inner, inner, (int)R, (int)K, (int)Rp, (int)KB,
+			panel_rows, out, flags, any);
+	} else {
+		dim3 g((unsigned)(Rp / 32), (unsigned)((KB * 16 + 63) / 64), (unsigned)entries);
+		pack_kernel<kSplit><<<g, 256, 0, s>>>(X, ldx, s_outer, s_inner, inner, trans, (int)R, (int)K, (int)Rp, (int)KB,
+			panel_rows, out, flags, any);
+	}
+}
+
 template <int kSplit, int kBN>
 static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
@@ -510,17 +637,15 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	const int inner = (int)d.batch_inner;
 
 	NNB_CUDA_TRY(cudaMemsetAsync(flags_a, 0, pl.flag_ints * sizeof(int), s));
-	dim3 ga((unsigned)(pl.Mp / 32), (unsigned)((pl.Kp + 63) / 64), (unsigned)pl.a_entries);
-	dim3 gb((unsigned)(pl.Np / 32), (unsigned)((pl.Kp + 63) / 64), (unsigned)pl.b_entries);
 	{
 		TraceScope ts(s, kTracePack, traced);
-		pack_kernel<kSplit><<<ga, 256, 0, s>>>(d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, (int)d.m, (int)d.k,
-			(int)pl.Mp, (int)pl.KB, kAPanelRows, pa, flags_a, any);
+		launch_pack<kSplit>(s, d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, d.m, d.k, pl.Mp, pl.KB, kAPanelRows,
+			pl.a_entries, pa, flags_a, any);
 	}
 	{
 		TraceScope ts(s, kTracePack, traced);
-		pack_kernel<kSplit><<<gb, 256, 0, s>>>(d.b, d.ldb, d.sb_outer, d.sb_inner, inner, !d.tb, (int)d.n, (int)d.k,
-			(int)pl.Np, (int)pl.KB, Cf::kBPanelRows, pb, flags_b, any);
+		launch_pack<kSplit>(s, d.b, d.ldb, d.sb_outer, d.sb_inner, inner, !d.tb, d.n, d.k, pl.Np, pl.KB,
+			Cf::kBPanelRows, pl.b_entries, pb, flags_b, any);
 	}
 	NNB_CUDA_TRY(cudaGetLastError());
 

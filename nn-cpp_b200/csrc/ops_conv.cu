@@ -77,23 +77,27 @@ __global__ void mask_grad_kernel(long long n, const float* __restrict__ g, const
 	GRID_STRIDE(i, n) out[i] = alive[i] ? g[i] : 0.0f;
 }
 
-// db[c] (+)= sum_n lane_sum(g[n][c][:]) in sample order (ops.cpp:804-812, 1441-1442, 1461)
-__global__ void conv_bias_grad_kernel(const float* __restrict__ g, int N, int Cout, long long hw, float* __restrict__ db,
-		int first) {
+// gb[n*Cout + c] = lane_sum(g[n][c][:]) (ops.cpp:804-812, 1441-1442): one thread per (sample, channel)
+__global__ void conv_plane_sum_kernel(const float* __restrict__ g, long long planes, long long hw, float* __restrict__ gb) {
+	const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+	if (idx >= planes) return;
+	const float* p = g + idx * hw;
+	float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+	long long i = 0;
+	for (; i + 8 <= hw; i += 8)
+#pragma unroll
+		for (int k = 0; k < 8; ++k) a[k] += p[i + k];
+	float t = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+	for (; i < hw; ++i) t += p[i];
+	gb[idx] = t;
+}
+
+// db[c] (+)= sum_n gb[n][c] in sample order (Tensor::sum(0), src/tensor.cpp:448-453; ops.cpp:1461)
+__global__ void conv_bias_grad_kernel(const float* __restrict__ gb, int N, int Cout, float* __restrict__ db, int first) {
 	const int c = blockIdx.x * blockDim.x + threadIdx.x;
 	if (c >= Cout) return;
 	float acc = 0.0f;
-	for (int n = 0; n < N; ++n) {
-		const float* p = g + ((long long)n * Cout + c) * hw;
-		float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-		long long i = 0;
-		for (; i + 8 <= hw; i += 8)
-#pragma unroll
-			for (int k = 0; k < 8; ++k) a[k] += p[i + k];
-		float t = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
-		for (; i < hw; ++i) t += p[i];
-		acc += t;
-	}
+	for (int n = 0; n < N; ++n) acc += gb[(long long)n * Cout + c];
 	db[c] = first ? acc + 0.0f : db[c] + acc;
 }
 
@@ -174,10 +178,12 @@ nnb_status nnb_conv2d_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W
 	const size_t col_f = need_col ? (size_t)N * K * hw : 0, gm_f = alive ? (size_t)out_n : 0,
 		gw_f = dweight ? (size_t)N * Cout * K : 0;
 	void* ws = nullptr;
-	NNB_TRY(nnb::scratch_alloc(&ws, (col_f + gm_f + gw_f + 64) * sizeof(float), s));
+	const size_t gb_f = (size_t)N * Cout;
+	NNB_TRY(nnb::scratch_alloc(&ws, (col_f + gm_f + gw_f + gb_f + 64) * sizeof(float), s));
 	float* col = static_cast<float*>(ws);
 	float* gm = col + col_f;
 	float* gw = gm + gm_f;
+	float* gb = gw + gw_f;
 	nnb_status st = NNB_OK;
 	do {
 		const float* gg = grad;
@@ -187,8 +193,13 @@ nnb_status nnb_conv2d_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W
 			gg = gm;
 		}
 		if (dbias) {
+			const long long planes = (long long)N * Cout;
+			{
+				nnb::TraceScope ts(s, nnb::kTraceConv);
+				nnb::conv_plane_sum_kernel<<<(unsigned)((planes + 127) / 128), 128, 0, s>>>(gg, planes, hw, gb);
+			}
 			nnb::TraceScope ts(s, nnb::kTraceConv);
-			nnb::conv_bias_grad_kernel<<<(unsigned)((Cout + 127) / 128), 128, 0, s>>>(gg, (int)N, (int)Cout, hw, dbias,
+			nnb::conv_bias_grad_kernel<<<(unsigned)((Cout + 127) / 128), 128, 0, s>>>(gb, (int)N, (int)Cout, dbias,
 				dbias_first);
 		}
 		if ((st = nnb::cuda_status(cudaGetLastError(), "conv bias grad launch")) != NNB_OK) break;

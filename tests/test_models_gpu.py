@@ -175,3 +175,34 @@ def test_cnn_forward_backward_matches_reference(cuda):
         assert rel <= 6e-2, (name, rel)
         if name.startswith("9."):                  # the last Linear layer
             _close(g, r, 2e-3)
+
+
+def test_graphed_cnn_step_matches_eager(cuda):
+    """A CUDA-graph replay of the CNN step (nnb.graph) gives the eager step's bits."""
+    torch = cuda
+    import nnb.functional as F
+    from nnb.autograd import Value
+    from nnb.graph import GraphedStep
+    from nnb.nn import Conv2d, Flatten, Linear, MaxPool2d, ReLU, Sequential
+
+    rng = np.random.default_rng(8)
+    dev = torch.device("cuda")
+    net = Sequential(Conv2d(1, 8, 3, 1, 1, rng, dev), ReLU(), MaxPool2d(2, 2), Flatten(), Linear(8 * 14 * 14, 10, rng, dev))
+    x = torch.from_numpy(orc.uniform(52, 16 * 784, 0.0, 1.0).reshape(16, 1, 28, 28)).cuda()
+    y = torch.from_numpy(orc.integers(53, 16, 0, 9)).cuda()
+
+    def step():
+        net.zero_grad()
+        loss = F.cross_entropy_loss(net(Value.leaf(x, False)), y)
+        loss.backward()
+        return loss
+
+    eager_loss = step().data.clone()
+    eager_grads = [p.grad.clone() for p in net.parameters()]
+    g = GraphedStep(step)
+    x.copy_(torch.from_numpy(orc.uniform(52, 16 * 784, 0.0, 1.0).reshape(16, 1, 28, 28)))
+    out = g()
+    torch.cuda.synchronize()
+    assert torch.equal(out.data, eager_loss)
+    for p, e in zip(net.parameters(), eager_grads):
+        assert torch.equal(p.grad, e)
