@@ -548,7 +548,9 @@ def run_cnn(steps: int, warmup: int, local_rank: int):
 
 
 def run_attention(steps: int, warmup: int, local_rank: int):
-    """Config 3: causal attention forward + backward, q/k/v [32, 256, 512], 8 heads, N(0,1)."""
+    """Config 3: causal attention forward + backward, q/k/v [32, 256, 512], 8 heads, N(0,1). The fused
+    kernels (nnb_flash_attention_*) are the timed path; the composed path that keeps the
+    probabilities (nnb_attention_*, the reference's structure) is timed beside it."""
     import torch
 
     import nnb
@@ -558,10 +560,19 @@ def run_attention(steps: int, warmup: int, local_rank: int):
     N, T, D, H = 32, 256, 512, 8
     q, k, v, go = (torch.randn(N, T, D, device=dev, generator=g) for _ in range(4))
     out, probs = torch.empty(N, T, D, device=dev), torch.empty(N, H, T, T, device=dev)
+    stats = torch.empty(N, H, T, 2, device=dev)
     dq, dk, dv = (torch.empty(N, T, D, device=dev) for _ in range(3))
     L = nnb.lib()
 
-    def step():
+    def fused():
+        s = torch.cuda.current_stream().cuda_stream
+        nnb.check(L.nnb_flash_attention_fwd(s, N, T, T, D, H, q.data_ptr(), k.data_ptr(), v.data_ptr(), None, 1,
+                                            out.data_ptr(), stats.data_ptr()))
+        nnb.check(L.nnb_flash_attention_bwd(s, N, T, T, D, H, go.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                            v.data_ptr(), out.data_ptr(), stats.data_ptr(), None, 1, dq.data_ptr(), 1,
+                                            dk.data_ptr(), 1, dv.data_ptr(), 1))
+
+    def composed():
         s = torch.cuda.current_stream().cuda_stream
         nnb.check(L.nnb_attention_fwd(s, N, T, T, D, H, q.data_ptr(), k.data_ptr(), v.data_ptr(), None, 1,
                                       out.data_ptr(), probs.data_ptr()))
@@ -570,11 +581,24 @@ def run_attention(steps: int, warmup: int, local_rank: int):
 
     from nnb.graph import GraphedStep
 
-    eager = _time_steps(torch, step, steps, warmup)
-    ms = _time_steps(torch, GraphedStep(step), steps, warmup)
+    eager = _time_steps(torch, fused, steps, warmup)
+    ms = _time_steps(torch, GraphedStep(fused), steps, warmup)
+    composed_ms = _time_steps(torch, GraphedStep(composed), steps, warmup)
+    # per-kernel device time of the fused step
+    nnb.trace_reset()
+    nnb.trace_enable(True)
+    for _ in range(5):
+        fused()
+    kernels = {}
+    for name, kind in (("pack", nnb.TRACE_PACK), ("attention", nnb.TRACE_ATTENTION)):
+        t, n = nnb.trace_query(kind)
+        kernels[name] = {"ms": round(t / 5, 4), "launches": n // 5}
+    nnb.trace_enable(False)
     return {"metric": "causal attention fwd+bwd ms/step", "value": ms, "unit": "ms", "higher_is_better": False,
-            "config": {"workload": "config 3: B32 H8 T256 Dh64 causal, fwd + bwd", "dispatch": "CUDA graph replay"},
-            "eager_ms": eager, "algorithmic_tflops_causal": ATTN_FLOP_PER_STEP / (ms * 1e-3) / 1e12}
+            "config": {"workload": "config 3: B32 H8 T256 Dh64 causal, fwd + bwd", "dispatch": "CUDA graph replay",
+                       "path": "fused (no probability matrix)"},
+            "eager_ms": eager, "composed_path_ms": composed_ms, "kernels": kernels,
+            "algorithmic_tflops_causal": ATTN_FLOP_PER_STEP / (ms * 1e-3) / 1e12}
 
 
 def run_matmul512(local_rank: int):

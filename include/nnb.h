@@ -187,6 +187,21 @@ NNB_API nnb_status nnb_attention_bwd(void* stream, size_t N, size_t Tq, size_t T
 		const float* g, const float* q, const float* k, const float* v, const float* probs,
 		const float* key_padding_mask, int causal, float* dq, int dq_first, float* dk, int dk_first, float* dv,
 		int dv_first);
+/* Fused attention for head size 64 (D / heads == 64): the same op and masks as nnb_attention_*,
+ * without the [N, heads, Tq, Tk] probabilities. The forward writes out and stats [N, heads, Tq, 2]
+ * (per query row: the max m of the masked scaled scores and the sum l of exp(score - m), from
+ * which the backward recomputes the probabilities); the backward takes the forward's out and stats. Results agree with nnb_attention_* to fp32 rounding
+ * (the softmax is computed online over 64-key tiles); each output element is written by one CTA
+ * in a fixed order, so they are bitwise reproducible. Other head sizes: NNB_ERR_UNSUPPORTED.
+ * Replaces the same reference interface as nnb_attention_fwd / _bwd (ops.cpp:1226-1296). */
+NNB_API int nnb_flash_attention_supported(size_t D, size_t heads);
+NNB_API nnb_status nnb_flash_attention_fwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* q, const float* k, const float* v, const float* key_padding_mask, int causal, float* out,
+		float* lse);
+NNB_API nnb_status nnb_flash_attention_bwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* g, const float* q, const float* k, const float* v, const float* out, const float* lse,
+		const float* key_padding_mask, int causal, float* dq, int dq_first, float* dk, int dk_first, float* dv,
+		int dv_first);
 /* masked_softmax_row over [N, H, Tq, Tk] scores in place (ops.cpp:1183-1204), and its backward
  * turning dL/dP into dL/dS in place (ops.cpp:1216-1224). */
 NNB_API nnb_status nnb_masked_softmax_fwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk, float* scores,

@@ -85,19 +85,6 @@ struct Params {
 // Pack
 // ---------------------------------------------------------------------------------------------
 
-__device__ __forceinline__ float to_tf32(float x) {
-	uint32_t r;
-	asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-	return __uint_as_float(r);
-}
-
-// hi + lo ~= x with hi, lo both TF32; finite x never gives a non-finite part.
-__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-	hi = to_tf32(x);
-	if (isinf(hi)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);  // |x| near FLT_MAX
-	lo = to_tf32(x - hi);
-}
-
 // One block: 32 rows x 64 depth of op(X) (X stored rows x K, or K x rows when trans), written
 // as 4 k-blocks of the packed panel layout with `panel_rows`-row panels.
 // grid = (Rp/32, ceil(Kp/64), batch entries); entry e reads X + (e / inner)*s_outer + (e % inner)*s_inner.

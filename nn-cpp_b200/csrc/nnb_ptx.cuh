@@ -18,6 +18,8 @@ enum DeviceError : int {
 	kDevTimeoutEmpty = 2,     // producer waited too long for a free stage
 	kDevTimeoutAccum = 3,     // epilogue waited too long for an accumulator
 	kDevTimeoutAccumFree = 4, // MMA issuer waited too long for an accumulator to drain
+	kDevTimeoutAttn = 5,      // a fused-attention role waited too long for another role
+	kDevTimeoutDrain = 6,     // a CTA waited too long for its own copies / MMAs before exiting
 };
 
 // Upper bound on any single mbarrier wait: 2 s. A healthy wait is a few microseconds.
@@ -181,6 +183,112 @@ __device__ __forceinline__ uint64_t smem_desc_k_sw64(uint32_t smem_addr) {
 // Instruction descriptor for kind::tf32: F32 accumulator, TF32 A and B, both K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
 	return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Instruction-descriptor bit selecting an MN-major B operand (N contiguous for each k).
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
+
+// Shared-memory descriptor for an MN-major 32-bit (tf32) operand. The one layout tcgen05 offers for
+// MN-major 32-bit operands is the 128-byte swizzle with 32-byte atoms (layout type 1): each 128-byte
+// row holds 32 consecutive N elements of one k, its four 32-byte chunks permuted as chunk c at
+// c ^ (k & 3); 4 k-rows form a 512-byte group (stride byte offset 512 to the next group) and the
+// next 32 N elements sit `lbo_bytes` further on (leading byte offset). One tf32 MMA step (K = 8)
+// reads two groups, so the k step moves the start by 1024 bytes.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128b32(uint32_t smem_addr, uint32_t lbo_bytes) {
+	uint64_t d = 0;
+	d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+	d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+	d |= (uint64_t)(512u >> 4) << 32;
+	d |= (uint64_t)1 << 46;
+	d |= (uint64_t)1 << 61;                         // SWIZZLE_128B_BASE32B
+	return d;
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::tf32, with A (M rows x K) read from tensor memory:
+// row i in lane i, K consecutive 32-bit columns starting at a_tmem's column.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+		uint32_t idesc, uint32_t accumulate) {
+	asm volatile(
+		"{\n\t.reg .pred p;\n\t"
+		"setp.ne.b32 p, %4, 0;\n\t"
+		"tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+		"r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+		: "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread t of the warp writes lane (base + t).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+	asm volatile(
+		"tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+		"{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+		"%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+		"r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+		"r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+		"r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+		"r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+		"r"(r[29]), "r"(r[30]), "r"(r[31])
+		: "memory");
+}
+
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+	asm volatile(
+		"tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+		"{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+		: "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+		"=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+		"=r"(r[14]), "=r"(r[15])
+		: "r"(taddr)
+		: "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+	asm volatile(
+		"tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+		"{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+		"r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+		"r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+		"r"(r[15])
+		: "memory");
+}
+
+// Barrier over `count` threads (a multiple of 32) with id 1..15; id 0 is __syncthreads.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+	asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// 2^x with the hardware base-2 exponential (ex2.approx: relative error about 2^-22; 2^-inf = +0).
+__device__ __forceinline__ float exp2_hw(float x) {
+	float y;
+	asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+	return y;
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+	asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Plain (untiled) bulk copy global -> this CTA's shared memory, completion counted on an
+// mbarrier. Both addresses 16-byte aligned, size a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_load(uint32_t smem_dst, const void* src, uint32_t bytes, uint32_t bar) {
+	asm volatile(
+		"cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_dst),
+		"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+		: "memory");
+}
+
+// TF32 rounding (round to nearest, ties away) and the 3xTF32 split x ~= hi + lo.
+__device__ __forceinline__ float to_tf32(float x) {
+	uint32_t r;
+	asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+	return __uint_as_float(r);
+}
+
+// hi + lo ~= x with hi, lo both TF32; finite x never gives a non-finite part.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+	hi = to_tf32(x);
+	if (isinf(hi)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);  // |x| near FLT_MAX
+	lo = to_tf32(x - hi);
 }
 
 }  // namespace nnb

@@ -66,6 +66,10 @@ _SIGS = {
     "nnb_batchnorm_bwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
     "nnb_attention_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _p], _i),
     "nnb_attention_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _p, _i], _i),
+    "nnb_flash_attention_supported": ([_sz, _sz], _i),
+    "nnb_flash_attention_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _p], _i),
+    "nnb_flash_attention_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _p, _i],
+                                _i),
     "nnb_masked_softmax_fwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _i, _f], _i),
     "nnb_masked_softmax_bwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _f], _i),
     "nnb_conv2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _i, _p, _p], _i),

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import os
 
 import torch
 
@@ -210,12 +211,20 @@ def batchnorm(x: Value, weight: Value, bias: Value, eps: float, fuse_relu: bool 
 # ---- attention (ops.cpp:1226-1296) --------------------------------------------------------------
 
 def attention(q: Value, k: Value, v: Value, heads: int, key_padding_mask: torch.Tensor | None = None,
-              causal: bool = False) -> Value:
+              causal: bool = False, fused: bool | None = None) -> Value:
+    """Multi-head attention (ops.cpp:1226-1296). Head size 64 runs the fused kernels (no
+    [N, heads, Tq, Tk] probabilities kept; the backward recomputes them from the row max and sum);
+    other head sizes, or fused=False (or NNB_ATTENTION=composed), run the reference's composition:
+    head-batched GEMMs around the masked softmax, keeping the probabilities."""
     qs, ks = q.shape, k.shape
     if len(qs) != 3 or len(ks) != 3 or v.shape != ks or qs[0] != ks[0] or qs[2] != ks[2]:
         raise TensorShapeError("attention: shapes do not agree")
     N, Tq, D = qs
     Tk = ks[1]
+    if fused is None:
+        fused = FUSED_ATTENTION
+    if fused and heads > 0 and lib().nnb_flash_attention_supported(D, heads):
+        return _flash_attention(q, k, v, heads, key_padding_mask, causal, N, Tq, Tk, D)
     out, probs = empty((N, Tq, D)), empty((N, heads, Tq, Tk))
     check(lib().nnb_attention_fwd(_s(), N, Tq, Tk, D, heads, _p(q.data), _p(k.data), _p(v.data),
                                   _p(key_padding_mask), int(causal), _p(out), _p(probs)))
@@ -228,6 +237,25 @@ def attention(q: Value, k: Value, v: Value, heads: int, key_padding_mask: torch.
         check(lib().nnb_attention_bwd(_s(), N, Tq, Tk, D, heads, _p(g), _p(q.data), _p(k.data), _p(v.data),
                                       _p(probs), _p(key_padding_mask), int(causal), _p(dq), fq, _p(dk), fk, _p(dv),
                                       fv))
+
+    return Value.node(out, (q, k, v), backward)
+
+
+FUSED_ATTENTION = os.environ.get("NNB_ATTENTION", "fused").lower() != "composed"
+
+
+def _flash_attention(q, k, v, heads, key_padding_mask, causal, N, Tq, Tk, D) -> Value:
+    out, stats = empty((N, Tq, D)), empty((N, heads, Tq, 2))
+    check(lib().nnb_flash_attention_fwd(_s(), N, Tq, Tk, D, heads, _p(q.data), _p(k.data), _p(v.data),
+                                        _p(key_padding_mask), int(causal), _p(out), _p(stats)))
+
+    def backward(g):
+        dv, fv = v.grad_accum() if _need(v) else (None, 0)
+        dq, fq = q.grad_accum() if _need(q) else (None, 0)
+        dk, fk = k.grad_accum() if _need(k) else (None, 0)
+        check(lib().nnb_flash_attention_bwd(_s(), N, Tq, Tk, D, heads, _p(g), _p(q.data), _p(k.data), _p(v.data),
+                                            _p(out), _p(stats), _p(key_padding_mask), int(causal), _p(dq), fq, _p(dk),
+                                            fk, _p(dv), fv))
 
     return Value.node(out, (q, k, v), backward)
 

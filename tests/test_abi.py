@@ -44,3 +44,17 @@ def test_built_for_sm100a_only():
     flags = " ".join(_build.NVCC_FLAGS)
     assert "arch=compute_100a,code=sm_100a" in flags
     assert flags.count("-gencode") == 1
+
+
+def test_flash_attention_host_checks():
+    """Head sizes other than 64 and bad shapes are rejected on the host, before any device work."""
+    lib = nnb.lib()
+    assert lib.nnb_flash_attention_supported(512, 8) == 1
+    assert lib.nnb_flash_attention_supported(48, 1) == 0
+    assert lib.nnb_flash_attention_supported(30, 4) == 0
+    st = lib.nnb_flash_attention_fwd(None, 2, 8, 8, 96, 2, None, None, None, None, 0, None, None)
+    assert st == 3 and "head size 48" in lib.nnb_last_error().decode()         # NNB_ERR_UNSUPPORTED
+    st = lib.nnb_flash_attention_fwd(None, 2, 8, 9, 128, 2, None, None, None, None, 1, None, None)
+    assert st == 5                                                              # causal needs Tq == Tk
+    st = lib.nnb_flash_attention_bwd(None, 1, 4, 4, 64, 3, *([None] * 7), 0, None, 1, None, 1, None, 1)
+    assert st == 5                                                              # heads does not divide D

@@ -1,0 +1,165 @@
+"""Fused attention (nnb_flash_attention_*) against the oracle's restatement of the reference's
+attention op (src/autograd/ops.cpp:1226-1296: scores, masked softmax, P V and the backward).
+
+The fused kernels compute the softmax online over 64-key tiles and never store the probabilities,
+so they agree with the reference to fp32 rounding, not bit for bit: |got - want| <= 1e-4 *
+(max|want| + |want|), the bound the composed attention path is held to. They are bitwise
+deterministic (each output element is written by one CTA in a fixed order).
+"""
+import numpy as np
+import pytest
+
+import nnb
+from oracle import orc
+
+pytestmark = pytest.mark.gpu
+P = orc.ptr
+O = orc.orc
+
+
+def lib():
+    return nnb.lib()
+
+
+def S(torch):
+    return torch.cuda.current_stream().cuda_stream
+
+
+def ok(st):
+    nnb.check(st)
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def nrm(seed, *shape):
+    return orc.normal(seed, int(np.prod(shape))).reshape(shape)
+
+
+def assert_close(got, want, rel):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    assert got.shape == want.shape
+    err = np.abs(got - want)
+    bound = rel * np.abs(want).max() + rel * np.abs(want) + 1e-30
+    bad = err > bound
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside; worst {err.max():.3e} (scale {np.abs(want).max():.3e})"
+
+
+def oracle(N, Tq, Tk, D, H, q, k, v, g, pad, causal):
+    out, pr = orc.zeros(N, Tq, D), orc.zeros(N, H, Tq, Tk)
+    O.orc_attention_fwd(N, Tq, Tk, D, H, P(q), P(k), P(v), P(pad), causal, P(out), P(pr))
+    dq, dk, dv = orc.zeros(N, Tq, D), orc.zeros(N, Tk, D), orc.zeros(N, Tk, D)
+    O.orc_attention_bwd(N, Tq, Tk, D, H, P(g), P(q), P(k), P(v), P(pr), P(pad), causal, P(dq), 1, P(dk), 1, P(dv), 1)
+    return out, dq, dk, dv
+
+
+def run_flash(torch, N, Tq, Tk, D, H, tq, tk, tv, tg, tpad, causal, first=1, grads=None):
+    out = torch.empty(N, Tq, D, device="cuda")
+    lse = torch.empty(N, H, Tq, 2, device="cuda")
+    padp = tpad.data_ptr() if tpad is not None else None
+    ok(lib().nnb_flash_attention_fwd(S(torch), N, Tq, Tk, D, H, tq.data_ptr(), tk.data_ptr(), tv.data_ptr(), padp,
+                                     causal, out.data_ptr(), lse.data_ptr()))
+    if grads is None:
+        grads = (torch.empty(N, Tq, D, device="cuda"), torch.empty(N, Tk, D, device="cuda"),
+                 torch.empty(N, Tk, D, device="cuda"))
+    dq, dk, dv = grads
+    ok(lib().nnb_flash_attention_bwd(S(torch), N, Tq, Tk, D, H, tg.data_ptr(), tq.data_ptr(), tk.data_ptr(),
+                                     tv.data_ptr(), out.data_ptr(), lse.data_ptr(), padp, causal, dq.data_ptr(), first,
+                                     dk.data_ptr(), first, dv.data_ptr(), first))
+    torch.cuda.synchronize()
+    assert lib().nnb_device_error(S(torch)) == 0
+    return out, lse, dq, dk, dv
+
+
+CASES = [
+    # N, Tq, Tk, D, H, causal, pad
+    (3, 19, 19, 64, 1, 1, None),           # one partial tile, causal
+    (2, 70, 70, 128, 2, 0, None),          # two heads, ragged
+    (2, 200, 200, 128, 2, 1, None),        # causal across 128-row and 64-key tiles
+    (3, 33, 150, 64, 1, 0, "some"),        # Tq != Tk, padded keys
+    (2, 40, 96, 64, 1, 0, "all"),          # one sample with every key padded: uniform probabilities
+    (2, 256, 256, 512, 8, 1, None),        # the attention benchmark's head layout and length
+]
+
+
+@pytest.mark.parametrize("N,Tq,Tk,D,H,causal,padmode", CASES)
+def test_flash_attention_matches_oracle(cuda, N, Tq, Tk, D, H, causal, padmode):
+    torch = cuda
+    q, k, v, g = nrm(61, N, Tq, D), nrm(62, N, Tk, D), nrm(63, N, Tk, D), nrm(64, N, Tq, D)
+    pad = None
+    if padmode == "some":
+        pad = np.ones((N, Tk), np.float32)
+        pad[1, Tk - 7:] = 0.0
+        pad[2 % N, 3] = 0.0
+    elif padmode == "all":
+        pad = np.ones((N, Tk), np.float32)
+        pad[1, :] = 0.0
+    out_o, dq_o, dk_o, dv_o = oracle(N, Tq, Tk, D, H, q, k, v, g, pad, causal)
+    tq, tk, tv, tg = dev(torch, q), dev(torch, k), dev(torch, v), dev(torch, g)
+    tpad = dev(torch, pad) if pad is not None else None
+    out, lse, dq, dk, dv = run_flash(torch, N, Tq, Tk, D, H, tq, tk, tv, tg, tpad, causal)
+    assert_close(out.cpu().numpy(), out_o, 1e-4)
+    assert_close(dq.cpu().numpy(), dq_o, 1e-4)
+    assert_close(dk.cpu().numpy(), dk_o, 1e-4)
+    assert_close(dv.cpu().numpy(), dv_o, 1e-4)
+    # stats = (row max m, row sum l): m + log(l) is the log of the softmax normaliser
+    Dh = D // H
+    qh = q.reshape(N, Tq, H, Dh).transpose(0, 2, 1, 3).astype(np.float64)
+    kh = k.reshape(N, Tk, H, Dh).transpose(0, 2, 1, 3).astype(np.float64)
+    s = qh @ kh.transpose(0, 1, 3, 2) * (1.0 / np.sqrt(Dh))
+    if pad is not None:
+        s = np.where(pad[:, None, None, :] == 0.0, -1e9, s)
+    if causal:
+        s = np.where(np.triu(np.ones((Tq, Tk), bool), 1)[None, None], -np.inf, s)
+    m = s.max(-1, keepdims=True)
+    want_lse = (m + np.log(np.exp(s - m).sum(-1, keepdims=True)))[..., 0]
+    st = lse.cpu().numpy().astype(np.float64)
+    assert_close(st[..., 0] + np.log(st[..., 1]), want_lse, 1e-5)
+
+
+def test_flash_attention_deterministic_and_accumulates(cuda):
+    torch = cuda
+    N, T, D, H = 2, 190, 128, 2
+    q, k, v, g = nrm(71, N, T, D), nrm(72, N, T, D), nrm(73, N, T, D), nrm(74, N, T, D)
+    tq, tk, tv, tg = dev(torch, q), dev(torch, k), dev(torch, v), dev(torch, g)
+    a = run_flash(torch, N, T, T, D, H, tq, tk, tv, tg, None, 1)
+    b = run_flash(torch, N, T, T, D, H, tq, tk, tv, tg, None, 1)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    # first = 0 adds onto what the gradient buffers hold
+    grads = tuple(t.clone() for t in a[2:])
+    run_flash(torch, N, T, T, D, H, tq, tk, tv, tg, None, 1, first=0, grads=grads)
+    for acc, once in zip(grads, a[2:]):
+        assert torch.equal(acc, once + once)
+
+
+def test_flash_attention_matches_composed_path(cuda):
+    """The fused and the composed (probability-keeping) paths of the same op agree to fp32 rounding."""
+    torch = cuda
+    N, T, D, H = 4, 160, 256, 4
+    q, k, v, g = (dev(torch, nrm(s, N, T, D)) for s in (81, 82, 83, 84))
+    out_f, _, dq_f, dk_f, dv_f = run_flash(torch, N, T, T, D, H, q, k, v, g, None, 1)
+    out, pr = torch.empty(N, T, D, device="cuda"), torch.empty(N, H, T, T, device="cuda")
+    ok(lib().nnb_attention_fwd(S(torch), N, T, T, D, H, q.data_ptr(), k.data_ptr(), v.data_ptr(), None, 1,
+                               out.data_ptr(), pr.data_ptr()))
+    dq, dk, dv = (torch.empty(N, T, D, device="cuda") for _ in range(3))
+    ok(lib().nnb_attention_bwd(S(torch), N, T, T, D, H, g.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                               pr.data_ptr(), None, 1, dq.data_ptr(), 1, dk.data_ptr(), 1, dv.data_ptr(), 1))
+    for got, want in ((out_f, out), (dq_f, dq), (dk_f, dk), (dv_f, dv)):
+        assert_close(got.cpu().numpy(), want.cpu().numpy(), 1e-4)
+
+
+def test_flash_attention_tf32_mode(cuda):
+    torch = cuda
+    N, T, D, H = 2, 130, 128, 2
+    q, k, v, g = nrm(91, N, T, D), nrm(92, N, T, D), nrm(93, N, T, D), nrm(94, N, T, D)
+    out_o, dq_o, dk_o, dv_o = oracle(N, T, T, D, H, q, k, v, g, None, 1)
+    prev = lib().nnb_get_math_mode()
+    lib().nnb_set_math_mode(1)
+    try:
+        out, _, dq, dk, dv = run_flash(torch, N, T, T, D, H, *(dev(torch, a) for a in (q, k, v, g)), None, 1)
+    finally:
+        lib().nnb_set_math_mode(prev)
+    for got, want in ((out, out_o), (dq, dq_o), (dk, dk_o), (dv, dv_o)):
+        assert_close(got.cpu().numpy(), want, 5e-3)

@@ -53,14 +53,15 @@ def _train(torch, cfg, x_d, y_d, steps, lr, wd, shards=1, seed=3):
     return model, losses, grads
 
 
-def test_transformer_training_matches_reference(cuda):
+@pytest.mark.parametrize("dim,heads", [(32, 4), (128, 2)])     # head size 8: composed attention; 64: fused
+def test_transformer_training_matches_reference(cuda, dim, heads):
     torch = cuda
     ref = orc.ref()
     if ref is None:
         pytest.skip("reference library not built (oracle/_ref)")
     from nnb.nn import Transformer, TransformerConfig
 
-    cfg = TransformerConfig(vocab_size=64, dim=32, heads=4, layers=2, max_len=16)
+    cfg = TransformerConfig(vocab_size=64, dim=dim, heads=heads, layers=2, max_len=16)
     N, T, steps, lr, wd = 4, 16, 3, 1e-2, 1e-2
     x, y, x_d, y_d = _batch(torch, 64, N, T, 90)
     init = _flat(Transformer(cfg, seed=3))
@@ -69,7 +70,7 @@ def test_transformer_training_matches_reference(cuda):
     r_losses = np.zeros(steps, np.float32)
     r_grads = np.zeros_like(init)
     r_params = np.zeros_like(init)
-    n = ref.ref_transformer_train(64, 32, 4, 2, 16, N, T, orc.ptr(init), orc.ptr(x), orc.ptr(y), lr, wd, steps,
+    n = ref.ref_transformer_train(64, dim, heads, 2, 16, N, T, orc.ptr(init), orc.ptr(x), orc.ptr(y), lr, wd, steps,
                                   orc.ptr(r_losses), orc.ptr(r_grads), orc.ptr(r_params))
     assert n == init.size
     np.testing.assert_allclose(losses, r_losses, rtol=1e-5)
@@ -85,14 +86,15 @@ def test_transformer_training_matches_reference(cuda):
     assert losses[-1] < losses[0]
 
 
-def test_transformer_training_deterministic_and_shard_invariant(cuda):
+@pytest.mark.parametrize("dim,heads", [(64, 4), (128, 2)])      # head size 16: composed attention; 64: fused
+def test_transformer_training_deterministic_and_shard_invariant(cuda, dim, heads):
     torch = cuda
     import nnb
     from nnb import functional as F
     from nnb.nn import AdamW, Transformer, TransformerConfig
     from nnb.train import ShardedTrainer
 
-    cfg = TransformerConfig(vocab_size=96, dim=64, heads=4, layers=2, max_len=32)
+    cfg = TransformerConfig(vocab_size=96, dim=dim, heads=heads, layers=2, max_len=32)
     _, _, x_d, y_d = _batch(torch, 96, 8, 32, 91)
     m1, l1, g1 = _train(torch, cfg, x_d, y_d, 2, 3e-3, 1e-2, shards=8)
     m2, l2, _ = _train(torch, cfg, x_d, y_d, 2, 3e-3, 1e-2, shards=8)
