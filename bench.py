@@ -440,8 +440,7 @@ def run_transformer(steps: int, warmup: int, rank: int, world: int, local_rank: 
         tr.step(x_d, y_d)
     torch.cuda.synchronize()
     first_loss = float(tr.loss.cpu()[0])
-    nnb.trace_reset()
-    nnb.trace_enable(True)
+    nnb.trace_reset()                       # zeroes the launch counter; the tracer stays off here
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -451,11 +450,7 @@ def run_transformer(steps: int, warmup: int, rank: int, world: int, local_rank: 
     e1.record()
     torch.cuda.synchronize()
     barrier()
-    nnb.trace_enable(False)
     launches = nnb.launch_count()
-    kinds = {name: nnb.trace_query(k) for name, k in (("gemm", nnb.TRACE_GEMM), ("pack", nnb.TRACE_PACK),
-                                                      ("rowwise", nnb.TRACE_ROWWISE), ("attention", nnb.TRACE_ATTENTION),
-                                                      ("aux", nnb.TRACE_AUX))}
     ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
     # end to end: ids and targets from pinned host memory every step, the loss read back every step
     e0.record()
@@ -467,6 +462,18 @@ def run_transformer(steps: int, warmup: int, rank: int, world: int, local_rank: 
     e1.record()
     torch.cuda.synchronize()
     e2e = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+    # per-kind device time from the library's event tracer, on separate (untimed) steps: the tracer
+    # records two events around every launch, which costs host time
+    traced = min(steps, 3)
+    nnb.trace_reset()
+    nnb.trace_enable(True)
+    for _ in range(traced):
+        tr.step(x_d, y_d)
+    torch.cuda.synchronize()
+    nnb.trace_enable(False)
+    kinds = {name: nnb.trace_query(k) for name, k in (("gemm", nnb.TRACE_GEMM), ("pack", nnb.TRACE_PACK),
+                                                      ("rowwise", nnb.TRACE_ROWWISE), ("attention", nnb.TRACE_ATTENTION),
+                                                      ("aux", nnb.TRACE_AUX))}
     if world > 1:
         import torch.distributed as dist
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -482,7 +489,8 @@ def run_transformer(steps: int, warmup: int, rank: int, world: int, local_rank: 
                    "math_mode": "fp32x3"},
         "algorithmic_tflops": T5_FLOP_PER_STEP / (ms_v * 1e-3) / 1e12,
         "loss_after_warmup": first_loss, "loss_final": float(tr.loss.cpu()[0]),
-        "kernel_ms_per_step": {k: v[0] / steps for k, v in kinds.items()},
+        "kernel_ms_per_step": {k: v[0] / traced for k, v in kinds.items()},
+        "l2": "inputs larger than L2 (weights, optimizer state and activations are several GB per step)",
         "gpu_launches": int(launches),
         "e2e": {"value": tokens / (e2e.item() * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": int(x_h.numel() * 8 * 2), "d2h_bytes_per_step": 4},
