@@ -155,12 +155,12 @@ __global__ void __launch_bounds__(256) pack_rows_vec_kernel(const float* __restr
 	constexpr int S = kSplit ? 2 : 1;
 	const int e = blockIdx.y;
 	const float* Xb = X + (long long)(e / inner) * s_outer + (long long)(e % inner) * s_inner;
-	const long long K4 = (long long)KB * 4, total = (long long)Rp * K4;
+	// Rp * KB * 4 < 2^31 (checked on the host), so the index arithmetic stays in 32 bits
+	const unsigned K4 = (unsigned)KB * 4u, total = (unsigned)Rp * K4;
 	const long long batch_off = (long long)e * Rp * KB * 16 * S;
 	const int panel_floats = panel_rows * 16;
-	for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
-			idx += (long long)gridDim.x * blockDim.x) {
-		const int r = (int)(idx / K4), q = (int)(idx - (long long)r * K4), k = q * 4;
+	for (unsigned idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+		const int r = (int)(idx / K4), q = (int)(idx - (unsigned)r * K4), k = q * 4;
 		float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 		if (r < R && k < K) v = __ldg(reinterpret_cast<const float4*>(Xb + (long long)r * ldx + k));
 		const bool ok = isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
@@ -596,7 +596,7 @@ static void launch_pack(cudaStream_t s, const float* X, long long ldx, long long
 		int* flags, int* any) {
 	const bool base16 = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
 	const bool strides4 = ldx % 4 == 0 && s_outer % 4 == 0 && s_inner % 4 == 0;
-	if (!trans && base16 && strides4 && K % 4 == 0) {
+	if (!trans && base16 && strides4 && K % 4 == 0 && Rp * KB * 4 < (1LL << 31)) {
 		const long long work = Rp * KB * 4;
 		const unsigned blocks = (unsigned)std::max<long long>(1, std::min<long long>((work + 255) / 256, 148 * 16));
 		pack_rows_vec_kernel<kSplit><<<dim3(blocks, (unsigned)entries), 256, 0, s>>>(X, ldx, s_outer, s_inner, inner,
@@ -721,15 +721,29 @@ static int depth_pieces(const GemmDesc& d) {
 __global__ void depth_sum_kernel(const float* __restrict__ part, int pieces, long long m, long long n,
 		float* __restrict__ c, long long ldc, long long sc, int accumulate) {
 	const long long mn = m * n;
-	part += (long long)blockIdx.y * pieces * mn;
-	c += (long long)blockIdx.y * sc;
-	for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < mn;
-			idx += (long long)gridDim.x * blockDim.x) {
-		float acc = part[idx];
-		for (int p = 1; p < pieces; ++p) acc += part[p * mn + idx];
-		const long long i = idx / n, j = idx - i * n;
-		float* dst = c + i * ldc + j;
-		*dst = accumulate ? *dst + acc : acc + 0.0f;
+	part += (long long)blockIdx.z * pieces * mn;
+	c += (long long)blockIdx.z * sc;
+	// rows over grid.y, columns over grid.x: no per-element division; the pieces are summed in
+	// order, their loads issued ahead of the adds
+	for (long long i = blockIdx.y; i < m; i += gridDim.y) {
+		for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x) {
+			const float* src = part + i * n + j;
+			float v[8];
+			float acc = 0.0f;
+			int p = 0;
+			for (; p + 8 <= pieces; p += 8) {
+#pragma unroll
+				for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (long long)(p + u) * mn);
+#pragma unroll
+				for (int u = 0; u < 8; ++u) acc = (p + u == 0) ? v[u] : acc + v[u];
+			}
+			for (; p < pieces; ++p) {
+				const float x = __ldg(src + (long long)p * mn);
+				acc = p == 0 ? x : acc + x;
+			}
+			float* dst = c + i * ldc + j;
+			*dst = accumulate ? *dst + acc : acc + 0.0f;
+		}
 	}
 }
 
@@ -773,11 +787,12 @@ static nnb_status gemm_depth_cut(cudaStream_t s, const DeviceState* dev, const G
 			t.sc_outer = (long long)pieces * mn;
 			if ((st = gemm_direct(s, dev, t)) != NNB_OK) break;
 		}
-		const unsigned blocks = (unsigned)std::min<long long>((mn + 255) / 256, 148 * 16);
+		const unsigned bx = (unsigned)std::min<long long>((d.n + 255) / 256, 64);
+		const unsigned by = (unsigned)std::min<long long>(d.m, std::max<long long>(1, (148 * 16) / ((long long)bx * E)));
 		{
 			TraceScope ts(s, kTraceAux);
-			depth_sum_kernel<<<dim3(blocks, (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc, d.sc_outer,
-				d.accumulate);
+			depth_sum_kernel<<<dim3(bx, std::max(by, 1u), (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc,
+				d.sc_outer, d.accumulate);
 		}
 		st = cuda_status(cudaGetLastError(), "depth sum launch");
 	} while (0);

@@ -7,6 +7,7 @@
 // embedding (forward and backward) and AdamW give the reference's bits on the same inputs.
 // The loss ops use CUDA's expf/logf and a fixed warp-tree order for the row sums, so they agree
 // within tolerance rather than bit for bit.
+#include <algorithm>
 #include <cmath>
 
 #include "nnb_internal.h"
@@ -75,6 +76,81 @@ __global__ void accumulate_kernel(long long n, const float* __restrict__ src, fl
 		if (negate) dst[i] = first ? 0.0f - src[i] : dst[i] - src[i];
 		else dst[i] = first ? src[i] + 0.0f : dst[i] + src[i];
 	}
+}
+
+// Vector (float4) forms of the elementwise kernels, used when the length is a multiple of 4 and
+// every pointer is 16-byte aligned: four elements per thread and 16-byte accesses, each element
+// getting exactly the scalar kernel's operations.
+__device__ __forceinline__ float4 ld4(const float* p, long long i) { return __ldg(reinterpret_cast<const float4*>(p) + i); }
+
+__device__ __forceinline__ float4 store_rule(float4 v, const float4* dst, int first) {
+	if (first) return make_float4(v.x + 0.0f, v.y + 0.0f, v.z + 0.0f, v.w + 0.0f);
+	const float4 c = *dst;
+	return make_float4(c.x + v.x, c.y + v.y, c.z + v.z, c.w + v.w);
+}
+
+__global__ void gelu_bwd_vec_kernel(long long n4, const float* __restrict__ x, const float* __restrict__ th,
+		const float* __restrict__ g, float* __restrict__ dx, int first) {
+	GRID_STRIDE(i, n4) {
+		const float4 xv = ld4(x, i), gv = ld4(g, i);
+		const float4 tv = th ? ld4(th, i)
+			: make_float4(tanh_one(gelu_tanh_arg(xv.x)), tanh_one(gelu_tanh_arg(xv.y)), tanh_one(gelu_tanh_arg(xv.z)),
+				tanh_one(gelu_tanh_arg(xv.w)));
+		const float4 v = make_float4(gelu_bwd(gv.x, xv.x, tv.x), gelu_bwd(gv.y, xv.y, tv.y), gelu_bwd(gv.z, xv.z, tv.z),
+			gelu_bwd(gv.w, xv.w, tv.w));
+		float4* d = reinterpret_cast<float4*>(dx) + i;
+		*d = store_rule(v, d, first);
+	}
+}
+
+__global__ void add_same_vec_kernel(long long n4, const float* __restrict__ a, const float* __restrict__ b,
+		float* __restrict__ y) {
+	GRID_STRIDE(i, n4) {
+		const float4 u = ld4(a, i), v = ld4(b, i);
+		reinterpret_cast<float4*>(y)[i] = make_float4(u.x + v.x, u.y + v.y, u.z + v.z, u.w + v.w);
+	}
+}
+
+// b broadcast over the rows of a [rows, period]: rows over grid.y, float4 columns over grid.x
+__global__ void add_bcast_vec_kernel(long long rows, long long period4, const float* __restrict__ a,
+		const float* __restrict__ b, float* __restrict__ y) {
+	for (long long r = blockIdx.y; r < rows; r += gridDim.y)
+		for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < period4; c += (long long)gridDim.x * blockDim.x) {
+			const float4 u = ld4(a, r * period4 + c), v = ld4(b, c);
+			reinterpret_cast<float4*>(y)[r * period4 + c] = make_float4(u.x + v.x, u.y + v.y, u.z + v.z, u.w + v.w);
+		}
+}
+
+__global__ void accumulate_vec_kernel(long long n4, const float* __restrict__ src, float* __restrict__ dst, int first,
+		int negate) {
+	GRID_STRIDE(i, n4) {
+		const float4 v = ld4(src, i);
+		float4* d = reinterpret_cast<float4*>(dst) + i;
+		if (negate) {
+			if (first) {
+				*d = make_float4(0.0f - v.x, 0.0f - v.y, 0.0f - v.z, 0.0f - v.w);
+			} else {
+				const float4 c = *d;
+				*d = make_float4(c.x - v.x, c.y - v.y, c.z - v.z, c.w - v.w);
+			}
+		} else {
+			*d = store_rule(v, d, first);
+		}
+	}
+}
+
+// rows over grid.y (at most 65535, the kernel loops), enough column blocks for about 32 blocks per SM
+inline dim3 ce_bwd_grid(long long rows, int C) {
+	const unsigned bx = (unsigned)std::max(1, (C + 255) / 256);
+	const long long by = std::min<long long>(rows, std::max<long long>(1, 148 * 32 / bx));
+	return dim3(bx, (unsigned)std::min<long long>(by, 65535));
+}
+
+__host__ __device__ inline bool vec4_ok(long long n, const void* p0, const void* p1 = nullptr, const void* p2 = nullptr,
+		const void* p3 = nullptr) {
+	const uintptr_t m = reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1) |
+		reinterpret_cast<uintptr_t>(p2) | reinterpret_cast<uintptr_t>(p3);
+	return n % 4 == 0 && (m & 15) == 0;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -239,21 +315,24 @@ __global__ void ce_bwd_kernel(long long rows, int C, const float* __restrict__ s
 		const float* __restrict__ grad_loss, const float* __restrict__ norm, float* __restrict__ dlogits,
 		int first) {
 	const float scale = use_ignore ? grad_loss[0] * norm[0] : grad_loss[0] / norm[0];
-	GRID_STRIDE(i, rows * (long long)C) {
-		const long long r = i / C;
-		const int c = (int)(i % C);
+	// rows over grid.y, columns over grid.x
+	for (long long r = blockIdx.y; r < rows; r += gridDim.y) {
 		const int64_t t = targets[r];
-		float v = 0.0f;
-		if (!(use_ignore && t == ignore_index) && t >= 0 && t < C) {
-			if (ls == 0.0f && !use_ignore) {
-				v = (c == t ? softmax[i] - 1.0f : softmax[i]) * scale;            // ops.cpp:1835
-			} else {
-				float q = softmax[i] - ls / (float)C;                             // ops.cpp:1972-1974
-				if (c == t) q -= 1.0f - ls;
-				v = q * scale;
+		const bool live = !(use_ignore && t == ignore_index) && t >= 0 && t < C;
+		for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < C; c += gridDim.x * blockDim.x) {
+			const long long i = r * C + c;
+			float v = 0.0f;
+			if (live) {
+				if (ls == 0.0f && !use_ignore) {
+					v = (c == t ? softmax[i] - 1.0f : softmax[i]) * scale;            // ops.cpp:1835
+				} else {
+					float q = softmax[i] - ls / (float)C;                             // ops.cpp:1972-1974
+					if (c == t) q -= 1.0f - ls;
+					v = q * scale;
+				}
 			}
+			dlogits[i] = first ? v + 0.0f : dlogits[i] + v;
 		}
-		dlogits[i] = first ? v + 0.0f : dlogits[i] + v;
 	}
 }
 
@@ -415,7 +494,11 @@ nnb_status nnb_gelu_bwd(void* stream, size_t n, const float* x, const float* tan
 	if (n == 0) return NNB_OK;
 	if (!x || !g || !dx) return nnb::fail(NNB_ERR_INVALID, "gelu_bwd: null pointer");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::gelu_bwd_kernel, (long long)n, x, tanh_saved, g, dx, dx_first);
+	if (nnb::vec4_ok((long long)n, x, tanh_saved, g, dx))
+		NNB_LAUNCH(kTraceRowwise, grid_for(n / 4, 256), 256, nnb::gelu_bwd_vec_kernel, (long long)n / 4, x, tanh_saved, g,
+			dx, dx_first);
+	else
+		NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::gelu_bwd_kernel, (long long)n, x, tanh_saved, g, dx, dx_first);
 	return nnb::cuda_status(cudaGetLastError(), "gelu_bwd launch");
 }
 
@@ -440,7 +523,16 @@ nnb_status nnb_add_fwd(void* stream, size_t n, const float* a, const float* b, s
 	if (!a || !b || !y) return nnb::fail(NNB_ERR_INVALID, "add_fwd: null pointer");
 	if (b_period == 0 || n % b_period != 0) return nnb::fail(NNB_ERR_SHAPE, "add_fwd: %zu is not a multiple of %zu", n, b_period);
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::add_kernel, (long long)n, a, b, (long long)b_period, y);
+	if (b_period == n && nnb::vec4_ok((long long)n, a, b, y)) {
+		NNB_LAUNCH(kTraceRowwise, grid_for(n / 4, 256), 256, nnb::add_same_vec_kernel, (long long)n / 4, a, b, y);
+	} else if (nnb::vec4_ok((long long)b_period, a, b, y)) {
+		const long long rows = (long long)(n / b_period), p4 = (long long)b_period / 4;
+		const unsigned bx = (unsigned)std::min<long long>((p4 + 255) / 256, 64);
+		const unsigned by = (unsigned)std::min<long long>(rows, 65535);
+		NNB_LAUNCH(kTraceRowwise, dim3(bx, by), 256, nnb::add_bcast_vec_kernel, rows, p4, a, b, y);
+	} else {
+		NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::add_kernel, (long long)n, a, b, (long long)b_period, y);
+	}
 	return nnb::cuda_status(cudaGetLastError(), "add_fwd launch");
 }
 
@@ -448,7 +540,11 @@ nnb_status nnb_accumulate(void* stream, size_t n, const float* src, float* dst, 
 	if (n == 0) return NNB_OK;
 	if (!src || !dst) return nnb::fail(NNB_ERR_INVALID, "accumulate: null pointer");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::accumulate_kernel, (long long)n, src, dst, first, negate);
+	if (nnb::vec4_ok((long long)n, src, dst))
+		NNB_LAUNCH(kTraceRowwise, grid_for(n / 4, 256), 256, nnb::accumulate_vec_kernel, (long long)n / 4, src, dst, first,
+			negate);
+	else
+		NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::accumulate_kernel, (long long)n, src, dst, first, negate);
 	return nnb::cuda_status(cudaGetLastError(), "accumulate launch");
 }
 
@@ -512,8 +608,8 @@ nnb_status nnb_cross_entropy_bwd(void* stream, size_t N, size_t C, const float* 
 		return nnb::fail(NNB_ERR_INVALID, "cross_entropy_bwd: null pointer");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	const long long n = (long long)N * C;
-	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::ce_bwd_kernel, (long long)N, (int)C, softmax, targets, 0, 0,
-		0.0f, grad_loss, norm, dlogits, first);
+	NNB_LAUNCH(kTraceRowwise, nnb::ce_bwd_grid((long long)N, (int)C), 256, nnb::ce_bwd_kernel, (long long)N, (int)C, softmax,
+		targets, 0, 0, 0.0f, grad_loss, norm, dlogits, first);
 	return nnb::cuda_status(cudaGetLastError(), "cross_entropy_bwd launch");
 }
 
@@ -535,8 +631,8 @@ nnb_status nnb_sequence_ce_bwd(void* stream, size_t P, size_t V, const float* so
 		return nnb::fail(NNB_ERR_INVALID, "sequence_ce_bwd: null pointer");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	const long long n = (long long)P * V;
-	NNB_LAUNCH(kTraceRowwise, grid_for(n, 256), 256, nnb::ce_bwd_kernel, (long long)P, (int)V, softmax, targets,
-		ignore_index, 1, label_smoothing, grad_loss, norm, dlogits, first);
+	NNB_LAUNCH(kTraceRowwise, nnb::ce_bwd_grid((long long)P, (int)V), 256, nnb::ce_bwd_kernel, (long long)P, (int)V, softmax,
+		targets, ignore_index, 1, label_smoothing, grad_loss, norm, dlogits, first);
 	return nnb::cuda_status(cudaGetLastError(), "sequence_ce_bwd launch");
 }
 

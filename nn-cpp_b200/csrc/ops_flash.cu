@@ -151,11 +151,14 @@ __device__ __forceinline__ void vals_to_tmem16(const float (&v)[16], uint32_t ta
 	tmem_st_32x32b_x16(taddr_lo, lo);
 }
 
-// One MMA step (depth 8) of D (+)= A B in the given split; A from tensor memory (hi, lo columns) or
-// shared memory (hi, lo descriptors), B from shared-memory descriptors (hi, lo).
+// One MMA step (depth 8) of D (+)= A B, three TF32 MMAs (lo*hi, hi*lo, hi*hi) in the 3xTF32 split
+// or one (hi*hi) in TF32; A from tensor memory (hi, lo columns) or shared memory (hi, lo
+// descriptors), B from shared-memory descriptors (hi, lo). The caller passes descriptors built once
+// per tile plus compile-time offsets, so issuing an MMA costs a few instructions.
+template <int kSplit>
 __device__ __forceinline__ void mma_step(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t b_hi, uint64_t b_lo,
-		uint32_t idesc, uint32_t acc, int split) {
-	if (split) {
+		uint32_t idesc, uint32_t acc) {
+	if (kSplit) {
 		mma_tf32_ts(d, a_lo, b_hi, idesc, acc);
 		mma_tf32_ts(d, a_hi, b_lo, idesc, 1u);
 		mma_tf32_ts(d, a_hi, b_hi, idesc, 1u);
@@ -163,9 +166,10 @@ __device__ __forceinline__ void mma_step(uint32_t d, uint32_t a_hi, uint32_t a_l
 		mma_tf32_ts(d, a_hi, b_hi, idesc, acc);
 	}
 }
+template <int kSplit>
 __device__ __forceinline__ void mma_step_ss(uint32_t d, uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo,
-		uint32_t idesc, uint32_t acc, int split) {
-	if (split) {
+		uint32_t idesc, uint32_t acc) {
+	if (kSplit) {
 		mma_tf32(d, a_lo, b_hi, idesc, acc);
 		mma_tf32(d, a_hi, b_lo, idesc, 1u);
 		mma_tf32(d, a_hi, b_hi, idesc, 1u);
@@ -173,6 +177,10 @@ __device__ __forceinline__ void mma_step_ss(uint32_t d, uint64_t a_hi, uint64_t 
 		mma_tf32(d, a_hi, b_hi, idesc, acc);
 	}
 }
+
+// Descriptor of (tile base + byte offset): the start-address field holds address / 16 in its low 14
+// bits, and every tile here lies below 256 KB, so an offset is a plain add.
+__device__ __forceinline__ uint64_t desc_at(uint64_t d, uint32_t byte_offset) { return d + (byte_offset >> 4); }
 
 // ---------------------------------------------------------------------------------------------
 // Pack: x [N, T, D] (head h in columns h*64 .. h*64+63) -> the K-major and / or MN-major image of
@@ -310,6 +318,7 @@ __device__ __forceinline__ void fwd_item(const FwdParams& p, int w, int& q0, int
 	J = (key_end + kFwdKeys - 1) / kFwdKeys;
 }
 
+template <int kSplit>
 __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParams p) {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -344,7 +353,7 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 	}
 	const uint32_t tmem = fa_setup_tmem(&tmem_base_sh, warp);
 	volatile int* abort_flag = &abort_sh;
-	const int parts = p.split ? 2 : 1;
+	constexpr int parts = kSplit ? 2 : 1;
 	const uint32_t qbase = smem_u32(smem);
 
 	if (warp == 0) {
@@ -391,6 +400,7 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			// ---------------------------------- MMA issuer ----------------------------------
 			const uint32_t id_s = idesc_tf32(kFwdRows, kFwdKeys);
 			const uint32_t id_pv = idesc_tf32(kFwdRows, kDh) | kIdescBMajorMN;
+			const uint64_t qd = smem_desc_k_sw64(qbase);
 			int t = 0, i = 0;
 			bool ok = true;
 			for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
@@ -406,15 +416,14 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 							break;
 						}
 						tc_fence_after();
-						const uint32_t kbase = smem_u32(smem + kFwdStageBase + s * kFwdStageBytes);
+						const uint64_t kd = smem_desc_k_sw64(smem_u32(smem + kFwdStageBase + s * kFwdStageBytes));
 						const uint32_t d = tmem + kFColS + (tt & 1) * 128;
 #pragma unroll
 						for (int ks = 0; ks < kDh / 8; ++ks) {
 							const uint32_t qo = (ks >> 1) * (kFwdRows * 64) + (ks & 1) * 32;
 							const uint32_t ko = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
-							mma_step_ss(d, smem_desc_k_sw64(qbase + qo), smem_desc_k_sw64(qbase + kFwdQPart + qo),
-								smem_desc_k_sw64(kbase + ko), smem_desc_k_sw64(kbase + kFwdOpBytes + ko), id_s, ks > 0,
-								p.split);
+							mma_step_ss<kSplit>(d, desc_at(qd, qo), desc_at(qd, kFwdQPart + qo), desc_at(kd, ko),
+								desc_at(kd, kFwdOpBytes + ko), id_s, ks > 0);
 						}
 						mma_commit(smem_u32(&s_full[tt & 1]));
 						if (j == J - 1) mma_commit(smem_u32(&q_empty));
@@ -428,13 +437,13 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 							break;
 						}
 						tc_fence_after();
-						const uint32_t vbase = smem_u32(smem + kFwdStageBase + s * kFwdStageBytes + 2 * kFwdOpBytes);
+						const uint64_t vd = smem_desc_mn_sw128b32(
+							smem_u32(smem + kFwdStageBase + s * kFwdStageBytes + 2 * kFwdOpBytes), kFwdKeys * 128);
 						const uint32_t d = tmem + kFColPV + b * 64, pc = tmem + kFColS + b * 128;
 #pragma unroll
 						for (int ks = 0; ks < kFwdKeys / 8; ++ks)
-							mma_step(d, pc + ks * 8, pc + 64 + ks * 8, smem_desc_mn_sw128b32(vbase + ks * 1024, kFwdKeys * 128),
-								smem_desc_mn_sw128b32(vbase + kFwdOpBytes + ks * 1024, kFwdKeys * 128), id_pv, ks > 0,
-								p.split);
+							mma_step<kSplit>(d, pc + ks * 8, pc + 64 + ks * 8, desc_at(vd, ks * 1024),
+								desc_at(vd, kFwdOpBytes + ks * 1024), id_pv, ks > 0);
 						mma_commit(smem_u32(&pv_full[b]));
 						mma_commit(smem_u32(&kv_empty[s]));
 					}
@@ -643,6 +652,7 @@ __device__ __forceinline__ void dq_item(const BwdParams& p, int w, int& q0, int&
 	J = (key_end + kFwdKeys - 1) / kFwdKeys;
 }
 
+template <int kSplit>
 __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdParams p) {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -668,7 +678,7 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 	}
 	const uint32_t tmem = fa_setup_tmem(&tmem_base_sh, warp);
 	volatile int* abort_flag = &abort_sh;
-	const int parts = p.split ? 2 : 1;
+	constexpr int parts = kSplit ? 2 : 1;
 
 	if (warp == 0) {
 		if (lane == 0) {
@@ -718,18 +728,19 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 					}
 					tc_fence_after();
 					const uint32_t kbase = smem_u32(smem + s * kDqStageBytes);
-					const uint32_t vbase = kbase + 2 * kFwdOpBytes, kmn = kbase + 4 * kFwdOpBytes;
+					const uint64_t kd = smem_desc_k_sw64(kbase), vd = smem_desc_k_sw64(kbase + 2 * kFwdOpBytes);
+					const uint64_t kmd = smem_desc_mn_sw128b32(kbase + 4 * kFwdOpBytes, kFwdKeys * 128);
 #pragma unroll
 					for (int ks = 0; ks < kDh / 8; ++ks) {      // S = Q K^T
 						const uint32_t off = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
-						mma_step(tmem + kQColS, tmem + kQColQhi + ks * 8, tmem + kQColQlo + ks * 8,
-							smem_desc_k_sw64(kbase + off), smem_desc_k_sw64(kbase + kFwdOpBytes + off), id_s, ks > 0, p.split);
+						mma_step<kSplit>(tmem + kQColS, tmem + kQColQhi + ks * 8, tmem + kQColQlo + ks * 8, desc_at(kd, off),
+							desc_at(kd, kFwdOpBytes + off), id_s, ks > 0);
 					}
 #pragma unroll
 					for (int ks = 0; ks < kDh / 8; ++ks) {      // dP = dO V^T
 						const uint32_t off = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
-						mma_step(tmem + kQColP, tmem + kQColOhi + ks * 8, tmem + kQColOlo + ks * 8,
-							smem_desc_k_sw64(vbase + off), smem_desc_k_sw64(vbase + kFwdOpBytes + off), id_s, ks > 0, p.split);
+						mma_step<kSplit>(tmem + kQColP, tmem + kQColOhi + ks * 8, tmem + kQColOlo + ks * 8, desc_at(vd, off),
+							desc_at(vd, kFwdOpBytes + off), id_s, ks > 0);
 					}
 					mma_commit(smem_u32(&sdp_full));
 					if (!mbar_wait(smem_u32(&ds_full), tt & 1, p.err, kDevTimeoutAttn, abort_flag)) {
@@ -739,10 +750,8 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 					tc_fence_after();
 #pragma unroll
 					for (int ks = 0; ks < kFwdKeys / 8; ++ks)   // dQ += dS K
-						mma_step(tmem + kQColAcc, tmem + kQColS + ks * 8, tmem + kQColSlo + ks * 8,
-							smem_desc_mn_sw128b32(kmn + ks * 1024, kFwdKeys * 128),
-							smem_desc_mn_sw128b32(kmn + kFwdOpBytes + ks * 1024, kFwdKeys * 128), id_dq, (j > 0 || ks > 0),
-							p.split);
+						mma_step<kSplit>(tmem + kQColAcc, tmem + kQColS + ks * 8, tmem + kQColSlo + ks * 8,
+							desc_at(kmd, ks * 1024), desc_at(kmd, kFwdOpBytes + ks * 1024), id_dq, (j > 0 || ks > 0));
 					mma_commit(smem_u32(&kv_empty[s]));
 				}
 				if (!ok) break;
@@ -874,6 +883,7 @@ __device__ __forceinline__ void kv_item(const BwdParams& p, int w, int& k0, int&
 	J = qt_end - qt_begin;
 }
 
+template <int kSplit>
 __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const BwdParams p) {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -899,7 +909,7 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 	}
 	const uint32_t tmem = fa_setup_tmem(&tmem_base_sh, warp);
 	volatile int* abort_flag = &abort_sh;
-	const int parts = p.split ? 2 : 1;
+	constexpr int parts = kSplit ? 2 : 1;
 
 	if (warp == 0) {
 		if (lane == 0) {
@@ -953,18 +963,20 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 					}
 					tc_fence_after();
 					const uint32_t qbase = smem_u32(smem + s * kKvStageBytes);
-					const uint32_t obase = qbase + 2 * kKvOpBytes, qmn = qbase + 4 * kKvOpBytes, omn = qbase + 6 * kKvOpBytes;
+					const uint64_t qd = smem_desc_k_sw64(qbase), od = smem_desc_k_sw64(qbase + 2 * kKvOpBytes);
+					const uint64_t qmd = smem_desc_mn_sw128b32(qbase + 4 * kKvOpBytes, kKvQ * 128);
+					const uint64_t omd = smem_desc_mn_sw128b32(qbase + 6 * kKvOpBytes, kKvQ * 128);
 #pragma unroll
 					for (int ks = 0; ks < kDh / 8; ++ks) {      // S^T = K Q^T
 						const uint32_t off = (ks >> 1) * (kKvQ * 64) + (ks & 1) * 32;
-						mma_step(tmem + kKColS, tmem + kKColKhi + ks * 8, tmem + kKColKlo + ks * 8,
-							smem_desc_k_sw64(qbase + off), smem_desc_k_sw64(qbase + kKvOpBytes + off), id_s, ks > 0, p.split);
+						mma_step<kSplit>(tmem + kKColS, tmem + kKColKhi + ks * 8, tmem + kKColKlo + ks * 8, desc_at(qd, off),
+							desc_at(qd, kKvOpBytes + off), id_s, ks > 0);
 					}
 #pragma unroll
 					for (int ks = 0; ks < kDh / 8; ++ks) {      // dP^T = V dO^T
 						const uint32_t off = (ks >> 1) * (kKvQ * 64) + (ks & 1) * 32;
-						mma_step(tmem + kKColP, tmem + kKColVhi + ks * 8, tmem + kKColVlo + ks * 8,
-							smem_desc_k_sw64(obase + off), smem_desc_k_sw64(obase + kKvOpBytes + off), id_s, ks > 0, p.split);
+						mma_step<kSplit>(tmem + kKColP, tmem + kKColVhi + ks * 8, tmem + kKColVlo + ks * 8, desc_at(od, off),
+							desc_at(od, kKvOpBytes + off), id_s, ks > 0);
 					}
 					mma_commit(smem_u32(&sdp_full));
 					if (!mbar_wait(smem_u32(&pds_full), tt & 1, p.err, kDevTimeoutAttn, abort_flag)) {
@@ -976,13 +988,11 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 					for (int ks = 0; ks < kKvQ / 8; ++ks) {
 						const uint32_t acc = (j > 0 || ks > 0);
 						// dV += P^T dO
-						mma_step(tmem + kKColDv, tmem + kKColS + ks * 8, tmem + kKColSlo + ks * 8,
-							smem_desc_mn_sw128b32(omn + ks * 1024, kKvQ * 128),
-							smem_desc_mn_sw128b32(omn + kKvOpBytes + ks * 1024, kKvQ * 128), id_acc, acc, p.split);
+						mma_step<kSplit>(tmem + kKColDv, tmem + kKColS + ks * 8, tmem + kKColSlo + ks * 8, desc_at(omd, ks * 1024),
+							desc_at(omd, kKvOpBytes + ks * 1024), id_acc, acc);
 						// dK += dS^T Q
-						mma_step(tmem + kKColDk, tmem + kKColP + ks * 8, tmem + kKColPlo + ks * 8,
-							smem_desc_mn_sw128b32(qmn + ks * 1024, kKvQ * 128),
-							smem_desc_mn_sw128b32(qmn + kKvOpBytes + ks * 1024, kKvQ * 128), id_acc, acc, p.split);
+						mma_step<kSplit>(tmem + kKColDk, tmem + kKColP + ks * 8, tmem + kKColPlo + ks * 8, desc_at(qmd, ks * 1024),
+							desc_at(qmd, kKvOpBytes + ks * 1024), id_acc, acc);
 					}
 					mma_commit(smem_u32(&q_empty[s]));
 				}
@@ -1100,9 +1110,12 @@ static bool g_fa_attr[64];
 static nnb_status fa_set_attrs(int dev) {
 	std::lock_guard<std::mutex> lock(g_fa_mutex);
 	if (g_fa_attr[dev & 63]) return NNB_OK;
-	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
-	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem));
-	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
+	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
+	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
+	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_bwd_dq_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem));
+	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_bwd_dq_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDqSmem));
+	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_bwd_dkdv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
+	NNB_CUDA_TRY(cudaFuncSetAttribute(flash_bwd_dkdv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kKvSmem));
 	g_fa_attr[dev & 63] = true;
 	return NNB_OK;
 }
@@ -1183,8 +1196,9 @@ nnb_status nnb_flash_attention_fwd(void* stream, size_t N, size_t Tq, size_t Tk,
 		p.causal = causal ? 1 : 0; p.split = split;
 		p.scale = 1.0f / std::sqrt(static_cast<float>(nnb::kDh));     // ops.cpp:1236
 		nnb::TraceScope ts(s, nnb::kTraceAttention);
-		nnb::flash_fwd_kernel<<<nnb::persistent_grid(NH * p.q_tiles, dev->sm_count), nnb::kThreadsFa, nnb::kFwdSmem,
-			s>>>(p);
+		const unsigned grid = nnb::persistent_grid(NH * p.q_tiles, dev->sm_count);
+		if (split) nnb::flash_fwd_kernel<1><<<grid, nnb::kThreadsFa, nnb::kFwdSmem, s>>>(p);
+		else nnb::flash_fwd_kernel<0><<<grid, nnb::kThreadsFa, nnb::kFwdSmem, s>>>(p);
 		st = nnb::cuda_status(cudaGetLastError(), "flash attention forward launch");
 	} while (0);
 	nnb_status st2 = nnb::scratch_free(ws, s);
@@ -1242,12 +1256,14 @@ nnb_status nnb_flash_attention_bwd(void* stream, size_t N, size_t Tq, size_t Tk,
 		p.scale = 1.0f / std::sqrt(static_cast<float>(nnb::kDh));
 		nnb::TraceScope ts(s, nnb::kTraceAttention);
 		// the dQ kernel also writes the m, 1/l statistics the dKdV kernel reads
-		nnb::flash_bwd_dq_kernel<<<nnb::persistent_grid(NH * p.q_tiles, dev->sm_count), nnb::kThreadsFa, nnb::kDqSmem,
-			s>>>(p);
+		const unsigned gq = nnb::persistent_grid(NH * p.q_tiles, dev->sm_count);
+		if (split) nnb::flash_bwd_dq_kernel<1><<<gq, nnb::kThreadsFa, nnb::kDqSmem, s>>>(p);
+		else nnb::flash_bwd_dq_kernel<0><<<gq, nnb::kThreadsFa, nnb::kDqSmem, s>>>(p);
 		if ((st = nnb::cuda_status(cudaGetLastError(), "flash attention dQ launch")) != NNB_OK) break;
 		if (dk || dv) {
-			nnb::flash_bwd_dkdv_kernel<<<nnb::persistent_grid(NH * p.k_tiles, dev->sm_count), nnb::kThreadsFa,
-				nnb::kKvSmem, s>>>(p);
+			const unsigned gk = nnb::persistent_grid(NH * p.k_tiles, dev->sm_count);
+			if (split) nnb::flash_bwd_dkdv_kernel<1><<<gk, nnb::kThreadsFa, nnb::kKvSmem, s>>>(p);
+			else nnb::flash_bwd_dkdv_kernel<0><<<gk, nnb::kThreadsFa, nnb::kKvSmem, s>>>(p);
 			st = nnb::cuda_status(cudaGetLastError(), "flash attention dKdV launch");
 		}
 	} while (0);

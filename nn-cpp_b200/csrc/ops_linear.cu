@@ -29,10 +29,20 @@ __global__ void colsum_partial_kernel(const float* __restrict__ g, long long row
 	const long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x;
 	const long long c = blockIdx.y, chunks = gridDim.y, z = blockIdx.z;
 	if (j >= cols) return;
-	const float* gz = g + z * rows * cols;
+	const float* gz = g + z * rows * cols + j;
 	const long long r0 = c * kColChunk, r1 = min(rows, r0 + kColChunk);
+	// serial in row order; 32 loads are issued ahead of their adds so that each thread keeps enough
+	// bytes in flight for the column walk to run at HBM speed
 	float s = 0.0f;
-	for (long long r = r0; r < r1; ++r) s += gz[r * cols + j];
+	long long r = r0;
+	for (; r + 32 <= r1; r += 32) {
+		float v[32];
+#pragma unroll
+		for (int u = 0; u < 32; ++u) v[u] = __ldg(gz + (r + u) * cols);
+#pragma unroll
+		for (int u = 0; u < 32; ++u) s += v[u];
+	}
+	for (; r < r1; ++r) s += __ldg(gz + r * cols);
 	partial[(z * chunks + c) * cols + j] = s;
 }
 

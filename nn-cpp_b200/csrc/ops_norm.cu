@@ -94,8 +94,25 @@ __global__ void layernorm_bwd_param_partial(const float* __restrict__ g, const f
 	if (j >= D) return;
 	const long long base = z * R;
 	const long long r0 = base + c * kChunk, r1 = base + min(R, (c + 1) * kChunk);
+	// serial in row order, with 16 rows' loads issued ahead of their adds
 	float sg = 0.0f, sb = 0.0f;
-	for (long long r = r0; r < r1; ++r) {
+	long long r = r0;
+	for (; r + 16 <= r1; r += 16) {
+		float gv[16], xv[16], mv[16], iv[16];
+#pragma unroll
+		for (int u = 0; u < 16; ++u) {
+			gv[u] = __ldg(g + (r + u) * D + j);
+			xv[u] = __ldg(x + (r + u) * D + j);
+			mv[u] = __ldg(mean + r + u);
+			iv[u] = __ldg(inv_std + r + u);
+		}
+#pragma unroll
+		for (int u = 0; u < 16; ++u) {
+			sg += gv[u] * ((xv[u] - mv[u]) * iv[u]);
+			sb += gv[u];
+		}
+	}
+	for (; r < r1; ++r) {
 		const float gv = g[r * D + j];
 		sg += gv * ((x[r * D + j] - mean[r]) * inv_std[r]);
 		sb += gv;
