@@ -14,6 +14,7 @@
 // the reference's order exactly.
 #include "nnb_gemm.h"
 #include "nnb_internal.h"
+#include "nnb_math.cuh"
 #include "nnb_ops.h"
 #include "nnb_trace.h"
 
@@ -22,6 +23,23 @@ namespace nnb {
 namespace {
 
 constexpr int kColChunk = 256;
+
+// y = gelu(pre) with the tanh of the reference's Cephes method (ops.cpp:451-466), four elements per
+// thread when aligned
+__global__ void gelu_apply_vec_kernel(long long n4, const float* __restrict__ pre, float* __restrict__ y) {
+	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+		const float4 v = __ldg(reinterpret_cast<const float4*>(pre) + i);
+		reinterpret_cast<float4*>(y)[i] = make_float4(gelu_fwd(v.x, tanh_one(gelu_tanh_arg(v.x))),
+			gelu_fwd(v.y, tanh_one(gelu_tanh_arg(v.y))), gelu_fwd(v.z, tanh_one(gelu_tanh_arg(v.z))),
+			gelu_fwd(v.w, tanh_one(gelu_tanh_arg(v.w))));
+	}
+}
+__global__ void gelu_apply_kernel(long long n, const float* __restrict__ pre, float* __restrict__ y) {
+	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+		const float v = pre[i];
+		y[i] = gelu_fwd(v, tanh_one(gelu_tanh_arg(v)));
+	}
+}
 
 // partial[z][c][j] = sum over rows [c*kColChunk, ...) of group z of g[r][j], serial from +0.
 __global__ void colsum_partial_kernel(const float* __restrict__ g, long long rows, long long cols,
@@ -117,14 +135,24 @@ nnb_status nnb_linear_gelu_fwd(void* stream, size_t M, size_t K, size_t n, const
 	if (M == 0 || n == 0) return NNB_OK;
 	if (!x || !w || !bias || !y || !pre) return nnb::fail(NNB_ERR_INVALID, "linear_gelu_fwd: null pointer");
 	if (K == 0) return nnb::fail(NNB_ERR_SHAPE, "linear_gelu_fwd: zero input features");
+	// The GEMM stores pre = x w^T + b (bias in its epilogue); the GELU then runs as its own HBM-bound
+	// pass. Computing the Cephes tanh inside the GEMM epilogue (4 warps per SM) left the tensor cores
+	// waiting on it; the separate pass gives the same bits (the same function of the same pre).
 	nnb::GemmDesc d;
 	d.ta = 0; d.tb = 1;
 	d.m = (long long)M; d.n = (long long)n; d.k = (long long)K;
-	d.a = x; d.lda = (long long)K; d.b = w; d.ldb = (long long)K; d.c = y; d.ldc = (long long)n;
+	d.a = x; d.lda = (long long)K; d.b = w; d.ldb = (long long)K; d.c = pre; d.ldc = (long long)n;
 	d.mode = nnb::math_mode();
 	d.epi.bias = bias; d.epi.bias_mode = nnb::kBiasCol;
-	d.epi.act = nnb::kActGelu; d.epi.pre = pre; d.epi.ld_aux = (long long)n;
-	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_TRY(nnb::gemm_run(s, d));
+	const long long total = (long long)M * (long long)n;
+	nnb::TraceScope ts(s, nnb::kTraceRowwise);
+	if (total % 4 == 0 && ((reinterpret_cast<uintptr_t>(pre) | reinterpret_cast<uintptr_t>(y)) & 15) == 0)
+		nnb::gelu_apply_vec_kernel<<<nnb::grid_for(total / 4, 256), 256, 0, s>>>(total / 4, pre, y);
+	else
+		nnb::gelu_apply_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, pre, y);
+	return nnb::cuda_status(cudaGetLastError(), "linear_gelu_fwd gelu launch");
 }
 
 nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const float* g, const float* x,
