@@ -408,11 +408,24 @@ __global__ void embedding_place_kernel(long long count, int V, int chunks, const
 		sid[t - t0] = (id >= 0 && id < V) ? (int)id : -1;
 	}
 	__syncthreads();
-	if (threadIdx.x != 0) return;
-	for (long long t = t0; t < t1; ++t) {
-		const int id = sid[t - t0];
-		if (id < 0) continue;
-		order[slots[id]++] = (int)t;
+	if (threadIdx.x >= 32) return;
+	// warp 0 places the chunk's tokens in token order, 32 at a time: lanes holding the same id take
+	// consecutive slots in lane (= token) order, and the group's first lane advances the id's slot,
+	// which gives exactly the serial placement
+	const int lane = threadIdx.x;
+	for (long long base = t0; base < t1; base += 32) {
+		const long long t = base + lane;
+		const int id = t < t1 ? sid[t - t0] : -1;
+		const unsigned same = __match_any_sync(0xffffffffu, id);
+		const int leader = __ffs(same) - 1;
+		const int rank = __popc(same & ((1u << lane) - 1u));
+		int pos = 0;
+		if (id >= 0 && lane == leader) pos = slots[id];
+		pos = __shfl_sync(0xffffffffu, pos, leader);
+		if (id >= 0) order[pos + rank] = (int)t;
+		__syncwarp();
+		if (id >= 0 && lane == leader) slots[id] = pos + __popc(same);
+		__syncwarp();
 	}
 }
 

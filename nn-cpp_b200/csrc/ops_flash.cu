@@ -285,7 +285,7 @@ __device__ __forceinline__ void fa_release_tmem(uint32_t tmem, int warp) {
 // Forward
 // ---------------------------------------------------------------------------------------------
 struct FwdParams {
-	const float* pq;     // Q, K-major image, Tpq rows per head
+	const float* q;      // [N, Tq, D]
 	const float* pk;     // K, K-major image, Tpk rows per head
 	const float* pv;     // V, MN-major image
 	const float* pad;    // [N, Tk] key-padding mask (0 = padded) or null
@@ -293,20 +293,21 @@ struct FwdParams {
 	float* stats;        // [N, H, Tq, 2]: row max m, row sum l of exp(score - m)
 	int* err;
 	long long D;
-	int N, H, Tq, Tk, Tpq, Tpk, q_tiles, causal, split;
+	int N, H, Tq, Tk, Tpk, q_tiles, causal, split;
 	float scale;
 };
 
 constexpr int kFwdRows = 128;                               // query rows per item (MMA M)
 constexpr int kFwdKeys = 64;                                // keys per tile (S columns, PV depth)
-constexpr int kFwdStages = 2;
-constexpr uint32_t kFwdQPart = kPanels * kFwdRows * 64;     // 32 KB: Q hi or Q lo of one item
 constexpr uint32_t kFwdOpBytes = kPanels * kFwdKeys * 64;   // 16 KB: one of K hi, K lo, V hi, V lo
-constexpr uint32_t kFwdStageBytes = 4 * kFwdOpBytes;
-constexpr uint32_t kFwdStageBase = 2 * kFwdQPart;
-constexpr uint32_t kFwdSmem = kFwdStageBase + kFwdStages * kFwdStageBytes + 1024;
-// tensor-memory columns: S/P-hi b | P-lo b (b = 0, 1, 128 columns per buffer) | PV 0 | PV 1
-constexpr uint32_t kFColS = 0, kFColPV = 256;
+// K and V tiles stream through separate rings: a K slot is free once the tile's score MMAs are done,
+// a V slot once its P V MMAs are, so the K loads run further ahead
+constexpr int kFwdSlots = 3;
+constexpr uint32_t kFwdSlotBytes = 2 * kFwdOpBytes;         // hi, lo
+constexpr uint32_t kFwdVBase = kFwdSlots * kFwdSlotBytes;
+constexpr uint32_t kFwdSmem = 2 * kFwdSlots * kFwdSlotBytes + 1024;
+// tensor-memory columns: Q hi | Q lo | S/P-hi b, P-lo b (b = 0, 1; 128 columns per buffer) | PV 0 | PV 1
+constexpr uint32_t kFColQhi = 0, kFColQlo = 64, kFColS = 128, kFColPV = 384;
 
 // Work item w -> (sample, head) and query tile; key tiles it streams. A head's query tiles are
 // consecutive items (heaviest causal tile first), so the CTAs that run them at the same time share
@@ -318,12 +319,21 @@ __device__ __forceinline__ void fwd_item(const FwdParams& p, int w, int& q0, int
 	J = (key_end + kFwdKeys - 1) / kFwdKeys;
 }
 
+// This thread's half row of Q for item w (row index `row` of the item), its global address or null.
+__device__ __forceinline__ const float* fwd_q_row(const FwdParams& p, int w, int row, int half) {
+	int q0, nh, J;
+	fwd_item(p, w, q0, nh, J);
+	if (q0 + row >= p.Tq) return nullptr;
+	const int n = nh / p.H, h = nh % p.H;
+	return p.q + ((long long)n * p.Tq + q0 + row) * p.D + h * kDh + half * 32;
+}
+
 template <int kSplit>
 __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParams p) {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-	__shared__ __align__(8) uint64_t q_full, q_empty, kv_full[kFwdStages], kv_empty[kFwdStages], s_full[2], p_full[2],
-		pv_full[2], pv_empty[2], xbar[4][2], drain;
+	__shared__ __align__(8) uint64_t k_full[kFwdSlots], k_empty[kFwdSlots], v_full[kFwdSlots], v_empty[kFwdSlots],
+		s_full[2], p_full[2], pv_full[2], pv_empty[2], q_ready, xbar[4][2], drain;
 	__shared__ float xval[2][2][kFwdRows];          // [exchange parity][half][row]
 	__shared__ uint32_t tmem_base_sh;
 	__shared__ int abort_sh;
@@ -331,11 +341,11 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int W = p.N * p.H * p.q_tiles;
 	if (threadIdx.x == 0) {
-		mbar_init(smem_u32(&q_full), 1);
-		mbar_init(smem_u32(&q_empty), 1);
-		for (int s = 0; s < kFwdStages; ++s) {
-			mbar_init(smem_u32(&kv_full[s]), 1);
-			mbar_init(smem_u32(&kv_empty[s]), 1);
+		for (int s = 0; s < kFwdSlots; ++s) {
+			mbar_init(smem_u32(&k_full[s]), 1);
+			mbar_init(smem_u32(&k_empty[s]), 1);
+			mbar_init(smem_u32(&v_full[s]), 1);
+			mbar_init(smem_u32(&v_empty[s]), 1);
 		}
 		for (int b = 0; b < 2; ++b) {
 			mbar_init(smem_u32(&s_full[b]), 1);
@@ -347,6 +357,7 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			mbar_init(smem_u32(&xbar[qd][0]), 64);
 			mbar_init(smem_u32(&xbar[qd][1]), 64);
 		}
+		mbar_init(smem_u32(&q_ready), kMathThreads);
 		mbar_init(smem_u32(&drain), 1);
 		abort_sh = 0;
 		fence_mbar_init();
@@ -354,98 +365,94 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 	const uint32_t tmem = fa_setup_tmem(&tmem_base_sh, warp);
 	volatile int* abort_flag = &abort_sh;
 	constexpr int parts = kSplit ? 2 : 1;
-	const uint32_t qbase = smem_u32(smem);
 
 	if (warp == 0) {
 		if (lane == 0) {
 			// ------------------------------ bulk-copy producer ------------------------------
-			int t = 0, nq = 0;
+			int t = 0;
 			bool ok = true;
 			for (int w = blockIdx.x; ok && w < W; w += gridDim.x) {
 				int q0, nh, J;
 				fwd_item(p, w, q0, nh, J);
-				// Q of this item once the previous item's last score MMA has read its Q
-				if (nq >= 1 && !mbar_wait(smem_u32(&q_empty), (nq - 1) & 1, p.err, kDevTimeoutAttn, abort_flag)) break;
-				mbar_arrive_expect_tx(smem_u32(&q_full), parts * kFwdQPart);
-				for (int hl = 0; hl < parts; ++hl)
-					copy_kmajor(qbase + hl * kFwdQPart, p.pq + (long long)nh * packed_head_floats(p.Tpq), hl, p.Tpq, q0,
-						kFwdRows, smem_u32(&q_full));
-				++nq;
 				const float* kb = p.pk + (long long)nh * packed_head_floats(p.Tpk);
 				const float* vb = p.pv + (long long)nh * packed_head_floats(p.Tpk);
 				for (int j = 0; j < J; ++j, ++t) {
-					const int s = t % kFwdStages, use = t / kFwdStages;
-					if (use >= 1 &&
-							!mbar_wait(smem_u32(&kv_empty[s]), (use - 1) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
+					const int s = t % kFwdSlots, use = t / kFwdSlots;
+					const long long r0 = (long long)j * kFwdKeys;
+					if (use >= 1 && !mbar_wait(smem_u32(&k_empty[s]), (use - 1) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
 						ok = false;
 						break;
 					}
-					const uint32_t fb = smem_u32(&kv_full[s]);
-					mbar_arrive_expect_tx(fb, parts * 2 * kFwdOpBytes);
-					const uint32_t dst = smem_u32(smem + kFwdStageBase + s * kFwdStageBytes);
-					for (int hl = 0; hl < parts; ++hl) {
-						copy_kmajor(dst + hl * kFwdOpBytes, kb, hl, p.Tpk, (long long)j * kFwdKeys, kFwdKeys, fb);
-						copy_mnmajor(dst + 2 * kFwdOpBytes + hl * kFwdOpBytes, vb, hl, p.Tpk, (long long)j * kFwdKeys,
-							kFwdKeys, fb);
+					mbar_arrive_expect_tx(smem_u32(&k_full[s]), parts * kFwdOpBytes);
+					for (int hl = 0; hl < parts; ++hl)
+						copy_kmajor(smem_u32(smem + s * kFwdSlotBytes + hl * kFwdOpBytes), kb, hl, p.Tpk, r0, kFwdKeys,
+							smem_u32(&k_full[s]));
+					if (use >= 1 && !mbar_wait(smem_u32(&v_empty[s]), (use - 1) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
+						ok = false;
+						break;
 					}
+					mbar_arrive_expect_tx(smem_u32(&v_full[s]), parts * kFwdOpBytes);
+					for (int hl = 0; hl < parts; ++hl)
+						copy_mnmajor(smem_u32(smem + kFwdVBase + s * kFwdSlotBytes + hl * kFwdOpBytes), vb, hl, p.Tpk, r0,
+							kFwdKeys, smem_u32(&v_full[s]));
 				}
 			}
-			// every issued copy has landed before the CTA can exit
-			if (nq >= 1) drain_wait(smem_u32(&q_full), (nq - 1) & 1, p.err);
-			for (int tt = max(0, t - kFwdStages); tt < t; ++tt)
-				drain_wait(smem_u32(&kv_full[tt % kFwdStages]), (tt / kFwdStages) & 1, p.err);
+			// every issued copy has landed before the CTA can exit (a V copy is issued after its K copy)
+			for (int tt = max(0, t - kFwdSlots); tt < t; ++tt) {
+				drain_wait(smem_u32(&k_full[tt % kFwdSlots]), (tt / kFwdSlots) & 1, p.err);
+				drain_wait(smem_u32(&v_full[tt % kFwdSlots]), (tt / kFwdSlots) & 1, p.err);
+			}
 		}
 	} else if (warp == 1) {
 		if (lane == 0) {
 			// ---------------------------------- MMA issuer ----------------------------------
 			const uint32_t id_s = idesc_tf32(kFwdRows, kFwdKeys);
 			const uint32_t id_pv = idesc_tf32(kFwdRows, kDh) | kIdescBMajorMN;
-			const uint64_t qd = smem_desc_k_sw64(qbase);
 			int t = 0, i = 0;
 			bool ok = true;
 			for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
 				int q0, nh, J;
 				fwd_item(p, w, q0, nh, J);
-				if (!mbar_wait(smem_u32(&q_full), i & 1, p.err, kDevTimeoutAttn, abort_flag)) break;
+				// this item's Q is in tensor memory (written after the previous item's last score MMA)
+				if (!mbar_wait(smem_u32(&q_ready), i & 1, p.err, kDevTimeoutAttn, abort_flag)) break;
 				tc_fence_after();
 				for (int j = 0; j <= J; ++j) {
 					if (j < J) {                       // S_t = Q K_t^T
-						const int tt = t + j, s = tt % kFwdStages;
-						if (!mbar_wait(smem_u32(&kv_full[s]), (tt / kFwdStages) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
+						const int tt = t + j, s = tt % kFwdSlots;
+						if (!mbar_wait(smem_u32(&k_full[s]), (tt / kFwdSlots) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
 							ok = false;
 							break;
 						}
 						tc_fence_after();
-						const uint64_t kd = smem_desc_k_sw64(smem_u32(smem + kFwdStageBase + s * kFwdStageBytes));
+						const uint64_t kd = smem_desc_k_sw64(smem_u32(smem + s * kFwdSlotBytes));
 						const uint32_t d = tmem + kFColS + (tt & 1) * 128;
 #pragma unroll
 						for (int ks = 0; ks < kDh / 8; ++ks) {
-							const uint32_t qo = (ks >> 1) * (kFwdRows * 64) + (ks & 1) * 32;
 							const uint32_t ko = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
-							mma_step_ss<kSplit>(d, desc_at(qd, qo), desc_at(qd, kFwdQPart + qo), desc_at(kd, ko),
+							mma_step<kSplit>(d, tmem + kFColQhi + ks * 8, tmem + kFColQlo + ks * 8, desc_at(kd, ko),
 								desc_at(kd, kFwdOpBytes + ko), id_s, ks > 0);
 						}
 						mma_commit(smem_u32(&s_full[tt & 1]));
-						if (j == J - 1) mma_commit(smem_u32(&q_empty));
+						mma_commit(smem_u32(&k_empty[s]));
 					}
 					if (j >= 1) {                      // O_t-1 part = P_t-1 V_t-1
-						const int tp = t + j - 1, b = tp & 1, s = tp % kFwdStages;
+						const int tp = t + j - 1, b = tp & 1, s = tp % kFwdSlots;
 						if (!mbar_wait(smem_u32(&p_full[b]), (tp >> 1) & 1, p.err, kDevTimeoutAttn, abort_flag) ||
 								(tp >= 2 && !mbar_wait(smem_u32(&pv_empty[b]), ((tp >> 1) - 1) & 1, p.err, kDevTimeoutAttn,
-									abort_flag))) {
+									abort_flag)) ||
+								!mbar_wait(smem_u32(&v_full[s]), (tp / kFwdSlots) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
 							ok = false;
 							break;
 						}
 						tc_fence_after();
-						const uint64_t vd = smem_desc_mn_sw128b32(
-							smem_u32(smem + kFwdStageBase + s * kFwdStageBytes + 2 * kFwdOpBytes), kFwdKeys * 128);
+						const uint64_t vd = smem_desc_mn_sw128b32(smem_u32(smem + kFwdVBase + s * kFwdSlotBytes), kFwdKeys * 128);
 						const uint32_t d = tmem + kFColPV + b * 64, pc = tmem + kFColS + b * 128;
 #pragma unroll
 						for (int ks = 0; ks < kFwdKeys / 8; ++ks)
 							mma_step<kSplit>(d, pc + ks * 8, pc + 64 + ks * 8, desc_at(vd, ks * 1024),
 								desc_at(vd, kFwdOpBytes + ks * 1024), id_pv, ks > 0);
 						mma_commit(smem_u32(&pv_full[b]));
-						mma_commit(smem_u32(&kv_empty[s]));
+						mma_commit(smem_u32(&v_empty[s]));
 					}
 				}
 				t += J;
@@ -468,6 +475,15 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			++xuse;
 			return r;
 		};
+		// Q of item w into tensor memory (zeros past Tq), then the MMA warp may issue its scores
+		auto load_q = [&](int w) {
+			const float* src = fwd_q_row(p, w, row, half);
+			half_row_to_tmem(src, src != nullptr, lb + kFColQhi + half * 32, lb + kFColQlo + half * 32);
+			tmem_wait_st();
+			tc_fence_before();
+			mbar_arrive(smem_u32(&q_ready));
+		};
+		if (blockIdx.x < W) load_q(blockIdx.x);
 		bool ok = true;
 		for (int w = blockIdx.x; ok && w < W; w += gridDim.x) {
 			int q0, nh, J;
@@ -475,6 +491,11 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			const int n = nh / p.H, h = nh % p.H;
 			const int qrow = q0 + row;
 			const bool row_ok = qrow < p.Tq;
+			const int wn = w + (int)gridDim.x;
+			if (wn < W) {
+				const float* nq = fwd_q_row(p, wn, row, half);
+				if (nq) prefetch_l2(nq);
+			}
 			const float* padn = p.pad ? p.pad + (long long)n * p.Tk : nullptr;
 			float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
 			float o[32];
@@ -563,6 +584,9 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 				tmem_wait_st();
 				tc_fence_before();
 				mbar_arrive(smem_u32(&p_full[b]));
+				// after the item's last tile every score MMA of the item has completed (s_full was
+				// observed), so the next item's Q can replace this one while P V and the epilogue run
+				if (j == J - 1 && wn < W) load_q(wn);
 				if (j >= 1 && !fold(tt - 1)) {
 					ok = false;
 					break;
@@ -1174,24 +1198,22 @@ nnb_status nnb_flash_attention_fwd(void* stream, size_t N, size_t Tq, size_t Tk,
 	const int split = nnb::math_mode() == NNB_MATH_FP32X3 ? 1 : 0;
 	const long long NH = (long long)N * heads;
 	const long long Tpq = nnb::round_up((long long)Tq, nnb::kRowAlign), Tpk = nnb::round_up((long long)Tk, nnb::kRowAlign);
-	const long long fq = NH * nnb::packed_head_floats(Tpq), fk = NH * nnb::packed_head_floats(Tpk);
+	const long long fk = NH * nnb::packed_head_floats(Tpk);
 	void* ws = nullptr;
-	NNB_TRY(nnb::scratch_alloc(&ws, (size_t)(fq + 2 * fk) * sizeof(float), s));
-	float* pq = static_cast<float*>(ws);
-	float* pk = pq + fq;
+	NNB_TRY(nnb::scratch_alloc(&ws, (size_t)(2 * fk) * sizeof(float), s));
+	float* pk = static_cast<float*>(ws);
 	float* pv = pk + fk;
 	nnb_status st = NNB_OK;
 	do {
 		nnb::PackSet ps{};
-		ps.src[0] = q; ps.kdst[0] = pq; ps.T[0] = (int)Tq; ps.Tp[0] = (int)Tpq;       // S = Q K^T
-		ps.src[1] = k; ps.kdst[1] = pk; ps.T[1] = (int)Tk; ps.Tp[1] = (int)Tpk;
-		ps.src[2] = v; ps.mdst[2] = pv; ps.T[2] = (int)Tk; ps.Tp[2] = (int)Tpk;       // O += P V
-		if ((st = nnb::fa_pack(s, 3, ps, NH, (int)heads, (long long)D, split)) != NNB_OK) break;
+		ps.src[0] = k; ps.kdst[0] = pk; ps.T[0] = (int)Tk; ps.Tp[0] = (int)Tpk;       // S = Q K^T
+		ps.src[1] = v; ps.mdst[1] = pv; ps.T[1] = (int)Tk; ps.Tp[1] = (int)Tpk;       // O += P V
+		if ((st = nnb::fa_pack(s, 2, ps, NH, (int)heads, (long long)D, split)) != NNB_OK) break;
 		nnb::FwdParams p{};
-		p.pq = pq; p.pk = pk; p.pv = pv; p.pad = key_padding_mask; p.out = out; p.stats = stats;
+		p.q = q; p.pk = pk; p.pv = pv; p.pad = key_padding_mask; p.out = out; p.stats = stats;
 		p.err = dev->error_word;
 		p.D = (long long)D; p.N = (int)N; p.H = (int)heads; p.Tq = (int)Tq; p.Tk = (int)Tk;
-		p.Tpq = (int)Tpq; p.Tpk = (int)Tpk;
+		p.Tpk = (int)Tpk;
 		p.q_tiles = (int)((Tq + nnb::kFwdRows - 1) / nnb::kFwdRows);
 		p.causal = causal ? 1 : 0; p.split = split;
 		p.scale = 1.0f / std::sqrt(static_cast<float>(nnb::kDh));     // ops.cpp:1236
