@@ -129,7 +129,7 @@ def _dp_worker(rank, world, port, out_dir):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        cfg = TransformerConfig(vocab_size=128, dim=64, heads=4, layers=2, max_len=64)
+        cfg = TransformerConfig(vocab_size=128, dim=128, heads=2, layers=2, max_len=64)   # head size 64: fused attention
         g = torch.Generator().manual_seed(3)
         ids = torch.randint(0, 128, (8, 65), generator=g)
         x, y = ids[:, :-1].contiguous().cuda(), ids[:, 1:].contiguous().cuda()
