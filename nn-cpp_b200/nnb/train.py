@@ -3,21 +3,29 @@
 The global batch is cut into a fixed number of virtual shards S (8 for the 64-sequence config).
 Each rank runs ONE forward and backward over the sequences of the shards it owns, with every
 parameter-gradient op writing one gradient per shard (the *_grouped entry points: per-shard weight
-gradients as one batched GEMM, per-shard bias / LayerNorm / embedding sums). The [S_local, P]
-shard gradients are all-gathered (NCCL over NVLink, one collective per step) into [S, P], and every
-rank sums the S rows in shard order 0, 1, ..., S-1 with one kernel (a serial sum from +0 per
-element) before the identical AdamW step.
+gradients as one batched GEMM, per-shard bias / LayerNorm / embedding sums), into [S_local, P].
+
+The parameters live in one flat buffer (each parameter a view of it), cut into `world` equal
+slices. One NCCL all-to-all gives every rank the S shard gradients of its own slice, in shard order
+([S, P/world]); the rank sums those S rows in shard order 0, 1, ..., S-1 (a serial sum from +0 per
+element), runs AdamW on its slice (one launch: AdamW is elementwise and its settings are shared by
+all parameters), and an in-place all-gather returns the updated slices to every rank. Per step a
+rank receives (world-1)/world of S_local x P gradients plus (world-1)/world of P weights, instead of
+every shard's full gradient.
 
 Every shard's arithmetic is independent of how many GPUs there are (a row's result never depends on
-how many rows a kernel processes, and the per-shard sums run over the shard's own rows), and so is
-the order of the final sum: the weights after a step are bitwise identical at 1, 2, 4 or 8 GPUs.
-The reference has no distributed training; its guarantee is the same independence from the thread
-count (tests/test_transformer.cpp:525).
+how many rows a kernel processes, and the per-shard sums run over the shard's own rows), and so are
+the order of the final sum and the elementwise update: the weights after a step are bitwise
+identical at 1, 2, 4 or 8 GPUs. The reference has no distributed training; its guarantee is the same
+independence from the thread count (tests/test_transformer.cpp:525).
 
 The loss gradient is normalised by the global number of positions (grad_norm), so the update is
-the one of the mean loss over the global batch.
+the one of the mean loss over the global batch. The trainer takes the optimizer's settings and step
+counter and performs its update itself (AdamW's per-parameter moment buffers are not used).
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -37,9 +45,30 @@ class ShardedTrainer:
         self.sizes = [p.data.numel() for p in self.params]
         self.total = sum(self.sizes)
         dev = self.params[0].data.device
+        s = torch.cuda.current_stream(dev).cuda_stream
+        # flat parameter storage, padded to `world` equal slices; parameters become views of it
+        self.chunk = -(-self.total // world)
+        self.flat_w = empty((self.chunk * world,), device=dev)
+        check(lib().nnb_fill(s, self.flat_w.numel(), 0.0, self.flat_w.data_ptr()))
+        off = 0
+        for p, n in zip(self.params, self.sizes):
+            view = self.flat_w[off: off + n].view(p.data.shape)
+            view.copy_(p.data)
+            p.data = view
+            off += n
+        self.lo = rank * self.chunk
+        self.hi = min(self.total, self.lo + self.chunk)
+        self.m, self.v = empty((self.chunk,), device=dev), empty((self.chunk,), device=dev)
+        for t in (self.m, self.v):
+            check(lib().nnb_fill(s, t.numel(), 0.0, t.data_ptr()))
         self.shard_grads = empty((len(self.owned), self.total), device=dev)
-        self.all_grads = self.shard_grads if world == 1 else empty((shards, self.total), device=dev)
-        self.reduced = empty((self.total,), device=dev)
+        if world > 1:
+            self.send = empty((world, len(self.owned), self.chunk), device=dev)
+            check(lib().nnb_fill(s, self.send.numel(), 0.0, self.send.data_ptr()))    # padding stays zero
+            self.recv = empty((shards, self.chunk), device=dev)
+            self.reduced = empty((self.chunk,), device=dev)
+        else:
+            self.reduced = empty((self.total,), device=dev)
         self.grad_norm = None
         self.local_loss = empty((1,), device=dev)
         self.all_loss = self.local_loss if world == 1 else empty((world,), device=dev)
@@ -52,6 +81,12 @@ class ShardedTrainer:
             p.grad = flat[..., off: off + n] if flat.dim() == 2 else flat[off: off + n].view(p.data.shape)
             p.grad_fresh = True
             off += n
+
+    def _adamw(self, s, n: int, w_ptr: int, g_ptr: int) -> None:
+        o = self.opt
+        check(lib().nnb_adamw_step(s, n, w_ptr, g_ptr, self.m.data_ptr(), self.v.data_ptr(), ctypes.c_float(o.lr),
+                                   ctypes.c_float(o.beta1), ctypes.c_float(o.beta2), ctypes.c_float(o.eps),
+                                   ctypes.c_float(o.weight_decay), o.t))
 
     def step(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """One step on the global batch ids/targets [B, T] (device int64); returns the mean loss
@@ -70,16 +105,28 @@ class ShardedTrainer:
             loss.backward()
         if any(p.grad_fresh for p in self.params):
             raise RuntimeError("a parameter received no gradient")
-        check(lib().nnb_accumulate(s, 1, loss.data.data_ptr(), self.local_loss.data_ptr(), 1, 0))
-        if self.world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(self.all_grads, self.shard_grads, group=self.group)
-            dist.all_gather_into_tensor(self.all_loss, self.local_loss, group=self.group)
-        check(lib().nnb_column_sum(s, self.shards, self.total, self.all_grads.data_ptr(), self.reduced.data_ptr(), 1))
-        self._point_grads(self.reduced)
         for p in self.params:
             p.grad_fresh = False
-        self.opt.step()
+        check(lib().nnb_accumulate(s, 1, loss.data.data_ptr(), self.local_loss.data_ptr(), 1, 0))
+        self.opt.t += 1
+        if self.world == 1:
+            check(lib().nnb_column_sum(s, self.shards, self.total, self.shard_grads.data_ptr(),
+                                       self.reduced.data_ptr(), 1))
+            self._adamw(s, self.total, self.flat_w.data_ptr(), self.reduced.data_ptr())
+        else:
+            import torch.distributed as dist
+            # my shards' gradients, cut by destination slice: send[d] = shard_grads[:, d-th slice]
+            for d in range(self.world):
+                d_lo, d_hi = d * self.chunk, min(self.total, (d + 1) * self.chunk)
+                self.send[d, :, : d_hi - d_lo].copy_(self.shard_grads[:, d_lo:d_hi])
+            # every rank's shards of my slice, source ranks in order = shards in order
+            dist.all_to_all_single(self.recv, self.send.view(self.world * len(self.owned), self.chunk),
+                                   group=self.group)
+            dist.all_gather_into_tensor(self.all_loss, self.local_loss, group=self.group)
+            check(lib().nnb_column_sum(s, self.shards, self.chunk, self.recv.data_ptr(), self.reduced.data_ptr(), 1))
+            self._adamw(s, self.hi - self.lo, self.flat_w[self.lo:].data_ptr(), self.reduced.data_ptr())
+            dist.all_gather_into_tensor(self.flat_w, self.flat_w[self.rank * self.chunk:(self.rank + 1) * self.chunk],
+                                        group=self.group)
         # mean loss over ranks (each rank's loss is the mean over its equal share of positions)
         check(lib().nnb_column_sum(s, self.world, 1, self.all_loss.data_ptr(), self.loss.data_ptr(), 1))
         check(lib().nnb_scale(s, 1, 1.0 / self.world, self.loss.data_ptr(), self.loss.data_ptr()))
