@@ -176,6 +176,21 @@ NNB_API nnb_status nnb_batchnorm_bwd(void* stream, size_t N, size_t C, size_t S,
 		const float* weight, const float* mean, const float* inv_std, const unsigned char* alive, float* dx,
 		int dx_first, float* dweight, int dweight_first, float* dbias, int dbias_first);
 
+/* BatchNorm1d / BatchNorm2d module pieces (src/nn/batchnorm.cpp): after a training-mode forward,
+ * running_mean = (1 - momentum) running_mean + momentum mean and, when count > 1, running_var =
+ * (1 - momentum) running_var + momentum var count / (count - 1) (batchnorm.cpp:38-47; count = N*S). */
+NNB_API nnb_status nnb_batchnorm_running_update(void* stream, size_t C, size_t count, const float* mean,
+		const float* var, float momentum, float* running_mean, float* running_var);
+/* Evaluation mode (batchnorm.cpp:51-55): y = ((x - running_mean) / sqrt(running_var + eps)) w + b,
+ * optionally followed by ReLU with its alive mask; the backward gives dx, dweight and dbias. */
+NNB_API nnb_status nnb_batchnorm_eval_fwd(void* stream, size_t N, size_t C, size_t S, const float* x,
+		const float* running_mean, const float* running_var, float eps, const float* weight, const float* bias,
+		int fuse_relu, float* y, unsigned char* alive);
+NNB_API nnb_status nnb_batchnorm_eval_bwd(void* stream, size_t N, size_t C, size_t S, const float* g, const float* x,
+		const float* running_mean, const float* running_var, float eps, const float* weight,
+		const unsigned char* alive, float* dx, int dx_first, float* dweight, int dweight_first, float* dbias,
+		int dbias_first);
+
 /* ---- attention (replaces Value attention, ops.hpp:324; ops.cpp:1183-1296) ------------------ */
 
 /* q [N, Tq, D], k/v [N, Tk, D], heads | D; key_padding_mask [N, Tk] (0 = padded) or NULL;
@@ -221,6 +236,18 @@ NNB_API nnb_status nnb_conv2d_bwd(void* stream, size_t N, size_t Cin, size_t H, 
 		const unsigned char* alive, float* dx, int dx_first, float* dweight, int dweight_first, float* dbias,
 		int dbias_first);
 
+/* conv2d with dilation and groups (replaces the general conv2d, ops.hpp:421; ops.cpp:1525-1607):
+ * weight [Cout, Cin/groups, kh, kw]; per sample and group an im2col + GEMM, the bias added after
+ * the product; the backward's bias gradient sums samples then positions serially, the weight
+ * gradient sums per-sample products in sample order, as the reference. */
+NNB_API nnb_status nnb_conv2d_ex_fwd(void* stream, size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh,
+		size_t kw, int stride, int padding, int dilation, int groups, const float* x, const float* weight,
+		const float* bias, float* y);
+NNB_API nnb_status nnb_conv2d_ex_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh,
+		size_t kw, int stride, int padding, int dilation, int groups, const float* grad, const float* x,
+		const float* weight, float* dx, int dx_first, float* dweight, int dweight_first, float* dbias,
+		int dbias_first);
+
 /* ---- support ops on the configs' paths ----------------------------------------------------- */
 
 /* relu (ops.cpp:775-793) */
@@ -244,6 +271,17 @@ NNB_API nnb_status nnb_maxpool2d_fwd(void* stream, size_t N, size_t C, size_t H,
 		size_t stride, const float* x, float* y, uint32_t* argmax);
 NNB_API nnb_status nnb_maxpool2d_bwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel,
 		size_t stride, const float* g, const uint32_t* argmax, float* dx, int dx_first);
+/* avgpool2d (ops.cpp:1707-1772): window sums in (row, column) order times 1/kernel^2. */
+NNB_API nnb_status nnb_avgpool2d_fwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel,
+		size_t stride, const float* x, float* y);
+NNB_API nnb_status nnb_avgpool2d_bwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel,
+		size_t stride, const float* g, float* dx, int dx_first);
+/* sum / mean over one axis of x viewed as [outer, n, inner] (Value sum / mean, ops.hpp:86-88;
+ * reduce_axis ops.cpp:284-376): a serial sum from +0, times 1/n for the mean. */
+NNB_API nnb_status nnb_reduce_axis_fwd(void* stream, size_t outer, size_t n, size_t inner, const float* x, int average,
+		float* y);
+NNB_API nnb_status nnb_reduce_axis_bwd(void* stream, size_t outer, size_t n, size_t inner, const float* g, int average,
+		float* dx, int dx_first);
 /* cross_entropy_loss (ops.cpp:1774-1840) over logits [N, C], targets (device int64) [N]; loss and
  * norm are device scalars (norm = N, the divisor of the backward scale). An out-of-range target
  * makes the loss NaN and sets the device error word (the reference throws TensorIndexError). */

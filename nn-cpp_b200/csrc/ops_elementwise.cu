@@ -204,6 +204,69 @@ __global__ void maxpool_bwd_kernel(long long planes, int H, int W, int k, int st
 }
 
 // ---------------------------------------------------------------------------------------------
+// avgpool2d (ops.cpp:1707-1772): window sum in (row, column) order from +0, times 1 / k^2
+// ---------------------------------------------------------------------------------------------
+
+__global__ void avgpool_fwd_kernel(long long planes, int H, int W, int k, int stride, int ho, int wo, float inv_area,
+		const float* __restrict__ x, float* __restrict__ y) {
+	GRID_STRIDE(i, planes * ho * wo) {
+		const long long p = i / ((long long)ho * wo);
+		const int oh = (int)((i / wo) % ho), ow = (int)(i % wo);
+		const float* plane = x + p * (long long)H * W;
+		float acc = 0.0f;
+		for (int ph = 0; ph < k; ++ph) {
+			const float* row = plane + (long long)(oh * stride + ph) * W + ow * stride;
+			for (int pw = 0; pw < k; ++pw) acc += row[pw];
+		}
+		y[i] = acc * inv_area;
+	}
+}
+
+// the reference scatters share = g * (1/k^2) into every window element, windows in (oh, ow) order;
+// gathered here per input element over the windows that contain it, in that order
+__global__ void avgpool_bwd_kernel(long long planes, int H, int W, int k, int stride, int ho, int wo, float inv_area,
+		const float* __restrict__ g, float* __restrict__ dx, int first) {
+	GRID_STRIDE(i, planes * (long long)H * W) {
+		const long long p = i / ((long long)H * W);
+		const int off = (int)(i % ((long long)H * W));
+		const int r = off / W, c = off % W;
+		const int oh_lo = r >= k ? (r - k) / stride + 1 : 0, oh_hi = min(ho - 1, r / stride);
+		const int ow_lo = c >= k ? (c - k) / stride + 1 : 0, ow_hi = min(wo - 1, c / stride);
+		float acc = first ? 0.0f : dx[i];
+		const long long obase = p * (long long)ho * wo;
+		for (int oh = oh_lo; oh <= oh_hi; ++oh)
+			for (int ow = ow_lo; ow <= ow_hi; ++ow) acc += g[obase + (long long)oh * wo + ow] * inv_area;
+		dx[i] = acc;
+	}
+}
+
+// ---------------------------------------------------------------------------------------------
+// sum / mean over one axis (reduce_axis, ops.cpp:284-376): x viewed as [outer, n, inner]
+// ---------------------------------------------------------------------------------------------
+
+__global__ void reduce_axis_fwd_kernel(long long outer, long long n, long long inner, const float* __restrict__ x,
+		int average, float factor, float* __restrict__ y) {
+	GRID_STRIDE(j, outer * inner) {
+		const long long base = (j / inner) * n * inner + j % inner;
+		float total = 0.0f;
+		for (long long k = 0; k < n; ++k) total += x[base + k * inner];
+		y[j] = average ? total * factor : total;
+	}
+}
+
+__global__ void reduce_axis_bwd_kernel(long long outer, long long n, long long inner, const float* __restrict__ g,
+		float factor, float* __restrict__ dx, int first) {
+	GRID_STRIDE(j, outer * inner) {
+		const long long base = (j / inner) * n * inner + j % inner;
+		const float v = g[j] * factor;
+		for (long long k = 0; k < n; ++k) {
+			float* d = dx + base + k * inner;
+			*d = first ? v + 0.0f : *d + v;
+		}
+	}
+}
+
+// ---------------------------------------------------------------------------------------------
 // Cross entropy over rows (ops.cpp:1774-1840) and sequences (ops.cpp:1908-1979)
 // ---------------------------------------------------------------------------------------------
 
@@ -586,6 +649,58 @@ nnb_status nnb_maxpool2d_bwd(void* stream, size_t N, size_t C, size_t H, size_t 
 	NNB_LAUNCH(kTraceRowwise, grid_for(planes * H * W, 256), 256, nnb::maxpool_bwd_kernel, planes, (int)H, (int)W,
 		(int)kernel, (int)stride, (int)ho, (int)wo, g, argmax, dx, dx_first);
 	return nnb::cuda_status(cudaGetLastError(), "maxpool2d_bwd launch");
+}
+
+nnb_status nnb_avgpool2d_fwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel, size_t stride,
+		const float* x, float* y) {
+	if (kernel == 0 || stride == 0 || kernel > H || kernel > W) return nnb::fail(NNB_ERR_SHAPE, "avgpool2d: bad window");
+	const long long ho = (long long)(H - kernel) / stride + 1, wo = (long long)(W - kernel) / stride + 1;
+	const long long planes = (long long)N * C;
+	if (planes == 0) return NNB_OK;
+	if (!x || !y) return nnb::fail(NNB_ERR_INVALID, "avgpool2d_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const float inv_area = 1.0f / static_cast<float>(kernel * kernel);      // ops.cpp:1727
+	NNB_LAUNCH(kTraceRowwise, grid_for(planes * ho * wo, 256), 256, nnb::avgpool_fwd_kernel, planes, (int)H, (int)W,
+		(int)kernel, (int)stride, (int)ho, (int)wo, inv_area, x, y);
+	return nnb::cuda_status(cudaGetLastError(), "avgpool2d_fwd launch");
+}
+
+nnb_status nnb_avgpool2d_bwd(void* stream, size_t N, size_t C, size_t H, size_t W, size_t kernel, size_t stride,
+		const float* g, float* dx, int dx_first) {
+	if (kernel == 0 || stride == 0 || kernel > H || kernel > W) return nnb::fail(NNB_ERR_SHAPE, "avgpool2d: bad window");
+	const long long ho = (long long)(H - kernel) / stride + 1, wo = (long long)(W - kernel) / stride + 1;
+	const long long planes = (long long)N * C;
+	if (planes == 0) return NNB_OK;
+	if (!g || !dx) return nnb::fail(NNB_ERR_INVALID, "avgpool2d_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const float inv_area = 1.0f / static_cast<float>(kernel * kernel);
+	NNB_LAUNCH(kTraceRowwise, grid_for(planes * H * W, 256), 256, nnb::avgpool_bwd_kernel, planes, (int)H, (int)W,
+		(int)kernel, (int)stride, (int)ho, (int)wo, inv_area, g, dx, dx_first);
+	return nnb::cuda_status(cudaGetLastError(), "avgpool2d_bwd launch");
+}
+
+nnb_status nnb_reduce_axis_fwd(void* stream, size_t outer, size_t n, size_t inner, const float* x, int average,
+		float* y) {
+	if (n == 0) return nnb::fail(NNB_ERR_SHAPE, "reduce_axis: empty axis");
+	if (outer == 0 || inner == 0) return NNB_OK;
+	if (!x || !y) return nnb::fail(NNB_ERR_INVALID, "reduce_axis_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const float factor = average ? 1.0f / static_cast<float>(n) : 1.0f;   // ops.cpp:300
+	NNB_LAUNCH(kTraceRowwise, grid_for((long long)(outer * inner), 256), 256, nnb::reduce_axis_fwd_kernel,
+		(long long)outer, (long long)n, (long long)inner, x, average, factor, y);
+	return nnb::cuda_status(cudaGetLastError(), "reduce_axis_fwd launch");
+}
+
+nnb_status nnb_reduce_axis_bwd(void* stream, size_t outer, size_t n, size_t inner, const float* g, int average,
+		float* dx, int dx_first) {
+	if (n == 0) return nnb::fail(NNB_ERR_SHAPE, "reduce_axis: empty axis");
+	if (outer == 0 || inner == 0) return NNB_OK;
+	if (!g || !dx) return nnb::fail(NNB_ERR_INVALID, "reduce_axis_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const float factor = average ? 1.0f / static_cast<float>(n) : 1.0f;
+	NNB_LAUNCH(kTraceRowwise, grid_for((long long)(outer * inner), 256), 256, nnb::reduce_axis_bwd_kernel,
+		(long long)outer, (long long)n, (long long)inner, g, factor, dx, dx_first);
+	return nnb::cuda_status(cudaGetLastError(), "reduce_axis_bwd launch");
 }
 
 // Shared body of the two cross-entropy forwards. `scratch` must hold rows floats + rows ints.

@@ -420,3 +420,129 @@ nnb_status nnb_batchnorm_bwd(void* stream, size_t N, size_t C, size_t S, const f
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// BatchNorm module pieces (src/nn/batchnorm.cpp): the running statistics update after a training
+// step, and the evaluation-mode transform built from the running statistics.
+// ---------------------------------------------------------------------------------------------
+namespace nnb {
+namespace {
+
+// batchnorm.cpp:38-47: float arithmetic in the reference's order
+__global__ void bn_running_update_kernel(int C, long long n, const float* __restrict__ mean,
+		const float* __restrict__ var, float momentum, float* __restrict__ rmean, float* __restrict__ rvar) {
+	const int c = blockIdx.x * blockDim.x + threadIdx.x;
+	if (c >= C) return;
+	rmean[c] = (1.0f - momentum) * rmean[c] + momentum * mean[c];
+	if (n > 1) {
+		const float unbiased = static_cast<float>(n) / static_cast<float>(n - 1);
+		rvar[c] = (1.0f - momentum) * rvar[c] + momentum * var[c] * unbiased;
+	}
+}
+
+// eval transform (batchnorm.cpp:51-55): inv = 1 / sqrt(rv + eps); y = ((x - rm) * inv) * w + b
+__device__ __forceinline__ float bn_eval_inv(const float* rvar, int c, float eps) {
+	return 1.0f / sqrtf(rvar[c] + eps);
+}
+
+__global__ void bn_eval_fwd_kernel(long long total, long long C, long long S, const float* __restrict__ x,
+		const float* __restrict__ rmean, const float* __restrict__ rvar, float eps, const float* __restrict__ w,
+		const float* __restrict__ b, int fuse_relu, float* __restrict__ y, unsigned char* __restrict__ alive) {
+	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+		const int c = (int)((i / S) % C);
+		const float v = ((x[i] - rmean[c]) * bn_eval_inv(rvar, c, eps)) * w[c] + b[c];
+		if (fuse_relu) {
+			const bool on = v > 0.0f;
+			y[i] = on ? v : 0.0f;
+			alive[i] = on ? 1 : 0;
+		} else {
+			y[i] = v;
+		}
+	}
+}
+
+// dx = ((g * w) * inv) (the chain of the reference's mul / sub backward); per channel, from +0 in
+// (sample, position) order: dw += g * normed, db += g
+__global__ void bn_eval_dx_kernel(long long total, long long C, long long S, const float* __restrict__ g,
+		const unsigned char* __restrict__ alive, const float* __restrict__ rvar, float eps, const float* __restrict__ w,
+		float* __restrict__ dx, int first) {
+	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+		const int c = (int)((i / S) % C);
+		const float gv = (alive && !alive[i]) ? 0.0f : g[i];
+		const float v = (gv * w[c]) * bn_eval_inv(rvar, c, eps);
+		dx[i] = first ? v + 0.0f : dx[i] + v;
+	}
+}
+
+__global__ void bn_eval_param_kernel(long long N, long long C, long long S, const float* __restrict__ g,
+		const unsigned char* __restrict__ alive, const float* __restrict__ x, const float* __restrict__ rmean,
+		const float* __restrict__ rvar, float eps, float* __restrict__ dw, int dw_first, float* __restrict__ db,
+		int db_first) {
+	const int c = blockIdx.x * blockDim.x + threadIdx.x;
+	if (c >= C) return;
+	const float inv = bn_eval_inv(rvar, c, eps);
+	float sw = 0.0f, sb = 0.0f;
+	for (long long n = 0; n < N; ++n)
+		for (long long p = 0; p < S; ++p) {
+			const long long i = (n * C + c) * S + p;
+			const float gv = (alive && !alive[i]) ? 0.0f : g[i];
+			sw += gv * ((x[i] - rmean[c]) * inv);
+			sb += gv;
+		}
+	if (dw) dw[c] = dw_first ? sw + 0.0f : dw[c] + sw;
+	if (db) db[c] = db_first ? sb + 0.0f : db[c] + sb;
+}
+
+}  // namespace
+}  // namespace nnb
+
+extern "C" {
+
+nnb_status nnb_batchnorm_running_update(void* stream, size_t C, size_t count, const float* mean, const float* var,
+		float momentum, float* running_mean, float* running_var) {
+	if (C == 0) return NNB_OK;
+	if (!mean || !var || !running_mean || !running_var)
+		return nnb::fail(NNB_ERR_INVALID, "batchnorm_running_update: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	nnb::TraceScope ts(s, nnb::kTraceRowwise);
+	nnb::bn_running_update_kernel<<<(unsigned)((C + 127) / 128), 128, 0, s>>>((int)C, (long long)count, mean, var, momentum,
+		running_mean, running_var);
+	return nnb::cuda_status(cudaGetLastError(), "batchnorm_running_update launch");
+}
+
+nnb_status nnb_batchnorm_eval_fwd(void* stream, size_t N, size_t C, size_t S, const float* x, const float* running_mean,
+		const float* running_var, float eps, const float* weight, const float* bias, int fuse_relu, float* y,
+		unsigned char* alive) {
+	const long long total = (long long)N * C * S;
+	if (total == 0) return NNB_OK;
+	if (!x || !running_mean || !running_var || !weight || !bias || !y || (fuse_relu && !alive))
+		return nnb::fail(NNB_ERR_INVALID, "batchnorm_eval_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	nnb::TraceScope ts(s, nnb::kTraceRowwise);
+	nnb::bn_eval_fwd_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, (long long)C, (long long)S, x, running_mean,
+		running_var, eps, weight, bias, fuse_relu, y, alive);
+	return nnb::cuda_status(cudaGetLastError(), "batchnorm_eval_fwd launch");
+}
+
+nnb_status nnb_batchnorm_eval_bwd(void* stream, size_t N, size_t C, size_t S, const float* g, const float* x,
+		const float* running_mean, const float* running_var, float eps, const float* weight, const unsigned char* alive,
+		float* dx, int dx_first, float* dweight, int dweight_first, float* dbias, int dbias_first) {
+	const long long total = (long long)N * C * S;
+	if (total == 0) return NNB_OK;
+	if (!g || !x || !running_mean || !running_var || !weight)
+		return nnb::fail(NNB_ERR_INVALID, "batchnorm_eval_bwd: null input");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	if (dx) {
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_eval_dx_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, (long long)C, (long long)S, g, alive,
+			running_var, eps, weight, dx, dx_first);
+	}
+	if (dweight || dbias) {
+		nnb::TraceScope ts(s, nnb::kTraceRowwise);
+		nnb::bn_eval_param_kernel<<<(unsigned)((C + 127) / 128), 128, 0, s>>>((long long)N, (long long)C, (long long)S, g,
+			alive, x, running_mean, running_var, eps, dweight, dweight_first, dbias, dbias_first);
+	}
+	return nnb::cuda_status(cudaGetLastError(), "batchnorm_eval_bwd launch");
+}
+
+}  // extern "C"

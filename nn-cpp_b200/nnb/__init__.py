@@ -87,6 +87,16 @@ _SIGS = {
     "nnb_accumulate": ([_p, _sz, _p, _p, _i, _i], _i),
     "nnb_maxpool2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p], _i),
     "nnb_maxpool2d_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _i], _i),
+    "nnb_avgpool2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p], _i),
+    "nnb_avgpool2d_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _i], _i),
+    "nnb_reduce_axis_fwd": ([_p, _sz, _sz, _sz, _p, _i, _p], _i),
+    "nnb_reduce_axis_bwd": ([_p, _sz, _sz, _sz, _p, _i, _p, _i], _i),
+    "nnb_conv2d_ex_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _i, _i, _p, _p, _p, _p], _i),
+    "nnb_conv2d_ex_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p, _i, _p, _i],
+                          _i),
+    "nnb_batchnorm_running_update": ([_p, _sz, _sz, _p, _p, _f, _p, _p], _i),
+    "nnb_batchnorm_eval_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _f, _p, _p, _i, _p, _p], _i),
+    "nnb_batchnorm_eval_bwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _f, _p, _p, _p, _i, _p, _i, _p, _i], _i),
     "nnb_cross_entropy_fwd": ([_p, _sz, _sz, _p, _p, _p, _p, _p], _i),
     "nnb_cross_entropy_bwd": ([_p, _sz, _sz, _p, _p, _p, _p, _p, _i], _i),
     "nnb_sequence_ce_fwd": ([_p, _sz, _sz, _p, _p, _c.c_int64, _f, _p, _p, _p], _i),

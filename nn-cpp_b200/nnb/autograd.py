@@ -87,9 +87,13 @@ class Value:
 
     # -- backward (value.cpp:80-132) -----------------------------------------------------------
     def backward(self, seed: torch.Tensor | None = None) -> None:
-        """Runs the backward rules; the root's gradient is 1, or the device scalar `seed`."""
-        if self.data.numel() != 1:
+        """Runs the backward rules; the root's gradient is 1, or `seed` (a device tensor with the
+        root's element count: an upstream gradient, which lets a non-scalar root be differentiated
+        as the reference's tests do with sum(y * g))."""
+        if seed is None and self.data.numel() != 1:
             raise ValueError("backward() needs a single-element value (AutogradShapeError)")
+        if seed is not None and seed.numel() != self.data.numel():
+            raise ValueError("backward(): the seed must have the root's element count")
         topo: list[Value] = []
         expanded, done = set(), set()
         stack = [self]

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import contextlib
 import ctypes
+import math
 import os
 
 import torch
@@ -185,14 +186,19 @@ def layernorm(x: Value, gamma: Value, beta: Value, eps: float) -> Value:
     return Value.node(y, (x, gamma, beta), backward)
 
 
-def batchnorm(x: Value, weight: Value, bias: Value, eps: float, fuse_relu: bool = False) -> Value:
+def batchnorm(x: Value, weight: Value, bias: Value, eps: float, fuse_relu: bool = False,
+              mean_out: torch.Tensor | None = None, var_out: torch.Tensor | None = None) -> Value:
+    """batchnorm in training mode (ops.cpp:900-1001); mean_out / var_out receive the batch statistics
+    (biased variance), as the reference's Tensor* outputs."""
     if len(x.shape) < 2:
         raise TensorShapeError("batchnorm: needs N and C axes")
     N, C = x.shape[0], x.shape[1]
     S = x.data.numel() // max(1, N * C)
     y = empty(x.shape)
     alive = empty(x.shape, dtype=torch.uint8) if fuse_relu else None
-    mean, var, inv = empty((C,)), empty((C,)), empty((C,))
+    mean = mean_out if mean_out is not None else empty((C,))
+    var = var_out if var_out is not None else empty((C,))
+    inv = empty((C,))
     check(lib().nnb_batchnorm_fwd(_s(), N, C, S, _p(x.data), _p(weight.data), _p(bias.data), ctypes.c_float(eps),
                                   int(fuse_relu), _p(y), _p(alive), _p(mean), _p(var), _p(inv)))
 
@@ -206,6 +212,30 @@ def batchnorm(x: Value, weight: Value, bias: Value, eps: float, fuse_relu: bool 
     out = Value.node(y, (x, weight, bias), backward)
     out.name = "batchnorm"
     return out
+
+
+def batchnorm_eval(x: Value, weight: Value, bias: Value, running_mean: torch.Tensor, running_var: torch.Tensor,
+                   eps: float, fuse_relu: bool = False) -> Value:
+    """Evaluation-mode batch normalisation from the running statistics (batchnorm.cpp:51-55)."""
+    if len(x.shape) < 2:
+        raise TensorShapeError("batchnorm: needs N and C axes")
+    N, C = x.shape[0], x.shape[1]
+    S = x.data.numel() // max(1, N * C)
+    y = empty(x.shape)
+    alive = empty(x.shape, dtype=torch.uint8) if fuse_relu else None
+    check(lib().nnb_batchnorm_eval_fwd(_s(), N, C, S, _p(x.data), _p(running_mean), _p(running_var),
+                                       ctypes.c_float(eps), _p(weight.data), _p(bias.data), int(fuse_relu), _p(y),
+                                       _p(alive)))
+
+    def backward(g):
+        dx, fx = x.grad_accum() if _need(x) else (None, 0)
+        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
+        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
+        check(lib().nnb_batchnorm_eval_bwd(_s(), N, C, S, _p(g), _p(x.data), _p(running_mean), _p(running_var),
+                                           ctypes.c_float(eps), _p(weight.data), _p(alive), _p(dx), fx, _p(dw), fw,
+                                           _p(db), fb))
+
+    return Value.node(y, (x, weight, bias), backward)
 
 
 # ---- attention (ops.cpp:1226-1296) --------------------------------------------------------------
@@ -262,7 +292,12 @@ def _flash_attention(q, k, v, heads, key_padding_mask, causal, N, Tq, Tk, D) -> 
 
 # ---- convolution and pooling ---------------------------------------------------------------------
 
-def conv2d(x: Value, weight: Value, bias: Value, stride: int, padding: int, fuse_relu: bool = False) -> Value:
+def conv2d(x: Value, weight: Value, bias: Value, stride: int, padding: int, fuse_relu: bool = False,
+           dilation: int = 1, groups: int = 1) -> Value:
+    if dilation != 1 or groups != 1:
+        if fuse_relu:
+            raise ValueError("conv2d: the folded ReLU needs dilation 1 and groups 1 (conv2d.hpp:72)")
+        return _conv2d_general(x, weight, bias, stride, padding, dilation, groups)
     if len(x.shape) != 4 or len(weight.shape) != 4:
         raise TensorShapeError("conv2d: needs 4-D input and weight")
     N, Cin, H, W = x.shape
@@ -287,6 +322,34 @@ def conv2d(x: Value, weight: Value, bias: Value, stride: int, padding: int, fuse
     return Value.node(y, (x, weight, bias), backward)
 
 
+def _conv2d_general(x: Value, weight: Value, bias: Value, stride: int, padding: int, dilation: int,
+                    groups: int) -> Value:
+    """conv2d with dilation / groups (ops.cpp:1525-1607): per sample and group, im2col + GEMM."""
+    if len(x.shape) != 4 or len(weight.shape) != 4:
+        raise TensorShapeError("conv2d: needs 4-D input and weight")
+    N, Cin, H, W = x.shape
+    Cout, Cg, kh, kw = weight.shape
+    if bias.shape != (Cout,) or groups <= 0 or dilation <= 0 or stride <= 0 or padding < 0 or Cin % groups \
+            or Cout % groups or Cg != Cin // groups:
+        raise TensorShapeError("conv2d: shapes do not agree")
+    ekh, ekw = dilation * (kh - 1) + 1, dilation * (kw - 1) + 1
+    if ekh > H + 2 * padding or ekw > W + 2 * padding:
+        raise TensorShapeError("conv2d: bad window")
+    ho, wo = (H + 2 * padding - ekh) // stride + 1, (W + 2 * padding - ekw) // stride + 1
+    y = empty((N, Cout, ho, wo))
+    check(lib().nnb_conv2d_ex_fwd(_s(), N, Cin, H, W, Cout, kh, kw, stride, padding, dilation, groups, _p(x.data),
+                                  _p(weight.data), _p(bias.data), _p(y)))
+
+    def backward(g):
+        dx, fx = x.grad_accum() if _need(x) else (None, 0)
+        dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
+        db, fb = bias.grad_accum() if _need(bias) else (None, 0)
+        check(lib().nnb_conv2d_ex_bwd(_s(), N, Cin, H, W, Cout, kh, kw, stride, padding, dilation, groups, _p(g),
+                                      _p(x.data), _p(weight.data), _p(dx), fx, _p(dw), fw, _p(db), fb))
+
+    return Value.node(y, (x, weight, bias), backward)
+
+
 def conv2d_relu(x: Value, weight: Value, bias: Value, stride: int, padding: int) -> Value:
     return conv2d(x, weight, bias, stride, padding, fuse_relu=True)
 
@@ -307,6 +370,58 @@ def maxpool2d(x: Value, kernel_size: int, stride: int) -> Value:
         check(lib().nnb_maxpool2d_bwd(_s(), N, C, H, W, kernel_size, stride, _p(g), _p(arg), _p(dx), f))
 
     return Value.node(y, (x,), backward)
+
+
+def avgpool2d(x: Value, kernel_size: int, stride: int) -> Value:
+    """avgpool2d (ops.cpp:1707-1772)."""
+    if len(x.shape) != 4 or kernel_size == 0 or stride == 0:
+        raise TensorShapeError("avgpool2d: bad input")
+    N, C, H, W = x.shape
+    if kernel_size > H or kernel_size > W:
+        raise TensorShapeError("avgpool2d: window larger than the input")
+    ho, wo = (H - kernel_size) // stride + 1, (W - kernel_size) // stride + 1
+    y = empty((N, C, ho, wo))
+    check(lib().nnb_avgpool2d_fwd(_s(), N, C, H, W, kernel_size, stride, _p(x.data), _p(y)))
+
+    def backward(g):
+        if _need(x):
+            dx, fx = x.grad_accum()
+            check(lib().nnb_avgpool2d_bwd(_s(), N, C, H, W, kernel_size, stride, _p(g), _p(dx), fx))
+
+    return Value.node(y, (x,), backward)
+
+
+def _reduce_axis(x: Value, axis: int, keepdim: bool, average: bool) -> Value:
+    """sum / mean over one axis (reduce_axis, ops.cpp:284-376)."""
+    shape = list(x.shape)
+    nd = len(shape)
+    if axis < -nd or axis >= nd:
+        raise IndexError("reduce over an axis out of range")     # the reference throws TensorIndexError
+    ax = axis + nd if axis < 0 else axis
+    n = shape[ax]
+    if n == 0:
+        raise TensorShapeError("reduce over an empty axis")
+    outer = math.prod(shape[:ax])
+    inner = math.prod(shape[ax + 1:])
+    out_shape = [d for i, d in enumerate(shape) if i != ax] if not keepdim else \
+        [1 if i == ax else d for i, d in enumerate(shape)]
+    y = empty(tuple(out_shape) if out_shape else (1,))
+    check(lib().nnb_reduce_axis_fwd(_s(), outer, n, inner, _p(x.data), int(average), _p(y)))
+
+    def backward(g):
+        if _need(x):
+            dx, fx = x.grad_accum()
+            check(lib().nnb_reduce_axis_bwd(_s(), outer, n, inner, _p(g), int(average), _p(dx), fx))
+
+    return Value.node(y, (x,), backward)
+
+
+def sum(x: Value, axis: int, keepdim: bool = False) -> Value:      # noqa: A001 - the reference's name
+    return _reduce_axis(x, axis, keepdim, False)
+
+
+def mean(x: Value, axis: int, keepdim: bool = False) -> Value:
+    return _reduce_axis(x, axis, keepdim, True)
 
 
 # ---- embedding and losses -----------------------------------------------------------------------

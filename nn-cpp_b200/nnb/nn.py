@@ -17,13 +17,14 @@ to reproduce the reference's own numbers the tests load the same values into bot
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
 import numpy as np
 import torch
 
-from . import check, lib
+from . import TensorShapeError, check, lib
 from . import functional as F
 from .autograd import Value
 
@@ -201,20 +202,93 @@ class Transformer(Module):
 
 
 class Conv2d(Module):
-    def __init__(self, cin: int, cout: int, k: int, stride: int, padding: int, rng, device):
-        lim = 1.0 / math.sqrt(cin * k * k)
-        self.stride, self.padding = stride, padding
-        self.weight = _param(rng.uniform(-lim, lim, (cout, cin, k, k)), device)
+    """conv2d layer (src/nn/conv2d.cpp; conv2d.hpp:37-72): k an int (square) or (kh, kw); weight
+    [cout, cin/groups, kh, kw] ~ U(+-1/sqrt(cin/groups * kh * kw)), zero bias."""
+
+    def __init__(self, cin: int, cout: int, k, stride: int, padding: int, rng, device, dilation: int = 1,
+                 groups: int = 1):
+        kh, kw = (k, k) if isinstance(k, int) else k
+        if dilation <= 0 or groups <= 0 or cin % groups or cout % groups:
+            raise ValueError("Conv2d: bad dilation / groups")
+        lim = 1.0 / math.sqrt((cin // groups) * kh * kw)
+        self.stride, self.padding, self.dilation, self.groups = stride, padding, dilation, groups
+        self.weight = _param(rng.uniform(-lim, lim, (cout, cin // groups, kh, kw)), device)
         self.bias = _param(np.zeros(cout), device)
 
+    @property
+    def can_fuse_relu(self) -> bool:
+        return self.dilation == 1 and self.groups == 1               # conv2d.hpp:72
+
     def forward(self, x: Value) -> Value:
-        return F.conv2d(x, self.weight, self.bias, self.stride, self.padding)
+        return F.conv2d(x, self.weight, self.bias, self.stride, self.padding, dilation=self.dilation,
+                        groups=self.groups)
 
     def forward_relu(self, x: Value) -> Value:
         return F.conv2d_relu(x, self.weight, self.bias, self.stride, self.padding)
 
     def named_parameters(self):
         return [("weight", self.weight), ("bias", self.bias)]
+
+
+class _BatchNorm(Module):
+    """Batch normalisation (src/nn/batchnorm.cpp): training mode normalises with the batch statistics
+    and updates running_mean / running_var (momentum, unbiased variance); evaluation mode uses the
+    running statistics. A following ReLU folds into the op in training mode only (batchnorm.hpp:50)."""
+
+    rank = 0
+
+    def __init__(self, num_features: int, device, eps: float = 1e-5, momentum: float = 0.1):
+        self.num_features, self.eps, self.momentum = num_features, eps, momentum
+        self.weight = _param(np.ones(num_features), device)
+        self.bias = _param(np.zeros(num_features), device)
+        self.running_mean = torch.zeros(num_features, device=device)
+        self.running_var = torch.ones(num_features, device=device)
+        self.training = True
+
+    def train(self, mode: bool = True):
+        self.training = mode
+        return self
+
+    def eval(self):
+        return self.train(False)
+
+    @property
+    def can_fuse_relu(self) -> bool:
+        return self.training
+
+    def forward(self, x: Value) -> Value:
+        return self._run(x, False)
+
+    def forward_relu(self, x: Value) -> Value:
+        return self._run(x, True)
+
+    def _run(self, x: Value, fuse_relu: bool) -> Value:
+        if len(x.shape) != self.rank or x.shape[1] != self.num_features:
+            raise TensorShapeError("BatchNorm: input shape does not match the layer")
+        if self.training:
+            C = self.num_features
+            mu, var = torch.empty(C, device=x.data.device), torch.empty(C, device=x.data.device)
+            out = F.batchnorm(x, self.weight, self.bias, self.eps, fuse_relu, mean_out=mu, var_out=var)
+            count = x.data.numel() // C
+            check(lib().nnb_batchnorm_running_update(torch.cuda.current_stream().cuda_stream, C, count, mu.data_ptr(),
+                                                     var.data_ptr(), ctypes.c_float(self.momentum),
+                                                     self.running_mean.data_ptr(), self.running_var.data_ptr()))
+            return out
+        return F.batchnorm_eval(x, self.weight, self.bias, self.running_mean, self.running_var, self.eps, fuse_relu)
+
+    def named_parameters(self):
+        return [("weight", self.weight), ("bias", self.bias)]
+
+    def named_buffers(self):
+        return [("running_mean", self.running_mean), ("running_var", self.running_var)]
+
+
+class BatchNorm1d(_BatchNorm):
+    rank = 2
+
+
+class BatchNorm2d(_BatchNorm):
+    rank = 4
 
 
 class ReLU(Module):
@@ -235,8 +309,26 @@ class Flatten(Module):
         return F.reshape(x, (x.shape[0], int(np.prod(x.shape[1:]))))
 
 
+class AvgPool2d(Module):
+    def __init__(self, k: int, stride: int):
+        self.k, self.stride = k, stride
+
+    def forward(self, x):
+        return F.avgpool2d(x, self.k, self.stride)
+
+
+class GlobalAvgPool2d(Module):
+    """mean over W then H (pool2d.cpp:20-23): [N, C, H, W] -> [N, C]."""
+
+    def forward(self, x):
+        if len(x.shape) != 4:
+            raise TensorShapeError("GlobalAvgPool2d: needs a 4-D input")
+        return F.mean(F.mean(x, 3), 2)
+
+
 class Sequential(Module):
-    """Runs layers in order; a Conv2d followed by a ReLU runs as one conv2d_relu (sequential.cpp:16-28)."""
+    """Runs layers in order; a layer that can fold a following ReLU (Conv2d without dilation / groups,
+    BatchNorm in training mode) runs both as one op (sequential.cpp:16-28)."""
 
     def __init__(self, *layers):
         self.layers = list(layers)
@@ -245,7 +337,8 @@ class Sequential(Module):
         i = 0
         while i < len(self.layers):
             layer = self.layers[i]
-            if isinstance(layer, Conv2d) and i + 1 < len(self.layers) and isinstance(self.layers[i + 1], ReLU):
+            if getattr(layer, "can_fuse_relu", False) and i + 1 < len(self.layers) and \
+                    isinstance(self.layers[i + 1], ReLU):
                 x = layer.forward_relu(x)
                 i += 2
                 continue
@@ -253,10 +346,26 @@ class Sequential(Module):
             i += 1
         return x
 
+    def train(self, mode: bool = True):
+        for layer in self.layers:
+            if hasattr(layer, "train"):
+                layer.train(mode)
+        return self
+
+    def eval(self):
+        return self.train(False)
+
     def named_parameters(self):
         out = []
         for i, layer in enumerate(self.layers):
             out += [(f"{i}.{n}", p) for n, p in layer.named_parameters()]
+        return out
+
+    def named_buffers(self):
+        out = []
+        for i, layer in enumerate(self.layers):
+            if hasattr(layer, "named_buffers"):
+                out += [(f"{i}.{n}", b) for n, b in layer.named_buffers()]
         return out
 
 

@@ -81,6 +81,11 @@ _REF_SIGS = {
     "ref_attention": ([_sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p], None),
     "ref_conv2d": ([_sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _i, _p, _p, _p, _p, _p], None),
     "ref_maxpool2d": ([_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
+    "ref_conv2d_ex": ([_sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], None),
+    "ref_avgpool2d": ([_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
+    "ref_reduce4": ([_sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _p], None),
+    "ref_global_avgpool": ([_sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
+    "ref_bn2d_module": ([_sz, _sz, _sz, _sz, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], None),
     "ref_gelu": ([_sz, _p, _p, _p, _p], None),
     "ref_relu": ([_sz, _p, _p, _p, _p], None),
     "ref_tanh_inplace": ([_p, _sz], None),

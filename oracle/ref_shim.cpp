@@ -12,6 +12,8 @@
 #include "nn/autograd/value.hpp"
 #include "nn/kernels/gemm.hpp"
 #include "nn/kernels/vmath.hpp"
+#include "nn/nn/batchnorm.hpp"
+#include "nn/nn/pool2d.hpp"
 #include "nn/nn/sequential.hpp"
 #include "nn/nn/transformer.hpp"
 #include "nn/optim/adamw.hpp"
@@ -49,6 +51,12 @@ void copy_out(const Tensor& t, float* dst) {
 // Runs a node's backward rule once with the given upstream gradient (the leaves' gradients start
 // at zero, so every contribution lands as 0 + term).
 void backward_with(const Value& out, const float* g) { out.impl()->backward_fn(tensor(out.data().shape(), g)); }
+
+// Backpropagates an upstream gradient g of y through y's whole graph: d sum(y * G) / dy = G exactly.
+void backward_through(const Value& y, const float* g) {
+	Value G = Value::leaf(tensor(y.data().shape(), g), false);
+	nn::sum(nn::mul(y, G)).backward();
+}
 
 Tensor ids_tensor(std::vector<size_t> shape, const int64_t* ids) {
 	std::vector<float> v(count_of(shape));
@@ -225,6 +233,75 @@ void ref_maxpool2d(size_t N, size_t C, size_t H, size_t W, size_t k, size_t stri
 	copy_out(Y.data(), y);
 	backward_with(Y, g);
 	copy_out(X.grad(), dx);
+}
+
+void ref_conv2d_ex(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh, size_t kw, int stride,
+		int padding, int dilation, int groups, const float* x, const float* w, const float* b, const float* g, float* y,
+		float* dx, float* dw, float* db) {
+	Value X = leaf({N, Cin, H, W}, x), Wt = leaf({Cout, Cin / (size_t)groups, kh, kw}, w), B = leaf({Cout}, b);
+	Value Y = nn::conv2d(X, Wt, B, stride, padding, dilation, groups);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+	copy_out(Wt.grad(), dw);
+	copy_out(B.grad(), db);
+}
+
+void ref_avgpool2d(size_t N, size_t C, size_t H, size_t W, size_t k, size_t stride, const float* x, const float* g,
+		float* y, float* dx) {
+	Value X = leaf({N, C, H, W}, x);
+	Value Y = nn::avgpool2d(X, k, stride);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+}
+
+// sum (average = 0) or mean over one axis of a 4-D x
+void ref_reduce4(size_t n0, size_t n1, size_t n2, size_t n3, int axis, int average, const float* x, const float* g,
+		float* y, float* dx) {
+	Value X = leaf({n0, n1, n2, n3}, x);
+	Value Y = average ? nn::mean(X, axis) : nn::sum(X, axis);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+}
+
+void ref_global_avgpool(size_t N, size_t C, size_t H, size_t W, const float* x, const float* g, float* y, float* dx) {
+	Value X = leaf({N, C, H, W}, x);
+	nn::GlobalAvgPool2d pool;
+	Value Y = pool.forward(X);
+	copy_out(Y.data(), y);
+	backward_through(Y, g);
+	copy_out(X.grad(), dx);
+}
+
+// BatchNorm2d(C) module: `train_steps` training-mode forwards on x, then (eval = 1) one
+// evaluation-mode forward, or (eval = 0) the last training forward, is returned with its backward
+// for the upstream gradient g; the running statistics are copied out after.
+void ref_bn2d_module(size_t N, size_t C, size_t H, size_t W, int train_steps, int eval, int fuse_relu, const float* x,
+		const float* g, float* y, float* dx, float* dw, float* db, float* running_mean, float* running_var) {
+	nn::BatchNorm2d bn(C);
+	std::vector<Value> params = bn.parameters();
+	Value X = leaf({N, C, H, W}, x);
+	Value Y = fuse_relu ? bn.forward_relu(X) : bn.forward(X);
+	for (int s = 1; s < train_steps; ++s) {
+		X = leaf({N, C, H, W}, x);
+		Y = fuse_relu ? bn.forward_relu(X) : bn.forward(X);
+	}
+	if (eval) {
+		bn.train(false);
+		X = leaf({N, C, H, W}, x);
+		Y = fuse_relu ? bn.forward_relu(X) : bn.forward(X);
+	}
+	for (Value& p : params) p.zero_grad();
+	copy_out(Y.data(), y);
+	backward_through(Y, g);
+	copy_out(X.grad(), dx);
+	copy_out(params[0].grad(), dw);
+	copy_out(params[1].grad(), db);
+	auto buffers = bn.named_buffers();
+	copy_out(*buffers[0].second, running_mean);
+	copy_out(*buffers[1].second, running_var);
 }
 
 void ref_gelu(size_t n, const float* x, const float* g, float* y, float* dx) {
