@@ -37,6 +37,9 @@ class Module:
     def named_parameters(self) -> list[tuple[str, Value]]:
         return []
 
+    def named_buffers(self) -> list[tuple[str, torch.Tensor]]:
+        return []
+
     def parameters(self) -> list[Value]:
         return [p for _, p in self.named_parameters()]
 
@@ -388,6 +391,42 @@ class AdamW:
     def zero_grad(self):
         for p in self.params:
             p.zero_grad()
+
+    # -- checkpoint state (src/optim/adam.cpp:46-71; AdamW has the same entries) -------------------
+    def state(self) -> list[tuple[str, torch.Tensor]]:
+        dev = self.m[0].device if self.m else torch.device("cpu")
+        out = [(n, torch.tensor([v], dtype=torch.float32, device=dev))
+               for n, v in (("lr", self.lr), ("beta1", self.beta1), ("beta2", self.beta2), ("eps", self.eps),
+                            ("t", float(self.t)))]
+        out += [(f"m.{i}", m) for i, m in enumerate(self.m)]
+        out += [(f"v.{i}", v) for i, v in enumerate(self.v)]
+        return out
+
+    def load_state(self, snapshot) -> None:
+        """All or nothing: every entry of state() with its shape, nothing else ("lr" may be absent,
+        the current one is kept), as Optimizer::check_state (src/optim/sgd.cpp:27-49)."""
+        got = dict(snapshot)
+        if len(got) != len(snapshot):
+            raise RuntimeError("optimizer state mismatch: duplicate entries")
+        if "lr" not in got:
+            got["lr"] = np.array([self.lr], np.float32)
+        want = self.state()
+        problems = ""
+        for name, t in want:
+            if name not in got:
+                problems += " missing:" + name
+            elif tuple(np.shape(got[name])) != tuple(t.shape):
+                problems += " shape-mismatch:" + name
+        names = {n for n, _ in want}
+        problems += "".join(" unexpected:" + n for n in got if n not in names)
+        if problems:
+            raise RuntimeError("optimizer state mismatch:" + problems)
+        val = lambda n: float(np.asarray(got[n], np.float32).reshape(-1)[0])
+        self.lr, self.beta1, self.beta2, self.eps = val("lr"), val("beta1"), val("beta2"), val("eps")
+        self.t = int(val("t"))
+        for i, (m, v) in enumerate(zip(self.m, self.v)):
+            m.copy_(torch.as_tensor(np.asarray(got[f"m.{i}"], np.float32)).to(m.device))
+            v.copy_(torch.as_tensor(np.asarray(got[f"v.{i}"], np.float32)).to(v.device))
 
     def step(self):
         import ctypes

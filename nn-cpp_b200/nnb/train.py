@@ -82,6 +82,36 @@ class ShardedTrainer:
             p.grad_fresh = True
             off += n
 
+    def optimizer_to_params(self) -> None:
+        """Copies the trainer's moment buffers into the optimizer's per-parameter ones (e.g. before
+        a checkpoint is saved); with several ranks every rank gathers the full buffers."""
+        self._moments(to_opt=True)
+
+    def optimizer_from_params(self) -> None:
+        """The reverse of optimizer_to_params (e.g. after a checkpoint was loaded into the optimizer)."""
+        self._moments(to_opt=False)
+
+    def _moments(self, to_opt: bool) -> None:
+        dev = self.m.device
+        for mine, theirs in ((self.m, self.opt.m), (self.v, self.opt.v)):
+            full = torch.zeros(self.chunk * self.world, device=dev)
+            if to_opt:
+                if self.world > 1:
+                    import torch.distributed as dist
+                    dist.all_gather_into_tensor(full, mine, group=self.group)
+                else:
+                    full[: self.chunk].copy_(mine)
+                off = 0
+                for t, n in zip(theirs, self.sizes):
+                    t.view(-1).copy_(full[off: off + n])
+                    off += n
+            else:
+                off = 0
+                for t, n in zip(theirs, self.sizes):
+                    full[off: off + n].copy_(t.view(-1))
+                    off += n
+                mine.copy_(full[self.lo: self.lo + self.chunk])
+
     def _adamw(self, s, n: int, w_ptr: int, g_ptr: int) -> None:
         o = self.opt
         check(lib().nnb_adamw_step(s, n, w_ptr, g_ptr, self.m.data_ptr(), self.v.data_ptr(), ctypes.c_float(o.lr),

@@ -86,6 +86,8 @@ _REF_SIGS = {
     "ref_reduce4": ([_sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _p], None),
     "ref_global_avgpool": ([_sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
     "ref_bn2d_module": ([_sz, _sz, _sz, _sz, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], None),
+    "ref_linear_checkpoint_save": ([_c.c_char_p, _p, _p, _p, _p, _f, _f, _c.c_longlong], _i),
+    "ref_linear_checkpoint_load": ([_c.c_char_p, _p, _p], _c.c_longlong),
     "ref_gelu": ([_sz, _p, _p, _p, _p], None),
     "ref_relu": ([_sz, _p, _p, _p, _p], None),
     "ref_tanh_inplace": ([_p, _sz], None),

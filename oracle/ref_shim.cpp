@@ -9,6 +9,8 @@
  * can run it on the same host buffers the CUDA path sees.
  */
 #include "nn/autograd/ops.hpp"
+#include "nn/checkpoint.hpp"
+#include "nn/nn/linear.hpp"
 #include "nn/autograd/value.hpp"
 #include "nn/kernels/gemm.hpp"
 #include "nn/kernels/vmath.hpp"
@@ -302,6 +304,48 @@ void ref_bn2d_module(size_t N, size_t C, size_t H, size_t W, int train_steps, in
 	auto buffers = bn.named_buffers();
 	copy_out(*buffers[0].second, running_mean);
 	copy_out(*buffers[1].second, running_var);
+}
+
+// Sequential{Linear(3, 2)} with weight w [2, 3] and bias b [2]; with grads given, one AdamW step
+// (lr, weight_decay, other settings default) first; then save_checkpoint(path, model, optim?, step).
+// Returns 0, or 1 when the reference threw.
+int ref_linear_checkpoint_save(const char* path, const float* w, const float* b, const float* gw, const float* gb,
+		float lr, float wd, int64_t step) {
+	try {
+		nn::Sequential m;
+		m.add(std::make_unique<nn::Linear>(3, 2));
+		auto p = m.named_parameters();
+		p[0].second.data().data().assign(w, w + 6);
+		p[1].second.data().data().assign(b, b + 2);
+		if (gw) {
+			nn::AdamW opt(m.parameters(), lr, 0.9f, 0.999f, 1e-8f, wd);
+			p[0].second.grad().data().assign(gw, gw + 6);
+			p[1].second.grad().data().assign(gb, gb + 2);
+			opt.step();
+			nn::save_checkpoint(path, m, &opt, step);
+		} else {
+			nn::save_checkpoint(path, m, nullptr, step);
+		}
+		return 0;
+	} catch (...) {
+		return 1;
+	}
+}
+
+// load_checkpoint(path) into Sequential{Linear(3, 2)} (optimizer entries ignored); the step, or -1
+// when the reference threw (a malformed or mismatching file).
+int64_t ref_linear_checkpoint_load(const char* path, float* w, float* b) {
+	try {
+		nn::Sequential m;
+		m.add(std::make_unique<nn::Linear>(3, 2));
+		const int64_t step = nn::load_checkpoint(path, m, nullptr);
+		auto p = m.named_parameters();
+		copy_out(p[0].second.data(), w);
+		copy_out(p[1].second.data(), b);
+		return step;
+	} catch (...) {
+		return -1;
+	}
 }
 
 void ref_gelu(size_t n, const float* x, const float* g, float* y, float* dx) {

@@ -1,4 +1,4 @@
-"""Generates tests/golden/gemm_golden.npz from the reference library itself.
+"""Generates the golden fixtures under tests/golden/ from the reference library itself.
 
 Run in a container that has the reference sources (oracle/Makefile builds oracle/_ref/libnnref.so
 from them):  python tests/golden/make_golden.py
@@ -8,7 +8,13 @@ test's problem builder (tests/test_kernels.cpp:68-86), the output of the referen
 triple-loop oracle (tests/reference_gemm.hpp) and the output of its production sgemm
 (src/kernels/gemm.cpp:546). The file is small and committed; the GPU box reads it without the
 reference present.
+
+It also writes two checkpoints with the reference's own writer (src/checkpoint.cpp): the
+Sequential{Linear(3, 2)} of tests/test_checkpoint.cpp's golden case saved at step 7 without an
+optimizer (linear_step7.nnck), and the same model after one AdamW step on fixed gradients, saved
+with the optimizer at step 1 (linear_adamw.nnck).
 """
+import os
 import pathlib
 import sys
 
@@ -48,6 +54,34 @@ def main():
     dst = pathlib.Path(__file__).resolve().parent / "gemm_golden.npz"
     np.savez_compressed(dst, **out)
     print(dst, dst.stat().st_size, "bytes")
+    checkpoints(ref)
+
+
+# Sequential{Linear(3, 2)} parameters of the reference's golden checkpoint test, and the gradients and
+# AdamW settings of the optimizer-state fixture.
+CKPT_W = [0.5, -1.25, 2.0, 3.0, 0.75, -0.5]
+CKPT_B = [0.125, -2.0]
+CKPT_GW = [0.25, -0.5, 1.5, -2.0, 0.125, 3.0]
+CKPT_GB = [-0.75, 0.375]
+CKPT_LR, CKPT_WD = 0.01, 0.1
+
+
+def checkpoints(ref):
+    here = pathlib.Path(__file__).resolve().parent
+    f32 = lambda v: np.array(v, np.float32)
+    w, b, gw, gb = f32(CKPT_W), f32(CKPT_B), f32(CKPT_GW), f32(CKPT_GB)
+    plain, adamw = here / "linear_step7.nnck", here / "linear_adamw.nnck"
+    if ref.ref_linear_checkpoint_save(str(plain).encode(), orc.ptr(w), orc.ptr(b), None, None, 0.0, 0.0, 7):
+        raise SystemExit("reference save failed")
+    if ref.ref_linear_checkpoint_save(str(adamw).encode(), orc.ptr(w), orc.ptr(b), orc.ptr(gw), orc.ptr(gb),
+                                      CKPT_LR, CKPT_WD, 1):
+        raise SystemExit("reference save failed")
+    for f in (plain, adamw):
+        print(f, f.stat().st_size, "bytes")
+    # the reference's own golden file for this model (tests/data/linear_v1.ckpt) pins the writer
+    golden = pathlib.Path(os.environ.get("REF", "/root/reference")) / "tests/data/linear_v1.ckpt"
+    if golden.exists() and golden.read_bytes() != plain.read_bytes():
+        raise SystemExit("reference writer disagrees with the reference's golden checkpoint")
 
 
 if __name__ == "__main__":
