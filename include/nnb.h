@@ -217,6 +217,18 @@ NNB_API nnb_status nnb_flash_attention_bwd(void* stream, size_t N, size_t Tq, si
 		const float* g, const float* q, const float* k, const float* v, const float* out, const float* lse,
 		const float* key_padding_mask, int causal, float* dq, int dq_first, float* dk, int dk_first, float* dv,
 		int dv_first);
+/* attention with dropout on the weights: MultiHeadAttention's composed path when its Dropout is
+ * active (src/nn/attention.cpp:36-47: matmul_bt, scaled_masked_softmax ops.cpp:1298-1343,
+ * Dropout::forward src/nn/dropout.cpp:20-31, matmul). keep = the dropout mask of the N*H*Tq*Tk
+ * weights from nnb_dropout_mask (bit e % 32 of word e / 32 = element e kept); probs and weights
+ * ([N, heads, Tq, Tk], the softmax and the dropped weights) are kept for the backward. */
+NNB_API nnb_status nnb_attention_dropout_fwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* q, const float* k, const float* v, const float* key_padding_mask, int causal, float p,
+		const uint32_t* keep, float* out, float* probs, float* weights);
+NNB_API nnb_status nnb_attention_dropout_bwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* g, const float* q, const float* k, const float* v, const float* probs, const float* weights,
+		float p, const uint32_t* keep, const float* key_padding_mask, int causal, float* dq, int dq_first, float* dk,
+		int dk_first, float* dv, int dv_first);
 /* masked_softmax_row over [N, H, Tq, Tk] scores in place (ops.cpp:1183-1204), and its backward
  * turning dL/dP into dL/dS in place (ops.cpp:1216-1224). */
 NNB_API nnb_status nnb_masked_softmax_fwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk, float* scores,
@@ -337,6 +349,28 @@ NNB_API nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float*
 NNB_API nnb_status nnb_sgemm_noalloc(void* stream, int trans_a, int trans_b, size_t m, size_t n,
 		size_t k, const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc,
 		int accumulate, int math_mode);
+
+/* ---- random streams and dropout (src/random.cpp, src/nn/dropout.cpp) ------------------------ */
+
+/* manual_seed / is_seeded / seed_epoch (include/nn/random.hpp:25-47); host only. */
+NNB_API void nnb_manual_seed(uint64_t seed);
+NNB_API int nnb_is_seeded(void);
+NNB_API uint64_t nnb_seed_epoch(void);
+/* derive_generator(stream) (random.hpp:58, random.cpp:67-79) as an mt19937 state in HOST memory:
+ * state[0..623] the untempered words, state[624] the index of the next word (624 after seeding).
+ * Copy it to the device for nnb_dropout_mask. Host only. */
+NNB_API nnb_status nnb_derive_generator(const char* stream_name, uint32_t* state);
+/* std::mt19937 seeded from std::seed_seq{seeds[0..count)}, in the same 625-word form; host only. */
+NNB_API nnb_status nnb_mt19937_seed_seq(const uint32_t* seeds, size_t count, uint32_t* state);
+/* Dropout::forward's draws (dropout.cpp:20-31): n outputs from the DEVICE state (advanced in place)
+ * into the keep mask keep[(n + 31) / 32] (bit e % 32 of word e / 32 = element e kept, i.e.
+ * u = float(x >> 8) * 2^-24 >= p). p == 0 keeps and p == 1 drops everything without drawing. */
+NNB_API nnb_status nnb_dropout_mask(void* stream, uint32_t* state, size_t n, float p, uint32_t* keep);
+/* y = x * m, m = kept ? 1 / (1 - p) : 0 (mul with the mask, ops.cpp:347). */
+NNB_API nnb_status nnb_dropout_apply(void* stream, size_t n, float p, const float* x, const uint32_t* keep, float* y);
+/* dx (+)= g * m with the grad_accum convention. */
+NNB_API nnb_status nnb_dropout_bwd(void* stream, size_t n, float p, const float* g, const uint32_t* keep, float* dx,
+		int dx_first);
 
 #ifdef __cplusplus
 }

@@ -13,6 +13,9 @@ nnb_status colsum(cudaStream_t s, const float* g, long long rows, long long cols
 nnb_status colsum_grouped(cudaStream_t s, const float* g, long long rows, long long cols, long long groups, float* out,
 		long long out_stride, int first);
 
+// Inverted dropout's factor for kept elements, 1 / (1 - p) in float (dropout.cpp:24); 0 for p == 1.
+float dropout_keep_scale(float p);
+
 // Elementwise ceiling for 1-D grids: enough blocks for n items, at most 148 * 64 blocks.
 inline unsigned grid_for(long long n, int threads) {
 	long long b = (n + threads - 1) / threads;

@@ -33,9 +33,16 @@ __device__ __forceinline__ float warp_sum(float v) {
 	return v;
 }
 
-// rows = N*H*Tq rows of Tk scores, in place. Row r: n = r / (H*Tq), i = r % Tq.
+__device__ __forceinline__ float keep_factor(const uint32_t* keep, long long i, float keep_scale) {
+	return ((keep[i >> 5] >> (i & 31)) & 1u) ? keep_scale : 0.0f;
+}
+
+// rows = N*H*Tq rows of Tk scores, in place. Row r: n = r / (H*Tq), i = r % Tq. With a keep mask
+// (dropout on the weights, attention.cpp:43-45) the dropped weights P * m also go to `weights`,
+// m = kept ? keep_scale : 0 (bit e of keep[e / 32] for element e = r * Tk + j).
 __global__ void masked_softmax_fwd_kernel(float* __restrict__ p, long long rows, int H, int Tq, int Tk,
-		const float* __restrict__ pad, int causal, float scale) {
+		const float* __restrict__ pad, int causal, float scale, const uint32_t* __restrict__ keep = nullptr,
+		float keep_scale = 0.0f, float* __restrict__ weights = nullptr) {
 	const int lane = threadIdx.x & 31;
 	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
 	if (r >= rows) return;
@@ -64,12 +71,23 @@ __global__ void masked_softmax_fwd_kernel(float* __restrict__ p, long long rows,
 		}
 	}
 	s = warp_sum(s);
-	for (int j = lane; j < Tk; j += 32) row[j] = row[j] / s;
+	if (keep) {
+		float* wrow = weights + r * Tk;
+		for (int j = lane; j < Tk; j += 32) {
+			const float y = row[j] / s;
+			row[j] = y;
+			wrow[j] = y * keep_factor(keep, r * Tk + j, keep_scale);
+		}
+	} else {
+		for (int j = lane; j < Tk; j += 32) row[j] = row[j] / s;
+	}
 }
 
-// g holds dL/dP on entry and dL/dS on exit; y = P
+// g holds dL/dP on entry and dL/dS on exit; y = P. With a keep mask g holds dL/d(P*m) on entry and
+// dL/dP = g * m + 0 (mul's backward into a fresh gradient, ops.cpp:347-356, 67-73) is used.
 __global__ void masked_softmax_bwd_kernel(const float* __restrict__ y, float* __restrict__ g, long long rows, int H,
-		int Tq, int Tk, const float* __restrict__ pad, int causal, float scale) {
+		int Tq, int Tk, const float* __restrict__ pad, int causal, float scale, const uint32_t* __restrict__ keep = nullptr,
+		float keep_scale = 0.0f) {
 	const int lane = threadIdx.x & 31;
 	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
 	if (r >= rows) return;
@@ -79,7 +97,15 @@ __global__ void masked_softmax_bwd_kernel(const float* __restrict__ y, float* __
 	const float* yr = y + r * Tk;
 	float* gr = g + r * Tk;
 	float dot = 0.0f;
-	for (int j = lane; j < Tk; j += 32) dot += gr[j] * yr[j];
+	if (keep) {
+		for (int j = lane; j < Tk; j += 32) {
+			const float gj = gr[j] * keep_factor(keep, r * Tk + j, keep_scale) + 0.0f;
+			gr[j] = gj;
+			dot += gj * yr[j];
+		}
+	} else {
+		for (int j = lane; j < Tk; j += 32) dot += gr[j] * yr[j];
+	}
 	dot = warp_sum(dot);
 	for (int j = lane; j < Tk; j += 32) {
 		const bool masked = (ph && ph[j] == 0.0f) || (causal && j > i);
@@ -171,6 +197,78 @@ nnb_status nnb_attention_bwd(void* stream, size_t N, size_t Tq, size_t Tk, size_
 		if (dq && (st = nnb::gemm_run(s, nnb::head_gemm(0, 0, Tq, Dh, Tk, ds, Tk, H * ps, ps, k, D, ks, Dh, dq, D, qs, Dh,
 				N, H, !dq_first))) != NNB_OK) break;
 		// dK (+)= dS^T Q_h  (ops.cpp:1291)
+		if (dk && (st = nnb::gemm_run(s, nnb::head_gemm(1, 0, Tk, Dh, Tq, ds, Tk, H * ps, ps, q, D, qs, Dh, dk, D, ks, Dh,
+				N, H, !dk_first))) != NNB_OK) break;
+	} while (0);
+	nnb_status st2 = nnb::scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
+}
+
+// Dropout on the attention weights (attention.cpp:36-47): the same head-batched products around
+// the masked softmax, with W = P * m between them; m comes from a keep mask drawn beforehand
+// (nnb_dropout_mask over the N*H*Tq*Tk weights in row-major order, as Dropout::forward draws).
+nnb_status nnb_attention_dropout_fwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* q, const float* k, const float* v, const float* key_padding_mask, int causal, float p,
+		const uint32_t* keep, float* out, float* probs, float* weights) {
+	NNB_TRY(nnb::check_shapes(N, Tq, Tk, D, heads, causal));
+	if (!(p >= 0.0f && p <= 1.0f)) return nnb::fail(NNB_ERR_INVALID, "attention_dropout_fwd: p must be in [0, 1]");
+	if (N == 0) return NNB_OK;
+	if (!q || !k || !v || !keep || !out || !probs || !weights)
+		return nnb::fail(NNB_ERR_INVALID, "attention_dropout_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long H = (long long)heads, Dh = (long long)(D / heads);
+	const long long qs = (long long)Tq * D, ks = (long long)Tk * D, ps = (long long)Tq * Tk;
+	const float scale = 1.0f / std::sqrt(static_cast<float>(Dh));     // attention.cpp:44
+	// scores = q k^T  (matmul_bt, attention.cpp:43)
+	NNB_TRY(nnb::gemm_run(s, nnb::head_gemm(0, 1, Tq, Tk, Dh, q, D, qs, Dh, k, D, ks, Dh, probs, Tk, H * ps, ps,
+		N, H, 0)));
+	const long long rows = (long long)N * H * Tq;
+	{
+		nnb::TraceScope ts(s, nnb::kTraceAttention);
+		nnb::masked_softmax_fwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(probs, rows, (int)H, (int)Tq,
+			(int)Tk, key_padding_mask, causal, scale, keep, nnb::dropout_keep_scale(p), weights);
+	}
+	NNB_CUDA_TRY(cudaGetLastError());
+	// merged = W v  (matmul, attention.cpp:46), written in place of the head transpose
+	return nnb::gemm_run(s, nnb::head_gemm(0, 0, Tq, Dh, Tk, weights, Tk, H * ps, ps, v, D, ks, Dh, out, D, qs, Dh, N,
+		H, 0));
+}
+
+nnb_status nnb_attention_dropout_bwd(void* stream, size_t N, size_t Tq, size_t Tk, size_t D, size_t heads,
+		const float* g, const float* q, const float* k, const float* v, const float* probs, const float* weights,
+		float p, const uint32_t* keep, const float* key_padding_mask, int causal, float* dq, int dq_first, float* dk,
+		int dk_first, float* dv, int dv_first) {
+	NNB_TRY(nnb::check_shapes(N, Tq, Tk, D, heads, causal));
+	if (!(p >= 0.0f && p <= 1.0f)) return nnb::fail(NNB_ERR_INVALID, "attention_dropout_bwd: p must be in [0, 1]");
+	if (N == 0) return NNB_OK;
+	if (!g || !q || !k || !v || !probs || !weights || !keep)
+		return nnb::fail(NNB_ERR_INVALID, "attention_dropout_bwd: null input");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	const long long H = (long long)heads, Dh = (long long)(D / heads);
+	const long long qs = (long long)Tq * D, ks = (long long)Tk * D, ps = (long long)Tq * Tk;
+	const float scale = 1.0f / std::sqrt(static_cast<float>(Dh));
+	void* ws = nullptr;
+	NNB_TRY(nnb::scratch_alloc(&ws, (size_t)N * H * ps * sizeof(float), s));
+	float* ds = static_cast<float*>(ws);
+	nnb_status st = NNB_OK;
+	do {
+		// dW = G v^T, dv (+)= W^T G  (matmul's backward)
+		if ((st = nnb::gemm_run(s, nnb::head_gemm(0, 1, Tq, Tk, Dh, g, D, qs, Dh, v, D, ks, Dh, ds, Tk, H * ps, ps, N, H,
+				0))) != NNB_OK) break;
+		if (dv && (st = nnb::gemm_run(s, nnb::head_gemm(1, 0, Tk, Dh, Tq, weights, Tk, H * ps, ps, g, D, qs, Dh, dv, D,
+				ks, Dh, N, H, !dv_first))) != NNB_OK) break;
+		if (!dq && !dk) break;
+		// dP = dW * m, then the masked softmax's backward, in one pass per row
+		const long long rows = (long long)N * H * Tq;
+		{
+			nnb::TraceScope ts(s, nnb::kTraceAttention);
+			nnb::masked_softmax_bwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(probs, ds, rows, (int)H,
+				(int)Tq, (int)Tk, key_padding_mask, causal, scale, keep, nnb::dropout_keep_scale(p));
+		}
+		if ((st = nnb::cuda_status(cudaGetLastError(), "softmax backward launch")) != NNB_OK) break;
+		// dq (+)= dS k, dk (+)= dS^T q  (matmul_bt's backward)
+		if (dq && (st = nnb::gemm_run(s, nnb::head_gemm(0, 0, Tq, Dh, Tk, ds, Tk, H * ps, ps, k, D, ks, Dh, dq, D, qs, Dh,
+				N, H, !dq_first))) != NNB_OK) break;
 		if (dk && (st = nnb::gemm_run(s, nnb::head_gemm(1, 0, Tk, Dh, Tq, ds, Tk, H * ps, ps, q, D, qs, Dh, dk, D, ks, Dh,
 				N, H, !dk_first))) != NNB_OK) break;
 	} while (0);

@@ -1,0 +1,306 @@
+// rng.cu -- the library's random streams (src/random.cpp) and inverted dropout (src/nn/dropout.cpp).
+//
+// Host side: the seeding registry. manual_seed(seed) fixes a base and resets the per-stream
+// counters; the k-th derive_generator(name) after it seeds an mt19937 from
+// splitmix64(base ^ fnv1a(name) ^ k * golden-ratio) split into two 32-bit words fed through a
+// seed_seq, exactly as src/random.cpp:67-79 does, so a given seed yields the reference's streams.
+// seed_seq::generate and mt19937's seed(seed_seq&) follow their definitions in the C++ standard
+// ([rand.util.seedseq], [rand.eng.mers]); SplitMix64 (Steele, Lea & Flood 2014) and FNV-1a 64
+// (Fowler, Noll & Vo) are the published functions.
+//
+// Device side: one generator state = 624 untempered words + the index of the next word to temper
+// (625 uint32 in HBM), so successive draws continue the stream across launches and inside CUDA
+// graphs. A draw of n outputs runs in ONE CTA of 640 threads: the twist that makes the next 624
+// words is three dependent data-parallel phases (words [0,227) read only the old block, [227,454)
+// and [454,624) read words 227 back in the new block), and each 32 consecutive outputs become one
+// keep-mask word through a warp ballot. The stream is serial by definition (the reference draws
+// output i for element i in row-major order), so the cost is ~one twist per 624 elements on one
+// SM; the masks are 1 bit per element (the reference keeps a float per element).
+//
+// Dropout (dropout.cpp:20-31): u = float(x >> 8) * 2^-24 per element, dropped when u < p, kept
+// elements scaled by 1/(1-p); p == 1 drops everything without drawing, p == 0 keeps everything
+// without drawing.
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <random>
+#include <string>
+
+#include "nnb_internal.h"
+#include "nnb_trace.h"
+
+namespace nnb {
+
+namespace {
+
+constexpr int kMtN = 624;
+constexpr int kMtShift = 397;
+constexpr int kMtHalf = kMtN - kMtShift;     // 227: words before this index read only old words
+constexpr int kMtThreads = 640;              // 20 warps: one keep-mask word each per block of 624
+constexpr uint32_t kMtMatrix = 0x9908b0dfu;
+
+// ---- host: seed_seq + mt19937 seeding ------------------------------------------------------------
+
+// seed_seq{seeds...}.generate(out, out + n) per [rand.util.seedseq]
+void seed_seq_generate(const uint32_t* seeds, size_t s, uint32_t* out, size_t n) {
+	for (size_t i = 0; i < n; i++) out[i] = 0x8b8b8b8bu;
+	const size_t t = n >= 623 ? 11 : n >= 68 ? 7 : n >= 39 ? 5 : n >= 7 ? 3 : (n - 1) / 2;
+	const size_t p = (n - t) / 2, q = p + t, m = std::max(s + 1, n);
+	auto T = [](uint32_t x) { return x ^ (x >> 27); };
+	for (size_t k = 0; k < m; k++) {
+		const uint32_t r1 = 1664525u * T(out[k % n] ^ out[(k + p) % n] ^ out[(k + n - 1) % n]);
+		uint32_t r2 = r1;
+		if (k == 0) r2 += static_cast<uint32_t>(s);
+		else if (k <= s) r2 += static_cast<uint32_t>(k % n) + seeds[k - 1];
+		else r2 += static_cast<uint32_t>(k % n);
+		out[(k + p) % n] += r1;
+		out[(k + q) % n] += r2;
+		out[k % n] = r2;
+	}
+	for (size_t k = m; k < m + n; k++) {
+		const uint32_t r3 = 1566083941u * T(out[k % n] + out[(k + p) % n] + out[(k + n - 1) % n]);
+		const uint32_t r4 = r3 - static_cast<uint32_t>(k % n);
+		out[(k + p) % n] ^= r3;
+		out[(k + q) % n] ^= r4;
+		out[k % n] = r4;
+	}
+}
+
+// mt19937::seed(seed_seq&) per [rand.eng.mers]: the 624 generated words are the state; an all-zero
+// state (ignoring the low 31 bits of word 0) becomes 2^31 in word 0. The index starts at 624, so
+// the first draw twists.
+void mt_seed_from_seq(const uint32_t* seeds, size_t s, uint32_t* state) {
+	seed_seq_generate(seeds, s, state, kMtN);
+	bool zero = (state[0] & 0x80000000u) == 0;
+	for (int i = 1; i < kMtN && zero; i++) zero = state[i] == 0;
+	if (zero) state[0] = 0x80000000u;
+	state[kMtN] = kMtN;
+}
+
+uint64_t splitmix64(uint64_t x) {
+	x += 0x9e3779b97f4a7c15ull;
+	x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+	x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+	return x ^ (x >> 31);
+}
+
+uint64_t fnv1a64(const char* s) {
+	uint64_t h = 0xcbf29ce484222325ull;
+	for (; *s; ++s) h = (h ^ static_cast<unsigned char>(*s)) * 0x100000001b3ull;
+	return h;
+}
+
+struct Registry {
+	std::mutex mu;
+	bool seeded = false, has_base = false;
+	uint64_t base = 0, epoch = 0;
+	std::map<std::string, uint64_t> counters;
+};
+
+Registry& registry() {
+	static Registry r;
+	return r;
+}
+
+// ---- device: mt19937 blocks and the keep mask ----------------------------------------------------
+
+__device__ __forceinline__ uint32_t mt_mix(uint32_t upper_of, uint32_t lower_of) {
+	const uint32_t y = (upper_of & 0x80000000u) | (lower_of & 0x7fffffffu);
+	return (y >> 1) ^ ((y & 1u) ? kMtMatrix : 0u);
+}
+
+__device__ __forceinline__ uint32_t mt_temper(uint32_t y) {
+	y ^= y >> 11;
+	y ^= (y << 7) & 0x9d2c5680u;
+	y ^= (y << 15) & 0xefc60000u;
+	return y ^ (y >> 18);
+}
+
+// nw = the block after `old` (all threads of the CTA call it; ends with the CTA synchronised)
+__device__ __forceinline__ void mt_next_block(const uint32_t* old, uint32_t* nw, int t) {
+	if (t < kMtHalf) nw[t] = old[t + kMtShift] ^ mt_mix(old[t], old[t + 1]);
+	__syncthreads();
+	if (t >= kMtHalf && t < 2 * kMtHalf) nw[t] = nw[t - kMtHalf] ^ mt_mix(old[t], old[t + 1]);
+	__syncthreads();
+	if (t >= 2 * kMtHalf && t < kMtN - 1) nw[t] = nw[t - kMtHalf] ^ mt_mix(old[t], old[t + 1]);
+	else if (t == kMtN - 1) nw[t] = nw[t - kMtHalf] ^ mt_mix(old[t], nw[0]);
+	__syncthreads();
+}
+
+// Draws n >= 1 outputs from `state` (advancing it) and writes keep[w] bit b = element 32w + b kept.
+// Output r (relative to the first one drawn) lives in block r / 624 at word r % 624, where block 0
+// is the state's current block (twisted first if its words are used up).
+__global__ void __launch_bounds__(kMtThreads, 1) dropout_mask_kernel(uint32_t* __restrict__ state,
+		unsigned long long n, float p, uint32_t* __restrict__ keep) {
+	__shared__ uint32_t buf[2][kMtN];
+	const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+	for (int i = t; i < kMtN; i += kMtThreads) buf[0][i] = state[i];
+	unsigned long long pos = state[kMtN];
+	__syncthreads();
+	int a = 0;
+	if (pos >= (unsigned long long)kMtN) {
+		mt_next_block(buf[0], buf[1], t);
+		a = 1;
+		pos = 0;
+	}
+	const unsigned long long last = pos + n - 1, last_block = last / kMtN, words = (n + 31) / 32;
+	for (unsigned long long blk = 0;; ++blk) {
+		if (blk < last_block) mt_next_block(buf[a], buf[a ^ 1], t);
+		// words whose first output falls in this block: 624 blk <= pos + 32 w < 624 (blk + 1)
+		const unsigned long long w_lo = blk == 0 ? 0 : (kMtN * blk - pos + 31) / 32;
+		unsigned long long w_hi = (kMtN * (blk + 1) - pos + 31) / 32;
+		if (w_hi > words) w_hi = words;
+		const unsigned long long w = w_lo + warp;
+		if (w < w_hi) {
+			const unsigned long long e = 32 * w + lane;
+			bool kept = false;
+			if (e < n) {
+				const unsigned long long idx = pos + e - kMtN * blk;      // < 2 * 624
+				const uint32_t x = idx < (unsigned long long)kMtN ? buf[a][idx] : buf[a ^ 1][idx - kMtN];
+				const float u = static_cast<float>(mt_temper(x) >> 8) * (1.0f / 16777216.0f);
+				kept = !(u < p);
+			}
+			const uint32_t word = __ballot_sync(0xffffffffu, kept);
+			if (lane == 0) keep[w] = word;
+		}
+		if (blk == last_block) {
+			for (int i = t; i < kMtN; i += kMtThreads) state[i] = buf[a][i];
+			if (t == 0) state[kMtN] = (uint32_t)(last % kMtN + 1);
+			return;
+		}
+		__syncthreads();       // every read of this block is done before the next twist overwrites it
+		a ^= 1;
+	}
+}
+
+__device__ __forceinline__ float keep_factor(const uint32_t* keep, unsigned long long i, float scale) {
+	return ((keep[i >> 5] >> (i & 31)) & 1u) ? scale : 0.0f;
+}
+
+// y = x * m, m = kept ? scale : 0 (mul, ops.cpp:347 on the mask tensor)
+__global__ void dropout_apply_kernel(unsigned long long n, float scale, const float* __restrict__ x,
+		const uint32_t* __restrict__ keep, float* __restrict__ y) {
+	const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+	for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < n; i += stride)
+		y[i] = x[i] * keep_factor(keep, i, scale);
+}
+
+// dx (first: =, else +=) g * m, with the grad_accum convention (ops.cpp:67-73)
+__global__ void dropout_bwd_kernel(unsigned long long n, float scale, const float* __restrict__ g,
+		const uint32_t* __restrict__ keep, float* __restrict__ dx, int first) {
+	const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+	for (unsigned long long i = blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x; i < n; i += stride) {
+		const float v = g[i] * keep_factor(keep, i, scale);
+		dx[i] = first ? v + 0.0f : dx[i] + v;
+	}
+}
+
+nnb_status elementwise_grid(unsigned long long n, unsigned* blocks) {
+	DeviceState* ds = nullptr;
+	NNB_TRY(device_state(&ds));
+	const unsigned long long want = (n + 255) / 256, cap = (unsigned long long)ds->sm_count * 8;
+	*blocks = (unsigned)(want < cap ? want : cap);
+	return NNB_OK;
+}
+
+nnb_status check_p(float p) {
+	if (!(p >= 0.0f && p <= 1.0f)) return fail(NNB_ERR_INVALID, "dropout: p must be in [0, 1] (got %g)", (double)p);
+	return NNB_OK;
+}
+
+}  // namespace
+
+float dropout_keep_scale(float p) { return p < 1.0f ? 1.0f / (1.0f - p) : 0.0f; }
+
+nnb_status dropout_mask(cudaStream_t s, uint32_t* state, size_t n, float p, uint32_t* keep) {
+	NNB_TRY(check_p(p));
+	if (n == 0) return NNB_OK;
+	if (!state || !keep) return fail(NNB_ERR_INVALID, "dropout_mask: null pointer");
+	const size_t words = (n + 31) / 32;
+	TraceScope ts(s, kTraceRowwise);
+	if (p == 0.0f || p == 1.0f)        // nothing is drawn (dropout.cpp:20-23)
+		return cuda_status(cudaMemsetAsync(keep, p == 0.0f ? 0xff : 0, words * sizeof(uint32_t), s), "dropout mask fill");
+	dropout_mask_kernel<<<1, kMtThreads, 0, s>>>(state, (unsigned long long)n, p, keep);
+	return cuda_status(cudaGetLastError(), "dropout_mask launch");
+}
+
+}  // namespace nnb
+
+extern "C" {
+
+void nnb_manual_seed(uint64_t seed) {
+	nnb::Registry& r = nnb::registry();
+	std::lock_guard<std::mutex> lock(r.mu);
+	r.seeded = r.has_base = true;
+	r.base = seed;
+	r.epoch++;
+	r.counters.clear();
+}
+
+int nnb_is_seeded(void) {
+	nnb::Registry& r = nnb::registry();
+	std::lock_guard<std::mutex> lock(r.mu);
+	return r.seeded ? 1 : 0;
+}
+
+uint64_t nnb_seed_epoch(void) {
+	nnb::Registry& r = nnb::registry();
+	std::lock_guard<std::mutex> lock(r.mu);
+	return r.epoch;
+}
+
+nnb_status nnb_derive_generator(const char* stream_name, uint32_t* state) {
+	if (!stream_name || !state) return nnb::fail(NNB_ERR_INVALID, "derive_generator: null pointer");
+	nnb::Registry& r = nnb::registry();
+	uint64_t s;
+	{
+		std::lock_guard<std::mutex> lock(r.mu);
+		if (!r.has_base) {           // unseeded: a nondeterministic base, taken once
+			std::random_device rd;
+			r.base = (static_cast<uint64_t>(rd()) << 32) ^ rd();
+			r.has_base = true;
+		}
+		const uint64_t k = r.counters[stream_name]++;
+		s = nnb::splitmix64(r.base ^ nnb::fnv1a64(stream_name) ^ (k * 0x9e3779b97f4a7c15ull));
+	}
+	const uint32_t seeds[2] = {static_cast<uint32_t>(s), static_cast<uint32_t>(s >> 32)};
+	nnb::mt_seed_from_seq(seeds, 2, state);
+	return NNB_OK;
+}
+
+nnb_status nnb_mt19937_seed_seq(const uint32_t* seeds, size_t count, uint32_t* state) {
+	if ((count && !seeds) || !state) return nnb::fail(NNB_ERR_INVALID, "mt19937_seed_seq: null pointer");
+	nnb::mt_seed_from_seq(seeds, count, state);
+	return NNB_OK;
+}
+
+nnb_status nnb_dropout_mask(void* stream, uint32_t* state, size_t n, float p, uint32_t* keep) {
+	return nnb::dropout_mask(static_cast<cudaStream_t>(stream), state, n, p, keep);
+}
+
+nnb_status nnb_dropout_apply(void* stream, size_t n, float p, const float* x, const uint32_t* keep, float* y) {
+	NNB_TRY(nnb::check_p(p));
+	if (n == 0) return NNB_OK;
+	if (!x || !keep || !y) return nnb::fail(NNB_ERR_INVALID, "dropout_apply: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	unsigned blocks;
+	NNB_TRY(nnb::elementwise_grid(n, &blocks));
+	nnb::TraceScope ts(s, nnb::kTraceRowwise);
+	nnb::dropout_apply_kernel<<<blocks, 256, 0, s>>>(n, nnb::dropout_keep_scale(p), x, keep, y);
+	return nnb::cuda_status(cudaGetLastError(), "dropout_apply launch");
+}
+
+nnb_status nnb_dropout_bwd(void* stream, size_t n, float p, const float* g, const uint32_t* keep, float* dx,
+		int dx_first) {
+	NNB_TRY(nnb::check_p(p));
+	if (n == 0) return NNB_OK;
+	if (!g || !keep || !dx) return nnb::fail(NNB_ERR_INVALID, "dropout_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	unsigned blocks;
+	NNB_TRY(nnb::elementwise_grid(n, &blocks));
+	nnb::TraceScope ts(s, nnb::kTraceRowwise);
+	nnb::dropout_bwd_kernel<<<blocks, 256, 0, s>>>(n, nnb::dropout_keep_scale(p), g, keep, dx, dx_first);
+	return nnb::cuda_status(cudaGetLastError(), "dropout_bwd launch");
+}
+
+}  // extern "C"

@@ -70,6 +70,9 @@ _SIGS = {
     "nnb_flash_attention_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _p], _i),
     "nnb_flash_attention_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _p, _i],
                                 _i),
+    "nnb_attention_dropout_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _f, _p, _p, _p, _p], _i),
+    "nnb_attention_dropout_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _f, _p, _p, _i, _p, _i, _p, _i,
+                                   _p, _i], _i),
     "nnb_masked_softmax_fwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _i, _f], _i),
     "nnb_masked_softmax_bwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _f], _i),
     "nnb_conv2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _i, _p, _p], _i),
@@ -104,6 +107,14 @@ _SIGS = {
     "nnb_embedding_fwd": ([_p, _sz, _sz, _p, _p, _sz, _p], _i),
     "nnb_embedding_bwd": ([_p, _sz, _sz, _p, _sz, _p, _p, _i], _i),
     "nnb_adamw_step": ([_p, _sz, _p, _p, _p, _p, _f, _f, _f, _f, _f, _c.c_longlong], _i),
+    "nnb_manual_seed": ([_c.c_uint64], None),
+    "nnb_is_seeded": ([], _i),
+    "nnb_seed_epoch": ([], _c.c_uint64),
+    "nnb_derive_generator": ([_c.c_char_p, _p], _i),
+    "nnb_mt19937_seed_seq": ([_p, _sz, _p], _i),
+    "nnb_dropout_mask": ([_p, _p, _sz, _f, _p], _i),
+    "nnb_dropout_apply": ([_p, _sz, _f, _p, _p, _p], _i),
+    "nnb_dropout_bwd": ([_p, _sz, _f, _p, _p, _p, _i], _i),
 }
 
 

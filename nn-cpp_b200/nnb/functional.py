@@ -290,6 +290,63 @@ def _flash_attention(q, k, v, heads, key_padding_mask, causal, N, Tq, Tk, D) -> 
     return Value.node(out, (q, k, v), backward)
 
 
+# ---- dropout (src/nn/dropout.cpp:20-31) and attention with dropout (src/nn/attention.cpp:36-47) ------
+
+def dropout_mask(state: torch.Tensor, n: int, p: float) -> torch.Tensor:
+    """Dropout::forward's n keep / drop decisions drawn from the device generator `state` (advanced
+    in place): (n + 31) // 32 words, bit e % 32 of word e // 32 set when element e is kept."""
+    keep = empty(((n + 31) // 32,), dtype=torch.int32, device=state.device)
+    check(lib().nnb_dropout_mask(_s(), _p(state), n, ctypes.c_float(p), _p(keep)))
+    return keep
+
+
+def dropout(x: Value, p: float, state: torch.Tensor) -> Value:
+    """x * m, m = 0 with probability p else 1 / (1 - p), the mask drawn from `state` in row-major order."""
+    n = x.data.numel()
+    keep = dropout_mask(state, n, p)
+    y = empty(x.shape, device=x.data.device)
+    check(lib().nnb_dropout_apply(_s(), n, ctypes.c_float(p), _p(x.data), _p(keep), _p(y)))
+
+    def backward(g):
+        if _need(x):
+            dx, f = x.grad_accum()
+            check(lib().nnb_dropout_bwd(_s(), n, ctypes.c_float(p), _p(g), _p(keep), _p(dx), f))
+
+    return Value.node(y, (x,), backward)
+
+
+def attention_dropout(q: Value, k: Value, v: Value, heads: int, key_padding_mask: torch.Tensor | None, causal: bool,
+                      p: float, state: torch.Tensor) -> Value:
+    """MultiHeadAttention's core with its Dropout active: per head scores = q k^T, scaled_masked_softmax
+    (ops.cpp:1298-1343), the dropout mask drawn over the [N, heads, Tq, Tk] weights, then weights v.
+    The probabilities and the dropped weights are kept for the backward, as the reference's graph
+    keeps them."""
+    qs, ks = q.shape, k.shape
+    if len(qs) != 3 or len(ks) != 3 or v.shape != ks or qs[0] != ks[0] or qs[2] != ks[2]:
+        raise TensorShapeError("attention: shapes do not agree")
+    N, Tq, D = qs
+    Tk = ks[1]
+    if heads == 0 or D % heads or (causal and Tq != Tk):
+        raise TensorShapeError("attention: bad heads or causal shape")
+    if key_padding_mask is not None and tuple(key_padding_mask.shape) != (N, Tk):
+        raise TensorShapeError("attention: key padding mask must be [N, Tk]")
+    keep = dropout_mask(state, N * heads * Tq * Tk, p)
+    out, probs, weights = empty((N, Tq, D)), empty((N, heads, Tq, Tk)), empty((N, heads, Tq, Tk))
+    check(lib().nnb_attention_dropout_fwd(_s(), N, Tq, Tk, D, heads, _p(q.data), _p(k.data), _p(v.data),
+                                          _p(key_padding_mask), int(causal), ctypes.c_float(p), _p(keep), _p(out),
+                                          _p(probs), _p(weights)))
+
+    def backward(g):
+        dv, fv = v.grad_accum() if _need(v) else (None, 0)
+        dq, fq = q.grad_accum() if _need(q) else (None, 0)
+        dk, fk = k.grad_accum() if _need(k) else (None, 0)
+        check(lib().nnb_attention_dropout_bwd(_s(), N, Tq, Tk, D, heads, _p(g), _p(q.data), _p(k.data), _p(v.data),
+                                              _p(probs), _p(weights), ctypes.c_float(p), _p(keep),
+                                              _p(key_padding_mask), int(causal), _p(dq), fq, _p(dk), fk, _p(dv), fv))
+
+    return Value.node(out, (q, k, v), backward)
+
+
 # ---- convolution and pooling ---------------------------------------------------------------------
 
 def conv2d(x: Value, weight: Value, bias: Value, stride: int, padding: int, fuse_relu: bool = False,

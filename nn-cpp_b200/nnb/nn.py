@@ -7,7 +7,8 @@ reference, so a checkpoint or a parameter list maps one to one:
   LayerNorm         src/nn/layernorm.cpp             gamma, beta
   Embedding         src/nn/embedding.cpp             weight [V, D]
   PositionalEncoding (sinusoidal) src/nn/positional.cpp:15-38
-  MultiHeadAttention src/nn/attention.cpp:15-48      q., k., v., o. (dropout 0: the fused attention op)
+  MultiHeadAttention src/nn/attention.cpp:15-48      q., k., v., o. (no active dropout: the fused attention op)
+  Dropout           src/nn/dropout.cpp               device mt19937 stream, 1-bit keep masks
   TransformerBlock  src/nn/transformer.cpp:37-55     ln1., attn., ln2., fc1., fc2.  (pre-LN)
   Transformer       src/nn/transformer.cpp:66-90     embed., pos., blocks.<i>., ln_f., head.
   Conv2d / Sequential (folds Conv2d + ReLU into conv2d_relu, src/nn/sequential.cpp:16-28)
@@ -26,6 +27,7 @@ import torch
 
 from . import TensorShapeError, check, lib
 from . import functional as F
+from . import random as nnb_random
 from .autograd import Value
 
 
@@ -34,8 +36,30 @@ def _param(array: np.ndarray, device) -> Value:
 
 
 class Module:
+    training = True
+
     def named_parameters(self) -> list[tuple[str, Value]]:
         return []
+
+    def train(self, mode: bool = True):
+        """Sets training / evaluation mode here and in every sub-module (Module::train, module.hpp:93)."""
+        self.training = mode
+        for child in vars(self).values():
+            for m in (child if isinstance(child, list) else [child]):
+                if isinstance(m, Module):
+                    m.train(mode)
+        return self
+
+    def eval(self):
+        return self.train(False)
+
+    def modules(self):
+        """This module and every sub-module, depth first in attribute order."""
+        yield self
+        for child in vars(self).values():
+            for m in (child if isinstance(child, list) else [child]):
+                if isinstance(m, Module):
+                    yield from m.modules()
 
     def named_buffers(self) -> list[tuple[str, torch.Tensor]]:
         return []
@@ -119,18 +143,52 @@ class PositionalEncoding(Module):
         return F.add(x, Value.leaf(self.pe.data[: x.shape[1]], False))
 
 
+class Dropout(Module):
+    """Inverted dropout (src/nn/dropout.cpp): in training mode each element is zeroed with probability
+    p and the rest scaled by 1 / (1 - p); identity in evaluation mode or for p == 0. The layer takes
+    the next "dropout" stream at construction (so layers built in the reference's order after the
+    same manual_seed draw its masks) and keeps the generator on the device."""
+
+    def __init__(self, p: float = 0.5, device=None):
+        if not (0.0 <= p <= 1.0):
+            raise ValueError("Dropout: p must be in [0, 1]")
+        self.p = p
+        self.state = nnb_random.device_generator("dropout", device or torch.device("cuda", torch.cuda.current_device()))
+
+    def active(self) -> bool:
+        return self.training and self.p > 0.0
+
+    def forward(self, x: Value) -> Value:
+        return F.dropout(x, self.p, self.state) if self.active() else x
+
+
 class MultiHeadAttention(Module):
-    def __init__(self, dim: int, heads: int, causal: bool, rng, device):
+    """Multi-head attention (src/nn/attention.cpp). Without active dropout the core is one op (the
+    fused kernels for head size 64); with it, the composed path with dropout on the weights."""
+
+    def __init__(self, dim: int, heads: int, causal: bool, rng, device, dropout: float = 0.0):
         if heads == 0 or dim % heads:
             raise ValueError("MultiHeadAttention: dim must be divisible by heads")
-        self.heads, self.causal = heads, causal
+        self.dim, self.heads, self.causal = dim, heads, causal
         self.q = Linear(dim, dim, rng, device)
         self.k = Linear(dim, dim, rng, device)
         self.v = Linear(dim, dim, rng, device)
         self.o = Linear(dim, dim, rng, device)
+        self.drop = Dropout(dropout, device)
 
     def forward(self, x: Value) -> Value:
-        return self.o(F.attention(self.q(x), self.k(x), self.v(x), self.heads, None, self.causal))
+        return self.attend(x, x)
+
+    def attend(self, query: Value, context: Value, key_padding_mask: torch.Tensor | None = None) -> Value:
+        """attention.cpp:22-48: queries from `query`, keys and values from `context`."""
+        qs, cs = query.shape, context.shape
+        if len(qs) != 3 or len(cs) != 3 or qs[2] != self.dim or cs[2] != self.dim or qs[0] != cs[0]:
+            raise TensorShapeError("MultiHeadAttention: bad input shapes")
+        q, k, v = self.q(query), self.k(context), self.v(context)
+        if not self.drop.active():
+            return self.o(F.attention(q, k, v, self.heads, key_padding_mask, self.causal))
+        return self.o(F.attention_dropout(q, k, v, self.heads, key_padding_mask, self.causal, self.drop.p,
+                                          self.drop.state))
 
     def named_parameters(self):
         out = []
@@ -140,19 +198,21 @@ class MultiHeadAttention(Module):
 
 
 class TransformerBlock(Module):
-    """x + attn(ln1(x)), then + fc2(gelu(fc1(ln2(.)))) (transformer.cpp:41-44); dropout 0 is the identity,
-    and fc1 + gelu run as one GEMM with the GELU in its epilogue."""
+    """x + attn(ln1(x)), then + drop(fc2(gelu(fc1(ln2(.))))) (transformer.cpp:41-44); fc1 + gelu run as
+    one GEMM with the GELU in its epilogue. The attention's and the block's Dropout layers are built
+    in the reference's member order (attention first), so their streams match its own."""
 
-    def __init__(self, dim: int, heads: int, mlp_ratio: int, causal: bool, rng, device):
+    def __init__(self, dim: int, heads: int, mlp_ratio: int, causal: bool, rng, device, dropout: float = 0.0):
         self.ln1 = LayerNorm(dim, device)
-        self.attn = MultiHeadAttention(dim, heads, causal, rng, device)
+        self.attn = MultiHeadAttention(dim, heads, causal, rng, device, dropout)
         self.ln2 = LayerNorm(dim, device)
         self.fc1 = Linear(dim, mlp_ratio * dim, rng, device)
         self.fc2 = Linear(mlp_ratio * dim, dim, rng, device)
+        self.drop = Dropout(dropout, device)
 
     def forward(self, x: Value) -> Value:
         h = F.add(x, self.attn(self.ln1(x)))
-        return F.add(h, self.fc2(F.linear_gelu(self.ln2(h), self.fc1.weight, self.fc1.bias)))
+        return F.add(h, self.drop(self.fc2(F.linear_gelu(self.ln2(h), self.fc1.weight, self.fc1.bias))))
 
     def named_parameters(self):
         out = []
@@ -164,13 +224,14 @@ class TransformerBlock(Module):
 
 @dataclass
 class TransformerConfig:
-    """include/nn/nn/transformer.hpp:36-46 (sinusoidal positions, dropout 0)."""
+    """include/nn/nn/transformer.hpp:36-46 (sinusoidal positions)."""
     vocab_size: int
     dim: int
     heads: int
     layers: int
     max_len: int
     mlp_ratio: int = 4
+    dropout: float = 0.0
     causal: bool = True
 
 
@@ -185,7 +246,8 @@ class Transformer(Module):
         self.config = c
         self.embed = Embedding(c.vocab_size, c.dim, rng, device)
         self.pos = PositionalEncoding(c.max_len, c.dim, device)
-        self.blocks = [TransformerBlock(c.dim, c.heads, c.mlp_ratio, c.causal, rng, device) for _ in range(c.layers)]
+        self.blocks = [TransformerBlock(c.dim, c.heads, c.mlp_ratio, c.causal, rng, device, c.dropout)
+                       for _ in range(c.layers)]
         self.ln_f = LayerNorm(c.dim, device)
         self.head = Linear(c.dim, c.vocab_size, rng, device)
 

@@ -38,6 +38,11 @@ class ShardedTrainer:
     def __init__(self, model, optimizer, shards: int = 8, world: int = 1, rank: int = 0, group=None):
         if shards % world:
             raise ValueError("the virtual shard count must be a multiple of the number of ranks")
+        from .nn import Dropout
+        if world > 1 and any(isinstance(m, Dropout) and m.p > 0 for m in model.modules()):
+            # the reference draws one mask over the whole batch; a rank's slice of that draw would need
+            # the whole serial stream on every rank
+            raise NotImplementedError("dropout with more than one rank")
         self.model, self.opt = model, optimizer
         self.shards, self.world, self.rank, self.group = shards, world, rank, group
         self.owned = list(range(rank * shards // world, (rank + 1) * shards // world))

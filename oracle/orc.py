@@ -74,6 +74,8 @@ _REF_SIGS = {
     "ref_matmul_nd": ([_p, _p, _i, _p, _p, _i, _i, _i, _p], _i),
     "ref_transformer_train": ([_sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _f, _f, _i, _p, _p, _p],
                               _c.c_longlong),
+    "ref_transformer_train_ex": ([_c.c_uint64, _f, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _f, _f, _i, _p, _p,
+                                  _p], _c.c_longlong),
     "ref_cnn_fwd_bwd": ([_sz, _p, _p, _p, _p, _p, _p], None),
     "ref_linear": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _p], None),
     "ref_layernorm": ([_sz, _sz, _p, _p, _p, _f, _p, _p, _p, _p, _p], None),
@@ -86,6 +88,10 @@ _REF_SIGS = {
     "ref_reduce4": ([_sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _p], None),
     "ref_global_avgpool": ([_sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
     "ref_bn2d_module": ([_sz, _sz, _sz, _sz, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], None),
+    "ref_mt19937_outputs": ([_p, _sz, _sz, _p], None),
+    "ref_derive_outputs": ([_c.c_uint64, _c.c_char_p, _i, _sz, _p], None),
+    "ref_dropout_masks": ([_c.c_uint64, _i, _f, _p, _i, _p], None),
+    "ref_mha_dropout": ([_c.c_uint64, _sz, _sz, _sz, _sz, _i, _f, _i, _p, _p, _p, _p, _p, _p], None),
     "ref_linear_checkpoint_save": ([_c.c_char_p, _p, _p, _p, _p, _f, _f, _c.c_longlong], _i),
     "ref_linear_checkpoint_load": ([_c.c_char_p, _p, _p], _c.c_longlong),
     "ref_gelu": ([_sz, _p, _p, _p, _p], None),
@@ -202,3 +208,30 @@ def sgemm_f64_sample(ta, tb, k, a, lda, b, ldb, c, ldc, accumulate, rows, cols):
     orc.orc_sgemm_f64_sample(int(ta), int(tb), k, ptr(a), lda, ptr(b), ldb, ptr(c) if c is not None else None,
                              ldc, int(accumulate), ptr(rows), ptr(cols), len(rows), ptr(val), ptr(mag))
     return val, mag
+
+
+# ---- random streams and dropout (src/random.cpp, src/nn/dropout.cpp) -----------------------------
+
+def mt_outputs(state: np.ndarray, n: int):
+    """n outputs of the mt19937 whose state is key = state[:624], next index = state[624] (numpy's
+    MT19937 bit generator, the published algorithm); returns (outputs uint32[n], new state)."""
+    bg = np.random.MT19937()
+    bg.state = {"bit_generator": "MT19937", "state": {"key": np.asarray(state[:624], np.uint32), "pos": int(state[624])}}
+    out = bg.random_raw(n).astype(np.uint32) if n else np.zeros(0, np.uint32)
+    st = bg.state["state"]
+    return out, np.concatenate([np.asarray(st["key"], np.uint32), np.array([st["pos"]], np.uint32)])
+
+
+def dropout_draws(state: np.ndarray, n: int, p: float):
+    """Dropout::forward's mask values (src/nn/dropout.cpp:20-31) from an mt19937 state: u = float(x >> 8)
+    * 2^-24, 0 when u < p else 1 / (1 - p) in float32; p == 0 or 1 draw nothing. Returns (mask
+    float32[n], new state)."""
+    p = np.float32(p)
+    if p == 0:
+        return np.ones(n, np.float32), np.array(state, np.uint32)
+    if p == 1:
+        return np.zeros(n, np.float32), np.array(state, np.uint32)
+    x, new = mt_outputs(state, n)
+    u = (x >> 8).astype(np.float32) * np.float32(1.0 / 16777216.0)
+    keep = np.float32(1.0) / (np.float32(1.0) - p)
+    return np.where(u < p, np.float32(0.0), keep).astype(np.float32), new

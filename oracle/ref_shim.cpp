@@ -10,6 +10,9 @@
  */
 #include "nn/autograd/ops.hpp"
 #include "nn/checkpoint.hpp"
+#include "nn/nn/attention.hpp"
+#include "nn/nn/dropout.hpp"
+#include "nn/random.hpp"
 #include "nn/nn/linear.hpp"
 #include "nn/autograd/value.hpp"
 #include "nn/kernels/gemm.hpp"
@@ -348,6 +351,67 @@ int64_t ref_linear_checkpoint_load(const char* path, float* w, float* b) {
 	}
 }
 
+// n outputs of std::mt19937 seeded from std::seed_seq{seeds[0..count)}.
+void ref_mt19937_outputs(const uint32_t* seeds, size_t count, size_t n, uint32_t* out) {
+	std::seed_seq seq(seeds, seeds + count);
+	std::mt19937 g(seq);
+	for (size_t i = 0; i < n; i++) out[i] = g();
+}
+
+// manual_seed(seed), `skip` derive_generator(stream) calls, then n outputs of the next one.
+void ref_derive_outputs(uint64_t seed, const char* stream, int skip, size_t n, uint32_t* out) {
+	nn::manual_seed(seed);
+	for (int i = 0; i < skip; i++) nn::derive_generator(stream);
+	std::mt19937 g = nn::derive_generator(stream);
+	for (size_t i = 0; i < n; i++) out[i] = g();
+}
+
+// manual_seed(seed), `skip` Dropout layers constructed and dropped, then Dropout(p) applied to
+// ones of sizes[0], sizes[1], ... in turn: out gets the masks one after another.
+void ref_dropout_masks(uint64_t seed, int skip, float p, const size_t* sizes, int count, float* out) {
+	nn::manual_seed(seed);
+	for (int i = 0; i < skip; i++) nn::Dropout unused(p);
+	nn::Dropout d(p);
+	size_t off = 0;
+	for (int c = 0; c < count; c++) {
+		std::vector<float> ones(sizes[c], 1.0f);
+		Value y = d.forward(Value::leaf(Tensor({sizes[c]}, ones), false));
+		copy_out(y.data(), out + off);
+		off += sizes[c];
+	}
+}
+
+// manual_seed(seed); MultiHeadAttention(D, heads, causal, p) with params = q.w, q.b, k.w, k.b, v.w,
+// v.b, o.w, o.b (flat); `calls` forward + backward passes of x [N, T, D] with upstream gradient g
+// (the dropout stream advances between them); y, dx and dparams (flat, same order) of the last.
+void ref_mha_dropout(uint64_t seed, size_t N, size_t T, size_t D, size_t heads, int causal, float p, int calls,
+		const float* params, const float* x, const float* g, float* y, float* dx, float* dparams) {
+	nn::manual_seed(seed);
+	nn::MultiHeadAttention mha(D, heads, causal != 0, p);
+	auto named = mha.named_parameters();
+	size_t off = 0;
+	for (auto& q : named) {
+		Tensor& d = q.second.data();
+		std::memcpy(d.data().data(), params + off, d.size() * sizeof(float));
+		off += d.size();
+	}
+	for (int c = 0; c < calls; c++) {
+		for (auto& q : named) q.second.grad() = Tensor(q.second.data().shape(), 0.0f);
+		Value X = leaf({N, T, D}, x);
+		Value Y = mha.forward(X);
+		backward_through(Y, g);
+		if (c + 1 == calls) {
+			copy_out(Y.data(), y);
+			copy_out(X.grad(), dx);
+			size_t o = 0;
+			for (auto& q : named) {
+				copy_out(q.second.grad(), dparams + o);
+				o += q.second.data().size();
+			}
+		}
+	}
+}
+
 void ref_gelu(size_t n, const float* x, const float* g, float* y, float* dx) {
 	Value X = leaf({n}, x);
 	Value Y = nn::gelu(X);
@@ -411,10 +475,24 @@ void ref_adamw(size_t n, float* w, const float* g, float lr, float b1, float b2,
  * step's gradients (flat), params_out the parameters after the last step. Returns the number of
  * parameter floats, or -1 if the sizes do not match.
  */
+long long ref_transformer_train_ex(uint64_t seed, float dropout, size_t vocab, size_t dim, size_t heads, size_t layers,
+		size_t max_len, size_t N, size_t T, const float* params_in, const int64_t* ids, const int64_t* targets, float lr,
+		float wd, int steps, float* losses, float* grads, float* params_out);
+
 long long ref_transformer_train(size_t vocab, size_t dim, size_t heads, size_t layers, size_t max_len, size_t N,
 		size_t T, const float* params_in, const int64_t* ids, const int64_t* targets, float lr, float wd, int steps,
 		float* losses, float* grads, float* params_out) {
+	return ref_transformer_train_ex(0, 0.0f, vocab, dim, heads, layers, max_len, N, T, params_in, ids, targets, lr, wd,
+		steps, losses, grads, params_out);
+}
+
+// The same with manual_seed(seed) before the model is built and dropout in its config.
+long long ref_transformer_train_ex(uint64_t seed, float dropout, size_t vocab, size_t dim, size_t heads, size_t layers,
+		size_t max_len, size_t N, size_t T, const float* params_in, const int64_t* ids, const int64_t* targets, float lr,
+		float wd, int steps, float* losses, float* grads, float* params_out) {
+	nn::manual_seed(seed);
 	nn::TransformerConfig c{vocab, dim, heads, layers, max_len};
+	c.dropout = dropout;
 	nn::Transformer model(c);
 	std::vector<std::pair<std::string, Value>> named = model.named_parameters();
 	size_t off = 0;

@@ -1,0 +1,170 @@
+"""Dropout and attention with dropout on the GPU, against the reference build (oracle/_ref).
+
+- The device generator's masks are the reference Dropout layer's masks bit for bit, call after call
+  (sizes straddling the 624-word blocks), for several p, after other layers took earlier streams;
+  the backward multiplies by the same mask; p 0 / 1 and evaluation mode.
+- A large draw (3M elements) against the oracle's draws from the same state.
+- MultiHeadAttention with dropout active (the composed path: head GEMMs around the masked softmax
+  and the dropped weights), two forward + backward calls, against the reference's module: outputs
+  and gradients to the fp32 bound of the other attention tests (the masks are identical, the
+  products are tensor-core 3xTF32).
+- A Transformer with dropout trained for three steps against the reference's.
+"""
+import numpy as np
+import pytest
+
+from oracle import orc
+
+pytestmark = pytest.mark.gpu
+SIZES = [1, 31, 32, 593, 624, 625, 1248, 1000, 64, 5000, 3, 40000]
+
+
+def ref():
+    r = orc.ref()
+    if r is None:
+        pytest.skip("reference library not built (oracle/_ref)")
+    return r
+
+
+def _close(got, want, rel):
+    got, want = np.asarray(got, np.float64), np.asarray(want, np.float64)
+    scale = np.abs(want).max()
+    err = np.abs(got - want).max()
+    assert err <= rel * scale, f"max err {err:.3e} vs scale {scale:.3e}"
+
+
+@pytest.mark.parametrize("p", [0.1, 0.5, 0.95, 1.0, 0.0])
+@pytest.mark.parametrize("skip", [0, 3])
+def test_dropout_layer_masks_bitwise(cuda, p, skip):
+    torch = cuda
+    import nnb.random as nr
+    from nnb.autograd import Value
+    from nnb.nn import Dropout
+    R = ref()
+    sizes = np.array(SIZES, np.uintp)
+    want = np.zeros(int(sizes.sum()), np.float32)
+    R.ref_dropout_masks(5, skip, p, sizes.ctypes.data, len(sizes), want.ctypes.data)
+    nr.manual_seed(5)
+    for _ in range(skip):
+        Dropout(p)
+    d = Dropout(p)
+    off = 0
+    for n in SIZES:
+        x = Value.leaf(torch.ones(n, device="cuda"), True)
+        y = d(x)
+        m = want[off: off + n]
+        assert y.data.cpu().numpy().tobytes() == m.tobytes(), f"mask of the call of size {n}"
+        if p > 0:                                  # p == 0 returns the input itself, as the reference
+            g = torch.arange(n, dtype=torch.float32, device="cuda") - 7.5
+            y.backward(g)
+            assert x.grad.cpu().numpy().tobytes() == (g.cpu().numpy() * m + np.float32(0)).tobytes()
+        off += n
+
+
+def test_dropout_large_draw_matches_oracle(cuda):
+    torch = cuda
+    import nnb.functional as F
+    import nnb.random as nr
+    nr.manual_seed(77)
+    host = nr.derive_generator("dropout")
+    state = torch.from_numpy(host.view(np.int32)).cuda()
+    n, p = 3_000_017, 0.3
+    mine = []
+    for size in (n, 1000):                         # the second call continues the stream
+        keep = F.dropout_mask(state, size, p).cpu().numpy().view(np.uint32)
+        bits = ((keep[:, None] >> np.arange(32, dtype=np.uint32)) & 1).reshape(-1)[:size]
+        mine.append(bits)
+    s = host
+    for size, bits in zip((n, 1000), mine):
+        m, s = orc.dropout_draws(s, size, p)
+        assert (bits == (m != 0)).all()
+    assert state.cpu().numpy().view(np.uint32).tobytes() == s.tobytes()      # the device state advanced alike
+
+
+def test_dropout_eval_mode_is_identity(cuda):
+    torch = cuda
+    from nnb.autograd import Value
+    from nnb.nn import Dropout
+    d = Dropout(0.5).eval()
+    x = Value.leaf(torch.randn(100, device="cuda"), True)
+    assert d(x) is x
+
+
+def _mha_params(D, seed):
+    ws = []
+    for i in range(4):
+        ws.append(orc.uniform(seed + 2 * i, D * D, -0.3, 0.3))
+        ws.append(orc.uniform(seed + 2 * i + 1, D, -0.1, 0.1))
+    return ws
+
+
+@pytest.mark.parametrize("D,heads,causal,p", [(32, 4, 1, 0.2), (64, 1, 0, 0.5), (48, 3, 1, 1.0)])
+def test_mha_with_dropout_matches_reference(cuda, D, heads, causal, p):
+    torch = cuda
+    import nnb.random as nr
+    from nnb.autograd import Value
+    from nnb.nn import MultiHeadAttention
+    R = ref()
+    N, T, calls = 2, 19, 2
+    params = _mha_params(D, 300)
+    flat = np.concatenate(params)
+    x, g = orc.normal(310, N * T * D), orc.normal(311, N * T * D)
+    y_r, dx_r, dp_r = orc.zeros(N * T * D), orc.zeros(N * T * D), np.zeros_like(flat)
+    R.ref_mha_dropout(21, N, T, D, heads, causal, p, calls, orc.ptr(flat), orc.ptr(x), orc.ptr(g), orc.ptr(y_r),
+                      orc.ptr(dx_r), orc.ptr(dp_r))
+    nr.manual_seed(21)
+    mha = MultiHeadAttention(D, heads, bool(causal), np.random.default_rng(0), torch.device("cuda"), dropout=p)
+    for (name, prm), w in zip(mha.named_parameters(), params):
+        prm.data.copy_(torch.from_numpy(w.reshape(prm.data.shape)))
+    for _ in range(calls):
+        for prm in mha.parameters():
+            prm.zero_grad()
+        X = Value.leaf(torch.from_numpy(x.reshape(N, T, D)).cuda(), True)
+        Y = mha(X)
+        Y.backward(torch.from_numpy(g.reshape(N, T, D)).cuda())
+    _close(Y.data.cpu().numpy().ravel(), y_r, 2e-5)
+    _close(X.grad.cpu().numpy().ravel(), dx_r, 2e-5)
+    got = np.concatenate([prm.grad.cpu().numpy().ravel() for prm in mha.parameters()]).astype(np.float64)
+    # per parameter against its own scale; k.bias's gradient is zero in exact arithmetic (softmax
+    # backward rows sum to zero), so both programs hold rounding noise there: bounded by the
+    # gradients' overall scale instead
+    floor = 2e-2 * np.abs(dp_r).max()
+    off = 0
+    for w in params:
+        seg_g, seg_r = got[off: off + w.size], dp_r[off: off + w.size].astype(np.float64)
+        assert np.abs(seg_g - seg_r).max() <= 5e-5 * max(np.abs(seg_r).max(), floor)
+        off += w.size
+
+
+def test_transformer_with_dropout_trains_like_reference(cuda):
+    torch = cuda
+    import nnb.random as nr
+    from nnb.nn import AdamW, Transformer, TransformerConfig
+    from nnb.train import ShardedTrainer
+    R = ref()
+    vocab, dim, heads, layers, T, N, steps, lr, wd, p = 64, 32, 4, 2, 16, 4, 3, 1e-2, 1e-2, 0.1
+    cfg = TransformerConfig(vocab_size=vocab, dim=dim, heads=heads, layers=layers, max_len=T, dropout=p)
+    ids = orc.integers(95, N * (T + 1), 0, vocab - 1).reshape(N, T + 1)
+    x, y = ids[:, :T].copy(), ids[:, 1:].copy()
+    nr.manual_seed(33)
+    model = Transformer(cfg, seed=3)
+    init = np.concatenate([q.data.cpu().numpy().ravel() for q in model.parameters()])
+    tr = ShardedTrainer(model, AdamW(model.parameters(), lr=lr, weight_decay=wd), shards=2)
+    losses = [float(tr.step(torch.from_numpy(x).cuda(), torch.from_numpy(y).cuda()).cpu()[0]) for _ in range(steps)]
+    r_losses, r_grads, r_params = np.zeros(steps, np.float32), np.zeros_like(init), np.zeros_like(init)
+    n = R.ref_transformer_train_ex(33, p, vocab, dim, heads, layers, T, N, T, orc.ptr(init), orc.ptr(x), orc.ptr(y),
+                                   lr, wd, steps, orc.ptr(r_losses), orc.ptr(r_grads), orc.ptr(r_params))
+    assert n == init.size
+    np.testing.assert_allclose(losses, r_losses, rtol=1e-5)
+    got = np.concatenate([q.data.cpu().numpy().ravel() for q in model.parameters()]).astype(np.float64)
+    err = np.abs(got - r_params)
+    assert err.max() <= 2 * lr * steps
+    assert (err <= 1e-5 * np.abs(r_params).max()).mean() > 0.995
+
+
+def test_sharded_trainer_rejects_dropout_on_several_ranks(cuda):
+    from nnb.nn import AdamW, Transformer, TransformerConfig
+    from nnb.train import ShardedTrainer
+    model = Transformer(TransformerConfig(vocab_size=16, dim=16, heads=2, layers=1, max_len=8, dropout=0.1))
+    with pytest.raises(NotImplementedError):
+        ShardedTrainer(model, AdamW(model.parameters()), shards=8, world=2, rank=0)
