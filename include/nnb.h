@@ -372,6 +372,31 @@ NNB_API nnb_status nnb_dropout_apply(void* stream, size_t n, float p, const floa
 NNB_API nnb_status nnb_dropout_bwd(void* stream, size_t n, float p, const float* g, const uint32_t* keep, float* dx,
 		int dx_first);
 
+/* Host-side draws of the reference's data pipeline (all host only, no device work):
+ * std::mt19937(seed) linear seeding (random_split, src/data/subset.cpp:63) in the 625-word form;
+ * n raw outputs of a host state; the FNV-1a / splitmix64 functions of derive_generator
+ * (random.hpp detail::); the portable Fisher-Yates shuffle (src/data/shuffle.hpp:45-49, rejection
+ * draws from raw outputs); the weighted draws of a weighted DataLoader epoch
+ * (dataloader.cpp:58-69: 53-bit uniform from two outputs, first running sum above u * total). */
+NNB_API nnb_status nnb_mt19937_seed(uint32_t seed, uint32_t* state);
+NNB_API nnb_status nnb_mt19937_next(uint32_t* state, size_t n, uint32_t* out);
+NNB_API uint64_t nnb_fnv1a64(const char* s);
+NNB_API uint64_t nnb_splitmix64(uint64_t x);
+NNB_API nnb_status nnb_portable_shuffle(uint32_t* state, uint64_t* v, size_t n);
+NNB_API nnb_status nnb_weighted_draws(uint32_t* state, const double* cumulative, size_t count, size_t num_samples,
+		uint64_t* out);
+
+/* ---- batch assembly from HBM-resident datasets (DataLoader::get_batch, dataloader.cpp:76-96) --- */
+
+/* dst[r] = src[index[r]] for r < count, rows of row_bytes bytes (TensorDataset rows). An index
+ * outside [0, rows) writes a zero row and sets the device error word. */
+NNB_API nnb_status nnb_gather_rows(void* stream, const void* src, size_t row_bytes, size_t rows, const int64_t* index,
+		size_t count, void* dst);
+/* SequenceDataset windows (src/data/text.cpp:60-70): x[b][t] = tokens[start[b] + t],
+ * y[b][t] = tokens[start[b] + 1 + t], t < block, as int64 ids; start[b] < n_tokens - block. */
+NNB_API nnb_status nnb_gather_windows(void* stream, const int32_t* tokens, size_t n_tokens, const int64_t* start,
+		size_t count, size_t block, int64_t* x, int64_t* y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -25,6 +25,7 @@
 #include <mutex>
 #include <random>
 #include <string>
+#include <utility>
 
 #include "nnb_internal.h"
 #include "nnb_trace.h"
@@ -100,6 +101,34 @@ struct Registry {
 Registry& registry() {
 	static Registry r;
 	return r;
+}
+
+// ---- host: mt19937 draws, the portable shuffle and weighted draws (src/data/shuffle.hpp,
+// src/data/dataloader.cpp:58-73) -------------------------------------------------------------------
+
+uint32_t host_mix(uint32_t upper_of, uint32_t lower_of) {
+	const uint32_t y = (upper_of & 0x80000000u) | (lower_of & 0x7fffffffu);
+	return (y >> 1) ^ ((y & 1u) ? kMtMatrix : 0u);
+}
+
+uint32_t host_next(uint32_t* st) {
+	if (st[kMtN] >= (uint32_t)kMtN) {
+		for (int i = 0; i < kMtN; i++) st[i] = st[(i + kMtShift) % kMtN] ^ host_mix(st[i], st[(i + 1) % kMtN]);
+		st[kMtN] = 0;
+	}
+	uint32_t y = st[st[kMtN]++];
+	y ^= y >> 11;
+	y ^= (y << 7) & 0x9d2c5680u;
+	y ^= (y << 15) & 0xefc60000u;
+	return y ^ (y >> 18);
+}
+
+// uniform in [0, bound) by rejecting the incomplete top bucket of 2^32 (shuffle.hpp:25-33)
+uint32_t bounded(uint32_t* st, uint32_t bound) {
+	const uint64_t limit = (uint64_t{1} << 32) - ((uint64_t{1} << 32) % bound);
+	uint32_t r = host_next(st);
+	while (r >= limit) r = host_next(st);
+	return r % bound;
 }
 
 // ---- device: mt19937 blocks and the keep mask ----------------------------------------------------
@@ -271,6 +300,52 @@ nnb_status nnb_derive_generator(const char* stream_name, uint32_t* state) {
 nnb_status nnb_mt19937_seed_seq(const uint32_t* seeds, size_t count, uint32_t* state) {
 	if ((count && !seeds) || !state) return nnb::fail(NNB_ERR_INVALID, "mt19937_seed_seq: null pointer");
 	nnb::mt_seed_from_seq(seeds, count, state);
+	return NNB_OK;
+}
+
+nnb_status nnb_mt19937_seed(uint32_t seed, uint32_t* state) {
+	if (!state) return nnb::fail(NNB_ERR_INVALID, "mt19937_seed: null pointer");
+	state[0] = seed;          // the published linear initialisation (init_genrand; [rand.eng.mers])
+	for (int i = 1; i < nnb::kMtN; i++) state[i] = 1812433253u * (state[i - 1] ^ (state[i - 1] >> 30)) + (uint32_t)i;
+	state[nnb::kMtN] = nnb::kMtN;
+	return NNB_OK;
+}
+
+nnb_status nnb_mt19937_next(uint32_t* state, size_t n, uint32_t* out) {
+	if (!state || (n && !out)) return nnb::fail(NNB_ERR_INVALID, "mt19937_next: null pointer");
+	for (size_t i = 0; i < n; i++) out[i] = nnb::host_next(state);
+	return NNB_OK;
+}
+
+uint64_t nnb_fnv1a64(const char* s) { return s ? nnb::fnv1a64(s) : 0; }
+
+uint64_t nnb_splitmix64(uint64_t x) { return nnb::splitmix64(x); }
+
+nnb_status nnb_portable_shuffle(uint32_t* state, uint64_t* v, size_t n) {
+	if (!state || (n && !v)) return nnb::fail(NNB_ERR_INVALID, "portable_shuffle: null pointer");
+	if (n > 0xFFFFFFFFull) return nnb::fail(NNB_ERR_INVALID, "portable_shuffle: more than 2^32 elements");
+	for (size_t i = n; i > 1; i--) std::swap(v[i - 1], v[nnb::bounded(state, (uint32_t)i)]);
+	return NNB_OK;
+}
+
+nnb_status nnb_weighted_draws(uint32_t* state, const double* cumulative, size_t count, size_t num_samples,
+		uint64_t* out) {
+	if (!state || !cumulative || count == 0 || (num_samples && !out))
+		return nnb::fail(NNB_ERR_INVALID, "weighted_draws: null pointer or no weights");
+	const double total = cumulative[count - 1];
+	for (size_t s = 0; s < num_samples; s++) {
+		// 53 random bits from two outputs: a uniform double in [0, 1), then the first running sum above it
+		const uint64_t a = nnb::host_next(state) >> 5, b = nnb::host_next(state) >> 6;
+		const double u = (static_cast<double>(a) * 67108864.0 + static_cast<double>(b)) / 9007199254740992.0;
+		const double target = u * total;
+		size_t lo = 0, hi = count;
+		while (lo < hi) {
+			const size_t mid = lo + (hi - lo) / 2;
+			if (cumulative[mid] > target) hi = mid;
+			else lo = mid + 1;
+		}
+		out[s] = lo < count ? lo : count - 1;
+	}
 	return NNB_OK;
 }
 

@@ -31,6 +31,10 @@ class TensorShapeError(ValueError):
     """Shapes of the operands do not agree (the reference's nn::TensorShapeError)."""
 
 
+class TensorIndexError(IndexError):
+    """An index outside a tensor or dataset (the reference's nn::TensorIndexError)."""
+
+
 _lib = None
 
 _c = ctypes
@@ -115,6 +119,14 @@ _SIGS = {
     "nnb_dropout_mask": ([_p, _p, _sz, _f, _p], _i),
     "nnb_dropout_apply": ([_p, _sz, _f, _p, _p, _p], _i),
     "nnb_dropout_bwd": ([_p, _sz, _f, _p, _p, _p, _i], _i),
+    "nnb_mt19937_seed": ([_c.c_uint32, _p], _i),
+    "nnb_mt19937_next": ([_p, _sz, _p], _i),
+    "nnb_fnv1a64": ([_c.c_char_p], _c.c_uint64),
+    "nnb_splitmix64": ([_c.c_uint64], _c.c_uint64),
+    "nnb_portable_shuffle": ([_p, _p, _sz], _i),
+    "nnb_weighted_draws": ([_p, _p, _sz, _sz, _p], _i),
+    "nnb_gather_rows": ([_p, _p, _sz, _sz, _p, _sz, _p], _i),
+    "nnb_gather_windows": ([_p, _p, _sz, _p, _sz, _sz, _p, _p], _i),
 }
 
 

@@ -88,6 +88,10 @@ _REF_SIGS = {
     "ref_reduce4": ([_sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _p], None),
     "ref_global_avgpool": ([_sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
     "ref_bn2d_module": ([_sz, _sz, _sz, _sz, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], None),
+    "ref_loader_orders": ([_c.c_uint64, _i, _sz, _sz, _i, _i, _i, _p], _sz),
+    "ref_loader_weighted": ([_c.c_uint64, _p, _sz, _sz, _sz, _i, _i, _p], _c.c_longlong),
+    "ref_random_split": ([_sz, _p, _i, _c.c_uint64, _p, _p], _i),
+    "ref_balanced_weights": ([_p, _sz, _sz, _p], _i),
     "ref_mt19937_outputs": ([_p, _sz, _sz, _p], None),
     "ref_derive_outputs": ([_c.c_uint64, _c.c_char_p, _i, _sz, _p], None),
     "ref_dropout_masks": ([_c.c_uint64, _i, _f, _p, _i, _p], None),

@@ -10,6 +10,9 @@
  */
 #include "nn/autograd/ops.hpp"
 #include "nn/checkpoint.hpp"
+#include "nn/data/dataloader.hpp"
+#include "nn/data/subset.hpp"
+#include "nn/data/tensor_dataset.hpp"
 #include "nn/nn/attention.hpp"
 #include "nn/nn/dropout.hpp"
 #include "nn/random.hpp"
@@ -348,6 +351,84 @@ int64_t ref_linear_checkpoint_load(const char* path, float* w, float* b) {
 		return step;
 	} catch (...) {
 		return -1;
+	}
+}
+
+// TensorDataset of n samples whose input and target rows are [i] (so a batch shows its indices).
+nn::TensorDataset index_dataset(size_t n) {
+	std::vector<float> v(n);
+	for (size_t i = 0; i < n; i++) v[i] = static_cast<float>(i);
+	return nn::TensorDataset(Tensor({n, 1}, v), Tensor({n, 1}, v));
+}
+
+// manual_seed(seed), `skip` loaders built first, then DataLoader(index dataset of n, batch, shuffle,
+// drop_last); for `epochs` epochs (reset_epoch before each but the first) every batch's inputs in
+// order go to out. Returns the number written.
+size_t ref_loader_orders(uint64_t seed, int skip, size_t n, size_t batch, int shuffle, int drop_last, int epochs,
+		float* out) {
+	nn::TensorDataset ds = index_dataset(n);
+	nn::manual_seed(seed);
+	for (int i = 0; i < skip; i++) nn::DataLoader unused(ds, batch, shuffle != 0);
+	nn::DataLoader loader(ds, batch, shuffle != 0, drop_last != 0);
+	size_t o = 0;
+	for (int e = 0; e < epochs; e++) {
+		if (e) loader.reset_epoch();
+		for (size_t b = 0; b < loader.num_batches(); b++) {
+			auto batch_xy = loader.get_batch(b);
+			for (float v : batch_xy.first.data().data()) out[o++] = v;
+		}
+	}
+	return o;
+}
+
+// The weighted form: DataLoader(index dataset of n, batch, weights, num_samples, drop_last); the
+// targets of every batch of `epochs` epochs. Returns the number written, or -1 when it threw.
+long long ref_loader_weighted(uint64_t seed, const double* w, size_t n, size_t batch, size_t num_samples,
+		int drop_last, int epochs, float* out) {
+	try {
+		nn::TensorDataset ds = index_dataset(n);
+		nn::manual_seed(seed);
+		std::vector<double> weights(w, w + n);
+		nn::DataLoader loader(ds, batch, weights, num_samples, drop_last != 0);
+		long long o = 0;
+		for (int e = 0; e < epochs; e++) {
+			if (e) loader.reset_epoch();
+			for (size_t b = 0; b < loader.num_batches(); b++) {
+				auto batch_xy = loader.get_batch(b);
+				for (float v : batch_xy.second.data()) out[o++] = v;
+			}
+		}
+		return o;
+	} catch (...) {
+		return -1;
+	}
+}
+
+// random_split(index dataset of n, fractions[0..k), seed): sizes[j] and the subsets' indices in
+// order to out. Returns 0, or 1 when it threw.
+int ref_random_split(size_t n, const double* fractions, int k, uint64_t seed, size_t* sizes, float* out) {
+	try {
+		nn::TensorDataset ds = index_dataset(n);
+		auto parts = nn::random_split(ds, std::vector<double>(fractions, fractions + k), seed);
+		size_t o = 0;
+		for (size_t j = 0; j < parts.size(); j++) {
+			sizes[j] = parts[j].size();
+			for (size_t i = 0; i < parts[j].size(); i++) out[o++] = parts[j].get(i).first.data()[0];
+		}
+		return 0;
+	} catch (...) {
+		return 1;
+	}
+}
+
+// balanced_sample_weights(labels, classes) into out; 0, or 1 when it threw.
+int ref_balanced_weights(const size_t* labels, size_t n, size_t classes, double* out) {
+	try {
+		auto w = nn::balanced_sample_weights(std::vector<size_t>(labels, labels + n), classes);
+		std::memcpy(out, w.data(), n * sizeof(double));
+		return 0;
+	} catch (...) {
+		return 1;
 	}
 }
 
