@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--size", type=int, default=8192, help="M = N = K")
     ap.add_argument("--mode", choices=("fp32x3", "tf32"), default="fp32x3")
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--gather", choices=("peer", "nccl"), default="peer",
+                    help="N>1 GEMM: bands stored into GPU 0's C by the GEMM epilogue (peer) or an NCCL gather after it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=("all", "gemm", "transformer", "cnn", "attention"), default="all",
                     help="one config alone, or all: the config 4 line with configs 2, 3 and 5 inside")
@@ -237,7 +239,7 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
 
     import nnb
 
-    from nnb.parallel import gather_rows, row_bands
+    from nnb.parallel import PeerBuffer, gather_rows, row_bands
 
     size = args.size
     mode = nnb.MATH_FP32X3 if args.mode == "fp32x3" else nnb.MATH_TF32
@@ -251,13 +253,19 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     gen.manual_seed(2000 + rank)
     a = torch.randn(rows, size, device=dev, generator=gen)
     c = torch.empty(rows, size, device=dev)
+    peer = PeerBuffer((size, size), owner=0) if world > 1 and args.gather == "peer" else None
+    c_out = c if peer is None else peer.ptr + bands[rank][0] * size * 4
+
+    def gemm_local():
+        nnb.sgemm(False, False, rows, size, size, a, size, b, size, c, size, False, math_mode=mode)
 
     def gemm():
-        nnb.sgemm(False, False, rows, size, size, a, size, b, size, c, size, False, math_mode=mode)
+        # with a peer buffer the epilogue stores this rank's tiles straight into GPU 0's C over NVLink
+        nnb.sgemm(False, False, rows, size, size, a, size, b, size, c_out, size, False, math_mode=mode)
 
     def step():
         gemm()
-        if world > 1:
+        if world > 1 and peer is None:
             gather_rows(c, bands, dst=0)
 
     def barrier():
@@ -307,6 +315,21 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     if world > 1:
         dist.all_reduce(comp, op=dist.ReduceOp.MAX)
 
+    # the collective baseline at N > 1: the GEMM into a local band, then an NCCL gather to GPU 0
+    nccl_gather = None
+    if world > 1:
+        barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(min(args.steps, 50)):
+            gemm_local()
+            gather_rows(c, bands, dst=0)
+        e1.record()
+        torch.cuda.synchronize()
+        ng = torch.tensor([e0.elapsed_time(e1) / min(args.steps, 50)], device=dev, dtype=torch.float64)
+        dist.all_reduce(ng, op=dist.ReduceOp.MAX)
+        nccl_gather = ng.item()
+
     # end to end through the public API from pinned host memory
     a_h = a.cpu().pin_memory()
     b_h = b.cpu().pin_memory()
@@ -318,13 +341,15 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     for _ in range(e2e_steps):
         a.copy_(a_h, non_blocking=True)
         b.copy_(b_h, non_blocking=True)
-        gemm()
+        gemm_local()
         c_h.copy_(c, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     e2e = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    if peer is not None:
+        peer.close()              # unmapped on every rank before GPU 0 may free its C
 
     # cuBLAS TF32 on the same operands: a measured TF32 tensor-core reference point (rank 0, N = 1)
     cublas_tf32 = None
@@ -382,6 +407,12 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
                      "cublas_tf32_tflops": cublas_tf32},
         "pack_ms_per_step": pack_ms_max,
         "ms_per_step_compute_only": comp.item(),
+        "gather": None if world == 1 else (
+            "fused: each rank's GEMM epilogue stores its tiles into GPU 0's C through CUDA IPC peer memory"
+            if peer is not None else "NCCL gather after the GEMM"),
+        "gather_baseline": None if nccl_gather is None else {
+            "what": "GEMM into a local band, then an NCCL gather to GPU 0", "ms_per_step": nccl_gather,
+            "value": flops / (nccl_gather * 1e-3) / 1e12, "unit": UNIT},
         "e2e": {"value": flops / (e2e.item() * 1e-3) / 1e12, "unit": UNIT,
                 "h2d_bytes_per_step": int((rows * size + size * size) * 4 * world),
                 "d2h_bytes_per_step": int(rows * size * 4 * world)},

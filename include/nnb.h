@@ -56,6 +56,15 @@ NNB_API int nnb_get_math_mode(void);
  * (0 = no kernel reported a timed-out wait). */
 NNB_API int nnb_device_error(void* stream);
 
+/* Peer memory between the processes of one node (one process per GPU): export a device pointer
+ * as a CUDA IPC handle (64 bytes) plus its offset inside its allocation; open another process's
+ * handle as a pointer this GPU can load from and store to over NVLink; close it again (before the
+ * owner frees the memory). Used by the sharded GEMM, whose epilogue stores each rank's tiles of C
+ * straight into the gathering GPU's C. */
+NNB_API nnb_status nnb_ipc_export(const void* ptr, unsigned char* handle, size_t* offset);
+NNB_API nnb_status nnb_ipc_open(const unsigned char* handle, size_t offset, void** ptr);
+NNB_API nnb_status nnb_ipc_close(void* ptr, size_t offset);
+
 /* ---- tracing (the counterpart of the reference bench's per-op timing, apps/bench/runner.cpp:29-96) */
 
 /* Kernel kinds for nnb_trace_query. */

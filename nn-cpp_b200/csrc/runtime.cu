@@ -25,6 +25,9 @@ std::mutex g_device_mutex;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
 
+PFN_cuMemGetAddressRange_v3020 g_range = nullptr;
+std::once_flag g_range_once;
+
 }  // namespace
 
 nnb_status fail(nnb_status st, const char* fmt, ...) {
@@ -137,6 +140,43 @@ nnb_status nnb_set_math_mode(int mode) {
 }
 
 int nnb_get_math_mode(void) { return nnb::math_mode(); }
+
+nnb_status nnb_ipc_export(const void* ptr, unsigned char* handle, size_t* offset) {
+	if (!ptr || !handle || !offset) return nnb::fail(NNB_ERR_INVALID, "ipc_export: null pointer");
+	std::call_once(nnb::g_range_once, [] {
+		void* fn = nullptr;
+		cudaDriverEntryPointQueryResult q;
+		if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) == cudaSuccess
+				&& q == cudaDriverEntryPointSuccess)
+			nnb::g_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+	});
+	if (!nnb::g_range) return nnb::fail(NNB_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+	CUdeviceptr base = 0;
+	size_t size = 0;
+	if (nnb::g_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS)
+		return nnb::fail(NNB_ERR_INVALID, "ipc_export: not a device allocation");
+	cudaIpcMemHandle_t h;
+	NNB_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+	std::memcpy(handle, &h, sizeof h);
+	*offset = static_cast<size_t>(reinterpret_cast<CUdeviceptr>(ptr) - base);
+	return NNB_OK;
+}
+
+nnb_status nnb_ipc_open(const unsigned char* handle, size_t offset, void** ptr) {
+	if (!handle || !ptr) return nnb::fail(NNB_ERR_INVALID, "ipc_open: null pointer");
+	cudaIpcMemHandle_t h;
+	std::memcpy(&h, handle, sizeof h);
+	void* base = nullptr;
+	NNB_CUDA_TRY(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+	*ptr = static_cast<char*>(base) + offset;
+	return NNB_OK;
+}
+
+nnb_status nnb_ipc_close(void* ptr, size_t offset) {
+	if (!ptr) return NNB_OK;
+	NNB_CUDA_TRY(cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset));
+	return NNB_OK;
+}
 
 int nnb_device_error(void* stream) {
 	nnb::DeviceState* st = nullptr;

@@ -5,8 +5,12 @@ not depend on the thread count (tests/test_kernels.cpp:343-380). The B200 build 
 guarantee across GPU counts: a large GEMM is split into contiguous bands of whole 128-row tiles of
 C (and A); every rank holds all of B and computes its band with the same tile sequence and k order
 as the single-GPU kernel, so the bands are bitwise the rows the single-GPU product would hold.
-Bands are gathered to one rank with a collective of the process group (NCCL over NVLink on GPUs,
-gloo on CPU in the tests).
+Bands reach the gathering rank in one of two ways:
+- fused: the gathering rank's full C is exported as CUDA IPC memory (PeerBuffer) and every rank runs
+  its GEMM with C pointing into it, so the kernel's epilogue stores each finished tile straight into
+  that GPU's memory over NVLink while the next tiles are computed -- the transfer overlaps the math
+  tile by tile and no collective moves data;
+- collective: gather_rows, an NCCL gather after the GEMM (gloo on CPU in the tests).
 """
 from __future__ import annotations
 
@@ -53,3 +57,55 @@ def gather_rows(band, bands, dst: int = 0, group=None):
     if rank != dst:
         return None
     return torch.cat([recv[r][: stop - start] for r, (start, stop) in enumerate(bands)], dim=0)
+
+
+class PeerBuffer:
+    """A float32 buffer of `shape` on rank `owner` that every rank of the group can store into.
+
+    The owner allocates it (``tensor``) and exports a CUDA IPC handle (nnb_ipc_export); the handle is
+    broadcast over the process group and the other ranks map it (nnb_ipc_open). ``ptr`` is the
+    buffer's address on this rank: the owner's own pointer, or the mapped peer pointer. ``close()``
+    unmaps on every rank and then synchronises the group, after which the owner may free the tensor.
+    """
+
+    def __init__(self, shape, owner: int = 0, group=None, device=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import check, lib
+
+        self.group, self.owner = group, owner
+        self.rank = dist.get_rank(group)
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        self.tensor = torch.empty(tuple(shape), dtype=torch.float32, device=device) if self.rank == owner else None
+        msg = torch.zeros(72, dtype=torch.uint8, device=device)
+        if self.rank == owner:
+            handle = (ctypes.c_ubyte * 64)()
+            offset = ctypes.c_size_t()
+            check(lib().nnb_ipc_export(self.tensor.data_ptr(), handle, ctypes.byref(offset)))
+            msg[:64] = torch.tensor(list(handle), dtype=torch.uint8)
+            msg[64:] = torch.tensor(list(offset.value.to_bytes(8, "little")), dtype=torch.uint8)
+        dist.broadcast(msg, src=owner, group=group)
+        raw = bytes(msg.cpu().tolist())
+        self.offset = int.from_bytes(raw[64:], "little")
+        if self.rank == owner:
+            self.ptr, self._mapped = self.tensor.data_ptr(), False
+        else:
+            handle = (ctypes.c_ubyte * 64).from_buffer_copy(raw[:64])
+            out = ctypes.c_void_p()
+            check(lib().nnb_ipc_open(handle, self.offset, ctypes.byref(out)))
+            self.ptr, self._mapped = out.value, True
+
+    def close(self) -> None:
+        import torch
+        import torch.distributed as dist
+
+        from . import check, lib
+
+        torch.cuda.synchronize()
+        if self._mapped:
+            check(lib().nnb_ipc_close(self.ptr, self.offset))
+            self._mapped = False
+        dist.barrier(group=self.group, device_ids=[torch.cuda.current_device()])

@@ -77,45 +77,63 @@ def test_gather_rows_gloo_world2(tmp_path):
     assert got.tobytes() == want.tobytes()
 
 
-def _nccl_worker(rank, world, port, m, n, k, mode, out_dir):
+def _nccl_worker(rank, world, port, m, n, k, mode, gather, out_dir):
+    import datetime
+
     import torch
     import torch.distributed as dist
 
     import nnb
-    from nnb.parallel import gather_rows, row_bands
+    from nnb.parallel import PeerBuffer, gather_rows, row_bands
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
     try:
         g = torch.Generator(device="cuda").manual_seed(5)
         a = torch.randn(m, k, device="cuda", generator=g)
         b = torch.randn(k, n, device="cuda", generator=g)
         bands = row_bands(m, world)
         s, e = bands[rank]
-        band = torch.empty(e - s, n, device="cuda")
-        nnb.sgemm(False, False, e - s, n, k, a[s:e], k, b, n, band, n, False, math_mode=mode)
-        full = gather_rows(band, bands)
+        if gather == "peer":
+            # the GEMM's epilogue stores this rank's tiles straight into rank 0's C over NVLink
+            peer = PeerBuffer((m, n), owner=0)
+            if e > s:
+                nnb.sgemm(False, False, e - s, n, k, a[s:e], k, b, n, peer.ptr + s * n * 4, n, False, math_mode=mode)
+            torch.cuda.synchronize()
+            dist.barrier(device_ids=[rank])
+            full = peer.tensor
+        else:
+            band = torch.empty(e - s, n, device="cuda")
+            nnb.sgemm(False, False, e - s, n, k, a[s:e], k, b, n, band, n, False, math_mode=mode)
+            full = gather_rows(band, bands)
         if rank == 0:
             single = torch.empty(m, n, device="cuda")
             nnb.sgemm(False, False, m, n, k, a, k, b, n, single, n, False, math_mode=mode)
-            np.save(os.path.join(out_dir, f"eq_{mode}.npy"), np.array([bool(torch.equal(full, single))]))
+            np.save(os.path.join(out_dir, f"eq_{mode}_{gather}.npy"), np.array([bool(torch.equal(full, single))]))
         dist.barrier(device_ids=[rank])
+        if gather == "peer":
+            peer.close()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("gather", ["nccl", "peer"])
 @pytest.mark.parametrize("mode", [0, 1])
-def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode):
+def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode, gather):
+    """Bands computed on 2-4 GPUs and gathered on GPU 0 (by an NCCL gather after the GEMM, or by the
+    GEMM's own epilogue storing into GPU 0's C through peer memory) equal the one-GPU product bit for
+    bit."""
     torch = cuda
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs two or more GPUs")
     m, n, k = 1000, 700, 900
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), m, n, k, mode, str(tmp_path)), nprocs=world,
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), m, n, k, mode, gather, str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")
-    assert bool(np.load(tmp_path / f"eq_{mode}.npy")[0])
+    assert bool(np.load(tmp_path / f"eq_{mode}_{gather}.npy")[0])
 
 
 def _dp_worker(rank, world, port, out_dir):
