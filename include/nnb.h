@@ -333,6 +333,18 @@ NNB_API nnb_status nnb_embedding_bwd_grouped(void* stream, size_t V, size_t D, s
  * step counts from 1 (the value of Adam::t_ after its increment). */
 NNB_API nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float* g, float* m, float* v, float lr,
 		float beta1, float beta2, float eps, float weight_decay, long long step);
+/* Adam's bias corrections (adam.cpp:25-27) for t = 1..len as out[2(t-1)] = 1 - beta1^t and
+ * out[2(t-1)+1] = 1 - beta2^t, computed on the host exactly as the reference computes them; the
+ * table ends at the first t where both are exactly 1.0f (every later t has the same values) or at
+ * max_len (at most 2^24). Returns len. Host only. */
+NNB_API size_t nnb_adam_bias_table(float beta1, float beta2, float* out, size_t max_len);
+/* *step += 1 on the device (a step counter that CUDA-graph replays advance). */
+NNB_API nnb_status nnb_step_advance(void* stream, int64_t* step);
+/* nnb_adamw_step with its scalars in device memory, for CUDA-graph replay: hyper = {1 - lr * wd, lr,
+ * beta1, beta2, eps}, the corrections table[min(*step, table_len) - 1] from nnb_adam_bias_table.
+ * Same arithmetic, same bits. */
+NNB_API nnb_status nnb_adamw_step_device(void* stream, size_t n, float* w, const float* g, float* m, float* v,
+		const float* hyper, const float* bias_table, size_t table_len, const int64_t* step);
 
 /*
  * nnb_sgemm_ex for callers that cannot allocate device memory. This entry point has no

@@ -527,6 +527,33 @@ __global__ void adamw_kernel(long long n, float* __restrict__ w, const float* __
 	}
 }
 
+// The same update with its per-step scalars in device memory, so a captured CUDA graph replays it:
+// hyper = {shrink, lr, beta1, beta2, eps}; (c1, c2) = table[min(t, len) - 1] for t = *step (the
+// corrections saturate at exactly 1.0f, where the table ends).
+__global__ void adamw_device_kernel(long long n, float* __restrict__ w, const float* __restrict__ g,
+		float* __restrict__ m, float* __restrict__ v, const float* __restrict__ hyper,
+		const float* __restrict__ table, long long table_len, const int64_t* __restrict__ step) {
+	const float shrink = hyper[0], lr = hyper[1], b1 = hyper[2], b2 = hyper[3], eps = hyper[4];
+	long long t = *step;
+	if (t < 1) return;
+	if (t > table_len) t = table_len;
+	const float c1 = table[2 * (t - 1)], c2 = table[2 * (t - 1) + 1];
+	GRID_STRIDE(k, n) {
+		float wk = w[k] * shrink;
+		const float gk = g[k];
+		const float mk = b1 * m[k] + (1.0f - b1) * gk;
+		const float vk = b2 * v[k] + (1.0f - b2) * gk * gk;
+		m[k] = mk;
+		v[k] = vk;
+		wk -= lr * (mk / c1) / (sqrtf(vk / c2) + eps);
+		w[k] = wk;
+	}
+}
+
+__global__ void step_advance_kernel(int64_t* step) {
+	if (threadIdx.x == 0 && blockIdx.x == 0) *step += 1;
+}
+
 }  // namespace
 
 }  // namespace nnb
@@ -836,6 +863,39 @@ nnb_status nnb_adamw_step(void* stream, size_t n, float* w, const float* g, floa
 	NNB_LAUNCH(kTraceRowwise, grid_for((long long)n, 256), 256, nnb::adamw_kernel, (long long)n, w, g, m, v, shrink, lr,
 		beta1, beta2, eps, c1, c2);
 	return nnb::cuda_status(cudaGetLastError(), "adamw launch");
+}
+
+size_t nnb_adam_bias_table(float beta1, float beta2, float* out, size_t max_len) {
+	if (!out || max_len == 0) return 0;
+	if (max_len > (size_t(1) << 24)) max_len = size_t(1) << 24;     // t is exact as a float up to 2^24
+	size_t len = 0;
+	for (size_t t = 1; t <= max_len; ++t) {
+		const float c1 = 1.0f - std::pow(beta1, static_cast<float>(t));
+		const float c2 = 1.0f - std::pow(beta2, static_cast<float>(t));
+		out[2 * (t - 1)] = c1;
+		out[2 * (t - 1) + 1] = c2;
+		len = t;
+		if (c1 == 1.0f && c2 == 1.0f) break;       // both saturated: every later step has these values
+	}
+	return len;
+}
+
+nnb_status nnb_step_advance(void* stream, int64_t* step) {
+	if (!step) return nnb::fail(NNB_ERR_INVALID, "step_advance: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceAux, 1, 32, nnb::step_advance_kernel, step);
+	return nnb::cuda_status(cudaGetLastError(), "step_advance launch");
+}
+
+nnb_status nnb_adamw_step_device(void* stream, size_t n, float* w, const float* g, float* m, float* v,
+		const float* hyper, const float* bias_table, size_t table_len, const int64_t* step) {
+	if (n == 0) return NNB_OK;
+	if (!w || !g || !m || !v || !hyper || !bias_table || !step || table_len == 0)
+		return nnb::fail(NNB_ERR_INVALID, "adamw_step_device: null pointer or empty table");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_LAUNCH(kTraceRowwise, grid_for((long long)n, 256), 256, nnb::adamw_device_kernel, (long long)n, w, g, m, v,
+		hyper, bias_table, (long long)table_len, step);
+	return nnb::cuda_status(cudaGetLastError(), "adamw_device launch");
 }
 
 }  // extern "C"

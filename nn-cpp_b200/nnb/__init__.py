@@ -114,6 +114,9 @@ _SIGS = {
     "nnb_embedding_fwd": ([_p, _sz, _sz, _p, _p, _sz, _p], _i),
     "nnb_embedding_bwd": ([_p, _sz, _sz, _p, _sz, _p, _p, _i], _i),
     "nnb_adamw_step": ([_p, _sz, _p, _p, _p, _p, _f, _f, _f, _f, _f, _c.c_longlong], _i),
+    "nnb_adam_bias_table": ([_f, _f, _p, _sz], _sz),
+    "nnb_step_advance": ([_p, _p], _i),
+    "nnb_adamw_step_device": ([_p, _sz, _p, _p, _p, _p, _p, _p, _sz, _p], _i),
     "nnb_manual_seed": ([_c.c_uint64], None),
     "nnb_is_seeded": ([], _i),
     "nnb_seed_epoch": ([], _c.c_uint64),

@@ -21,12 +21,16 @@ independence from the thread count (tests/test_transformer.cpp:525).
 
 The loss gradient is normalised by the global number of positions (grad_norm), so the update is
 the one of the mean loss over the global batch. The trainer takes the optimizer's settings and step
-counter and performs its update itself (AdamW's per-parameter moment buffers are not used).
+counter and performs its update itself (AdamW's per-parameter moment buffers are not used). The step
+counter, the settings and Adam's bias corrections (a table computed on the host with the reference's
+own formula) live in device memory, so a whole step -- forward, backward, the collectives and the
+update -- can be captured once into a CUDA graph and replayed (capture()): no per-launch host work.
 """
 from __future__ import annotations
 
 import ctypes
 
+import numpy as np
 import torch
 
 from . import check, lib
@@ -75,6 +79,11 @@ class ShardedTrainer:
         else:
             self.reduced = empty((self.total,), device=dev)
         self.grad_norm = None
+        # step counter, settings and bias corrections on the device (graph-replayable update)
+        self.step_dev = torch.tensor([int(optimizer.t)], dtype=torch.int64, device=dev)
+        self.hyper_dev = empty((5,), device=dev)
+        self._hyper_key, self._betas, self.table_dev, self.table_len = None, None, None, 0
+        self._refresh_hyper()
         self.local_loss = empty((1,), device=dev)
         self.all_loss = self.local_loss if world == 1 else empty((world,), device=dev)
         self.loss = empty((1,), device=dev)
@@ -95,6 +104,29 @@ class ShardedTrainer:
     def optimizer_from_params(self) -> None:
         """The reverse of optimizer_to_params (e.g. after a checkpoint was loaded into the optimizer)."""
         self._moments(to_opt=False)
+        self.step_dev.fill_(int(self.opt.t))
+        self._refresh_hyper()
+
+    def _refresh_hyper(self) -> None:
+        """Copies the optimizer's settings to the device when they changed (outside a captured graph),
+        and rebuilds the bias-correction table when the betas changed."""
+        o = self.opt
+        f = np.float32
+        key = (f(o.lr), f(o.beta1), f(o.beta2), f(o.eps), f(o.weight_decay))
+        if key == self._hyper_key:
+            return
+        lr, b1, b2, eps, wd = key
+        shrink = f(1.0) - lr * wd                      # float arithmetic, as AdamW::step (adamw.cpp:16)
+        self.hyper_dev.copy_(torch.from_numpy(np.array([shrink, lr, b1, b2, eps], np.float32)))
+        if (b1, b2) != self._betas:
+            for cap in (1 << 16, 1 << 20, 1 << 24):
+                table = np.zeros(2 * cap, np.float32)
+                n = lib().nnb_adam_bias_table(ctypes.c_float(b1), ctypes.c_float(b2), table.ctypes.data, cap)
+                if n < cap or (table[2 * n - 2] == 1.0 and table[2 * n - 1] == 1.0):
+                    break
+            self.table_dev = torch.from_numpy(table[: 2 * n].copy()).to(self.hyper_dev.device)
+            self.table_len, self._betas = n, (b1, b2)
+        self._hyper_key = key
 
     def _moments(self, to_opt: bool) -> None:
         dev = self.m.device
@@ -118,14 +150,14 @@ class ShardedTrainer:
                 mine.copy_(full[self.lo: self.lo + self.chunk])
 
     def _adamw(self, s, n: int, w_ptr: int, g_ptr: int) -> None:
-        o = self.opt
-        check(lib().nnb_adamw_step(s, n, w_ptr, g_ptr, self.m.data_ptr(), self.v.data_ptr(), ctypes.c_float(o.lr),
-                                   ctypes.c_float(o.beta1), ctypes.c_float(o.beta2), ctypes.c_float(o.eps),
-                                   ctypes.c_float(o.weight_decay), o.t))
+        check(lib().nnb_adamw_step_device(s, n, w_ptr, g_ptr, self.m.data_ptr(), self.v.data_ptr(),
+                                          self.hyper_dev.data_ptr(), self.table_dev.data_ptr(), self.table_len,
+                                          self.step_dev.data_ptr()))
 
     def step(self, ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         """One step on the global batch ids/targets [B, T] (device int64); returns the mean loss
         over the global batch (a device scalar)."""
+        self._refresh_hyper()
         B, T = ids.shape
         per = B // self.shards
         lo, hi = self.owned[0] * per, (self.owned[-1] + 1) * per
@@ -144,6 +176,7 @@ class ShardedTrainer:
             p.grad_fresh = False
         check(lib().nnb_accumulate(s, 1, loss.data.data_ptr(), self.local_loss.data_ptr(), 1, 0))
         self.opt.t += 1
+        check(lib().nnb_step_advance(s, self.step_dev.data_ptr()))
         if self.world == 1:
             check(lib().nnb_column_sum(s, self.shards, self.total, self.shard_grads.data_ptr(),
                                        self.reduced.data_ptr(), 1))
@@ -166,3 +199,50 @@ class ShardedTrainer:
         check(lib().nnb_column_sum(s, self.world, 1, self.all_loss.data_ptr(), self.loss.data_ptr(), 1))
         check(lib().nnb_scale(s, 1, 1.0 / self.world, self.loss.data_ptr(), self.loss.data_ptr()))
         return self.loss
+
+    def capture(self, ids: torch.Tensor, targets: torch.Tensor, warmup: int = 2) -> "GraphedTrainStep":
+        """Runs `warmup` ordinary steps on (ids, targets), then captures one step into a CUDA graph
+        (see GraphedTrainStep). The warm-up steps are real training steps."""
+        return GraphedTrainStep(self, ids, targets, warmup)
+
+
+class GraphedTrainStep:
+    """One ShardedTrainer step captured into a CUDA graph, collectives included.
+
+    Calling it copies the batch into the graph's fixed input buffers (when given), refreshes the
+    optimizer's settings on the device if they changed, replays the graph and returns the loss
+    buffer (a device scalar, valid once the stream reaches it). Every replay is exactly one step: the
+    device step counter advances inside the graph and the host mirror (optimizer.t) here.
+    """
+
+    def __init__(self, trainer: ShardedTrainer, ids: torch.Tensor, targets: torch.Tensor, warmup: int = 2):
+        self.trainer = trainer
+        self.ids, self.targets = ids.clone(), targets.clone()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(max(1, warmup)):
+                trainer.step(self.ids, self.targets)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        lib().nnb_trace_enable(0)                 # no event records inside the graph
+        t_host = trainer.opt.t
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, capture_error_mode="thread_local"):
+            self.loss = trainer.step(self.ids, self.targets)
+        trainer.opt.t = t_host                    # capturing ran nothing
+        torch.cuda.synchronize()
+
+    def __call__(self, ids: torch.Tensor | None = None, targets: torch.Tensor | None = None) -> torch.Tensor:
+        if ids is not None:
+            self.ids.copy_(ids, non_blocking=True)
+        if targets is not None:
+            self.targets.copy_(targets, non_blocking=True)
+        self.trainer._refresh_hyper()
+        self.graph.replay()
+        self.trainer.opt.t += 1
+        return self.loss
+
+    def release(self) -> None:
+        """Drops the graph (needed before the process group is destroyed when it holds collectives)."""
+        self.graph = None

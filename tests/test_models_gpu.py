@@ -132,6 +132,41 @@ def test_transformer_training_deterministic_and_shard_invariant(cuda, dim, heads
     assert reduced.cpu().numpy().tobytes() == g1.tobytes()
 
 
+@pytest.mark.parametrize("dim,heads,dropout", [(64, 1, 0.0), (32, 4, 0.1)])
+def test_graphed_training_step_bitwise_equal_to_eager(cuda, dim, heads, dropout):
+    """The trainer's step captured into a CUDA graph (warm-up steps, capture, replays) gives the eager
+    steps' weights, losses and optimizer step count bit for bit -- with dropout too (the generator
+    state advances inside the graph)."""
+    torch = cuda
+    import nnb.random as nr
+    from nnb.nn import AdamW, Transformer, TransformerConfig
+    from nnb.train import ShardedTrainer
+
+    cfg = TransformerConfig(vocab_size=96, dim=dim, heads=heads, layers=2, max_len=32, dropout=dropout)
+    _, _, x_d, y_d = _batch(torch, 96, 8, 32, 92)
+    runs = []
+    for graphed in (False, True):
+        nr.manual_seed(4)
+        model = Transformer(cfg, seed=3)
+        tr = ShardedTrainer(model, AdamW(model.parameters(), lr=3e-3, weight_decay=1e-2), shards=8)
+        losses = []
+        if graphed:
+            step = tr.capture(x_d, y_d, warmup=2)
+            losses += [None, None]
+            for _ in range(3):
+                losses.append(float(step().cpu()[0]))
+            step.release()
+        else:
+            for _ in range(5):
+                losses.append(float(tr.step(x_d, y_d).cpu()[0]))
+            losses[:2] = [None, None]
+        runs.append((_flat(model), losses, tr.opt.t))
+    (w_e, l_e, t_e), (w_g, l_g, t_g) = runs
+    assert t_e == t_g == 5
+    assert l_e == l_g
+    assert w_e.tobytes() == w_g.tobytes()
+
+
 def test_cnn_forward_backward_matches_reference(cuda):
     torch = cuda
     ref = orc.ref()

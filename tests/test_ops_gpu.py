@@ -7,6 +7,8 @@ built on the tensor-core GEMM or on warp-tree row sums must match to fp32-grade 
 |got - want| <= 2e-5 * max|want| + 2e-5 * |want| (GEMM, attention, conv) and 1e-5 scaled the same
 way (layernorm, softmax / cross entropy).
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -350,6 +352,33 @@ def test_adamw_bitwise(cuda):
     assert_bits(host(tw), w)
     assert_bits(host(tm), m)
     assert_bits(host(tv), v)
+
+
+def test_adamw_device_scalars_bitwise(cuda):
+    """The graph-replayable AdamW (step counter, settings and bias-correction table in device memory)
+    gives the host-scalar update's bits, also past the table's end where the corrections saturate."""
+    torch = cuda
+    n = 50000
+    w0, g = nrm(34, n), nrm(35, n)
+    table = np.zeros(2 * (1 << 16), np.float32)
+    tlen = lib().nnb_adam_bias_table(ctypes.c_float(0.9), ctypes.c_float(0.999), table.ctypes.data, 1 << 16)
+    assert 1000 < tlen < (1 << 16) and table[2 * tlen - 2] == 1.0 and table[2 * tlen - 1] == 1.0
+    tab = dev(torch, table[: 2 * tlen].copy())
+    f = np.float32
+    shrink = f(1.0) - f(3e-4) * f(1e-2)
+    hyper = dev(torch, np.array([shrink, 3e-4, 0.9, 0.999, 1e-8], np.float32))
+    for t in (1, 2, 3, 500, tlen, tlen + 12345):
+        a = [dev(torch, w0), dev(torch, g), dev(torch, nrm(36, n) * 0.1), dev(torch, np.abs(nrm(37, n)) * 0.01)]
+        b = [x.clone() for x in a]
+        ok(lib().nnb_adamw_step(S(torch), n, a[0].data_ptr(), a[1].data_ptr(), a[2].data_ptr(), a[3].data_ptr(), 3e-4,
+                                0.9, 0.999, 1e-8, 1e-2, t))
+        step = torch.tensor([t - 1], dtype=torch.int64, device="cuda")
+        ok(lib().nnb_step_advance(S(torch), step.data_ptr()))
+        ok(lib().nnb_adamw_step_device(S(torch), n, b[0].data_ptr(), b[1].data_ptr(), b[2].data_ptr(), b[3].data_ptr(),
+                                       hyper.data_ptr(), tab.data_ptr(), tlen, step.data_ptr()))
+        assert int(step.item()) == t
+        for x, y in zip(a, b):
+            assert_bits(host(x), host(y))
 
 
 def test_shape_errors(cuda):

@@ -156,13 +156,23 @@ def _dp_worker(rank, world, port, out_dir):
         for _ in range(2):
             tr.step(x, y)
         flat = torch.cat([p.data.reshape(-1) for p in model.parameters()])
+        # the same two steps with the second one captured into a CUDA graph (all-to-all and all-gather
+        # inside the graph) and replayed
+        gmodel = Transformer(cfg, seed=4)
+        gtr = ShardedTrainer(gmodel, AdamW(gmodel.parameters(), lr=3e-3), shards=8, world=world, rank=rank)
+        step = gtr.capture(x, y, warmup=1)
+        step()
+        torch.cuda.synchronize()
+        gflat = torch.cat([p.data.reshape(-1) for p in gmodel.parameters()])
+        step.release()
         if rank == 0:
             ref_model = Transformer(cfg, seed=4)
             ref_tr = ShardedTrainer(ref_model, AdamW(ref_model.parameters(), lr=3e-3), shards=8)
             for _ in range(2):
                 ref_tr.step(x, y)
             ref_flat = torch.cat([p.data.reshape(-1) for p in ref_model.parameters()])
-            np.save(os.path.join(out_dir, "dp_eq.npy"), np.array([bool(torch.equal(flat, ref_flat))]))
+            np.save(os.path.join(out_dir, "dp_eq.npy"), np.array([bool(torch.equal(flat, ref_flat)),
+                                                                  bool(torch.equal(gflat, ref_flat))]))
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
@@ -180,4 +190,6 @@ def test_data_parallel_step_bitwise_equal_to_single_gpu(cuda, tmp_path):
         world = 2
     mp.start_processes(_dp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
-    assert bool(np.load(tmp_path / "dp_eq.npy")[0])
+    eq = np.load(tmp_path / "dp_eq.npy")
+    assert bool(eq[0]), "eager data-parallel steps differ from one GPU"
+    assert bool(eq[1]), "graph-replayed data-parallel step differs from one GPU"
