@@ -55,7 +55,7 @@ def parse_args():
     ap.add_argument("--gather", choices=("peer", "nccl"), default="peer",
                     help="N>1 GEMM: bands stored into GPU 0's C by the GEMM epilogue (peer) or an NCCL gather after it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("all", "gemm", "transformer", "cnn", "attention"), default="all",
+    ap.add_argument("--workload", choices=("all", "gemm", "transformer", "cnn", "attention", "next"), default="all",
                     help="one config alone, or all: the config 4 line with configs 2, 3 and 5 inside")
     ap.add_argument("--t-steps", type=int, default=10, help="timed transformer steps")
     ap.add_argument("--t-warmup", type=int, default=3)
@@ -374,6 +374,7 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
             transformer["cnn"] = run_cnn(20, 3, local_rank)
             transformer["attention"] = run_attention(10, 3, local_rank)
             transformer["matmul512"] = run_matmul512(local_rank)
+            transformer["next_rows"] = run_next_rows(local_rank, with_cpu=not args.no_cpu_baseline)
     if rank != 0:
         return
     flops = 2.0 * size ** 3
@@ -420,7 +421,7 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
         "clocks": clk,
     }
     if transformer is not None:
-        for key in ("cnn", "attention", "matmul512"):
+        for key in ("cnn", "attention", "matmul512", "next_rows"):
             if key in transformer:
                 line[key] = transformer.pop(key)
         line["transformer"] = transformer
@@ -688,6 +689,184 @@ def run_matmul512(local_rank: int):
             "config": {"workload": "config 1: nn::matmul 512^3 fp32 (3xTF32)", "dispatch": "CUDA graph replay"}}
 
 
+def run_next_rows(local_rank: int, with_cpu: bool = True):
+    """The rows built after the hot path, each timed on the GPU beside the reference's own CPU code on
+    the same shapes (oracle/_ref, all host cores, bounded samples): attention with dropout active,
+    the dropout stream, the DataLoader, checkpoints and the general (dilated, grouped) conv."""
+    import ctypes
+    import tempfile
+
+    import numpy as np
+    import torch
+
+    import nnb
+    import nnb.functional as F
+    import nnb.random as nr
+    from nnb.autograd import Value
+    from nnb.graph import GraphedStep
+
+    dev = torch.device("cuda", local_rank)
+    L = nnb.lib()
+    ref = None
+    if with_cpu:
+        from oracle import orc
+        ref = orc.ref()
+        if ref is not None:
+            ref.ref_set_threads(os.cpu_count() or 1)
+    cores = os.cpu_count() or 1
+    out = {}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def events(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    # -- attention with dropout active (config-3 shape, p = 0.1), mask drawn inside the step ----------
+    N, T, D, H, p = 32, 256, 512, 8, 0.1
+    g = torch.Generator(device=dev).manual_seed(7)
+    q, k, v, go = (torch.randn(N, T, D, device=dev, generator=g) for _ in range(4))
+    nr.manual_seed(1)
+    state = nr.device_generator("dropout", dev)
+    keep = torch.empty((N * H * T * T + 31) // 32, dtype=torch.int32, device=dev)
+    o, probs, wts = torch.empty(N, T, D, device=dev), torch.empty(N, H, T, T, device=dev), torch.empty(N, H, T, T, device=dev)
+    dq, dk, dv = (torch.empty(N, T, D, device=dev) for _ in range(3))
+
+    def mask():
+        nnb.check(L.nnb_dropout_mask(torch.cuda.current_stream().cuda_stream, state.data_ptr(), N * H * T * T,
+                                     ctypes.c_float(p), keep.data_ptr()))
+
+    def attn_drop():
+        s = torch.cuda.current_stream().cuda_stream
+        mask()
+        nnb.check(L.nnb_attention_dropout_fwd(s, N, T, T, D, H, q.data_ptr(), k.data_ptr(), v.data_ptr(), None, 1,
+                                              ctypes.c_float(p), keep.data_ptr(), o.data_ptr(), probs.data_ptr(),
+                                              wts.data_ptr()))
+        nnb.check(L.nnb_attention_dropout_bwd(s, N, T, T, D, H, go.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                              v.data_ptr(), probs.data_ptr(), wts.data_ptr(), ctypes.c_float(p),
+                                              keep.data_ptr(), None, 1, dq.data_ptr(), 1, dk.data_ptr(), 1,
+                                              dv.data_ptr(), 1))
+
+    step_ms = events(GraphedStep(attn_drop), 5)
+    mask_ms = events(mask, 5)
+    draws = N * H * T * T
+    row = {"metric": "attention with dropout fwd+bwd ms/step", "value": step_ms, "unit": "ms",
+           "config": {"workload": "config-3 shape B32 H8 T256 Dh64 causal, dropout 0.1 on the weights (composed path)",
+                      "dispatch": "CUDA graph replay"},
+           "mask_ms": mask_ms,
+           "dropout_stream": {"draws_per_s": draws / (mask_ms * 1e-3), "draws": draws,
+                              "bound": "serial: one mt19937 stream per layer (the reference's draw order), one CTA"}}
+    if ref is not None:
+        qa, ka, va, ga = (x.cpu().numpy().ravel() for x in (q, k, v, go))
+        oa, dqa, dka, dva = (np.zeros(N * T * D, np.float32) for _ in range(4))
+        t0 = time.perf_counter()
+        ref.ref_attention_dropout(1, N, T, D, H, 1, p, *(orc.ptr(a) for a in (qa, ka, va, ga, oa, dqa, dka, dva)))
+        row["cpu_baseline"] = {"value": (time.perf_counter() - t0) * 1e3, "unit": "ms", "cores": cores,
+                               "kind": "reference", "sample": "one full fwd+bwd of the same shape"}
+        sizes = np.array([1 << 22], np.uintp)
+        masks = np.zeros(1 << 22, np.float32)
+        t0 = time.perf_counter()
+        ref.ref_dropout_masks(1, 0, p, sizes.ctypes.data, 1, masks.ctypes.data)
+        row["dropout_stream"]["cpu_baseline_draws_per_s"] = (1 << 22) / (time.perf_counter() - t0)
+    out["attention_dropout"] = row
+
+    # -- DataLoader: batches gathered from an HBM-resident dataset, and the host path -------------------
+    from nnb.data import DataLoader, SequenceDataset, TensorDataset
+    n, feat = 60000, 784
+    xs = np.random.default_rng(0).random((n, 1, 28, 28), dtype=np.float32)
+    ys = np.random.default_rng(1).integers(0, 10, n).astype(np.int64)
+    nr.manual_seed(2)
+    ld = DataLoader(TensorDataset(xs, ys), 64, True, device=dev)
+    ld.get_batch(0)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record()
+    for xb, yb in ld:
+        pass
+    e1.record()
+    torch.cuda.synchronize()
+    epoch_s = time.perf_counter() - t0
+    nb = ld.num_batches()
+    big = DataLoader(TensorDataset(xs, ys), 8192, True, device=dev)
+    big_ms = events(lambda: big.get_batch(1), 10)
+    moved = 2 * 8192 * (feat * 4 + 8)
+    seq = DataLoader(SequenceDataset(np.random.default_rng(3).integers(0, 4096, 1 << 24), 512), 64, True, device=dev)
+    seq_ms = events(lambda: seq.get_batch(5), 20)
+    row = {"metric": "DataLoader batch (64 x 1x28x28 + labels) us", "value": epoch_s / nb * 1e6, "unit": "us",
+           "config": {"workload": "MNIST-shaped TensorDataset 60000 x 784 fp32 + int64 labels in HBM, batch 64, "
+                                  "shuffled epoch (host wall time per batch, Python iteration included)"},
+           "device_us_per_batch": e0.elapsed_time(e1) / nb * 1e3,
+           "gather_8192": {"ms": big_ms, "gbs": moved / (big_ms * 1e-3) / 1e9,
+                           "roofline": {"bound": "hbm", "achieved": moved / (big_ms * 1e-3) / 1e9,
+                                        "peak": load_peaks()["hbm_gbs"], "unit": "GB/s"}},
+           "sequence_batch_us": seq_ms * 1e3}
+    if ref is not None:
+        sec = ref.ref_time_loader(n, feat, 64, 200)
+        row["cpu_baseline"] = {"value": sec / 200 * 1e6, "unit": "us", "cores": cores, "kind": "reference",
+                               "sample": "200 get_batch calls of the same loader shape (host stacking)"}
+    out["dataloader"] = row
+
+    # -- checkpoint of a 4096 x 4096 Linear with its AdamW state ----------------------------------------
+    from nnb.checkpoint import load_checkpoint, save_checkpoint
+    from nnb.nn import AdamW, Linear, Sequential
+    m = Sequential(Linear(4096, 4096, np.random.default_rng(4), dev))
+    opt = AdamW(m.parameters())
+    for prm in m.parameters():
+        prm.grad.fill_(0.5)
+        prm.grad_fresh = False
+    opt.step()
+    torch.cuda.synchronize()
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "ck.nnck")
+        t0 = time.perf_counter()
+        save_checkpoint(path, m, opt, step=1)
+        load_checkpoint(path, m, opt)
+        torch.cuda.synchronize()
+        sec = time.perf_counter() - t0
+        nbytes = os.path.getsize(path)
+        row = {"metric": "checkpoint save+load s", "value": sec, "unit": "s",
+               "config": {"workload": "Sequential{Linear(4096, 4096)} + AdamW state (NNCK v1, 201 MB), local temp dir"},
+               "mb_per_s": 2 * nbytes / sec / 1e6, "bytes": nbytes}
+        if ref is not None:
+            rsec = ref.ref_time_checkpoint(os.path.join(tmp, "ref.nnck").encode(), 4096, 4096)
+            row["cpu_baseline"] = {"value": rsec, "unit": "s", "cores": cores, "kind": "reference",
+                                   "sample": "one save + load of the same model and optimizer"}
+    out["checkpoint"] = row
+
+    # -- general conv: dilation 2, groups 4 ---------------------------------------------------------------
+    Nc, Cin, Hc, Wc, Cout, kk, stride, pad, dil, groups = 64, 32, 28, 28, 64, 3, 1, 2, 2, 4
+    xc = torch.randn(Nc, Cin, Hc, Wc, device=dev, generator=g)
+    wc = torch.randn(Cout, Cin // groups, kk, kk, device=dev, generator=g) * 0.1
+    bc = torch.randn(Cout, device=dev, generator=g)
+    gc = torch.randn(Nc, Cout, Hc, Wc, device=dev, generator=g)
+
+    def conv():
+        X, Wt, B = Value.leaf(xc, True), Value.leaf(wc, True), Value.leaf(bc, True)
+        Y = F.conv2d(X, Wt, B, stride, pad, dilation=dil, groups=groups)
+        Y.backward(gc)
+
+    conv_ms = events(conv, 10)
+    flops = 3 * 2 * Nc * Cout * Hc * Wc * (Cin // groups) * kk * kk
+    row = {"metric": "conv2d (dilation 2, groups 4) fwd+bwd ms", "value": conv_ms, "unit": "ms",
+           "config": {"workload": "x [64, 32, 28, 28], w [64, 8, 3, 3], pad 2, dilation 2, groups 4, eager"},
+           "algorithmic_tflops": flops / (conv_ms * 1e-3) / 1e12}
+    if ref is not None:
+        xa, wa, ba, ga2 = (t.cpu().numpy().ravel() for t in (xc, wc, bc, gc))
+        ya, dxa, dwa, dba = (np.zeros(a.size, np.float32) for a in (ga2, xa, wa, ba))
+        t0 = time.perf_counter()
+        ref.ref_conv2d_ex(Nc, Cin, Hc, Wc, Cout, kk, kk, stride, pad, dil, groups, *(orc.ptr(a) for a in
+                                                                                  (xa, wa, ba, ga2, ya, dxa, dwa, dba)))
+        row["cpu_baseline"] = {"value": (time.perf_counter() - t0) * 1e3, "unit": "ms", "cores": cores,
+                               "kind": "reference", "sample": "one fwd+bwd of the same shape"}
+    out["conv_general"] = row
+    return out
+
+
 def cpu_baselines(cores: int | None = None):
     """The reference's own CPU code (oracle/_ref) on the host cores for configs 1, 2, 3 and 5, each a
     bounded sample (a few seconds)."""
@@ -761,7 +940,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if args.workload in ("cnn", "attention"):
+        if args.workload == "next":
+            if rank == 0:
+                print(json.dumps(run_next_rows(local_rank, with_cpu=not args.no_cpu_baseline)), flush=True)
+        elif args.workload in ("cnn", "attention"):
             if rank == 0:
                 fn = run_cnn if args.workload == "cnn" else run_attention
                 print(json.dumps(fn(max(args.t_steps, 10), args.t_warmup, local_rank)), flush=True)

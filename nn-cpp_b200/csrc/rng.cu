@@ -10,17 +10,18 @@
 //
 // Device side: one generator state = 624 untempered words + the index of the next word to temper
 // (625 uint32 in HBM), so successive draws continue the stream across launches and inside CUDA
-// graphs. A draw of n outputs runs in ONE CTA of 640 threads: the twist that makes the next 624
-// words is three dependent data-parallel phases (words [0,227) read only the old block, [227,454)
-// and [454,624) read words 227 back in the new block), and each 32 consecutive outputs become one
-// keep-mask word through a warp ballot. The stream is serial by definition (the reference draws
-// output i for element i in row-major order), so the cost is ~one twist per 624 elements on one
-// SM; the masks are 1 bit per element (the reference keeps a float per element).
+// graphs. A draw of n outputs is two launches per 2^24 outputs: ONE CTA advances the twist, read as
+// the linear recurrence it is, 454 words per barrier (227 threads, two chained words each) and
+// streams the raw words out; then a grid-wide kernel tempers them, compares with p and packs one
+// keep word per 32 outputs (warp ballot). The stream is serial by definition (the reference draws
+// output i for element i in row-major order); the masks are 1 bit per element (the reference keeps
+// a float per element).
 //
 // Dropout (dropout.cpp:20-31): u = float(x >> 8) * 2^-24 per element, dropped when u < p, kept
 // elements scaled by 1/(1-p); p == 1 drops everything without drawing, p == 0 keeps everything
 // without drawing.
 #include <algorithm>
+#include <cmath>
 #include <map>
 #include <mutex>
 #include <random>
@@ -37,7 +38,6 @@ namespace {
 constexpr int kMtN = 624;
 constexpr int kMtShift = 397;
 constexpr int kMtHalf = kMtN - kMtShift;     // 227: words before this index read only old words
-constexpr int kMtThreads = 640;              // 20 warps: one keep-mask word each per block of 624
 constexpr uint32_t kMtMatrix = 0x9908b0dfu;
 
 // ---- host: seed_seq + mt19937 seeding ------------------------------------------------------------
@@ -145,60 +145,62 @@ __device__ __forceinline__ uint32_t mt_temper(uint32_t y) {
 	return y ^ (y >> 18);
 }
 
-// nw = the block after `old` (all threads of the CTA call it; ends with the CTA synchronised)
-__device__ __forceinline__ void mt_next_block(const uint32_t* old, uint32_t* nw, int t) {
-	if (t < kMtHalf) nw[t] = old[t + kMtShift] ^ mt_mix(old[t], old[t + 1]);
+// The stream as one sequence: X[0..623] = the state's words, and for j >= 624
+//   X[j] = X[j - 227] ^ mix(X[j - 624], X[j - 623]),
+// which is exactly the twist (block b+1's word i reads block b's words i, i+1, i+397 for i < 227 and
+// block b+1's word i-227 above). Output o of a draw that starts at state index p is temper(X[p + o]).
+// Every word depends only on words at least 227 back, so a round computes 454 new words: thread
+// t < 227 makes X[f + t] and then X[f + t + 227] (which needs X[f + t] -- its own register -- and
+// words 396 / 397 back, all older than the round); one barrier per round. X lives in a 2048-word
+// shared ring. This serial part only streams the raw words X[p .. p + n) to global memory; tempering,
+// the comparison with p and the bit packing run afterwards over the whole GPU.
+constexpr int kRing = 2048;
+constexpr int kRound = 2 * kMtHalf;              // 454 words per round
+constexpr int kStreamThreads = 256;
+constexpr unsigned long long kChunk = 1ull << 24;  // outputs per serial launch (64 MB of raw words)
+
+__global__ void __launch_bounds__(kStreamThreads, 1) mt_stream_kernel(uint32_t* __restrict__ state,
+		unsigned long long n, uint32_t* __restrict__ raw) {
+	__shared__ uint32_t ring[kRing];
+	const int t = threadIdx.x;
+	for (int i = t; i < kMtN; i += kStreamThreads) ring[i] = state[i];
+	const unsigned long long p0 = state[kMtN] > (uint32_t)kMtN ? (unsigned long long)kMtN : state[kMtN];
 	__syncthreads();
-	if (t >= kMtHalf && t < 2 * kMtHalf) nw[t] = nw[t - kMtHalf] ^ mt_mix(old[t], old[t + 1]);
-	__syncthreads();
-	if (t >= 2 * kMtHalf && t < kMtN - 1) nw[t] = nw[t - kMtHalf] ^ mt_mix(old[t], old[t + 1]);
-	else if (t == kMtN - 1) nw[t] = nw[t - kMtHalf] ^ mt_mix(old[t], nw[0]);
-	__syncthreads();
+	const unsigned long long end = p0 + n, last = end - 1;                // outputs are X[p0 .. end)
+	const unsigned long long block0 = (last / kMtN) * kMtN, need = block0 + kMtN;
+	for (unsigned long long i = p0 + t; i < end && i < (unsigned long long)kMtN; i += kStreamThreads)
+		raw[i - p0] = ring[i];
+	for (unsigned long long frontier = kMtN; frontier < need; frontier += kRound) {
+		if (t < kMtHalf) {
+			const unsigned long long j = frontier + t, j2 = j + kMtHalf;
+			const uint32_t x1 = ring[(j - kMtHalf) & (kRing - 1)] ^
+				mt_mix(ring[(j - kMtN) & (kRing - 1)], ring[(j - kMtN + 1) & (kRing - 1)]);
+			const uint32_t x2 = x1 ^ mt_mix(ring[(j - kMtShift) & (kRing - 1)], ring[(j - kMtShift + 1) & (kRing - 1)]);
+			ring[j & (kRing - 1)] = x1;
+			ring[j2 & (kRing - 1)] = x2;
+			if (j >= p0 && j < end) raw[j - p0] = x1;
+			if (j2 >= p0 && j2 < end) raw[j2 - p0] = x2;
+		}
+		__syncthreads();
+	}
+	for (int i = t; i < kMtN; i += kStreamThreads) state[i] = ring[(block0 + i) & (kRing - 1)];
+	if (t == 0) state[kMtN] = (uint32_t)(last - block0 + 1);
 }
 
-// Draws n >= 1 outputs from `state` (advancing it) and writes keep[w] bit b = element 32w + b kept.
-// Output r (relative to the first one drawn) lives in block r / 624 at word r % 624, where block 0
-// is the state's current block (twisted first if its words are used up).
-__global__ void __launch_bounds__(kMtThreads, 1) dropout_mask_kernel(uint32_t* __restrict__ state,
-		unsigned long long n, float p, uint32_t* __restrict__ keep) {
-	__shared__ uint32_t buf[2][kMtN];
-	const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-	for (int i = t; i < kMtN; i += kMtThreads) buf[0][i] = state[i];
-	unsigned long long pos = state[kMtN];
-	__syncthreads();
-	int a = 0;
-	if (pos >= (unsigned long long)kMtN) {
-		mt_next_block(buf[0], buf[1], t);
-		a = 1;
-		pos = 0;
-	}
-	const unsigned long long last = pos + n - 1, last_block = last / kMtN, words = (n + 31) / 32;
-	for (unsigned long long blk = 0;; ++blk) {
-		if (blk < last_block) mt_next_block(buf[a], buf[a ^ 1], t);
-		// words whose first output falls in this block: 624 blk <= pos + 32 w < 624 (blk + 1)
-		const unsigned long long w_lo = blk == 0 ? 0 : (kMtN * blk - pos + 31) / 32;
-		unsigned long long w_hi = (kMtN * (blk + 1) - pos + 31) / 32;
-		if (w_hi > words) w_hi = words;
-		const unsigned long long w = w_lo + warp;
-		if (w < w_hi) {
-			const unsigned long long e = 32 * w + lane;
-			bool kept = false;
-			if (e < n) {
-				const unsigned long long idx = pos + e - kMtN * blk;      // < 2 * 624
-				const uint32_t x = idx < (unsigned long long)kMtN ? buf[a][idx] : buf[a ^ 1][idx - kMtN];
-				const float u = static_cast<float>(mt_temper(x) >> 8) * (1.0f / 16777216.0f);
-				kept = !(u < p);
-			}
-			const uint32_t word = __ballot_sync(0xffffffffu, kept);
-			if (lane == 0) keep[w] = word;
-		}
-		if (blk == last_block) {
-			for (int i = t; i < kMtN; i += kMtThreads) state[i] = buf[a][i];
-			if (t == 0) state[kMtN] = (uint32_t)(last % kMtN + 1);
-			return;
-		}
-		__syncthreads();       // every read of this block is done before the next twist overwrites it
-		a ^= 1;
+// keep[w] bit b = output 32w + b kept: temper(x) >> 8 >= threshold, where threshold = ceil(p * 2^24)
+// makes the integer test equal to the reference's float test u = float(x >> 8) * 2^-24 < p (both
+// sides are exact: x >> 8 < 2^24 and p * 2^24 only rescales p).
+__global__ void keep_pack_kernel(const uint32_t* __restrict__ raw, unsigned long long n, uint32_t threshold,
+		uint32_t* __restrict__ keep) {
+	const int lane = threadIdx.x & 31;
+	const unsigned long long warps = (unsigned long long)gridDim.x * (blockDim.x >> 5);
+	const unsigned long long words = (n + 31) / 32;
+	for (unsigned long long w = (blockIdx.x * (unsigned long long)blockDim.x + threadIdx.x) >> 5; w < words;
+			w += warps) {
+		const unsigned long long e = 32 * w + lane;
+		const bool kept = e < n && (mt_temper(raw[e]) >> 8) >= threshold;
+		const uint32_t word = __ballot_sync(0xffffffffu, kept);
+		if (lane == 0) keep[w] = word;
 	}
 }
 
@@ -249,8 +251,26 @@ nnb_status dropout_mask(cudaStream_t s, uint32_t* state, size_t n, float p, uint
 	TraceScope ts(s, kTraceRowwise);
 	if (p == 0.0f || p == 1.0f)        // nothing is drawn (dropout.cpp:20-23)
 		return cuda_status(cudaMemsetAsync(keep, p == 0.0f ? 0xff : 0, words * sizeof(uint32_t), s), "dropout mask fill");
-	dropout_mask_kernel<<<1, kMtThreads, 0, s>>>(state, (unsigned long long)n, p, keep);
-	return cuda_status(cudaGetLastError(), "dropout_mask launch");
+	const double scaled = std::ceil(static_cast<double>(p) * 16777216.0);    // exact: p * 2^24 <= 2^24
+	const uint32_t threshold = static_cast<uint32_t>(scaled);
+	void* ws = nullptr;
+	const size_t chunk = n < kChunk ? n : (size_t)kChunk;
+	NNB_TRY(scratch_alloc(&ws, chunk * sizeof(uint32_t), s));
+	uint32_t* raw = static_cast<uint32_t*>(ws);
+	DeviceState* dev = nullptr;
+	nnb_status st = device_state(&dev);
+	for (size_t off = 0; st == NNB_OK && off < n; off += kChunk) {    // chunks are multiples of 32 outputs
+		const size_t c = n - off < kChunk ? n - off : (size_t)kChunk;
+		mt_stream_kernel<<<1, kStreamThreads, 0, s>>>(state, (unsigned long long)c, raw);
+		const unsigned long long words = (c + 31) / 32;
+		unsigned blocks = (unsigned)((words + 7) / 8);
+		const unsigned cap = (unsigned)dev->sm_count * 16;
+		if (blocks > cap) blocks = cap;
+		keep_pack_kernel<<<blocks, 256, 0, s>>>(raw, (unsigned long long)c, threshold, keep + off / 32);
+		st = cuda_status(cudaGetLastError(), "dropout_mask launch");
+	}
+	nnb_status st2 = scratch_free(ws, s);
+	return st != NNB_OK ? st : st2;
 }
 
 }  // namespace nnb

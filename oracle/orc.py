@@ -93,8 +93,11 @@ _REF_SIGS = {
     "ref_random_split": ([_sz, _p, _i, _c.c_uint64, _p, _p], _i),
     "ref_balanced_weights": ([_p, _sz, _sz, _p], _i),
     "ref_mt19937_outputs": ([_p, _sz, _sz, _p], None),
+    "ref_time_loader": ([_sz, _sz, _sz, _sz], _d),
+    "ref_time_checkpoint": ([_c.c_char_p, _sz, _sz], _d),
     "ref_derive_outputs": ([_c.c_uint64, _c.c_char_p, _i, _sz, _p], None),
     "ref_dropout_masks": ([_c.c_uint64, _i, _f, _p, _i, _p], None),
+    "ref_attention_dropout": ([_c.c_uint64, _sz, _sz, _sz, _sz, _i, _f, _p, _p, _p, _p, _p, _p, _p, _p], None),
     "ref_mha_dropout": ([_c.c_uint64, _sz, _sz, _sz, _sz, _i, _f, _i, _p, _p, _p, _p, _p, _p], None),
     "ref_linear_checkpoint_save": ([_c.c_char_p, _p, _p, _p, _p, _f, _f, _c.c_longlong], _i),
     "ref_linear_checkpoint_load": ([_c.c_char_p, _p, _p], _c.c_longlong),

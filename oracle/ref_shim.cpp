@@ -30,6 +30,7 @@
 #include "reference_gemm.hpp"   // the reference's own test oracle, tests/reference_gemm.hpp
 
 #include <chrono>
+#include <cmath>
 #include <cstddef>
 #include <cstring>
 #include <vector>
@@ -432,6 +433,36 @@ int ref_balanced_weights(const size_t* labels, size_t n, size_t classes, double*
 	}
 }
 
+// Seconds for `batches` get_batch calls of a DataLoader(batch, shuffle) over a TensorDataset of n
+// rows of `row` floats (targets one float per row): the reference's host-side batch assembly.
+double ref_time_loader(size_t n, size_t row, size_t batch, size_t batches) {
+	std::vector<float> x(n * row), y(n);
+	for (size_t i = 0; i < x.size(); i++) x[i] = static_cast<float>(i % 251);
+	for (size_t i = 0; i < n; i++) y[i] = static_cast<float>(i % 10);
+	nn::TensorDataset ds(Tensor({n, row}, x), Tensor({n, 1}, y));
+	nn::manual_seed(1);
+	nn::DataLoader loader(ds, batch, true);
+	const auto t0 = std::chrono::steady_clock::now();
+	float sink = 0.0f;
+	for (size_t b = 0; b < batches; b++) sink += loader.get_batch(b % loader.num_batches()).second.data()[0];
+	const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+	return sink < -1.0f ? -sec : sec;
+}
+
+// Seconds for one save_checkpoint and one load_checkpoint (model and AdamW state) of
+// Sequential{Linear(in, out)} at `path`.
+double ref_time_checkpoint(const char* path, size_t in, size_t out) {
+	nn::Sequential m;
+	m.add(std::make_unique<nn::Linear>(in, out));
+	nn::AdamW opt(m.parameters(), 1e-3f);
+	for (auto& p : m.parameters()) p.grad() = Tensor(p.data().shape(), 0.5f);
+	opt.step();
+	const auto t0 = std::chrono::steady_clock::now();
+	nn::save_checkpoint(path, m, &opt, 1);
+	nn::load_checkpoint(path, m, &opt);
+	return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
 // n outputs of std::mt19937 seeded from std::seed_seq{seeds[0..count)}.
 void ref_mt19937_outputs(const uint32_t* seeds, size_t count, size_t n, uint32_t* out) {
 	std::seed_seq seq(seeds, seeds + count);
@@ -460,6 +491,27 @@ void ref_dropout_masks(uint64_t seed, int skip, float p, const size_t* sizes, in
 		copy_out(y.data(), out + off);
 		off += sizes[c];
 	}
+}
+
+// The core of MultiHeadAttention::attend's dropout branch (src/nn/attention.cpp:36-47) on q, k, v
+// [N, T, D]: split heads, matmul_bt, scaled_masked_softmax, Dropout(p) (taken after
+// manual_seed(seed)), matmul, merge heads; then the backward of upstream g. Any output may be null.
+void ref_attention_dropout(uint64_t seed, size_t N, size_t T, size_t D, size_t heads, int causal, float p,
+		const float* q, const float* k, const float* v, const float* g, float* out, float* dq, float* dk, float* dv) {
+	nn::manual_seed(seed);
+	nn::Dropout drop(p);
+	const size_t Dh = D / heads;
+	Value Q = leaf({N, T, D}, q), K = leaf({N, T, D}, k), V = leaf({N, T, D}, v);
+	auto split = [&](const Value& x) { return nn::transpose(nn::reshape(x, {N, T, heads, Dh}), {0, 2, 1, 3}); };
+	Value scores = nn::matmul_bt(split(Q), split(K));
+	Value w = drop.forward(nn::scaled_masked_softmax(scores, 1.0f / std::sqrt(static_cast<float>(Dh)), Tensor({0}),
+		causal != 0));
+	Value merged = nn::reshape(nn::transpose(nn::matmul(w, split(V)), {0, 2, 1, 3}), {N, T, D});
+	backward_through(merged, g);
+	copy_out(merged.data(), out);
+	copy_out(Q.grad(), dq);
+	copy_out(K.grad(), dk);
+	copy_out(V.grad(), dv);
 }
 
 // manual_seed(seed); MultiHeadAttention(D, heads, causal, p) with params = q.w, q.b, k.w, k.b, v.w,

@@ -90,6 +90,29 @@ def test_dropout_eval_mode_is_identity(cuda):
     assert d(x) is x
 
 
+@pytest.mark.parametrize("N,T,D,H,causal,p", [(2, 33, 64, 2, 1, 0.3), (3, 17, 48, 4, 0, 0.1), (1, 130, 64, 1, 1, 0.5)])
+def test_attention_dropout_op_matches_reference(cuda, N, T, D, H, causal, p):
+    """The attention core with dropout (nnb_dropout_mask + nnb_attention_dropout_fwd/bwd) against the
+    reference's own composition (split heads, matmul_bt, scaled_masked_softmax, Dropout, matmul):
+    identical masks, products to the fp32 bound."""
+    torch = cuda
+    import nnb.functional as F
+    import nnb.random as nr
+    from nnb.autograd import Value
+    R = ref()
+    q, k, v, g = (orc.normal(400 + i, N * T * D) for i in range(4))
+    o_r, dq_r, dk_r, dv_r = (orc.zeros(N * T * D) for _ in range(4))
+    R.ref_attention_dropout(12, N, T, D, H, causal, p, *(orc.ptr(a) for a in (q, k, v, g, o_r, dq_r, dk_r, dv_r)))
+    nr.manual_seed(12)
+    state = nr.device_generator("dropout", torch.device("cuda"))
+    Q, K, V = (Value.leaf(torch.from_numpy(a.reshape(N, T, D)).cuda(), True) for a in (q, k, v))
+    Y = F.attention_dropout(Q, K, V, H, None, bool(causal), p, state)
+    Y.backward(torch.from_numpy(g.reshape(N, T, D)).cuda())
+    _close(Y.data.cpu().numpy().ravel(), o_r, 2e-5)
+    for got, want in ((Q.grad, dq_r), (K.grad, dk_r), (V.grad, dv_r)):
+        _close(got.cpu().numpy().ravel(), want, 2e-5)
+
+
 def _mha_params(D, seed):
     ws = []
     for i in range(4):
