@@ -533,11 +533,27 @@ __global__ void zero_fill_kernel(float* c, long long ldc, long long s_outer, lon
 inline long long round_up(long long x, long long a) { return (x + a - 1) / a * a; }
 
 // Column tile: the widest of 256 / 128 / 64 whose padding waste is within 12.5 % of the least.
-static int choose_bn(long long n) {
-	const long long best = std::min({round_up(n, 256), round_up(n, 128), round_up(n, 64)});
-	for (int bn : {256, 128, 64})
-		if (round_up(n, bn) * 8 <= best * 9) return bn;
-	return 64;
+// Tile width. A tile's time is its MMA instruction count (the same for every width) times the cost of
+// one tf32 instruction, measured at about 44 + 0.38 N cycles, and the persistent grid works through
+// the tiles in waves of one per SM: the width with the fewest waves x instruction cost wins, a
+// narrower one only when clearly better. Big products keep 256; products with few tiles (a rank's
+// share of a data-parallel batch) get narrower tiles that fill the SMs. The width does not change any
+// element's arithmetic (each is one k-ordered chain in the accumulator), so results stay bitwise
+// independent of it, of the batch size and of the GPU count.
+static int choose_bn(long long m, long long n, long long entries, int sms) {
+	const long long mt = entries * (round_up(m, kBM) / kBM);
+	int best = 256;
+	double best_cost = 0.0;
+	for (int bn : {256, 128, 64}) {
+		const long long tiles = mt * (round_up(n, bn) / bn);
+		const long long waves = (tiles + sms - 1) / sms;
+		const double cost = (double)waves * (44.0 + 0.38 * bn);
+		if (bn == 256 || cost < best_cost * 0.97) {
+			best = bn;
+			best_cost = cost;
+		}
+	}
+	return best;
 }
 
 static bool g_attr_set[64][2][3];
@@ -562,9 +578,9 @@ struct Plan {
 	size_t off_b, off_f, flag_ints, total;
 };
 
-static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0) {
+static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int sms = 148) {
 	pl.S = d.mode == NNB_MATH_FP32X3 ? 2 : 1;
-	pl.bn = force_bn ? force_bn : choose_bn(d.n);
+	pl.bn = force_bn ? force_bn : choose_bn(d.m, d.n, d.batch_outer * d.batch_inner, sms > 0 ? sms : 148);
 	pl.b_panel_rows = b_panel_rows(pl.bn);
 	pl.Mp = round_up(d.m, kBM);
 	pl.Np = round_up(d.n, pl.bn);
@@ -749,7 +765,7 @@ __global__ void depth_sum_kernel(const float* __restrict__ part, int pieces, lon
 
 static nnb_status gemm_direct(cudaStream_t s, const DeviceState* dev, const GemmDesc& d) {
 	Plan pl;
-	NNB_TRY(make_plan(d, pl));
+	NNB_TRY(make_plan(d, pl, 0, dev->sm_count));
 	void* ws = nullptr;
 	NNB_TRY(scratch_alloc(&ws, pl.total, s));
 	nnb_status st = d.mode == NNB_MATH_FP32X3
