@@ -318,6 +318,9 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     # the collective baseline at N > 1: the GEMM into a local band, then an NCCL gather to GPU 0
     nccl_gather = None
     if world > 1:
+        for _ in range(3):                # first gathers set up NCCL's peer connections: untimed
+            gemm_local()
+            gather_rows(c, bands, dst=0)
         barrier()
         torch.cuda.synchronize()
         e0.record()

@@ -48,7 +48,8 @@ struct Cfg {
 	static constexpr int kStageBytes = kABytes + kBBytes;
 	static constexpr int kStagesRaw = kSmemBudget / kStageBytes;
 	static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-	static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+	static constexpr int kEpiBytes = 4 * 32 * 32 * 4;        // one 32 x 32 staging tile per epilogue warp
+	static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024;
 	static constexpr int kTmemCols = 2 * kBN;                // two accumulators
 	static constexpr int kBPanelRows = b_panel_rows(kBN);
 	static constexpr int kBPanels = kBN / kBPanelRows;
@@ -419,6 +420,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 		const int row = quad * 32 + lane;
 		const bool vec_ok = p.act == kActNone && (p.ldc % 4 == 0) && (p.sc_outer % 4 == 0) &&
 			(p.sc_inner % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+		// 32 x 32 staging tile of this warp: element (r, c) at float r*32 + 4*((c/4) ^ (r & 7)) + c%4, so that
+		// both the row-per-lane writes and the 4-rows-per-instruction reads are free of bank conflicts
+		float* stage = reinterpret_cast<float*>(smem + (size_t)kStages * C::kStageBytes) + quad * 1024;
 		int it = 0;
 		for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
 			const int buf = it & 1;
@@ -429,7 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 			tile_coords(t, p, bi, mt, nt);
 			const int gm = mt * kBM + row;
 			const bool row_ok = gm < p.M;
-			float* crow = p.C + batch_offset(bi, p.batch_inner, p.sc_outer, p.sc_inner) + (long long)gm * p.ldc;
+			float* cbase = p.C + batch_offset(bi, p.batch_inner, p.sc_outer, p.sc_inner);
+			float* crow = cbase + (long long)gm * p.ldc;
 			const long long aux_row = batch_offset(bi, p.batch_inner, p.s_aux_outer, p.s_aux_inner) + (long long)gm * p.ld_aux;
 			const bool fix = *p.any_nonfinite != 0;
 			const bool row_bad = fix && row_ok && p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0;
@@ -442,11 +447,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 				uint32_t r[32];
 				tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + buf * kBN + ch * 32, r);
 				tmem_wait_ld();
-				if (!row_ok) continue;
+				// whole 32-column chunks of a vector-friendly C go out through the staging tile as
+				// 128-byte row segments (coalesced: one line per 8 lanes, also over NVLink when C is a
+				// peer's memory); every lane takes part, rows past M only skip the global stores
+				const bool staged = vec_ok && gn0 + 32 <= p.N;       // warp-uniform
+				if (!row_ok && !staged) continue;
 				float v[32];
 #pragma unroll
 				for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-				if (fix) {
+				if (fix && row_ok) {
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {
 						const int gn = gn0 + j;
@@ -481,17 +490,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 						v[j] = gelu_fwd(v[j], tanh_one(gelu_tanh_arg(v[j])));
 					}
 				}
-				if (vec_ok && gn0 + 32 <= p.N) {
-					float4* c4 = reinterpret_cast<float4*>(crow + gn0);
+				if (staged) {
+					float4* st4 = reinterpret_cast<float4*>(stage);
 #pragma unroll
-					for (int j = 0; j < 8; ++j) {
-						float4 o = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-						if (p.accumulate) {
-							const float4 c = c4[j];
-							o.x = c.x + o.x; o.y = c.y + o.y; o.z = c.z + o.z; o.w = c.w + o.w;
+					for (int g = 0; g < 8; ++g)
+						st4[lane * 8 + (g ^ (lane & 7))] = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+					__syncwarp();
+					const int g = lane & 7;
+#pragma unroll
+					for (int k = 0; k < 8; ++k) {
+						const int rr = 4 * k + (lane >> 3);
+						const int grow = mt * kBM + quad * 32 + rr;
+						float4 o = st4[rr * 8 + (g ^ (rr & 7))];
+						if (grow < p.M) {
+							float4* dst = reinterpret_cast<float4*>(cbase + (long long)grow * p.ldc + gn0) + g;
+							if (p.accumulate) {
+								const float4 c = *dst;
+								o.x = c.x + o.x; o.y = c.y + o.y; o.z = c.z + o.z; o.w = c.w + o.w;
+							}
+							*dst = o;
 						}
-						c4[j] = o;
 					}
+					__syncwarp();                   // the tile is read before the next chunk is written
 				} else {
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {
@@ -532,7 +552,6 @@ __global__ void zero_fill_kernel(float* c, long long ldc, long long s_outer, lon
 
 inline long long round_up(long long x, long long a) { return (x + a - 1) / a * a; }
 
-// Column tile: the widest of 256 / 128 / 64 whose padding waste is within 12.5 % of the least.
 // Tile width. A tile's time is its MMA instruction count (the same for every width) times the cost of
 // one tf32 instruction, measured at about 44 + 0.38 N cycles, and the persistent grid works through
 // the tiles in waves of one per SM: the width with the fewest waves x instruction cost wins, a
