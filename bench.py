@@ -354,6 +354,28 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     if peer is not None:
         peer.close()              # unmapped on every rank before GPU 0 may free its C
 
+    # the plain-TF32 mode on the same operands, reported beside the 3xTF32 headline (N = 1)
+    tf32_mode = None
+    if world == 1 and mode == nnb.MATH_FP32X3:
+        def gemm_tf32():
+            nnb.sgemm(False, False, rows, size, size, a, size, b, size, c, size, False, math_mode=nnb.MATH_TF32)
+        for _ in range(3):
+            gemm_tf32()
+        torch.cuda.synchronize()
+        nnb.trace_reset()
+        nnb.trace_enable(True)
+        e0.record()
+        for _ in range(50):
+            gemm_tf32()
+        e1.record()
+        torch.cuda.synchronize()
+        nnb.trace_enable(False)
+        t_ms, t_n = nnb.trace_query(nnb.TRACE_GEMM)
+        tf32_step = e0.elapsed_time(e1) / 50
+        tf32_mode = {"value": 2.0 * rows * size * size / (tf32_step * 1e-3) / 1e12, "unit": UNIT,
+                     "ms_per_step": tf32_step, "kernel_ms": t_ms / max(t_n, 1),
+                     "kernel_tflops": 2.0 * rows * size * size / (t_ms / max(t_n, 1) * 1e-3) / 1e12}
+
     # cuBLAS TF32 on the same operands: a measured TF32 tensor-core reference point (rank 0, N = 1)
     cublas_tf32 = None
     if world == 1:
@@ -411,6 +433,11 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
                      "cublas_tf32_tflops": cublas_tf32},
         "pack_ms_per_step": pack_ms_max,
         "ms_per_step_compute_only": comp.item(),
+        "tf32_mode": None if tf32_mode is None else dict(tf32_mode, roofline={
+            "bound": "tensor", "achieved": tf32_mode["kernel_tflops"], "peak": bf16_peak / 2.0, "unit": UNIT,
+            "frac": tf32_mode["kernel_tflops"] / (bf16_peak / 2.0),
+            "peak_basis": f"{peaks['source']} dense bf16 {peak_kind} {bf16_peak} TFLOP/s / 2 (TF32 rate)",
+            "cublas_tf32_tflops": cublas_tf32}),
         "gather": None if world == 1 else (
             "fused: each rank's GEMM epilogue stores its tiles into GPU 0's C through CUDA IPC peer memory"
             if peer is not None else "NCCL gather after the GEMM"),
