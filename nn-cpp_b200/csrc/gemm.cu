@@ -742,42 +742,58 @@ namespace gemm {
 // the device, the grid or the number of GPUs. A row of C therefore gets the same sequence of
 // operations however many rows the call has, which keeps row-sharded products (and the data-parallel
 // training step) bitwise identical at any GPU count.
+// Pieces are at least 1024 deep and at least n deep (the partial slabs, pieces x m x n, stay small next
+// to the operands): a 512-wide weight gradient summed over 4096 rows (one shard of a data-parallel
+// batch) is cut into 4 pieces, so it fills the GPU even when a rank computes it for a single shard.
 constexpr long long kCutMinDepth = 1024;
 constexpr long long kCutMaxPieces = 32;
 
 static int depth_pieces(const GemmDesc& d) {
 	if (d.batch_inner != 1 || d.epi.bias_mode != kBiasNone || d.epi.act != kActNone) return 1;
-	const long long p = std::min<long long>(kCutMaxPieces, d.k / std::max<long long>(kCutMinDepth, 4 * d.n));
+	const long long p = std::min<long long>(kCutMaxPieces, d.k / std::max<long long>(kCutMinDepth, d.n));
 	return p >= 2 ? (int)p : 1;
 }
 
 // c_e = (accumulate ? c_e : 0) + (((part_e0 + part_e1) + part_e2) + ...), part_ep an m x n slab;
 // entry e = blockIdx.y, c_e = c + e * sc
+__device__ __forceinline__ float4 f4_add(float4 a, float4 b) {
+	return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w);
+}
+
+__device__ __forceinline__ float depth_v(float x) { return x; }
+__device__ __forceinline__ float4 depth_v(float4 x) { return x; }
+__device__ __forceinline__ float depth_add(float a, float b) { return a + b; }
+__device__ __forceinline__ float4 depth_add(float4 a, float4 b) { return f4_add(a, b); }
+__device__ __forceinline__ float depth_zero_fix(float a) { return a + 0.0f; }
+__device__ __forceinline__ float4 depth_zero_fix(float4 a) { return f4_add(a, make_float4(0.0f, 0.0f, 0.0f, 0.0f)); }
+
+// c_e = (accumulate ? c_e : 0) + (((part_e0 + part_e1) + part_e2) + ...), part_ep an m x n slab;
+// entry e = blockIdx.z, c_e = c + e * sc. V = float or float4 (4 consecutive columns, when n, ldc and
+// the pointers allow). Up to 8 pieces' loads are issued before their adds, which stay in piece order.
+template <typename V>
 __global__ void depth_sum_kernel(const float* __restrict__ part, int pieces, long long m, long long n,
 		float* __restrict__ c, long long ldc, long long sc, int accumulate) {
-	const long long mn = m * n;
+	constexpr int W = sizeof(V) / sizeof(float);
+	const long long mn = m * n, nv = n / W;
 	part += (long long)blockIdx.z * pieces * mn;
 	c += (long long)blockIdx.z * sc;
-	// rows over grid.y, columns over grid.x: no per-element division; the pieces are summed in
-	// order, their loads issued ahead of the adds
 	for (long long i = blockIdx.y; i < m; i += gridDim.y) {
-		for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x) {
-			const float* src = part + i * n + j;
-			float v[8];
-			float acc = 0.0f;
-			int p = 0;
-			for (; p + 8 <= pieces; p += 8) {
+		for (long long jv = blockIdx.x * (long long)blockDim.x + threadIdx.x; jv < nv;
+				jv += (long long)gridDim.x * blockDim.x) {
+			const V* src = reinterpret_cast<const V*>(part + i * n) + jv;
+			const long long stride = mn / W;                 // one slab, in V units
+			V acc{};
+			for (int p = 0; p < pieces; p += 8) {
+				V v[8];
 #pragma unroll
-				for (int u = 0; u < 8; ++u) v[u] = __ldg(src + (long long)(p + u) * mn);
+				for (int u = 0; u < 8; ++u)
+					if (p + u < pieces) v[u] = __ldg(src + (long long)(p + u) * stride);
 #pragma unroll
-				for (int u = 0; u < 8; ++u) acc = (p + u == 0) ? v[u] : acc + v[u];
+				for (int u = 0; u < 8; ++u)
+					if (p + u < pieces) acc = (p + u == 0) ? depth_v(v[u]) : depth_add(acc, v[u]);
 			}
-			for (; p < pieces; ++p) {
-				const float x = __ldg(src + (long long)p * mn);
-				acc = p == 0 ? x : acc + x;
-			}
-			float* dst = c + i * ldc + j;
-			*dst = accumulate ? *dst + acc : acc + 0.0f;
+			V* dst = reinterpret_cast<V*>(c + i * ldc) + jv;
+			*dst = accumulate ? depth_add(*dst, acc) : depth_zero_fix(acc);
 		}
 	}
 }
@@ -822,12 +838,19 @@ static nnb_status gemm_depth_cut(cudaStream_t s, const DeviceState* dev, const G
 			t.sc_outer = (long long)pieces * mn;
 			if ((st = gemm_direct(s, dev, t)) != NNB_OK) break;
 		}
-		const unsigned bx = (unsigned)std::min<long long>((d.n + 255) / 256, 64);
+		const bool vec = d.n % 4 == 0 && d.ldc % 4 == 0 && d.sc_outer % 4 == 0 &&
+			(reinterpret_cast<uintptr_t>(d.c) & 15) == 0;
+		const long long nv = vec ? d.n / 4 : d.n;
+		const unsigned bx = (unsigned)std::min<long long>((nv + 255) / 256, 64);
 		const unsigned by = (unsigned)std::min<long long>(d.m, std::max<long long>(1, (148 * 16) / ((long long)bx * E)));
 		{
 			TraceScope ts(s, kTraceAux);
-			depth_sum_kernel<<<dim3(bx, std::max(by, 1u), (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc,
-				d.sc_outer, d.accumulate);
+			if (vec)
+				depth_sum_kernel<float4><<<dim3(bx, std::max(by, 1u), (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n,
+					d.c, d.ldc, d.sc_outer, d.accumulate);
+			else
+				depth_sum_kernel<float><<<dim3(bx, std::max(by, 1u), (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n,
+					d.c, d.ldc, d.sc_outer, d.accumulate);
 		}
 		st = cuda_status(cudaGetLastError(), "depth sum launch");
 	} while (0);

@@ -98,14 +98,18 @@ nnb_status colsum_grouped(cudaStream_t s, const float* g, long long rows, long l
 	void* ws = nullptr;
 	NNB_TRY(scratch_alloc(&ws, groups * chunks * cols * sizeof(float), s));
 	float* partial = static_cast<float*>(ws);
-	const unsigned bx = (unsigned)((cols + 127) / 128);
+	// The chunk partition (the summation order) is fixed by the row count; the block width only sets how
+	// many blocks share the SMs: 32 columns per block when the columns alone would not fill them (one
+	// shard's 512 columns x 16 chunks become 256 blocks), 128 for wide sums (the shard-gradient sum)
+	const unsigned tpb = cols * chunks * groups >= 148LL * 1024 ? 128u : 32u;
+	const unsigned bx = (unsigned)((cols + tpb - 1) / tpb);
 	{
 		TraceScope ts(s, kTraceRowwise);
-		colsum_partial_kernel<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 128, 0, s>>>(g, rows, cols, partial);
+		colsum_partial_kernel<<<dim3(bx, (unsigned)chunks, (unsigned)groups), tpb, 0, s>>>(g, rows, cols, partial);
 	}
 	{
 		TraceScope ts(s, kTraceRowwise);
-		colsum_final_kernel<<<dim3(bx, (unsigned)groups), 128, 0, s>>>(partial, chunks, cols, out, out_stride, first);
+		colsum_final_kernel<<<dim3(bx, (unsigned)groups), tpb, 0, s>>>(partial, chunks, cols, out, out_stride, first);
 	}
 	nnb_status st = cuda_status(cudaGetLastError(), "column sum launch");
 	nnb_status st2 = scratch_free(ws, s);

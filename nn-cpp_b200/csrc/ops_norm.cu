@@ -322,15 +322,16 @@ nnb_status nnb_layernorm_bwd_grouped(void* stream, size_t R, size_t D, size_t gr
 		NNB_TRY(nnb::scratch_alloc(&ws, 2 * groups * chunks * D * sizeof(float), s));
 		float* pg = static_cast<float*>(ws);
 		float* pb = pg + groups * chunks * D;
-		const unsigned bx = (unsigned)((D + 127) / 128);
+		// 32 columns per block (the chunking, and so every sum's order, depends only on the rows)
+		const unsigned bx = (unsigned)((D + 31) / 32);
 		{
 			nnb::TraceScope ts(s, nnb::kTraceRowwise);
-			nnb::layernorm_bwd_param_partial<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 128, 0, s>>>(g, x, mean,
+			nnb::layernorm_bwd_param_partial<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 32, 0, s>>>(g, x, mean,
 				inv_std, Rg, (int)D, pg, pb);
 		}
 		{
 			nnb::TraceScope ts(s, nnb::kTraceRowwise);
-			nnb::layernorm_bwd_param_final<<<dim3(bx, (unsigned)groups), 128, 0, s>>>(pg, pb, chunks, (int)D, dgamma,
+			nnb::layernorm_bwd_param_final<<<dim3(bx, (unsigned)groups), 32, 0, s>>>(pg, pb, chunks, (int)D, dgamma,
 				dgamma_stride ? (long long)dgamma_stride : (long long)D, dgamma_first, dbeta,
 				dbeta_stride ? (long long)dbeta_stride : (long long)D, dbeta_first);
 		}
