@@ -59,6 +59,8 @@ _SIGS = {
     "nnb_launch_count": ([], _c.c_longlong),
     "nnb_sgemm": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i], _i),
     "nnb_sgemm_ex": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
+    "nnb_sgemm_host": ([_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i], _i),
+    "nnb_sgemm_host_async": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
     "nnb_sgemm_strided_batched": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz,
                                    _sz, _i, _i], _i),
     "nnb_sgemm_noalloc": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
@@ -235,6 +237,27 @@ def sgemm(trans_a: bool, trans_b: bool, m: int, n: int, k: int, a, lda: int, b, 
         st = lib().nnb_sgemm_ex(s, int(trans_a), int(trans_b), m, n, k, _ptr(a), lda, _ptr(b), ldb, _ptr(c),
                                 ldc, int(accumulate), math_mode)
     check(st)
+
+
+def sgemm_host(trans_a: bool, trans_b: bool, m: int, n: int, k: int, a, lda: int, b, ldb: int, c, ldc: int,
+               accumulate: bool, math_mode: int | None = None, stream=None, blocking: bool = True) -> None:
+    """nn::kernels::sgemm on host buffers (numpy arrays or CPU torch tensors, page-locked for full
+    copy speed) through nnb_sgemm_host[_async]: copies, pipelined GEMM bands and copy-back inside.
+    With blocking=False the call is ordered on `stream` (the current one by default) and returns at
+    once; the host buffers must stay alive until that stream reaches the end of the call."""
+    def addr(x):
+        if x is None:
+            return None
+        if isinstance(x, int):
+            return x
+        return x.ctypes.data if hasattr(x, "ctypes") else x.data_ptr()
+    mode = get_math_mode() if math_mode is None else math_mode
+    s = _stream_ptr(stream)
+    check(lib().nnb_sgemm_host_async(s, int(trans_a), int(trans_b), m, n, k, addr(a), lda, addr(b), ldb, addr(c), ldc,
+                                     int(accumulate), mode))
+    if blocking:
+        import torch
+        torch.cuda.current_stream().synchronize() if stream is None else stream.synchronize()
 
 
 def matmul(a, b, trans_a: bool = False, trans_b: bool = False, stream=None):

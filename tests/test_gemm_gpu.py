@@ -221,3 +221,38 @@ def test_depth_cut_small_output_long_depth(cuda, mode, rel):
     assert np.array_equal(np.isnan(got), np.isnan(loop))
     inf = np.isinf(loop)
     assert np.array_equal(got[inf], loop[inf])
+
+
+@pytest.mark.parametrize("mode", [nnb.MATH_FP32X3, nnb.MATH_TF32])
+@pytest.mark.parametrize("ta,tb,m,n,k,pad,acc", [
+    (0, 0, 3000, 520, 300, 0, 0),       # several bands, partial last band
+    (1, 0, 1400, 257, 129, 3, 1),       # transposed A (column bands of its storage), strides, accumulate
+    (0, 1, 77, 1030, 700, 1, 0),        # one band
+    (1, 1, 2100, 64, 2048, 2, 1),       # deep k (depth cut inside each band)
+])
+def test_sgemm_host_bitwise_equal_to_device(cuda, mode, ta, tb, m, n, k, pad, acc):
+    """nnb_sgemm_host (host buffers, banded pipeline of copies and GEMMs) gives the device entry's bits
+    on the same operands, padding columns of C untouched."""
+    torch = cuda
+    p = orc.Problem(ta, tb, m, n, k, pad, 7000 + m)
+    want = run_gpu(torch, p, acc, mode)
+    c_host = p.c.copy()
+    nnb.sgemm_host(ta, tb, m, n, k, p.a, p.lda, p.b, p.ldb, c_host, p.ldc, acc, math_mode=mode)
+    assert c_host.tobytes() == want.tobytes()
+
+
+def test_sgemm_host_pinned_golden(cuda):
+    """Pinned torch host tensors, and the reference build's golden case of this module."""
+    torch = cuda
+    g = np.load(orc.HERE.parent / "tests" / "golden" / "gemm_golden.npz")
+    ta, tb, m, n, k, pad, seed, acc = (int(v) for v in g["cases"][1])
+    a = torch.from_numpy(g["a1"]).pin_memory()
+    b = torch.from_numpy(g["b1"]).pin_memory()
+    c = torch.from_numpy(g["c1"].copy()).pin_memory()
+    lda = (m if ta else k) + pad
+    ldb = (k if tb else n) + pad
+    ldc = n + pad
+    nnb.sgemm_host(ta, tb, m, n, k, a, lda, b, ldb, c, ldc, acc)
+    got = c.numpy().reshape(-1)[: m * ldc].reshape(m, ldc)[:, :n].astype(np.float64)
+    ref = g["loop1"].reshape(-1)[: m * ldc].reshape(m, ldc)[:, :n].astype(np.float64)
+    assert np.abs(got - ref).max() <= 1e-5 * max(1.0, np.abs(ref).max()) * np.sqrt(k)
