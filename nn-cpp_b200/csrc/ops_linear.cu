@@ -64,6 +64,26 @@ __global__ void colsum_partial_kernel(const float* __restrict__ g, long long row
 	partial[(z * chunks + c) * cols + j] = s;
 }
 
+// The same partials for tall, narrow sums (one shard's bias gradient: 4096 rows x 512 columns): a
+// block of 256 threads stages its chunk's rows x 32 columns in shared memory with every load in
+// flight, then warp 0 sums each column serially in row order from +0 -- the same additions in the
+// same order as colsum_partial_kernel, without its per-thread latency chain.
+__global__ void __launch_bounds__(256) colsum_partial_staged_kernel(const float* __restrict__ g, long long rows,
+		long long cols, float* __restrict__ partial) {
+	__shared__ float tile[kColChunk][32];
+	const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+	const long long j = blockIdx.x * 32LL + lane;
+	const long long c = blockIdx.y, chunks = gridDim.y, z = blockIdx.z;
+	const long long r0 = c * kColChunk, n = min(rows - r0, (long long)kColChunk);
+	const float* gz = g + z * rows * cols;
+	for (int rr = warp; rr < n; rr += 8) tile[rr][lane] = j < cols ? __ldg(gz + (r0 + rr) * cols + j) : 0.0f;
+	__syncthreads();
+	if (warp != 0 || j >= cols) return;
+	float s = 0.0f;
+	for (int rr = 0; rr < n; ++rr) s += tile[rr][lane];
+	partial[(z * chunks + c) * cols + j] = s;
+}
+
 // out[z*out_stride + j] = (first ? 0 : out[..]) + sum_c partial[z][c][j] (serial from +0 in chunk order).
 __global__ void colsum_final_kernel(const float* __restrict__ partial, long long chunks, long long cols,
 		float* __restrict__ out, long long out_stride, int first) {
@@ -105,7 +125,11 @@ nnb_status colsum_grouped(cudaStream_t s, const float* g, long long rows, long l
 	const unsigned bx = (unsigned)((cols + tpb - 1) / tpb);
 	{
 		TraceScope ts(s, kTraceRowwise);
-		colsum_partial_kernel<<<dim3(bx, (unsigned)chunks, (unsigned)groups), tpb, 0, s>>>(g, rows, cols, partial);
+		if (rows >= 64)          // tall sums: staged through shared memory (same order, loads in flight)
+			colsum_partial_staged_kernel<<<dim3((unsigned)((cols + 31) / 32), (unsigned)chunks, (unsigned)groups), 256, 0,
+				s>>>(g, rows, cols, partial);
+		else
+			colsum_partial_kernel<<<dim3(bx, (unsigned)chunks, (unsigned)groups), tpb, 0, s>>>(g, rows, cols, partial);
 	}
 	{
 		TraceScope ts(s, kTraceRowwise);

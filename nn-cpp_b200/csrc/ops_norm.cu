@@ -121,6 +121,45 @@ __global__ void layernorm_bwd_param_partial(const float* __restrict__ g, const f
 	pb[(z * chunks + c) * D + j] = sb;
 }
 
+// The same partials with the chunk staged in shared memory (256 threads keep every load in flight),
+// then warp 0 accumulates each column serially in row order: the additions and their order are those
+// of layernorm_bwd_param_partial.
+__global__ void __launch_bounds__(256) layernorm_bwd_param_partial_staged(const float* __restrict__ g,
+		const float* __restrict__ x, const float* __restrict__ mean, const float* __restrict__ inv_std, long long R, int D,
+		float* __restrict__ pg, float* __restrict__ pb) {
+	constexpr int kPass = kChunk / 2;                // rows staged at a time (shared memory < 48 KB)
+	__shared__ float tg[kPass][32], tx[kPass][32], tm[kPass], ti[kPass];
+	const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+	const int j = blockIdx.x * 32 + lane;
+	const long long c = blockIdx.y, chunks = gridDim.y, z = blockIdx.z;
+	const long long r0 = z * R + c * kChunk;
+	const int n = (int)min(R - c * kChunk, (long long)kChunk);
+	float sg = 0.0f, sb = 0.0f;
+	for (int p0 = 0; p0 < n; p0 += kPass) {
+		const int m = min(kPass, n - p0);
+		for (int rr = warp; rr < m; rr += 8) {
+			tg[rr][lane] = j < D ? __ldg(g + (r0 + p0 + rr) * D + j) : 0.0f;
+			tx[rr][lane] = j < D ? __ldg(x + (r0 + p0 + rr) * D + j) : 0.0f;
+		}
+		for (int rr = threadIdx.x; rr < m; rr += 256) {
+			tm[rr] = __ldg(mean + r0 + p0 + rr);
+			ti[rr] = __ldg(inv_std + r0 + p0 + rr);
+		}
+		__syncthreads();
+		if (warp == 0) {                              // serial in row order, continuing across the passes
+			for (int rr = 0; rr < m; ++rr) {
+				const float gv = tg[rr][lane];
+				sg += gv * ((tx[rr][lane] - tm[rr]) * ti[rr]);
+				sb += gv;
+			}
+		}
+		__syncthreads();                              // the pass is read before the next one is written
+	}
+	if (warp != 0 || j >= D) return;
+	pg[(z * chunks + c) * D + j] = sg;
+	pb[(z * chunks + c) * D + j] = sb;
+}
+
 __global__ void layernorm_bwd_param_final(const float* __restrict__ pg, const float* __restrict__ pb,
 		long long chunks, int D, float* __restrict__ dgamma, long long dg_stride, int dg_first,
 		float* __restrict__ dbeta, long long db_stride, int db_first) {
@@ -326,8 +365,12 @@ nnb_status nnb_layernorm_bwd_grouped(void* stream, size_t R, size_t D, size_t gr
 		const unsigned bx = (unsigned)((D + 31) / 32);
 		{
 			nnb::TraceScope ts(s, nnb::kTraceRowwise);
-			nnb::layernorm_bwd_param_partial<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 32, 0, s>>>(g, x, mean,
-				inv_std, Rg, (int)D, pg, pb);
+			if (Rg >= 64)           // tall sums: chunk staged in shared memory (same order, loads in flight)
+				nnb::layernorm_bwd_param_partial_staged<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 256, 0, s>>>(g, x,
+					mean, inv_std, Rg, (int)D, pg, pb);
+			else
+				nnb::layernorm_bwd_param_partial<<<dim3(bx, (unsigned)chunks, (unsigned)groups), 32, 0, s>>>(g, x, mean,
+					inv_std, Rg, (int)D, pg, pb);
 		}
 		{
 			nnb::TraceScope ts(s, nnb::kTraceRowwise);
