@@ -400,6 +400,8 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
             transformer["attention"] = run_attention(10, 3, local_rank)
             transformer["matmul512"] = run_matmul512(local_rank)
             transformer["next_rows"] = run_next_rows(local_rank, with_cpu=not args.no_cpu_baseline)
+        else:
+            transformer["attention"] = run_attention_sharded(10, 3, rank, world, local_rank)
     if rank != 0:
         return
     flops = 2.0 * size ** 3
@@ -687,6 +689,42 @@ def run_attention(steps: int, warmup: int, local_rank: int):
                        "path": "fused (no probability matrix)"},
             "eager_ms": eager, "composed_path_ms": composed_ms, "kernels": kernels,
             "algorithmic_tflops_causal": ATTN_FLOP_PER_STEP / (ms * 1e-3) / 1e12}
+
+
+def run_attention_sharded(steps: int, warmup: int, rank: int, world: int, local_rank: int):
+    """Config 3 on N GPUs: the batch x head units split by samples (32 / N per GPU), O, dQ, dK and dV
+    gathered on GPU 0 (nnb.parallel.ShardedAttention: the backward kernels store dQ / dK / dV there
+    through peer memory, O goes by a peer copy overlapping the backward). Max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from nnb.parallel import ShardedAttention
+
+    dev = torch.device("cuda", local_rank)
+    N, T, D, H = 32, 256, 512, 8
+    sa = ShardedAttention(N, T, D, H, causal=True)
+    g = torch.Generator(device=dev).manual_seed(6 + rank)
+    q, k, v, go = (torch.randn(max(sa.local, 1), T, D, device=dev, generator=g) for _ in range(4))
+    for _ in range(warmup):
+        sa.step(q, k, v, go)
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[local_rank])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        sa.step(q, k, v, go)
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier(device_ids=[local_rank])
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev, dtype=torch.float64)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    sa.close()
+    return {"metric": "causal attention fwd+bwd ms/step", "value": ms.item(), "unit": "ms", "higher_is_better": False,
+            "n_gpus": world, "scaling": "strong",
+            "config": {"workload": "config 3: B32 H8 T256 Dh64 causal, fwd + bwd",
+                       "parallelism": f"samples x{world} ({N // world} per GPU), O / dQ / dK / dV gathered on GPU 0 "
+                                      "(backward epilogues store through peer memory; O by a peer copy)"},
+            "algorithmic_tflops_causal": ATTN_FLOP_PER_STEP / (ms.item() * 1e-3) / 1e12}
 
 
 def run_matmul512(local_rank: int):

@@ -64,6 +64,8 @@ NNB_API int nnb_device_error(void* stream);
 NNB_API nnb_status nnb_ipc_export(const void* ptr, unsigned char* handle, size_t* offset);
 NNB_API nnb_status nnb_ipc_open(const unsigned char* handle, size_t offset, void** ptr);
 NNB_API nnb_status nnb_ipc_close(void* ptr, size_t offset);
+/* bytes from src to dst on `stream` by the copy engines (device, peer-mapped or host memory). */
+NNB_API nnb_status nnb_copy_async(void* stream, void* dst, const void* src, size_t bytes);
 
 /* ---- tracing (the counterpart of the reference bench's per-op timing, apps/bench/runner.cpp:29-96) */
 

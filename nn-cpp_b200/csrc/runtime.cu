@@ -172,6 +172,13 @@ nnb_status nnb_ipc_open(const unsigned char* handle, size_t offset, void** ptr) 
 	return NNB_OK;
 }
 
+nnb_status nnb_copy_async(void* stream, void* dst, const void* src, size_t bytes) {
+	if (bytes == 0) return NNB_OK;
+	if (!dst || !src) return nnb::fail(NNB_ERR_INVALID, "copy_async: null pointer");
+	NNB_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
+	return NNB_OK;
+}
+
 nnb_status nnb_ipc_close(void* ptr, size_t offset) {
 	if (!ptr) return NNB_OK;
 	NNB_CUDA_TRY(cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset));

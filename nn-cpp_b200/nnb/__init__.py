@@ -53,6 +53,7 @@ _SIGS = {
     "nnb_ipc_export": ([_p, _p, _c.POINTER(_sz)], _i),
     "nnb_ipc_open": ([_p, _sz, _c.POINTER(_p)], _i),
     "nnb_ipc_close": ([_p, _sz], _i),
+    "nnb_copy_async": ([_p, _p, _p, _sz], _i),
     "nnb_trace_enable": ([_i], None),
     "nnb_trace_reset": ([], None),
     "nnb_trace_query": ([_i, _c.POINTER(_c.c_double), _c.POINTER(_c.c_longlong)], _i),

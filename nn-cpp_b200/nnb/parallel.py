@@ -109,3 +109,67 @@ class PeerBuffer:
             check(lib().nnb_ipc_close(self.ptr, self.offset))
             self._mapped = False
         dist.barrier(group=self.group, device_ids=[torch.cuda.current_device()])
+
+
+class ShardedAttention:
+    """Multi-head attention forward + backward of a batch split by samples over the ranks, with O, dQ,
+    dK and dV gathered on rank `owner` (the batch x head partition of the attention workload).
+
+    Each rank holds q, k, v and the upstream gradient for its samples [n0, n1) of the global batch of
+    `batch` samples. The owner's full-size O, dQ, dK and dV are PeerBuffers: the backward kernels'
+    epilogues store this rank's dQ / dK / dV tiles straight into them over NVLink, and O (written
+    locally, since the backward reads it) is copied to the owner by a peer copy that overlaps the
+    backward. Every (sample, head) is computed exactly as on one GPU, so the gathered results are
+    bitwise the one-GPU ones. Head size 64 runs the fused kernels.
+    """
+
+    def __init__(self, batch: int, T: int, D: int, heads: int, causal: bool = True, owner: int = 0, group=None,
+                 device=None):
+        import torch
+        import torch.distributed as dist
+
+        from . import lib
+
+        if not lib().nnb_flash_attention_supported(D, heads):
+            raise ValueError("ShardedAttention: the fused kernels need head size 64")
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.batch, self.T, self.D, self.heads, self.causal = batch, T, D, heads, causal
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.bands = row_bands(batch, self.world, align=1)
+        self.n0, self.n1 = self.bands[self.rank]
+        self.local = self.n1 - self.n0
+        self.out, self.dq, self.dk, self.dv = (PeerBuffer((batch, T, D), owner, group, self.device) for _ in range(4))
+        self.o_local = torch.empty(max(self.local, 1), T, D, device=self.device)
+        self.stats = torch.empty(max(self.local, 1), heads, T, 2, device=self.device)
+        self.copy_stream = torch.cuda.Stream(self.device)
+        self.group = group
+
+    def _at(self, buf: "PeerBuffer") -> int:
+        return buf.ptr + self.n0 * self.T * self.D * 4
+
+    def step(self, q, k, v, go) -> None:
+        """Forward and backward of this rank's samples (q, k, v, go: [local, T, D] on this device),
+        enqueued on the current stream; the owner's buffers hold them once every rank's stream has
+        passed this point (synchronise and barrier before reading)."""
+        import torch
+
+        from . import check, lib
+
+        if self.local == 0:
+            return
+        L, s = lib(), torch.cuda.current_stream(self.device)
+        N, T, D, H = self.local, self.T, self.D, self.heads
+        check(L.nnb_flash_attention_fwd(s.cuda_stream, N, T, T, D, H, q.data_ptr(), k.data_ptr(), v.data_ptr(), None,
+                                        int(self.causal), self.o_local.data_ptr(), self.stats.data_ptr()))
+        # O to the owner on the copy stream (a copy-engine peer copy) while the backward runs
+        self.copy_stream.wait_stream(s)
+        check(L.nnb_copy_async(self.copy_stream.cuda_stream, self._at(self.out), self.o_local.data_ptr(), N * T * D * 4))
+        check(L.nnb_flash_attention_bwd(s.cuda_stream, N, T, T, D, H, go.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                        v.data_ptr(), self.o_local.data_ptr(), self.stats.data_ptr(), None,
+                                        int(self.causal), self._at(self.dq), 1, self._at(self.dk), 1,
+                                        self._at(self.dv), 1))
+        s.wait_stream(self.copy_stream)
+
+    def close(self) -> None:
+        for b in (self.out, self.dq, self.dk, self.dv):
+            b.close()

@@ -193,3 +193,58 @@ def test_data_parallel_step_bitwise_equal_to_single_gpu(cuda, tmp_path):
     eq = np.load(tmp_path / "dp_eq.npy")
     assert bool(eq[0]), "eager data-parallel steps differ from one GPU"
     assert bool(eq[1]), "graph-replayed data-parallel step differs from one GPU"
+
+
+def _attn_worker(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import nnb
+    from nnb.parallel import ShardedAttention
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        B, T, D, H = 6, 130, 128, 2                  # 6 samples over 2-4 ranks: unequal shares
+        g = torch.Generator(device="cuda").manual_seed(21)
+        q, k, v, go = (torch.randn(B, T, D, device="cuda", generator=g) for _ in range(4))
+        sa = ShardedAttention(B, T, D, H, causal=True)
+        n0, n1 = sa.n0, sa.n1
+        sa.step(q[n0:n1].contiguous(), k[n0:n1].contiguous(), v[n0:n1].contiguous(), go[n0:n1].contiguous())
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[rank])
+        if rank == 0:
+            L, s = nnb.lib(), torch.cuda.current_stream().cuda_stream
+            o = torch.empty(B, T, D, device="cuda")
+            st = torch.empty(B, H, T, 2, device="cuda")
+            dq, dk, dv = (torch.empty(B, T, D, device="cuda") for _ in range(3))
+            nnb.check(L.nnb_flash_attention_fwd(s, B, T, T, D, H, q.data_ptr(), k.data_ptr(), v.data_ptr(), None, 1,
+                                                o.data_ptr(), st.data_ptr()))
+            nnb.check(L.nnb_flash_attention_bwd(s, B, T, T, D, H, go.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                                v.data_ptr(), o.data_ptr(), st.data_ptr(), None, 1, dq.data_ptr(), 1,
+                                                dk.data_ptr(), 1, dv.data_ptr(), 1))
+            torch.cuda.synchronize()
+            eq = [bool(torch.equal(a.tensor, b)) for a, b in ((sa.out, o), (sa.dq, dq), (sa.dk, dk), (sa.dv, dv))]
+            np.save(os.path.join(out_dir, "attn_eq.npy"), np.array(eq))
+        dist.barrier(device_ids=[rank])
+        sa.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_sharded_attention_bitwise_equal_to_single_gpu(cuda, tmp_path):
+    """Attention forward + backward split by samples over 2-4 GPUs, O / dQ / dK / dV gathered on GPU 0
+    (dQ / dK / dV stored there by the backward kernels through peer memory, O by a peer copy): the
+    one-GPU results, bit for bit."""
+    torch = cuda
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    mp.start_processes(_attn_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+                       start_method="spawn")
+    assert np.load(tmp_path / "attn_eq.npy").all()
