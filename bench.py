@@ -338,6 +338,8 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     b_h = b.cpu().pin_memory()
     c_h = torch.empty(rows, size).pin_memory()
     e2e_steps = max(1, args.e2e_steps)
+    for _ in range(2):            # first calls allocate the entry's device buffers and streams: untimed
+        nnb.sgemm_host(False, False, rows, size, size, a_h, size, b_h, size, c_h, size, False, math_mode=mode)
     barrier()
     torch.cuda.synchronize()
     e0.record()

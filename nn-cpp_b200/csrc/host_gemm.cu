@@ -107,9 +107,12 @@ nnb_status sgemm_host(cudaStream_t caller, bool blocking, int ta, int tb, size_t
 	NNB_TRY(grow(&x.da, &x.cap_a, m * k));
 	NNB_TRY(grow(&x.db, &x.cap_b, k * n));
 	NNB_TRY(grow(&x.dc, &x.cap_c, m * n));
-	const size_t tiles = (m + 127) / 128;
-	const size_t bands = std::min<size_t>(kMaxBands, std::max<size_t>(1, std::min<size_t>(tiles, m / 1024 + 1)));
-	const size_t per = (tiles + bands - 1) / bands * 128;                     // rows per band, whole tiles
+	// band height: about two waves of 128 x 256 tiles on the SMs (an 8192-wide C: 9 row tiles, 288
+	// tiles, 97 % of two waves), at most kMaxBands bands
+	const size_t tiles = (m + 127) / 128, tiles_n = (n + 255) / 256;
+	size_t per_tiles = std::max<size_t>(1, (size_t)(2 * dev->sm_count) / tiles_n);
+	per_tiles = std::max(per_tiles, (tiles + kMaxBands - 1) / kMaxBands);
+	const size_t per = per_tiles * 128;                                         // rows per band, whole tiles
 	if (k > 0) {
 		if (tb) NNB_TRY(h2d(x.db, b, n, k, ldb, x.copy));
 		else NNB_TRY(h2d(x.db, b, k, n, ldb, x.copy));
