@@ -9,8 +9,6 @@ it gives what the allocating entry point (nnb_sgemm_ex) gives, within the GEMM t
 This file is named to be collected last, so a run that stops at the first failure has run every
 other test before it; it also passes alone in a fresh process.
 """
-import ctypes
-
 import numpy as np
 import pytest
 
