@@ -4,8 +4,9 @@
 One "step" is one M = N = K = 8192 fp32 GEMM C = A.B (A, B ~ N(0,1)) in 3xTF32 mode through the
 library's C ABI (nnb_sgemm: pack/split kernels + the tcgen05 GEMM kernel). With N GPUs
 (torchrun, one rank per GPU) the 8192 rows of A are split into N contiguous bands, every rank
-holds all of B, computes its band of C, and the bands are gathered to GPU 0 with NCCL each step
-(total work fixed: strong scaling). Inputs are 256 MiB per operand, larger than the 126 MB L2,
+holds all of B, computes its band of C, and each rank's GEMM epilogue stores its band into GPU 0's C
+through peer memory (`--gather nccl`: an NCCL gather after the GEMM instead) every step (total work
+fixed: strong scaling). Inputs are 256 MiB per operand, larger than the 126 MB L2,
 so no flush is needed between steps.
 
 Keys beyond the base contract:
@@ -15,7 +16,7 @@ Keys beyond the base contract:
   cpu_baseline  the reference's own AVX2 sgemm (built from its sources into oracle/_ref) on all
                 host cores, on a 1024-row band of the same problem;
   e2e           the same GEMM through the public API from pinned host buffers: H2D of A (band)
-                and B, the GEMM, D2H of C, every step.
+                and B, the GEMM, D2H of C, every step; `pcie_floor` times the same copies alone.
 `python bench.py --impl reference` times the reference's CPU sgemm alone (see run_reference).
 """
 from __future__ import annotations
@@ -353,6 +354,34 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
     e2e = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    # the PCIe floor of e2e: the same bytes copied in (A, B) and out (C) and nothing else, the two
+    # directions concurrent as inside the call (a_h and b_h hold a's and b's values: a no-op rewrite)
+    c_dev = torch.empty(rows, size, device=dev)
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+
+    def host_copies():
+        cur = torch.cuda.current_stream()
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        with torch.cuda.stream(s_in):
+            b.copy_(b_h, non_blocking=True)
+            a.copy_(a_h, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            c_h.copy_(c_dev, non_blocking=True)
+        cur.wait_stream(s_in)
+        cur.wait_stream(s_out)
+
+    host_copies()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        host_copies()
+    e1.record()
+    torch.cuda.synchronize()
+    pcie = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(pcie, op=dist.ReduceOp.MAX)
+    del c_dev
     if peer is not None:
         peer.close()              # unmapped on every rank before GPU 0 may free its C
 
@@ -451,7 +480,10 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
         "e2e": {"value": flops / (e2e.item() * 1e-3) / 1e12, "unit": UNIT,
                 "h2d_bytes_per_step": int((rows * size + size * size) * 4 * world),
                 "d2h_bytes_per_step": int(rows * size * 4 * world),
-                "api": "nnb_sgemm_host_async (host buffers, page-locked): copies in, banded GEMMs, copy back"},
+                "api": "nnb_sgemm_host_async (host buffers, page-locked): copies in, banded GEMMs, copy back",
+                "pcie_floor": {"what": "the same bytes copied in and out concurrently, no GEMM",
+                               "ms_per_step": pcie.item(), "e2e_ms_per_step": e2e.item(),
+                               "frac": pcie.item() / e2e.item()}},
         "gpu_launches": int(launches),
         "clocks": clk,
     }

@@ -72,6 +72,7 @@ struct Params {
 	long long ld_aux, s_aux_outer, s_aux_inner;
 	// exact IEEE handling of non-finite inputs
 	const int* any_nonfinite;
+	const int* any_b;                // B's any-flag (the same word unless B came packed)
 	const int* flags_a;              // [a_batches][Mp]
 	const int* flags_b;              // [b_batches][Np]
 	const float* A;
@@ -436,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 			float* cbase = p.C + batch_offset(bi, p.batch_inner, p.sc_outer, p.sc_inner);
 			float* crow = cbase + (long long)gm * p.ldc;
 			const long long aux_row = batch_offset(bi, p.batch_inner, p.s_aux_outer, p.s_aux_inner) + (long long)gm * p.ld_aux;
-			const bool fix = *p.any_nonfinite != 0;
+			const bool fix = (*p.any_nonfinite | *p.any_b) != 0;
 			const bool row_bad = fix && row_ok && p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0;
 			const int* fcol = p.flags_b + (long long)(p.b_batched ? bi : 0) * p.Np;
 			const float row_bias = (p.bias_mode == kBiasRow && row_ok) ? p.bias[gm] : 0.0f;
@@ -615,8 +616,10 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 			pl.rows_a, pl.rows_b);
 	if (pl.entries > 65535) return fail(NNB_ERR_UNSUPPORTED, "gemm: more than 65535 batch entries");
 	if (pl.entries * (pl.Mp / kBM) * (pl.Np / pl.bn) > INT32_MAX) return fail(NNB_ERR_UNSUPPORTED, "gemm: too many tiles");
-	const size_t bytes_a = (size_t)pl.rows_a * kBK * 4, bytes_b = (size_t)pl.rows_b * kBK * 4;
-	pl.flag_ints = (size_t)(pl.a_entries * pl.Mp + pl.b_entries * pl.Np + 1);
+	// a B that arrives packed (GemmDesc::packed_b) has its panels and flags outside the workspace
+	const bool pre_b = d.packed_b != nullptr;
+	const size_t bytes_a = (size_t)pl.rows_a * kBK * 4, bytes_b = pre_b ? 0 : (size_t)pl.rows_b * kBK * 4;
+	pl.flag_ints = (size_t)(pl.a_entries * pl.Mp + (pre_b ? 0 : pl.b_entries * pl.Np) + 1);
 	pl.off_b = round_up(bytes_a, 1024);
 	pl.off_f = pl.off_b + round_up(bytes_b, 1024);
 	pl.total = pl.off_f + pl.flag_ints * sizeof(int);
@@ -651,11 +654,23 @@ template <int kSplit, int kBN>
 static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
 	using Cf = Cfg<kSplit, kBN>;
+	const bool pre_b = d.packed_b != nullptr;
 	float* pa = reinterpret_cast<float*>(ws);
-	float* pb = reinterpret_cast<float*>(ws + pl.off_b);
 	int* flags_a = reinterpret_cast<int*>(ws + pl.off_f);
-	int* flags_b = flags_a + pl.a_entries * pl.Mp;
-	int* any = flags_b + pl.b_entries * pl.Np;
+	float* pb;
+	int *flags_b, *any, *any_b;
+	if (pre_b) {                                           // panels, then Np flags, then B's any-flag
+		unsigned char* buf = static_cast<unsigned char*>(const_cast<void*>(d.packed_b));
+		pb = reinterpret_cast<float*>(buf);
+		flags_b = reinterpret_cast<int*>(buf + round_up((long long)pl.rows_b * kBK * 4, 1024));
+		any_b = flags_b + pl.Np;
+		any = flags_a + pl.a_entries * pl.Mp;
+	} else {
+		pb = reinterpret_cast<float*>(ws + pl.off_b);
+		flags_b = flags_a + pl.a_entries * pl.Mp;
+		any = flags_b + pl.b_entries * pl.Np;
+		any_b = any;
+	}
 	const int inner = (int)d.batch_inner;
 
 	NNB_CUDA_TRY(cudaMemsetAsync(flags_a, 0, pl.flag_ints * sizeof(int), s));
@@ -664,7 +679,7 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 		launch_pack<kSplit>(s, d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, d.m, d.k, pl.Mp, pl.KB, kAPanelRows,
 			pl.a_entries, pa, flags_a, any);
 	}
-	{
+	if (!pre_b) {
 		TraceScope ts(s, kTracePack, traced);
 		launch_pack<kSplit>(s, d.b, d.ldb, d.sb_outer, d.sb_inner, inner, !d.tb, d.n, d.k, pl.Np, pl.KB,
 			Cf::kBPanelRows, pl.b_entries, pb, flags_b, any);
@@ -686,7 +701,7 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	p.bias = d.epi.bias; p.bias_mode = d.epi.bias_mode; p.act = d.epi.act;
 	p.mask = d.epi.mask; p.pre = d.epi.pre;
 	p.ld_aux = d.epi.ld_aux; p.s_aux_outer = d.epi.s_aux_outer; p.s_aux_inner = d.epi.s_aux_inner;
-	p.any_nonfinite = any; p.flags_a = flags_a; p.flags_b = flags_b;
+	p.any_nonfinite = any; p.any_b = any_b; p.flags_a = flags_a; p.flags_b = flags_b;
 	p.A = d.a; p.lda = d.lda; p.sa_outer = d.sa_outer; p.sa_inner = d.sa_inner;
 	p.B = d.b; p.ldb = d.ldb; p.sb_outer = d.sb_outer; p.sb_inner = d.sb_inner;
 	p.ta = d.ta; p.tb = d.tb; p.err = err;
@@ -728,6 +743,9 @@ static nnb_status validate(const GemmDesc& d) {
 	if (d.epi.act == kActGelu && !d.epi.pre) return fail(NNB_ERR_INVALID, "gemm: gelu pre-activation is null");
 	if ((d.epi.act != kActNone || d.epi.bias_mode != kBiasNone) && d.k == 0)
 		return fail(NNB_ERR_UNSUPPORTED, "gemm: fused epilogue with k == 0");
+	if (d.bn != 0 && d.bn != 64 && d.bn != 128 && d.bn != 256) return fail(NNB_ERR_INVALID, "gemm: tile width %d", d.bn);
+	if (d.packed_b && (d.bn == 0 || d.batch_outer * d.batch_inner != 1))
+		return fail(NNB_ERR_INVALID, "gemm: a packed B needs its tile width and a single batch entry");
 	return NNB_OK;
 }
 
@@ -800,7 +818,7 @@ __global__ void depth_sum_kernel(const float* __restrict__ part, int pieces, lon
 
 static nnb_status gemm_direct(cudaStream_t s, const DeviceState* dev, const GemmDesc& d) {
 	Plan pl;
-	NNB_TRY(make_plan(d, pl, 0, dev->sm_count));
+	NNB_TRY(make_plan(d, pl, d.bn, dev->sm_count));
 	void* ws = nullptr;
 	NNB_TRY(scratch_alloc(&ws, pl.total, s));
 	nnb_status st = d.mode == NNB_MATH_FP32X3
@@ -875,8 +893,45 @@ nnb_status gemm_run(cudaStream_t s, const GemmDesc& d) {
 		return cuda_status(cudaGetLastError(), "zero fill launch");
 	}
 	const int pieces = depth_pieces(d);
+	if (pieces > 1 && d.packed_b) return fail(NNB_ERR_INVALID, "gemm: a packed B with a depth cut");
 	if (pieces > 1) return gemm_depth_cut(s, dev, d, pieces);
 	return gemm_direct(s, dev, d);
+}
+
+int gemm_tile_width(const GemmDesc& d, int sms) {
+	return gemm::choose_bn(d.m, d.n, d.batch_outer * d.batch_inner, sms > 0 ? sms : 148);
+}
+
+int gemm_depth_pieces(const GemmDesc& d) { return gemm::depth_pieces(d); }
+
+size_t gemm_packed_b_bytes(const GemmDesc& d, int bn) {
+	gemm::Plan pl;
+	if (gemm::make_plan(d, pl, bn) != NNB_OK) return 0;
+	return (size_t)gemm::round_up((long long)pl.rows_b * gemm::kBK * 4, 1024) + (size_t)(pl.Np + 1) * sizeof(int);
+}
+
+nnb_status gemm_pack_b(cudaStream_t s, const GemmDesc& d, int bn, void* buf) {
+	using namespace gemm;
+	NNB_TRY(validate(d));
+	if (bn != 64 && bn != 128 && bn != 256) return fail(NNB_ERR_INVALID, "gemm_pack_b: tile width %d", bn);
+	if (d.batch_outer * d.batch_inner != 1 || d.k == 0 || d.n == 0)
+		return fail(NNB_ERR_INVALID, "gemm_pack_b: needs one batch entry and k, n > 0");
+	if (!buf) return fail(NNB_ERR_INVALID, "gemm_pack_b: buffer is null");
+	Plan pl;
+	NNB_TRY(make_plan(d, pl, bn));
+	float* pb = static_cast<float*>(buf);
+	int* flags = reinterpret_cast<int*>(static_cast<unsigned char*>(buf) + round_up((long long)pl.rows_b * kBK * 4, 1024));
+	NNB_CUDA_TRY(cudaMemsetAsync(flags, 0, (size_t)(pl.Np + 1) * sizeof(int), s));
+	{
+		TraceScope ts(s, kTracePack);
+		if (d.mode == NNB_MATH_FP32X3)
+			launch_pack<1>(s, d.b, d.ldb, 0, 0, 1, !d.tb, d.n, d.k, pl.Np, pl.KB, b_panel_rows(bn), 1, pb, flags,
+				flags + pl.Np);
+		else
+			launch_pack<0>(s, d.b, d.ldb, 0, 0, 1, !d.tb, d.n, d.k, pl.Np, pl.KB, b_panel_rows(bn), 1, pb, flags,
+				flags + pl.Np);
+	}
+	return cuda_status(cudaGetLastError(), "gemm_pack_b launch");
 }
 
 }  // namespace nnb

@@ -42,9 +42,24 @@ struct GemmDesc {
 	int accumulate = 0;
 	int mode = NNB_MATH_FP32X3;
 	GemmEpilogue epi;
+	// B already in the packed panel layout, written by gemm_pack_b for this n, k, math mode and tile
+	// width (one batch entry, no depth cut); b/ldb stay the unpacked operand (non-finite fix-ups)
+	const void* packed_b = nullptr;
+	int bn = 0;                         // tile width: 0 chooses it from the shape; 64, 128 or 256
 };
 
 // Validates and enqueues the product (pack kernels + one persistent tensor-core kernel).
 nnb_status gemm_run(cudaStream_t s, const GemmDesc& d);
+
+// Tile width gemm_run picks for d on a device with `sms` SMs (it never changes the result's bits).
+int gemm_tile_width(const GemmDesc& d, int sms);
+
+// Depth pieces gemm_run cuts d's k into (1: none); the cut depends on n, k and the epilogue only.
+int gemm_depth_pieces(const GemmDesc& d);
+
+// Packed form of d's B operand for tile width bn: its size in bytes, and the pack itself (panels,
+// then one non-finite flag per padded row of op(B)^T, then the any-non-finite flag).
+size_t gemm_packed_b_bytes(const GemmDesc& d, int bn);
+nnb_status gemm_pack_b(cudaStream_t s, const GemmDesc& d, int bn, void* buf);
 
 }  // namespace nnb

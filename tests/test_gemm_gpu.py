@@ -225,10 +225,11 @@ def test_depth_cut_small_output_long_depth(cuda, mode, rel):
 
 @pytest.mark.parametrize("mode", [nnb.MATH_FP32X3, nnb.MATH_TF32])
 @pytest.mark.parametrize("ta,tb,m,n,k,pad,acc", [
-    (0, 0, 3000, 520, 300, 0, 0),       # several bands, partial last band
-    (1, 0, 1400, 257, 129, 3, 1),       # transposed A (column bands of its storage), strides, accumulate
+    (0, 0, 3000, 4100, 300, 0, 0),      # several bands over one packed B, partial last band
+    (1, 0, 5000, 2300, 129, 3, 1),      # transposed A (column bands of its storage), strides, accumulate
     (0, 1, 77, 1030, 700, 1, 0),        # one band
-    (1, 1, 2100, 64, 2048, 2, 1),       # deep k (depth cut inside each band)
+    (1, 1, 2100, 64, 2048, 2, 1),       # deep k (depth cut inside the band, B packed per piece)
+    (1, 1, 5000, 2048, 4096, 2, 1),     # depth cut in several bands
 ])
 def test_sgemm_host_bitwise_equal_to_device(cuda, mode, ta, tb, m, n, k, pad, acc):
     """nnb_sgemm_host (host buffers, banded pipeline of copies and GEMMs) gives the device entry's bits
@@ -239,6 +240,25 @@ def test_sgemm_host_bitwise_equal_to_device(cuda, mode, ta, tb, m, n, k, pad, ac
     c_host = p.c.copy()
     nnb.sgemm_host(ta, tb, m, n, k, p.a, p.lda, p.b, p.ldb, c_host, p.ldc, acc, math_mode=mode)
     assert c_host.tobytes() == want.tobytes()
+
+
+@pytest.mark.parametrize("mode", [nnb.MATH_FP32X3, nnb.MATH_TF32])
+def test_sgemm_host_non_finite_bitwise_equal_to_device(cuda, mode):
+    """Infinities and NaNs in A and in the once-packed B reach every band's exact fix-up: the same
+    bits as the device entry, and the IEEE pattern of the fp32 loop."""
+    torch = cuda
+    p = orc.Problem(0, 0, 2000, 4100, 96, 0, 611)
+    p.a[1500 * p.lda + 7] = np.inf                    # a row in a later band
+    p.b[40 * p.ldb + 4000] = np.nan                   # a column every band reads
+    p.b[3 * p.ldb + 17] = -np.inf
+    want = run_gpu(torch, p, 0, mode)
+    c_host = p.c.copy()
+    nnb.sgemm_host(0, 0, p.m, p.n, p.k, p.a, p.lda, p.b, p.ldb, c_host, p.ldc, 0, math_mode=mode)
+    assert c_host.tobytes() == want.tobytes()
+    loop = orc.sgemm_f32(p, p.c, 0)
+    assert np.array_equal(np.isnan(c_host), np.isnan(loop))
+    inf = np.isinf(loop)
+    assert np.array_equal(c_host[inf], loop[inf])
 
 
 def test_sgemm_host_pinned_golden(cuda):
