@@ -37,7 +37,9 @@ constexpr int kGroupM = 16;              // tiles of M walked together for L2 re
 constexpr int kThreads = 192;
 constexpr int kSmemBudget = 200 * 1024;  // dynamic shared memory for the stage ring
 
-__host__ __device__ constexpr int b_panel_rows(int bn) { return bn < 128 ? bn : 128; }
+// Rows per packed B panel (one TMA box): 128 for the widths that are multiples of 128, else the width.
+__host__ __device__ constexpr int b_panel_rows(int bn) { return bn % 128 == 0 ? 128 : bn; }
+__host__ __device__ constexpr int tmem_cols_pow2(int cols) { return cols <= 32 ? 32 : 2 * tmem_cols_pow2((cols + 1) / 2); }
 
 template <int kSplit, int kBN>
 struct Cfg {
@@ -50,7 +52,7 @@ struct Cfg {
 	static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
 	static constexpr int kEpiBytes = 4 * 32 * 32 * 4;        // one 32 x 32 staging tile per epilogue warp
 	static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024;
-	static constexpr int kTmemCols = 2 * kBN;                // two accumulators
+	static constexpr int kTmemCols = tmem_cols_pow2(2 * kBN); // two accumulators (allocations are powers of 2)
 	static constexpr int kBPanelRows = b_panel_rows(kBN);
 	static constexpr int kBPanels = kBN / kBPanelRows;
 };
@@ -193,7 +195,7 @@ __global__ void __launch_bounds__(256) pack_rows_vec_kernel(const float* __restr
 
 // Vectorised pack for X stored K x rows (rows contiguous) with 16-byte aligned k-rows and R % 4 == 0:
 // a 64-row x 32-depth tile is read with float4 loads along the rows, transposed in shared memory,
-// and written as float4 groups of 4 consecutive k. grid = (Rp/64, ceil(Kp/32), batch entries).
+// and written as float4 groups of 4 consecutive k. grid = (ceil(Rp/64), ceil(Kp/32), batch entries).
 template <int kSplit>
 __global__ void __launch_bounds__(256) pack_cols_vec_kernel(const float* __restrict__ X, long long ldx,
 		long long s_outer, long long s_inner, int inner, int R, int K, int Rp, int KB, int panel_rows,
@@ -223,7 +225,7 @@ __global__ void __launch_bounds__(256) pack_cols_vec_kernel(const float* __restr
 		const int f = t + 256 * i;                // (row, k-quad) pairs: 64 rows x 8 quads
 		const int rl = f >> 3, q = f & 7;
 		const int gr = r0 + rl, k = k0 + q * 4, kb = k >> 4;
-		if (kb >= KB) continue;
+		if (kb >= KB || gr >= Rp) continue;
 		float4 v = make_float4(tile[rl][q * 4], tile[rl][q * 4 + 1], tile[rl][q * 4 + 2], tile[rl][q * 4 + 3]);
 		const bool ok = isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
 		if (!ok) {
@@ -556,15 +558,17 @@ inline long long round_up(long long x, long long a) { return (x + a - 1) / a * a
 // Tile width. A tile's time is its MMA instruction count (the same for every width) times the cost of
 // one tf32 instruction, measured at about 44 + 0.38 N cycles, and the persistent grid works through
 // the tiles in waves of one per SM: the width with the fewest waves x instruction cost wins, a
-// narrower one only when clearly better. Big products keep 256; products with few tiles (a rank's
-// share of a data-parallel batch) get narrower tiles that fill the SMs. The width does not change any
+// narrower one only when clearly better. Big products keep 256; a product whose 256-wide tiles leave
+// its last wave part-empty may take 224 (a 1024 x 8192 row band: 296 tiles, two full waves on 148 SMs,
+// against 256 tiles in two waves at 256); products with few tiles (a rank's share of a data-parallel
+// batch) get narrower tiles that fill the SMs. The width does not change any
 // element's arithmetic (each is one k-ordered chain in the accumulator), so results stay bitwise
 // independent of it, of the batch size and of the GPU count.
 static int choose_bn(long long m, long long n, long long entries, int sms) {
 	const long long mt = entries * (round_up(m, kBM) / kBM);
 	int best = 256;
 	double best_cost = 0.0;
-	for (int bn : {256, 128, 64}) {
+	for (int bn : {256, 224, 128, 64}) {
 		const long long tiles = mt * (round_up(n, bn) / bn);
 		const long long waves = (tiles + sms - 1) / sms;
 		const double cost = (double)waves * (44.0 + 0.38 * bn);
@@ -576,12 +580,12 @@ static int choose_bn(long long m, long long n, long long entries, int sms) {
 	return best;
 }
 
-static bool g_attr_set[64][2][3];
+static bool g_attr_set[64][2][4];
 static std::mutex g_attr_mutex;
 
 template <int kSplit, int kBN>
 static nnb_status set_smem_attr(int dev) {
-	const int bi = kBN == 64 ? 0 : kBN == 128 ? 1 : 2;
+	const int bi = kBN == 64 ? 0 : kBN == 128 ? 1 : kBN == 224 ? 3 : 2;
 	std::lock_guard<std::mutex> lock(g_attr_mutex);
 	if (g_attr_set[dev & 63][kSplit][bi]) return NNB_OK;
 	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -640,7 +644,7 @@ static void launch_pack(cudaStream_t s, const float* X, long long ldx, long long
 		pack_rows_vec_kernel<kSplit><<<dim3(blocks, (unsigned)entries), 256, 0, s>>>(X, ldx, s_outer, s_inner, inner,
 			(int)R, (int)K, (int)Rp, (int)KB, panel_rows, out, flags, any);
 	} else if (trans && base16 && strides4 && R % 4 == 0) {
-		dim3 g((unsigned)(Rp / 64), (unsigned)((KB * 16 + 31) / 32), (unsigned)entries);
+		dim3 g((unsigned)((Rp + 63) / 64), (unsigned)((KB * 16 + 31) / 32), (unsigned)entries);
 		pack_cols_vec_kernel<kSplit><<<g, 256, 0, s>>>(X, ldx, s_outer, s_inner, inner, (int)R, (int)K, (int)Rp, (int)KB,
 			panel_rows, out, flags, any);
 	} else {
@@ -720,6 +724,7 @@ template <int kSplit>
 static nnb_status dispatch_bn(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
 	if (pl.bn == 256) return launch_main<kSplit, 256>(s, dev, sm_count, err, d, pl, ws, traced);
+	if (pl.bn == 224) return launch_main<kSplit, 224>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 128) return launch_main<kSplit, 128>(s, dev, sm_count, err, d, pl, ws, traced);
 	return launch_main<kSplit, 64>(s, dev, sm_count, err, d, pl, ws, traced);
 }
@@ -743,7 +748,8 @@ static nnb_status validate(const GemmDesc& d) {
 	if (d.epi.act == kActGelu && !d.epi.pre) return fail(NNB_ERR_INVALID, "gemm: gelu pre-activation is null");
 	if ((d.epi.act != kActNone || d.epi.bias_mode != kBiasNone) && d.k == 0)
 		return fail(NNB_ERR_UNSUPPORTED, "gemm: fused epilogue with k == 0");
-	if (d.bn != 0 && d.bn != 64 && d.bn != 128 && d.bn != 256) return fail(NNB_ERR_INVALID, "gemm: tile width %d", d.bn);
+	if (d.bn != 0 && d.bn != 64 && d.bn != 128 && d.bn != 224 && d.bn != 256)
+		return fail(NNB_ERR_INVALID, "gemm: tile width %d", d.bn);
 	if (d.packed_b && (d.bn == 0 || d.batch_outer * d.batch_inner != 1))
 		return fail(NNB_ERR_INVALID, "gemm: a packed B needs its tile width and a single batch entry");
 	return NNB_OK;
@@ -913,7 +919,7 @@ size_t gemm_packed_b_bytes(const GemmDesc& d, int bn) {
 nnb_status gemm_pack_b(cudaStream_t s, const GemmDesc& d, int bn, void* buf) {
 	using namespace gemm;
 	NNB_TRY(validate(d));
-	if (bn != 64 && bn != 128 && bn != 256) return fail(NNB_ERR_INVALID, "gemm_pack_b: tile width %d", bn);
+	if (bn != 64 && bn != 128 && bn != 224 && bn != 256) return fail(NNB_ERR_INVALID, "gemm_pack_b: tile width %d", bn);
 	if (d.batch_outer * d.batch_inner != 1 || d.k == 0 || d.n == 0)
 		return fail(NNB_ERR_INVALID, "gemm_pack_b: needs one batch entry and k, n > 0");
 	if (!buf) return fail(NNB_ERR_INVALID, "gemm_pack_b: buffer is null");

@@ -183,11 +183,11 @@ nnb_status sgemm_host(cudaStream_t caller, bool blocking, int ta, int tb, size_t
 		d.a = da; d.lda = ta ? (long long)rows : (long long)k;
 		d.c = dc;
 		if (pre) {
-			// a short band may take a narrower width that reads the same 128-row panels of B over
-			// the same padded width
+			// a short band may go from 256 to 128, which reads the same 128-row panels of B over the
+			// same padded width; every other band keeps the width B was packed for
 			int w = gemm_tile_width(d, dev->sm_count);
-			if (w == 64) w = 128;
-			if (w > bn || (w == 128 && (n + 127) / 128 * 128 != (n + 255) / 256 * 256)) w = bn;
+			if (!(bn == 256 && w < bn && (n + 127) / 128 * 128 == (n + 255) / 256 * 256)) w = bn;
+			else w = 128;
 			d.packed_b = x.pb;
 			d.bn = w;
 		}

@@ -190,6 +190,25 @@ def test_large_sampled(cuda):
             assert np.all(err <= rel * mag), (m, n, k, mode, (err / mag).max())
 
 
+@pytest.mark.parametrize("mode", [nnb.MATH_FP32X3, nnb.MATH_TF32])
+@pytest.mark.parametrize("tb,n", [(0, 8192), (1, 8192), (0, 8000)])
+def test_tile_width_does_not_change_bits(cuda, mode, tb, n):
+    """A 1024-row band of a wide product runs on 224-wide tiles (296 tiles: two full waves of 148 SMs),
+    the 4096-row product it is cut from on 256-wide ones: the band's rows are the same bits."""
+    torch = cuda
+    m_big, m_band, k = 4096, 1024, 256
+    a = torch.from_numpy(orc.normal(71, m_big * k)).cuda().view(m_big, k)
+    b = torch.from_numpy(orc.normal(72, k * n)).cuda()
+    ldb = k if tb else n
+    big = torch.zeros(m_big, n, device="cuda")
+    nnb.sgemm(False, bool(tb), m_big, n, k, a, k, b, ldb, big, n, False, math_mode=mode)
+    for r0 in (0, 2048):
+        band = torch.zeros(m_band, n, device="cuda")
+        nnb.sgemm(False, bool(tb), m_band, n, k, a[r0:], k, b, ldb, band, n, False, math_mode=mode)
+        assert band.cpu().numpy().tobytes() == big[r0:r0 + m_band].cpu().numpy().tobytes()
+    assert nnb.device_error() == 0
+
+
 def test_argument_errors(cuda):
     torch = cuda
     a = torch.zeros(64, device="cuda")
