@@ -122,15 +122,15 @@ def _nccl_worker(rank, world, port, m, n, k, mode, gather, out_dir):
 @pytest.mark.gpu
 @pytest.mark.parametrize("gather", ["nccl", "peer"])
 @pytest.mark.parametrize("mode", [0, 1])
-def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode, gather):
+@pytest.mark.parametrize("m,n,k", [(1000, 700, 900), (4096, 8192, 128)])
+def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode, gather, m, n, k):
     """Bands computed on 2-4 GPUs and gathered on GPU 0 (by an NCCL gather after the GEMM, or by the
     GEMM's own epilogue storing into GPU 0's C through peer memory) equal the one-GPU product bit for
-    bit."""
+    bit. In the wide case the bands run on 224-wide tiles and the one-GPU product on 256-wide ones."""
     torch = cuda
     world = min(torch.cuda.device_count(), 4)
     if world < 2:
         pytest.skip("needs two or more GPUs")
-    m, n, k = 1000, 700, 900
     mp.start_processes(_nccl_worker, args=(world, _free_port(), m, n, k, mode, gather, str(tmp_path)), nprocs=world,
                        join=True, start_method="spawn")
     assert bool(np.load(tmp_path / f"eq_{mode}_{gather}.npy")[0])
