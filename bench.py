@@ -234,6 +234,82 @@ def run_reference(args, rank: int):
 # GPU arm
 # ---------------------------------------------------------------------------------------------
 
+SWEEP_SIZES = (1024, 2048, 4096, 8192, 16384)
+
+
+def run_gemm_sweep(rank: int, world: int, local_rank: int, reps: int = 5):
+    """Config 4's sweep: M = N = K over SWEEP_SIZES in both math modes, A and B ~ N(0,1), the M rows
+    cut into one band per rank whose GEMM epilogue stores into GPU 0's C through peer memory (N > 1).
+    Per size and mode: whole-job TFLOP/s over `reps` timed calls after two untimed ones (x4 calls below
+    4096), device events, max over ranks, and the per-GPU fraction of the measured ceiling (3xTF32:
+    dense bf16 / 6, TF32: / 2; burst and sustained). A call is one nnb_sgemm (packs and the kernel)
+    replayed from a CUDA graph, so the small sizes measure the GPU rather than host dispatch."""
+    import torch
+    import torch.distributed as dist
+
+    import nnb
+    from nnb.graph import GraphedStep
+    from nnb.parallel import PeerBuffer, row_bands
+
+    dev = torch.device("cuda", local_rank)
+    peaks = load_peaks()
+    burst = peaks["bf16_tflops"]
+    sustained = peaks.get("bf16_tflops_sustained") or burst
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    results = []
+    for size in SWEEP_SIZES:
+        r0, r1 = row_bands(size, world)[rank]
+        rows = r1 - r0
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(3000 + size)
+        b = torch.randn(size, size, device=dev, generator=gen)
+        gen.manual_seed(4000 + size + rank)
+        a = torch.randn(max(rows, 1), size, device=dev, generator=gen)
+        peer = PeerBuffer((size, size), owner=0) if world > 1 else None
+        c = torch.empty(size, size, device=dev) if peer is None else None
+        c_out = c if peer is None else peer.ptr + r0 * size * 4
+        for mode, name, div in ((nnb.MATH_FP32X3, "fp32x3", 6.0), (nnb.MATH_TF32, "tf32", 2.0)):
+            def call():
+                if rows:
+                    nnb.sgemm(False, False, rows, size, size, a, size, b, size, c_out, size, False, math_mode=mode)
+
+            n_calls = reps if size >= 4096 else 4 * reps
+            graphed = GraphedStep(call)
+            for _ in range(2):
+                graphed()
+            if world > 1:
+                dist.barrier(device_ids=[local_rank])
+            clocks = ClockSampler(local_rank) if size >= 8192 else None     # loops long enough to sample
+            if clocks is not None:
+                clocks.start()
+            torch.cuda.synchronize()
+            e0.record()
+            for _ in range(n_calls):
+                graphed()
+            e1.record()
+            torch.cuda.synchronize()
+            clk = clocks.stop() if clocks is not None else None
+            del graphed
+            t = torch.tensor([e0.elapsed_time(e1) / n_calls], device=dev, dtype=torch.float64)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = t.item()
+            tf = 2.0 * size ** 3 / (ms * 1e-3) / 1e12
+            results.append({"size": size, "mode": name, "ms_per_step": ms, "tflops": tf,
+                            "frac_of_burst": tf / world / (burst / div),
+                            "frac_of_sustained": tf / world / (sustained / div),
+                            "clocks": None if clk is None else {k: clk[k] for k in ("sm_mhz", "reasons", "power_w_max")}})
+        if nnb.device_error() != 0:
+            raise SystemExit(f"device error in the sweep at {size}")
+        if peer is not None:
+            peer.close()              # unmapped on every rank before GPU 0 may free its C
+        del a, b, c, peer
+        torch.cuda.empty_cache()
+    return {"what": "config 4 sweep, M = N = K, one nnb_sgemm per step"
+                    + (f", {world} row bands stored into GPU 0's C by the epilogues" if world > 1 else ""),
+            "unit": UNIT, "peak_source": peaks["source"], "results": results}
+
+
 def run_nnb(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -421,10 +497,12 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
         torch.backends.cuda.matmul.allow_tf32 = False
         cublas_tf32 = 2.0 * rows * size * size / (e0.elapsed_time(e1) / 20 * 1e-3) / 1e12
 
+    del a, b, c, a_h, b_h, c_h
+    torch.cuda.empty_cache()
+    sweep = run_gemm_sweep(rank, world, local_rank) if args.gather == "peer" else None
+
     transformer = None
     if args.workload == "all":
-        del a, b, c, a_h, b_h, c_h
-        torch.cuda.empty_cache()
         transformer = run_transformer(args.t_steps, args.t_warmup, rank, world, local_rank)
         if world == 1:
             transformer["cnn"] = run_cnn(20, 3, local_rank)
@@ -466,6 +544,7 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
                      "cublas_tf32_tflops": cublas_tf32},
         "pack_ms_per_step": pack_ms_max,
         "ms_per_step_compute_only": comp.item(),
+        "sweep": sweep,
         "tf32_mode": None if tf32_mode is None else dict(tf32_mode, roofline={
             "bound": "tensor", "achieved": tf32_mode["kernel_tflops"], "peak": bf16_peak / 2.0, "unit": UNIT,
             "frac": tf32_mode["kernel_tflops"] / (bf16_peak / 2.0),

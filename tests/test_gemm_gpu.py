@@ -190,6 +190,27 @@ def test_large_sampled(cuda):
             assert np.all(err <= rel * mag), (m, n, k, mode, (err / mag).max())
 
 
+def test_16384_sampled(cuda):
+    """The top of config 4's sweep, 16384^3 (1 GiB operands, 2^24 packed rows per operand): sampled
+    rows and columns against fp64, both math modes."""
+    torch = cuda
+    m = n = k = 16384
+    a = orc.normal(51, m * k)
+    b = orc.normal(52, k * n)
+    da, db = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    rows = np.r_[0, m - 1, np.arange(0, m, 1021)].repeat(8)
+    cols = np.tile(np.r_[0, n - 1, 255, 256, 8191, 8192, n - 2, 4097], len(rows) // 8)
+    val, mag = orc.sgemm_f64_sample(0, 0, k, a, k, b, n, None, n, 0, rows, cols)
+    for mode, rel in MODES:
+        dc = torch.empty(m, n, device="cuda")
+        nnb.sgemm(False, False, m, n, k, da, k, db, n, dc, n, False, math_mode=mode)
+        got = dc[torch.from_numpy(rows).cuda(), torch.from_numpy(cols).cuda()].cpu().numpy()
+        del dc
+        err = np.abs(got - val)
+        assert np.all(err <= rel * mag), (mode, (err / mag).max())
+    assert nnb.device_error() == 0
+
+
 @pytest.mark.parametrize("mode", [nnb.MATH_FP32X3, nnb.MATH_TF32])
 @pytest.mark.parametrize("tb,n", [(0, 8192), (1, 8192), (0, 8000)])
 def test_tile_width_does_not_change_bits(cuda, mode, tb, n):
