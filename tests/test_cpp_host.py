@@ -1,0 +1,66 @@
+"""The GEMM seam as C++17 host code: tests/cpp/sgemm_shim.cpp is the nn::kernels::sgemm
+(include/nn/kernels/gemm.hpp:57-59) a maintainer of nn-cpp would add, forwarding to the C ABI's
+host-buffer entry. It must compile against include/nnb.h alone, link libnnb.so, reject bad arguments
+before any device work (CPU test), and give the device entry's bits from host buffers (GPU test).
+"""
+import pathlib
+import shutil
+import subprocess
+
+import numpy as np
+import pytest
+
+import nnb
+from oracle import orc
+
+HERE = pathlib.Path(__file__).resolve().parent
+ROOT = HERE.parent
+
+
+@pytest.fixture(scope="module")
+def shim(tmp_path_factory):
+    cxx = shutil.which("g++")
+    assert cxx is not None, "g++ is needed to build the C++ host shim"
+    exe = tmp_path_factory.mktemp("cpp") / "sgemm_shim"
+    lib_dir = str(nnb.LIB_PATH.parent)
+    cmd = [cxx, "-std=c++17", "-O2", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"),
+           str(HERE / "cpp" / "sgemm_shim.cpp"), "-L", lib_dir, "-lnnb", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    return exe
+
+
+def test_cpp_shim_builds_and_rejects_bad_arguments(shim):
+    out = subprocess.run([str(shim), "checks"], capture_output=True, text=True, timeout=120)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert "checks ok" in out.stdout
+    assert out.stdout.count("invalid_argument:") == 3
+    assert f"version {nnb.lib().nnb_version().decode()}" in out.stdout
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ta,tb,m,n,k,pad,acc", [
+    (0, 0, 257, 300, 129, 0, 0),
+    (1, 1, 1000, 4100, 96, 3, 1),        # several bands over one packed B, strided, accumulate
+    (0, 1, 33, 7, 2100, 1, 0),           # deep k: the depth cut inside the band
+])
+def test_cpp_shim_product_equals_device_entry(cuda, shim, tmp_path, ta, tb, m, n, k, pad, acc):
+    torch = cuda
+    p = orc.Problem(ta, tb, m, n, k, pad, 8100 + m)
+    (tmp_path / "in.bin").write_bytes(p.a.tobytes() + p.b.tobytes() + p.c.tobytes())
+    args = [str(v) for v in (ta, tb, m, n, k, p.lda, p.ldb, p.ldc, acc)]
+    out = subprocess.run([str(shim), "run", *args, str(tmp_path / "in.bin"), str(tmp_path / "out.bin")],
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    got = np.fromfile(tmp_path / "out.bin", np.float32)
+    # the device entry on device copies of the same operands
+    da, db = torch.from_numpy(p.a).cuda(), torch.from_numpy(p.b).cuda()
+    dc = torch.from_numpy(p.c.copy()).cuda()
+    nnb.sgemm(ta, tb, m, n, k, da, p.lda, db, p.ldb, dc, p.ldc, acc)
+    assert got.tobytes() == dc.cpu().numpy().tobytes()
+    # and the reference test's bound against fp64 (tests/test_kernels.cpp), padding untouched
+    full = got[: m * p.ldc].reshape(m, p.ldc)
+    assert np.all(full[:, n:] == orc.SENTINEL)
+    want = orc.sgemm_f64(p, p.c, acc)
+    mag = orc.magnitude(p, p.c, acc)
+    assert np.all(np.abs(full[:, :n].astype(np.float64) - want) <= np.maximum(1e-5 * mag, 1e-6))
