@@ -56,6 +56,7 @@ def parse_args():
     ap.add_argument("--gather", choices=("peer", "nccl"), default="peer",
                     help="N>1 GEMM: bands stored into GPU 0's C by the GEMM epilogue (peer) or an NCCL gather after it")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true", help="skip config 4's size sweep (small profiling runs)")
     ap.add_argument("--workload", choices=("all", "gemm", "transformer", "cnn", "attention", "next"), default="all",
                     help="one config alone, or all: the config 4 line with configs 2, 3 and 5 inside")
     ap.add_argument("--t-steps", type=int, default=10, help="timed transformer steps")
@@ -499,7 +500,7 @@ def run_nnb(args, rank: int, world: int, local_rank: int):
 
     del a, b, c, a_h, b_h, c_h
     torch.cuda.empty_cache()
-    sweep = run_gemm_sweep(rank, world, local_rank) if args.gather == "peer" else None
+    sweep = run_gemm_sweep(rank, world, local_rank) if args.gather == "peer" and not args.no_sweep else None
 
     transformer = None
     if args.workload == "all":
