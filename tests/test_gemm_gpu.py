@@ -270,6 +270,11 @@ def test_depth_cut_small_output_long_depth(cuda, mode, rel):
     (0, 1, 77, 1030, 700, 1, 0),        # one band
     (1, 1, 2100, 64, 2048, 2, 1),       # deep k (depth cut inside the band, B packed per piece)
     (1, 1, 5000, 2048, 4096, 2, 1),     # depth cut in several bands
+    (0, 0, 1, 1, 1, 0, 0),              # the reference sweep's smallest sizes
+    (1, 0, 7, 33, 257, 1, 1),
+    (0, 1, 257, 1, 33, 2, 0),           # one output column
+    (0, 0, 300, 40, 0, 0, 0),           # k == 0: C zeroed
+    (1, 1, 300, 40, 0, 1, 1),           # k == 0 accumulating: C unchanged
 ])
 def test_sgemm_host_bitwise_equal_to_device(cuda, mode, ta, tb, m, n, k, pad, acc):
     """nnb_sgemm_host (host buffers, banded pipeline of copies and GEMMs) gives the device entry's bits
