@@ -109,15 +109,21 @@ NNB_API nnb_status nnb_sgemm_ex(void* stream, int trans_a, int trans_b, size_t m
 
 /* nn::kernels::sgemm on HOST buffers (include/nn/kernels/gemm.hpp:57-59, the reference's own calling
  * convention: row-major, host pointers, returns with C written): the drop-in for the reference's
- * kernel. B is copied to the device, then op(A) in row bands whose GEMMs run while the next bands
- * are copied in and finished bands of C are copied back (three streams). Bitwise equal to
- * nnb_sgemm on device copies of the same operands. Page-locked host buffers give full copy speed. */
+ * kernel. B is copied to the device and packed once, then op(A) in row bands whose GEMMs run while
+ * the next bands are copied in and finished bands of C are copied back (a copy stream, two compute
+ * streams, a copy-back stream). Bitwise equal to nnb_sgemm on device copies of the same operands.
+ * Page-locked host buffers give full copy speed. The device buffers it grows are kept per device
+ * for the next call until nnb_sgemm_host_release. */
 NNB_API nnb_status nnb_sgemm_host(int trans_a, int trans_b, size_t m, size_t n, size_t k, const float* a,
 		size_t lda, const float* b, size_t ldb, float* c, size_t ldc, int accumulate);
 /* The same, stream-ordered and not blocking: it starts once `stream` reaches it and `stream` waits for
  * the last copy-back, so the host buffers must stay valid until then (events on `stream` time it). */
 NNB_API nnb_status nnb_sgemm_host_async(void* stream, int trans_a, int trans_b, size_t m, size_t n, size_t k,
 		const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc, int accumulate, int math_mode);
+/* Waits for every device's host-buffer GEMM work and frees the device buffers it keeps between calls
+ * (about 5 x the operands' bytes after an 8192^3 call); the next call grows them again. No reference
+ * counterpart: the reference's kernel keeps only host-side thread-local packing buffers. */
+NNB_API nnb_status nnb_sgemm_host_release(void);
 
 /*
  * `batch` independent products C_i = op(A_i)·op(B_i) (+= when accumulating) with

@@ -32,6 +32,7 @@ namespace {
 
 struct HostGemmCtx {
 	bool ready = false;
+	int device = -1;
 	cudaStream_t copy = nullptr, compute[2] = {nullptr, nullptr}, out = nullptr;
 	cudaEvent_t b_done = nullptr, b_packed = nullptr, start = nullptr, done = nullptr;
 	bool has_prev = false;                       // `done` marks the previous call's last copy-back
@@ -67,6 +68,24 @@ nnb_status ctx_setup(HostGemmCtx& c) {
 	NNB_CUDA_TRY(cudaEventCreateWithFlags(&c.done, cudaEventDisableTiming));
 	c.ready = true;
 	return NNB_OK;
+}
+
+// Waits for the context's streams and frees its device buffers (streams and events are kept).
+nnb_status release_buffers(HostGemmCtx& c) {
+	if (!c.ready) return NNB_OK;
+	int prev = 0;
+	NNB_CUDA_TRY(cudaGetDevice(&prev));
+	NNB_CUDA_TRY(cudaSetDevice(c.device));
+	nnb_status st = NNB_OK;
+	for (cudaStream_t s : {c.copy, c.compute[0], c.compute[1], c.out})
+		if (st == NNB_OK) st = cuda_status(cudaStreamSynchronize(s), "sgemm_host_release");
+	for (float** p : {&c.da, &c.db, &c.dc, &c.pb}) {
+		if (*p && st == NNB_OK) st = cuda_status(cudaFree(*p), "sgemm_host_release");
+		if (st == NNB_OK) *p = nullptr;
+	}
+	if (st == NNB_OK) c.cap_a = c.cap_b = c.cap_c = c.cap_pb = 0;
+	const nnb_status st2 = cuda_status(cudaSetDevice(prev), "sgemm_host_release");
+	return st != NNB_OK ? st : st2;
 }
 
 nnb_status ensure_events(HostGemmCtx& c, size_t count) {
@@ -120,6 +139,7 @@ nnb_status sgemm_host(cudaStream_t caller, bool blocking, int ta, int tb, size_t
 	std::lock_guard<std::mutex> lock(g_mu[di]);
 	HostGemmCtx& x = g_ctx[di];
 	NNB_TRY(ctx_setup(x));
+	x.device = dev->device;
 	// ordered after the caller's stream and after the previous call (whose buffers are reused)
 	NNB_CUDA_TRY(cudaEventRecord(x.start, caller));
 	for (cudaStream_t st : {x.copy, x.compute[0], x.compute[1], x.out}) {
@@ -212,6 +232,14 @@ nnb_status nnb_sgemm_host(int trans_a, int trans_b, size_t m, size_t n, size_t k
 		const float* b, size_t ldb, float* c, size_t ldc, int accumulate) {
 	return nnb::sgemm_host(nullptr, true, trans_a != 0, trans_b != 0, m, n, k, a, lda, b, ldb, c, ldc, accumulate,
 		nnb::math_mode());
+}
+
+nnb_status nnb_sgemm_host_release(void) {
+	for (int i = 0; i < nnb::kMaxDev; ++i) {
+		std::lock_guard<std::mutex> lock(nnb::g_mu[i]);
+		NNB_TRY(nnb::release_buffers(nnb::g_ctx[i]));
+	}
+	return NNB_OK;
 }
 
 nnb_status nnb_sgemm_host_async(void* stream, int trans_a, int trans_b, size_t m, size_t n, size_t k, const float* a,

@@ -62,6 +62,7 @@ _SIGS = {
     "nnb_sgemm_ex": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
     "nnb_sgemm_host": ([_i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i], _i),
     "nnb_sgemm_host_async": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
+    "nnb_sgemm_host_release": ([], _i),
     "nnb_sgemm_strided_batched": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz,
                                    _sz, _i, _i], _i),
     "nnb_sgemm_noalloc": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
@@ -259,6 +260,11 @@ def sgemm_host(trans_a: bool, trans_b: bool, m: int, n: int, k: int, a, lda: int
     if blocking:
         import torch
         torch.cuda.current_stream().synchronize() if stream is None else stream.synchronize()
+
+
+def sgemm_host_release() -> None:
+    """Frees the device buffers nnb_sgemm_host keeps between calls (after waiting for its work)."""
+    check(lib().nnb_sgemm_host_release())
 
 
 def matmul(a, b, trans_a: bool = False, trans_b: bool = False, stream=None):

@@ -58,3 +58,8 @@ def test_flash_attention_host_checks():
     assert st == 5                                                              # causal needs Tq == Tk
     st = lib.nnb_flash_attention_bwd(None, 1, 4, 4, 64, 3, *([None] * 7), 0, None, 1, None, 1, None, 1)
     assert st == 5                                                              # heads does not divide D
+
+
+def test_sgemm_host_release_without_calls():
+    """Releasing the host-buffer GEMM's device buffers before any call is a no-op (no CUDA work)."""
+    nnb.sgemm_host_release()

@@ -306,6 +306,23 @@ def test_sgemm_host_non_finite_bitwise_equal_to_device(cuda, mode):
     assert np.array_equal(c_host[inf], loop[inf])
 
 
+def test_sgemm_host_release_frees_and_regrows(cuda):
+    """nnb_sgemm_host_release frees the kept device buffers; the next call grows them again and gives
+    the same bits."""
+    torch = cuda
+    p = orc.Problem(0, 0, 2048, 2048, 2048, 0, 77)
+    c1, c2 = p.c.copy(), p.c.copy()
+    nnb.sgemm_host(0, 0, p.m, p.n, p.k, p.a, p.lda, p.b, p.ldb, c1, p.ldc, 0)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    nnb.sgemm_host_release()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 - free0 >= 4 * 2048 * 2048 * 4          # at least A, B, C and the packed B
+    nnb.sgemm_host(0, 0, p.m, p.n, p.k, p.a, p.lda, p.b, p.ldb, c2, p.ldc, 0)
+    assert c1.tobytes() == c2.tobytes()
+    assert nnb.device_error() == 0
+
+
 def test_sgemm_host_pinned_golden(cuda):
     """Pinned torch host tensors, and the reference build's golden case of this module."""
     torch = cuda
