@@ -10,16 +10,17 @@
 //   out stream       waits for band i's GEMM and copies band i of C back to the host.
 // Bands are about one wave of tiles high, and the last wave's worth is cut into halves, quarters, ...
 // down to one row of tiles, with the narrower tile width when the packed B allows it: the last band
-// -- computed and copied back after the last byte of A has arrived -- is short. Bands are whole 128-row tiles of C and each element is one
-// k-ordered chain, so the result is bitwise the one nnb_sgemm gives on device copies of the same
-// operands (and, as there, independent of the band count and tile width). When the product's depth is
-// cut into pieces (a deep k next to a narrow n), every band packs its own B as nnb_sgemm does.
-// Strided host layouts are moved with 2-D copies. The host
-// buffers should be page-locked for full copy speed; pageable memory works, at the copy engine's
-// pageable rate. Device buffers and streams are kept per device and grown on demand; consecutive
-// calls are chained, so a call never overwrites buffers the previous one still reads. The stream-
-// ordered form starts after the caller's stream reaches it and makes that stream wait for the last
-// copy-back, so CUDA events on the caller's stream time the whole call.
+// -- computed and copied back after the last byte of A has arrived -- is short. Bands are whole
+// 128-row tiles of C and each element is one k-ordered chain, so the result is bitwise the one
+// nnb_sgemm gives on device copies of the same operands (and, as there, independent of the band
+// count and tile width). When the product's depth is cut into pieces (a deep k next to a narrow n),
+// every band packs its own B as nnb_sgemm does. Strided host layouts are moved with 2-D copies.
+// The host buffers should be page-locked for full copy speed; pageable memory works, at the copy
+// engine's pageable rate. Device buffers and streams are kept per device and grown on demand
+// (nnb_sgemm_host_release frees the buffers); consecutive calls are chained, so a call never
+// overwrites buffers the previous one still reads. The stream-ordered form starts after the
+// caller's stream reaches it and makes that stream wait for the last copy-back, so CUDA events on the
+// caller's stream time the whole call.
 #include <mutex>
 #include <vector>
 
@@ -125,27 +126,9 @@ nnb_status d2h(float* dst, size_t ld, const float* src, size_t rows, size_t cols
 	return NNB_OK;
 }
 
-}  // namespace
-
-nnb_status sgemm_host(cudaStream_t caller, bool blocking, int ta, int tb, size_t m, size_t n, size_t k, const float* a,
-		size_t lda, const float* b, size_t ldb, float* c, size_t ldc, int accumulate, int mode) {
-	if (m == 0 || n == 0) return NNB_OK;
-	if (!c || (k > 0 && (!a || !b))) return fail(NNB_ERR_INVALID, "sgemm_host: null pointer");
-	if (ldc < n || (k > 0 && (lda < (ta ? m : k) || ldb < (tb ? k : n))))
-		return fail(NNB_ERR_INVALID, "sgemm_host: leading dimension too small");
-	DeviceState* dev = nullptr;
-	NNB_TRY(device_state(&dev));
-	const int di = dev->device & (kMaxDev - 1);
-	std::lock_guard<std::mutex> lock(g_mu[di]);
-	HostGemmCtx& x = g_ctx[di];
-	NNB_TRY(ctx_setup(x));
-	x.device = dev->device;
-	// ordered after the caller's stream and after the previous call (whose buffers are reused)
-	NNB_CUDA_TRY(cudaEventRecord(x.start, caller));
-	for (cudaStream_t st : {x.copy, x.compute[0], x.compute[1], x.out}) {
-		NNB_CUDA_TRY(cudaStreamWaitEvent(st, x.start, 0));
-		if (x.has_prev) NNB_CUDA_TRY(cudaStreamWaitEvent(st, x.done, 0));
-	}
+// The enqueued part of one call: copies, packs and band GEMMs over the context's streams.
+nnb_status enqueue(HostGemmCtx& x, const DeviceState* dev, int ta, int tb, size_t m, size_t n, size_t k,
+		const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc, int accumulate, int mode) {
 	// op(A) band r0..r1 on the device: rows of A (ta = 0, dense band x k) or columns of A (ta = 1,
 	// dense k x band); B dense as stored (k x n or n x k); C dense m x n
 	NNB_TRY(grow(&x.da, &x.cap_a, m * k));
@@ -216,10 +199,41 @@ nnb_status sgemm_host(cudaStream_t caller, bool blocking, int ta, int tb, size_t
 		NNB_CUDA_TRY(cudaStreamWaitEvent(x.out, x.c_done[band], 0));
 		NNB_TRY(d2h(c + r0 * ldc, ldc, dc, rows, n, x.out));
 	}
-	// the out stream has waited for every GEMM, and every GEMM for its copies: its end is the call's end
+	return NNB_OK;
+}
+
+}  // namespace
+
+nnb_status sgemm_host(cudaStream_t caller, bool blocking, int ta, int tb, size_t m, size_t n, size_t k, const float* a,
+		size_t lda, const float* b, size_t ldb, float* c, size_t ldc, int accumulate, int mode) {
+	if (m == 0 || n == 0) return NNB_OK;
+	if (!c || (k > 0 && (!a || !b))) return fail(NNB_ERR_INVALID, "sgemm_host: null pointer");
+	if (ldc < n || (k > 0 && (lda < (ta ? m : k) || ldb < (tb ? k : n))))
+		return fail(NNB_ERR_INVALID, "sgemm_host: leading dimension too small");
+	DeviceState* dev = nullptr;
+	NNB_TRY(device_state(&dev));
+	const int di = dev->device & (kMaxDev - 1);
+	std::lock_guard<std::mutex> lock(g_mu[di]);
+	HostGemmCtx& x = g_ctx[di];
+	NNB_TRY(ctx_setup(x));
+	x.device = dev->device;
+	// ordered after the caller's stream and after the previous call (whose buffers are reused)
+	NNB_CUDA_TRY(cudaEventRecord(x.start, caller));
+	for (cudaStream_t st : {x.copy, x.compute[0], x.compute[1], x.out}) {
+		NNB_CUDA_TRY(cudaStreamWaitEvent(st, x.start, 0));
+		if (x.has_prev) NNB_CUDA_TRY(cudaStreamWaitEvent(st, x.done, 0));
+	}
+	const nnb_status st = enqueue(x, dev, ta, tb, m, n, k, a, lda, b, ldb, c, ldc, accumulate, mode);
+	// the call ends when all four streams have: joined on the out stream even when enqueueing failed
+	// part-way, so the next call never reuses buffers that work enqueued here still reads or writes
+	for (cudaStream_t s : {x.copy, x.compute[0], x.compute[1]}) {
+		NNB_CUDA_TRY(cudaEventRecord(x.start, s));
+		NNB_CUDA_TRY(cudaStreamWaitEvent(x.out, x.start, 0));
+	}
 	NNB_CUDA_TRY(cudaEventRecord(x.done, x.out));
 	x.has_prev = true;
 	NNB_CUDA_TRY(cudaStreamWaitEvent(caller, x.done, 0));
+	if (st != NNB_OK) return st;
 	if (blocking) NNB_CUDA_TRY(cudaStreamSynchronize(caller));
 	return NNB_OK;
 }
