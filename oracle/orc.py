@@ -52,6 +52,10 @@ _ORC_SIGS = {
     "orc_conv2d_bwd": [_sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i],
     "orc_maxpool2d_fwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p],
     "orc_maxpool2d_bwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _i],
+    "orc_avgpool2d_fwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p],
+    "orc_avgpool2d_bwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _i],
+    "orc_reduce_axis_fwd": [_sz, _sz, _sz, _i, _p, _p],
+    "orc_reduce_axis_bwd": [_sz, _sz, _sz, _i, _p, _p, _i],
     "orc_cross_entropy_fwd": [_sz, _sz, _p, _p, _p, _p],
     "orc_cross_entropy_bwd": [_sz, _sz, _p, _p, _f, _p, _i],
     "orc_sequence_ce_fwd": [_sz, _sz, _p, _p, _c.c_int64, _f, _p, _p],

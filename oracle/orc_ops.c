@@ -436,6 +436,63 @@ void orc_maxpool2d_bwd(size_t N, size_t C, size_t H, size_t W, size_t k, size_t 
 	}
 }
 
+/* ---- avgpool2d (ops.cpp:1707-1770) ----
+ * y = (window sum from 0, rows then columns) * (1 / (k*k)); the backward adds g * (1 / (k*k)) to
+ * every element of each window, windows in (oh, ow) order, into dx (zeroed first when `first`). */
+void orc_avgpool2d_fwd(size_t N, size_t C, size_t H, size_t W, size_t k, size_t st, const float* x, float* y) {
+	const size_t ho = (H - k) / st + 1, wo = (W - k) / st + 1;
+	const float inv = 1.0f / (float)(k * k);
+	for (size_t p = 0; p < N * C; p++)
+		for (size_t oh = 0; oh < ho; oh++)
+			for (size_t ow = 0; ow < wo; ow++) {
+				float acc = 0.0f;
+				for (size_t ph = 0; ph < k; ph++)
+					for (size_t pw = 0; pw < k; pw++) acc += x[p * H * W + (oh * st + ph) * W + ow * st + pw];
+				y[p * ho * wo + oh * wo + ow] = acc * inv;
+			}
+}
+
+void orc_avgpool2d_bwd(size_t N, size_t C, size_t H, size_t W, size_t k, size_t st, const float* g, float* dx,
+		int first) {
+	const size_t ho = (H - k) / st + 1, wo = (W - k) / st + 1;
+	const float inv = 1.0f / (float)(k * k);
+	for (size_t p = 0; p < N * C; p++) {
+		float* plane = dx + p * H * W;
+		if (first) memset(plane, 0, H * W * sizeof(float));
+		for (size_t oh = 0; oh < ho; oh++)
+			for (size_t ow = 0; ow < wo; ow++) {
+				const float share = g[p * ho * wo + oh * wo + ow] * inv;
+				for (size_t ph = 0; ph < k; ph++)
+					for (size_t pw = 0; pw < k; pw++) plane[(oh * st + ph) * W + ow * st + pw] += share;
+			}
+	}
+}
+
+/* ---- sum / mean over one axis (ops.cpp:284-327) ----
+ * x viewed as [outer, n, inner]; y[o, i] = sum over j in order from 0 (times 1/n for the mean); the
+ * backward stores g * factor + 0 (first) or adds g * factor to every x element of the reduced line. */
+void orc_reduce_axis_fwd(size_t outer, size_t n, size_t inner, int average, const float* x, float* y) {
+	const float factor = average ? 1.0f / (float)n : 1.0f;
+	for (size_t o = 0; o < outer; o++)
+		for (size_t i = 0; i < inner; i++) {
+			float total = 0.0f;
+			for (size_t j = 0; j < n; j++) total += x[(o * n + j) * inner + i];
+			y[o * inner + i] = average ? total * factor : total;
+		}
+}
+
+void orc_reduce_axis_bwd(size_t outer, size_t n, size_t inner, int average, const float* g, float* dx, int first) {
+	const float factor = average ? 1.0f / (float)n : 1.0f;
+	for (size_t o = 0; o < outer; o++)
+		for (size_t i = 0; i < inner; i++) {
+			const float v = g[o * inner + i] * factor;
+			for (size_t j = 0; j < n; j++) {
+				float* d = dx + (o * n + j) * inner + i;
+				*d = first ? v + 0.0f : *d + v;
+			}
+		}
+}
+
 /* ---- cross entropy (ops.cpp:1774-1840) ---- */
 void orc_cross_entropy_fwd(size_t N, size_t C, const float* logits, const int64_t* t, float* sm, float* loss) {
 	float total = 0.0f;

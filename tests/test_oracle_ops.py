@@ -153,6 +153,38 @@ def test_maxpool_bitwise(k, stride):
     assert y.tobytes() == y_r.tobytes() and dx.tobytes() == dx_r.tobytes()
 
 
+@pytest.mark.parametrize("k,stride", [(2, 2), (3, 1), (3, 2)])
+def test_avgpool_bitwise(k, stride):
+    """avgpool2d (ops.cpp:1707-1770), overlapping windows included (stride < k)."""
+    N, C, H, W = 2, 3, 9, 10
+    x = nrm(25, N, C, H, W)
+    ho, wo = (H - k) // stride + 1, (W - k) // stride + 1
+    g = nrm(26, N, C, ho, wo)
+    y_r, dx_r = orc.zeros(N, C, ho, wo), orc.zeros(N, C, H, W)
+    ref.ref_avgpool2d(N, C, H, W, k, stride, P(x), P(g), P(y_r), P(dx_r))
+    y, dx = orc.zeros(N, C, ho, wo), orc.zeros(N, C, H, W)
+    O.orc_avgpool2d_fwd(N, C, H, W, k, stride, P(x), P(y))
+    O.orc_avgpool2d_bwd(N, C, H, W, k, stride, P(g), P(dx), 1)
+    assert y.tobytes() == y_r.tobytes() and dx.tobytes() == dx_r.tobytes()
+
+
+@pytest.mark.parametrize("axis", [0, 1, 2, 3, -1])
+@pytest.mark.parametrize("average", [0, 1])
+def test_reduce_axis_bitwise(axis, average):
+    """sum / mean over one axis (ops.cpp:284-327) of a 4-D tensor."""
+    shape = (3, 5, 7, 11)
+    x = nrm(27, *shape)
+    ax = axis % 4
+    outer, n, inner = int(np.prod(shape[:ax])), shape[ax], int(np.prod(shape[ax + 1:]))
+    g = nrm(28, outer * inner)
+    y_r, dx_r = orc.zeros(outer * inner), orc.zeros(*shape)
+    ref.ref_reduce4(*shape, axis, average, P(x), P(g), P(y_r), P(dx_r))
+    y, dx = orc.zeros(outer * inner), orc.zeros(*shape)
+    O.orc_reduce_axis_fwd(outer, n, inner, average, P(x), P(y))
+    O.orc_reduce_axis_bwd(outer, n, inner, average, P(g), P(dx), 1)
+    assert y.tobytes() == y_r.tobytes() and dx.tobytes() == dx_r.tobytes()
+
+
 def test_cross_entropy_bitwise():
     N, C = 33, 10
     logits, t = nrm(25, N, C), orc.integers(26, N, 0, C - 1)
