@@ -185,6 +185,22 @@ def test_reduce_axis_bitwise(axis, average):
     assert y.tobytes() == y_r.tobytes() and dx.tobytes() == dx_r.tobytes()
 
 
+def test_global_avgpool_is_two_axis_means_bitwise():
+    """GlobalAvgPool2d (pool2d.cpp:20-23) is mean(mean(x, 3), 2): the axis restatement twice."""
+    N, C, H, W = 2, 3, 5, 6
+    x = nrm(29, N, C, H, W)
+    g = nrm(30, N * C)
+    y_r, dx_r = orc.zeros(N * C), orc.zeros(N, C, H, W)
+    ref.ref_global_avgpool(N, C, H, W, P(x), P(g), P(y_r), P(dx_r))
+    m3, y = orc.zeros(N * C * H), orc.zeros(N * C)
+    O.orc_reduce_axis_fwd(N * C * H, W, 1, 1, P(x), P(m3))
+    O.orc_reduce_axis_fwd(N * C, H, 1, 1, P(m3), P(y))
+    d3, dx = orc.zeros(N * C * H), orc.zeros(N, C, H, W)
+    O.orc_reduce_axis_bwd(N * C, H, 1, 1, P(g), P(d3), 1)
+    O.orc_reduce_axis_bwd(N * C * H, W, 1, 1, P(d3), P(dx), 1)
+    assert y.tobytes() == y_r.tobytes() and dx.tobytes() == dx_r.tobytes()
+
+
 def test_cross_entropy_bitwise():
     N, C = 33, 10
     logits, t = nrm(25, N, C), orc.integers(26, N, 0, C - 1)
