@@ -316,14 +316,16 @@ void orc_attention_bwd(size_t N, size_t Tq, size_t Tk, size_t D, size_t H, const
 }
 
 /* ---- conv2d / conv2d_relu (ops.cpp:188-243, 1345-1472) ---- */
+/* column matrix [Cin*kh*kw, ho*wo] of one sample (or one group's channels); tap (ph, pw) reads input
+ * row oh*st + ph*dl - pd and column ow*st + pw*dl - pd, zero outside (ops.cpp:1486-1500 with dl > 1) */
 static void im2col(const float* x, float* col, size_t Cin, size_t H, size_t W, size_t kh, size_t kw, size_t st,
-		size_t pd, size_t ho, size_t wo) {
+		size_t pd, size_t dl, size_t ho, size_t wo) {
 	for (size_t c = 0; c < Cin; c++)
 		for (size_t ph = 0; ph < kh; ph++)
 			for (size_t pw = 0; pw < kw; pw++)
 				for (size_t oh = 0; oh < ho; oh++)
 					for (size_t ow = 0; ow < wo; ow++) {
-						const long ih = (long)(oh * st + ph) - (long)pd, iw = (long)(ow * st + pw) - (long)pd;
+						const long ih = (long)(oh * st + ph * dl) - (long)pd, iw = (long)(ow * st + pw * dl) - (long)pd;
 						float v = 0.0f;
 						if (ih >= 0 && ih < (long)H && iw >= 0 && iw < (long)W) v = x[(c * H + (size_t)ih) * W + (size_t)iw];
 						col[((c * kh + ph) * kw + pw) * ho * wo + oh * wo + ow] = v;
@@ -331,13 +333,13 @@ static void im2col(const float* x, float* col, size_t Cin, size_t H, size_t W, s
 }
 
 static void col2im_add(const float* col, float* x, size_t Cin, size_t H, size_t W, size_t kh, size_t kw, size_t st,
-		size_t pd, size_t ho, size_t wo) {
+		size_t pd, size_t dl, size_t ho, size_t wo) {
 	for (size_t c = 0; c < Cin; c++)
 		for (size_t ph = 0; ph < kh; ph++)
 			for (size_t pw = 0; pw < kw; pw++)
 				for (size_t oh = 0; oh < ho; oh++)
 					for (size_t ow = 0; ow < wo; ow++) {
-						const long ih = (long)(oh * st + ph) - (long)pd, iw = (long)(ow * st + pw) - (long)pd;
+						const long ih = (long)(oh * st + ph * dl) - (long)pd, iw = (long)(ow * st + pw * dl) - (long)pd;
 						if (ih >= 0 && ih < (long)H && iw >= 0 && iw < (long)W)
 							x[(c * H + (size_t)ih) * W + (size_t)iw] += col[((c * kh + ph) * kw + pw) * ho * wo + oh * wo + ow];
 					}
@@ -348,7 +350,7 @@ void orc_conv2d_fwd(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_
 	const size_t ho = (H + 2 * pd - kh) / st + 1, wo = (W + 2 * pd - kw) / st + 1, K = Cin * kh * kw, hw = ho * wo;
 	float* col = (float*)malloc(K * hw * sizeof(float));
 	for (size_t n = 0; n < N; n++) {
-		im2col(x + n * Cin * H * W, col, Cin, H, W, kh, kw, st, pd, ho, wo);
+		im2col(x + n * Cin * H * W, col, Cin, H, W, kh, kw, st, pd, 1, ho, wo);
 		float* yn = y + n * Cout * hw;
 		orc_sgemm_f32(0, 0, Cout, hw, K, w, K, col, hw, yn, hw, 0);
 		for (size_t c = 0; c < Cout; c++)
@@ -377,13 +379,13 @@ void orc_conv2d_bwd(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_
 		const float* g = grad + n * Cout * hw;
 		for (size_t i = 0; i < Cout * hw; i++) gm[i] = alive ? (alive[n * Cout * hw + i] ? g[i] : 0.0f) : g[i];
 		for (size_t c = 0; c < Cout; c++) gb[n * Cout + c] = lane_sum(gm + c * hw, hw);
-		im2col(x + n * Cin * H * W, col, Cin, H, W, kh, kw, st, pd, ho, wo);
+		im2col(x + n * Cin * H * W, col, Cin, H, W, kh, kw, st, pd, 1, ho, wo);
 		orc_sgemm_f32(0, 1, Cout, K, hw, gm, hw, col, hw, gw + n * Cout * K, K, 0);
 		if (dx) {
 			orc_sgemm_f32(1, 0, K, hw, Cout, w, K, gm, hw, col, hw, 0);
 			float* dxn = dx + n * Cin * H * W;
 			if (dx_first) memset(dxn, 0, Cin * H * W * sizeof(float));
-			col2im_add(col, dxn, Cin, H, W, kh, kw, st, pd, ho, wo);
+			col2im_add(col, dxn, Cin, H, W, kh, kw, st, pd, 1, ho, wo);
 		}
 	}
 	if (db)
@@ -402,6 +404,60 @@ void orc_conv2d_bwd(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_
 	free(gm);
 	free(gw);
 	free(gb);
+}
+
+/* ---- conv2d with dilation and groups (ops.cpp:1525-1607) ----
+ * Per sample n and group g: the group's Cg = Cin/G input channels go through the dilated im2col, its
+ * Cog = Cout/G filters (w rows g*Cog..) multiply the column matrix, then the bias is added. Backward:
+ * dW per sample, summed over samples in order; dX by the transposed product and col2im per group into
+ * a zeroed per-sample buffer; the bias gradient sums, per channel, samples then positions in order. */
+void orc_conv2d_ex_fwd(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh, size_t kw, size_t st,
+		size_t pd, size_t dl, size_t G, const float* x, const float* w, const float* b, float* y) {
+	const size_t Cg = Cin / G, Cog = Cout / G, K = Cg * kh * kw;
+	const size_t ho = (H + 2 * pd - (dl * (kh - 1) + 1)) / st + 1, wo = (W + 2 * pd - (dl * (kw - 1) + 1)) / st + 1;
+	const size_t hw = ho * wo;
+	float* col = (float*)malloc(K * hw * sizeof(float));
+	for (size_t n = 0; n < N; n++)
+		for (size_t g = 0; g < G; g++) {
+			im2col(x + (n * Cin + g * Cg) * H * W, col, Cg, H, W, kh, kw, st, pd, dl, ho, wo);
+			float* yg = y + (n * Cout + g * Cog) * hw;
+			orc_sgemm_f32(0, 0, Cog, hw, K, w + g * Cog * K, K, col, hw, yg, hw, 0);
+			for (size_t c = 0; c < Cog; c++)
+				for (size_t i = 0; i < hw; i++) yg[c * hw + i] += b[g * Cog + c];
+		}
+	free(col);
+}
+
+void orc_conv2d_ex_bwd(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh, size_t kw, size_t st,
+		size_t pd, size_t dl, size_t G, const float* grad, const float* x, const float* w, float* dx, float* dw,
+		float* db) {
+	const size_t Cg = Cin / G, Cog = Cout / G, K = Cg * kh * kw;
+	const size_t ho = (H + 2 * pd - (dl * (kh - 1) + 1)) / st + 1, wo = (W + 2 * pd - (dl * (kw - 1) + 1)) / st + 1;
+	const size_t hw = ho * wo, wsz = Cout * K;
+	float* col = (float*)malloc(K * hw * sizeof(float));
+	float* gw = (float*)malloc(N * wsz * sizeof(float));
+	memset(dx, 0, N * Cin * H * W * sizeof(float));
+	for (size_t n = 0; n < N; n++)
+		for (size_t g = 0; g < G; g++) {
+			const float* gy = grad + (n * Cout + g * Cog) * hw;
+			im2col(x + (n * Cin + g * Cg) * H * W, col, Cg, H, W, kh, kw, st, pd, dl, ho, wo);
+			orc_sgemm_f32(0, 1, Cog, K, hw, gy, hw, col, hw, gw + n * wsz + g * Cog * K, K, 0);
+			orc_sgemm_f32(1, 0, K, hw, Cog, w + g * Cog * K, K, gy, hw, col, hw, 0);
+			col2im_add(col, dx + (n * Cin + g * Cg) * H * W, Cg, H, W, kh, kw, st, pd, dl, ho, wo);
+		}
+	for (size_t c = 0; c < Cout; c++) {
+		float s = 0.0f;
+		for (size_t n = 0; n < N; n++)
+			for (size_t i = 0; i < hw; i++) s += grad[(n * Cout + c) * hw + i];
+		db[c] = s + 0.0f;
+	}
+	for (size_t j = 0; j < wsz; j++) {
+		float s = 0.0f;
+		for (size_t n = 0; n < N; n++) s += gw[n * wsz + j];
+		dw[j] = s + 0.0f;
+	}
+	free(col);
+	free(gw);
 }
 
 /* ---- maxpool2d (ops.cpp:1609-1705) ---- */

@@ -138,6 +138,29 @@ def test_conv2d_matches_reference(fuse, stride, pad):
         assert db.tobytes() == db_r.tobytes()
 
 
+@pytest.mark.parametrize("stride,pad,dil,groups", [(1, 1, 2, 1), (2, 2, 2, 2), (1, 0, 1, 3), (2, 1, 3, 6)])
+def test_conv2d_dilated_grouped_matches_reference(stride, pad, dil, groups):
+    """conv2d with dilation and groups (ops.cpp:1525-1607): GEMM-built outputs to the reference test's
+    GEMM tolerance, the bias gradient (plain loops) bit for bit."""
+    N, Cin, H, W, Cout, kh, kw = 2, 6, 11, 10, 6, 3, 3
+    x, w, b = nrm(31, N, Cin, H, W), rnd(32, Cout, Cin // groups, kh, kw), rnd(33, Cout)
+    ho = (H + 2 * pad - (dil * (kh - 1) + 1)) // stride + 1
+    wo = (W + 2 * pad - (dil * (kw - 1) + 1)) // stride + 1
+    g = nrm(34, N, Cout, ho, wo)
+    y_r, dx_r = orc.zeros(N, Cout, ho, wo), orc.zeros(N, Cin, H, W)
+    dw_r, db_r = orc.zeros(Cout, Cin // groups, kh, kw), orc.zeros(Cout)
+    ref.ref_conv2d_ex(N, Cin, H, W, Cout, kh, kw, stride, pad, dil, groups, P(x), P(w), P(b), P(g), P(y_r), P(dx_r),
+                      P(dw_r), P(db_r))
+    y, dx = orc.zeros(N, Cout, ho, wo), orc.zeros(N, Cin, H, W)
+    dw, db = orc.zeros(Cout, Cin // groups, kh, kw), orc.zeros(Cout)
+    O.orc_conv2d_ex_fwd(N, Cin, H, W, Cout, kh, kw, stride, pad, dil, groups, P(x), P(w), P(b), P(y))
+    O.orc_conv2d_ex_bwd(N, Cin, H, W, Cout, kh, kw, stride, pad, dil, groups, P(g), P(x), P(w), P(dx), P(dw), P(db))
+    for got, want in ((y, y_r), (dx, dx_r), (dw, dw_r)):
+        ok, err = close(got, want, rel=1e-4, floor=1e-5)
+        assert ok, err
+    assert db.tobytes() == db_r.tobytes()
+
+
 @pytest.mark.parametrize("k,stride", [(2, 2), (3, 1), (3, 2)])
 def test_maxpool_bitwise(k, stride):
     N, C, H, W = 2, 3, 9, 10
