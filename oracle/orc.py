@@ -54,6 +54,9 @@ _ORC_SIGS = {
     "orc_maxpool2d_bwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _i],
     "orc_conv2d_ex_fwd": [_sz] * 11 + [_p, _p, _p, _p],
     "orc_conv2d_ex_bwd": [_sz] * 11 + [_p, _p, _p, _p, _p, _p],
+    "orc_bn_running_update": [_sz, _sz, _f, _p, _p, _p, _p],
+    "orc_batchnorm_eval_fwd": [_sz, _sz, _sz, _p, _p, _p, _p, _p, _f, _i, _p],
+    "orc_batchnorm_eval_bwd": [_sz, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _f, _i, _p, _p, _p],
     "orc_avgpool2d_fwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p],
     "orc_avgpool2d_bwd": [_sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _i],
     "orc_reduce_axis_fwd": [_sz, _sz, _sz, _i, _p, _p],

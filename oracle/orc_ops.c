@@ -315,6 +315,82 @@ void orc_attention_bwd(size_t N, size_t Tq, size_t Tk, size_t D, size_t H, const
 	free(ds);
 }
 
+/* ---- BatchNorm module: running statistics and evaluation mode (batchnorm.cpp:27-60) ----
+ * Training forwards update rm = (1-m)*rm + m*mean and rv = (1-m)*rv + (m*var)*(n/(n-1)) (only rm
+ * when n = 1), from the batch statistics of orc_batchnorm_fwd. Evaluation composes the reference's
+ * broadcasting ops: inv = 1/sqrt(rv + eps), normed = (x - rm)*inv, y = normed*w + b (ReLU on top when
+ * fused). Its backward, for Y's gradient gy (the caller's seed, stored as g + 0), follows the op graph:
+ * every node's gradient is stored as v + 0, ReLU passes g or +0, and the broadcast parameters' gradients
+ * are reduced to [1, C, 1, 1] as sum_to_shape does (ops.cpp:35-53): over axis 0, then 2, then 3, each
+ * only when its extent is not 1, each a serial sum from zero. */
+void orc_bn_running_update(size_t C, size_t n, float momentum, const float* mean, const float* var, float* rm,
+		float* rv) {
+	const float unbiased = n > 1 ? (float)n / (float)(n - 1) : 0.0f;
+	for (size_t c = 0; c < C; c++) {
+		rm[c] = (1.0f - momentum) * rm[c] + momentum * mean[c];
+		if (n > 1) rv[c] = (1.0f - momentum) * rv[c] + momentum * var[c] * unbiased;
+	}
+}
+
+void orc_reduce_axis_fwd(size_t outer, size_t n, size_t inner, int average, const float* x, float* y);
+
+static void sum_to_channels(size_t N, size_t C, size_t H, size_t W, const float* t, float* out) {
+	float* a = (float*)malloc(N * C * H * W * sizeof(float));
+	float* b = (float*)malloc(N * C * H * W * sizeof(float));
+	memcpy(a, t, N * C * H * W * sizeof(float));
+	size_t n0 = N, h = H, w = W;
+	if (n0 != 1) { orc_reduce_axis_fwd(1, n0, C * h * w, 0, a, b); memcpy(a, b, C * h * w * sizeof(float)); n0 = 1; }
+	if (h != 1) { orc_reduce_axis_fwd(C, h, w, 0, a, b); memcpy(a, b, C * w * sizeof(float)); h = 1; }
+	if (w != 1) { orc_reduce_axis_fwd(C, w, 1, 0, a, b); memcpy(a, b, C * sizeof(float)); w = 1; }
+	memcpy(out, a, C * sizeof(float));
+	free(a);
+	free(b);
+}
+
+void orc_batchnorm_eval_fwd(size_t N, size_t C, size_t S, const float* x, const float* w, const float* b,
+		const float* rm, const float* rv, float eps, int fuse_relu, float* y) {
+	for (size_t c = 0; c < C; c++) {
+		const float inv = 1.0f / sqrtf(rv[c] + eps);
+		for (size_t n = 0; n < N; n++)
+			for (size_t s = 0; s < S; s++) {
+				const size_t i = (n * C + c) * S + s;
+				const float o = ((x[i] - rm[c]) * inv) * w[c] + b[c];
+				y[i] = fuse_relu ? (o > 0.0f ? o : 0.0f) : o;
+			}
+	}
+}
+
+void orc_batchnorm_eval_bwd(size_t N, size_t C, size_t H, size_t W, const float* gy, const float* x, const float* w,
+		const float* b, const float* rm, const float* rv, float eps, int fuse_relu, float* dx, float* dw, float* db) {
+	const size_t S = H * W, T = N * C * S;
+	float* r = (float*)malloc(T * sizeof(float));
+	float* t = (float*)malloc(T * sizeof(float));
+	float* red = (float*)malloc(C * sizeof(float));
+	for (size_t c = 0; c < C; c++) {
+		const float inv = 1.0f / sqrtf(rv[c] + eps);
+		for (size_t n = 0; n < N; n++)
+			for (size_t s = 0; s < S; s++) {
+				const size_t i = (n * C + c) * S + s;
+				const float normed = (x[i] - rm[c]) * inv;
+				const float g = gy[i] + 0.0f;                                  /* Y's gradient */
+				const float ri = fuse_relu ? ((normed * w[c] + b[c] > 0.0f ? g : 0.0f) + 0.0f) : g;
+				r[i] = ri;                                                     /* the add node's gradient */
+				const float g1 = ri + 0.0f;                                    /* normed * w */
+				t[i] = g1 * normed;
+				const float g2 = g1 * w[c] + 0.0f;                             /* normed */
+				const float g3 = g2 * inv + 0.0f;                              /* x - rm */
+				dx[i] = g3 + 0.0f;
+			}
+	}
+	sum_to_channels(N, C, H, W, t, red);
+	for (size_t c = 0; c < C; c++) dw[c] = red[c] + 0.0f;
+	sum_to_channels(N, C, H, W, r, red);
+	for (size_t c = 0; c < C; c++) db[c] = red[c] + 0.0f;
+	free(r);
+	free(t);
+	free(red);
+}
+
 /* ---- conv2d / conv2d_relu (ops.cpp:188-243, 1345-1472) ---- */
 /* column matrix [Cin*kh*kw, ho*wo] of one sample (or one group's channels); tap (ph, pw) reads input
  * row oh*st + ph*dl - pd and column ow*st + pw*dl - pd, zero outside (ops.cpp:1486-1500 with dl > 1) */

@@ -161,6 +161,33 @@ def test_conv2d_dilated_grouped_matches_reference(stride, pad, dil, groups):
     assert db.tobytes() == db_r.tobytes()
 
 
+@pytest.mark.parametrize("fuse", [0, 1])
+@pytest.mark.parametrize("steps", [1, 3])
+def test_batchnorm_module_eval_bitwise(fuse, steps):
+    """BatchNorm2d (batchnorm.cpp:27-60, default eps 1e-5, momentum 0.1, weight 1, bias 0): `steps`
+    training forwards update the running statistics, then one evaluation-mode forward and its backward,
+    all bit for bit."""
+    N, C, H, W = 4, 3, 5, 6
+    x = nrm(35, N, C, H, W) * 2.0 + 0.5
+    g = nrm(36, N, C, H, W)
+    y_r, dx_r, dw_r, db_r = orc.zeros(N, C, H, W), orc.zeros(N, C, H, W), orc.zeros(C), orc.zeros(C)
+    rm_r, rv_r = orc.zeros(C), orc.zeros(C)
+    ref.ref_bn2d_module(N, C, H, W, steps, 1, fuse, P(x), P(g), P(y_r), P(dx_r), P(dw_r), P(db_r), P(rm_r), P(rv_r))
+    w, b = np.ones(C, np.float32), np.zeros(C, np.float32)
+    rm, rv = np.zeros(C, np.float32), np.ones(C, np.float32)
+    y_t, alive = orc.zeros(N, C, H, W), np.zeros((N, C, H, W), np.uint8)
+    mean, var, inv = orc.zeros(C), orc.zeros(C), orc.zeros(C)
+    for _ in range(steps):
+        O.orc_batchnorm_fwd(N, C, H * W, P(x), P(w), P(b), 1e-5, fuse, P(y_t), P(alive), P(mean), P(var), P(inv))
+        O.orc_bn_running_update(C, N * H * W, 0.1, P(mean), P(var), P(rm), P(rv))
+    assert rm.tobytes() == rm_r.tobytes() and rv.tobytes() == rv_r.tobytes()
+    y, dx, dw, db = orc.zeros(N, C, H, W), orc.zeros(N, C, H, W), orc.zeros(C), orc.zeros(C)
+    O.orc_batchnorm_eval_fwd(N, C, H * W, P(x), P(w), P(b), P(rm), P(rv), 1e-5, fuse, P(y))
+    O.orc_batchnorm_eval_bwd(N, C, H, W, P(g), P(x), P(w), P(b), P(rm), P(rv), 1e-5, fuse, P(dx), P(dw), P(db))
+    for got, want in ((y, y_r), (dx, dx_r), (dw, dw_r), (db, db_r)):
+        assert got.tobytes() == want.tobytes()
+
+
 @pytest.mark.parametrize("k,stride", [(2, 2), (3, 1), (3, 2)])
 def test_maxpool_bitwise(k, stride):
     N, C, H, W = 2, 3, 9, 10
