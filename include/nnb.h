@@ -211,12 +211,14 @@ NNB_API nnb_status nnb_batchnorm_bwd(void* stream, size_t N, size_t C, size_t S,
 NNB_API nnb_status nnb_batchnorm_running_update(void* stream, size_t C, size_t count, const float* mean,
 		const float* var, float momentum, float* running_mean, float* running_var);
 /* Evaluation mode (batchnorm.cpp:51-55): y = ((x - running_mean) / sqrt(running_var + eps)) w + b,
- * optionally followed by ReLU with its alive mask; the backward gives dx, dweight and dbias. */
+ * optionally followed by ReLU with its alive mask; the backward gives dx, dweight and dbias. x is
+ * [N, C, H, W] (S = H * W in the forward; a 3-D input is [N, C, L, 1], a 2-D one [N, C, 1, 1]); the
+ * parameter gradients are summed over N, then H, then W, as the reference's sum_to_shape does. */
 NNB_API nnb_status nnb_batchnorm_eval_fwd(void* stream, size_t N, size_t C, size_t S, const float* x,
 		const float* running_mean, const float* running_var, float eps, const float* weight, const float* bias,
 		int fuse_relu, float* y, unsigned char* alive);
-NNB_API nnb_status nnb_batchnorm_eval_bwd(void* stream, size_t N, size_t C, size_t S, const float* g, const float* x,
-		const float* running_mean, const float* running_var, float eps, const float* weight,
+NNB_API nnb_status nnb_batchnorm_eval_bwd(void* stream, size_t N, size_t C, size_t H, size_t W, const float* g,
+		const float* x, const float* running_mean, const float* running_var, float eps, const float* weight,
 		const unsigned char* alive, float* dx, int dx_first, float* dweight, int dweight_first, float* dbias,
 		int dbias_first);
 
@@ -264,6 +266,15 @@ NNB_API nnb_status nnb_masked_softmax_fwd(void* stream, size_t N, size_t H, size
 		const float* key_padding_mask, int causal, float scale);
 NNB_API nnb_status nnb_masked_softmax_bwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk,
 		const float* probs, float* grad, const float* key_padding_mask, int causal, float scale);
+/* scaled_masked_softmax (ops.hpp scaled_masked_softmax; ops.cpp:1298-1343): y = the masked softmax of
+ * x [N, H, Tq, Tk] (x is not modified; causal rows need not be square). The backward writes
+ * dL/dx into dx under the grad_accum rule: dx_first stores (0 at masked positions), otherwise it
+ * adds and leaves masked positions as they are. */
+NNB_API nnb_status nnb_scaled_masked_softmax_fwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk,
+		const float* x, float* y, const float* key_padding_mask, int causal, float scale);
+NNB_API nnb_status nnb_scaled_masked_softmax_bwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk,
+		const float* y, const float* g, float* dx, int dx_first, const float* key_padding_mask, int causal,
+		float scale);
 
 /* ---- convolution (replaces conv2d / conv2d_relu, ops.hpp:402; ops.cpp:1345-1472) ------------ */
 
@@ -385,11 +396,23 @@ NNB_API nnb_status nnb_adamw_step_device(void* stream, size_t n, float* w, const
  *   zero are cleared on the stream by every call. Calls that overlap on the GPU race on the array:
  *   order them (one stream, or events) yourself.
  * - No cudaMalloc/cudaFree or other allocating routine is called. A bounded wait that expires in this
- *   entry point's kernels is recorded in a device word of its own, not in nnb_device_error.
+ *   entry point's kernels is recorded in a device word of its own, not in nnb_device_error: read it
+ *   with nnb_sgemm_noalloc_error after the calls whose results matter.
+ * - The tile is always 256 columns wide and the product is never cut along its depth. nnb_sgemm_ex
+ *   cuts a long-depth product (k >= 2 * max(1024, n)) into consecutive depth pieces summed in order
+ *   (its counterpart of the reference's depth cut, gemm.cpp:453-485), so for such shapes the two
+ *   entry points give different bits (both within the fp32 bound) and this one keeps fewer SMs busy
+ *   when the output is small. For every other shape they give the same bits.
  */
 NNB_API nnb_status nnb_sgemm_noalloc(void* stream, int trans_a, int trans_b, size_t m, size_t n,
 		size_t k, const float* a, size_t lda, const float* b, size_t ldb, float* c, size_t ldc,
 		int accumulate, int math_mode);
+/* The error word of nnb_sgemm_noalloc's kernels on the current device (no counterpart in the
+ * reference): *out = 0 if no bounded wait in them has expired since the word was last cleared,
+ * otherwise the code of the first wait that gave up (1-6, the same codes nnb_device_error reports);
+ * the C of that call is then incomplete. Waits for `stream` to reach this point and clears the word
+ * when `clear` is set. Allocates nothing (plain copies from and to the device symbol). */
+NNB_API nnb_status nnb_sgemm_noalloc_error(void* stream, int* out, int clear);
 
 /* ---- random streams and dropout (src/random.cpp, src/nn/dropout.cpp) ------------------------ */
 

@@ -1086,3 +1086,25 @@ extern "C" nnb_status nnb_sgemm_noalloc(void* stream, int trans_a, int trans_b, 
 		return launch_main<1, 256>(s, dev, nd->sm_count, nd->error, d, pl, nd->scratch, false);
 	return launch_main<0, 256>(s, dev, nd->sm_count, nd->error, d, pl, nd->scratch, false);
 }
+
+extern "C" nnb_status nnb_sgemm_noalloc_error(void* stream, int* out, int clear) {
+	using namespace nnb;
+	using namespace nnb::gemm;
+	if (!out) return fail(NNB_ERR_INVALID, "sgemm_noalloc_error: out is null");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NoAllocDevice* nd = nullptr;
+	int dev = 0;
+	NNB_TRY(noalloc_setup(&nd, &dev));
+	// Plain copies from and to the symbol on the caller's stream: no allocation; the host value is
+	// read once the stream has reached this point.
+	int word = 0;
+	NNB_CUDA_TRY(cudaMemcpyFromSymbolAsync(&word, g_noalloc_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s));
+	NNB_CUDA_TRY(cudaStreamSynchronize(s));
+	*out = word;
+	if (clear && word != 0) {
+		static const int zero = 0;
+		NNB_CUDA_TRY(cudaMemcpyToSymbolAsync(g_noalloc_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s));
+		NNB_CUDA_TRY(cudaStreamSynchronize(s));
+	}
+	return NNB_OK;
+}

@@ -113,6 +113,68 @@ __global__ void masked_softmax_bwd_kernel(const float* __restrict__ y, float* __
 	}
 }
 
+// scaled_masked_softmax (ops.cpp:1298-1343) out of place: y = softmax rows of x, the same row
+// arithmetic as masked_softmax_fwd_kernel. Causal rows need not be square here (row i keeps keys
+// 0..i of however many there are), as in the reference.
+__global__ void softmax_rows_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, long long rows, int H,
+		int Tq, int Tk, const float* __restrict__ pad, int causal, float scale) {
+	const int lane = threadIdx.x & 31;
+	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+	if (r >= rows) return;
+	const long long n = r / ((long long)H * Tq);
+	const int i = (int)(r % Tq);
+	const float* ph = pad ? pad + n * Tk : nullptr;
+	const float* xr = x + r * Tk;
+	float* row = y + r * Tk;
+	float m = -INFINITY;
+	for (int j = lane; j < Tk; j += 32) {
+		float v = xr[j] * scale;
+		if (ph && ph[j] == 0.0f) v = -1e9f;
+		if (causal && j > i) v = -2e9f;
+		row[j] = v;
+		m = fmaxf(m, v);
+	}
+	m = warp_max(m);
+	const int live = causal ? min(Tk, i + 1) : Tk;
+	float s = 0.0f;
+	for (int j = lane; j < Tk; j += 32) {
+		if (j < live) {
+			const float e = expf(row[j] - m);
+			row[j] = e;
+			s += e;
+		} else {
+			row[j] = 0.0f;
+		}
+	}
+	s = warp_sum(s);
+	for (int j = lane; j < Tk; j += 32) row[j] = row[j] / s;
+}
+
+// Its backward into a gradient buffer under the grad_accum rule: first stores term + 0 (0 at masked
+// positions), otherwise adds term and leaves masked positions untouched (ops.cpp:1331-1338).
+__global__ void softmax_rows_bwd_kernel(const float* __restrict__ y, const float* __restrict__ g,
+		float* __restrict__ dx, int first, long long rows, int H, int Tq, int Tk, const float* __restrict__ pad,
+		int causal, float scale) {
+	const int lane = threadIdx.x & 31;
+	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+	if (r >= rows) return;
+	const long long n = r / ((long long)H * Tq);
+	const int i = (int)(r % Tq);
+	const float* ph = pad ? pad + n * Tk : nullptr;
+	const float* yr = y + r * Tk;
+	const float* gr = g + r * Tk;
+	float* dr = dx + r * Tk;
+	float dot = 0.0f;
+	for (int j = lane; j < Tk; j += 32) dot += gr[j] * yr[j];
+	dot = warp_sum(dot);
+	for (int j = lane; j < Tk; j += 32) {
+		const bool masked = (ph && ph[j] == 0.0f) || (causal && j > i);
+		const float term = scale * (yr[j] * (gr[j] - dot));
+		if (first) dr[j] = masked ? 0.0f : term + 0.0f;
+		else if (!masked) dr[j] += term;
+	}
+}
+
 }  // namespace
 
 // Head-batched GEMM over all (n, h): X_(n,h) = x + n * sx_n + h * sx_h
@@ -301,6 +363,32 @@ nnb_status nnb_masked_softmax_bwd(void* stream, size_t N, size_t H, size_t Tq, s
 	nnb::masked_softmax_bwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(probs, grad, rows, (int)H, (int)Tq,
 		(int)Tk, key_padding_mask, causal, scale);
 	return nnb::cuda_status(cudaGetLastError(), "masked_softmax_bwd launch");
+}
+
+nnb_status nnb_scaled_masked_softmax_fwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk, const float* x,
+		float* y, const float* key_padding_mask, int causal, float scale) {
+	if (Tk == 0) return nnb::fail(NNB_ERR_SHAPE, "scaled_masked_softmax: empty rows");
+	const long long rows = (long long)N * H * Tq;
+	if (rows == 0) return NNB_OK;
+	if (!x || !y) return nnb::fail(NNB_ERR_INVALID, "scaled_masked_softmax_fwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	nnb::TraceScope ts(s, nnb::kTraceAttention);
+	nnb::softmax_rows_fwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(x, y, rows, (int)H, (int)Tq,
+		(int)Tk, key_padding_mask, causal, scale);
+	return nnb::cuda_status(cudaGetLastError(), "scaled_masked_softmax_fwd launch");
+}
+
+nnb_status nnb_scaled_masked_softmax_bwd(void* stream, size_t N, size_t H, size_t Tq, size_t Tk, const float* y,
+		const float* g, float* dx, int dx_first, const float* key_padding_mask, int causal, float scale) {
+	if (Tk == 0) return nnb::fail(NNB_ERR_SHAPE, "scaled_masked_softmax: empty rows");
+	const long long rows = (long long)N * H * Tq;
+	if (rows == 0) return NNB_OK;
+	if (!y || !g || !dx) return nnb::fail(NNB_ERR_INVALID, "scaled_masked_softmax_bwd: null pointer");
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	nnb::TraceScope ts(s, nnb::kTraceAttention);
+	nnb::softmax_rows_bwd_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(y, g, dx, dx_first, rows, (int)H,
+		(int)Tq, (int)Tk, key_padding_mask, causal, scale);
+	return nnb::cuda_status(cudaGetLastError(), "scaled_masked_softmax_bwd launch");
 }
 
 }  // extern "C"

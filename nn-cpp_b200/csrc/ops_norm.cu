@@ -505,36 +505,74 @@ __global__ void bn_eval_fwd_kernel(long long total, long long C, long long S, co
 	}
 }
 
-// dx = ((g * w) * inv) (the chain of the reference's mul / sub backward); per channel, from +0 in
-// (sample, position) order: dw += g * normed, db += g
+// dx: the gradient through the reference's op graph add(mul(normed, w), b) then mul(x - mean, inv),
+// each node's gradient stored with its +0 (ops.cpp:67-73): g1 = g (0 where the fused ReLU was off),
+// dx = ((g1 * w) + 0) * inv + 0, stored (first) or added.
 __global__ void bn_eval_dx_kernel(long long total, long long C, long long S, const float* __restrict__ g,
 		const unsigned char* __restrict__ alive, const float* __restrict__ rvar, float eps, const float* __restrict__ w,
 		float* __restrict__ dx, int first) {
 	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
 		const int c = (int)((i / S) % C);
-		const float gv = (alive && !alive[i]) ? 0.0f : g[i];
-		const float v = (gv * w[c]) * bn_eval_inv(rvar, c, eps);
+		const float gv = ((alive && !alive[i]) ? 0.0f : g[i]) + 0.0f;
+		const float v = ((gv * w[c]) + 0.0f) * bn_eval_inv(rvar, c, eps) + 0.0f;
 		dx[i] = first ? v + 0.0f : dx[i] + v;
 	}
 }
 
-__global__ void bn_eval_param_kernel(long long N, long long C, long long S, const float* __restrict__ g,
+// dweight and dbias: per element terms g1 * normed and g1, reduced to the {1, C, 1, 1} parameter
+// shape as the reference's sum_to_shape does it (ops.cpp:35-53): over the sample axis first (one
+// sum from 0 for every (c, h, w)), then over h, then over w, each axis only when its size is not 1;
+// the result is stored with +0 (first) or added. One block per channel; each thread owns columns
+// w = tid, tid + blockDim, ... and the column totals are added in w order by thread 0.
+__global__ void bn_eval_param_kernel(long long N, long long C, long long H, long long W, const float* __restrict__ g,
 		const unsigned char* __restrict__ alive, const float* __restrict__ x, const float* __restrict__ rmean,
 		const float* __restrict__ rvar, float eps, float* __restrict__ dw, int dw_first, float* __restrict__ db,
 		int db_first) {
-	const int c = blockIdx.x * blockDim.x + threadIdx.x;
-	if (c >= C) return;
-	const float inv = bn_eval_inv(rvar, c, eps);
-	float sw = 0.0f, sb = 0.0f;
-	for (long long n = 0; n < N; ++n)
-		for (long long p = 0; p < S; ++p) {
-			const long long i = (n * C + c) * S + p;
-			const float gv = (alive && !alive[i]) ? 0.0f : g[i];
-			sw += gv * ((x[i] - rmean[c]) * inv);
-			sb += gv;
+	__shared__ float col_w[256], col_b[256];
+	const long long c = blockIdx.x;
+	const float inv = bn_eval_inv(rvar, (int)c, eps);
+	const float mu = rmean[c];
+	float red_w = 0.0f, red_b = 0.0f;
+	float one_w = 0.0f, one_b = 0.0f;           // the single column's total when W == 1
+	for (long long w0 = 0; w0 < W; w0 += blockDim.x) {
+		const long long w = w0 + threadIdx.x;
+		if (w < W) {
+			float hw = 0.0f, hb = 0.0f;
+			for (long long h = 0; h < H; ++h) {
+				float nw = 0.0f, nb = 0.0f;
+				for (long long n = 0; n < N; ++n) {
+					const long long i = ((n * C + c) * H + h) * W + w;
+					const float gv = ((alive && !alive[i]) ? 0.0f : g[i]) + 0.0f;
+					const float tw = gv * ((x[i] - mu) * inv);
+					if (N == 1) { nw = tw; nb = gv; }
+					else { nw += tw; nb += gv; }
+				}
+				if (H == 1) { hw = nw; hb = nb; }
+				else { hw += nw; hb += nb; }
+			}
+			col_w[threadIdx.x] = hw;
+			col_b[threadIdx.x] = hb;
 		}
-	if (dw) dw[c] = dw_first ? sw + 0.0f : dw[c] + sw;
-	if (db) db[c] = db_first ? sb + 0.0f : db[c] + sb;
+		__syncthreads();
+		if (threadIdx.x == 0) {
+			const long long cnt = min((long long)blockDim.x, W - w0);
+			if (W == 1) {
+				one_w = col_w[0];
+				one_b = col_b[0];
+			} else {
+				for (long long j = 0; j < cnt; ++j) {
+					red_w += col_w[j];
+					red_b += col_b[j];
+				}
+			}
+		}
+		__syncthreads();
+	}
+	if (threadIdx.x == 0) {
+		const float tw = W == 1 ? one_w : red_w, tb = W == 1 ? one_b : red_b;
+		if (dw) dw[c] = dw_first ? tw + 0.0f : dw[c] + (tw + 0.0f);
+		if (db) db[c] = db_first ? tb + 0.0f : db[c] + (tb + 0.0f);
+	}
 }
 
 }  // namespace
@@ -568,22 +606,25 @@ nnb_status nnb_batchnorm_eval_fwd(void* stream, size_t N, size_t C, size_t S, co
 	return nnb::cuda_status(cudaGetLastError(), "batchnorm_eval_fwd launch");
 }
 
-nnb_status nnb_batchnorm_eval_bwd(void* stream, size_t N, size_t C, size_t S, const float* g, const float* x,
-		const float* running_mean, const float* running_var, float eps, const float* weight, const unsigned char* alive,
-		float* dx, int dx_first, float* dweight, int dweight_first, float* dbias, int dbias_first) {
+nnb_status nnb_batchnorm_eval_bwd(void* stream, size_t N, size_t C, size_t H, size_t W, const float* g,
+		const float* x, const float* running_mean, const float* running_var, float eps, const float* weight,
+		const unsigned char* alive, float* dx, int dx_first, float* dweight, int dweight_first, float* dbias,
+		int dbias_first) {
+	const long long S = (long long)H * W;
 	const long long total = (long long)N * C * S;
 	if (total == 0) return NNB_OK;
 	if (!g || !x || !running_mean || !running_var || !weight)
 		return nnb::fail(NNB_ERR_INVALID, "batchnorm_eval_bwd: null input");
+	if (C > 0x7fffffffLL) return nnb::fail(NNB_ERR_UNSUPPORTED, "batchnorm_eval_bwd: too many channels");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	if (dx) {
 		nnb::TraceScope ts(s, nnb::kTraceRowwise);
-		nnb::bn_eval_dx_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, (long long)C, (long long)S, g, alive,
+		nnb::bn_eval_dx_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, (long long)C, S, g, alive,
 			running_var, eps, weight, dx, dx_first);
 	}
 	if (dweight || dbias) {
 		nnb::TraceScope ts(s, nnb::kTraceRowwise);
-		nnb::bn_eval_param_kernel<<<(unsigned)((C + 127) / 128), 128, 0, s>>>((long long)N, (long long)C, (long long)S, g,
+		nnb::bn_eval_param_kernel<<<(unsigned)C, 256, 0, s>>>((long long)N, (long long)C, (long long)H, (long long)W, g,
 			alive, x, running_mean, running_var, eps, dweight, dweight_first, dbias, dbias_first);
 	}
 	return nnb::cuda_status(cudaGetLastError(), "batchnorm_eval_bwd launch");

@@ -66,6 +66,7 @@ _SIGS = {
     "nnb_sgemm_strided_batched": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz, _p, _sz, _sz,
                                    _sz, _i, _i], _i),
     "nnb_sgemm_noalloc": ([_p, _i, _i, _sz, _sz, _sz, _p, _sz, _p, _sz, _p, _sz, _i, _i], _i),
+    "nnb_sgemm_noalloc_error": ([_p, _p, _i], _i),
     "nnb_matmul": ([_p, _p, _p, _i, _p, _p, _i, _i, _i, _p, _p, _p], _i),
     "nnb_linear_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p], _i),
     "nnb_linear_gelu_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p], _i),
@@ -86,6 +87,8 @@ _SIGS = {
                                    _p, _i], _i),
     "nnb_masked_softmax_fwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _i, _f], _i),
     "nnb_masked_softmax_bwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _f], _i),
+    "nnb_scaled_masked_softmax_fwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _f], _i),
+    "nnb_scaled_masked_softmax_bwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _p, _i, _f], _i),
     "nnb_conv2d_fwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _i, _p, _p], _i),
     "nnb_conv2d_bwd": ([_p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i], _i),
     "nnb_relu_fwd": ([_p, _sz, _p, _p], _i),
@@ -110,7 +113,7 @@ _SIGS = {
                           _i),
     "nnb_batchnorm_running_update": ([_p, _sz, _sz, _p, _p, _f, _p, _p], _i),
     "nnb_batchnorm_eval_fwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _f, _p, _p, _i, _p, _p], _i),
-    "nnb_batchnorm_eval_bwd": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _f, _p, _p, _p, _i, _p, _i, _p, _i], _i),
+    "nnb_batchnorm_eval_bwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _f, _p, _p, _p, _i, _p, _i, _p, _i], _i),
     "nnb_cross_entropy_fwd": ([_p, _sz, _sz, _p, _p, _p, _p, _p], _i),
     "nnb_cross_entropy_bwd": ([_p, _sz, _sz, _p, _p, _p, _p, _p, _i], _i),
     "nnb_sequence_ce_fwd": ([_p, _sz, _sz, _p, _p, _c.c_int64, _f, _p, _p, _p], _i),

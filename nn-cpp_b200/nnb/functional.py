@@ -101,6 +101,109 @@ def linear_gelu(x: Value, weight: Value, bias: Value) -> Value:
     return Value.node(y, (x, weight, bias), backward)
 
 
+# ---- matmul / matmul_bt (ops.cpp:683-712, 747-773) ------------------------------------------------
+
+def _sum_to_shape_into(g: torch.Tensor, target: tuple, dst: torch.Tensor, first: int) -> None:
+    """accumulate_grad (ops.cpp:110-117) of a gradient with the broadcast shape g.shape into dst (the
+    gradient of a value shaped `target`): the leading axes are summed away one at a time (each a
+    Tensor::sum(0), src/tensor.cpp:422-455), then every axis where target has 1 and g does not, in
+    axis order (sum_to_shape, ops.cpp:35-53); the result is stored (first) or added into dst."""
+    cur = g
+    while cur.dim() > len(target):
+        red = empty(cur.shape[1:])
+        check(lib().nnb_column_sum(_s(), cur.shape[0], red.numel(), _p(cur), _p(red), 1))
+        cur = red
+    for i, t in enumerate(target):
+        if t == 1 and cur.shape[i] != 1:
+            sh = list(cur.shape)
+            red = empty(sh[:i] + [1] + sh[i + 1:])
+            check(lib().nnb_reduce_axis_fwd(_s(), math.prod(sh[:i]), sh[i], math.prod(sh[i + 1:]), _p(cur), 0, _p(red)))
+            cur = red
+    if tuple(cur.shape) != tuple(target):
+        raise TensorShapeError("matmul: gradient does not reduce to the operand's shape")
+    check(lib().nnb_accumulate(_s(), cur.numel(), _p(cur), _p(dst), first, 0))
+
+
+def _accumulate_grad(v: Value, grad: torch.Tensor) -> None:
+    dst, first = v.grad_accum()
+    if tuple(grad.shape) == v.shape:
+        check(lib().nnb_accumulate(_s(), grad.numel(), _p(grad), _p(dst), first, 0))
+    else:
+        _sum_to_shape_into(grad, v.shape, dst, first)
+
+
+def _sgemm_into(ta, tb, m, n, k, a, lda, b, ldb, c, ldc, first):
+    check(lib().nnb_sgemm(_s(), ta, tb, m, n, k, _p(a), lda, _p(b), ldb, _p(c), ldc, 0 if first else 1))
+
+
+def _matmul_value(a: Value, b: Value, bt: bool) -> Value:
+    from . import matmul as tensor_matmul
+    y = tensor_matmul(a.data, b.data, False, bt)
+
+    def backward(g):
+        if len(b.shape) == 2 and len(a.shape) >= 2:
+            # b a plain matrix: a's leading axes fold into M rows and both gradients come from one
+            # GEMM each, stored (first) or accumulated (ops.cpp:686-700, 750-761)
+            if bt:
+                n, K = b.shape
+            else:
+                K, n = b.shape
+            M = a.data.numel() // K
+            if _need(a):
+                da, fa = a.grad_accum()
+                if bt:
+                    _sgemm_into(0, 0, M, K, n, g, n, b.data, K, da, K, fa)
+                else:
+                    _sgemm_into(0, 1, M, K, n, g, n, b.data, n, da, K, fa)
+            if _need(b):
+                db, fb = b.grad_accum()
+                if bt:
+                    _sgemm_into(1, 0, n, K, M, g, n, a.data, K, db, K, fb)
+                else:
+                    _sgemm_into(1, 0, K, n, M, a.data, K, g, n, db, n, fb)
+            return
+        # batched b: the batched products, then the broadcast axes summed away (ops.cpp:703-710)
+        if _need(a):
+            _accumulate_grad(a, tensor_matmul(g, b.data, False, not bt))
+        if _need(b):
+            _accumulate_grad(b, tensor_matmul(g, a.data, True, False) if bt else tensor_matmul(a.data, g, True, False))
+
+    return Value.node(y, (a, b), backward)
+
+
+def matmul(a: Value, b: Value) -> Value:
+    """a @ b with batch axes broadcast (nn::matmul(const Value&, const Value&), ops.cpp:683)."""
+    return _matmul_value(a, b, False)
+
+
+def matmul_bt(a: Value, b: Value) -> Value:
+    """a @ b^T over the last two axes (nn::matmul_bt, ops.cpp:747)."""
+    return _matmul_value(a, b, True)
+
+
+def scaled_masked_softmax(x: Value, scale: float, key_padding_mask: torch.Tensor | None = None,
+                          causal: bool = False) -> Value:
+    """softmax(masked(x * scale)) over the last axis of x [N, H, Tq, Tk] (ops.cpp:1298-1343): padded
+    keys (mask 0) get -1e9 and causally hidden keys (j > i) -2e9 before the softmax."""
+    if len(x.shape) != 4 or x.shape[3] == 0:
+        raise TensorShapeError("scaled_masked_softmax: x must be [N, H, Tq, Tk]")
+    N, H, Tq, Tk = x.shape
+    if key_padding_mask is not None and key_padding_mask.numel() and tuple(key_padding_mask.shape) != (N, Tk):
+        raise TensorShapeError("scaled_masked_softmax: key_padding_mask must be [N, Tk]")
+    pad = key_padding_mask if key_padding_mask is not None and key_padding_mask.numel() else None
+    y = empty(x.shape)
+    check(lib().nnb_scaled_masked_softmax_fwd(_s(), N, H, Tq, Tk, _p(x.data), _p(y), _p(pad), int(causal),
+                                              ctypes.c_float(scale)))
+
+    def backward(g):
+        if _need(x):
+            dx, f = x.grad_accum()
+            check(lib().nnb_scaled_masked_softmax_bwd(_s(), N, H, Tq, Tk, _p(y), _p(g), _p(dx), f, _p(pad), int(causal),
+                                                      ctypes.c_float(scale)))
+
+    return Value.node(y, (x,), backward)
+
+
 # ---- elementwise ------------------------------------------------------------------------------
 
 def add(a: Value, b: Value) -> Value:
@@ -221,6 +324,10 @@ def batchnorm_eval(x: Value, weight: Value, bias: Value, running_mean: torch.Ten
         raise TensorShapeError("batchnorm: needs N and C axes")
     N, C = x.shape[0], x.shape[1]
     S = x.data.numel() // max(1, N * C)
+    if len(x.shape) > 4:
+        raise TensorShapeError("batchnorm: at most four axes")
+    Hs = x.shape[2] if len(x.shape) > 2 else 1      # the axes the parameter gradients sum over, in order
+    Ws = x.shape[3] if len(x.shape) > 3 else 1
     y = empty(x.shape)
     alive = empty(x.shape, dtype=torch.uint8) if fuse_relu else None
     check(lib().nnb_batchnorm_eval_fwd(_s(), N, C, S, _p(x.data), _p(running_mean), _p(running_var),
@@ -231,7 +338,7 @@ def batchnorm_eval(x: Value, weight: Value, bias: Value, running_mean: torch.Ten
         dx, fx = x.grad_accum() if _need(x) else (None, 0)
         dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
         db, fb = bias.grad_accum() if _need(bias) else (None, 0)
-        check(lib().nnb_batchnorm_eval_bwd(_s(), N, C, S, _p(g), _p(x.data), _p(running_mean), _p(running_var),
+        check(lib().nnb_batchnorm_eval_bwd(_s(), N, C, Hs, Ws, _p(g), _p(x.data), _p(running_mean), _p(running_var),
                                            ctypes.c_float(eps), _p(weight.data), _p(alive), _p(dx), fx, _p(dw), fw,
                                            _p(db), fb))
 

@@ -111,6 +111,18 @@ class PeerBuffer:
         dist.barrier(group=self.group, device_ids=[torch.cuda.current_device()])
 
 
+def sample_shares(batch: int, world: int) -> list[tuple[int, int]]:
+    """The attention workload's partition: rank r holds samples [n0, n1) of the global batch, contiguous
+    runs as equal as possible in rank order (all heads of a sample stay on one rank)."""
+    return row_bands(batch, world, align=1)
+
+
+def share_offset_bytes(n0: int, T: int, D: int) -> int:
+    """Byte offset of sample n0 in a [batch, T, D] fp32 buffer: where a rank's share of O / dQ / dK /
+    dV lands in the owner's full-size buffers."""
+    return n0 * T * D * 4
+
+
 class ShardedAttention:
     """Multi-head attention forward + backward of a batch split by samples over the ranks, with O, dQ,
     dK and dV gathered on rank `owner` (the batch x head partition of the attention workload).
@@ -135,7 +147,7 @@ class ShardedAttention:
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         self.batch, self.T, self.D, self.heads, self.causal = batch, T, D, heads, causal
         self.device = device or torch.device("cuda", torch.cuda.current_device())
-        self.bands = row_bands(batch, self.world, align=1)
+        self.bands = sample_shares(batch, self.world)
         self.n0, self.n1 = self.bands[self.rank]
         self.local = self.n1 - self.n0
         self.out, self.dq, self.dk, self.dv = (PeerBuffer((batch, T, D), owner, group, self.device) for _ in range(4))
@@ -145,7 +157,7 @@ class ShardedAttention:
         self.group = group
 
     def _at(self, buf: "PeerBuffer") -> int:
-        return buf.ptr + self.n0 * self.T * self.D * 4
+        return buf.ptr + share_offset_bytes(self.n0, self.T, self.D)
 
     def step(self, q, k, v, go) -> None:
         """Forward and backward of this rank's samples (q, k, v, go: [local, T, D] on this device),

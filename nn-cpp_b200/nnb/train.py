@@ -38,6 +38,38 @@ from . import functional as F
 from .autograd import empty
 
 
+def shard_owners(shards: int, world: int, rank: int) -> list[int]:
+    """The virtual shards rank `rank` owns: a contiguous run, equal for every rank, in shard order."""
+    if shards % world:
+        raise ValueError("the virtual shard count must be a multiple of the number of ranks")
+    return list(range(rank * shards // world, (rank + 1) * shards // world))
+
+
+def exchange_shard_gradients(shard_grads: torch.Tensor, send: torch.Tensor, recv: torch.Tensor, chunk: int,
+                             world: int, group=None) -> None:
+    """The data-parallel step's one gradient exchange.
+
+    shard_grads [S_local, P]: this rank's per-shard gradients. The flat parameters are cut into
+    `world` slices of `chunk` elements (the last one padded). send [world, S_local, chunk] receives
+    slice d of every local shard in send[d] (padding left as it is: zero), and one all-to-all leaves in
+    recv [S, chunk] every rank's shards of THIS rank's slice, source ranks in order -- which is shard
+    order, since each rank owns a contiguous run of shards. Plain tensor copies and one collective:
+    it runs on CUDA tensors over NCCL and on CPU tensors over gloo alike."""
+    import torch.distributed as dist
+    total = shard_grads.shape[1]
+    for d in range(world):
+        d_lo, d_hi = d * chunk, min(total, (d + 1) * chunk)
+        if d_hi > d_lo:
+            send[d, :, : d_hi - d_lo].copy_(shard_grads[:, d_lo:d_hi])
+    dist.all_to_all_single(recv, send.view(world * shard_grads.shape[0], chunk), group=group)
+
+
+def gather_weight_slices(flat_w: torch.Tensor, chunk: int, rank: int, group=None) -> None:
+    """Every rank's updated slice of the flat parameters back to every rank, in place."""
+    import torch.distributed as dist
+    dist.all_gather_into_tensor(flat_w, flat_w[rank * chunk:(rank + 1) * chunk], group=group)
+
+
 class ShardedTrainer:
     def __init__(self, model, optimizer, shards: int = 8, world: int = 1, rank: int = 0, group=None):
         if shards % world:
@@ -49,7 +81,7 @@ class ShardedTrainer:
             raise NotImplementedError("dropout with more than one rank")
         self.model, self.opt = model, optimizer
         self.shards, self.world, self.rank, self.group = shards, world, rank, group
-        self.owned = list(range(rank * shards // world, (rank + 1) * shards // world))
+        self.owned = shard_owners(shards, world, rank)
         self.params = model.parameters()
         self.sizes = [p.data.numel() for p in self.params]
         self.total = sum(self.sizes)
@@ -183,18 +215,11 @@ class ShardedTrainer:
             self._adamw(s, self.total, self.flat_w.data_ptr(), self.reduced.data_ptr())
         else:
             import torch.distributed as dist
-            # my shards' gradients, cut by destination slice: send[d] = shard_grads[:, d-th slice]
-            for d in range(self.world):
-                d_lo, d_hi = d * self.chunk, min(self.total, (d + 1) * self.chunk)
-                self.send[d, :, : d_hi - d_lo].copy_(self.shard_grads[:, d_lo:d_hi])
-            # every rank's shards of my slice, source ranks in order = shards in order
-            dist.all_to_all_single(self.recv, self.send.view(self.world * len(self.owned), self.chunk),
-                                   group=self.group)
+            exchange_shard_gradients(self.shard_grads, self.send, self.recv, self.chunk, self.world, self.group)
             dist.all_gather_into_tensor(self.all_loss, self.local_loss, group=self.group)
             check(lib().nnb_column_sum(s, self.shards, self.chunk, self.recv.data_ptr(), self.reduced.data_ptr(), 1))
             self._adamw(s, self.hi - self.lo, self.flat_w[self.lo:].data_ptr(), self.reduced.data_ptr())
-            dist.all_gather_into_tensor(self.flat_w, self.flat_w[self.rank * self.chunk:(self.rank + 1) * self.chunk],
-                                        group=self.group)
+            gather_weight_slices(self.flat_w, self.chunk, self.rank, self.group)
         # mean loss over ranks (each rank's loss is the mean over its equal share of positions)
         check(lib().nnb_column_sum(s, self.world, 1, self.all_loss.data_ptr(), self.loss.data_ptr(), 1))
         check(lib().nnb_scale(s, 1, 1.0 / self.world, self.loss.data_ptr(), self.loss.data_ptr()))

@@ -81,11 +81,14 @@ _REF_SIGS = {
     "ref_time_matmul": ([_sz, _sz, _sz, _p, _p, _i], _d),
     "ref_time_sgemm": ([_sz, _sz, _sz, _p, _p, _p, _i], _d),
     "ref_matmul_nd": ([_p, _p, _i, _p, _p, _i, _i, _i, _p], _i),
+    "ref_matmul_value": ([_p, _p, _i, _p, _p, _i, _i, _i, _p, _p, _p, _p], _i),
+    "ref_scaled_masked_softmax": ([_sz, _sz, _sz, _sz, _p, _f, _p, _i, _p, _p, _p], None),
     "ref_transformer_train": ([_sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _f, _f, _i, _p, _p, _p],
                               _c.c_longlong),
     "ref_transformer_train_ex": ([_c.c_uint64, _f, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _p, _p, _p, _f, _f, _i, _p, _p,
                                   _p], _c.c_longlong),
     "ref_cnn_fwd_bwd": ([_sz, _p, _p, _p, _p, _p, _p], None),
+    "ref_cnn_fwd_bwd_ex": ([_sz, _p, _p, _p, _p, _p, _p, _p], None),
     "ref_linear": ([_sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _p, _p], None),
     "ref_layernorm": ([_sz, _sz, _p, _p, _p, _f, _p, _p, _p, _p, _p], None),
     "ref_batchnorm": ([_sz, _sz, _sz, _p, _p, _p, _f, _i, _p, _p, _p, _p, _p, _p, _p], None),
@@ -97,6 +100,7 @@ _REF_SIGS = {
     "ref_reduce4": ([_sz, _sz, _sz, _sz, _i, _i, _p, _p, _p, _p], None),
     "ref_global_avgpool": ([_sz, _sz, _sz, _sz, _p, _p, _p, _p], None),
     "ref_bn2d_module": ([_sz, _sz, _sz, _sz, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], None),
+    "ref_bn2d_module_ex": ([_sz, _sz, _sz, _sz, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p], None),
     "ref_loader_orders": ([_c.c_uint64, _i, _sz, _sz, _i, _i, _i, _p], _sz),
     "ref_loader_weighted": ([_c.c_uint64, _p, _sz, _sz, _sz, _i, _i, _p], _c.c_longlong),
     "ref_random_split": ([_sz, _p, _i, _c.c_uint64, _p, _p], _i),

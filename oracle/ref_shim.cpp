@@ -175,6 +175,39 @@ int ref_matmul_nd(const float* a, const int64_t* as, int an, const float* b, con
 
 /* ---- the reference's autograd ops, forward then one backward with upstream gradient g ---- */
 
+/*
+ * nn::matmul / nn::matmul_bt on Values (ops.cpp:683-712, 747-773): y = op(a, b), or with `twice`
+ * y = add(op(a, b), op(a, b)) so each gradient is stored by one backward rule and added to by the
+ * other; then d sum(y * g) through the graph. Returns 0, or 1 when the reference throws.
+ */
+int ref_matmul_value(const float* a, const int64_t* as, int an, const float* b, const int64_t* bs, int bn, int bt,
+		int twice, const float* g, float* y, float* da, float* db) {
+	try {
+		Value A = leaf(std::vector<size_t>(as, as + an), a), B = leaf(std::vector<size_t>(bs, bs + bn), b);
+		Value Y = bt ? nn::matmul_bt(A, B) : nn::matmul(A, B);
+		if (twice) Y = nn::add(Y, bt ? nn::matmul_bt(A, B) : nn::matmul(A, B));
+		copy_out(Y.data(), y);
+		backward_through(Y, g);
+		copy_out(A.grad(), da);
+		copy_out(B.grad(), db);
+		return 0;
+	} catch (const std::exception&) {
+		return 1;
+	}
+}
+
+/* nn::scaled_masked_softmax (ops.cpp:1298-1343) on x [N, H, Tq, Tk], then the backward of g. */
+void ref_scaled_masked_softmax(size_t N, size_t H, size_t Tq, size_t Tk, const float* x, float scale,
+		const float* pad, int causal, const float* g, float* y, float* dx) {
+	Value X = leaf({N, H, Tq, Tk}, x);
+	Tensor mask = pad ? tensor({N, Tk}, pad) : Tensor({0});
+	Value Y = nn::scaled_masked_softmax(X, scale, mask, causal != 0);
+	copy_out(Y.data(), y);
+	backward_with(Y, g);
+	copy_out(X.grad(), dx);
+}
+
+
 void ref_linear(size_t M, size_t K, size_t n, const float* x, const float* w, const float* b, const float* g,
 		float* y, float* dx, float* dw, float* db) {
 	Value X = leaf({M, K}, x), W = leaf({n, K}, w), B = leaf({n}, b);
@@ -287,10 +320,25 @@ void ref_global_avgpool(size_t N, size_t C, size_t H, size_t W, const float* x, 
 // BatchNorm2d(C) module: `train_steps` training-mode forwards on x, then (eval = 1) one
 // evaluation-mode forward, or (eval = 0) the last training forward, is returned with its backward
 // for the upstream gradient g; the running statistics are copied out after.
+void ref_bn2d_module_ex(size_t N, size_t C, size_t H, size_t W, int train_steps, int eval, int fuse_relu, const float* x,
+		const float* g, const float* w_in, const float* b_in, float* y, float* dx, float* dw, float* db,
+		float* running_mean, float* running_var);
+
 void ref_bn2d_module(size_t N, size_t C, size_t H, size_t W, int train_steps, int eval, int fuse_relu, const float* x,
 		const float* g, float* y, float* dx, float* dw, float* db, float* running_mean, float* running_var) {
+	ref_bn2d_module_ex(N, C, H, W, train_steps, eval, fuse_relu, x, g, nullptr, nullptr, y, dx, dw, db, running_mean,
+		running_var);
+}
+
+// The same with the module's weight and bias set from w_in and b_in (C floats each; null keeps the
+// defaults 1 and 0).
+void ref_bn2d_module_ex(size_t N, size_t C, size_t H, size_t W, int train_steps, int eval, int fuse_relu, const float* x,
+		const float* g, const float* w_in, const float* b_in, float* y, float* dx, float* dw, float* db,
+		float* running_mean, float* running_var) {
 	nn::BatchNorm2d bn(C);
 	std::vector<Value> params = bn.parameters();
+	if (w_in) std::memcpy(params[0].data().data().data(), w_in, C * sizeof(float));
+	if (b_in) std::memcpy(params[1].data().data().data(), b_in, C * sizeof(float));
 	Value X = leaf({N, C, H, W}, x);
 	Value Y = fuse_relu ? bn.forward_relu(X) : bn.forward(X);
 	for (int s = 1; s < train_steps; ++s) {
@@ -668,8 +716,17 @@ long long ref_transformer_train_ex(uint64_t seed, float dropout, size_t vocab, s
  * as Sequential runs it (src/nn/sequential.cpp:16-28): one forward and backward. params and grads
  * are flat in order conv1.w, conv1.b, conv2.w, conv2.b, fc1.w, fc1.b, fc2.w, fc2.b.
  */
+void ref_cnn_fwd_bwd_ex(size_t N, const float* x, const int64_t* labels, const float* params, float* loss,
+		float* logits_out, float* grads, float* fc1_out);
+
 void ref_cnn_fwd_bwd(size_t N, const float* x, const int64_t* labels, const float* params, float* loss,
 		float* logits_out, float* grads) {
+	ref_cnn_fwd_bwd_ex(N, x, labels, params, loss, logits_out, grads, nullptr);
+}
+
+// The same, also giving fc1's output before its ReLU (N x 128) in fc1_out when not null.
+void ref_cnn_fwd_bwd_ex(size_t N, const float* x, const int64_t* labels, const float* params, float* loss,
+		float* logits_out, float* grads, float* fc1_out) {
 	const std::vector<std::vector<size_t>> shapes = {{32, 1, 3, 3}, {32}, {64, 32, 3, 3}, {64}, {128, 3136}, {128},
 		{10, 128}, {10}};
 	std::vector<Value> P;
@@ -684,7 +741,9 @@ void ref_cnn_fwd_bwd(size_t N, const float* x, const int64_t* labels, const floa
 	h = nn::conv2d_relu(h, P[2], P[3], 1, 1);
 	h = nn::maxpool2d(h, 2, 2);
 	h = nn::reshape(h, {N, 3136});
-	h = nn::relu(nn::linear(h, P[4], P[5]));
+	h = nn::linear(h, P[4], P[5]);
+	copy_out(h.data(), fc1_out);
+	h = nn::relu(h);
 	Value logits = nn::linear(h, P[6], P[7]);
 	Value L = nn::cross_entropy_loss(logits, ids_tensor({N}, labels));
 	L.backward();

@@ -1,7 +1,7 @@
 """Generates the golden fixtures under tests/golden/ from the reference library itself.
 
-Run in a container that has the reference sources (oracle/Makefile builds oracle/_ref/libnnref.so
-from them):  python tests/golden/make_golden.py
+Run in a container that has the reference sources, with REF naming their root (oracle/Makefile
+builds oracle/_ref/libnnref.so from them):  REF=<reference root> python tests/golden/make_golden.py
 
 For each case (ta, tb, m, n, k, pad, seed, accumulate) it stores the inputs made by the reference
 test's problem builder (tests/test_kernels.cpp:68-86), the output of the reference's own
@@ -39,6 +39,8 @@ CASES = [
 
 
 def main():
+    if not os.environ.get("REF"):
+        raise SystemExit("set REF to the reference's source tree (the root holding src/ and tests/)")
     ref = orc.ref()
     if ref is None:
         raise SystemExit("oracle/_ref/libnnref.so not built; run make -C oracle")
@@ -79,8 +81,10 @@ def checkpoints(ref):
     for f in (plain, adamw):
         print(f, f.stat().st_size, "bytes")
     # the reference's own golden file for this model (tests/data/linear_v1.ckpt) pins the writer
-    golden = pathlib.Path(os.environ.get("REF", "/root/reference")) / "tests/data/linear_v1.ckpt"
-    if golden.exists() and golden.read_bytes() != plain.read_bytes():
+    golden = pathlib.Path(os.environ["REF"]) / "tests/data/linear_v1.ckpt"
+    if not golden.exists():
+        raise SystemExit(f"{golden} not found: REF must name the reference's source tree")
+    if golden.read_bytes() != plain.read_bytes():
         raise SystemExit("reference writer disagrees with the reference's golden checkpoint")
 
 

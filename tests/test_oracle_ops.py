@@ -163,17 +163,25 @@ def test_conv2d_dilated_grouped_matches_reference(stride, pad, dil, groups):
 
 @pytest.mark.parametrize("fuse", [0, 1])
 @pytest.mark.parametrize("steps", [1, 3])
-def test_batchnorm_module_eval_bitwise(fuse, steps):
-    """BatchNorm2d (batchnorm.cpp:27-60, default eps 1e-5, momentum 0.1, weight 1, bias 0): `steps`
-    training forwards update the running statistics, then one evaluation-mode forward and its backward,
-    all bit for bit."""
-    N, C, H, W = 4, 3, 5, 6
+@pytest.mark.parametrize("params", ["default", "random"])
+@pytest.mark.parametrize("shape", [(4, 3, 5, 6), (1, 3, 1, 7), (5, 2, 4, 1)])
+def test_batchnorm_module_eval_bitwise(fuse, steps, params, shape):
+    """BatchNorm2d (batchnorm.cpp:27-60, default eps 1e-5, momentum 0.1): `steps` training forwards
+    update the running statistics, then one evaluation-mode forward and its backward, all bit for bit;
+    with the default weight 1 and bias 0, and with random weight and bias of both signs (so the fused
+    ReLU's decisions move and every w / b term of the restatement counts); shapes with size-1 axes
+    check that a reduction is skipped where the reference skips it."""
+    N, C, H, W = shape
     x = nrm(35, N, C, H, W) * 2.0 + 0.5
     g = nrm(36, N, C, H, W)
+    if params == "default":
+        w, b = np.ones(C, np.float32), np.zeros(C, np.float32)
+    else:
+        w, b = rnd(37, C, lo=-1.5, hi=1.5), rnd(38, C, lo=-1.0, hi=1.0)
     y_r, dx_r, dw_r, db_r = orc.zeros(N, C, H, W), orc.zeros(N, C, H, W), orc.zeros(C), orc.zeros(C)
     rm_r, rv_r = orc.zeros(C), orc.zeros(C)
-    ref.ref_bn2d_module(N, C, H, W, steps, 1, fuse, P(x), P(g), P(y_r), P(dx_r), P(dw_r), P(db_r), P(rm_r), P(rv_r))
-    w, b = np.ones(C, np.float32), np.zeros(C, np.float32)
+    ref.ref_bn2d_module_ex(N, C, H, W, steps, 1, fuse, P(x), P(g), P(w), P(b), P(y_r), P(dx_r), P(dw_r), P(db_r),
+                           P(rm_r), P(rv_r))
     rm, rv = np.zeros(C, np.float32), np.ones(C, np.float32)
     y_t, alive = orc.zeros(N, C, H, W), np.zeros((N, C, H, W), np.uint8)
     mean, var, inv = orc.zeros(C), orc.zeros(C), orc.zeros(C)
@@ -186,6 +194,8 @@ def test_batchnorm_module_eval_bitwise(fuse, steps):
     O.orc_batchnorm_eval_bwd(N, C, H, W, P(g), P(x), P(w), P(b), P(rm), P(rv), 1e-5, fuse, P(dx), P(dw), P(db))
     for got, want in ((y, y_r), (dx, dx_r), (dw, dw_r), (db, db_r)):
         assert got.tobytes() == want.tobytes()
+    if params == "random" and fuse:
+        assert 0 < np.count_nonzero(y) < y.size          # the ReLU is active in both directions
 
 
 @pytest.mark.parametrize("k,stride", [(2, 2), (3, 1), (3, 2)])

@@ -124,11 +124,11 @@ def _nccl_worker(rank, world, port, m, n, k, mode, gather, out_dir):
 @pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("m,n,k", [(1000, 700, 900), (4096, 8192, 128)])
 def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode, gather, m, n, k):
-    """Bands computed on 2-4 GPUs and gathered on GPU 0 (by an NCCL gather after the GEMM, or by the
+    """Bands computed on every GPU of the box (2-8) and gathered on GPU 0 (by an NCCL gather after the GEMM, or by the
     GEMM's own epilogue storing into GPU 0's C through peer memory) equal the one-GPU product bit for
     bit. In the wide case the bands run on 224-wide tiles and the one-GPU product on 256-wide ones."""
     torch = cuda
-    world = min(torch.cuda.device_count(), 4)
+    world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two or more GPUs")
     mp.start_processes(_nccl_worker, args=(world, _free_port(), m, n, k, mode, gather, str(tmp_path)), nprocs=world,
@@ -180,14 +180,14 @@ def _dp_worker(rank, world, port, out_dir):
 
 @pytest.mark.gpu
 def test_data_parallel_step_bitwise_equal_to_single_gpu(cuda, tmp_path):
-    """Two training steps of the virtual-shard data-parallel step on 2 (or 4) GPUs give the same
-    weights, bit for bit, as on one GPU."""
+    """Two training steps of the virtual-shard data-parallel step on every GPU of the box (2, 4 or 8;
+    the largest divisor of 8 otherwise) give the same weights, bit for bit, as on one GPU."""
     torch = cuda
-    world = min(torch.cuda.device_count(), 4)
+    world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two or more GPUs")
-    if 8 % world:
-        world = 2
+    while 8 % world:               # the 8 virtual shards need a world that divides them
+        world -= 1
     mp.start_processes(_dp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     eq = np.load(tmp_path / "dp_eq.npy")
@@ -209,7 +209,7 @@ def _attn_worker(rank, world, port, out_dir):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
                             timeout=datetime.timedelta(seconds=60))
     try:
-        B, T, D, H = 6, 130, 128, 2                  # 6 samples over 2-4 ranks: unequal shares
+        B, T, D, H = 11, 130, 128, 2                 # 11 samples over 2-8 ranks: unequal shares
         g = torch.Generator(device="cuda").manual_seed(21)
         q, k, v, go = (torch.randn(B, T, D, device="cuda", generator=g) for _ in range(4))
         sa = ShardedAttention(B, T, D, H, causal=True)
@@ -238,13 +238,127 @@ def _attn_worker(rank, world, port, out_dir):
 
 @pytest.mark.gpu
 def test_sharded_attention_bitwise_equal_to_single_gpu(cuda, tmp_path):
-    """Attention forward + backward split by samples over 2-4 GPUs, O / dQ / dK / dV gathered on GPU 0
+    """Attention forward + backward split by samples over every GPU of the box (2-8), O / dQ / dK / dV gathered on GPU 0
     (dQ / dK / dV stored there by the backward kernels through peer memory, O by a peer copy): the
     one-GPU results, bit for bit."""
     torch = cuda
-    world = min(torch.cuda.device_count(), 4)
+    world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two or more GPUs")
     mp.start_processes(_attn_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     assert np.load(tmp_path / "attn_eq.npy").all()
+
+
+# ---- host logic of the data-parallel exchange and of the attention shares (gloo, CPU) ----------
+
+def _dp_exchange_worker(rank, world, port, shards, total, out_dir):
+    import torch
+    import torch.distributed as dist
+
+    from nnb.train import exchange_shard_gradients, gather_weight_slices, shard_owners
+    from oracle import orc
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        owned = shard_owners(shards, world, rank)
+        # shard i's gradient is a fixed function of i alone, wherever it is computed
+        shard_grads = torch.from_numpy(np.stack([orc.normal(300 + i, total) for i in owned]))
+        chunk = -(-total // world)
+        send = torch.zeros(world, len(owned), chunk)
+        recv = torch.empty(shards, chunk)
+        exchange_shard_gradients(shard_grads, send, recv, chunk, world)
+        reduced = np.zeros(chunk, np.float32)
+        orc.orc.orc_colsum(shards, chunk, orc.ptr(recv.numpy()), orc.ptr(reduced), 1)
+        flat_w = torch.zeros(chunk * world)
+        lo = rank * chunk
+        n = min(total, lo + chunk) - lo
+        flat_w[lo:lo + n] = torch.from_numpy(reduced[:n])      # stands in for AdamW on this rank's slice
+        gather_weight_slices(flat_w, chunk, rank)
+        np.save(os.path.join(out_dir, f"flat_{rank}.npy"), flat_w[:total].numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total", [(2, 1001), (4, 37)])
+def test_data_parallel_exchange_gloo(tmp_path, world, total):
+    """The data-parallel step's exchange on CPU ranks: slicing into the send buffer, the all-to-all,
+    the shard-order sum of the received rows (the oracle's Tensor::sum(0)) and the in-place all-gather
+    of the slices leave on EVERY rank the single-process shard-order sum of all 8 shards, bit for
+    bit (an uneven last slice included)."""
+    from oracle import orc
+
+    shards = 8
+    mp.start_processes(_dp_exchange_worker, args=(world, _free_port(), shards, total, str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    allg = np.stack([orc.normal(300 + i, total) for i in range(shards)])
+    want = np.zeros(total, np.float32)
+    orc.orc.orc_colsum(shards, total, orc.ptr(allg), orc.ptr(want), 1)
+    for r in range(world):
+        assert np.load(tmp_path / f"flat_{r}.npy").tobytes() == want.tobytes()
+
+
+def test_shard_owners():
+    from nnb.train import shard_owners
+    for world in (1, 2, 4, 8):
+        runs = [shard_owners(8, world, r) for r in range(world)]
+        assert sum(runs, []) == list(range(8))
+        assert all(len(r) == 8 // world for r in runs)
+    with pytest.raises(ValueError):
+        shard_owners(8, 3, 0)
+
+
+def _attn_share_worker(rank, world, port, B, T, D, H, path):
+    import torch.distributed as dist
+
+    from nnb.parallel import sample_shares, share_offset_bytes
+    from oracle import orc
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        shares = sample_shares(B, world)
+        n0, n1 = shares[rank]
+        q, k, v = (orc.normal(310 + j, B * T * D).reshape(B, T, D) for j in range(3))
+        # the owner's full-size O buffer, shared by the ranks as the peer buffer is on the GPUs
+        owner = np.memmap(path, dtype=np.float32, mode="r+", shape=(B, T, D))
+        if n1 > n0:
+            o = np.zeros((n1 - n0, T, D), np.float32)
+            p = np.zeros((n1 - n0, H, T, T), np.float32)
+            orc.orc.orc_attention_fwd(n1 - n0, T, T, D, H, orc.ptr(np.ascontiguousarray(q[n0:n1])),
+                                      orc.ptr(np.ascontiguousarray(k[n0:n1])), orc.ptr(np.ascontiguousarray(v[n0:n1])),
+                                      None, 1, orc.ptr(o), orc.ptr(p))
+            raw = owner.view(np.uint8).reshape(-1)
+            off = share_offset_bytes(n0, T, D)
+            raw[off: off + o.nbytes] = o.view(np.uint8).reshape(-1)
+            owner.flush()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,B", [(2, 5), (3, 7)])
+def test_sharded_attention_shares_gloo(tmp_path, world, B):
+    """ShardedAttention's partition on CPU ranks: every rank computes the attention of its samples
+    (the oracle standing in for the fused kernels) and stores it at its share's byte offset in the
+    owner's full-size buffer; the assembled output is the whole-batch result bit for bit (the shares
+    tile the batch with no gap or overlap, and samples are independent)."""
+    from nnb.parallel import sample_shares
+    from oracle import orc
+
+    T, D, H = 9, 8, 2
+    shares = sample_shares(B, world)
+    assert shares[0][0] == 0 and shares[-1][1] == B
+    assert all(a[1] == b[0] for a, b in zip(shares, shares[1:]))
+    assert max(e - s for s, e in shares) - min(e - s for s, e in shares) <= 1
+    path = tmp_path / "owner_o.bin"
+    np.zeros((B, T, D), np.float32).tofile(path)
+    mp.start_processes(_attn_share_worker, args=(world, _free_port(), B, T, D, H, str(path)), nprocs=world, join=True,
+                       start_method="spawn")
+    got = np.fromfile(path, np.float32).reshape(B, T, D)
+    q, k, v = (orc.normal(310 + j, B * T * D).reshape(B, T, D) for j in range(3))
+    want = np.zeros((B, T, D), np.float32)
+    probs = np.zeros((B, H, T, T), np.float32)
+    orc.orc.orc_attention_fwd(B, T, T, D, H, orc.ptr(q), orc.ptr(k), orc.ptr(v), None, 1, orc.ptr(want), orc.ptr(probs))
+    assert got.tobytes() == want.tobytes()

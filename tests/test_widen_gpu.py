@@ -133,21 +133,27 @@ def test_global_avgpool_bitwise(cuda):
 
 
 @pytest.mark.parametrize("evaluate,fuse_relu", [(0, 0), (0, 1), (1, 0), (1, 1)])
-def test_batchnorm2d_module_matches_reference(cuda, evaluate, fuse_relu):
+@pytest.mark.parametrize("shape", [(6, 5, 7, 9), (1, 3, 1, 300)])
+def test_batchnorm2d_module_matches_reference(cuda, evaluate, fuse_relu, shape):
     """Two training-mode steps (running statistics updated with momentum 0.1 and the unbiased
     variance), then, with evaluate, one evaluation-mode forward; output and gradients of the last
-    forward, and the running statistics, against the reference's BatchNorm2d."""
+    forward, and the running statistics, against the reference's BatchNorm2d with a random weight and
+    bias of both signs -- all bit for bit (the evaluation-mode parameter gradients are summed over N,
+    then H, then W, as the reference's sum_to_shape does)."""
     torch = cuda
     from nnb.autograd import Value
     from nnb.nn import BatchNorm2d
     R = ref()
-    N, C, H, W = 6, 5, 7, 9
+    N, C, H, W = shape
     x, g = nrm(241, N, C, H, W), nrm(242, N, C, H, W)
+    w, b = orc.uniform(243, C, -1.5, 1.5), orc.uniform(244, C, -1.0, 1.0)
     y_r, dx_r, dw_r, db_r = orc.zeros(N, C, H, W), orc.zeros(N, C, H, W), orc.zeros(C), orc.zeros(C)
     rm_r, rv_r = orc.zeros(C), orc.zeros(C)
-    R.ref_bn2d_module(N, C, H, W, 2, evaluate, fuse_relu, P(x), P(g), P(y_r), P(dx_r), P(dw_r), P(db_r), P(rm_r),
-                      P(rv_r))
+    R.ref_bn2d_module_ex(N, C, H, W, 2, evaluate, fuse_relu, P(x), P(g), P(w), P(b), P(y_r), P(dx_r), P(dw_r),
+                         P(db_r), P(rm_r), P(rv_r))
     bn = BatchNorm2d(C, torch.device("cuda"))
+    bn.weight.data.copy_(dev(torch, w))
+    bn.bias.data.copy_(dev(torch, b))
     xd = dev(torch, x)
     for _ in range(2):
         X = Value.leaf(xd, True)
@@ -163,12 +169,49 @@ def test_batchnorm2d_module_matches_reference(cuda, evaluate, fuse_relu):
     assert_bits(bn.running_var.cpu().numpy(), rv_r)
     assert_bits(Y.data.cpu().numpy(), y_r)
     assert_bits(X.grad.cpu().numpy(), dx_r)
-    if evaluate:          # per-channel sums through the reference's broadcast reductions: fp32 bound
-        assert_close(bn.weight.grad.cpu().numpy(), dw_r, 1e-5)
-        assert_close(bn.bias.grad.cpu().numpy(), db_r, 1e-5)
-    else:
-        assert_bits(bn.weight.grad.cpu().numpy(), dw_r)
-        assert_bits(bn.bias.grad.cpu().numpy(), db_r)
+    assert_bits(bn.weight.grad.cpu().numpy(), dw_r)
+    assert_bits(bn.bias.grad.cpu().numpy(), db_r)
+
+
+@pytest.mark.parametrize("shape", [(4, 3, 5, 6), (2, 4, 1, 1), (3, 2, 6, 1), (1, 5, 4, 300)])
+@pytest.mark.parametrize("fuse", [0, 1])
+def test_batchnorm_eval_op_matches_oracle(cuda, shape, fuse):
+    """nnb_batchnorm_eval_fwd / _bwd through the C ABI against the oracle's restatement
+    (orc_batchnorm_eval_fwd / _bwd), bit for bit, storing and then accumulating the gradients."""
+    torch = cuda
+    import ctypes
+    N, C, H, W = shape
+    x, g = nrm(251, N, C, H, W) * 2.0 + 0.3, nrm(252, N, C, H, W)
+    w, b = orc.uniform(253, C, -1.5, 1.5), orc.uniform(254, C, -1.0, 1.0)
+    rm, rv = orc.uniform(255, C, -0.5, 0.5), orc.uniform(256, C, 0.5, 2.0)
+    y_o, dx_o, dw_o, db_o = orc.zeros(N, C, H, W), orc.zeros(N, C, H, W), orc.zeros(C), orc.zeros(C)
+    O = orc.orc
+    O.orc_batchnorm_eval_fwd(N, C, H * W, P(x), P(w), P(b), P(rm), P(rv), 1e-5, fuse, P(y_o))
+    O.orc_batchnorm_eval_bwd(N, C, H, W, P(g), P(x), P(w), P(b), P(rm), P(rv), 1e-5, fuse, P(dx_o), P(dw_o), P(db_o))
+    xd, gd, wd, bd, rmd, rvd = (dev(torch, a) for a in (x, g, w, b, rm, rv))
+    y = torch.empty(N, C, H, W, device="cuda")
+    alive = torch.empty(N, C, H, W, device="cuda", dtype=torch.uint8) if fuse else None
+    s = torch.cuda.current_stream().cuda_stream
+    L = nnb.lib()
+    eps = ctypes.c_float(1e-5)
+    nnb.check(L.nnb_batchnorm_eval_fwd(s, N, C, H * W, xd.data_ptr(), rmd.data_ptr(), rvd.data_ptr(), eps,
+                                       wd.data_ptr(), bd.data_ptr(), fuse, y.data_ptr(),
+                                       None if alive is None else alive.data_ptr()))
+    dx = torch.full((N, C, H, W), 7.0, device="cuda")
+    dw, db = torch.full((C,), 7.0, device="cuda"), torch.full((C,), 7.0, device="cuda")
+    for first in (1, 0):
+        nnb.check(L.nnb_batchnorm_eval_bwd(s, N, C, H, W, gd.data_ptr(), xd.data_ptr(), rmd.data_ptr(),
+                                           rvd.data_ptr(), eps, wd.data_ptr(),
+                                           None if alive is None else alive.data_ptr(), dx.data_ptr(), first,
+                                           dw.data_ptr(), first, db.data_ptr(), first))
+        if first:
+            assert_bits(y.cpu().numpy(), y_o)
+            assert_bits(dx.cpu().numpy(), dx_o)
+            assert_bits(dw.cpu().numpy(), dw_o)
+            assert_bits(db.cpu().numpy(), db_o)
+    assert_bits(dx.cpu().numpy(), dx_o + dx_o)
+    assert_bits(dw.cpu().numpy(), dw_o + dw_o)
+    assert_bits(db.cpu().numpy(), db_o + db_o)
 
 
 def test_sequential_folds_relu_like_reference(cuda):

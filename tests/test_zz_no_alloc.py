@@ -4,7 +4,9 @@ Some hosts of this library cannot call the CUDA allocator on the call path (thei
 already owns the GPU's memory, or a latency-critical loop must not meet cudaMalloc's device-wide
 synchronisation or a pool growth). This entry point keeps the GEMM's scratch in a fixed 32 MiB
 device array instead. These tests call it through the C ABI and check, on two calls in a row, that
-it gives what the allocating entry point (nnb_sgemm_ex) gives, within the GEMM tests' tolerance.
+it gives the allocating entry point's (nnb_sgemm_ex's) bits -- neither shape is cut along its depth
+and the tile width does not change an element's arithmetic -- and that both are within the GEMM
+tests' fp64-oracle bound; and that the entry point's own error word reads 0 after clean calls.
 
 This file is named to be collected last, so a run that stops at the first failure has run every
 other test before it; it also passes alone in a fresh process.
@@ -41,17 +43,28 @@ def _call_allocating(torch, p, acc, mode, c_host):
     return dc.cpu().numpy()
 
 
-def _assert_close(p, got, want, acc, mode):
+def _assert_matches(p, got, want, acc, mode):
+    """got (no-alloc) has want's (allocating entry's) bits, and both are within the fp64 bound."""
     g = got[: p.m * p.ldc].reshape(p.m, p.ldc)
     w = want[: p.m * p.ldc].reshape(p.m, p.ldc)
     assert np.all(g[:, p.n:] == orc.SENTINEL)           # padding untouched
-    g, w = g[:, : p.n].astype(np.float64), w[:, : p.n].astype(np.float64)
-    assert np.array_equal(np.isnan(g), np.isnan(w))
-    inf = np.isinf(g) | np.isinf(w)
-    assert np.array_equal(g[inf], w[inf])
-    fin = ~(np.isnan(w) | inf)
+    assert g.tobytes() == w.tobytes()
+    g = g[:, : p.n].astype(np.float64)
+    exact = orc.sgemm_f64(p, p.c, acc)
+    assert np.array_equal(np.isnan(g), np.isnan(exact))
+    inf = np.isinf(g) | np.isinf(exact)
+    assert np.array_equal(g[inf], exact[inf])
+    fin = ~(np.isnan(exact) | inf)
     mag = orc.magnitude(p, p.c, acc)
-    assert np.all(np.abs(g[fin] - w[fin]) <= np.maximum(TOL[mode] * mag[fin], 1e-6))
+    assert np.all(np.abs(g[fin] - exact[fin]) <= np.maximum(TOL[mode] * mag[fin], 1e-6))
+
+
+def _error_word(torch, clear=1):
+    import ctypes
+    word = ctypes.c_int(-1)
+    st = nnb.lib().nnb_sgemm_noalloc_error(torch.cuda.current_stream().cuda_stream, ctypes.byref(word), clear)
+    assert st == nnb.NNB_OK, nnb.last_error()
+    return word.value
 
 
 @pytest.mark.parametrize("mode", [nnb.MATH_FP32X3, nnb.MATH_TF32])
@@ -63,14 +76,15 @@ def test_noalloc_matches_allocating_entry_on_two_calls_in_a_row(cuda, mode):
     p1.b[7 * p1.ldb + 3] = np.nan
     got1 = _call_noalloc(torch, p1, True, mode, p1.c)
     want1 = _call_allocating(torch, p1, True, mode, p1.c)
-    _assert_close(p1, got1, want1, True, mode)
+    _assert_matches(p1, got1, want1, True, mode)
     # Second call, straight after: finite data of another shape; stale flags or panels from the
     # first call must not leak into it
     p2 = orc.Problem(0, 1, 190, 333, 200, 1, 9002)
     got2 = _call_noalloc(torch, p2, False, mode, p2.c)
     want2 = _call_allocating(torch, p2, False, mode, p2.c)
-    _assert_close(p2, got2, want2, False, mode)
+    _assert_matches(p2, got2, want2, False, mode)
     assert np.all(np.isfinite(got2[: p2.m * p2.ldc].reshape(p2.m, p2.ldc)[:, : p2.n]))
+    assert _error_word(torch) == 0
 
 
 def test_noalloc_rejects_sizes_beyond_its_buffer(cuda):
