@@ -151,6 +151,20 @@ def ref():
     return _ref
 
 
+REF_NNB_PATH = HERE / "_ref" / "libnnref_nnb.so"
+_ref_nnb = None
+
+
+def ref_nnb():
+    """The reference library with its GEMM translation unit (src/kernels/gemm.cpp) replaced by the
+    B200 drop-in (nn-cpp_b200/host/nn_kernels_gemm.cpp over libnnb.so): the reference's own modules
+    and ops, unchanged, with every sgemm on the GPU. None if it was not built."""
+    global _ref_nnb
+    if _ref_nnb is None and REF_NNB_PATH.exists():
+        _ref_nnb = _load(REF_NNB_PATH, _REF_SIGS)
+    return _ref_nnb
+
+
 def ptr(a) -> int | None:
     """Address of a numpy array's data (None passes through as a NULL pointer)."""
     return None if a is None else a.ctypes.data

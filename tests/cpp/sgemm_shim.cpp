@@ -1,7 +1,8 @@
-// The drop-in a maintainer of nn-cpp would add for its GEMM seam, nn::kernels::sgemm
-// (include/nn/kernels/gemm.hpp:57-59, src/kernels/gemm.cpp:546-556): the same signature, host
-// buffers in and C written on return, forwarded to the C ABI's host-buffer entry. Compiled as C++17
-// against include/nnb.h and linked with libnnb.so by tests/test_cpp_host.py, with a small driver:
+// A driver for the drop-in a maintainer of nn-cpp would add for its GEMM seam, nn::kernels::sgemm
+// (include/nn/kernels/gemm.hpp:57-59, src/kernels/gemm.cpp:546-556; the drop-in itself is
+// nn-cpp_b200/host/nn_kernels_gemm.cpp): the same signature, host buffers in and C written on
+// return, forwarded to the C ABI's host-buffer entry. Compiled as C++17 against include/nnb.h together
+// with the drop-in and linked with libnnb.so by tests/test_cpp_host.py:
 //
 //   sgemm_shim checks
 //       host-side paths only, no GPU needed: the library's version, the empty products the
@@ -18,16 +19,12 @@
 
 #include "nnb.h"
 
+// nn::kernels::sgemm as include/nn/kernels/gemm.hpp:57-59 declares it; the definition is the
+// drop-in nn-cpp_b200/host/nn_kernels_gemm.cpp, compiled with this file.
 namespace nn {
 namespace kernels {
-
 void sgemm(bool trans_a, bool trans_b, size_t m, size_t n, size_t k, const float* a, size_t lda, const float* b,
-		size_t ldb, float* c, size_t ldc, bool accumulate) {
-	const nnb_status st = nnb_sgemm_host(trans_a, trans_b, m, n, k, a, lda, b, ldb, c, ldc, accumulate);
-	if (st == NNB_ERR_INVALID) throw std::invalid_argument(nnb_last_error());
-	if (st != NNB_OK) throw std::runtime_error(nnb_last_error());
-}
-
+		size_t ldb, float* c, size_t ldc, bool accumulate);
 }  // namespace kernels
 }  // namespace nn
 

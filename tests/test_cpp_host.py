@@ -27,7 +27,8 @@ def shim(tmp_path_factory):
     exe = tmp_path_factory.mktemp("cpp") / "sgemm_shim"
     lib_dir = str(nnb.LIB_PATH.parent)
     cmd = [cxx, "-std=c++17", "-O2", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"),
-           str(HERE / "cpp" / "sgemm_shim.cpp"), "-L", lib_dir, "-lnnb", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)]
+           str(HERE / "cpp" / "sgemm_shim.cpp"), str(ROOT / "nn-cpp_b200" / "host" / "nn_kernels_gemm.cpp"),
+           "-L", lib_dir, "-lnnb", f"-Wl,-rpath,{lib_dir}", "-o", str(exe)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     assert res.returncode == 0, res.stderr
     return exe

@@ -182,8 +182,15 @@ def test_cnn_forward_backward_matches_reference(cuda):
     fc1, fc2 = Linear(3136, 128, rng, dev), Linear(128, 10, rng, dev)
     front = Sequential(conv1, ReLU(), MaxPool2d(2, 2), conv2, ReLU(), MaxPool2d(2, 2), Flatten(), fc1)
     params_l = list(front.parameters()) + list(fc2.parameters())
+    # Decisions must match for the gradients to compare element by element (a flipped ReLU or a
+    # different first maximum in a pooling window routes a gradient elsewhere). Images that are
+    # multiples of 1/8 and conv weights that are multiples of 2^-8 make every conv output exact in
+    # fp32 on both sides (few-bit products, short exact sums; 3xTF32 splits such operands without
+    # loss), so the conv ReLU and pooling decisions are identical; fc1's are shared below.
+    for conv in (conv1, conv2):
+        conv.weight.data.copy_(torch.round(conv.weight.data * 256) / 256)
     N = 64
-    x = orc.uniform(50, N * 784, 0.0, 1.0).reshape(N, 1, 28, 28)
+    x = (np.round(orc.uniform(50, N * 784, 0.0, 1.0) * 8) / 8).astype(np.float32).reshape(N, 1, 28, 28)
     labels = orc.integers(51, N, 0, 9)
     params = np.concatenate([p.data.cpu().numpy().ravel() for p in params_l])
 
@@ -245,11 +252,16 @@ def test_transformer_config5_shape_matches_reference(cuda):
     assert n == init.size == 16808960
     np.testing.assert_allclose(losses, r_losses, rtol=1e-5)
     _close(grads, r_grads, 1e-4)
-    # per parameter tensor too, so a small tensor's error is not hidden by the embedding's scale
+    # per parameter tensor too, so a small tensor's error is not hidden by the embedding's scale; a
+    # tensor whose true gradient is zero (the attention key biases: a bias added to every key shifts a
+    # softmax row by a constant) holds rounding noise only and is held to the global scale
     off = 0
+    floor = 1e-3 * np.abs(r_grads).max()
     for name, p in model.named_parameters():
         k = p.data.numel()
-        _close(grads[off:off + k], r_grads[off:off + k], 2e-4)
+        got, want = grads[off:off + k].astype(np.float64), r_grads[off:off + k].astype(np.float64)
+        scale = max(np.abs(want).max(), floor)
+        assert np.abs(got - want).max() <= 2e-4 * scale, name
         off += k
     got = _flat(model).astype(np.float64)
     err = np.abs(got - r_params)
