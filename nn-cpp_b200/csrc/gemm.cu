@@ -34,7 +34,9 @@ constexpr int kBM = 128;                 // rows of C per tile (MMA M)
 constexpr int kBK = 16;                  // floats of depth per pipeline stage (one 64 B row)
 constexpr int kAPanelRows = 128;         // rows per packed panel of A
 constexpr int kGroupM = 16;              // tiles of M walked together for L2 reuse of B
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;            // TMA producer, MMA issuer, 4 epilogue warps
+constexpr int kGatherThreads = 128;      // + 4 warps that gather B into the stages (implicit GEMM)
+__host__ __device__ constexpr int threads_for(int gather) { return gather ? kThreads + kGatherThreads : kThreads; }
 constexpr int kSmemBudget = 200 * 1024;  // dynamic shared memory for the stage ring
 
 // Rows per packed B panel (one TMA box): 128 for the widths that are multiples of 128, else the width.
@@ -83,6 +85,10 @@ struct Params {
 	long long ldb, sb_outer, sb_inner;
 	int ta, tb;
 	int* err;
+	// B gathered by the kernel (implicit GEMM); its non-finite flags are set by the gathering warps
+	GemmGather g;
+	int* gflags_b;                   // writable view of flags_b
+	int* gany_b;                     // writable view of any_b
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -272,6 +278,187 @@ __device__ __forceinline__ long long batch_offset(int bi, int inner, long long s
 	return (long long)(bi / inner) * s_outer + (long long)(bi % inner) * s_inner;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Gathered B (implicit GEMM for the convolutions; the modes are described in nnb_gemm.h)
+// ---------------------------------------------------------------------------------------------
+
+// The gather geometry copied into registers once by each gather thread (the hot loops read no kernel
+// parameter memory).
+struct GatherRegs {
+	const float* src;
+	long long s_outer, s_inner;
+	int mode, N, K, inner, H, W, ho, wo, kh, kw, stride, pad, dil, cout;
+};
+
+__device__ __forceinline__ GatherRegs gather_regs(const Params& p) {
+	GatherRegs r;
+	r.src = p.g.src; r.s_outer = p.g.s_outer; r.s_inner = p.g.s_inner;
+	r.mode = p.g.mode; r.N = p.N; r.K = p.K; r.inner = p.batch_inner;
+	r.H = p.g.H; r.W = p.g.W; r.ho = p.g.ho; r.wo = p.g.wo; r.kh = p.g.kh; r.kw = p.g.kw;
+	r.stride = p.g.stride; r.pad = p.g.pad; r.dil = p.g.dil; r.cout = p.g.cout;
+	return r;
+}
+
+__device__ __forceinline__ const float* gather_src(const Params& p, int bi) {
+	return p.g.src + (long long)(bi / p.batch_inner) * p.g.s_outer + (long long)(bi % p.batch_inner) * p.g.s_inner;
+}
+
+// Element (j, k) of op(B)^T of batch entry bi, decoded from scratch (the non-finite fix-up path).
+__device__ float gather_elem(const Params& p, int bi, int j, int k) {
+	const GemmGather& g = p.g;
+	const float* src = gather_src(p, bi);
+	if (j >= p.N || k >= p.K) return 0.0f;
+	const int khw = g.kh * g.kw;
+	if (g.mode == kGatherTransposed) {
+		const int ih = j / g.W, iw = j % g.W;
+		const int t = k / g.cout, co = k % g.cout, ph = t / g.kw, pw = t % g.kw;
+		const int th = ih + g.pad - ph * g.dil, tw = iw + g.pad - pw * g.dil;
+		if (th < 0 || tw < 0 || th % g.stride || tw % g.stride) return 0.0f;
+		const int oh = th / g.stride, ow = tw / g.stride;
+		if (oh >= g.ho || ow >= g.wo) return 0.0f;
+		return src[((long long)co * g.ho + oh) * g.wo + ow];
+	}
+	const int kk = g.mode == kGatherIm2col ? k : j, pos = g.mode == kGatherIm2col ? j : k;
+	const int c = kk / khw, r = kk % khw, ph = r / g.kw, pw = r % g.kw;
+	const int oh = pos / g.wo, ow = pos % g.wo;
+	const int ih = oh * g.stride + ph * g.dil - g.pad, iw = ow * g.stride + pw * g.dil - g.pad;
+	if (ih < 0 || ih >= g.H || iw < 0 || iw >= g.W) return 0.0f;
+	return src[((long long)c * g.H + ih) * g.W + iw];
+}
+
+// Smem byte offset of element (row r, depth q) of a 16-deep K-major tile in the 64-byte swizzle the
+// TMA loads would write: 16-byte unit u = q / 4 of row r sits at u ^ ((r >> 1) & 3).
+__device__ __forceinline__ uint32_t sw64_offset(int r, int q) {
+	return (uint32_t)(r * (kBK * 4) + ((((q >> 2) ^ (r >> 1)) & 3) << 4) + ((q & 3) << 2));
+}
+
+// Issues the 4-byte asynchronous copies of row j, depths k0 .. k0 + 15, of op(B)^T into the hi part of
+// a stage (raw fp32, at the positions hi will occupy); positions outside the tensor are zero-filled.
+// The index is decoded once, then stepped.
+__device__ __forceinline__ void gather_issue_row(const GatherRegs& g, const float* __restrict__ src, int j, int k0,
+		uint32_t row_base, int rr) {
+	const bool row_ok = j < g.N;
+	if (g.mode == kGatherIm2col) {
+		const int oh = j / g.wo, ow = j - (j / g.wo) * g.wo;
+		const int khw = g.kh * g.kw;
+		int c = k0 / khw, r = k0 - c * khw, ph = r / g.kw, pw = r - (r / g.kw) * g.kw;
+#pragma unroll
+		for (int q = 0; q < 16; ++q) {
+			const int ih = oh * g.stride + ph * g.dil - g.pad, iw = ow * g.stride + pw * g.dil - g.pad;
+			const bool in = row_ok && k0 + q < g.K && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
+			cp_async_4(row_base + sw64_offset(rr, q), in ? src + ((long long)c * g.H + ih) * g.W + iw : src, in ? 4u : 0u);
+			if (++pw == g.kw) {
+				pw = 0;
+				if (++ph == g.kh) { ph = 0; ++c; }
+			}
+		}
+	} else if (g.mode == kGatherTransposed && g.cout % 16 == 0) {
+		// 16 consecutive output channels of one kernel tap: one window position for the whole stage
+		const int ih = j / g.W, iw = j - (j / g.W) * g.W;
+		const int t = k0 / g.cout, co0 = k0 - t * g.cout, ph = t / g.kw, pw = t - (t / g.kw) * g.kw;
+		const int th = ih + g.pad - ph * g.dil, tw = iw + g.pad - pw * g.dil;
+		const int oh = th / g.stride, ow = tw / g.stride;
+		const bool in = k0 < g.K && th >= 0 && tw >= 0 && oh * g.stride == th && ow * g.stride == tw && oh < g.ho &&
+			ow < g.wo;
+		const long long plane = (long long)g.ho * g.wo;
+		const float* base = in ? src + co0 * plane + (long long)oh * g.wo + ow : src;
+#pragma unroll
+		for (int q = 0; q < 16; ++q)
+			cp_async_4(row_base + sw64_offset(rr, q), in ? base + q * plane : src, in ? 4u : 0u);
+	} else if (g.mode == kGatherTransposed) {
+		const int ih = j / g.W, iw = j - (j / g.W) * g.W;
+		const int t = k0 / g.cout;
+		int co = k0 - t * g.cout, ph = t / g.kw, pw = t - (t / g.kw) * g.kw;
+#pragma unroll
+		for (int q = 0; q < 16; ++q) {
+			const int th = ih + g.pad - ph * g.dil, tw = iw + g.pad - pw * g.dil;
+			const int oh = th / g.stride, ow = tw / g.stride;
+			const bool in = row_ok && k0 + q < g.K && th >= 0 && tw >= 0 && oh * g.stride == th && ow * g.stride == tw &&
+				oh < g.ho && ow < g.wo;
+			cp_async_4(row_base + sw64_offset(rr, q), in ? src + ((long long)co * g.ho + oh) * g.wo + ow : src, in ? 4u : 0u);
+			if (++co == g.cout) {
+				co = 0;
+				if (++pw == g.kw) { pw = 0; ++ph; }
+			}
+		}
+	} else {                                   // kGatherIm2colRows
+		const int khw = g.kh * g.kw;
+		const int c = j / khw, r = j - c * khw, ph = r / g.kw, pw = r - (r / g.kw) * g.kw;
+		int oh = k0 / g.wo, ow = k0 - (k0 / g.wo) * g.wo;
+#pragma unroll
+		for (int q = 0; q < 16; ++q) {
+			const int ih = oh * g.stride + ph * g.dil - g.pad, iw = ow * g.stride + pw * g.dil - g.pad;
+			const bool in = row_ok && k0 + q < g.K && ih >= 0 && ih < g.H && iw >= 0 && iw < g.W;
+			cp_async_4(row_base + sw64_offset(rr, q), in ? src + ((long long)c * g.H + ih) * g.W + iw : src, in ? 4u : 0u);
+			if (++ow == g.wo) { ow = 0; ++oh; }
+		}
+	}
+}
+
+// Gathered B, step 1: the 128 gather threads (thread gt owns rows gt, gt + 128, ...) issue the copies
+// of one stage's B tile (kBN rows x 16 depth) into its hi part, as one copy group.
+template <int kBN>
+__device__ __forceinline__ void gather_issue(const GatherRegs& g, int bi, int nt, int kb, int gt, uint32_t bpart) {
+	const float* src = g.src + (long long)(bi / g.inner) * g.s_outer + (long long)(bi % g.inner) * g.s_inner;
+#pragma unroll
+	for (int i = 0; i < (kBN + kGatherThreads - 1) / kGatherThreads; ++i) {
+		const int rr = gt + kGatherThreads * i;
+		// columns of C past N are never stored, so their B rows are left as they are
+		if (rr >= kBN || nt * kBN + rr >= g.N) break;
+		gather_issue_row(g, src, nt * kBN + rr, kb * kBK, bpart, rr);
+	}
+	cp_async_commit();
+}
+
+// Gathered B, step 2 (once this thread's copies of the stage have landed): each row is read back,
+// non-finite values are zeroed and flag their row (as the pack kernels do), and the values are split
+// into hi (in place) and lo, in the layout the MMA reads.
+template <int kSplit, int kBN>
+__device__ __forceinline__ void gather_finish(int* __restrict__ flags_b, int* __restrict__ any_b, int rows_valid, int nt,
+		int gt, uint8_t* bpart) {
+#pragma unroll
+	for (int i = 0; i < (kBN + kGatherThreads - 1) / kGatherThreads; ++i) {
+		const int rr = gt + kGatherThreads * i;
+		if (rr >= kBN || rr >= rows_valid) break;
+		const int sw = (rr >> 1) & 3;
+		float4* hrow = reinterpret_cast<float4*>(bpart + rr * (kBK * 4));
+		float4* lrow = reinterpret_cast<float4*>(bpart + Cfg<kSplit, kBN>::kBPartBytes + rr * (kBK * 4));
+		float4 x[4];
+		bool bad = false;
+#pragma unroll
+		for (int u = 0; u < 4; ++u) {
+			x[u] = hrow[u ^ sw];
+			const bool f = isfinite(x[u].x) && isfinite(x[u].y) && isfinite(x[u].z) && isfinite(x[u].w);
+			if (!f) {
+				bad = true;
+				x[u].x = isfinite(x[u].x) ? x[u].x : 0.0f;
+				x[u].y = isfinite(x[u].y) ? x[u].y : 0.0f;
+				x[u].z = isfinite(x[u].z) ? x[u].z : 0.0f;
+				x[u].w = isfinite(x[u].w) ? x[u].w : 0.0f;
+			}
+		}
+		if (bad) {
+			atomicOr(flags_b + nt * kBN + rr, 1);
+			atomicOr(any_b, 1);
+			__threadfence();
+		}
+#pragma unroll
+		for (int u = 0; u < 4; ++u) {
+			float4 h, l;
+			if (kSplit) {
+				split_tf32(x[u].x, h.x, l.x);
+				split_tf32(x[u].y, h.y, l.y);
+				split_tf32(x[u].z, h.z, l.z);
+				split_tf32(x[u].w, h.w, l.w);
+				lrow[u ^ sw] = l;
+			} else {
+				h = make_float4(to_tf32(x[u].x), to_tf32(x[u].y), to_tf32(x[u].z), to_tf32(x[u].w));
+			}
+			hrow[u ^ sw] = h;
+		}
+	}
+}
+
 // IEEE value of sum_p op(A)(i,p)*op(B)(p,j) for an element whose row or column holds Inf/NaN:
 // NaN if any product is NaN or both infinities occur, else the infinity that occurs.
 __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, int j, float v) {
@@ -280,7 +467,8 @@ __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, i
 	bool nan = false, pinf = false, ninf = false;
 	for (int q = 0; q < p.K; ++q) {
 		const float a = p.ta ? A[(long long)q * p.lda + i] : A[(long long)i * p.lda + q];
-		const float b = p.tb ? B[(long long)j * p.ldb + q] : B[(long long)q * p.ldb + j];
+		const float b = p.g.mode != kGatherNone ? gather_elem(p, bi, j, q)
+			: p.tb ? B[(long long)j * p.ldb + q] : B[(long long)q * p.ldb + j];
 		const float pr = a * b;
 		if (pr != pr) nan = true;
 		else if (isinf(pr)) (pr > 0.0f ? pinf : ninf) = true;
@@ -291,9 +479,9 @@ __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, i
 	return v;
 }
 
-template <int kSplit, int kBN>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
-		const __grid_constant__ CUtensorMap tm_b, const Params p) {
+template <int kSplit, int kBN, int kGather>
+__global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
+		const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ Params p) {
 	using C = Cfg<kSplit, kBN>;
 	constexpr int S = C::S;
 	constexpr int kStages = C::kStages;
@@ -306,7 +494,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	if (threadIdx.x == 0) {
 		for (int s = 0; s < kStages; ++s) {
-			mbar_init(smem_u32(&full_bar[s]), 1);
+			// the TMA producer's arrival (+ one per gather warp when B is gathered)
+			mbar_init(smem_u32(&full_bar[s]), kGather ? 1 + kGatherThreads / 32 : 1);
 			mbar_init(smem_u32(&empty_bar[s]), 1);
 		}
 		for (int b = 0; b < 2; ++b) {
@@ -316,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 		abort_sh = 0;
 		fence_mbar_init();
 		tma_prefetch_desc(&tm_a);
-		tma_prefetch_desc(&tm_b);
+		if (!kGather) tma_prefetch_desc(&tm_b);
 	}
 	if (warp == 1) {
 		tmem_alloc(smem_u32(&tmem_base_sh), C::kTmemCols);
@@ -347,14 +536,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 						break;
 					}
 					const uint32_t fb = smem_u32(&full_bar[stage]);
-					mbar_arrive_expect_tx(fb, C::kStageBytes);
+					mbar_arrive_expect_tx(fb, kGather ? C::kABytes : C::kStageBytes);
 					const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
 					const int ya = (int)((((long long)ab * a_panels + mt) * p.KB + kb) * S * kAPanelRows);
 #pragma unroll
 					for (int s = 0; s < S; ++s)
 						tma_load_2d(base + s * (kAPanelRows * kBK * 4), &tm_a, fb, 0, ya + s * kAPanelRows);
 #pragma unroll
-					for (int q = 0; q < C::kBPanels; ++q) {
+					for (int q = 0; q < (kGather ? 0 : C::kBPanels); ++q) {
 						const long long panel = (long long)bb * b_panels + (long long)nt * C::kBPanels + q;
 						const int yb = (int)((panel * p.KB + kb) * S * C::kBPanelRows);
 #pragma unroll
@@ -417,6 +606,66 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 				mma_commit(smem_u32(&accf_bar[buf]));
 			}
 		}
+	} else if (kGather && warp >= kThreads / 32) {
+		// ------------------------- B gatherers (implicit GEMM) -------------------------
+		// Copies of up to kAhead stages are in flight per thread; a stage is split and handed to the MMA
+		// issuer once its own copies have landed (cp.async.wait_group), so the gather's load latency
+		// overlaps the stages before it. kAhead < kStages: a stage still being gathered is never needed
+		// free before it is finished.
+		constexpr int kAhead = kStages - 1;
+		const int gt = threadIdx.x - kThreads;
+		const GatherRegs gr = gather_regs(p);
+		int* const gflags = p.gflags_b;
+		int* const gany = p.gany_b;
+		const long long flag_stride = p.b_batched ? p.Np : 0;
+		int pend_stage[kAhead], pend_bi[kAhead], pend_nt[kAhead];
+		int head = 0, count = 0;
+		int stage = 0;
+		uint32_t phase = 0;
+		bool ok = true;
+		for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+			int bi, mt, nt;
+			tile_coords(t, p, bi, mt, nt);
+			for (int kb = 0; kb < p.KB; ++kb) {
+				const bool got = mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.err, kDevTimeoutEmpty, abort_flag);
+				if (!__all_sync(0xffffffffu, got)) {
+					ok = false;
+					break;
+				}
+				gather_issue<kBN>(gr, bi, nt, kb, gt, smem_u32(smem + stage * C::kStageBytes + C::kABytes));
+				int slot = head + count;
+				if (slot >= kAhead) slot -= kAhead;
+				pend_stage[slot] = stage;
+				pend_bi[slot] = bi;
+				pend_nt[slot] = nt;
+				if (++count == kAhead) {
+					cp_async_wait<kAhead - 1>();
+					gather_finish<kSplit, kBN>(gflags + pend_bi[head] * flag_stride, gany, gr.N - pend_nt[head] * kBN, pend_nt[head], gt,
+						smem + pend_stage[head] * C::kStageBytes + C::kABytes);
+					fence_proxy_async_smem();
+					__syncwarp();
+					if (lane == 0) mbar_arrive(smem_u32(&full_bar[pend_stage[head]]));
+					head = head + 1 == kAhead ? 0 : head + 1;
+					--count;
+				}
+				if (++stage == kStages) {
+					stage = 0;
+					phase ^= 1;
+				}
+			}
+		}
+		// the stages still pending: all copies landed, finished in order (also on the abort path, so no
+		// copy is in flight when the CTA exits)
+		cp_async_wait<0>();
+		while (count > 0) {
+			gather_finish<kSplit, kBN>(gflags + pend_bi[head] * flag_stride, gany, gr.N - pend_nt[head] * kBN, pend_nt[head], gt,
+				smem + pend_stage[head] * C::kStageBytes + C::kABytes);
+			fence_proxy_async_smem();
+			__syncwarp();
+			if (lane == 0) mbar_arrive(smem_u32(&full_bar[pend_stage[head]]));
+			head = head + 1 == kAhead ? 0 : head + 1;
+			--count;
+		}
 	} else {
 		// ---------------------------------- epilogue ----------------------------------
 		const int quad = warp & 3;                 // TMEM lanes this warp may access
@@ -439,7 +688,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 			float* cbase = p.C + batch_offset(bi, p.batch_inner, p.sc_outer, p.sc_inner);
 			float* crow = cbase + (long long)gm * p.ldc;
 			const long long aux_row = batch_offset(bi, p.batch_inner, p.s_aux_outer, p.s_aux_inner) + (long long)gm * p.ld_aux;
-			const bool fix = (*p.any_nonfinite | *p.any_b) != 0;
+			// a gathered B's flags are set during this kernel (by atomics, at L2): read them past L1
+			const bool fix = (*p.any_nonfinite | (kGather ? __ldcg(p.any_b) : *p.any_b)) != 0;
 			const bool row_bad = fix && row_ok && p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0;
 			const int* fcol = p.flags_b + (long long)(p.b_batched ? bi : 0) * p.Np;
 			const float row_bias = (p.bias_mode == kBiasRow && row_ok) ? p.bias[gm] : 0.0f;
@@ -462,7 +712,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(const __grid_const
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {
 						const int gn = gn0 + j;
-						if (gn < p.N && (row_bad || fcol[gn] != 0)) v[j] = nonfinite_result(p, bi, gm, gn, v[j]);
+						if (gn < p.N && (row_bad || (kGather ? __ldcg(fcol + gn) : fcol[gn]) != 0))
+							v[j] = nonfinite_result(p, bi, gm, gn, v[j]);
 					}
 				}
 #pragma unroll
@@ -580,17 +831,17 @@ static int choose_bn(long long m, long long n, long long entries, int sms) {
 	return best;
 }
 
-static bool g_attr_set[64][2][4];
+static bool g_attr_set[64][2][4][2];
 static std::mutex g_attr_mutex;
 
-template <int kSplit, int kBN>
+template <int kSplit, int kBN, int kGather = 0>
 static nnb_status set_smem_attr(int dev) {
 	const int bi = kBN == 64 ? 0 : kBN == 128 ? 1 : kBN == 224 ? 3 : 2;
 	std::lock_guard<std::mutex> lock(g_attr_mutex);
-	if (g_attr_set[dev & 63][kSplit][bi]) return NNB_OK;
-	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+	if (g_attr_set[dev & 63][kSplit][bi][kGather]) return NNB_OK;
+	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN, kGather>, cudaFuncAttributeMaxDynamicSharedMemorySize,
 		Cfg<kSplit, kBN>::kSmemBytes));
-	g_attr_set[dev & 63][kSplit][bi] = true;
+	g_attr_set[dev & 63][kSplit][bi][kGather] = true;
 	return NNB_OK;
 }
 
@@ -605,6 +856,7 @@ struct Plan {
 static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int sms = 148) {
 	pl.S = d.mode == NNB_MATH_FP32X3 ? 2 : 1;
 	pl.bn = force_bn ? force_bn : choose_bn(d.m, d.n, d.batch_outer * d.batch_inner, sms > 0 ? sms : 148);
+	if (d.gather.mode != kGatherNone && pl.bn == 224) pl.bn = 256;
 	pl.b_panel_rows = b_panel_rows(pl.bn);
 	pl.Mp = round_up(d.m, kBM);
 	pl.Np = round_up(d.n, pl.bn);
@@ -612,7 +864,8 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	pl.KB = pl.Kp / kBK;
 	pl.entries = d.batch_outer * d.batch_inner;
 	pl.a_entries = (d.sa_outer || d.sa_inner) ? pl.entries : 1;
-	pl.b_entries = (d.sb_outer || d.sb_inner) ? pl.entries : 1;
+	const bool gathered = d.gather.mode != kGatherNone;
+	pl.b_entries = (gathered ? (d.gather.s_outer || d.gather.s_inner) : (d.sb_outer || d.sb_inner)) ? pl.entries : 1;
 	pl.rows_a = pl.a_entries * pl.Mp * pl.KB * pl.S;
 	pl.rows_b = pl.b_entries * pl.Np * pl.KB * pl.S;
 	if (pl.rows_a > INT32_MAX || pl.rows_b > INT32_MAX)
@@ -620,9 +873,11 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 			pl.rows_a, pl.rows_b);
 	if (pl.entries > 65535) return fail(NNB_ERR_UNSUPPORTED, "gemm: more than 65535 batch entries");
 	if (pl.entries * (pl.Mp / kBM) * (pl.Np / pl.bn) > INT32_MAX) return fail(NNB_ERR_UNSUPPORTED, "gemm: too many tiles");
-	// a B that arrives packed (GemmDesc::packed_b) has its panels and flags outside the workspace
+	// a B that arrives packed (GemmDesc::packed_b) has its panels and flags outside the workspace; a
+	// gathered B has no panels at all, only its flags
 	const bool pre_b = d.packed_b != nullptr;
-	const size_t bytes_a = (size_t)pl.rows_a * kBK * 4, bytes_b = pre_b ? 0 : (size_t)pl.rows_b * kBK * 4;
+	const size_t bytes_a = (size_t)pl.rows_a * kBK * 4,
+		bytes_b = (pre_b || gathered) ? 0 : (size_t)pl.rows_b * kBK * 4;
 	pl.flag_ints = (size_t)(pl.a_entries * pl.Mp + (pre_b ? 0 : pl.b_entries * pl.Np) + 1);
 	pl.off_b = round_up(bytes_a, 1024);
 	pl.off_f = pl.off_b + round_up(bytes_b, 1024);
@@ -654,7 +909,7 @@ static void launch_pack(cudaStream_t s, const float* X, long long ldx, long long
 	}
 }
 
-template <int kSplit, int kBN>
+template <int kSplit, int kBN, int kGather = 0>
 static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
 	using Cf = Cfg<kSplit, kBN>;
@@ -683,7 +938,7 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 		launch_pack<kSplit>(s, d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, d.m, d.k, pl.Mp, pl.KB, kAPanelRows,
 			pl.a_entries, pa, flags_a, any);
 	}
-	if (!pre_b) {
+	if (!pre_b && !kGather) {
 		TraceScope ts(s, kTracePack, traced);
 		launch_pack<kSplit>(s, d.b, d.ldb, d.sb_outer, d.sb_inner, inner, !d.tb, d.n, d.k, pl.Np, pl.KB,
 			Cf::kBPanelRows, pl.b_entries, pb, flags_b, any);
@@ -692,8 +947,11 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 
 	CUtensorMap tma, tmb;
 	NNB_TRY(encode_tiled_2d(&tma, pa, kBK, (uint64_t)pl.rows_a, kBK * 4, kBK, kAPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
-	NNB_TRY(encode_tiled_2d(&tmb, pb, kBK, (uint64_t)pl.rows_b, kBK * 4, kBK, Cf::kBPanelRows,
-		CU_TENSOR_MAP_SWIZZLE_64B));
+	if (kGather)
+		tmb = tma;                               // not read: B is gathered by the kernel
+	else
+		NNB_TRY(encode_tiled_2d(&tmb, pb, kBK, (uint64_t)pl.rows_b, kBK * 4, kBK, Cf::kBPanelRows,
+			CU_TENSOR_MAP_SWIZZLE_64B));
 
 	Params p;
 	p.M = (int)d.m; p.N = (int)d.n; p.K = (int)d.k; p.KB = (int)pl.KB;
@@ -709,13 +967,16 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	p.A = d.a; p.lda = d.lda; p.sa_outer = d.sa_outer; p.sa_inner = d.sa_inner;
 	p.B = d.b; p.ldb = d.ldb; p.sb_outer = d.sb_outer; p.sb_inner = d.sb_inner;
 	p.ta = d.ta; p.tb = d.tb; p.err = err;
+	p.g = d.gather;
+	p.gflags_b = flags_b;
+	p.gany_b = any_b;
 
-	NNB_TRY((set_smem_attr<kSplit, kBN>(dev)));
+	NNB_TRY((set_smem_attr<kSplit, kBN, kGather>(dev)));
 	const long long tiles = pl.entries * p.tiles_m * p.tiles_n;
 	const int grid = (int)std::min<long long>(tiles, sm_count);
 	{
-		TraceScope ts(s, kTraceGemm, traced);
-		gemm_tc_kernel<kSplit, kBN><<<grid, kThreads, Cf::kSmemBytes, s>>>(tma, tmb, p);
+		TraceScope ts(s, kGather ? kTraceConv : kTraceGemm, traced);
+		gemm_tc_kernel<kSplit, kBN, kGather><<<grid, threads_for(kGather), Cf::kSmemBytes, s>>>(tma, tmb, p);
 	}
 	return cuda_status(cudaGetLastError(), "gemm launch");
 }
@@ -723,6 +984,11 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 template <int kSplit>
 static nnb_status dispatch_bn(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
+	if (d.gather.mode != kGatherNone) {         // widths 64, 128, 256 (make_plan never gives 224 here)
+		if (pl.bn == 256) return launch_main<kSplit, 256, 1>(s, dev, sm_count, err, d, pl, ws, traced);
+		if (pl.bn == 128) return launch_main<kSplit, 128, 1>(s, dev, sm_count, err, d, pl, ws, traced);
+		return launch_main<kSplit, 64, 1>(s, dev, sm_count, err, d, pl, ws, traced);
+	}
 	if (pl.bn == 256) return launch_main<kSplit, 256>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 224) return launch_main<kSplit, 224>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 128) return launch_main<kSplit, 128>(s, dev, sm_count, err, d, pl, ws, traced);
@@ -739,9 +1005,10 @@ static nnb_status validate(const GemmDesc& d) {
 	if (d.m > lim || d.n > lim || d.k > lim || d.batch_outer * d.batch_inner > lim)
 		return fail(NNB_ERR_UNSUPPORTED, "gemm: dimension above 2^30");
 	if (d.k > 0) {
-		if (!d.a || !d.b) return fail(NNB_ERR_INVALID, "gemm: A or B is null");
+		if (!d.a || (!d.b && d.gather.mode == kGatherNone)) return fail(NNB_ERR_INVALID, "gemm: A or B is null");
 		if (d.lda < (d.ta ? d.m : d.k)) return fail(NNB_ERR_INVALID, "gemm: lda %lld too small", d.lda);
-		if (d.ldb < (d.tb ? d.k : d.n)) return fail(NNB_ERR_INVALID, "gemm: ldb %lld too small", d.ldb);
+		if (d.gather.mode == kGatherNone && d.ldb < (d.tb ? d.k : d.n))
+			return fail(NNB_ERR_INVALID, "gemm: ldb %lld too small", d.ldb);
 	}
 	if (d.epi.bias_mode != kBiasNone && !d.epi.bias) return fail(NNB_ERR_INVALID, "gemm: bias is null");
 	if (d.epi.act == kActRelu && !d.epi.mask) return fail(NNB_ERR_INVALID, "gemm: relu mask is null");
@@ -752,6 +1019,12 @@ static nnb_status validate(const GemmDesc& d) {
 		return fail(NNB_ERR_INVALID, "gemm: tile width %d", d.bn);
 	if (d.packed_b && (d.bn == 0 || d.batch_outer * d.batch_inner != 1))
 		return fail(NNB_ERR_INVALID, "gemm: a packed B needs its tile width and a single batch entry");
+	if (d.gather.mode != kGatherNone) {
+		const GemmGather& g = d.gather;
+		if (d.packed_b || d.bn == 224 || !g.src || g.kh < 1 || g.kw < 1 || g.stride < 1 || g.dil < 1 || g.pad < 0 ||
+				g.H < 1 || g.W < 1 || g.ho < 1 || g.wo < 1 || (g.mode == kGatherTransposed && g.cout < 1))
+			return fail(NNB_ERR_INVALID, "gemm: bad gather geometry");
+	}
 	return NNB_OK;
 }
 
@@ -898,7 +1171,7 @@ nnb_status gemm_run(cudaStream_t s, const GemmDesc& d) {
 		zero_fill_kernel<<<g, 256, 0, s>>>(d.c, d.ldc, d.sc_outer, d.sc_inner, (int)d.batch_inner, (int)d.m, (int)d.n);
 		return cuda_status(cudaGetLastError(), "zero fill launch");
 	}
-	const int pieces = depth_pieces(d);
+	const int pieces = d.gather.mode != kGatherNone ? 1 : depth_pieces(d);
 	if (pieces > 1 && d.packed_b) return fail(NNB_ERR_INVALID, "gemm: a packed B with a depth cut");
 	if (pieces > 1) return gemm_depth_cut(s, dev, d, pieces);
 	return gemm_direct(s, dev, d);

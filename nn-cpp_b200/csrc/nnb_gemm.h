@@ -26,6 +26,25 @@ struct GemmEpilogue {
 	long long ld_aux = 0, s_aux_outer = 0, s_aux_inner = 0;
 };
 
+// A B operand gathered on the fly from a 4-D tensor [N, C, H, W] into the GEMM's shared-memory stages
+// (implicit GEMM: no column matrix in global memory). Batch entry e = (o, i) reads
+// src + o * s_outer + i * s_inner; op(B)^T element (j, k) of that entry is, by mode:
+//   kGatherIm2col     conv forward, j = output position (oh, ow), k = (c, ph, pw):
+//                     src[c][oh*stride + ph*dil - pad][ow*stride + pw*dil - pad], 0 outside
+//   kGatherTransposed conv input gradient, j = input position (ih, iw), k = (ph, pw, co), src the
+//                     output gradient [co][oh][ow] at oh = (ih + pad - ph*dil) / stride (and ow
+//                     likewise) when that divides exactly and lands inside, else 0
+//   kGatherIm2colRows conv weight gradient, j = (c, ph, pw), k = output position (oh, ow):
+//                     src[c][oh*stride + ph*dil - pad][ow*stride + pw*dil - pad], 0 outside
+// C, H, W are the gathered tensor's channels (per batch entry) and plane; ho, wo the conv output plane.
+enum GatherMode : int { kGatherNone = 0, kGatherIm2col = 1, kGatherTransposed = 2, kGatherIm2colRows = 3 };
+struct GemmGather {
+	int mode = kGatherNone;
+	const float* src = nullptr;
+	long long s_outer = 0, s_inner = 0;
+	int C = 0, H = 0, W = 0, ho = 0, wo = 0, kh = 1, kw = 1, stride = 1, pad = 0, dil = 1, cout = 0;
+};
+
 // C_e = op(A_e) op(B_e) for batch entries e = (o, i), o < batch_outer, i < batch_inner, where
 // X_e = x + o * sx_outer + i * sx_inner (floats). A zero stride shares the operand.
 struct GemmDesc {
@@ -46,6 +65,8 @@ struct GemmDesc {
 	// width (one batch entry, no depth cut); b/ldb stay the unpacked operand (non-finite fix-ups)
 	const void* packed_b = nullptr;
 	int bn = 0;                         // tile width: 0 chooses it from the shape; 64, 128 or 256
+	// B gathered by the GEMM kernel itself (b, ldb, sb_*, tb unused); never cut along its depth
+	GemmGather gather;
 };
 
 // Validates and enqueues the product (pack kernels + one persistent tensor-core kernel).

@@ -59,6 +59,22 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 	asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// 4-byte asynchronous copy global -> shared (L1-allocating); src_bytes 0 writes a zero instead of
+// reading (the source address is then not dereferenced but must still be a valid pointer).
+__device__ __forceinline__ void cp_async_4(uint32_t smem_dst, const void* src, uint32_t src_bytes) {
+	asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most N of this thread's committed copy groups are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Orders this thread's ordinary shared-memory stores before later reads of that memory by the async
+// proxy (tensor-core operand reads): each writing thread fences, then signals the MMA issuer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+	asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 	uint32_t ok;
 	asm volatile(

@@ -1,15 +1,21 @@
-// ops_conv.cu -- `conv2d` / `conv2d_relu` (src/autograd/ops.cpp:1345-1472) as im2col + the
-// tensor-core GEMM, with the reference's per-sample structure kept where it fixes the order of a sum.
+// ops_conv.cu -- `conv2d` / `conv2d_relu` (src/autograd/ops.cpp:1345-1472) and the general conv
+// (dilation, groups; ops.cpp:1525-1607) as implicit GEMMs on the tensor-core kernel: the kernel's
+// gather warps build the column operand straight into its shared-memory stages from the activation
+// (or the output gradient), so no column matrix [K, N*hw] is ever written to global memory.
 //
-// Forward: every sample is unrolled (im2col_sample, ops.cpp:188-212) into col[n] (K x hw,
-// K = Cin*kh*kw), then ONE batched GEMM over the samples computes y[n] = W col[n] with the bias
-// (per output channel = per row of y[n]) and the folded ReLU + 1-byte alive mask in its epilogue
-// (ops.cpp:1395-1408).
-// Backward: the gradient masked by `alive`; db per channel = sum over samples, in sample order, of
-// the 8-lane sum of the channel's plane (ops.cpp:1441-1442, 1461); dW = sum over samples, in sample
-// order, of g[n] col[n]^T (one batched GEMM into per-sample buffers, then an ordered sum,
-// ops.cpp:1449, 1462); dX = col2im(W^T g[n]) (ops.cpp:1452-1455), written as a gather that adds each
-// input element's contributions in the reference's (kernel row, kernel column) order.
+// Forward: y[n][g] = W_g im2col(x[n][g]) for every (sample, group) in ONE launch, the im2col of the
+// reference (im2col_sample, ops.cpp:188-212) gathered per stage (kGatherIm2col); bias (per output
+// channel = per row), ReLU and the 1-byte alive mask in the epilogue (ops.cpp:1395-1408). The grouped
+// path adds its bias afterwards, as the reference's general path does (ops.cpp:1556-1557).
+// Backward: the gradient masked by `alive`; db per channel = sum over samples, in sample order, of the
+// 8-lane sum of the channel's plane (ops.cpp:1441-1442, 1461); dW = sum over samples, in sample order,
+// of g[n] im2col(x[n])^T (one launch into per-sample buffers, the column rows gathered per stage:
+// kGatherIm2colRows; then an ordered sum, ops.cpp:1449, 1462); dX = col2im(W^T g[n]) (ops.cpp:1452-1455)
+// as ONE product per (sample, group): rows = input channels, columns = input positions, depth =
+// (kernel row, kernel column, output channel) over W rearranged to [c][(ph, pw, co)] and the output
+// gradient gathered at the window position that reads each input position (kGatherTransposed). Each
+// dX element is one k-ordered chain over the taps and channels, where the reference adds per-tap
+// products in (kernel row, kernel column) order: the same terms, fp32-bound apart.
 #include "nnb_gemm.h"
 #include "nnb_internal.h"
 #include "nnb_ops.h"
@@ -30,48 +36,17 @@ struct Geo {
 #define GRID_STRIDE(i, n) \
 	for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < (n); i += (long long)gridDim.x * blockDim.x)
 
-// col[n][(c*kh + ph)*kw + pw][oh*wo + ow] = x[n][c][oh*s + ph - p][ow*s + pw - p] (0 in the padding)
-__global__ void im2col_kernel(Geo g, const float* __restrict__ x, float* __restrict__ col) {
-	const long long K = g.K(), hw = g.hw();
-	GRID_STRIDE(i, (long long)g.N * K * hw) {
-		const long long n = i / (K * hw);
-		const long long rem = i - n * K * hw;
-		const int kr = (int)(rem / hw), o = (int)(rem % hw);
-		const int c = kr / (g.kh * g.kw), ph = (kr / g.kw) % g.kh, pw = kr % g.kw;
-		const int oh = o / g.wo, ow = o % g.wo;
-		const int ih = oh * g.stride + ph * g.dil - g.pad, iw = ow * g.stride + pw * g.dil - g.pad;
-		float v = 0.0f;
-		if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W)
-			v = x[((n * g.Cin + c) * (long long)g.H + ih) * g.W + iw];
-		col[i] = v;
-	}
-}
-
-// grad_x[n][c][ih][iw] = sum over (ph, pw), in that order, from +0, of dcol[n][(c*kh+ph)*kw+pw][oh*wo+ow]
-// for the window position (oh, ow) that reads (ih, iw), if any; then dx = grad_x + 0 (first) or
-// dx + grad_x, as the reference builds grad_x and adds it to x.grad() (ops.cpp:1452-1455, 1604)
-__global__ void col2im_kernel(Geo g, const float* __restrict__ dcol, float* __restrict__ dx, int first) {
-	const long long K = g.K(), hw = g.hw();
-	GRID_STRIDE(i, (long long)g.N * g.Cin * g.H * g.W) {
-		const long long n = i / ((long long)g.Cin * g.H * g.W);
-		const int c = (int)((i / ((long long)g.H * g.W)) % g.Cin);
-		const int ih = (int)((i / g.W) % g.H), iw = (int)(i % g.W);
-		float acc = 0.0f;
-		const float* base = dcol + n * K * hw;
-		for (int ph = 0; ph < g.kh; ++ph) {
-			const int th = ih + g.pad - ph * g.dil;
-			if (th < 0 || th % g.stride != 0) continue;
-			const int oh = th / g.stride;
-			if (oh >= g.ho) continue;
-			for (int pw = 0; pw < g.kw; ++pw) {
-				const int tw = iw + g.pad - pw * g.dil;
-				if (tw < 0 || tw % g.stride != 0) continue;
-				const int ow = tw / g.stride;
-				if (ow >= g.wo) continue;
-				acc += base[((long long)(c * g.kh + ph) * g.kw + pw) * hw + (long long)oh * g.wo + ow];
-			}
-		}
-		dx[i] = first ? acc + 0.0f : dx[i] + acc;
+// wt[g][c][(ph*kw + pw)*Cog + co] = w[g*Cog + co][c][ph][pw]: the A operand of the input gradient
+__global__ void conv_weight_taps_kernel(long long total, int Cg, int Cog, int khw, const float* __restrict__ w,
+		float* __restrict__ wt) {
+	GRID_STRIDE(i, total) {
+		const long long per_group = (long long)Cg * khw * Cog;
+		const long long grp = i / per_group;
+		const long long r = i - grp * per_group;
+		const int c = (int)(r / ((long long)khw * Cog));
+		const int rem = (int)(r - (long long)c * khw * Cog);
+		const int t = rem / Cog, co = rem - t * Cog;
+		wt[i] = w[((grp * Cog + co) * Cg + c) * khw + t];
 	}
 }
 
@@ -163,6 +138,73 @@ nnb_status make_geo_ex(size_t N, size_t Cin, size_t H, size_t W, size_t Cout, si
 	return NNB_OK;
 }
 
+GemmGather gather_of(const Geo& g, int mode, const float* src) {
+	GemmGather q;
+	q.mode = mode;
+	q.src = src;
+	const int Cg = g.Cin / g.groups, Cog = g.Cout / g.groups;
+	if (mode == kGatherTransposed) {          // the output gradient [N][Cout][ho][wo], per (sample, group)
+		q.s_outer = (long long)g.Cout * g.hw();
+		q.s_inner = (long long)Cog * g.hw();
+		q.C = Cog;
+	} else {                                  // the input [N][Cin][H][W], per (sample, group)
+		q.s_outer = (long long)g.Cin * g.H * g.W;
+		q.s_inner = (long long)Cg * g.H * g.W;
+		q.C = Cg;
+	}
+	q.H = g.H; q.W = g.W; q.ho = g.ho; q.wo = g.wo; q.kh = g.kh; q.kw = g.kw;
+	q.stride = g.stride; q.pad = g.pad; q.dil = g.dil; q.cout = Cog;
+	return q;
+}
+
+// y[n][g] = W_g im2col(x[n][g]) (+ the epilogue in d.epi), one launch over every (sample, group)
+nnb_status conv_forward(cudaStream_t s, const Geo& g, const float* x, const float* w, float* y, const GemmEpilogue& epi) {
+	const long long G = g.groups, Kg = g.K() / G, Cog = g.Cout / G, hw = g.hw();
+	GemmDesc d;
+	d.m = Cog; d.n = hw; d.k = Kg;
+	d.a = w; d.lda = Kg;
+	d.c = y; d.ldc = hw;
+	d.batch_outer = g.N; d.batch_inner = G;
+	d.sa_outer = 0; d.sa_inner = Cog * Kg;
+	d.sc_outer = (long long)g.Cout * hw; d.sc_inner = Cog * hw;
+	d.mode = math_mode();
+	d.epi = epi;
+	d.gather = gather_of(g, kGatherIm2col, x);
+	return gemm_run(s, d);
+}
+
+// gw[n][g] = gg[n][g] im2col(x[n][g])^T : [Cog, hw] x [hw, Kg], per (sample, group)
+nnb_status conv_weight_grad(cudaStream_t s, const Geo& g, const float* gg, const float* x, float* gw) {
+	const long long G = g.groups, Kg = g.K() / G, Cog = g.Cout / G, hw = g.hw();
+	GemmDesc d;
+	d.m = Cog; d.n = Kg; d.k = hw;
+	d.a = gg; d.lda = hw;
+	d.c = gw; d.ldc = Kg;
+	d.batch_outer = g.N; d.batch_inner = G;
+	d.sa_outer = (long long)g.Cout * hw; d.sa_inner = Cog * hw;
+	d.sc_outer = (long long)g.Cout * Kg; d.sc_inner = Cog * Kg;
+	d.mode = math_mode();
+	d.gather = gather_of(g, kGatherIm2colRows, x);
+	return gemm_run(s, d);
+}
+
+// dx[n][g] (+)= Wt_g gather(gg[n][g]) : [Cg, khw*Cog] x [khw*Cog, H*W], per (sample, group)
+nnb_status conv_input_grad(cudaStream_t s, const Geo& g, const float* gg, const float* wt, float* dx, int first) {
+	const long long G = g.groups, Cg = g.Cin / G, Cog = g.Cout / G, khw = (long long)g.kh * g.kw;
+	const long long plane = (long long)g.H * g.W;
+	GemmDesc d;
+	d.m = Cg; d.n = plane; d.k = khw * Cog;
+	d.a = wt; d.lda = khw * Cog;
+	d.c = dx; d.ldc = plane;
+	d.batch_outer = g.N; d.batch_inner = G;
+	d.sa_outer = 0; d.sa_inner = Cg * khw * Cog;
+	d.sc_outer = (long long)g.Cin * plane; d.sc_inner = Cg * plane;
+	d.accumulate = first ? 0 : 1;
+	d.mode = math_mode();
+	d.gather = gather_of(g, kGatherTransposed, gg);
+	return gemm_run(s, d);
+}
+
 }  // namespace
 
 }  // namespace nnb
@@ -176,34 +218,16 @@ nnb_status nnb_conv2d_fwd(void* stream, size_t N, size_t Cin, size_t H, size_t W
 	NNB_TRY(nnb::make_geo(N, Cin, H, W, Cout, kh, kw, stride, padding, g));
 	if (N == 0 || Cout == 0) return NNB_OK;
 	if (!x || !weight || !bias || !y || (fuse_relu && !alive)) return nnb::fail(NNB_ERR_INVALID, "conv2d_fwd: null pointer");
-	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	const long long K = g.K(), hw = g.hw();
-	void* ws = nullptr;
-	NNB_TRY(nnb::scratch_alloc(&ws, (size_t)N * K * hw * sizeof(float), s));
-	float* col = static_cast<float*>(ws);
-	nnb_status st = NNB_OK;
-	{
-		nnb::TraceScope ts(s, nnb::kTraceConv);
-		nnb::im2col_kernel<<<nnb::grid_for((long long)N * K * hw, 256), 256, 0, s>>>(g, x, col);
+	nnb::GemmEpilogue epi;
+	epi.bias = bias;
+	epi.bias_mode = nnb::kBiasRow;
+	if (fuse_relu) {
+		epi.act = nnb::kActRelu;
+		epi.mask = alive;
+		epi.ld_aux = g.hw();
+		epi.s_aux_outer = (long long)Cout * g.hw();
 	}
-	st = nnb::cuda_status(cudaGetLastError(), "im2col launch");
-	if (st == NNB_OK) {
-		nnb::GemmDesc d;
-		d.m = (long long)Cout; d.n = hw; d.k = K;
-		d.a = weight; d.lda = K; d.b = col; d.ldb = hw; d.c = y; d.ldc = hw;
-		d.batch_outer = (long long)N; d.sa_outer = 0; d.sb_outer = K * hw; d.sc_outer = (long long)Cout * hw;
-		d.mode = nnb::math_mode();
-		d.epi.bias = bias; d.epi.bias_mode = nnb::kBiasRow;
-		if (fuse_relu) {
-			d.epi.act = nnb::kActRelu;
-			d.epi.mask = alive;
-			d.epi.ld_aux = hw;
-			d.epi.s_aux_outer = (long long)Cout * hw;
-		}
-		st = nnb::gemm_run(s, d);
-	}
-	nnb_status st2 = nnb::scratch_free(ws, s);
-	return st != NNB_OK ? st : st2;
+	return nnb::conv_forward(static_cast<cudaStream_t>(stream), g, x, weight, y, epi);
 }
 
 nnb_status nnb_conv2d_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh, size_t kw,
@@ -215,16 +239,14 @@ nnb_status nnb_conv2d_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W
 	if (!grad || !x || !weight) return nnb::fail(NNB_ERR_INVALID, "conv2d_bwd: null input");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	const long long K = g.K(), hw = g.hw(), out_n = (long long)N * Cout * hw;
-	const bool need_col = dweight || dx;
-	const size_t col_f = need_col ? (size_t)N * K * hw : 0, gm_f = alive ? (size_t)out_n : 0,
-		gw_f = dweight ? (size_t)N * Cout * K : 0;
+	const size_t gm_f = alive ? (size_t)out_n : 0, gw_f = dweight ? (size_t)N * Cout * K : 0;
+	const size_t wt_f = dx ? (size_t)Cout * K : 0, gb_f = (size_t)N * Cout;
 	void* ws = nullptr;
-	const size_t gb_f = (size_t)N * Cout;
-	NNB_TRY(nnb::scratch_alloc(&ws, (col_f + gm_f + gw_f + gb_f + 64) * sizeof(float), s));
-	float* col = static_cast<float*>(ws);
-	float* gm = col + col_f;
+	NNB_TRY(nnb::scratch_alloc(&ws, (gm_f + gw_f + wt_f + gb_f + 64) * sizeof(float), s));
+	float* gm = static_cast<float*>(ws);
 	float* gw = gm + gm_f;
-	float* gb = gw + gw_f;
+	float* wt = gw + gw_f;
+	float* gb = wt + wt_f;
 	nnb_status st = NNB_OK;
 	do {
 		const float* gg = grad;
@@ -245,31 +267,19 @@ nnb_status nnb_conv2d_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W
 		}
 		if ((st = nnb::cuda_status(cudaGetLastError(), "conv bias grad launch")) != NNB_OK) break;
 		if (dweight) {
-			{
-				nnb::TraceScope ts(s, nnb::kTraceConv);
-				nnb::im2col_kernel<<<nnb::grid_for((long long)N * K * hw, 256), 256, 0, s>>>(g, x, col);
-			}
-			nnb::GemmDesc d;     // gw[n] = g[n] col[n]^T : [Cout, hw] x [hw, K]
-			d.tb = 1;
-			d.m = (long long)Cout; d.n = K; d.k = hw;
-			d.a = gg; d.lda = hw; d.b = col; d.ldb = hw; d.c = gw; d.ldc = K;
-			d.batch_outer = (long long)N; d.sa_outer = (long long)Cout * hw; d.sb_outer = K * hw; d.sc_outer = (long long)Cout * K;
-			d.mode = nnb::math_mode();
-			if ((st = nnb::gemm_run(s, d)) != NNB_OK) break;
+			if ((st = nnb::conv_weight_grad(s, g, gg, x, gw)) != NNB_OK) break;
 			const long long per = (long long)Cout * K;
 			nnb::TraceScope ts(s, nnb::kTraceConv);
 			nnb::sum_samples_kernel<<<nnb::grid_for(per, 256), 256, 0, s>>>(gw, (int)N, per, dweight, dweight_first);
 		}
 		if (dx) {
-			nnb::GemmDesc d;     // dcol[n] = W^T g[n] : [K, Cout] x [Cout, hw], into the col buffer
-			d.ta = 1;
-			d.m = K; d.n = hw; d.k = (long long)Cout;
-			d.a = weight; d.lda = K; d.b = gg; d.ldb = hw; d.c = col; d.ldc = hw;
-			d.batch_outer = (long long)N; d.sa_outer = 0; d.sb_outer = (long long)Cout * hw; d.sc_outer = K * hw;
-			d.mode = nnb::math_mode();
-			if ((st = nnb::gemm_run(s, d)) != NNB_OK) break;
-			nnb::TraceScope ts(s, nnb::kTraceConv);
-			nnb::col2im_kernel<<<nnb::grid_for((long long)N * Cin * H * W, 256), 256, 0, s>>>(g, col, dx, dx_first);
+			{
+				nnb::TraceScope ts(s, nnb::kTraceConv);
+				nnb::conv_weight_taps_kernel<<<nnb::grid_for((long long)Cout * K, 256), 256, 0, s>>>((long long)Cout * K,
+					(int)Cin, (int)Cout, (int)(kh * kw), weight, wt);
+			}
+			if ((st = nnb::cuda_status(cudaGetLastError(), "conv weight taps launch")) != NNB_OK) break;
+			if ((st = nnb::conv_input_grad(s, g, gg, wt, dx, dx_first)) != NNB_OK) break;
 		}
 		st = nnb::cuda_status(cudaGetLastError(), "conv2d_bwd launch");
 	} while (0);
@@ -286,34 +296,12 @@ nnb_status nnb_conv2d_ex_fwd(void* stream, size_t N, size_t Cin, size_t H, size_
 	if (N == 0 || Cout == 0) return NNB_OK;
 	if (!x || !weight || !bias || !y) return nnb::fail(NNB_ERR_INVALID, "conv2d_ex_fwd: null pointer");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	const long long K = g.K(), hw = g.hw(), G = groups, Kg = K / G, Cog = (long long)Cout / G;
-	void* ws = nullptr;
-	NNB_TRY(nnb::scratch_alloc(&ws, (size_t)N * K * hw * sizeof(float), s));
-	float* col = static_cast<float*>(ws);
-	nnb_status st = NNB_OK;
-	do {
-		{
-			nnb::TraceScope ts(s, nnb::kTraceConv);
-			nnb::im2col_kernel<<<nnb::grid_for((long long)N * K * hw, 256), 256, 0, s>>>(g, x, col);
-		}
-		if ((st = nnb::cuda_status(cudaGetLastError(), "im2col launch")) != NNB_OK) break;
-		// y[n][g] = W_g col[n][g] for every (sample, group): ops.cpp:1552-1555
-		nnb::GemmDesc d;
-		d.m = Cog; d.n = hw; d.k = Kg;
-		d.a = weight; d.lda = Kg; d.b = col; d.ldb = hw; d.c = y; d.ldc = hw;
-		d.batch_outer = (long long)N; d.batch_inner = G;
-		d.sa_outer = 0; d.sa_inner = Cog * Kg;
-		d.sb_outer = K * hw; d.sb_inner = Kg * hw;
-		d.sc_outer = (long long)Cout * hw; d.sc_inner = Cog * hw;
-		d.mode = nnb::math_mode();
-		if ((st = nnb::gemm_run(s, d)) != NNB_OK) break;
-		const long long total = (long long)N * Cout * hw;
-		nnb::TraceScope ts(s, nnb::kTraceConv);
-		nnb::conv_add_bias_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, hw, (int)Cout, bias, y);
-		st = nnb::cuda_status(cudaGetLastError(), "conv bias launch");
-	} while (0);
-	nnb_status st2 = nnb::scratch_free(ws, s);
-	return st != NNB_OK ? st : st2;
+	// y[n][g] = W_g col[n][g] for every (sample, group) (ops.cpp:1552-1555), then the bias
+	NNB_TRY(nnb::conv_forward(s, g, x, weight, y, nnb::GemmEpilogue()));
+	const long long total = (long long)N * Cout * g.hw();
+	nnb::TraceScope ts(s, nnb::kTraceConv);
+	nnb::conv_add_bias_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, g.hw(), (int)Cout, bias, y);
+	return nnb::cuda_status(cudaGetLastError(), "conv bias launch");
 }
 
 nnb_status nnb_conv2d_ex_bwd(void* stream, size_t N, size_t Cin, size_t H, size_t W, size_t Cout, size_t kh, size_t kw,
@@ -325,52 +313,34 @@ nnb_status nnb_conv2d_ex_bwd(void* stream, size_t N, size_t Cin, size_t H, size_
 	if (N == 0 || Cout == 0) return NNB_OK;
 	if (!grad || !x || !weight) return nnb::fail(NNB_ERR_INVALID, "conv2d_ex_bwd: null input");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
-	const long long K = g.K(), hw = g.hw(), G = groups, Kg = K / G, Cog = (long long)Cout / G;
-	const size_t col_f = (dweight || dx) ? (size_t)N * K * hw : 0, gw_f = dweight ? (size_t)N * Cout * Kg : 0;
+	const long long K = g.K(), G = groups, Kg = K / G;
+	const size_t gw_f = dweight ? (size_t)N * Cout * Kg : 0, wt_f = dx ? (size_t)Cout * Kg : 0;
 	void* ws = nullptr;
-	NNB_TRY(nnb::scratch_alloc(&ws, (col_f + gw_f + 64) * sizeof(float), s));
-	float* col = static_cast<float*>(ws);
-	float* gw = col + col_f;
+	NNB_TRY(nnb::scratch_alloc(&ws, (gw_f + wt_f + 64) * sizeof(float), s));
+	float* gw = static_cast<float*>(ws);
+	float* wt = gw + gw_f;
 	nnb_status st = NNB_OK;
 	do {
 		if (dbias) {
 			nnb::TraceScope ts(s, nnb::kTraceConv);
-			nnb::conv_bias_grad_serial_kernel<<<(unsigned)((Cout + 127) / 128), 128, 0, s>>>(grad, (int)N, (int)Cout, hw,
-				dbias, dbias_first);
+			nnb::conv_bias_grad_serial_kernel<<<(unsigned)((Cout + 127) / 128), 128, 0, s>>>(grad, (int)N, (int)Cout,
+				g.hw(), dbias, dbias_first);
 		}
 		if ((st = nnb::cuda_status(cudaGetLastError(), "conv bias grad launch")) != NNB_OK) break;
-		if (dweight) {
-			{
-				nnb::TraceScope ts(s, nnb::kTraceConv);
-				nnb::im2col_kernel<<<nnb::grid_for((long long)N * K * hw, 256), 256, 0, s>>>(g, x, col);
-			}
-			nnb::GemmDesc d;     // gw[n][g] = g[n][g] col[n][g]^T : [Cog, hw] x [hw, Kg]  (ops.cpp:1580-1581)
-			d.tb = 1;
-			d.m = Cog; d.n = Kg; d.k = hw;
-			d.a = grad; d.lda = hw; d.b = col; d.ldb = hw; d.c = gw; d.ldc = Kg;
-			d.batch_outer = (long long)N; d.batch_inner = G;
-			d.sa_outer = (long long)Cout * hw; d.sa_inner = Cog * hw;
-			d.sb_outer = K * hw; d.sb_inner = Kg * hw;
-			d.sc_outer = (long long)Cout * Kg; d.sc_inner = Cog * Kg;
-			d.mode = nnb::math_mode();
-			if ((st = nnb::gemm_run(s, d)) != NNB_OK) break;
+		if (dweight) {      // gw[n][g] = g[n][g] col[n][g]^T (ops.cpp:1580-1581), then the sample-order sum
+			if ((st = nnb::conv_weight_grad(s, g, grad, x, gw)) != NNB_OK) break;
 			const long long per = (long long)Cout * Kg;
 			nnb::TraceScope ts(s, nnb::kTraceConv);
 			nnb::sum_samples_kernel<<<nnb::grid_for(per, 256), 256, 0, s>>>(gw, (int)N, per, dweight, dweight_first);
 		}
-		if (dx) {
-			nnb::GemmDesc d;     // dcol[n][g] = W_g^T g[n][g] : [Kg, Cog] x [Cog, hw]  (ops.cpp:1584-1585)
-			d.ta = 1;
-			d.m = Kg; d.n = hw; d.k = Cog;
-			d.a = weight; d.lda = Kg; d.b = grad; d.ldb = hw; d.c = col; d.ldc = hw;
-			d.batch_outer = (long long)N; d.batch_inner = G;
-			d.sa_outer = 0; d.sa_inner = Cog * Kg;
-			d.sb_outer = (long long)Cout * hw; d.sb_inner = Cog * hw;
-			d.sc_outer = K * hw; d.sc_inner = Kg * hw;
-			d.mode = nnb::math_mode();
-			if ((st = nnb::gemm_run(s, d)) != NNB_OK) break;
-			nnb::TraceScope ts(s, nnb::kTraceConv);
-			nnb::col2im_kernel<<<nnb::grid_for((long long)N * Cin * H * W, 256), 256, 0, s>>>(g, col, dx, dx_first);
+		if (dx) {           // dcol[n][g] = W_g^T g[n][g] folded back (ops.cpp:1584-1587), one product
+			{
+				nnb::TraceScope ts(s, nnb::kTraceConv);
+				nnb::conv_weight_taps_kernel<<<nnb::grid_for((long long)Cout * Kg, 256), 256, 0, s>>>((long long)Cout * Kg,
+					(int)(Cin / G), (int)(Cout / G), (int)(kh * kw), weight, wt);
+			}
+			if ((st = nnb::cuda_status(cudaGetLastError(), "conv weight taps launch")) != NNB_OK) break;
+			if ((st = nnb::conv_input_grad(s, g, grad, wt, dx, dx_first)) != NNB_OK) break;
 		}
 		st = nnb::cuda_status(cudaGetLastError(), "conv2d_ex_bwd launch");
 	} while (0);

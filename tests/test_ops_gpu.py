@@ -209,6 +209,55 @@ def test_conv2d(cuda, N, Cin, H, W, Cout, k, stride, pad, fuse):
         assert np.array_equal(host(al)[~near0], al_o[~near0])
 
 
+@pytest.mark.parametrize("N,Cin,H,W,Cout,k,stride,pad", [(2, 3, 11, 10, 7, 5, 2, 2), (1, 4, 6, 7, 300, 3, 3, 1),
+                                                         (5, 130, 5, 5, 3, 1, 1, 0)])
+def test_conv2d_implicit_gemm_edges(cuda, N, Cin, H, W, Cout, k, stride, pad):
+    """The gathered-operand convolution at shapes the configs do not reach: a 5x5 kernel at stride 2
+    (the input gradient's gather skips positions no window reads), more output channels than one
+    128-row tile, a 1x1 kernel with 130 input channels (the depth spans several 16-wide stages); then
+    accumulation into existing gradients (first = 0) and Inf / NaN inputs propagated as IEEE fp32."""
+    torch = cuda
+    x, w, b = nrm(23, N, Cin, H, W), rnd(24, Cout, Cin, k, k), rnd(25, Cout)
+    ho, wo = (H + 2 * pad - k) // stride + 1, (W + 2 * pad - k) // stride + 1
+    g = nrm(26, N, Cout, ho, wo)
+    y_o, al_o = orc.zeros(N, Cout, ho, wo), np.zeros((N, Cout, ho, wo), np.uint8)
+    O.orc_conv2d_fwd(N, Cin, H, W, Cout, k, k, stride, pad, P(x), P(w), P(b), 0, P(y_o), P(al_o))
+    dx_o, dw_o, db_o = orc.zeros(N, Cin, H, W), orc.zeros(Cout, Cin, k, k), orc.zeros(Cout)
+    O.orc_conv2d_bwd(N, Cin, H, W, Cout, k, k, stride, pad, P(g), P(x), P(w), None, P(dx_o), 1, P(dw_o), 1, P(db_o), 1)
+    tx, tw, tb, tg = dev(torch, x), dev(torch, w), dev(torch, b), dev(torch, g)
+    y = torch.empty(N, Cout, ho, wo, device="cuda")
+    ok(lib().nnb_conv2d_fwd(S(torch), N, Cin, H, W, Cout, k, k, stride, pad, tx.data_ptr(), tw.data_ptr(),
+                            tb.data_ptr(), 0, y.data_ptr(), None))
+    assert_close(host(y), y_o)
+    dx = torch.full((N, Cin, H, W), 3.0, device="cuda")
+    dw = torch.full((Cout, Cin, k, k), 3.0, device="cuda")
+    db = torch.full((Cout,), 3.0, device="cuda")
+    for first in (1, 0):
+        ok(lib().nnb_conv2d_bwd(S(torch), N, Cin, H, W, Cout, k, k, stride, pad, tg.data_ptr(), tx.data_ptr(),
+                                tw.data_ptr(), None, dx.data_ptr(), first, dw.data_ptr(), first, db.data_ptr(), first))
+        if first:
+            assert_close(host(dx), dx_o)
+            assert_close(host(dw), dw_o)
+            assert_bits(host(db), db_o)
+    assert_close(host(dx), 2 * dx_o)
+    assert_close(host(dw), 2 * dw_o)
+    assert_bits(host(db), db_o + db_o)
+    # non-finite inputs
+    x[0, 0, 1, 1] = np.inf
+    x[N - 1, Cin - 1, H - 1, W - 2] = np.nan
+    y_o2, al_o2 = orc.zeros(N, Cout, ho, wo), np.zeros((N, Cout, ho, wo), np.uint8)
+    O.orc_conv2d_fwd(N, Cin, H, W, Cout, k, k, stride, pad, P(x), P(w), P(b), 0, P(y_o2), P(al_o2))
+    ok(lib().nnb_conv2d_fwd(S(torch), N, Cin, H, W, Cout, k, k, stride, pad, dev(torch, x).data_ptr(), tw.data_ptr(),
+                            tb.data_ptr(), 0, y.data_ptr(), None))
+    got = host(y)
+    assert np.array_equal(np.isnan(got), np.isnan(y_o2))
+    inf = np.isinf(y_o2)
+    assert np.array_equal(got[inf], y_o2[inf]) and not np.isinf(got[~inf]).any()
+    fin = np.isfinite(y_o2)
+    assert_close(got[fin], y_o2[fin])
+    assert nnb.device_error() == 0
+
+
 @pytest.mark.parametrize("k,stride,shape", [(2, 2, (64, 32, 28, 28)), (3, 1, (2, 3, 9, 10)), (3, 2, (2, 3, 9, 10))])
 def test_maxpool_bitwise(cuda, k, stride, shape):
     torch = cuda
