@@ -430,6 +430,13 @@ NNB_API nnb_status nnb_mt19937_seed_seq(const uint32_t* seeds, size_t count, uin
  * into the keep mask keep[(n + 31) / 32] (bit e % 32 of word e / 32 = element e kept, i.e.
  * u = float(x >> 8) * 2^-24 >= p). p == 0 keeps and p == 1 drops everything without drawing. */
 NNB_API nnb_status nnb_dropout_mask(void* stream, uint32_t* state, size_t n, float p, uint32_t* keep);
+/* The same draw of `total` outputs (the state ends where nnb_dropout_mask(total) leaves it) keeping
+ * only the decisions of outputs [offset, offset + count) in keep[(count + 31) / 32] (bit e of the
+ * slice = output offset + e; offset a multiple of 32): one data-parallel rank's rows of a layer's
+ * mask, bit for bit the rows of the whole batch's mask (dropout.cpp:20-31 draws the batch row-major
+ * from one generator). The serial generator still runs through every output. */
+NNB_API nnb_status nnb_dropout_mask_slice(void* stream, uint32_t* state, size_t total, size_t offset, size_t count,
+		float p, uint32_t* keep);
 /* y = x * m, m = kept ? 1 / (1 - p) : 0 (mul with the mask, ops.cpp:347). */
 NNB_API nnb_status nnb_dropout_apply(void* stream, size_t n, float p, const float* x, const uint32_t* keep, float* y);
 /* dx (+)= g * m with the grad_accum convention. */

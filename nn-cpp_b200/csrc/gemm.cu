@@ -670,7 +670,13 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 		// ---------------------------------- epilogue ----------------------------------
 		const int quad = warp & 3;                 // TMEM lanes this warp may access
 		const int row = quad * 32 + lane;
-		const bool vec_ok = p.act == kActNone && (p.ldc % 4 == 0) && (p.sc_outer % 4 == 0) &&
+		// the auxiliary output of a fused activation (ReLU's 1-byte mask, GELU's pre-activation) goes out
+		// through the staging tile too when its rows are 4-element aligned
+		const bool aux_ok = p.act == kActNone ||
+			((p.ld_aux % 4 == 0) && (p.s_aux_outer % 4 == 0) && (p.s_aux_inner % 4 == 0) &&
+			 (p.act == kActRelu ? (reinterpret_cast<uintptr_t>(p.mask) & 3) == 0
+			                    : (reinterpret_cast<uintptr_t>(p.pre) & 15) == 0));
+		const bool vec_ok = aux_ok && (p.ldc % 4 == 0) && (p.sc_outer % 4 == 0) &&
 			(p.sc_inner % 4 == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
 		// 32 x 32 staging tile of this warp: element (r, c) at float r*32 + 4*((c/4) ^ (r & 7)) + c%4, so that
 		// both the row-per-lane writes and the 4-rows-per-instruction reads are free of bank conflicts
@@ -687,7 +693,34 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 			const bool row_ok = gm < p.M;
 			float* cbase = p.C + batch_offset(bi, p.batch_inner, p.sc_outer, p.sc_inner);
 			float* crow = cbase + (long long)gm * p.ldc;
-			const long long aux_row = batch_offset(bi, p.batch_inner, p.s_aux_outer, p.s_aux_inner) + (long long)gm * p.ld_aux;
+			const long long aux_base = batch_offset(bi, p.batch_inner, p.s_aux_outer, p.s_aux_inner);
+			const long long aux_row = aux_base + (long long)gm * p.ld_aux;
+			float4* st4 = reinterpret_cast<float4*>(stage);
+			// the warp's 32 x 32 values v (row per lane) to rows of dst (row stride ld) at column gn0, as
+			// 128-byte row segments: lane (row) writes into the staging tile, then 8 lanes per row read
+			// 16-byte pieces back and store them (rows past M are skipped)
+			auto stage_rows = [&](float* dst, long long ld, int gn0, const float (&v)[32], bool acc) {
+#pragma unroll
+				for (int g = 0; g < 8; ++g)
+					st4[lane * 8 + (g ^ (lane & 7))] = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+				__syncwarp();
+				const int g = lane & 7;
+#pragma unroll
+				for (int k = 0; k < 8; ++k) {
+					const int rr = 4 * k + (lane >> 3);
+					const int grow = mt * kBM + quad * 32 + rr;
+					float4 o = st4[rr * 8 + (g ^ (rr & 7))];
+					if (grow < p.M) {
+						float4* d4 = reinterpret_cast<float4*>(dst + (long long)grow * ld + gn0) + g;
+						if (acc) {
+							const float4 c = *d4;
+							o.x = c.x + o.x; o.y = c.y + o.y; o.z = c.z + o.z; o.w = c.w + o.w;
+						}
+						*d4 = o;
+					}
+				}
+				__syncwarp();                       // the tile is read before it is written again
+			};
 			// a gathered B's flags are set during this kernel (by atomics, at L2): read them past L1
 			const bool fix = (*p.any_nonfinite | (kGather ? __ldcg(p.any_b) : *p.any_b)) != 0;
 			const bool row_bad = fix && row_ok && p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0;
@@ -728,44 +761,58 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 						v[j] = v[j] + (gn < p.N ? __ldg(p.bias + gn) : 0.0f);
 					}
 				}
+				uint32_t alive_bits = 0;
 				if (p.act == kActRelu) {
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {
-						const int gn = gn0 + j;
 						const bool alive = v[j] > 0.0f;
 						v[j] = alive ? v[j] : 0.0f;
-						if (gn < p.N) p.mask[aux_row + gn] = alive ? 1 : 0;
+						alive_bits |= (alive ? 1u : 0u) << j;
+					}
+					if (!staged) {
+#pragma unroll
+						for (int j = 0; j < 32; ++j)
+							if (gn0 + j < p.N) p.mask[aux_row + gn0 + j] = (alive_bits >> j) & 1u;
 					}
 				} else if (p.act == kActGelu) {
+					if (staged) {
+						stage_rows(p.pre + aux_base, p.ld_aux, gn0, v, false);
+					} else {
 #pragma unroll
-					for (int j = 0; j < 32; ++j) {
-						const int gn = gn0 + j;
-						if (gn < p.N) p.pre[aux_row + gn] = v[j];
-						v[j] = gelu_fwd(v[j], tanh_one(gelu_tanh_arg(v[j])));
+						for (int j = 0; j < 32; ++j)
+							if (gn0 + j < p.N) p.pre[aux_row + gn0 + j] = v[j];
 					}
+#pragma unroll
+					for (int j = 0; j < 32; ++j) v[j] = gelu_fwd(v[j], tanh_one(gelu_tanh_arg(v[j])));
 				}
 				if (staged) {
-					float4* st4 = reinterpret_cast<float4*>(stage);
+					stage_rows(cbase, p.ldc, gn0, v, p.accumulate != 0);
+					if (p.act == kActRelu) {
+						// the 32 x 32 alive bytes: row per lane into the tile (8 words of 4 bytes, the
+						// same XOR placement), then 4 rows of 32 bytes per store instruction
+						uint32_t* st = reinterpret_cast<uint32_t*>(stage);
 #pragma unroll
-					for (int g = 0; g < 8; ++g)
-						st4[lane * 8 + (g ^ (lane & 7))] = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
-					__syncwarp();
-					const int g = lane & 7;
-#pragma unroll
-					for (int k = 0; k < 8; ++k) {
-						const int rr = 4 * k + (lane >> 3);
-						const int grow = mt * kBM + quad * 32 + rr;
-						float4 o = st4[rr * 8 + (g ^ (rr & 7))];
-						if (grow < p.M) {
-							float4* dst = reinterpret_cast<float4*>(cbase + (long long)grow * p.ldc + gn0) + g;
-							if (p.accumulate) {
-								const float4 c = *dst;
-								o.x = c.x + o.x; o.y = c.y + o.y; o.z = c.z + o.z; o.w = c.w + o.w;
-							}
-							*dst = o;
+						for (int w = 0; w < 8; ++w) {
+							const uint32_t b = alive_bits >> (4 * w);
+							st[lane * 8 + (w ^ (lane & 7))] = (b & 1u) | ((b >> 1) & 1u) << 8 | ((b >> 2) & 1u) << 16 |
+								((b >> 3) & 1u) << 24;
 						}
+						__syncwarp();
+						const int w = lane & 7;
+#pragma unroll
+						for (int k = 0; k < 4; ++k) {
+							const int rr = 8 * k + (lane >> 3) * 2;
+#pragma unroll
+							for (int h2 = 0; h2 < 2; ++h2) {
+								const int r2 = rr + h2;
+								const int grow = mt * kBM + quad * 32 + r2;
+								if (grow < p.M)
+									*reinterpret_cast<uint32_t*>(p.mask + aux_base + (long long)grow * p.ld_aux + gn0 + 4 * w) =
+										st[r2 * 8 + (w ^ (r2 & 7))];
+							}
+						}
+						__syncwarp();
 					}
-					__syncwarp();                   // the tile is read before the next chunk is written
 				} else {
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {

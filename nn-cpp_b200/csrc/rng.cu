@@ -159,8 +159,10 @@ constexpr int kRound = 2 * kMtHalf;              // 454 words per round
 constexpr int kStreamThreads = 256;
 constexpr unsigned long long kChunk = 1ull << 24;  // outputs per serial launch (64 MB of raw words)
 
+// Outputs o in [w0, w1) of this launch's n go to raw[o - w0]; the others only advance the state (a
+// rank that needs a slice of a longer draw still runs the whole serial stream).
 __global__ void __launch_bounds__(kStreamThreads, 1) mt_stream_kernel(uint32_t* __restrict__ state,
-		unsigned long long n, uint32_t* __restrict__ raw) {
+		unsigned long long n, uint32_t* __restrict__ raw, unsigned long long w0, unsigned long long w1) {
 	__shared__ uint32_t ring[kRing];
 	const int t = threadIdx.x;
 	for (int i = t; i < kMtN; i += kStreamThreads) ring[i] = state[i];
@@ -168,8 +170,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1) mt_stream_kernel(uint32_t* 
 	__syncthreads();
 	const unsigned long long end = p0 + n, last = end - 1;                // outputs are X[p0 .. end)
 	const unsigned long long block0 = (last / kMtN) * kMtN, need = block0 + kMtN;
-	for (unsigned long long i = p0 + t; i < end && i < (unsigned long long)kMtN; i += kStreamThreads)
-		raw[i - p0] = ring[i];
+	const unsigned long long lo = p0 + w0, hi = p0 + (w1 < n ? w1 : n);   // X[lo .. hi) are written
+	for (unsigned long long i = lo + t; i < hi && i < (unsigned long long)kMtN; i += kStreamThreads)
+		raw[i - lo] = ring[i];
 	for (unsigned long long frontier = kMtN; frontier < need; frontier += kRound) {
 		if (t < kMtHalf) {
 			const unsigned long long j = frontier + t, j2 = j + kMtHalf;
@@ -178,8 +181,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) mt_stream_kernel(uint32_t* 
 			const uint32_t x2 = x1 ^ mt_mix(ring[(j - kMtShift) & (kRing - 1)], ring[(j - kMtShift + 1) & (kRing - 1)]);
 			ring[j & (kRing - 1)] = x1;
 			ring[j2 & (kRing - 1)] = x2;
-			if (j >= p0 && j < end) raw[j - p0] = x1;
-			if (j2 >= p0 && j2 < end) raw[j2 - p0] = x2;
+			if (j >= lo && j < hi) raw[j - lo] = x1;
+			if (j2 >= lo && j2 < hi) raw[j2 - lo] = x2;
 		}
 		__syncthreads();
 	}
@@ -243,34 +246,56 @@ nnb_status check_p(float p) {
 
 float dropout_keep_scale(float p) { return p < 1.0f ? 1.0f / (1.0f - p) : 0.0f; }
 
-nnb_status dropout_mask(cudaStream_t s, uint32_t* state, size_t n, float p, uint32_t* keep) {
+nnb_status dropout_mask_slice(cudaStream_t s, uint32_t* state, size_t total, size_t offset, size_t count, float p,
+		uint32_t* keep) {
 	NNB_TRY(check_p(p));
-	if (n == 0) return NNB_OK;
-	if (!state || !keep) return fail(NNB_ERR_INVALID, "dropout_mask: null pointer");
-	const size_t words = (n + 31) / 32;
+	if (offset > total || count > total - offset)
+		return fail(NNB_ERR_INVALID, "dropout_mask: slice [%zu, +%zu) outside %zu draws", offset, count, total);
+	if (offset % 32) return fail(NNB_ERR_UNSUPPORTED, "dropout_mask: slice offset %zu not a multiple of 32", offset);
+	if (total == 0) return NNB_OK;
+	if (!state || (count && !keep)) return fail(NNB_ERR_INVALID, "dropout_mask: null pointer");
+	const size_t words = (count + 31) / 32;
 	TraceScope ts(s, kTraceRowwise);
 	if (p == 0.0f || p == 1.0f)        // nothing is drawn (dropout.cpp:20-23)
-		return cuda_status(cudaMemsetAsync(keep, p == 0.0f ? 0xff : 0, words * sizeof(uint32_t), s), "dropout mask fill");
+		return count ? cuda_status(cudaMemsetAsync(keep, p == 0.0f ? 0xff : 0, words * sizeof(uint32_t), s),
+			"dropout mask fill") : NNB_OK;
 	const double scaled = std::ceil(static_cast<double>(p) * 16777216.0);    // exact: p * 2^24 <= 2^24
 	const uint32_t threshold = static_cast<uint32_t>(scaled);
 	void* ws = nullptr;
-	const size_t chunk = n < kChunk ? n : (size_t)kChunk;
-	NNB_TRY(scratch_alloc(&ws, chunk * sizeof(uint32_t), s));
+	const size_t chunk = count < kChunk ? count : (size_t)kChunk;
+	NNB_TRY(scratch_alloc(&ws, (chunk ? chunk : 1) * sizeof(uint32_t), s));
 	uint32_t* raw = static_cast<uint32_t*>(ws);
 	DeviceState* dev = nullptr;
 	nnb_status st = device_state(&dev);
-	for (size_t off = 0; st == NNB_OK && off < n; off += kChunk) {    // chunks are multiples of 32 outputs
-		const size_t c = n - off < kChunk ? n - off : (size_t)kChunk;
-		mt_stream_kernel<<<1, kStreamThreads, 0, s>>>(state, (unsigned long long)c, raw);
-		const unsigned long long words = (c + 31) / 32;
-		unsigned blocks = (unsigned)((words + 7) / 8);
-		const unsigned cap = (unsigned)dev->sm_count * 16;
-		if (blocks > cap) blocks = cap;
-		keep_pack_kernel<<<blocks, 256, 0, s>>>(raw, (unsigned long long)c, threshold, keep + off / 32);
+	// chunks of the whole draw are multiples of 32 outputs; the slice's part of each is tempered and
+	// packed at its bit position in `keep`
+	for (size_t g0 = 0; st == NNB_OK && g0 < total; g0 += kChunk) {
+		const size_t c = total - g0 < kChunk ? total - g0 : (size_t)kChunk;
+		// this chunk's part of the slice, [lo_g, hi_g) in output numbers (empty when they do not meet)
+		const size_t lo_g = offset > g0 ? offset : g0;
+		const size_t hi_g = offset + count < g0 + c ? offset + count : g0 + c;
+		const bool some = lo_g < hi_g;
+		const size_t a = some ? lo_g - g0 : 0, b = some ? hi_g - g0 : 0;
+		if (b > c || b - a > chunk) {              // the window always fits the chunk and the raw buffer
+			st = fail(NNB_ERR_INVALID, "dropout_mask: internal slice window [%zu, %zu) of %zu", a, b, c);
+			break;
+		}
+		mt_stream_kernel<<<1, kStreamThreads, 0, s>>>(state, (unsigned long long)c, raw, a, b);
+		if (some) {
+			const unsigned long long wn = (unsigned long long)(b - a);
+			unsigned blocks = (unsigned)(((wn + 31) / 32 + 7) / 8);
+			const unsigned cap = (unsigned)dev->sm_count * 16;
+			if (blocks > cap) blocks = cap;
+			keep_pack_kernel<<<blocks, 256, 0, s>>>(raw, wn, threshold, keep + (lo_g - offset) / 32);
+		}
 		st = cuda_status(cudaGetLastError(), "dropout_mask launch");
 	}
 	nnb_status st2 = scratch_free(ws, s);
 	return st != NNB_OK ? st : st2;
+}
+
+nnb_status dropout_mask(cudaStream_t s, uint32_t* state, size_t n, float p, uint32_t* keep) {
+	return dropout_mask_slice(s, state, n, 0, n, p, keep);
 }
 
 }  // namespace nnb
@@ -371,6 +396,11 @@ nnb_status nnb_weighted_draws(uint32_t* state, const double* cumulative, size_t 
 
 nnb_status nnb_dropout_mask(void* stream, uint32_t* state, size_t n, float p, uint32_t* keep) {
 	return nnb::dropout_mask(static_cast<cudaStream_t>(stream), state, n, p, keep);
+}
+
+nnb_status nnb_dropout_mask_slice(void* stream, uint32_t* state, size_t total, size_t offset, size_t count, float p,
+		uint32_t* keep) {
+	return nnb::dropout_mask_slice(static_cast<cudaStream_t>(stream), state, total, offset, count, p, keep);
 }
 
 nnb_status nnb_dropout_apply(void* stream, size_t n, float p, const float* x, const uint32_t* keep, float* y) {

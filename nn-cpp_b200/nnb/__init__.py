@@ -130,6 +130,7 @@ _SIGS = {
     "nnb_derive_generator": ([_c.c_char_p, _p], _i),
     "nnb_mt19937_seed_seq": ([_p, _sz, _p], _i),
     "nnb_dropout_mask": ([_p, _p, _sz, _f, _p], _i),
+    "nnb_dropout_mask_slice": ([_p, _p, _sz, _sz, _sz, _f, _p], _i),
     "nnb_dropout_apply": ([_p, _sz, _f, _p, _p, _p], _i),
     "nnb_dropout_bwd": ([_p, _sz, _f, _p, _p, _p, _i], _i),
     "nnb_mt19937_seed": ([_c.c_uint32, _p], _i),

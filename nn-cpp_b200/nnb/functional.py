@@ -399,11 +399,40 @@ def _flash_attention(q, k, v, heads, key_padding_mask, causal, N, Tq, Tk, D) -> 
 
 # ---- dropout (src/nn/dropout.cpp:20-31) and attention with dropout (src/nn/attention.cpp:36-47) ------
 
+# Batch slice of a data-parallel rank: (rows of the whole batch, first row, end row) while a rank runs
+# its rows of a batch whose dropout masks the reference draws over all rows at once.
+_BATCH_SLICE = None
+
+
+@contextlib.contextmanager
+def batch_slice(total_rows: int, row_lo: int, row_hi: int):
+    """Inside, every dropout mask is drawn as this rank's rows [row_lo, row_hi) of the mask the whole
+    batch of total_rows rows would draw (dropout.cpp:20-31 draws row-major from one generator), and
+    the generator advances past the whole batch's draws: ranks stay in step and every rank's masks are
+    the single-process masks' rows."""
+    global _BATCH_SLICE
+    old = _BATCH_SLICE
+    _BATCH_SLICE = None if (row_lo == 0 and row_hi == total_rows) else (total_rows, row_lo, row_hi)
+    try:
+        yield
+    finally:
+        _BATCH_SLICE = old
+
+
 def dropout_mask(state: torch.Tensor, n: int, p: float) -> torch.Tensor:
     """Dropout::forward's n keep / drop decisions drawn from the device generator `state` (advanced
-    in place): (n + 31) // 32 words, bit e % 32 of word e // 32 set when element e is kept."""
+    in place): (n + 31) // 32 words, bit e % 32 of word e // 32 set when element e is kept. Inside
+    batch_slice, n covers this rank's rows and the draw is that slice of the whole batch's."""
     keep = empty(((n + 31) // 32,), dtype=torch.int32, device=state.device)
-    check(lib().nnb_dropout_mask(_s(), _p(state), n, ctypes.c_float(p), _p(keep)))
+    if _BATCH_SLICE is None:
+        check(lib().nnb_dropout_mask(_s(), _p(state), n, ctypes.c_float(p), _p(keep)))
+    else:
+        total_rows, lo, hi = _BATCH_SLICE
+        if hi <= lo or n % (hi - lo):
+            raise ValueError("dropout under batch_slice: the tensor's leading axis is not the rank's rows")
+        per_row = n // (hi - lo)
+        check(lib().nnb_dropout_mask_slice(_s(), _p(state), per_row * total_rows, per_row * lo, n, ctypes.c_float(p),
+                                           _p(keep)))
     return keep
 
 

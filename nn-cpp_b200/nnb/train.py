@@ -74,11 +74,6 @@ class ShardedTrainer:
     def __init__(self, model, optimizer, shards: int = 8, world: int = 1, rank: int = 0, group=None):
         if shards % world:
             raise ValueError("the virtual shard count must be a multiple of the number of ranks")
-        from .nn import Dropout
-        if world > 1 and any(isinstance(m, Dropout) and m.p > 0 for m in model.modules()):
-            # the reference draws one mask over the whole batch; a rank's slice of that draw would need
-            # the whole serial stream on every rank
-            raise NotImplementedError("dropout with more than one rank")
         self.model, self.opt = model, optimizer
         self.shards, self.world, self.rank, self.group = shards, world, rank, group
         self.owned = shard_owners(shards, world, rank)
@@ -198,7 +193,8 @@ class ShardedTrainer:
             self.grad_norm = torch.tensor([1.0 / (B * T)], dtype=torch.float32, device=ids.device)
         self._point_grads(self.shard_grads)
         groups = len(self.owned)
-        with F.param_groups(groups):
+        # with several ranks each dropout mask is this rank's rows of the whole batch's draw
+        with F.param_groups(groups), F.batch_slice(B, lo, hi):
             logits = self.model(ids[lo:hi])
             loss = F.sequence_cross_entropy(logits, targets[lo:hi], grad_norm=self.grad_norm)
             loss.backward()

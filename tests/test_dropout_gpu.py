@@ -185,9 +185,82 @@ def test_transformer_with_dropout_trains_like_reference(cuda):
     assert (err <= 1e-5 * np.abs(r_params).max()).mean() > 0.995
 
 
-def test_sharded_trainer_rejects_dropout_on_several_ranks(cuda):
-    from nnb.nn import AdamW, Transformer, TransformerConfig
+def test_dropout_mask_slice_is_the_rows_of_the_whole_draw(cuda):
+    """nnb_dropout_mask_slice: a rank's slice of a draw has the bits of the same outputs of the whole
+    draw, and the generator ends where the whole draw leaves it -- for slices inside one 2^24-output
+    chunk, across a chunk boundary, at the end, and empty."""
+    torch = cuda
+    import ctypes
+    import nnb
+    import nnb.random as nr
+    nr.manual_seed(71)
+    state0 = nr.device_generator("dropout", torch.device("cuda"))
+    total, p = (1 << 24) + 3 * 4096 + 96, 0.3
+    s = torch.cuda.current_stream().cuda_stream
+    full_state = state0.clone()
+    full = torch.empty((total + 31) // 32, dtype=torch.int32, device="cuda")
+    nnb.check(nnb.lib().nnb_dropout_mask(s, full_state.data_ptr(), total, ctypes.c_float(p), full.data_ptr()))
+    bits = np.unpackbits(full.cpu().numpy().view(np.uint8), bitorder="little")[:total]
+    for offset, count in ((0, 4096), (4096 * 7, 12288 + 5), ((1 << 24) - 4096, 8192), (total - 96, 96), (64, 0)):
+        st = state0.clone()
+        keep = torch.zeros(max(1, (count + 31) // 32), dtype=torch.int32, device="cuda")
+        nnb.check(nnb.lib().nnb_dropout_mask_slice(s, st.data_ptr(), total, offset, count, ctypes.c_float(p),
+                                                   keep.data_ptr()))
+        got = np.unpackbits(keep.cpu().numpy().view(np.uint8), bitorder="little")[:count]
+        assert np.array_equal(got, bits[offset:offset + count]), (offset, count)
+        assert torch.equal(st, full_state), (offset, count)
+    with pytest.raises(nnb.NnbError):
+        nnb.check(nnb.lib().nnb_dropout_mask_slice(s, state0.clone().data_ptr(), total, 5, 10, ctypes.c_float(p),
+                                                   full.data_ptr()))
+
+
+def test_data_parallel_dropout_ranks_emulated(cuda):
+    """The data-parallel step with dropout, each rank's pass run one after another on one GPU (the
+    generators reset to the step's start state for every rank, as separate GPUs hold their own copies):
+    every rank's rows draw their part of the whole batch's masks, so the gathered shard gradients
+    equal the one-rank step's bit for bit, the loss agrees, and every rank's generators end in the same
+    state."""
+    torch = cuda
+    import nnb
+    import nnb.random as nr
+    from nnb import functional as F
+    from nnb.nn import AdamW, Dropout, Transformer, TransformerConfig
     from nnb.train import ShardedTrainer
-    model = Transformer(TransformerConfig(vocab_size=16, dim=16, heads=2, layers=1, max_len=8, dropout=0.1))
-    with pytest.raises(NotImplementedError):
-        ShardedTrainer(model, AdamW(model.parameters()), shards=8, world=2, rank=0)
+    cfg = TransformerConfig(vocab_size=48, dim=64, heads=1, layers=2, max_len=32, dropout=0.1)  # head size 64
+    ids = orc.integers(96, 8 * 33, 0, 47).reshape(8, 33)
+    x_d, y_d = torch.from_numpy(ids[:, :32].copy()).cuda(), torch.from_numpy(ids[:, 1:].copy()).cuda()
+    nr.manual_seed(5)
+    m1 = Transformer(cfg, seed=3)
+    tr1 = ShardedTrainer(m1, AdamW(m1.parameters(), lr=1e-3), shards=8)
+    drops1 = [mod for mod in m1.modules() if isinstance(mod, Dropout)]
+    start = [d.state.clone() for d in drops1]
+    loss1 = tr1.step(x_d, y_d).clone()
+    g1 = tr1.reduced.clone()
+    end1 = [d.state.clone() for d in drops1]
+    # the same step as 4 ranks of 2 shards each
+    nr.manual_seed(5)
+    m4 = Transformer(cfg, seed=3)
+    drops4 = [mod for mod in m4.modules() if isinstance(mod, Dropout)]
+    opt = AdamW(m4.parameters(), lr=1e-3)
+    trs = [ShardedTrainer(m4, opt, shards=8, world=4, rank=r) for r in range(4)]
+    norm = torch.tensor([1.0 / x_d.numel()], device="cuda")
+    gathered = torch.empty(8, trs[0].total, device="cuda")
+    losses = []
+    for r, tr in enumerate(trs):
+        for d, s0 in zip(drops4, start):
+            d.state.copy_(s0)
+        tr._point_grads(tr.shard_grads)
+        with F.param_groups(2), F.batch_slice(8, 2 * r, 2 * r + 2):
+            logits = m4(x_d[2 * r:2 * r + 2])
+            loss = F.sequence_cross_entropy(logits, y_d[2 * r:2 * r + 2], grad_norm=norm)
+            loss.backward()
+        losses.append(loss.data.clone())
+        gathered[2 * r:2 * r + 2].copy_(tr.shard_grads)
+        for d, e in zip(drops4, end1):
+            assert torch.equal(d.state, e)
+    reduced = torch.empty(trs[0].total, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    nnb.check(nnb.lib().nnb_column_sum(s, 8, trs[0].total, gathered.data_ptr(), reduced.data_ptr(), 1))
+    assert torch.equal(reduced, g1)
+    # the loss is each rank's mean, averaged over ranks: the same value, summed in another order
+    np.testing.assert_allclose(float(torch.cat(losses).mean()), float(loss1[0]), rtol=1e-6)

@@ -169,3 +169,38 @@ def test_scaled_masked_softmax_matches_reference(cuda, N, H, Tq, Tk, causal, pad
     got = acc.cpu().numpy()
     assert np.all(got[masked] == 7.0)
     assert_close(got[~masked] - 7.0, dx_r[~masked], rel=1e-5 * 8)
+
+
+@pytest.mark.parametrize("N,H,T,causal,padded", [(2, 3, 17, True, False), (3, 2, 40, False, True), (2, 8, 64, True, True)])
+def test_masked_softmax_rows_in_place(cuda, N, H, T, causal, padded):
+    """nnb_masked_softmax_fwd / _bwd, the attention paths' in-place row kernels (masked_softmax_row and
+    its backward, ops.cpp:1183-1224), called directly: against the reference's scaled_masked_softmax on
+    the same scores (the same row arithmetic: scale, pad -> -1e9, causal -> -2e9 / 0, softmax), and the
+    backward turning dL/dP into dL/dS in place with 0 at masked positions."""
+    torch = cuda
+    ref = _ref()
+    x = orc.normal(220, N * H * T * T).reshape(N, H, T, T)
+    g = orc.normal(221, x.size).reshape(x.shape)
+    pad = None
+    if padded:
+        pad = np.ones((N, T), np.float32)
+        pad[:, T - 3:] = 0.0
+    scale = 0.125
+    y_r, dx_r = np.zeros_like(x), np.zeros_like(x)
+    ref.ref_scaled_masked_softmax(N, H, T, T, orc.ptr(x), scale, orc.ptr(pad), int(causal), orc.ptr(g), orc.ptr(y_r),
+                                  orc.ptr(dx_r))
+    s = torch.cuda.current_stream().cuda_stream
+    scores = torch.from_numpy(x).cuda()
+    pad_d = None if pad is None else torch.from_numpy(pad).cuda()
+    nnb.check(nnb.lib().nnb_masked_softmax_fwd(s, N, H, T, T, scores.data_ptr(),
+                                               None if pad_d is None else pad_d.data_ptr(), int(causal),
+                                               ctypes.c_float(scale)))
+    assert_close(scores.cpu().numpy(), y_r, rel=1e-5)
+    grad = torch.from_numpy(g).cuda()
+    nnb.check(nnb.lib().nnb_masked_softmax_bwd(s, N, H, T, T, scores.data_ptr(), grad.data_ptr(),
+                                               None if pad_d is None else pad_d.data_ptr(), int(causal),
+                                               ctypes.c_float(scale)))
+    got = grad.cpu().numpy()
+    assert_close(got, dx_r, rel=1e-5)
+    if causal:
+        assert np.all(got[..., np.triu(np.ones((T, T), bool), 1)] == 0.0)

@@ -136,10 +136,11 @@ def test_sharded_gemm_bitwise_equal_to_single_gpu(cuda, tmp_path, mode, gather, 
     assert bool(np.load(tmp_path / f"eq_{mode}_{gather}.npy")[0])
 
 
-def _dp_worker(rank, world, port, out_dir):
+def _dp_worker(rank, world, port, out_dir, dropout=0.0):
     import torch
     import torch.distributed as dist
 
+    import nnb.random as nr
     from nnb.nn import AdamW, Transformer, TransformerConfig
     from nnb.train import ShardedTrainer
 
@@ -147,7 +148,9 @@ def _dp_worker(rank, world, port, out_dir):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
     try:
-        cfg = TransformerConfig(vocab_size=128, dim=128, heads=2, layers=2, max_len=64)   # head size 64: fused attention
+        nr.manual_seed(9)
+        # head size 64: fused attention without dropout, the composed path with it
+        cfg = TransformerConfig(vocab_size=128, dim=128, heads=2, layers=2, max_len=64, dropout=dropout)
         g = torch.Generator().manual_seed(3)
         ids = torch.randint(0, 128, (8, 65), generator=g)
         x, y = ids[:, :-1].contiguous().cuda(), ids[:, 1:].contiguous().cuda()
@@ -158,6 +161,7 @@ def _dp_worker(rank, world, port, out_dir):
         flat = torch.cat([p.data.reshape(-1) for p in model.parameters()])
         # the same two steps with the second one captured into a CUDA graph (all-to-all and all-gather
         # inside the graph) and replayed
+        nr.manual_seed(9)
         gmodel = Transformer(cfg, seed=4)
         gtr = ShardedTrainer(gmodel, AdamW(gmodel.parameters(), lr=3e-3), shards=8, world=world, rank=rank)
         step = gtr.capture(x, y, warmup=1)
@@ -166,31 +170,34 @@ def _dp_worker(rank, world, port, out_dir):
         gflat = torch.cat([p.data.reshape(-1) for p in gmodel.parameters()])
         step.release()
         if rank == 0:
+            nr.manual_seed(9)
             ref_model = Transformer(cfg, seed=4)
             ref_tr = ShardedTrainer(ref_model, AdamW(ref_model.parameters(), lr=3e-3), shards=8)
             for _ in range(2):
                 ref_tr.step(x, y)
             ref_flat = torch.cat([p.data.reshape(-1) for p in ref_model.parameters()])
-            np.save(os.path.join(out_dir, "dp_eq.npy"), np.array([bool(torch.equal(flat, ref_flat)),
-                                                                  bool(torch.equal(gflat, ref_flat))]))
+            np.save(os.path.join(out_dir, f"dp_eq_{dropout}.npy"), np.array([bool(torch.equal(flat, ref_flat)),
+                                                                             bool(torch.equal(gflat, ref_flat))]))
         dist.barrier(device_ids=[rank])
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.gpu
-def test_data_parallel_step_bitwise_equal_to_single_gpu(cuda, tmp_path):
+@pytest.mark.parametrize("dropout", [0.0, 0.1])
+def test_data_parallel_step_bitwise_equal_to_single_gpu(cuda, tmp_path, dropout):
     """Two training steps of the virtual-shard data-parallel step on every GPU of the box (2, 4 or 8;
-    the largest divisor of 8 otherwise) give the same weights, bit for bit, as on one GPU."""
+    the largest divisor of 8 otherwise) give the same weights, bit for bit, as on one GPU -- with
+    dropout too (each rank draws its rows of the whole batch's masks)."""
     torch = cuda
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs two or more GPUs")
     while 8 % world:               # the 8 virtual shards need a world that divides them
         world -= 1
-    mp.start_processes(_dp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_dp_worker, args=(world, _free_port(), str(tmp_path), dropout), nprocs=world, join=True,
                        start_method="spawn")
-    eq = np.load(tmp_path / "dp_eq.npy")
+    eq = np.load(tmp_path / f"dp_eq_{dropout}.npy")
     assert bool(eq[0]), "eager data-parallel steps differ from one GPU"
     assert bool(eq[1]), "graph-replayed data-parallel step differs from one GPU"
 
