@@ -560,51 +560,49 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 			}
 		}
 	} else if (warp == 1) {
-		if (lane == 0) {
-			// ------------------------------ MMA issuer --------------------------------
-			constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
-			int stage = 0;
-			uint32_t phase = 0;
-			int it = 0;
-			for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-				const int buf = it & 1;
-				const uint32_t acc_phase = (it >> 1) & 1;
-				if (!mbar_wait(smem_u32(&acce_bar[buf]), acc_phase ^ 1, p.err, kDevTimeoutAccumFree, abort_flag)) break;
+		// --------------------- MMA issuer (the whole warp; one elected lane issues) ---------------------
+		constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
+		int stage = 0;
+		uint32_t phase = 0;
+		int it = 0;
+		for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+			const int buf = it & 1;
+			const uint32_t acc_phase = (it >> 1) & 1;
+			if (!mbar_wait_warp(smem_u32(&acce_bar[buf]), acc_phase ^ 1, p.err, kDevTimeoutAccumFree, abort_flag)) break;
+			tc_fence_after();
+			const uint32_t d_tmem = tmem_base + buf * kBN;
+			bool ok = true;
+			for (int kb = 0; kb < p.KB; ++kb) {
+				if (!mbar_wait_warp(smem_u32(&full_bar[stage]), phase, p.err, kDevTimeoutFull, abort_flag)) {
+					ok = false;
+					break;
+				}
 				tc_fence_after();
-				const uint32_t d_tmem = tmem_base + buf * kBN;
-				bool ok = true;
-				for (int kb = 0; kb < p.KB; ++kb) {
-					if (!mbar_wait(smem_u32(&full_bar[stage]), phase, p.err, kDevTimeoutFull, abort_flag)) {
-						ok = false;
-						break;
-					}
-					tc_fence_after();
-					const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
+				const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
 #pragma unroll
-					for (int kk = 0; kk < kBK / 8; ++kk) {
-						const uint32_t off = kk * 32;    // 8 tf32 = 32 bytes along the swizzled row
-						const uint64_t a_hi = smem_desc_k_sw64(base + off);
-						const uint64_t b_hi = smem_desc_k_sw64(base + C::kABytes + off);
-						const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-						if (kSplit) {
-							const uint64_t a_lo = smem_desc_k_sw64(base + kAPanelRows * kBK * 4 + off);
-							const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
-							mma_tf32(d_tmem, a_lo, b_hi, idesc, first);
-							mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
-							mma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
-						} else {
-							mma_tf32(d_tmem, a_hi, b_hi, idesc, first);
-						}
-					}
-					mma_commit(smem_u32(&empty_bar[stage]));
-					if (++stage == kStages) {
-						stage = 0;
-						phase ^= 1;
+				for (int kk = 0; kk < kBK / 8; ++kk) {
+					const uint32_t off = kk * 32;    // 8 tf32 = 32 bytes along the swizzled row
+					const uint64_t a_hi = smem_desc_k_sw64(base + off);
+					const uint64_t b_hi = smem_desc_k_sw64(base + C::kABytes + off);
+					const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+					if (kSplit) {
+						const uint64_t a_lo = smem_desc_k_sw64(base + kAPanelRows * kBK * 4 + off);
+						const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
+						mma_tf32_elect(d_tmem, a_lo, b_hi, idesc, first);
+						mma_tf32_elect(d_tmem, a_hi, b_lo, idesc, 1u);
+						mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, 1u);
+					} else {
+						mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, first);
 					}
 				}
-				if (!ok) break;
-				mma_commit(smem_u32(&accf_bar[buf]));
+				mma_commit_elect(smem_u32(&empty_bar[stage]));
+				if (++stage == kStages) {
+					stage = 0;
+					phase ^= 1;
+				}
 			}
+			if (!ok) break;
+			mma_commit_elect(smem_u32(&accf_bar[buf]));
 		}
 	} else if (kGather && warp >= kThreads / 32) {
 		// ------------------------- B gatherers (implicit GEMM) -------------------------

@@ -106,6 +106,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
 	}
 }
 
+// mbar_wait by every lane of a converged warp, with a warp-uniform result (false if any lane's wait
+// gave up), for roles whose whole warp runs the loop.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, int* err, int code, volatile int* abort) {
+	return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code, abort));
+}
+
 // ---------------------------------------------------------------------------------------------
 // TMA (bulk tensor copies, global -> shared, completion counted on an mbarrier). No multicast.
 // ---------------------------------------------------------------------------------------------
@@ -229,6 +235,41 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
 		"setp.ne.b32 p, %4, 0;\n\t"
 		"tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
 		"r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+		: "memory");
+}
+
+// Warp-collective forms of the MMA and commit: every lane of a converged warp executes them with the
+// same (warp-uniform) operands and the lane that elect.sync picks -- always the lowest, so the same
+// lane for every call -- issues the instruction. A role that runs its whole loop this way keeps its
+// descriptors and tensor-memory addresses warp-uniform: measured with clock stamps in the attention
+// kernels, issuing took about 50 cycles per MMA from a loop run by one lane of a diverged warp and
+// about 25-30 from the whole warp -- the tensor core needs about 16-32 cycles for a 128 x 32..64 x 8
+// tf32 MMA, so the one-lane loop, not the tensor core, set the pace.
+__device__ __forceinline__ void mma_tf32_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+		uint32_t accumulate) {
+	asm volatile(
+		"{\n\t.reg .pred p, e;\n\t"
+		"elect.sync _|e, 0xffffffff;\n\t"
+		"setp.ne.b32 p, %4, 0;\n\t"
+		"@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+		"l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+		: "memory");
+}
+__device__ __forceinline__ void mma_tf32_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+		uint32_t accumulate) {
+	asm volatile(
+		"{\n\t.reg .pred p, e;\n\t"
+		"elect.sync _|e, 0xffffffff;\n\t"
+		"setp.ne.b32 p, %4, 0;\n\t"
+		"@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+		"r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+		: "memory");
+}
+__device__ __forceinline__ void mma_commit_elect(uint32_t bar) {
+	asm volatile(
+		"{\n\t.reg .pred e;\n\t"
+		"elect.sync _|e, 0xffffffff;\n\t"
+		"@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
 		: "memory");
 }
 

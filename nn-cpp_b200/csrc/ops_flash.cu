@@ -151,30 +151,55 @@ __device__ __forceinline__ void vals_to_tmem16(const float (&v)[16], uint32_t ta
 	tmem_st_32x32b_x16(taddr_lo, lo);
 }
 
+// Bit c set when key key0 + c takes part in query row qrow's softmax: below Tk and, causal, not after
+// the row. Built arithmetically so that the masked paths below select per column without branching (a
+// per-column test of a lane-dependent condition around the padding load made every column a divergent
+// branch: the masked tiles ran about six times slower than the others).
+__device__ __forceinline__ uint32_t live_bits32(int key0, int qrow, int Tk, int causal) {
+	int n = Tk - key0;
+	if (causal) n = min(n, qrow - key0 + 1);
+	return n <= 0 ? 0u : n >= 32 ? 0xffffffffu : (1u << n) - 1u;
+}
+
+// Bit c set when key key0 + c is live and marked as padding (0) in the key-padding row padn (null: none).
+__device__ __forceinline__ uint32_t padded_bits32(const float* padn, int key0, uint32_t live) {
+	uint32_t bits = 0;
+	if (padn) {
+#pragma unroll
+		for (int c = 0; c < 32; ++c) {
+			const bool on = (live >> c) & 1u;
+			const float f = on ? padn[key0 + c] : 1.0f;
+			bits |= (f == 0.0f ? 1u : 0u) << c;
+		}
+	}
+	return bits;
+}
+
 // One MMA step (depth 8) of D (+)= A B, three TF32 MMAs (lo*hi, hi*lo, hi*hi) in the 3xTF32 split
 // or one (hi*hi) in TF32; A from tensor memory (hi, lo columns) or shared memory (hi, lo
 // descriptors), B from shared-memory descriptors (hi, lo). The caller passes descriptors built once
-// per tile plus compile-time offsets, so issuing an MMA costs a few instructions.
+// per tile plus compile-time offsets, so issuing an MMA costs a few instructions. Warp-collective:
+// the whole MMA warp calls it and one elected lane issues.
 template <int kSplit>
 __device__ __forceinline__ void mma_step(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint64_t b_hi, uint64_t b_lo,
 		uint32_t idesc, uint32_t acc) {
 	if (kSplit) {
-		mma_tf32_ts(d, a_lo, b_hi, idesc, acc);
-		mma_tf32_ts(d, a_hi, b_lo, idesc, 1u);
-		mma_tf32_ts(d, a_hi, b_hi, idesc, 1u);
+		mma_tf32_ts_elect(d, a_lo, b_hi, idesc, acc);
+		mma_tf32_ts_elect(d, a_hi, b_lo, idesc, 1u);
+		mma_tf32_ts_elect(d, a_hi, b_hi, idesc, 1u);
 	} else {
-		mma_tf32_ts(d, a_hi, b_hi, idesc, acc);
+		mma_tf32_ts_elect(d, a_hi, b_hi, idesc, acc);
 	}
 }
 template <int kSplit>
 __device__ __forceinline__ void mma_step_ss(uint32_t d, uint64_t a_hi, uint64_t a_lo, uint64_t b_hi, uint64_t b_lo,
 		uint32_t idesc, uint32_t acc) {
 	if (kSplit) {
-		mma_tf32(d, a_lo, b_hi, idesc, acc);
-		mma_tf32(d, a_hi, b_lo, idesc, 1u);
-		mma_tf32(d, a_hi, b_hi, idesc, 1u);
+		mma_tf32_elect(d, a_lo, b_hi, idesc, acc);
+		mma_tf32_elect(d, a_hi, b_lo, idesc, 1u);
+		mma_tf32_elect(d, a_hi, b_hi, idesc, 1u);
 	} else {
-		mma_tf32(d, a_hi, b_hi, idesc, acc);
+		mma_tf32_elect(d, a_hi, b_hi, idesc, acc);
 	}
 }
 
@@ -404,63 +429,61 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			}
 		}
 	} else if (warp == 1) {
-		if (lane == 0) {
-			// ---------------------------------- MMA issuer ----------------------------------
-			const uint32_t id_s = idesc_tf32(kFwdRows, kFwdKeys);
-			const uint32_t id_pv = idesc_tf32(kFwdRows, kDh) | kIdescBMajorMN;
-			int t = 0, i = 0;
-			bool ok = true;
-			for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
-				int q0, nh, J;
-				fwd_item(p, w, q0, nh, J);
-				// this item's Q is in tensor memory (written after the previous item's last score MMA)
-				if (!mbar_wait(smem_u32(&q_ready), i & 1, p.err, kDevTimeoutAttn, abort_flag)) break;
-				tc_fence_after();
-				for (int j = 0; j <= J; ++j) {
-					if (j < J) {                       // S_t = Q K_t^T
-						const int tt = t + j, s = tt % kFwdSlots;
-						if (!mbar_wait(smem_u32(&k_full[s]), (tt / kFwdSlots) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
-							ok = false;
-							break;
-						}
-						tc_fence_after();
-						const uint64_t kd = smem_desc_k_sw64(smem_u32(smem + s * kFwdSlotBytes));
-						const uint32_t d = tmem + kFColS + (tt & 1) * 128;
-#pragma unroll
-						for (int ks = 0; ks < kDh / 8; ++ks) {
-							const uint32_t ko = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
-							mma_step<kSplit>(d, tmem + kFColQhi + ks * 8, tmem + kFColQlo + ks * 8, desc_at(kd, ko),
-								desc_at(kd, kFwdOpBytes + ko), id_s, ks > 0);
-						}
-						mma_commit(smem_u32(&s_full[tt & 1]));
-						mma_commit(smem_u32(&k_empty[s]));
+		// ---------------------------------- MMA issuer ----------------------------------
+		const uint32_t id_s = idesc_tf32(kFwdRows, kFwdKeys);
+		const uint32_t id_pv = idesc_tf32(kFwdRows, kDh) | kIdescBMajorMN;
+		int t = 0, i = 0;
+		bool ok = true;
+		for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
+			int q0, nh, J;
+			fwd_item(p, w, q0, nh, J);
+			// this item's Q is in tensor memory (written after the previous item's last score MMA)
+			if (!warp_wait(smem_u32(&q_ready), i & 1, p.err, abort_flag)) break;
+			tc_fence_after();
+			for (int j = 0; j <= J; ++j) {
+				if (j < J) {                       // S_t = Q K_t^T
+					const int tt = t + j, s = tt % kFwdSlots;
+					if (!warp_wait(smem_u32(&k_full[s]), (tt / kFwdSlots) & 1, p.err, abort_flag)) {
+						ok = false;
+						break;
 					}
-					if (j >= 1) {                      // O_t-1 part = P_t-1 V_t-1
-						const int tp = t + j - 1, b = tp & 1, s = tp % kFwdSlots;
-						if (!mbar_wait(smem_u32(&p_full[b]), (tp >> 1) & 1, p.err, kDevTimeoutAttn, abort_flag) ||
-								(tp >= 2 && !mbar_wait(smem_u32(&pv_empty[b]), ((tp >> 1) - 1) & 1, p.err, kDevTimeoutAttn,
-									abort_flag)) ||
-								!mbar_wait(smem_u32(&v_full[s]), (tp / kFwdSlots) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
-							ok = false;
-							break;
-						}
-						tc_fence_after();
-						const uint64_t vd = smem_desc_mn_sw128b32(smem_u32(smem + kFwdVBase + s * kFwdSlotBytes), kFwdKeys * 128);
-						const uint32_t d = tmem + kFColPV + b * 64, pc = tmem + kFColS + b * 128;
+					tc_fence_after();
+					const uint64_t kd = smem_desc_k_sw64(smem_u32(smem + s * kFwdSlotBytes));
+					const uint32_t d = tmem + kFColS + (tt & 1) * 128;
 #pragma unroll
-						for (int ks = 0; ks < kFwdKeys / 8; ++ks)
-							mma_step<kSplit>(d, pc + ks * 8, pc + 64 + ks * 8, desc_at(vd, ks * 1024),
-								desc_at(vd, kFwdOpBytes + ks * 1024), id_pv, ks > 0);
-						mma_commit(smem_u32(&pv_full[b]));
-						mma_commit(smem_u32(&v_empty[s]));
+					for (int ks = 0; ks < kDh / 8; ++ks) {
+						const uint32_t ko = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
+						mma_step<kSplit>(d, tmem + kFColQhi + ks * 8, tmem + kFColQlo + ks * 8, desc_at(kd, ko),
+							desc_at(kd, kFwdOpBytes + ko), id_s, ks > 0);
 					}
+					mma_commit_elect(smem_u32(&s_full[tt & 1]));
+					mma_commit_elect(smem_u32(&k_empty[s]));
 				}
-				t += J;
+				if (j >= 1) {                      // O_t-1 part = P_t-1 V_t-1
+					const int tp = t + j - 1, b = tp & 1, s = tp % kFwdSlots;
+					if (!warp_wait(smem_u32(&p_full[b]), (tp >> 1) & 1, p.err, abort_flag) ||
+							(tp >= 2 && !warp_wait(smem_u32(&pv_empty[b]), ((tp >> 1) - 1) & 1, p.err,
+								abort_flag)) ||
+							!warp_wait(smem_u32(&v_full[s]), (tp / kFwdSlots) & 1, p.err, abort_flag)) {
+						ok = false;
+						break;
+					}
+					tc_fence_after();
+					const uint64_t vd = smem_desc_mn_sw128b32(smem_u32(smem + kFwdVBase + s * kFwdSlotBytes), kFwdKeys * 128);
+					const uint32_t d = tmem + kFColPV + b * 64, pc = tmem + kFColS + b * 128;
+#pragma unroll
+					for (int ks = 0; ks < kFwdKeys / 8; ++ks)
+						mma_step<kSplit>(d, pc + ks * 8, pc + 64 + ks * 8, desc_at(vd, ks * 1024),
+							desc_at(vd, kFwdOpBytes + ks * 1024), id_pv, ks > 0);
+					mma_commit_elect(smem_u32(&pv_full[b]));
+					mma_commit_elect(smem_u32(&v_empty[s]));
+				}
 			}
-			// every issued MMA has completed before tensor memory is released
-			mma_commit(smem_u32(&drain));
-			drain_wait(smem_u32(&drain), 0, p.err);
+			t += J;
 		}
+		// every issued MMA has completed before tensor memory is released
+		mma_commit_elect(smem_u32(&drain));
+		drain_wait(smem_u32(&drain), 0, p.err);
 	} else {
 		// ------------- softmax: two threads per query row, 32 key columns each -------------
 		const int quad = warp & 3, half = (warp - 2) >> 2;
@@ -536,17 +559,18 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 				const bool general =
 					padn || (p.causal && j * kFwdKeys + kFwdKeys - 1 > q0) || (j * kFwdKeys + kFwdKeys > p.Tk);
 				float mt = -INFINITY;
+				uint32_t live = 0xffffffffu, padb = 0u;
 				if (!general) {
 #pragma unroll
 					for (int c = 0; c < 32; ++c) mt = fmaxf(mt, sv[c]);
 					mt = mt * p.scale;                 // scale > 0: the max of the scaled scores
 				} else {
+					live = live_bits32(key0, qrow, p.Tk, p.causal);
+					padb = padded_bits32(padn, key0, live);
 #pragma unroll
 					for (int c = 0; c < 32; ++c) {
-						const int key = key0 + c;
-						const bool live = key < p.Tk && (!p.causal || key <= qrow);
-						const bool padded = padn && live && padn[key] == 0.0f;
-						mt = fmaxf(mt, !live ? -INFINITY : padded ? -1e9f : sv[c] * p.scale);
+						const bool lv = (live >> c) & 1u, pd = (padb >> c) & 1u;
+						mt = fmaxf(mt, !lv ? -INFINITY : pd ? -1e9f : sv[c] * p.scale);
 					}
 				}
 				float mo;
@@ -568,12 +592,10 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 				} else {
 #pragma unroll
 					for (int c = 0; c < 32; ++c) {
-						const int key = key0 + c;
-						const bool live = key < p.Tk && (!p.causal || key <= qrow);
-						const bool padded = padn && live && padn[key] == 0.0f;
+						const bool lv = (live >> c) & 1u, pd = (padb >> c) & 1u;
 						// a padded key's exponent is formed from -1e9 - m, exact when the whole row is padded
-						const float e = !live ? 0.0f
-							: exp2_hw(padded ? (-1e9f - m_new) * kLog2e : __fmaf_rn(sv[c], c1, -mlog));
+						const float e = !lv ? 0.0f
+							: exp2_hw(pd ? (-1e9f - m_new) * kLog2e : __fmaf_rn(sv[c], c1, -mlog));
 						sv[c] = e;
 						sum += e;
 					}
@@ -734,57 +756,53 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 				drain_wait(smem_u32(&kv_full[tt % kDqStages]), (tt / kDqStages) & 1, p.err);
 		}
 	} else if (warp == 1) {
-		if (lane == 0) {
-			const uint32_t id_s = idesc_tf32(kFwdRows, kFwdKeys);
-			const uint32_t id_dq = idesc_tf32(kFwdRows, kDh) | kIdescBMajorMN;
-			int t = 0, i = 0;
-			bool ok = true;
-			for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
-				int q0, nh, J;
-				dq_item(p, w, q0, nh, J);
-				if (!mbar_wait(smem_u32(&q_ready), i & 1, p.err, kDevTimeoutAttn, abort_flag)) break;
-				tc_fence_after();
-				for (int j = 0; j < J; ++j) {
-					const int tt = t + j, s = tt % kDqStages;
-					if (!mbar_wait(smem_u32(&kv_full[s]), (tt / kDqStages) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
-						ok = false;
-						break;
-					}
-					tc_fence_after();
-					const uint32_t kbase = smem_u32(smem + s * kDqStageBytes);
-					const uint64_t kd = smem_desc_k_sw64(kbase), vd = smem_desc_k_sw64(kbase + 2 * kFwdOpBytes);
-					const uint64_t kmd = smem_desc_mn_sw128b32(kbase + 4 * kFwdOpBytes, kFwdKeys * 128);
-#pragma unroll
-					for (int ks = 0; ks < kDh / 8; ++ks) {      // S = Q K^T
-						const uint32_t off = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
-						mma_step<kSplit>(tmem + kQColS, tmem + kQColQhi + ks * 8, tmem + kQColQlo + ks * 8, desc_at(kd, off),
-							desc_at(kd, kFwdOpBytes + off), id_s, ks > 0);
-					}
-#pragma unroll
-					for (int ks = 0; ks < kDh / 8; ++ks) {      // dP = dO V^T
-						const uint32_t off = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
-						mma_step<kSplit>(tmem + kQColP, tmem + kQColOhi + ks * 8, tmem + kQColOlo + ks * 8, desc_at(vd, off),
-							desc_at(vd, kFwdOpBytes + off), id_s, ks > 0);
-					}
-					mma_commit(smem_u32(&sdp_full));
-					if (!mbar_wait(smem_u32(&ds_full), tt & 1, p.err, kDevTimeoutAttn, abort_flag)) {
-						ok = false;
-						break;
-					}
-					tc_fence_after();
-#pragma unroll
-					for (int ks = 0; ks < kFwdKeys / 8; ++ks)   // dQ += dS K
-						mma_step<kSplit>(tmem + kQColAcc, tmem + kQColS + ks * 8, tmem + kQColSlo + ks * 8,
-							desc_at(kmd, ks * 1024), desc_at(kmd, kFwdOpBytes + ks * 1024), id_dq, (j > 0 || ks > 0));
-					mma_commit(smem_u32(&kv_empty[s]));
+		const uint32_t id_s = idesc_tf32(kFwdRows, kFwdKeys);
+		const uint32_t id_dq = idesc_tf32(kFwdRows, kDh) | kIdescBMajorMN;
+		int t = 0, i = 0;
+		bool ok = true;
+		for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
+			int q0, nh, J;
+			dq_item(p, w, q0, nh, J);
+			if (!warp_wait(smem_u32(&q_ready), i & 1, p.err, abort_flag)) break;
+			tc_fence_after();
+			for (int j = 0; j < J; ++j) {
+				const int tt = t + j, s = tt % kDqStages;
+				if (!warp_wait(smem_u32(&kv_full[s]), (tt / kDqStages) & 1, p.err, abort_flag)) {
+					ok = false;
+					break;
 				}
-				if (!ok) break;
-				mma_commit(smem_u32(&acc_full));
-				t += J;
+				tc_fence_after();
+				const uint32_t kbase = smem_u32(smem + s * kDqStageBytes);
+				const uint64_t kd = smem_desc_k_sw64(kbase), vd = smem_desc_k_sw64(kbase + 2 * kFwdOpBytes);
+				const uint64_t kmd = smem_desc_mn_sw128b32(kbase + 4 * kFwdOpBytes, kFwdKeys * 128);
+				// S = Q K^T and dP = dO V^T, their depth steps interleaved: two independent accumulator
+				// chains keep the tensor pipe busy while one step's result feeds the next of its chain
+#pragma unroll
+				for (int ks = 0; ks < kDh / 8; ++ks) {
+					const uint32_t off = (ks >> 1) * (kFwdKeys * 64) + (ks & 1) * 32;
+					mma_step<kSplit>(tmem + kQColS, tmem + kQColQhi + ks * 8, tmem + kQColQlo + ks * 8, desc_at(kd, off),
+						desc_at(kd, kFwdOpBytes + off), id_s, ks > 0);
+					mma_step<kSplit>(tmem + kQColP, tmem + kQColOhi + ks * 8, tmem + kQColOlo + ks * 8, desc_at(vd, off),
+						desc_at(vd, kFwdOpBytes + off), id_s, ks > 0);
+				}
+				mma_commit_elect(smem_u32(&sdp_full));
+				if (!warp_wait(smem_u32(&ds_full), tt & 1, p.err, abort_flag)) {
+					ok = false;
+					break;
+				}
+				tc_fence_after();
+#pragma unroll
+				for (int ks = 0; ks < kFwdKeys / 8; ++ks)   // dQ += dS K
+					mma_step<kSplit>(tmem + kQColAcc, tmem + kQColS + ks * 8, tmem + kQColSlo + ks * 8,
+						desc_at(kmd, ks * 1024), desc_at(kmd, kFwdOpBytes + ks * 1024), id_dq, (j > 0 || ks > 0));
+				mma_commit_elect(smem_u32(&kv_empty[s]));
 			}
-			mma_commit(smem_u32(&drain));
-			drain_wait(smem_u32(&drain), 0, p.err);
+			if (!ok) break;
+			mma_commit_elect(smem_u32(&acc_full));
+			t += J;
 		}
+		mma_commit_elect(smem_u32(&drain));
+		drain_wait(smem_u32(&drain), 0, p.err);
 	} else {
 		// ------------- score gradients: two threads per query row, 32 key columns each -------------
 		const int quad = warp & 3, half = (warp - 2) >> 2;
@@ -854,13 +872,12 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 						ds[c] = p.scale * (pr * (__uint_as_float(rp[c]) - drow));
 					}
 				} else {
+					const uint32_t live = row_ok ? live_bits32(key0, qrow, p.Tk, p.causal) : 0u;
+					const uint32_t use = live & ~padded_bits32(padn, key0, live);
 #pragma unroll
 					for (int c = 0; c < 32; ++c) {
-						const int key = key0 + c;
-						const bool live = row_ok && key < p.Tk && (!p.causal || key <= qrow);
-						const bool padded = padn && live && padn[key] == 0.0f;
 						const float pr = exp2_hw(__fmaf_rn(__uint_as_float(rsv[c]), c1, -mlog)) * inv_l;
-						ds[c] = (live && !padded) ? p.scale * (pr * (__uint_as_float(rp[c]) - drow)) : 0.0f;
+						ds[c] = ((use >> c) & 1u) ? p.scale * (pr * (__uint_as_float(rp[c]) - drow)) : 0.0f;
 					}
 				}
 				vals_to_tmem(ds, lb + kQColS + half * 32, lb + kQColSlo + half * 32);
@@ -969,64 +986,59 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 				drain_wait(smem_u32(&q_full[tt % kKvStages]), (tt / kKvStages) & 1, p.err);
 		}
 	} else if (warp == 1) {
-		if (lane == 0) {
-			const uint32_t id_s = idesc_tf32(kKvRows, kKvQ);
-			const uint32_t id_acc = idesc_tf32(kKvRows, kDh) | kIdescBMajorMN;
-			int t = 0, i = 0;
-			bool ok = true;
-			for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
-				int k0, nh, qt_begin, J;
-				kv_item(p, w, k0, nh, qt_begin, J);
-				if (!mbar_wait(smem_u32(&kv_ready), i & 1, p.err, kDevTimeoutAttn, abort_flag)) break;
-				tc_fence_after();
-				for (int j = 0; j < J; ++j) {
-					const int tt = t + j, s = tt % kKvStages;
-					if (!mbar_wait(smem_u32(&q_full[s]), (tt / kKvStages) & 1, p.err, kDevTimeoutAttn, abort_flag)) {
-						ok = false;
-						break;
-					}
-					tc_fence_after();
-					const uint32_t qbase = smem_u32(smem + s * kKvStageBytes);
-					const uint64_t qd = smem_desc_k_sw64(qbase), od = smem_desc_k_sw64(qbase + 2 * kKvOpBytes);
-					const uint64_t qmd = smem_desc_mn_sw128b32(qbase + 4 * kKvOpBytes, kKvQ * 128);
-					const uint64_t omd = smem_desc_mn_sw128b32(qbase + 6 * kKvOpBytes, kKvQ * 128);
-#pragma unroll
-					for (int ks = 0; ks < kDh / 8; ++ks) {      // S^T = K Q^T
-						const uint32_t off = (ks >> 1) * (kKvQ * 64) + (ks & 1) * 32;
-						mma_step<kSplit>(tmem + kKColS, tmem + kKColKhi + ks * 8, tmem + kKColKlo + ks * 8, desc_at(qd, off),
-							desc_at(qd, kKvOpBytes + off), id_s, ks > 0);
-					}
-#pragma unroll
-					for (int ks = 0; ks < kDh / 8; ++ks) {      // dP^T = V dO^T
-						const uint32_t off = (ks >> 1) * (kKvQ * 64) + (ks & 1) * 32;
-						mma_step<kSplit>(tmem + kKColP, tmem + kKColVhi + ks * 8, tmem + kKColVlo + ks * 8, desc_at(od, off),
-							desc_at(od, kKvOpBytes + off), id_s, ks > 0);
-					}
-					mma_commit(smem_u32(&sdp_full));
-					if (!mbar_wait(smem_u32(&pds_full), tt & 1, p.err, kDevTimeoutAttn, abort_flag)) {
-						ok = false;
-						break;
-					}
-					tc_fence_after();
-#pragma unroll
-					for (int ks = 0; ks < kKvQ / 8; ++ks) {
-						const uint32_t acc = (j > 0 || ks > 0);
-						// dV += P^T dO
-						mma_step<kSplit>(tmem + kKColDv, tmem + kKColS + ks * 8, tmem + kKColSlo + ks * 8, desc_at(omd, ks * 1024),
-							desc_at(omd, kKvOpBytes + ks * 1024), id_acc, acc);
-						// dK += dS^T Q
-						mma_step<kSplit>(tmem + kKColDk, tmem + kKColP + ks * 8, tmem + kKColPlo + ks * 8, desc_at(qmd, ks * 1024),
-							desc_at(qmd, kKvOpBytes + ks * 1024), id_acc, acc);
-					}
-					mma_commit(smem_u32(&q_empty[s]));
+		const uint32_t id_s = idesc_tf32(kKvRows, kKvQ);
+		const uint32_t id_acc = idesc_tf32(kKvRows, kDh) | kIdescBMajorMN;
+		int t = 0, i = 0;
+		bool ok = true;
+		for (int w = blockIdx.x; ok && w < W; w += gridDim.x, ++i) {
+			int k0, nh, qt_begin, J;
+			kv_item(p, w, k0, nh, qt_begin, J);
+			if (!warp_wait(smem_u32(&kv_ready), i & 1, p.err, abort_flag)) break;
+			tc_fence_after();
+			for (int j = 0; j < J; ++j) {
+				const int tt = t + j, s = tt % kKvStages;
+				if (!warp_wait(smem_u32(&q_full[s]), (tt / kKvStages) & 1, p.err, abort_flag)) {
+					ok = false;
+					break;
 				}
-				if (!ok) break;
-				mma_commit(smem_u32(&acc_full));
-				t += J;
+				tc_fence_after();
+				const uint32_t qbase = smem_u32(smem + s * kKvStageBytes);
+				const uint64_t qd = smem_desc_k_sw64(qbase), od = smem_desc_k_sw64(qbase + 2 * kKvOpBytes);
+				const uint64_t qmd = smem_desc_mn_sw128b32(qbase + 4 * kKvOpBytes, kKvQ * 128);
+				const uint64_t omd = smem_desc_mn_sw128b32(qbase + 6 * kKvOpBytes, kKvQ * 128);
+				// S^T = K Q^T and dP^T = V dO^T, depth steps interleaved (two independent chains)
+#pragma unroll
+				for (int ks = 0; ks < kDh / 8; ++ks) {
+					const uint32_t off = (ks >> 1) * (kKvQ * 64) + (ks & 1) * 32;
+					mma_step<kSplit>(tmem + kKColS, tmem + kKColKhi + ks * 8, tmem + kKColKlo + ks * 8, desc_at(qd, off),
+						desc_at(qd, kKvOpBytes + off), id_s, ks > 0);
+					mma_step<kSplit>(tmem + kKColP, tmem + kKColVhi + ks * 8, tmem + kKColVlo + ks * 8, desc_at(od, off),
+						desc_at(od, kKvOpBytes + off), id_s, ks > 0);
+				}
+				mma_commit_elect(smem_u32(&sdp_full));
+				if (!warp_wait(smem_u32(&pds_full), tt & 1, p.err, abort_flag)) {
+					ok = false;
+					break;
+				}
+				tc_fence_after();
+#pragma unroll
+				for (int ks = 0; ks < kKvQ / 8; ++ks) {
+					const uint32_t acc = (j > 0 || ks > 0);
+					// dV += P^T dO
+					mma_step<kSplit>(tmem + kKColDv, tmem + kKColS + ks * 8, tmem + kKColSlo + ks * 8, desc_at(omd, ks * 1024),
+						desc_at(omd, kKvOpBytes + ks * 1024), id_acc, acc);
+					// dK += dS^T Q
+					mma_step<kSplit>(tmem + kKColDk, tmem + kKColP + ks * 8, tmem + kKColPlo + ks * 8, desc_at(qmd, ks * 1024),
+						desc_at(qmd, kKvOpBytes + ks * 1024), id_acc, acc);
+				}
+				mma_commit_elect(smem_u32(&q_empty[s]));
 			}
-			mma_commit(smem_u32(&drain));
-			drain_wait(smem_u32(&drain), 0, p.err);
+			if (!ok) break;
+			mma_commit_elect(smem_u32(&acc_full));
+			t += J;
 		}
+		mma_commit_elect(smem_u32(&drain));
+		drain_wait(smem_u32(&drain), 0, p.err);
 	} else {
 		// ------------- P^T and dS^T: two threads per key row, 16 query columns each -------------
 		const int quad = warp & 3, half = (warp - 2) >> 2;
