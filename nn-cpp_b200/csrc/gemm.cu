@@ -43,13 +43,19 @@ constexpr int kSmemBudget = 200 * 1024;  // dynamic shared memory for the stage 
 __host__ __device__ constexpr int b_panel_rows(int bn) { return bn % 128 == 0 ? 128 : bn; }
 __host__ __device__ constexpr int tmem_cols_pow2(int cols) { return cols <= 32 ? 32 : 2 * tmem_cols_pow2((cols + 1) / 2); }
 
-template <int kSplit, int kBN>
+// 16-deep k-blocks per pipeline stage. A TF32-mode k-block carries two MMAs, against six in 3xTF32,
+// so its stages take two k-blocks: each full / empty barrier round trip then covers four MMAs. (The
+// gathered-operand path keeps one: its gather warps fill a stage per k-block.)
+__host__ __device__ constexpr int kblocks_per_stage(int split, int gather) { return (!split && !gather) ? 2 : 1; }
+
+template <int kSplit, int kBN, int kKPS = 1>
 struct Cfg {
 	static constexpr int S = kSplit ? 2 : 1;                 // hi[, lo]
 	static constexpr int kABytes = S * kBM * kBK * 4;
 	static constexpr int kBPartBytes = kBN * kBK * 4;        // one part (hi or lo) of the B tile
 	static constexpr int kBBytes = S * kBPartBytes;
-	static constexpr int kStageBytes = kABytes + kBBytes;
+	static constexpr int kKBlockBytes = kABytes + kBBytes;   // one k-block: A parts, then B parts
+	static constexpr int kStageBytes = kKPS * kKBlockBytes;
 	static constexpr int kStagesRaw = kSmemBudget / kStageBytes;
 	static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
 	static constexpr int kEpiBytes = 4 * 32 * 32 * 4;        // one 32 x 32 staging tile per epilogue warp
@@ -482,7 +488,8 @@ __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, i
 template <int kSplit, int kBN, int kGather>
 __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
 		const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ Params p) {
-	using C = Cfg<kSplit, kBN>;
+	constexpr int kKPS = kblocks_per_stage(kSplit, kGather);
+	using C = Cfg<kSplit, kBN, kKPS>;
 	constexpr int S = C::S;
 	constexpr int kStages = C::kStages;
 	extern __shared__ uint8_t smem_raw[];
@@ -530,26 +537,32 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 				tile_coords(t, p, bi, mt, nt);
 				const int ab = p.a_batched ? bi : 0, bb = p.b_batched ? bi : 0;
 				bool ok = true;
-				for (int kb = 0; kb < p.KB; ++kb) {
+				for (int kb0 = 0; kb0 < p.KB; kb0 += kKPS) {
 					if (!mbar_wait(smem_u32(&empty_bar[stage]), phase ^ 1, p.err, kDevTimeoutEmpty, abort_flag)) {
 						ok = false;
 						break;
 					}
+					const int nkb = min(kKPS, p.KB - kb0);
 					const uint32_t fb = smem_u32(&full_bar[stage]);
-					mbar_arrive_expect_tx(fb, kGather ? C::kABytes : C::kStageBytes);
-					const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
-					const int ya = (int)((((long long)ab * a_panels + mt) * p.KB + kb) * S * kAPanelRows);
+					mbar_arrive_expect_tx(fb, kGather ? C::kABytes : nkb * C::kKBlockBytes);
 #pragma unroll
-					for (int s = 0; s < S; ++s)
-						tma_load_2d(base + s * (kAPanelRows * kBK * 4), &tm_a, fb, 0, ya + s * kAPanelRows);
-#pragma unroll
-					for (int q = 0; q < (kGather ? 0 : C::kBPanels); ++q) {
-						const long long panel = (long long)bb * b_panels + (long long)nt * C::kBPanels + q;
-						const int yb = (int)((panel * p.KB + kb) * S * C::kBPanelRows);
+					for (int g = 0; g < kKPS; ++g) {
+						if (g >= nkb) break;
+						const int kb = kb0 + g;
+						const uint32_t base = smem_u32(smem + stage * C::kStageBytes + g * C::kKBlockBytes);
+						const int ya = (int)((((long long)ab * a_panels + mt) * p.KB + kb) * S * kAPanelRows);
 #pragma unroll
 						for (int s = 0; s < S; ++s)
-							tma_load_2d(base + C::kABytes + s * C::kBPartBytes + q * (C::kBPanelRows * kBK * 4), &tm_b,
-								fb, 0, yb + s * C::kBPanelRows);
+							tma_load_2d(base + s * (kAPanelRows * kBK * 4), &tm_a, fb, 0, ya + s * kAPanelRows);
+#pragma unroll
+						for (int q = 0; q < (kGather ? 0 : C::kBPanels); ++q) {
+							const long long panel = (long long)bb * b_panels + (long long)nt * C::kBPanels + q;
+							const int yb = (int)((panel * p.KB + kb) * S * C::kBPanelRows);
+#pragma unroll
+							for (int s = 0; s < S; ++s)
+								tma_load_2d(base + C::kABytes + s * C::kBPartBytes + q * (C::kBPanelRows * kBK * 4), &tm_b,
+									fb, 0, yb + s * C::kBPanelRows);
+						}
 					}
 					if (++stage == kStages) {
 						stage = 0;
@@ -572,27 +585,32 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 			tc_fence_after();
 			const uint32_t d_tmem = tmem_base + buf * kBN;
 			bool ok = true;
-			for (int kb = 0; kb < p.KB; ++kb) {
+			for (int kb0 = 0; kb0 < p.KB; kb0 += kKPS) {
 				if (!mbar_wait_warp(smem_u32(&full_bar[stage]), phase, p.err, kDevTimeoutFull, abort_flag)) {
 					ok = false;
 					break;
 				}
 				tc_fence_after();
-				const uint32_t base = smem_u32(smem + stage * C::kStageBytes);
 #pragma unroll
-				for (int kk = 0; kk < kBK / 8; ++kk) {
-					const uint32_t off = kk * 32;    // 8 tf32 = 32 bytes along the swizzled row
-					const uint64_t a_hi = smem_desc_k_sw64(base + off);
-					const uint64_t b_hi = smem_desc_k_sw64(base + C::kABytes + off);
-					const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-					if (kSplit) {
-						const uint64_t a_lo = smem_desc_k_sw64(base + kAPanelRows * kBK * 4 + off);
-						const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
-						mma_tf32_elect(d_tmem, a_lo, b_hi, idesc, first);
-						mma_tf32_elect(d_tmem, a_hi, b_lo, idesc, 1u);
-						mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, 1u);
-					} else {
-						mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, first);
+				for (int g = 0; g < kKPS; ++g) {
+					const int kb = kb0 + g;
+					if (kb >= p.KB) break;
+					const uint32_t base = smem_u32(smem + stage * C::kStageBytes + g * C::kKBlockBytes);
+#pragma unroll
+					for (int kk = 0; kk < kBK / 8; ++kk) {
+						const uint32_t off = kk * 32;    // 8 tf32 = 32 bytes along the swizzled row
+						const uint64_t a_hi = smem_desc_k_sw64(base + off);
+						const uint64_t b_hi = smem_desc_k_sw64(base + C::kABytes + off);
+						const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
+						if (kSplit) {
+							const uint64_t a_lo = smem_desc_k_sw64(base + kAPanelRows * kBK * 4 + off);
+							const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
+							mma_tf32_elect(d_tmem, a_lo, b_hi, idesc, first);
+							mma_tf32_elect(d_tmem, a_hi, b_lo, idesc, 1u);
+							mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, 1u);
+						} else {
+							mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, first);
+						}
 					}
 				}
 				mma_commit_elect(smem_u32(&empty_bar[stage]));
@@ -885,7 +903,7 @@ static nnb_status set_smem_attr(int dev) {
 	std::lock_guard<std::mutex> lock(g_attr_mutex);
 	if (g_attr_set[dev & 63][kSplit][bi][kGather]) return NNB_OK;
 	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN, kGather>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-		Cfg<kSplit, kBN>::kSmemBytes));
+		Cfg<kSplit, kBN, kblocks_per_stage(kSplit, kGather)>::kSmemBytes));
 	g_attr_set[dev & 63][kSplit][bi][kGather] = true;
 	return NNB_OK;
 }
@@ -957,7 +975,7 @@ static void launch_pack(cudaStream_t s, const float* X, long long ldx, long long
 template <int kSplit, int kBN, int kGather = 0>
 static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
-	using Cf = Cfg<kSplit, kBN>;
+	using Cf = Cfg<kSplit, kBN, kblocks_per_stage(kSplit, kGather)>;   // the kernel's own stage layout
 	const bool pre_b = d.packed_b != nullptr;
 	float* pa = reinterpret_cast<float*>(ws);
 	int* flags_a = reinterpret_cast<int*>(ws + pl.off_f);

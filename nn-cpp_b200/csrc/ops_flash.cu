@@ -110,6 +110,86 @@ __device__ __forceinline__ void half_row_to_tmem(const float* src, bool valid, u
 	tmem_st_32x32b_x32(taddr_lo, lo);
 }
 
+// Row transfers between global memory and the math threads, which hold one row per lane (the tensor-
+// memory lane layout). A thread reading or writing its own row's 128 bytes makes every load or store
+// instruction touch 32 rows. These helpers move a warp's 32 rows x 16 floats through a 2 KB shared-memory
+// tile of that warp instead, so that each global instruction covers 8 rows x 64 contiguous bytes. In the
+// tile, 16-byte unit u of row r sits at u ^ ((r >> 1) & 3): conflict-free for both access patterns. The
+// forward uses them for Q and O (2 % faster at the config-5 shape); in the backward kernels, whose
+// item boundaries load two operands, the extra dependent rounds cost more than the coalescing saved.
+constexpr int kRowTileFloats = 32 * 16;
+constexpr uint32_t kRowTileBytes = kMathWarps * kRowTileFloats * 4;    // one tile per math warp
+
+__device__ __forceinline__ int row_tile_at(int r, int u) { return r * 4 + (u ^ ((r >> 1) & 3)); }
+
+// Row `lane` of 32 rows (row r at base + r * ld, rows >= nvalid read as zeros), 16 floats, into v.
+__device__ __forceinline__ void warp_rows_in16(const float* base, long long ld, int nvalid, float4* tile, int lane,
+		float4 (&v)[4]) {
+	const int u = lane & 3;
+	float4 x[4];
+#pragma unroll
+	for (int k = 0; k < 4; ++k) {
+		const int r = 8 * k + (lane >> 2);
+		x[k] = r < nvalid ? __ldg(reinterpret_cast<const float4*>(base + r * ld) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+	}
+#pragma unroll
+	for (int k = 0; k < 4; ++k) tile[row_tile_at(8 * k + (lane >> 2), u)] = x[k];
+	__syncwarp();
+#pragma unroll
+	for (int w = 0; w < 4; ++w) v[w] = tile[row_tile_at(lane, w)];
+	__syncwarp();
+}
+
+// The inverse: row `lane`'s 16 values v go to base + lane * ld (rows >= nvalid are not written), stored
+// as they are or, with accumulate, added to what is there (c + v).
+__device__ __forceinline__ void warp_rows_out16(float* base, long long ld, int nvalid, float4* tile, int lane,
+		const float4 (&v)[4], int accumulate) {
+#pragma unroll
+	for (int w = 0; w < 4; ++w) tile[row_tile_at(lane, w)] = v[w];
+	__syncwarp();
+	const int u = lane & 3;
+#pragma unroll
+	for (int k = 0; k < 4; ++k) {
+		const int r = 8 * k + (lane >> 2);
+		if (r < nvalid) {
+			float4 x = tile[row_tile_at(r, u)];
+			float4* d = reinterpret_cast<float4*>(base + r * ld) + u;
+			if (accumulate) {
+				const float4 c = *d;
+				x.x = c.x + x.x; x.y = c.y + x.y; x.z = c.z + x.z; x.w = c.w + x.w;
+			}
+			*d = x;
+		}
+	}
+	__syncwarp();
+}
+
+// 32 columns of the warp's 32 rows (as warp_rows_in16) split into TF32 hi / lo and stored to 32
+// tensor-memory columns each at taddr_hi / taddr_lo of the warp's lanes.
+__device__ __forceinline__ void warp_rows_to_tmem32(const float* base, long long ld, int nvalid, float4* tile, int lane,
+		uint32_t taddr_hi, uint32_t taddr_lo) {
+#pragma unroll
+	for (int g = 0; g < 2; ++g) {
+		float4 v[4];
+		warp_rows_in16(base + 16 * g, ld, nvalid, tile, lane, v);
+		uint32_t hi[16], lo[16];
+#pragma unroll
+		for (int w = 0; w < 4; ++w) {
+			float4 h, l;
+			split4(v[w], h, l);
+			hi[4 * w] = __float_as_uint(h.x); hi[4 * w + 1] = __float_as_uint(h.y);
+			hi[4 * w + 2] = __float_as_uint(h.z); hi[4 * w + 3] = __float_as_uint(h.w);
+			lo[4 * w] = __float_as_uint(l.x); lo[4 * w + 1] = __float_as_uint(l.y);
+			lo[4 * w + 2] = __float_as_uint(l.z); lo[4 * w + 3] = __float_as_uint(l.w);
+		}
+		tmem_st_32x32b_x16(taddr_hi + 16 * g, hi);
+		tmem_st_32x32b_x16(taddr_lo + 16 * g, lo);
+	}
+}
+
+// Rows of the warp: how many of the 32 rows starting at index r0 lie below T.
+__device__ __forceinline__ int rows_valid(int r0, int T) { return max(0, min(32, T - r0)); }
+
 __device__ __forceinline__ void prefetch_l2(const void* p) {
 	asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
 }
@@ -330,7 +410,8 @@ constexpr uint32_t kFwdOpBytes = kPanels * kFwdKeys * 64;   // 16 KB: one of K h
 constexpr int kFwdSlots = 3;
 constexpr uint32_t kFwdSlotBytes = 2 * kFwdOpBytes;         // hi, lo
 constexpr uint32_t kFwdVBase = kFwdSlots * kFwdSlotBytes;
-constexpr uint32_t kFwdSmem = 2 * kFwdSlots * kFwdSlotBytes + 1024;
+constexpr uint32_t kFwdRowTile = 2 * kFwdSlots * kFwdSlotBytes;      // the math warps' row tiles
+constexpr uint32_t kFwdSmem = kFwdRowTile + kRowTileBytes + 1024;
 // tensor-memory columns: Q hi | Q lo | S/P-hi b, P-lo b (b = 0, 1; 128 columns per buffer) | PV 0 | PV 1
 constexpr uint32_t kFColQhi = 0, kFColQlo = 64, kFColS = 128, kFColPV = 384;
 
@@ -498,10 +579,14 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			++xuse;
 			return r;
 		};
+		float4* const rtile = reinterpret_cast<float4*>(smem + kFwdRowTile) + (warp - 2) * (kRowTileFloats / 4);
 		// Q of item w into tensor memory (zeros past Tq), then the MMA warp may issue its scores
 		auto load_q = [&](int w) {
-			const float* src = fwd_q_row(p, w, row, half);
-			half_row_to_tmem(src, src != nullptr, lb + kFColQhi + half * 32, lb + kFColQlo + half * 32);
+			int q0w, nhw, Jw;
+			fwd_item(p, w, q0w, nhw, Jw);
+			const int r0 = q0w + quad * 32;
+			warp_rows_to_tmem32(p.q + ((long long)(nhw / p.H) * p.Tq + r0) * p.D + (nhw % p.H) * kDh + half * 32, p.D,
+				rows_valid(r0, p.Tq), rtile, lane, lb + kFColQhi + half * 32, lb + kFColQlo + half * 32);
 			tmem_wait_st();
 			tc_fence_before();
 			mbar_arrive(smem_u32(&q_ready));
@@ -618,14 +703,22 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			if (ok) ok = fold(t + J - 1);
 			float l_other = 0.0f;
 			if (ok) ok = swap(l, l_other);
-			if (ok && row_ok) {
+			if (ok) {
 				const float lt = half == 0 ? l + l_other : l_other + l;
 				const float inv_l = 1.0f / lt;
-				float4* orow = reinterpret_cast<float4*>(p.out + ((long long)n * p.Tq + qrow) * p.D + h * kDh + half * 32);
+				const int r0 = q0 + quad * 32;
+				float* obase = p.out + ((long long)n * p.Tq + r0) * p.D + h * kDh + half * 32;
 #pragma unroll
-				for (int u = 0; u < 8; ++u)
-					orow[u] = make_float4(o[4 * u] * inv_l, o[4 * u + 1] * inv_l, o[4 * u + 2] * inv_l, o[4 * u + 3] * inv_l);
-				if (half == 0) {
+				for (int g = 0; g < 2; ++g) {
+					float4 v[4];
+#pragma unroll
+					for (int w4 = 0; w4 < 4; ++w4) {
+						const float* oc = o + 16 * g + 4 * w4;
+						v[w4] = make_float4(oc[0] * inv_l, oc[1] * inv_l, oc[2] * inv_l, oc[3] * inv_l);
+					}
+					warp_rows_out16(obase + 16 * g, p.D, rows_valid(r0, p.Tq), rtile, lane, v, 0);
+				}
+				if (half == 0 && row_ok) {
 					// m and l are kept apart: with the reference's -1e9 padding scores, m + log(l) would
 					// lose log(l) to rounding for a row whose keys are all padded
 					p.stats[((long long)nh * p.Tq + qrow) * 2] = m;
