@@ -46,12 +46,15 @@ __host__ __device__ constexpr int tmem_cols_pow2(int cols) { return cols <= 32 ?
 // 16-deep k-blocks per pipeline stage. A TF32-mode k-block carries two MMAs, against six in 3xTF32,
 // so its stages take two k-blocks: each full / empty barrier round trip then covers four MMAs. (The
 // gathered-operand path keeps one: its gather warps fill a stage per k-block.)
-__host__ __device__ constexpr int kblocks_per_stage(int split, int gather) { return (!split && !gather) ? 2 : 1; }
+// A 256-row ("wide") tile, TF32 mode only, holds two 128-row A panels per k-block instead (below).
+__host__ __device__ constexpr int kblocks_per_stage(int split, int gather, int wide = 0) {
+	return (!split && !gather && !wide) ? 2 : 1;
+}
 
-template <int kSplit, int kBN, int kKPS = 1>
+template <int kSplit, int kBN, int kKPS = 1, int kAM = 1>
 struct Cfg {
 	static constexpr int S = kSplit ? 2 : 1;                 // hi[, lo]
-	static constexpr int kABytes = S * kBM * kBK * 4;
+	static constexpr int kABytes = kAM * S * kBM * kBK * 4;  // kAM 128-row A panels, each hi[, lo]
 	static constexpr int kBPartBytes = kBN * kBK * 4;        // one part (hi or lo) of the B tile
 	static constexpr int kBBytes = S * kBPartBytes;
 	static constexpr int kKBlockBytes = kABytes + kBBytes;   // one k-block: A parts, then B parts
@@ -268,15 +271,19 @@ __global__ void __launch_bounds__(256) pack_cols_vec_kernel(const float* __restr
 // Main kernel
 // ---------------------------------------------------------------------------------------------
 
+// Work item t -> batch entry, row tile and column tile. A work item is kAM consecutive 128-row tiles
+// (1, or 2 for the wide TF32 tile) of one column tile; mt is its first 128-row tile.
+template <int kAM = 1>
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& bi, int& mt, int& nt) {
-	const int per_batch = p.tiles_m * p.tiles_n;
+	const int tiles_m = p.tiles_m / kAM;
+	const int per_batch = tiles_m * p.tiles_n;
 	bi = t / per_batch;
 	const int r = t - bi * per_batch;
 	const int group = r / (kGroupM * p.tiles_n);
 	const int first_m = group * kGroupM;
-	const int gsz = min(p.tiles_m - first_m, kGroupM);
+	const int gsz = min(tiles_m - first_m, kGroupM);
 	const int in = r - group * kGroupM * p.tiles_n;
-	mt = first_m + in % gsz;
+	mt = (first_m + in % gsz) * kAM;
 	nt = in / gsz;
 }
 
@@ -485,11 +492,18 @@ __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, i
 	return v;
 }
 
-template <int kSplit, int kBN, int kGather>
+// kWide (TF32 mode, no gather, BN = 256): each work item is a 256 x 256 tile, two 128-row halves that
+// share every B stage, one half per TMEM accumulator. Per 16-deep k-block the CTA then loads 32 KB for
+// four 128 x 256 x 8 MMAs instead of 24 KB for two: a third less operand traffic per MMA, and the
+// 192 KB of stages hold 1.5x the tensor time. The cost: no accumulator double buffering (the next
+// tile's MMAs wait for both halves' epilogues). Each element's arithmetic is the narrow kernel's.
+template <int kSplit, int kBN, int kGather, int kWide = 0>
 __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
 		const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ Params p) {
-	constexpr int kKPS = kblocks_per_stage(kSplit, kGather);
-	using C = Cfg<kSplit, kBN, kKPS>;
+	static_assert(!kWide || (!kSplit && !kGather && kBN == 256), "wide tiles: TF32, no gather, 256 columns");
+	constexpr int kAM = kWide ? 2 : 1;
+	constexpr int kKPS = kblocks_per_stage(kSplit, kGather, kWide);
+	using C = Cfg<kSplit, kBN, kKPS, kAM>;
 	constexpr int S = C::S;
 	constexpr int kStages = C::kStages;
 	extern __shared__ uint8_t smem_raw[];
@@ -524,7 +538,7 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 	const uint32_t tmem_base = tmem_base_sh;
 	volatile int* abort_flag = &abort_sh;
 
-	const int num_tiles = p.batch * p.tiles_m * p.tiles_n;
+	const int num_tiles = p.batch * (p.tiles_m / kAM) * p.tiles_n;      // work items
 	const int a_panels = p.Mp / kAPanelRows, b_panels = p.Np / C::kBPanelRows;
 
 	if (warp == 0) {
@@ -534,7 +548,7 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 			uint32_t phase = 0;
 			for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
 				int bi, mt, nt;
-				tile_coords(t, p, bi, mt, nt);
+				tile_coords<kAM>(t, p, bi, mt, nt);
 				const int ab = p.a_batched ? bi : 0, bb = p.b_batched ? bi : 0;
 				bool ok = true;
 				for (int kb0 = 0; kb0 < p.KB; kb0 += kKPS) {
@@ -550,10 +564,13 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 						if (g >= nkb) break;
 						const int kb = kb0 + g;
 						const uint32_t base = smem_u32(smem + stage * C::kStageBytes + g * C::kKBlockBytes);
-						const int ya = (int)((((long long)ab * a_panels + mt) * p.KB + kb) * S * kAPanelRows);
 #pragma unroll
-						for (int s = 0; s < S; ++s)
-							tma_load_2d(base + s * (kAPanelRows * kBK * 4), &tm_a, fb, 0, ya + s * kAPanelRows);
+						for (int h = 0; h < kAM; ++h) {
+							const int ya = (int)((((long long)ab * a_panels + mt + h) * p.KB + kb) * S * kAPanelRows);
+#pragma unroll
+							for (int s = 0; s < S; ++s)
+								tma_load_2d(base + (h * S + s) * (kAPanelRows * kBK * 4), &tm_a, fb, 0, ya + s * kAPanelRows);
+						}
 #pragma unroll
 						for (int q = 0; q < (kGather ? 0 : C::kBPanels); ++q) {
 							const long long panel = (long long)bb * b_panels + (long long)nt * C::kBPanels + q;
@@ -574,17 +591,23 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 		}
 	} else if (warp == 1) {
 		// --------------------- MMA issuer (the whole warp; one elected lane issues) ---------------------
+		// accumulator v (the v-th 128-row tile this CTA hands to the epilogue) lives in buffer v & 1; a
+		// wide work item fills two of them, one per 128-row half
 		constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
 		int stage = 0;
 		uint32_t phase = 0;
 		int it = 0;
-		for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-			const int buf = it & 1;
-			const uint32_t acc_phase = (it >> 1) & 1;
-			if (!mbar_wait_warp(smem_u32(&acce_bar[buf]), acc_phase ^ 1, p.err, kDevTimeoutAccumFree, abort_flag)) break;
-			tc_fence_after();
-			const uint32_t d_tmem = tmem_base + buf * kBN;
+		for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, it += kAM) {
 			bool ok = true;
+#pragma unroll
+			for (int h = 0; h < kAM; ++h) {
+				const int v = it + h;
+				if (ok && !mbar_wait_warp(smem_u32(&acce_bar[v & 1]), ((v >> 1) & 1) ^ 1, p.err, kDevTimeoutAccumFree,
+						abort_flag))
+					ok = false;
+			}
+			if (!ok) break;
+			tc_fence_after();
 			for (int kb0 = 0; kb0 < p.KB; kb0 += kKPS) {
 				if (!mbar_wait_warp(smem_u32(&full_bar[stage]), phase, p.err, kDevTimeoutFull, abort_flag)) {
 					ok = false;
@@ -599,17 +622,22 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 #pragma unroll
 					for (int kk = 0; kk < kBK / 8; ++kk) {
 						const uint32_t off = kk * 32;    // 8 tf32 = 32 bytes along the swizzled row
-						const uint64_t a_hi = smem_desc_k_sw64(base + off);
 						const uint64_t b_hi = smem_desc_k_sw64(base + C::kABytes + off);
 						const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
-						if (kSplit) {
-							const uint64_t a_lo = smem_desc_k_sw64(base + kAPanelRows * kBK * 4 + off);
-							const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
-							mma_tf32_elect(d_tmem, a_lo, b_hi, idesc, first);
-							mma_tf32_elect(d_tmem, a_hi, b_lo, idesc, 1u);
-							mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, 1u);
-						} else {
-							mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, first);
+#pragma unroll
+						for (int h = 0; h < kAM; ++h) {
+							const uint32_t d_tmem = tmem_base + ((it + h) & 1) * kBN;
+							const uint32_t abase = base + h * S * (kAPanelRows * kBK * 4);
+							const uint64_t a_hi = smem_desc_k_sw64(abase + off);
+							if (kSplit) {
+								const uint64_t a_lo = smem_desc_k_sw64(abase + kAPanelRows * kBK * 4 + off);
+								const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
+								mma_tf32_elect(d_tmem, a_lo, b_hi, idesc, first);
+								mma_tf32_elect(d_tmem, a_hi, b_lo, idesc, 1u);
+								mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, 1u);
+							} else {
+								mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, first);
+							}
 						}
 					}
 				}
@@ -620,7 +648,8 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 				}
 			}
 			if (!ok) break;
-			mma_commit_elect(smem_u32(&accf_bar[buf]));
+#pragma unroll
+			for (int h = 0; h < kAM; ++h) mma_commit_elect(smem_u32(&accf_bar[(it + h) & 1]));
 		}
 	} else if (kGather && warp >= kThreads / 32) {
 		// ------------------------- B gatherers (implicit GEMM) -------------------------
@@ -697,14 +726,17 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 		// 32 x 32 staging tile of this warp: element (r, c) at float r*32 + 4*((c/4) ^ (r & 7)) + c%4, so that
 		// both the row-per-lane writes and the 4-rows-per-instruction reads are free of bank conflicts
 		float* stage = reinterpret_cast<float*>(smem + (size_t)kStages * C::kStageBytes) + quad * 1024;
-		int it = 0;
-		for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+		// the it-th 128-row tile of this CTA: half it % kAM of work item blockIdx.x + (it / kAM) * gridDim.x
+		for (int it = 0;; ++it) {
+			const int t = blockIdx.x + (it / kAM) * gridDim.x;
+			if (t >= num_tiles) break;
 			const int buf = it & 1;
 			const uint32_t acc_phase = (it >> 1) & 1;
 			if (!mbar_wait(smem_u32(&accf_bar[buf]), acc_phase, p.err, kDevTimeoutAccum, abort_flag)) break;
 			tc_fence_after();
 			int bi, mt, nt;
-			tile_coords(t, p, bi, mt, nt);
+			tile_coords<kAM>(t, p, bi, mt, nt);
+			mt += it % kAM;
 			const int gm = mt * kBM + row;
 			const bool row_ok = gm < p.M;
 			float* cbase = p.C + batch_offset(bi, p.batch_inner, p.sc_outer, p.sc_inner);
@@ -894,23 +926,27 @@ static int choose_bn(long long m, long long n, long long entries, int sms) {
 	return best;
 }
 
-static bool g_attr_set[64][2][4][2];
+static bool g_attr_set[64][2][4][2][2];
 static std::mutex g_attr_mutex;
 
-template <int kSplit, int kBN, int kGather = 0>
+template <int kSplit, int kBN, int kGather, int kWide>
+using KernelCfg = Cfg<kSplit, kBN, kblocks_per_stage(kSplit, kGather, kWide), kWide ? 2 : 1>;
+
+template <int kSplit, int kBN, int kGather = 0, int kWide = 0>
 static nnb_status set_smem_attr(int dev) {
 	const int bi = kBN == 64 ? 0 : kBN == 128 ? 1 : kBN == 224 ? 3 : 2;
 	std::lock_guard<std::mutex> lock(g_attr_mutex);
-	if (g_attr_set[dev & 63][kSplit][bi][kGather]) return NNB_OK;
-	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN, kGather>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-		Cfg<kSplit, kBN, kblocks_per_stage(kSplit, kGather)>::kSmemBytes));
-	g_attr_set[dev & 63][kSplit][bi][kGather] = true;
+	if (g_attr_set[dev & 63][kSplit][bi][kGather][kWide]) return NNB_OK;
+	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN, kGather, kWide>,
+		cudaFuncAttributeMaxDynamicSharedMemorySize, KernelCfg<kSplit, kBN, kGather, kWide>::kSmemBytes));
+	g_attr_set[dev & 63][kSplit][bi][kGather][kWide] = true;
 	return NNB_OK;
 }
 
 // Scratch layout of one product: packed A, packed B, then the non-finite flags.
 struct Plan {
 	int S, bn, b_panel_rows;
+	int wide;                                 // 256 x 256 TF32 tiles (rows padded to 256)
 	long long Mp, Np, Kp, KB, entries, a_entries, b_entries;
 	long long rows_a, rows_b;                 // packed 16-float rows of each operand
 	size_t off_b, off_f, flag_ints, total;
@@ -921,7 +957,14 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	pl.bn = force_bn ? force_bn : choose_bn(d.m, d.n, d.batch_outer * d.batch_inner, sms > 0 ? sms : 148);
 	if (d.gather.mode != kGatherNone && pl.bn == 224) pl.bn = 256;
 	pl.b_panel_rows = b_panel_rows(pl.bn);
-	pl.Mp = round_up(d.m, kBM);
+	pl.entries = d.batch_outer * d.batch_inner;
+	pl.KB = round_up(d.k, kBK) / kBK;
+	// Wide tiles in TF32 mode when the width was left to the plan, the 256-wide tiles are chosen, the
+	// 256 x 256 work items still fill the SMs and the depth amortises the unoverlapped epilogue
+	pl.wide = (d.mode == NNB_MATH_TF32 && force_bn == 0 && d.gather.mode == kGatherNone && pl.bn == 256 &&
+		pl.KB >= 64 && pl.entries * (round_up(d.m, 2 * kBM) / (2 * kBM)) * (round_up(d.n, 256) / 256) >= (sms > 0 ? sms : 148))
+		? 1 : 0;
+	pl.Mp = round_up(d.m, pl.wide ? 2 * kBM : kBM);
 	pl.Np = round_up(d.n, pl.bn);
 	pl.Kp = round_up(d.k, kBK);
 	pl.KB = pl.Kp / kBK;
@@ -972,10 +1015,10 @@ static void launch_pack(cudaStream_t s, const float* X, long long ldx, long long
 	}
 }
 
-template <int kSplit, int kBN, int kGather = 0>
+template <int kSplit, int kBN, int kGather = 0, int kWide = 0>
 static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
-	using Cf = Cfg<kSplit, kBN, kblocks_per_stage(kSplit, kGather)>;   // the kernel's own stage layout
+	using Cf = KernelCfg<kSplit, kBN, kGather, kWide>;   // the kernel's own stage layout
 	const bool pre_b = d.packed_b != nullptr;
 	float* pa = reinterpret_cast<float*>(ws);
 	int* flags_a = reinterpret_cast<int*>(ws + pl.off_f);
@@ -1034,12 +1077,12 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	p.gflags_b = flags_b;
 	p.gany_b = any_b;
 
-	NNB_TRY((set_smem_attr<kSplit, kBN, kGather>(dev)));
-	const long long tiles = pl.entries * p.tiles_m * p.tiles_n;
+	NNB_TRY((set_smem_attr<kSplit, kBN, kGather, kWide>(dev)));
+	const long long tiles = pl.entries * (p.tiles_m / (kWide ? 2 : 1)) * p.tiles_n;     // work items
 	const int grid = (int)std::min<long long>(tiles, sm_count);
 	{
 		TraceScope ts(s, kGather ? kTraceConv : kTraceGemm, traced);
-		gemm_tc_kernel<kSplit, kBN, kGather><<<grid, threads_for(kGather), Cf::kSmemBytes, s>>>(tma, tmb, p);
+		gemm_tc_kernel<kSplit, kBN, kGather, kWide><<<grid, threads_for(kGather), Cf::kSmemBytes, s>>>(tma, tmb, p);
 	}
 	return cuda_status(cudaGetLastError(), "gemm launch");
 }
@@ -1051,6 +1094,9 @@ static nnb_status dispatch_bn(cudaStream_t s, int dev, int sm_count, int* err, c
 		if (pl.bn == 256) return launch_main<kSplit, 256, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 		if (pl.bn == 128) return launch_main<kSplit, 128, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 		return launch_main<kSplit, 64, 1>(s, dev, sm_count, err, d, pl, ws, traced);
+	}
+	if constexpr (kSplit == 0) {
+		if (pl.wide) return launch_main<0, 256, 0, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 	}
 	if (pl.bn == 256) return launch_main<kSplit, 256>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 224) return launch_main<kSplit, 224>(s, dev, sm_count, err, d, pl, ws, traced);

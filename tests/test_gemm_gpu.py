@@ -230,6 +230,35 @@ def test_tile_width_does_not_change_bits(cuda, mode, tb, n):
     assert nnb.device_error() == 0
 
 
+@pytest.mark.parametrize("ta,tb,m,n,k", [(0, 0, 4096, 4096, 1024), (1, 1, 4000, 4096, 1100), (0, 1, 3000, 4096, 2048)])
+def test_tf32_wide_tiles_same_bits_as_narrow(cuda, ta, tb, m, n, k):
+    """TF32 products with at least 148 256 x 256 work items and a depth of 64+ k-blocks run on the wide
+    tiles (two 128-row halves sharing each B stage); the 2048-row bands they are cut into here have too
+    few such items and run on the 128 x 256 tiles. Each band's rows are the full product's bits, and the
+    full product is within the TF32 bound of the fp64 oracle on sampled elements."""
+    torch = cuda
+    a_h = orc.normal(81, m * k)
+    b_h = orc.normal(82, k * n)
+    a = torch.from_numpy(a_h).cuda()
+    b = torch.from_numpy(b_h).cuda()
+    lda, ldb = (m if ta else k), (k if tb else n)
+    full = torch.zeros(m, n, device="cuda")
+    nnb.sgemm(bool(ta), bool(tb), m, n, k, a, lda, b, ldb, full, n, False, math_mode=nnb.MATH_TF32)
+    for r0 in range(0, m, 2048):
+        rows = min(2048, m - r0)
+        band = torch.zeros(rows, n, device="cuda")
+        a_band = a[r0:] if ta else a[r0 * k:]         # op(A) rows r0.. : columns of a stored k x m
+        nnb.sgemm(bool(ta), bool(tb), rows, n, k, a_band, lda, b, ldb, band, n, False, math_mode=nnb.MATH_TF32)
+        assert band.cpu().numpy().tobytes() == full[r0:r0 + rows].cpu().numpy().tobytes(), r0
+    got = full.cpu().numpy()
+    rows = np.r_[0, m - 1, np.arange(0, m, 251)].repeat(8)
+    cols = np.tile(np.r_[0, n - 1, 255, 256, n // 2, 127, n - 2, 1], len(rows) // 8)
+    val, mag = orc.sgemm_f64_sample(ta, tb, k, a_h, lda, b_h, ldb, None, n, 0, rows, cols)
+    err = np.abs(got[rows, cols] - val)
+    assert np.all(err <= 5e-3 * mag), (err / mag).max()
+    assert nnb.device_error() == 0
+
+
 def test_argument_errors(cuda):
     torch = cuda
     a = torch.zeros(64, device="cuda")
