@@ -500,7 +500,7 @@ __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, i
 template <int kSplit, int kBN, int kGather, int kWide = 0>
 __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
 		const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ Params p) {
-	static_assert(!kWide || (!kSplit && !kGather && kBN == 256), "wide tiles: TF32, no gather, 256 columns");
+	static_assert(!kWide || (!kGather && kBN == 256), "wide tiles: no gather, 256 columns");
 	constexpr int kAM = kWide ? 2 : 1;
 	constexpr int kKPS = kblocks_per_stage(kSplit, kGather, kWide);
 	using C = Cfg<kSplit, kBN, kKPS, kAM>;
@@ -961,7 +961,7 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	pl.KB = round_up(d.k, kBK) / kBK;
 	// Wide tiles in TF32 mode when the width was left to the plan, the 256-wide tiles are chosen, the
 	// 256 x 256 work items still fill the SMs and the depth amortises the unoverlapped epilogue
-	pl.wide = (d.mode == NNB_MATH_TF32 && force_bn == 0 && d.gather.mode == kGatherNone && pl.bn == 256 &&
+	pl.wide = (force_bn == 0 && d.gather.mode == kGatherNone && pl.bn == 256 &&
 		pl.KB >= 64 && pl.entries * (round_up(d.m, 2 * kBM) / (2 * kBM)) * (round_up(d.n, 256) / 256) >= (sms > 0 ? sms : 148))
 		? 1 : 0;
 	pl.Mp = round_up(d.m, pl.wide ? 2 * kBM : kBM);
@@ -1095,9 +1095,7 @@ static nnb_status dispatch_bn(cudaStream_t s, int dev, int sm_count, int* err, c
 		if (pl.bn == 128) return launch_main<kSplit, 128, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 		return launch_main<kSplit, 64, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 	}
-	if constexpr (kSplit == 0) {
-		if (pl.wide) return launch_main<0, 256, 0, 1>(s, dev, sm_count, err, d, pl, ws, traced);
-	}
+	if (pl.wide) return launch_main<kSplit, 256, 0, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 256) return launch_main<kSplit, 256>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 224) return launch_main<kSplit, 224>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 128) return launch_main<kSplit, 128>(s, dev, sm_count, err, d, pl, ws, traced);
