@@ -7,8 +7,8 @@
 // work is split into items -- 128 query rows (or 128 keys) of one (sample, head) -- and a persistent
 // grid of one CTA per SM walks the items, heaviest causal items first, with every barrier phase
 // carried from item to item so that one item's loads and MMAs overlap the previous item's tail.
-//   forward   S = Q K^T (Q and K tiles in shared memory), online softmax in registers (two threads
-//             per query row, 32 keys each), P split into TF32 hi/lo and stored to tensor memory,
+//   forward   S = Q K^T (Q in tensor memory, K tiles in shared memory), online softmax in registers
+//             (four threads per query row, 16 keys each), P split into TF32 hi/lo and stored to tensor memory,
 //             then O += P V (TS MMA: P from tensor memory, V an MN-major B operand). Only O and the
 //             row statistics (max m, sum l of exp(score - m)) are written.
 //   backward  two kernels, each output element written by exactly one CTA (no atomics, fixed order):
@@ -53,11 +53,9 @@ constexpr int kPanels = kDh / 16;             // K-major image: 16-float (64-byt
 constexpr int kBlocks = kDh / 32;             // MN-major image: 32-float (128-byte) blocks
 constexpr int kRowAlign = 128;                // packed rows per (sample, head) are padded to this
 constexpr uint32_t kTmemCols = 512;
-// warp 0 loads, warp 1 issues MMAs, warps 2-9 do the per-element math: two warps per tensor-memory
-// lane quarter (warp w reaches lanes 32 (w % 4) .. +31), each taking half of a row's columns
-constexpr int kMathWarps = 8;
-constexpr int kMathThreads = 32 * kMathWarps;
-constexpr int kThreadsFa = 64 + kMathThreads;
+// Every kernel here: warp 0 loads, warp 1 issues MMAs, warps 2-17 do the per-element math, four warps
+// per tensor-memory lane quarter (warp w reaches lanes 32 (w % 4) .. +31), each taking a quarter of a
+// row's columns (kFwdParts, kDqParts, kKvParts below).
 constexpr float kLog2e = 1.4426950408889634f;   // exp(x) = 2^(x log2 e)
 
 // Floats of one (sample, head) image of Tp rows, either form: hi and lo, 64 floats per row each.
@@ -92,133 +90,12 @@ __device__ __forceinline__ void split4(float4 x, float4& hi, float4& lo) {
 	split_tf32(x.w, hi.w, lo.w);
 }
 
-// Loads 32 consecutive floats of a head row (zeros when !valid), splits them and stores hi to the
-// 32 columns at taddr_hi and lo to those at taddr_lo of this thread's tensor-memory lane.
-__device__ __forceinline__ void half_row_to_tmem(const float* src, bool valid, uint32_t taddr_hi, uint32_t taddr_lo) {
-	uint32_t hi[32], lo[32];
-#pragma unroll
-	for (int u = 0; u < 8; ++u) {
-		float4 x = valid ? __ldg(reinterpret_cast<const float4*>(src) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
-		float4 h, l;
-		split4(x, h, l);
-		hi[4 * u] = __float_as_uint(h.x); hi[4 * u + 1] = __float_as_uint(h.y);
-		hi[4 * u + 2] = __float_as_uint(h.z); hi[4 * u + 3] = __float_as_uint(h.w);
-		lo[4 * u] = __float_as_uint(l.x); lo[4 * u + 1] = __float_as_uint(l.y);
-		lo[4 * u + 2] = __float_as_uint(l.z); lo[4 * u + 3] = __float_as_uint(l.w);
-	}
-	tmem_st_32x32b_x32(taddr_hi, hi);
-	tmem_st_32x32b_x32(taddr_lo, lo);
-}
-
-// Row transfers between global memory and the math threads, which hold one row per lane (the tensor-
-// memory lane layout). A thread reading or writing its own row's 128 bytes makes every load or store
-// instruction touch 32 rows. These helpers move a warp's 32 rows x 16 floats through a 2 KB shared-memory
-// tile of that warp instead, so that each global instruction covers 8 rows x 64 contiguous bytes. In the
-// tile, 16-byte unit u of row r sits at u ^ ((r >> 1) & 3): conflict-free for both access patterns. The
-// forward uses them for Q and O (2 % faster at the config-5 shape); in the backward kernels, whose
-// item boundaries load two operands, the extra dependent rounds cost more than the coalescing saved.
-constexpr int kRowTileFloats = 32 * 16;
-constexpr uint32_t kRowTileBytes = kMathWarps * kRowTileFloats * 4;    // one tile per math warp
-
-__device__ __forceinline__ int row_tile_at(int r, int u) { return r * 4 + (u ^ ((r >> 1) & 3)); }
-
-// Row `lane` of 32 rows (row r at base + r * ld, rows >= nvalid read as zeros), 16 floats, into v.
-__device__ __forceinline__ void warp_rows_in16(const float* base, long long ld, int nvalid, float4* tile, int lane,
-		float4 (&v)[4]) {
-	const int u = lane & 3;
-	float4 x[4];
-#pragma unroll
-	for (int k = 0; k < 4; ++k) {
-		const int r = 8 * k + (lane >> 2);
-		x[k] = r < nvalid ? __ldg(reinterpret_cast<const float4*>(base + r * ld) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
-	}
-#pragma unroll
-	for (int k = 0; k < 4; ++k) tile[row_tile_at(8 * k + (lane >> 2), u)] = x[k];
-	__syncwarp();
-#pragma unroll
-	for (int w = 0; w < 4; ++w) v[w] = tile[row_tile_at(lane, w)];
-	__syncwarp();
-}
-
-// The inverse: row `lane`'s 16 values v go to base + lane * ld (rows >= nvalid are not written), stored
-// as they are or, with accumulate, added to what is there (c + v).
-__device__ __forceinline__ void warp_rows_out16(float* base, long long ld, int nvalid, float4* tile, int lane,
-		const float4 (&v)[4], int accumulate) {
-#pragma unroll
-	for (int w = 0; w < 4; ++w) tile[row_tile_at(lane, w)] = v[w];
-	__syncwarp();
-	const int u = lane & 3;
-#pragma unroll
-	for (int k = 0; k < 4; ++k) {
-		const int r = 8 * k + (lane >> 2);
-		if (r < nvalid) {
-			float4 x = tile[row_tile_at(r, u)];
-			float4* d = reinterpret_cast<float4*>(base + r * ld) + u;
-			if (accumulate) {
-				const float4 c = *d;
-				x.x = c.x + x.x; x.y = c.y + x.y; x.z = c.z + x.z; x.w = c.w + x.w;
-			}
-			*d = x;
-		}
-	}
-	__syncwarp();
-}
-
-// 32 columns of the warp's 32 rows (as warp_rows_in16) split into TF32 hi / lo and stored to 32
-// tensor-memory columns each at taddr_hi / taddr_lo of the warp's lanes.
-__device__ __forceinline__ void warp_rows_to_tmem32(const float* base, long long ld, int nvalid, float4* tile, int lane,
-		uint32_t taddr_hi, uint32_t taddr_lo) {
-#pragma unroll
-	for (int g = 0; g < 2; ++g) {
-		float4 v[4];
-		warp_rows_in16(base + 16 * g, ld, nvalid, tile, lane, v);
-		uint32_t hi[16], lo[16];
-#pragma unroll
-		for (int w = 0; w < 4; ++w) {
-			float4 h, l;
-			split4(v[w], h, l);
-			hi[4 * w] = __float_as_uint(h.x); hi[4 * w + 1] = __float_as_uint(h.y);
-			hi[4 * w + 2] = __float_as_uint(h.z); hi[4 * w + 3] = __float_as_uint(h.w);
-			lo[4 * w] = __float_as_uint(l.x); lo[4 * w + 1] = __float_as_uint(l.y);
-			lo[4 * w + 2] = __float_as_uint(l.z); lo[4 * w + 3] = __float_as_uint(l.w);
-		}
-		tmem_st_32x32b_x16(taddr_hi + 16 * g, hi);
-		tmem_st_32x32b_x16(taddr_lo + 16 * g, lo);
-	}
-}
-
-// Rows of the warp: how many of the 32 rows starting at index r0 lie below T.
-__device__ __forceinline__ int rows_valid(int r0, int T) { return max(0, min(32, T - r0)); }
-
 __device__ __forceinline__ void prefetch_l2(const void* p) {
 	asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
 }
 
-// The two math threads that share a row (one per half) swap a value through shared memory:
-// each writes its own, arrives on the pair's mbarrier (count 64) and waits, bounded, for the phase.
-// Returns false (warp-uniform) when the wait ran out.
-__device__ __forceinline__ bool pair_swap(float* slot_mine, const float* slot_other, float v, float& other,
-		uint32_t bar, uint32_t parity, int* err, volatile int* abort) {
-	*slot_mine = v;
-	mbar_arrive(bar);
-	if (!warp_wait(bar, parity, err, abort)) return false;
-	other = *slot_other;
-	return true;
-}
-
-// Splits 32 (16) finite values well inside the fp32 range and stores hi / lo to two column groups of
-// this thread's lane.
-__device__ __forceinline__ void vals_to_tmem(const float (&v)[32], uint32_t taddr_hi, uint32_t taddr_lo) {
-	uint32_t hi[32], lo[32];
-#pragma unroll
-	for (int c = 0; c < 32; ++c) {
-		const float h = to_tf32(v[c]);
-		hi[c] = __float_as_uint(h);
-		lo[c] = __float_as_uint(to_tf32(v[c] - h));
-	}
-	tmem_st_32x32b_x32(taddr_hi, hi);
-	tmem_st_32x32b_x32(taddr_lo, lo);
-}
+// Splits 16 finite values well inside the fp32 range and stores hi / lo to two column groups of this
+// thread's lane.
 __device__ __forceinline__ void vals_to_tmem16(const float (&v)[16], uint32_t taddr_hi, uint32_t taddr_lo) {
 	uint32_t hi[16], lo[16];
 #pragma unroll
@@ -410,8 +287,7 @@ constexpr uint32_t kFwdOpBytes = kPanels * kFwdKeys * 64;   // 16 KB: one of K h
 constexpr int kFwdSlots = 3;
 constexpr uint32_t kFwdSlotBytes = 2 * kFwdOpBytes;         // hi, lo
 constexpr uint32_t kFwdVBase = kFwdSlots * kFwdSlotBytes;
-constexpr uint32_t kFwdRowTile = 2 * kFwdSlots * kFwdSlotBytes;      // the math warps' row tiles
-constexpr uint32_t kFwdSmem = kFwdRowTile + kRowTileBytes + 1024;
+constexpr uint32_t kFwdSmem = 2 * kFwdSlots * kFwdSlotBytes + 1024;
 // tensor-memory columns: Q hi | Q lo | S/P-hi b, P-lo b (b = 0, 1; 128 columns per buffer) | PV 0 | PV 1
 constexpr uint32_t kFColQhi = 0, kFColQlo = 64, kFColS = 128, kFColPV = 384;
 
@@ -425,22 +301,35 @@ __device__ __forceinline__ void fwd_item(const FwdParams& p, int w, int& q0, int
 	J = (key_end + kFwdKeys - 1) / kFwdKeys;
 }
 
-// This thread's half row of Q for item w (row index `row` of the item), its global address or null.
-__device__ __forceinline__ const float* fwd_q_row(const FwdParams& p, int w, int row, int half) {
-	int q0, nh, J;
-	fwd_item(p, w, q0, nh, J);
-	if (q0 + row >= p.Tq) return nullptr;
-	const int n = nh / p.H, h = nh % p.H;
-	return p.q + ((long long)n * p.Tq + q0 + row) * p.D + h * kDh + half * 32;
+// The forward's softmax is its critical path (about 2400 cycles per 64-key tile with two math warps
+// per lane quarter against about 1400 of MMA issue), so it runs four math warps per lane quarter, each
+// thread a quarter of a row's columns: twice the warps per scheduler to hide the latencies of the same
+// instruction stream.
+constexpr int kFwdParts = 4;                                // math threads per query row
+constexpr int kFwdMathThreads = 32 * 4 * kFwdParts;
+constexpr int kFwdThreads = 64 + kFwdMathThreads;
+constexpr int kFwdCols = kFwdKeys / kFwdParts;             // score columns per math thread
+constexpr int kFwdHeadCols = kDh / kFwdParts;              // output columns per math thread
+
+// The kFwdParts math threads of a row exchange one value each through shared memory (mbarrier
+// count kFwdMathThreads / 4 per lane quarter); returns false (warp-uniform) if the wait ran out.
+__device__ __forceinline__ bool row_exchange(float (*slots)[kFwdRows], int part, int row, float v, float (&all)[kFwdParts],
+		uint32_t bar, uint32_t parity, int* err, volatile int* abort) {
+	slots[part][row] = v;
+	mbar_arrive(bar);
+	if (!warp_wait(bar, parity, err, abort)) return false;
+#pragma unroll
+	for (int q = 0; q < kFwdParts; ++q) all[q] = slots[q][row];
+	return true;
 }
 
 template <int kSplit>
-__global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParams p) {
+__global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdParams p) {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 	__shared__ __align__(8) uint64_t k_full[kFwdSlots], k_empty[kFwdSlots], v_full[kFwdSlots], v_empty[kFwdSlots],
 		s_full[2], p_full[2], pv_full[2], pv_empty[2], q_ready, xbar[4][2], drain;
-	__shared__ float xval[2][2][kFwdRows];          // [exchange parity][half][row]
+	__shared__ float xval[2][kFwdParts][kFwdRows];  // [exchange parity][part][row]
 	__shared__ uint32_t tmem_base_sh;
 	__shared__ int abort_sh;
 
@@ -455,15 +344,15 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 		}
 		for (int b = 0; b < 2; ++b) {
 			mbar_init(smem_u32(&s_full[b]), 1);
-			mbar_init(smem_u32(&p_full[b]), kMathThreads);
+			mbar_init(smem_u32(&p_full[b]), kFwdMathThreads);
 			mbar_init(smem_u32(&pv_full[b]), 1);
-			mbar_init(smem_u32(&pv_empty[b]), kMathThreads);
+			mbar_init(smem_u32(&pv_empty[b]), kFwdMathThreads);
 		}
 		for (int qd = 0; qd < 4; ++qd) {
-			mbar_init(smem_u32(&xbar[qd][0]), 64);
-			mbar_init(smem_u32(&xbar[qd][1]), 64);
+			mbar_init(smem_u32(&xbar[qd][0]), 32 * kFwdParts);
+			mbar_init(smem_u32(&xbar[qd][1]), 32 * kFwdParts);
 		}
-		mbar_init(smem_u32(&q_ready), kMathThreads);
+		mbar_init(smem_u32(&q_ready), kFwdMathThreads);
 		mbar_init(smem_u32(&drain), 1);
 		abort_sh = 0;
 		fence_mbar_init();
@@ -566,27 +455,42 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 		mma_commit_elect(smem_u32(&drain));
 		drain_wait(smem_u32(&drain), 0, p.err);
 	} else {
-		// ------------- softmax: two threads per query row, 32 key columns each -------------
-		const int quad = warp & 3, half = (warp - 2) >> 2;
+		// ------------- softmax: kFwdParts threads per query row, kFwdCols key columns each -------------
+		const int quad = warp & 3, part = (warp - 2) >> 2;
 		const int row = quad * 32 + lane;
 		const uint32_t lb = tmem + ((uint32_t)(quad * 32) << 16);
 		const float c1 = p.scale * kLog2e;
 		int t = 0, xuse = 0;
-		auto swap = [&](float v, float& other) -> bool {
+		auto exchange = [&](float v, float (&all)[kFwdParts]) -> bool {
 			const int par = xuse & 1;
-			const bool r = pair_swap(&xval[par][half][row], &xval[par][half ^ 1][row], v, other,
-				smem_u32(&xbar[quad][par]), (xuse >> 1) & 1, p.err, abort_flag);
+			const bool r = row_exchange(xval[par], part, row, v, all, smem_u32(&xbar[quad][par]), (xuse >> 1) & 1,
+				p.err, abort_flag);
 			++xuse;
 			return r;
 		};
-		float4* const rtile = reinterpret_cast<float4*>(smem + kFwdRowTile) + (warp - 2) * (kRowTileFloats / 4);
-		// Q of item w into tensor memory (zeros past Tq), then the MMA warp may issue its scores
-		auto load_q = [&](int w) {
+		// this thread's kFwdHeadCols columns of the query row of item w (row index `row`), or null past Tq
+		auto q_src = [&](int w) -> const float* {
 			int q0w, nhw, Jw;
 			fwd_item(p, w, q0w, nhw, Jw);
-			const int r0 = q0w + quad * 32;
-			warp_rows_to_tmem32(p.q + ((long long)(nhw / p.H) * p.Tq + r0) * p.D + (nhw % p.H) * kDh + half * 32, p.D,
-				rows_valid(r0, p.Tq), rtile, lane, lb + kFColQhi + half * 32, lb + kFColQlo + half * 32);
+			if (q0w + row >= p.Tq) return nullptr;
+			return p.q + ((long long)(nhw / p.H) * p.Tq + q0w + row) * p.D + (nhw % p.H) * kDh + part * kFwdHeadCols;
+		};
+		// Q of item w into tensor memory (zeros past Tq), then the MMA warp may issue its scores
+		auto load_q = [&](int w) {
+			const float* src = q_src(w);
+			uint32_t hi[kFwdHeadCols], lo[kFwdHeadCols];
+#pragma unroll
+			for (int u = 0; u < kFwdHeadCols / 4; ++u) {
+				const float4 x = src ? __ldg(reinterpret_cast<const float4*>(src) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+				float4 h4, l4;
+				split4(x, h4, l4);
+				hi[4 * u] = __float_as_uint(h4.x); hi[4 * u + 1] = __float_as_uint(h4.y);
+				hi[4 * u + 2] = __float_as_uint(h4.z); hi[4 * u + 3] = __float_as_uint(h4.w);
+				lo[4 * u] = __float_as_uint(l4.x); lo[4 * u + 1] = __float_as_uint(l4.y);
+				lo[4 * u + 2] = __float_as_uint(l4.z); lo[4 * u + 3] = __float_as_uint(l4.w);
+			}
+			tmem_st_32x32b_x16(lb + kFColQhi + part * kFwdHeadCols, hi);
+			tmem_st_32x32b_x16(lb + kFColQlo + part * kFwdHeadCols, lo);
 			tmem_wait_st();
 			tc_fence_before();
 			mbar_arrive(smem_u32(&q_ready));
@@ -601,24 +505,24 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 			const bool row_ok = qrow < p.Tq;
 			const int wn = w + (int)gridDim.x;
 			if (wn < W) {
-				const float* nq = fwd_q_row(p, wn, row, half);
+				const float* nq = q_src(wn);
 				if (nq) prefetch_l2(nq);
 			}
 			const float* padn = p.pad ? p.pad + (long long)n * p.Tk : nullptr;
 			float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
-			float o[32];
+			float o[kFwdHeadCols];
 #pragma unroll
-			for (int c = 0; c < 32; ++c) o[c] = 0.0f;
-			// O = alpha O + PV_tt (this thread's 32 head columns) for the finished tile tt
+			for (int c = 0; c < kFwdHeadCols; ++c) o[c] = 0.0f;
+			// O = alpha O + PV_tt (this thread's head columns) for the finished tile tt
 			auto fold = [&](int tt) -> bool {
 				const int b = tt & 1;
 				if (!warp_wait(smem_u32(&pv_full[b]), (tt >> 1) & 1, p.err, abort_flag)) return false;
 				tc_fence_after();
-				uint32_t r[32];
-				tmem_ld_32x32b_x32(lb + kFColPV + b * 64 + half * 32, r);
+				uint32_t r[kFwdHeadCols];
+				tmem_ld_32x32b_x16(lb + kFColPV + b * 64 + part * kFwdHeadCols, r);
 				tmem_wait_ld();
 #pragma unroll
-				for (int c = 0; c < 32; ++c) o[c] = o[c] * alpha_prev + __uint_as_float(r[c]);
+				for (int c = 0; c < kFwdHeadCols; ++c) o[c] = o[c] * alpha_prev + __uint_as_float(r[c]);
 				tc_fence_before();
 				mbar_arrive(smem_u32(&pv_empty[b]));
 				return true;
@@ -630,53 +534,53 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 					break;
 				}
 				tc_fence_after();
-				float sv[32];
+				float sv[kFwdCols];
 				{
-					uint32_t r[32];
-					tmem_ld_32x32b_x32(lb + kFColS + b * 128 + half * 32, r);
+					uint32_t r[kFwdCols];
+					tmem_ld_32x32b_x16(lb + kFColS + b * 128 + part * kFwdCols, r);
 					tmem_wait_ld();
 #pragma unroll
-					for (int c = 0; c < 32; ++c) sv[c] = __uint_as_float(r[c]);
+					for (int c = 0; c < kFwdCols; ++c) sv[c] = __uint_as_float(r[c]);
 				}
 				// tiles on the causal diagonal, past the last key, or under a padding mask take the
 				// masked path (the same for every thread of the CTA)
-				const int key0 = j * kFwdKeys + half * 32;
+				const int key0 = j * kFwdKeys + part * kFwdCols;
 				const bool general =
 					padn || (p.causal && j * kFwdKeys + kFwdKeys - 1 > q0) || (j * kFwdKeys + kFwdKeys > p.Tk);
 				float mt = -INFINITY;
 				uint32_t live = 0xffffffffu, padb = 0u;
 				if (!general) {
 #pragma unroll
-					for (int c = 0; c < 32; ++c) mt = fmaxf(mt, sv[c]);
+					for (int c = 0; c < kFwdCols; ++c) mt = fmaxf(mt, sv[c]);
 					mt = mt * p.scale;                 // scale > 0: the max of the scaled scores
 				} else {
 					live = live_bits32(key0, qrow, p.Tk, p.causal);
-					padb = padded_bits32(padn, key0, live);
+					padb = padded_bits32(padn, key0, live & ((1u << kFwdCols) - 1u));
 #pragma unroll
-					for (int c = 0; c < 32; ++c) {
+					for (int c = 0; c < kFwdCols; ++c) {
 						const bool lv = (live >> c) & 1u, pd = (padb >> c) & 1u;
 						mt = fmaxf(mt, !lv ? -INFINITY : pd ? -1e9f : sv[c] * p.scale);
 					}
 				}
-				float mo;
-				if (!swap(mt, mo)) {
+				float all[kFwdParts];
+				if (!exchange(mt, all)) {
 					ok = false;
 					break;
 				}
-				const float m_new = fmaxf(m, fmaxf(mt, mo));
+				const float m_new = fmaxf(m, fmaxf(fmaxf(all[0], all[1]), fmaxf(all[2], all[3])));
 				const float alpha = exp2_hw((m - m_new) * kLog2e);     // 0 on the first tile (m = -inf)
 				const float mlog = m_new * kLog2e;
 				float sum = 0.0f;
 				if (!general) {
 #pragma unroll
-					for (int c = 0; c < 32; ++c) {
+					for (int c = 0; c < kFwdCols; ++c) {
 						const float e = exp2_hw(__fmaf_rn(sv[c], c1, -mlog));
 						sv[c] = e;
 						sum += e;
 					}
 				} else {
 #pragma unroll
-					for (int c = 0; c < 32; ++c) {
+					for (int c = 0; c < kFwdCols; ++c) {
 						const bool lv = (live >> c) & 1u, pd = (padb >> c) & 1u;
 						// a padded key's exponent is formed from -1e9 - m, exact when the whole row is padded
 						const float e = !lv ? 0.0f
@@ -687,7 +591,7 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 				}
 				l = l * alpha + sum;
 				m = m_new;
-				vals_to_tmem(sv, lb + kFColS + b * 128 + half * 32, lb + kFColS + b * 128 + 64 + half * 32);
+				vals_to_tmem16(sv, lb + kFColS + b * 128 + part * kFwdCols, lb + kFColS + b * 128 + 64 + part * kFwdCols);
 				tmem_wait_st();
 				tc_fence_before();
 				mbar_arrive(smem_u32(&p_full[b]));
@@ -701,24 +605,18 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_fwd_kernel(const FwdParam
 				alpha_prev = alpha;
 			}
 			if (ok) ok = fold(t + J - 1);
-			float l_other = 0.0f;
-			if (ok) ok = swap(l, l_other);
-			if (ok) {
-				const float lt = half == 0 ? l + l_other : l_other + l;
+			float ls[kFwdParts];
+			if (ok) ok = exchange(l, ls);
+			if (ok && row_ok) {
+				// the row sum in part order: the same bits in every thread of the row
+				const float lt = ((ls[0] + ls[1]) + ls[2]) + ls[3];
 				const float inv_l = 1.0f / lt;
-				const int r0 = q0 + quad * 32;
-				float* obase = p.out + ((long long)n * p.Tq + r0) * p.D + h * kDh + half * 32;
+				float4* orow = reinterpret_cast<float4*>(p.out + ((long long)n * p.Tq + qrow) * p.D + h * kDh +
+					part * kFwdHeadCols);
 #pragma unroll
-				for (int g = 0; g < 2; ++g) {
-					float4 v[4];
-#pragma unroll
-					for (int w4 = 0; w4 < 4; ++w4) {
-						const float* oc = o + 16 * g + 4 * w4;
-						v[w4] = make_float4(oc[0] * inv_l, oc[1] * inv_l, oc[2] * inv_l, oc[3] * inv_l);
-					}
-					warp_rows_out16(obase + 16 * g, p.D, rows_valid(r0, p.Tq), rtile, lane, v, 0);
-				}
-				if (half == 0 && row_ok) {
+				for (int u = 0; u < kFwdHeadCols / 4; ++u)
+					orow[u] = make_float4(o[4 * u] * inv_l, o[4 * u + 1] * inv_l, o[4 * u + 2] * inv_l, o[4 * u + 3] * inv_l);
+				if (part == 0) {
 					// m and l are kept apart: with the reference's -1e9 padding scores, m + log(l) would
 					// lose log(l) to rounding for a row whose keys are all padded
 					p.stats[((long long)nh * p.Tq + qrow) * 2] = m;
@@ -791,8 +689,49 @@ __device__ __forceinline__ void dq_item(const BwdParams& p, int w, int& q0, int&
 	J = (key_end + kFwdKeys - 1) / kFwdKeys;
 }
 
+// Four math warps per lane quarter here too, each thread a quarter of a row's columns: the per-tile math
+// sits on the critical path between the score MMAs and the dQ MMAs.
+constexpr int kDqParts = 4;
+constexpr int kDqMathThreads = 32 * 4 * kDqParts;
+constexpr int kDqThreads = 64 + kDqMathThreads;
+constexpr int kDqCols = kFwdKeys / kDqParts;               // score columns per math thread (16)
+constexpr int kDqHeadCols = kDh / kDqParts;                // head columns per math thread (16)
+
+// 16 consecutive floats of a head row (zeros when !valid), split into hi and lo, stored to 16 columns
+// each at taddr_hi / taddr_lo of this thread's tensor-memory lane.
+__device__ __forceinline__ void row16_to_tmem(const float* src, bool valid, uint32_t taddr_hi, uint32_t taddr_lo) {
+	uint32_t hi[16], lo[16];
+#pragma unroll
+	for (int u = 0; u < 4; ++u) {
+		const float4 x = valid ? __ldg(reinterpret_cast<const float4*>(src) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+		float4 h4, l4;
+		split4(x, h4, l4);
+		hi[4 * u] = __float_as_uint(h4.x); hi[4 * u + 1] = __float_as_uint(h4.y);
+		hi[4 * u + 2] = __float_as_uint(h4.z); hi[4 * u + 3] = __float_as_uint(h4.w);
+		lo[4 * u] = __float_as_uint(l4.x); lo[4 * u + 1] = __float_as_uint(l4.y);
+		lo[4 * u + 2] = __float_as_uint(l4.z); lo[4 * u + 3] = __float_as_uint(l4.w);
+	}
+	tmem_st_32x32b_x16(taddr_hi, hi);
+	tmem_st_32x32b_x16(taddr_lo, lo);
+}
+
+// Stores (first: value + 0) or adds 16 values to a head row segment.
+__device__ __forceinline__ void store16(float* dst, const uint32_t (&r)[16], int first) {
+	float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+	for (int u = 0; u < 4; ++u) {
+		float4 v = make_float4(__uint_as_float(r[4 * u]) + 0.0f, __uint_as_float(r[4 * u + 1]) + 0.0f,
+			__uint_as_float(r[4 * u + 2]) + 0.0f, __uint_as_float(r[4 * u + 3]) + 0.0f);
+		if (!first) {
+			const float4 c = d4[u];
+			v.x = c.x + v.x; v.y = c.y + v.y; v.z = c.z + v.z; v.w = c.w + v.w;
+		}
+		d4[u] = v;
+	}
+}
+
 template <int kSplit>
-__global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(kDqThreads, 1) flash_bwd_dq_kernel(const BwdParams p) {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 	__shared__ __align__(8) uint64_t kv_full[kDqStages], kv_empty[kDqStages], sdp_full, ds_full, acc_full, q_ready,
@@ -808,9 +747,9 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 			mbar_init(smem_u32(&kv_empty[s]), 1);
 		}
 		mbar_init(smem_u32(&sdp_full), 1);
-		mbar_init(smem_u32(&ds_full), kMathThreads);
+		mbar_init(smem_u32(&ds_full), kDqMathThreads);
 		mbar_init(smem_u32(&acc_full), 1);
-		mbar_init(smem_u32(&q_ready), kMathThreads);
+		mbar_init(smem_u32(&q_ready), kDqMathThreads);
 		mbar_init(smem_u32(&drain), 1);
 		abort_sh = 0;
 		fence_mbar_init();
@@ -897,8 +836,8 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 		mma_commit_elect(smem_u32(&drain));
 		drain_wait(smem_u32(&drain), 0, p.err);
 	} else {
-		// ------------- score gradients: two threads per query row, 32 key columns each -------------
-		const int quad = warp & 3, half = (warp - 2) >> 2;
+		// ------------- score gradients: kDqParts threads per query row, kDqCols key columns each -------------
+		const int quad = warp & 3, part = (warp - 2) >> 2;
 		const int row = quad * 32 + lane;
 		const uint32_t lb = tmem + ((uint32_t)(quad * 32) << 16);
 		const float c1 = p.scale * kLog2e;
@@ -910,21 +849,25 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 			const int n = nh / p.H, h = nh % p.H;
 			const int qrow = q0 + row;
 			const bool row_ok = qrow < p.Tq;
-			const long long roff = ((long long)n * p.Tq + (row_ok ? qrow : 0)) * p.D + h * kDh + half * 32;
+			const long long roff = ((long long)n * p.Tq + (row_ok ? qrow : 0)) * p.D + h * kDh + part * kDqHeadCols;
 			// this item's Q and dO rows go to tensor memory (the previous item's MMAs have all
 			// completed: its dQ was read after acc_full); the next item's rows are prefetched to L2
-			half_row_to_tmem(p.q + roff, row_ok, lb + kQColQhi + half * 32, lb + kQColQlo + half * 32);
-			half_row_to_tmem(p.dout + roff, row_ok, lb + kQColOhi + half * 32, lb + kQColOlo + half * 32);
+			row16_to_tmem(p.q + roff, row_ok, lb + kQColQhi + part * kDqHeadCols, lb + kQColQlo + part * kDqHeadCols);
+			row16_to_tmem(p.dout + roff, row_ok, lb + kQColOhi + part * kDqHeadCols, lb + kQColOlo + part * kDqHeadCols);
 			if (w + (int)gridDim.x < W) {
 				int nq0, nnh, nJ;
 				dq_item(p, w + gridDim.x, nq0, nnh, nJ);
 				const int nn = nnh / p.H, nhh = nnh % p.H;
 				if (nq0 + row < p.Tq) {
-					const long long noff = ((long long)nn * p.Tq + nq0 + row) * p.D + nhh * kDh + half * 32;
+					const long long noff = ((long long)nn * p.Tq + nq0 + row) * p.D + nhh * kDh + part * kDqHeadCols;
 					prefetch_l2(p.q + noff);
 					prefetch_l2(p.dout + noff);
 				}
 			}
+			tmem_wait_st();
+			tc_fence_before();
+			mbar_arrive(smem_u32(&q_ready));
+			// the row's statistics (not needed by the MMAs, so loaded after the hand-off)
 			float* rs = p.rowstat + (long long)nh * 3 * p.Tpq;
 			float mrow = 0.0f, inv_l = 1.0f;
 			const float drow = rs[2 * p.Tpq + qrow];
@@ -932,14 +875,11 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 				mrow = p.stats[((long long)nh * p.Tq + qrow) * 2];
 				inv_l = 1.0f / p.stats[((long long)nh * p.Tq + qrow) * 2 + 1];
 			}
-			if (half == 0) {
+			if (part == 0) {
 				// rows past Tq get neutral statistics (m 0, 1/l 1; D is 0): their Q and dO rows are zero
 				rs[qrow] = mrow;
 				rs[p.Tpq + qrow] = inv_l;
 			}
-			tmem_wait_st();
-			tc_fence_before();
-			mbar_arrive(smem_u32(&q_ready));
 
 			const float* padn = p.pad ? p.pad + (long long)n * p.Tk : nullptr;
 			const float mlog = mrow * kLog2e;
@@ -950,30 +890,30 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 					break;
 				}
 				tc_fence_after();
-				uint32_t rsv[32], rp[32];
-				tmem_ld_32x32b_x32(lb + kQColS + half * 32, rsv);
-				tmem_ld_32x32b_x32(lb + kQColP + half * 32, rp);
+				uint32_t rsv[kDqCols], rp[kDqCols];
+				tmem_ld_32x32b_x16(lb + kQColS + part * kDqCols, rsv);
+				tmem_ld_32x32b_x16(lb + kQColP + part * kDqCols, rp);
 				tmem_wait_ld();
-				const int key0 = j * kFwdKeys + half * 32;
+				const int key0 = j * kFwdKeys + part * kDqCols;
 				const bool general =
 					padn || (p.causal && j * kFwdKeys + kFwdKeys - 1 > q0) || (j * kFwdKeys + kFwdKeys > p.Tk);
-				float ds[32];
+				float ds[kDqCols];
 				if (!general) {
 #pragma unroll
-					for (int c = 0; c < 32; ++c) {
+					for (int c = 0; c < kDqCols; ++c) {
 						const float pr = exp2_hw(__fmaf_rn(__uint_as_float(rsv[c]), c1, -mlog)) * inv_l;
 						ds[c] = p.scale * (pr * (__uint_as_float(rp[c]) - drow));
 					}
 				} else {
-					const uint32_t live = row_ok ? live_bits32(key0, qrow, p.Tk, p.causal) : 0u;
+					const uint32_t live = (row_ok ? live_bits32(key0, qrow, p.Tk, p.causal) : 0u) & ((1u << kDqCols) - 1u);
 					const uint32_t use = live & ~padded_bits32(padn, key0, live);
 #pragma unroll
-					for (int c = 0; c < 32; ++c) {
+					for (int c = 0; c < kDqCols; ++c) {
 						const float pr = exp2_hw(__fmaf_rn(__uint_as_float(rsv[c]), c1, -mlog)) * inv_l;
 						ds[c] = ((use >> c) & 1u) ? p.scale * (pr * (__uint_as_float(rp[c]) - drow)) : 0.0f;
 					}
 				}
-				vals_to_tmem(ds, lb + kQColS + half * 32, lb + kQColSlo + half * 32);
+				vals_to_tmem16(ds, lb + kQColS + part * kDqCols, lb + kQColSlo + part * kDqCols);
 				tmem_wait_st();
 				tc_fence_before();
 				mbar_arrive(smem_u32(&ds_full));
@@ -981,10 +921,10 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dq_kernel(const BwdPa
 			if (ok) ok = warp_wait(smem_u32(&acc_full), i & 1, p.err, abort_flag);
 			if (ok) {
 				tc_fence_after();
-				uint32_t r[32];
-				tmem_ld_32x32b_x32(lb + kQColAcc + half * 32, r);
+				uint32_t r[kDqHeadCols];
+				tmem_ld_32x32b_x16(lb + kQColAcc + part * kDqHeadCols, r);
 				tmem_wait_ld();
-				if (row_ok && p.dq) store32(p.dq + roff, r, p.dq_first);
+				if (row_ok && p.dq) store16(p.dq + roff, r, p.dq_first);
 			}
 			t += J;
 		}
@@ -1017,8 +957,27 @@ __device__ __forceinline__ void kv_item(const BwdParams& p, int w, int& k0, int&
 	J = qt_end - qt_begin;
 }
 
+// Four math warps per lane quarter, each thread a quarter of a tile's 32 query columns (8).
+constexpr int kKvParts = 4;
+constexpr int kKvMathThreads = 32 * 4 * kKvParts;
+constexpr int kKvThreads = 64 + kKvMathThreads;
+constexpr int kKvCols = kKvQ / kKvParts;                   // query columns per math thread (8)
+
+// Splits 8 finite values and stores hi / lo to two column groups of this thread's lane.
+__device__ __forceinline__ void vals_to_tmem8(const float (&v)[8], uint32_t taddr_hi, uint32_t taddr_lo) {
+	uint32_t hi[8], lo[8];
+#pragma unroll
+	for (int c = 0; c < 8; ++c) {
+		const float h = to_tf32(v[c]);
+		hi[c] = __float_as_uint(h);
+		lo[c] = __float_as_uint(to_tf32(v[c] - h));
+	}
+	tmem_st_32x32b_x8(taddr_hi, hi);
+	tmem_st_32x32b_x8(taddr_lo, lo);
+}
+
 template <int kSplit>
-__global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const BwdParams p) {
+__global__ void __launch_bounds__(kKvThreads, 1) flash_bwd_dkdv_kernel(const BwdParams p) {
 	extern __shared__ uint8_t smem_raw[];
 	uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 	__shared__ __align__(8) uint64_t q_full[kKvStages], q_empty[kKvStages], sdp_full, pds_full, acc_full, kv_ready,
@@ -1034,9 +993,9 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 			mbar_init(smem_u32(&q_empty[s]), 1);
 		}
 		mbar_init(smem_u32(&sdp_full), 1);
-		mbar_init(smem_u32(&pds_full), kMathThreads);
+		mbar_init(smem_u32(&pds_full), kKvMathThreads);
 		mbar_init(smem_u32(&acc_full), 1);
-		mbar_init(smem_u32(&kv_ready), kMathThreads);
+		mbar_init(smem_u32(&kv_ready), kKvMathThreads);
 		mbar_init(smem_u32(&drain), 1);
 		abort_sh = 0;
 		fence_mbar_init();
@@ -1133,8 +1092,8 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 		mma_commit_elect(smem_u32(&drain));
 		drain_wait(smem_u32(&drain), 0, p.err);
 	} else {
-		// ------------- P^T and dS^T: two threads per key row, 16 query columns each -------------
-		const int quad = warp & 3, half = (warp - 2) >> 2;
+		// ------------- P^T and dS^T: kKvParts threads per key row, kKvCols query columns each -------------
+		const int quad = warp & 3, part = (warp - 2) >> 2;
 		const int row = quad * 32 + lane;
 		const uint32_t lb = tmem + ((uint32_t)(quad * 32) << 16);
 		const float c1 = p.scale * kLog2e;
@@ -1149,14 +1108,15 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 			const long long roff = ((long long)n * p.Tk + (key_ok ? key : 0)) * p.D + h * kDh;
 			// this item's K and V rows go to tensor memory (the previous item's MMAs have all
 			// completed: its dK / dV were read after acc_full); the next item's rows go to L2
-			half_row_to_tmem(p.k + roff + half * 32, key_ok, lb + kKColKhi + half * 32, lb + kKColKlo + half * 32);
-			half_row_to_tmem(p.v + roff + half * 32, key_ok, lb + kKColVhi + half * 32, lb + kKColVlo + half * 32);
+			const int hc = part * (kDh / kKvParts);
+			row16_to_tmem(p.k + roff + hc, key_ok, lb + kKColKhi + hc, lb + kKColKlo + hc);
+			row16_to_tmem(p.v + roff + hc, key_ok, lb + kKColVhi + hc, lb + kKColVlo + hc);
 			if (w + (int)gridDim.x < W) {
 				int nk0, nnh, nqb, nJ;
 				kv_item(p, w + gridDim.x, nk0, nnh, nqb, nJ);
 				const int nn = nnh / p.H, nhh = nnh % p.H;
 				if (nk0 + row < p.Tk) {
-					const long long noff = ((long long)nn * p.Tk + nk0 + row) * p.D + nhh * kDh + half * 32;
+					const long long noff = ((long long)nn * p.Tk + nk0 + row) * p.D + nhh * kDh + hc;
 					prefetch_l2(p.k + noff);
 					prefetch_l2(p.v + noff);
 				}
@@ -1175,27 +1135,27 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 					break;
 				}
 				tc_fence_after();
-				const float* m_j = reinterpret_cast<const float*>(smem + s * kKvStageBytes + kKvStatOff) + half * 16;
+				const float* m_j = reinterpret_cast<const float*>(smem + s * kKvStageBytes + kKvStatOff) + part * kKvCols;
 				const float* il_j = m_j + kKvQ;
 				const float* d_j = m_j + 2 * kKvQ;
-				const int qbeg = (qt_begin + j) * kKvQ + half * 16;
-				uint32_t rs[16], rp[16];
-				tmem_ld_32x32b_x16(lb + kKColS + half * 16, rs);
-				tmem_ld_32x32b_x16(lb + kKColP + half * 16, rp);
+				const int qbeg = (qt_begin + j) * kKvQ + part * kKvCols;
+				uint32_t rs[kKvCols], rp[kKvCols];
+				tmem_ld_32x32b_x8(lb + kKColS + part * kKvCols, rs);
+				tmem_ld_32x32b_x8(lb + kKColP + part * kKvCols, rp);
 				tmem_wait_ld();
 				// queries past Tq have zero Q / dO rows and neutral statistics, keys past Tk zero K / V
 				// rows (their dK / dV rows are not stored): only the causal diagonal and padding need masks
 				const bool general = padded || (p.causal && k0 + kKvRows - 1 > (qt_begin + j) * kKvQ);
-				float pr[16], ds[16];
+				float pr[kKvCols], ds[kKvCols];
 				if (!general) {
 #pragma unroll
-					for (int c = 0; c < 16; ++c) {
+					for (int c = 0; c < kKvCols; ++c) {
 						pr[c] = exp2_hw(__fmaf_rn(__uint_as_float(rs[c]), c1, -(m_j[c] * kLog2e))) * il_j[c];
 						ds[c] = p.scale * (pr[c] * (__uint_as_float(rp[c]) - d_j[c]));
 					}
 				} else {
 #pragma unroll
-					for (int c = 0; c < 16; ++c) {
+					for (int c = 0; c < kKvCols; ++c) {
 						const bool live = !p.causal || key <= qbeg + c;
 						const float x = padded ? (-1e9f - m_j[c]) * kLog2e
 							: __fmaf_rn(__uint_as_float(rs[c]), c1, -(m_j[c] * kLog2e));
@@ -1203,8 +1163,8 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 						ds[c] = (live && !padded) ? p.scale * (pr[c] * (__uint_as_float(rp[c]) - d_j[c])) : 0.0f;
 					}
 				}
-				vals_to_tmem16(pr, lb + kKColS + half * 16, lb + kKColSlo + half * 16);
-				vals_to_tmem16(ds, lb + kKColP + half * 16, lb + kKColPlo + half * 16);
+				vals_to_tmem8(pr, lb + kKColS + part * kKvCols, lb + kKColSlo + part * kKvCols);
+				vals_to_tmem8(ds, lb + kKColP + part * kKvCols, lb + kKColPlo + part * kKvCols);
 				tmem_wait_st();
 				tc_fence_before();
 				mbar_arrive(smem_u32(&pds_full));
@@ -1212,17 +1172,15 @@ __global__ void __launch_bounds__(kThreadsFa, 1) flash_bwd_dkdv_kernel(const Bwd
 			if (ok) ok = warp_wait(smem_u32(&acc_full), i & 1, p.err, abort_flag);
 			if (ok) {
 				tc_fence_after();
-				// half 0 writes dV, half 1 writes dK (64 columns each, as two 32-column halves)
-				float* dst = half == 0 ? p.dv : p.dk;
-				const int first = half == 0 ? p.dv_first : p.dk_first;
-				const uint32_t col = half == 0 ? kKColDv : kKColDk;
-#pragma unroll
-				for (int hh = 0; hh < 2; ++hh) {
-					uint32_t r[32];
-					tmem_ld_32x32b_x32(lb + col + hh * 32, r);
-					tmem_wait_ld();
-					if (key_ok && dst) store32(dst + roff + hh * 32, r, first);
-				}
+				// parts 0, 1 write dV, parts 2, 3 dK: 32 of the 64 columns each
+				float* dst = part < 2 ? p.dv : p.dk;
+				const int first = part < 2 ? p.dv_first : p.dk_first;
+				const int hh = part & 1;
+				const uint32_t col = (part < 2 ? kKColDv : kKColDk) + hh * 32;
+				uint32_t r[32];
+				tmem_ld_32x32b_x32(lb + col, r);
+				tmem_wait_ld();
+				if (key_ok && dst) store32(dst + roff + hh * 32, r, first);
 			}
 			t += J;
 		}
@@ -1324,8 +1282,8 @@ nnb_status nnb_flash_attention_fwd(void* stream, size_t N, size_t Tq, size_t Tk,
 		p.scale = 1.0f / std::sqrt(static_cast<float>(nnb::kDh));     // ops.cpp:1236
 		nnb::TraceScope ts(s, nnb::kTraceAttention);
 		const unsigned grid = nnb::persistent_grid(NH * p.q_tiles, dev->sm_count);
-		if (split) nnb::flash_fwd_kernel<1><<<grid, nnb::kThreadsFa, nnb::kFwdSmem, s>>>(p);
-		else nnb::flash_fwd_kernel<0><<<grid, nnb::kThreadsFa, nnb::kFwdSmem, s>>>(p);
+		if (split) nnb::flash_fwd_kernel<1><<<grid, nnb::kFwdThreads, nnb::kFwdSmem, s>>>(p);
+		else nnb::flash_fwd_kernel<0><<<grid, nnb::kFwdThreads, nnb::kFwdSmem, s>>>(p);
 		st = nnb::cuda_status(cudaGetLastError(), "flash attention forward launch");
 	} while (0);
 	nnb_status st2 = nnb::scratch_free(ws, s);
@@ -1384,13 +1342,13 @@ nnb_status nnb_flash_attention_bwd(void* stream, size_t N, size_t Tq, size_t Tk,
 		nnb::TraceScope ts(s, nnb::kTraceAttention);
 		// the dQ kernel also writes the m, 1/l statistics the dKdV kernel reads
 		const unsigned gq = nnb::persistent_grid(NH * p.q_tiles, dev->sm_count);
-		if (split) nnb::flash_bwd_dq_kernel<1><<<gq, nnb::kThreadsFa, nnb::kDqSmem, s>>>(p);
-		else nnb::flash_bwd_dq_kernel<0><<<gq, nnb::kThreadsFa, nnb::kDqSmem, s>>>(p);
+		if (split) nnb::flash_bwd_dq_kernel<1><<<gq, nnb::kDqThreads, nnb::kDqSmem, s>>>(p);
+		else nnb::flash_bwd_dq_kernel<0><<<gq, nnb::kDqThreads, nnb::kDqSmem, s>>>(p);
 		if ((st = nnb::cuda_status(cudaGetLastError(), "flash attention dQ launch")) != NNB_OK) break;
 		if (dk || dv) {
 			const unsigned gk = nnb::persistent_grid(NH * p.k_tiles, dev->sm_count);
-			if (split) nnb::flash_bwd_dkdv_kernel<1><<<gk, nnb::kThreadsFa, nnb::kKvSmem, s>>>(p);
-			else nnb::flash_bwd_dkdv_kernel<0><<<gk, nnb::kThreadsFa, nnb::kKvSmem, s>>>(p);
+			if (split) nnb::flash_bwd_dkdv_kernel<1><<<gk, nnb::kKvThreads, nnb::kKvSmem, s>>>(p);
+			else nnb::flash_bwd_dkdv_kernel<0><<<gk, nnb::kKvThreads, nnb::kKvSmem, s>>>(p);
 			st = nnb::cuda_status(cudaGetLastError(), "flash attention dKdV launch");
 		}
 	} while (0);
