@@ -94,16 +94,33 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
 	asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
 }
 
-// Splits 16 finite values well inside the fp32 range and stores hi / lo to two column groups of this
-// thread's lane.
+// hi / lo split of an even count of per-tile values (probabilities, score gradients), two at a time
+// with packed fp32 instructions. hi is Veltkamp's splitting (Dekker 1971) with the constant 2^13 + 1:
+// p = 8193 v, hi = (v - p) + p keeps the top 11 significant bits of v rounded to nearest (a TF32
+// value, low 13 bits zero) and lo = v - hi is exact. lo keeps up to 13 significant bits, of which the
+// TF32 MMA reads the top 11 (it ignores an operand's low 13 bits), so lo is not rounded here: the
+// products' error stays near 2^-21 of |v| (against 2^-22 for a rounded lo), and the split costs four
+// fp32 operations per value instead of two conversions. |v| must stay below 2^128 / 8193.
+template <int kN>
+__device__ __forceinline__ void split_pairs(const float (&v)[kN], uint32_t (&hi)[kN], uint32_t (&lo)[kN]) {
+	const float2 sig = make_float2(8193.0f, 8193.0f);
+#pragma unroll
+	for (int c = 0; c < kN; c += 2) {
+		const float2 x = make_float2(v[c], v[c + 1]);
+		const float2 p = __fmul2_rn(x, sig);
+		const float2 h = __fadd2_rn(__fadd2_rn(x, make_float2(-p.x, -p.y)), p);
+		const float2 l = __fadd2_rn(x, make_float2(-h.x, -h.y));
+		hi[c] = __float_as_uint(h.x);
+		hi[c + 1] = __float_as_uint(h.y);
+		lo[c] = __float_as_uint(l.x);
+		lo[c + 1] = __float_as_uint(l.y);
+	}
+}
+
+// Splits 16 values (|v| < 2^128 / 8193) and stores hi / lo to two column groups of this thread's lane.
 __device__ __forceinline__ void vals_to_tmem16(const float (&v)[16], uint32_t taddr_hi, uint32_t taddr_lo) {
 	uint32_t hi[16], lo[16];
-#pragma unroll
-	for (int c = 0; c < 16; ++c) {
-		const float h = to_tf32(v[c]);
-		hi[c] = __float_as_uint(h);
-		lo[c] = __float_as_uint(to_tf32(v[c] - h));
-	}
+	split_pairs<16>(v, hi, lo);
 	tmem_st_32x32b_x16(taddr_hi, hi);
 	tmem_st_32x32b_x16(taddr_lo, lo);
 }
@@ -521,8 +538,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdPara
 				uint32_t r[kFwdHeadCols];
 				tmem_ld_32x32b_x16(lb + kFColPV + b * 64 + part * kFwdHeadCols, r);
 				tmem_wait_ld();
+				// o * alpha, then + PV (two roundings, as the scalar form), two columns per instruction
+				const float2 av = make_float2(alpha_prev, alpha_prev);
 #pragma unroll
-				for (int c = 0; c < kFwdHeadCols; ++c) o[c] = o[c] * alpha_prev + __uint_as_float(r[c]);
+				for (int c = 0; c < kFwdHeadCols; c += 2) {
+					const float2 y = __fadd2_rn(__fmul2_rn(make_float2(o[c], o[c + 1]), av),
+						make_float2(__uint_as_float(r[c]), __uint_as_float(r[c + 1])));
+					o[c] = y.x;
+					o[c + 1] = y.y;
+				}
 				tc_fence_before();
 				mbar_arrive(smem_u32(&pv_empty[b]));
 				return true;
@@ -572,21 +596,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdPara
 				const float mlog = m_new * kLog2e;
 				float sum = 0.0f;
 				if (!general) {
+					// the exponents' FMAs two columns at a time (packed fp32), the sum in column order
+					const float2 c1v = make_float2(c1, c1), mv = make_float2(-mlog, -mlog);
 #pragma unroll
-					for (int c = 0; c < kFwdCols; ++c) {
-						const float e = exp2_hw(__fmaf_rn(sv[c], c1, -mlog));
-						sv[c] = e;
-						sum += e;
+					for (int c = 0; c < kFwdCols; c += 2) {
+						const float2 x = __ffma2_rn(make_float2(sv[c], sv[c + 1]), c1v, mv);
+						const float e0 = exp2_hw(x.x), e1 = exp2_hw(x.y);
+						sv[c] = e0;
+						sv[c + 1] = e1;
+						sum += e0;
+						sum += e1;
 					}
 				} else {
+					// a padded key's exponent is formed from -1e9 - m, exact when the whole row is padded
+					const float xpad = (-1e9f - m_new) * kLog2e;
+					const float2 c1v = make_float2(c1, c1), mv = make_float2(-mlog, -mlog);
 #pragma unroll
-					for (int c = 0; c < kFwdCols; ++c) {
-						const bool lv = (live >> c) & 1u, pd = (padb >> c) & 1u;
-						// a padded key's exponent is formed from -1e9 - m, exact when the whole row is padded
-						const float e = !lv ? 0.0f
-							: exp2_hw(pd ? (-1e9f - m_new) * kLog2e : __fmaf_rn(sv[c], c1, -mlog));
-						sv[c] = e;
-						sum += e;
+					for (int c = 0; c < kFwdCols; c += 2) {
+						const float2 x = __ffma2_rn(make_float2(sv[c], sv[c + 1]), c1v, mv);
+						const bool lv0 = (live >> c) & 1u, pd0 = (padb >> c) & 1u;
+						const bool lv1 = (live >> (c + 1)) & 1u, pd1 = (padb >> (c + 1)) & 1u;
+						const float e0 = !lv0 ? 0.0f : exp2_hw(pd0 ? xpad : x.x);
+						const float e1 = !lv1 ? 0.0f : exp2_hw(pd1 ? xpad : x.y);
+						sv[c] = e0;
+						sv[c + 1] = e1;
+						sum += e0;
+						sum += e1;
 					}
 				}
 				l = l * alpha + sum;
@@ -613,9 +648,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdPara
 				const float inv_l = 1.0f / lt;
 				float4* orow = reinterpret_cast<float4*>(p.out + ((long long)n * p.Tq + qrow) * p.D + h * kDh +
 					part * kFwdHeadCols);
+				const float2 il2 = make_float2(inv_l, inv_l);
 #pragma unroll
-				for (int u = 0; u < kFwdHeadCols / 4; ++u)
-					orow[u] = make_float4(o[4 * u] * inv_l, o[4 * u + 1] * inv_l, o[4 * u + 2] * inv_l, o[4 * u + 3] * inv_l);
+				for (int u = 0; u < kFwdHeadCols / 4; ++u) {
+					const float2 a = __fmul2_rn(make_float2(o[4 * u], o[4 * u + 1]), il2);
+					const float2 b2 = __fmul2_rn(make_float2(o[4 * u + 2], o[4 * u + 3]), il2);
+					orow[u] = make_float4(a.x, a.y, b2.x, b2.y);
+				}
 				if (part == 0) {
 					// m and l are kept apart: with the reference's -1e9 padding scores, m + log(l) would
 					// lose log(l) to rounding for a row whose keys are all padded
@@ -899,18 +938,31 @@ __global__ void __launch_bounds__(kDqThreads, 1) flash_bwd_dq_kernel(const BwdPa
 					padn || (p.causal && j * kFwdKeys + kFwdKeys - 1 > q0) || (j * kFwdKeys + kFwdKeys > p.Tk);
 				float ds[kDqCols];
 				if (!general) {
+					// the same operations as the masked form below, two columns per packed instruction
+					const float2 c1v = make_float2(c1, c1), mv = make_float2(-mlog, -mlog), ilv = make_float2(inv_l, inv_l),
+						dv = make_float2(-drow, -drow), sc = make_float2(p.scale, p.scale);
 #pragma unroll
-					for (int c = 0; c < kDqCols; ++c) {
-						const float pr = exp2_hw(__fmaf_rn(__uint_as_float(rsv[c]), c1, -mlog)) * inv_l;
-						ds[c] = p.scale * (pr * (__uint_as_float(rp[c]) - drow));
+					for (int c = 0; c < kDqCols; c += 2) {
+						const float2 x = __ffma2_rn(make_float2(__uint_as_float(rsv[c]), __uint_as_float(rsv[c + 1])), c1v, mv);
+						const float2 pr = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), ilv);
+						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])), dv);
+						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pr, t2));
+						ds[c] = d2.x;
+						ds[c + 1] = d2.y;
 					}
 				} else {
 					const uint32_t live = (row_ok ? live_bits32(key0, qrow, p.Tk, p.causal) : 0u) & ((1u << kDqCols) - 1u);
 					const uint32_t use = live & ~padded_bits32(padn, key0, live);
+					const float2 c1v = make_float2(c1, c1), mv = make_float2(-mlog, -mlog), ilv = make_float2(inv_l, inv_l),
+						dv = make_float2(-drow, -drow), sc = make_float2(p.scale, p.scale);
 #pragma unroll
-					for (int c = 0; c < kDqCols; ++c) {
-						const float pr = exp2_hw(__fmaf_rn(__uint_as_float(rsv[c]), c1, -mlog)) * inv_l;
-						ds[c] = ((use >> c) & 1u) ? p.scale * (pr * (__uint_as_float(rp[c]) - drow)) : 0.0f;
+					for (int c = 0; c < kDqCols; c += 2) {
+						const float2 x = __ffma2_rn(make_float2(__uint_as_float(rsv[c]), __uint_as_float(rsv[c + 1])), c1v, mv);
+						const float2 pr = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), ilv);
+						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])), dv);
+						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pr, t2));
+						ds[c] = ((use >> c) & 1u) ? d2.x : 0.0f;
+						ds[c + 1] = ((use >> (c + 1)) & 1u) ? d2.y : 0.0f;
 					}
 				}
 				vals_to_tmem16(ds, lb + kQColS + part * kDqCols, lb + kQColSlo + part * kDqCols);
@@ -963,15 +1015,10 @@ constexpr int kKvMathThreads = 32 * 4 * kKvParts;
 constexpr int kKvThreads = 64 + kKvMathThreads;
 constexpr int kKvCols = kKvQ / kKvParts;                   // query columns per math thread (8)
 
-// Splits 8 finite values and stores hi / lo to two column groups of this thread's lane.
+// Splits 8 values (|v| < 2^128 / 8193) and stores hi / lo to two column groups of this thread's lane.
 __device__ __forceinline__ void vals_to_tmem8(const float (&v)[8], uint32_t taddr_hi, uint32_t taddr_lo) {
 	uint32_t hi[8], lo[8];
-#pragma unroll
-	for (int c = 0; c < 8; ++c) {
-		const float h = to_tf32(v[c]);
-		hi[c] = __float_as_uint(h);
-		lo[c] = __float_as_uint(to_tf32(v[c] - h));
-	}
+	split_pairs<8>(v, hi, lo);
 	tmem_st_32x32b_x8(taddr_hi, hi);
 	tmem_st_32x32b_x8(taddr_lo, lo);
 }
@@ -1148,19 +1195,43 @@ __global__ void __launch_bounds__(kKvThreads, 1) flash_bwd_dkdv_kernel(const Bwd
 				const bool general = padded || (p.causal && k0 + kKvRows - 1 > (qt_begin + j) * kKvQ);
 				float pr[kKvCols], ds[kKvCols];
 				if (!general) {
+					// the same operations as the masked form below, two columns per packed instruction
+					const float2 c1v = make_float2(c1, c1), l2e = make_float2(kLog2e, kLog2e), sc = make_float2(p.scale, p.scale);
 #pragma unroll
-					for (int c = 0; c < kKvCols; ++c) {
-						pr[c] = exp2_hw(__fmaf_rn(__uint_as_float(rs[c]), c1, -(m_j[c] * kLog2e))) * il_j[c];
-						ds[c] = p.scale * (pr[c] * (__uint_as_float(rp[c]) - d_j[c]));
+					for (int c = 0; c < kKvCols; c += 2) {
+						const float2 ml = __fmul2_rn(make_float2(m_j[c], m_j[c + 1]), l2e);
+						const float2 x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), c1v,
+							make_float2(-ml.x, -ml.y));
+						const float2 pv = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), make_float2(il_j[c], il_j[c + 1]));
+						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
+							make_float2(-d_j[c], -d_j[c + 1]));
+						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pv, t2));
+						pr[c] = pv.x;
+						pr[c + 1] = pv.y;
+						ds[c] = d2.x;
+						ds[c + 1] = d2.y;
 					}
 				} else {
+					const float2 c1v = make_float2(c1, c1), l2e = make_float2(kLog2e, kLog2e), sc = make_float2(p.scale, p.scale);
 #pragma unroll
-					for (int c = 0; c < kKvCols; ++c) {
-						const bool live = !p.causal || key <= qbeg + c;
-						const float x = padded ? (-1e9f - m_j[c]) * kLog2e
-							: __fmaf_rn(__uint_as_float(rs[c]), c1, -(m_j[c] * kLog2e));
-						pr[c] = live ? exp2_hw(x) * il_j[c] : 0.0f;
-						ds[c] = (live && !padded) ? p.scale * (pr[c] * (__uint_as_float(rp[c]) - d_j[c])) : 0.0f;
+					for (int c = 0; c < kKvCols; c += 2) {
+						const bool live0 = !p.causal || key <= qbeg + c, live1 = !p.causal || key <= qbeg + c + 1;
+						float2 x;
+						if (padded) {
+							x = __fmul2_rn(__fadd2_rn(make_float2(-1e9f, -1e9f), make_float2(-m_j[c], -m_j[c + 1])), l2e);
+						} else {
+							const float2 ml = __fmul2_rn(make_float2(m_j[c], m_j[c + 1]), l2e);
+							x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), c1v,
+								make_float2(-ml.x, -ml.y));
+						}
+						const float2 pv = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), make_float2(il_j[c], il_j[c + 1]));
+						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
+							make_float2(-d_j[c], -d_j[c + 1]));
+						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pv, t2));
+						pr[c] = live0 ? pv.x : 0.0f;
+						pr[c + 1] = live1 ? pv.y : 0.0f;
+						ds[c] = (live0 && !padded) ? d2.x : 0.0f;
+						ds[c + 1] = (live1 && !padded) ? d2.y : 0.0f;
 					}
 				}
 				vals_to_tmem8(pr, lb + kKColS + part * kKvCols, lb + kKColSlo + part * kKvCols);
