@@ -70,13 +70,25 @@ __global__ void colsum_partial_kernel(const float* __restrict__ g, long long row
 // same order as colsum_partial_kernel, without its per-thread latency chain.
 __global__ void __launch_bounds__(256) colsum_partial_staged_kernel(const float* __restrict__ g, long long rows,
 		long long cols, float* __restrict__ partial) {
-	__shared__ float tile[kColChunk][32];
+	__shared__ __align__(16) float tile[kColChunk][32];
 	const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 	const long long j = blockIdx.x * 32LL + lane;
 	const long long c = blockIdx.y, chunks = gridDim.y, z = blockIdx.z;
 	const long long r0 = c * kColChunk, n = min(rows - r0, (long long)kColChunk);
 	const float* gz = g + z * rows * cols;
-	for (int rr = warp; rr < n; rr += 8) tile[rr][lane] = j < cols ? __ldg(gz + (r0 + rr) * cols + j) : 0.0f;
+	const long long j0 = blockIdx.x * 32LL;
+	if (n == kColChunk && j0 + 32 <= cols && cols % 4 == 0 && (reinterpret_cast<uintptr_t>(g) & 15) == 0) {
+		// a whole chunk of 32 full columns: eight 16-byte loads per thread, all issued before any store
+		const int c4 = (threadIdx.x & 7) * 4, rq = threadIdx.x >> 3;
+		float4 v[kColChunk / 32];
+#pragma unroll
+		for (int u = 0; u < kColChunk / 32; ++u)
+			v[u] = __ldg(reinterpret_cast<const float4*>(gz + (r0 + rq + 32 * u) * cols + j0 + c4));
+#pragma unroll
+		for (int u = 0; u < kColChunk / 32; ++u) *reinterpret_cast<float4*>(&tile[rq + 32 * u][c4]) = v[u];
+	} else {
+		for (int rr = warp; rr < n; rr += 8) tile[rr][lane] = j < cols ? __ldg(gz + (r0 + rr) * cols + j) : 0.0f;
+	}
 	__syncthreads();
 	if (warp != 0 || j >= cols) return;
 	float s = 0.0f;

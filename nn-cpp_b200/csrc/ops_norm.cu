@@ -128,7 +128,8 @@ __global__ void __launch_bounds__(256) layernorm_bwd_param_partial_staged(const 
 		const float* __restrict__ x, const float* __restrict__ mean, const float* __restrict__ inv_std, long long R, int D,
 		float* __restrict__ pg, float* __restrict__ pb) {
 	constexpr int kPass = kChunk / 2;                // rows staged at a time (shared memory < 48 KB)
-	__shared__ float tg[kPass][32], tx[kPass][32], tm[kPass], ti[kPass];
+	__shared__ __align__(16) float tg[kPass][32], tx[kPass][32];
+	__shared__ float tm[kPass], ti[kPass];
 	const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 	const int j = blockIdx.x * 32 + lane;
 	const long long c = blockIdx.y, chunks = gridDim.y, z = blockIdx.z;
@@ -137,9 +138,29 @@ __global__ void __launch_bounds__(256) layernorm_bwd_param_partial_staged(const 
 	float sg = 0.0f, sb = 0.0f;
 	for (int p0 = 0; p0 < n; p0 += kPass) {
 		const int m = min(kPass, n - p0);
-		for (int rr = warp; rr < m; rr += 8) {
-			tg[rr][lane] = j < D ? __ldg(g + (r0 + p0 + rr) * D + j) : 0.0f;
-			tx[rr][lane] = j < D ? __ldg(x + (r0 + p0 + rr) * D + j) : 0.0f;
+		const int j0 = blockIdx.x * 32;
+		if (m == kPass && j0 + 32 <= D && D % 4 == 0 &&
+				((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(x)) & 15) == 0) {
+			// a whole pass of 32 full columns: every thread's 16-byte loads issued before any store
+			constexpr int kLoads = kPass * 32 / 4 / 256;
+			const int c4 = (threadIdx.x & 7) * 4, rq = threadIdx.x >> 3;
+			float4 vg[kLoads], vx[kLoads];
+#pragma unroll
+			for (int u = 0; u < kLoads; ++u) {
+				const long long off = (r0 + p0 + rq + 32 * u) * D + j0 + c4;
+				vg[u] = __ldg(reinterpret_cast<const float4*>(g + off));
+				vx[u] = __ldg(reinterpret_cast<const float4*>(x + off));
+			}
+#pragma unroll
+			for (int u = 0; u < kLoads; ++u) {
+				*reinterpret_cast<float4*>(&tg[rq + 32 * u][c4]) = vg[u];
+				*reinterpret_cast<float4*>(&tx[rq + 32 * u][c4]) = vx[u];
+			}
+		} else {
+			for (int rr = warp; rr < m; rr += 8) {
+				tg[rr][lane] = j < D ? __ldg(g + (r0 + p0 + rr) * D + j) : 0.0f;
+				tx[rr][lane] = j < D ? __ldg(x + (r0 + p0 + rr) * D + j) : 0.0f;
+			}
 		}
 		for (int rr = threadIdx.x; rr < m; rr += 256) {
 			tm[rr] = __ldg(mean + r0 + p0 + rr);
