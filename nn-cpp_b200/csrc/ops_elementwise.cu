@@ -330,6 +330,89 @@ __global__ void ce_rows_kernel(long long rows, int C, const float* __restrict__ 
 	}
 }
 
+// The same row results for wide rows (C % 4 == 0, 16-byte aligned, C <= 4096): one 128-thread block
+// per row keeps the row in registers (up to eight float4 per thread), so the logits are read from HBM
+// once instead of three times; the max and the sums are combined in a fixed order (each thread's
+// elements in order, then the warp's xor tree, then the four warps in order), so the results are
+// deterministic. The operations per element are those of ce_rows_kernel.
+constexpr int kCeBlock = 128, kCeV4 = 8;
+__global__ void __launch_bounds__(kCeBlock) ce_rows_block_kernel(long long rows, int C,
+		const float* __restrict__ logits, const int64_t* __restrict__ targets, int64_t ignore_index, int use_ignore,
+		float ls, float* __restrict__ softmax, float* __restrict__ row_loss, int* __restrict__ valid, int* err) {
+	__shared__ float red[2][kCeBlock / 32];
+	const long long r = blockIdx.x;
+	const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+	const int64_t t = targets[r];
+	if (use_ignore && t == ignore_index) {
+		if (tid == 0) {
+			row_loss[r] = 0.0f;
+			valid[r] = 0;
+		}
+		return;
+	}
+	if (t < 0 || t >= C) {
+		if (tid == 0) {
+			row_loss[r] = __int_as_float(0x7fc00000);
+			valid[r] = 0;
+			atomicCAS(err, 0, kDevBadIndex);
+		}
+		return;
+	}
+	const int C4 = C >> 2;
+	const float4* row = reinterpret_cast<const float4*>(logits + r * C);
+	float4 v[kCeV4];
+	float m = -INFINITY;
+#pragma unroll
+	for (int u = 0; u < kCeV4; ++u) {
+		const int i = tid + u * kCeBlock;
+		v[u] = i < C4 ? __ldg(row + i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+		m = fmaxf(fmaxf(fmaxf(m, v[u].x), fmaxf(v[u].y, v[u].z)), v[u].w);
+	}
+	m = warp_max(m);
+	if (lane == 0) red[0][warp] = m;
+	__syncthreads();
+	m = fmaxf(fmaxf(red[0][0], red[0][1]), fmaxf(red[0][2], red[0][3]));
+	float se = 0.0f;
+#pragma unroll
+	for (int u = 0; u < kCeV4; ++u)
+		if (tid + u * kCeBlock < C4) {
+			se += expf(v[u].x - m);
+			se += expf(v[u].y - m);
+			se += expf(v[u].z - m);
+			se += expf(v[u].w - m);
+		}
+	se = warp_sum(se);
+	if (lane == 0) red[1][warp] = se;
+	__syncthreads();
+	se = ((red[1][0] + red[1][1]) + red[1][2]) + red[1][3];
+	const float lse = logf(se);
+	float4* sm = reinterpret_cast<float4*>(softmax + r * C);
+	float mean_nll = 0.0f;
+	const float inv_c = 1.0f / (float)C;
+#pragma unroll
+	for (int u = 0; u < kCeV4; ++u) {
+		const int i = tid + u * kCeBlock;
+		if (i < C4) {
+			const float l0 = v[u].x - m - lse, l1 = v[u].y - m - lse, l2 = v[u].z - m - lse, l3 = v[u].w - m - lse;
+			sm[i] = make_float4(expf(l0), expf(l1), expf(l2), expf(l3));
+			mean_nll -= l0 * inv_c;
+			mean_nll -= l1 * inv_c;
+			mean_nll -= l2 * inv_c;
+			mean_nll -= l3 * inv_c;
+		}
+	}
+	mean_nll = warp_sum(mean_nll);
+	__syncthreads();                          // red[0] is reused below
+	if (lane == 0) red[0][warp] = mean_nll;
+	__syncthreads();
+	if (tid == 0) {
+		mean_nll = ((red[0][0] + red[0][1]) + red[0][2]) + red[0][3];
+		const float nll = -(logits[r * C + t] - m - lse);
+		row_loss[r] = ls == 0.0f ? nll : (1.0f - ls) * nll + ls * mean_nll;
+		valid[r] = 1;
+	}
+}
+
 // loss = sum(row_loss) / count in fixed order: 256 threads sum contiguous slices serially
 // (fp64 for sequences, as the reference; fp32 otherwise), then thread 0 sums the slices in order.
 // norm: the backward scale's divisor N (rows) or multiplier 1/count (sequences)
@@ -396,6 +479,42 @@ __global__ void ce_bwd_kernel(long long rows, int C, const float* __restrict__ s
 			}
 			dlogits[i] = first ? v + 0.0f : dlogits[i] + v;
 		}
+	}
+}
+
+// The same gradient four columns at a time (C % 4 == 0, 16-byte aligned pointers): a grid-stride walk
+// over the float4 groups of the whole [rows, C] array, each element getting ce_bwd_kernel's operations.
+__global__ void ce_bwd_vec_kernel(long long n4, int C, const float* __restrict__ softmax,
+		const int64_t* __restrict__ targets, int64_t ignore_index, int use_ignore, float ls,
+		const float* __restrict__ grad_loss, const float* __restrict__ norm, float* __restrict__ dlogits,
+		int first) {
+	const float scale = use_ignore ? grad_loss[0] * norm[0] : grad_loss[0] / norm[0];
+	const int C4 = C >> 2;
+	GRID_STRIDE(i, n4) {
+		const long long r = i / C4;
+		const int c0 = (int)(i - r * C4) * 4;
+		const int64_t t = __ldg(targets + r);
+		const bool live = !(use_ignore && t == ignore_index) && t >= 0 && t < C;
+		float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+		if (live) {
+			const float4 p = ld4(softmax, i);
+			const float pv[4] = {p.x, p.y, p.z, p.w};
+			float o[4];
+#pragma unroll
+			for (int j = 0; j < 4; ++j) {
+				const int c = c0 + j;
+				if (ls == 0.0f && !use_ignore) {
+					o[j] = (c == t ? pv[j] - 1.0f : pv[j]) * scale;                // ops.cpp:1835
+				} else {
+					float q = pv[j] - ls / (float)C;                               // ops.cpp:1972-1974
+					if (c == t) q -= 1.0f - ls;
+					o[j] = q * scale;
+				}
+			}
+			v = make_float4(o[0], o[1], o[2], o[3]);
+		}
+		float4* d = reinterpret_cast<float4*>(dlogits) + i;
+		*d = store_rule(v, d, first);
 	}
 }
 
@@ -740,8 +859,12 @@ static nnb_status ce_forward(cudaStream_t s, long long rows, int C, const float*
 	float* row_loss = static_cast<float*>(ws);
 	int* valid = reinterpret_cast<int*>(row_loss + rows);
 	const long long threads = rows * 32;
-	NNB_LAUNCH(kTraceRowwise, (unsigned)((threads + 255) / 256), 256, nnb::ce_rows_kernel, rows, C, logits, targets,
-		ignore_index, use_ignore, ls, softmax, row_loss, valid, dev->error_word);
+	if (C > 1024 && C <= 4 * nnb::kCeBlock * nnb::kCeV4 && rows <= 0x7fffffffLL && nnb::vec4_ok(C, logits, softmax))
+		NNB_LAUNCH(kTraceRowwise, (unsigned)rows, nnb::kCeBlock, nnb::ce_rows_block_kernel, rows, C, logits, targets,
+			ignore_index, use_ignore, ls, softmax, row_loss, valid, dev->error_word);
+	else
+		NNB_LAUNCH(kTraceRowwise, (unsigned)((threads + 255) / 256), 256, nnb::ce_rows_kernel, rows, C, logits, targets,
+			ignore_index, use_ignore, ls, softmax, row_loss, valid, dev->error_word);
 	NNB_LAUNCH(kTraceRowwise, 1, 256, nnb::ce_total_kernel, rows, row_loss, valid, as_double, loss, norm);
 	nnb_status st = nnb::cuda_status(cudaGetLastError(), "cross entropy launch");
 	nnb_status st2 = nnb::scratch_free(ws, s);
@@ -763,8 +886,12 @@ nnb_status nnb_cross_entropy_bwd(void* stream, size_t N, size_t C, const float* 
 		return nnb::fail(NNB_ERR_INVALID, "cross_entropy_bwd: null pointer");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	const long long n = (long long)N * C;
-	NNB_LAUNCH(kTraceRowwise, nnb::ce_bwd_grid((long long)N, (int)C), 256, nnb::ce_bwd_kernel, (long long)N, (int)C, softmax,
-		targets, 0, 0, 0.0f, grad_loss, norm, dlogits, first);
+	if (nnb::vec4_ok(n, softmax, dlogits) && C % 4 == 0)
+		NNB_LAUNCH(kTraceRowwise, nnb::grid_for(n / 4, 256), 256, nnb::ce_bwd_vec_kernel, n / 4, (int)C, softmax, targets, 0,
+			0, 0.0f, grad_loss, norm, dlogits, first);
+	else
+		NNB_LAUNCH(kTraceRowwise, nnb::ce_bwd_grid((long long)N, (int)C), 256, nnb::ce_bwd_kernel, (long long)N, (int)C,
+			softmax, targets, 0, 0, 0.0f, grad_loss, norm, dlogits, first);
 	return nnb::cuda_status(cudaGetLastError(), "cross_entropy_bwd launch");
 }
 
@@ -786,8 +913,12 @@ nnb_status nnb_sequence_ce_bwd(void* stream, size_t P, size_t V, const float* so
 		return nnb::fail(NNB_ERR_INVALID, "sequence_ce_bwd: null pointer");
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	const long long n = (long long)P * V;
-	NNB_LAUNCH(kTraceRowwise, nnb::ce_bwd_grid((long long)P, (int)V), 256, nnb::ce_bwd_kernel, (long long)P, (int)V, softmax,
-		targets, ignore_index, 1, label_smoothing, grad_loss, norm, dlogits, first);
+	if (nnb::vec4_ok(n, softmax, dlogits) && V % 4 == 0)
+		NNB_LAUNCH(kTraceRowwise, nnb::grid_for(n / 4, 256), 256, nnb::ce_bwd_vec_kernel, n / 4, (int)V, softmax, targets,
+			ignore_index, 1, label_smoothing, grad_loss, norm, dlogits, first);
+	else
+		NNB_LAUNCH(kTraceRowwise, nnb::ce_bwd_grid((long long)P, (int)V), 256, nnb::ce_bwd_kernel, (long long)P, (int)V,
+			softmax, targets, ignore_index, 1, label_smoothing, grad_loss, norm, dlogits, first);
 	return nnb::cuda_status(cudaGetLastError(), "sequence_ce_bwd launch");
 }
 
