@@ -158,6 +158,14 @@ NNB_API nnb_status nnb_matmul(void* stream, const float* a, const int64_t* a_sha
 /* y[M, n] = x[M, K] · w[n, K]^T + bias[n] (bias added in the GEMM epilogue). */
 NNB_API nnb_status nnb_linear_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
 		const float* bias, float* y);
+/* linear of one input under `count` weights (the q, k and v projections of a self-attention,
+ * src/nn/attention.cpp:34, `q_.forward(query), k_.forward(context), v_.forward(context)` with
+ * query == context): y_i = x · w_i^T + b_i with w_i = w + i·w_stride, b_i = bias + i·bias_stride and
+ * y_i = y + i·y_stride (floats), i < count. x is packed once and the products run as one launch;
+ * every y_i has the bits of nnb_linear_fwd(x, w_i, b_i). Strides that make consecutive weights,
+ * biases or outputs overlap are rejected (NNB_ERR_INVALID). */
+NNB_API nnb_status nnb_linear_multi_fwd(void* stream, size_t count, size_t M, size_t K, size_t n, const float* x,
+		const float* w, size_t w_stride, const float* bias, size_t bias_stride, float* y, size_t y_stride);
 /* gelu(linear(x, w, bias)) as one GEMM with the GELU in its epilogue (the transformer's fc1 followed
  * by gelu, ops.cpp:451-466): y = gelu(pre), pre = x·w^T + bias is kept for the backward pass
  * (nnb_gelu_bwd with tanh_saved = NULL recomputes the tanh from pre, bit for bit). */

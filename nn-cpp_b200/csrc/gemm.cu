@@ -79,6 +79,7 @@ struct Params {
 	int accumulate;
 	// epilogue
 	const float* bias;
+	long long s_bias_outer;          // bias offset per outer batch entry
 	int bias_mode, act;
 	unsigned char* mask;
 	float* pre;
@@ -773,7 +774,8 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 			const bool fix = (*p.any_nonfinite | (kGather ? __ldcg(p.any_b) : *p.any_b)) != 0;
 			const bool row_bad = fix && row_ok && p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0;
 			const int* fcol = p.flags_b + (long long)(p.b_batched ? bi : 0) * p.Np;
-			const float row_bias = (p.bias_mode == kBiasRow && row_ok) ? p.bias[gm] : 0.0f;
+			const float* bias_e = p.bias + (long long)(bi / p.batch_inner) * p.s_bias_outer;
+			const float row_bias = (p.bias_mode == kBiasRow && row_ok) ? bias_e[gm] : 0.0f;
 #pragma unroll 1
 			for (int ch = 0; ch < kBN / 32; ++ch) {
 				const int gn0 = nt * kBN + ch * 32;
@@ -806,7 +808,7 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {
 						const int gn = gn0 + j;
-						v[j] = v[j] + (gn < p.N ? __ldg(p.bias + gn) : 0.0f);
+						v[j] = v[j] + (gn < p.N ? __ldg(bias_e + gn) : 0.0f);
 					}
 				}
 				uint32_t alive_bits = 0;
@@ -1066,7 +1068,7 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	p.a_batched = pl.a_entries > 1; p.b_batched = pl.b_entries > 1;
 	p.Mp = (int)pl.Mp; p.Np = (int)pl.Np;
 	p.C = d.c; p.ldc = d.ldc; p.sc_outer = d.sc_outer; p.sc_inner = d.sc_inner; p.accumulate = d.accumulate;
-	p.bias = d.epi.bias; p.bias_mode = d.epi.bias_mode; p.act = d.epi.act;
+	p.bias = d.epi.bias; p.s_bias_outer = d.epi.s_bias_outer; p.bias_mode = d.epi.bias_mode; p.act = d.epi.act;
 	p.mask = d.epi.mask; p.pre = d.epi.pre;
 	p.ld_aux = d.epi.ld_aux; p.s_aux_outer = d.epi.s_aux_outer; p.s_aux_inner = d.epi.s_aux_inner;
 	p.any_nonfinite = any; p.any_b = any_b; p.flags_a = flags_a; p.flags_b = flags_b;

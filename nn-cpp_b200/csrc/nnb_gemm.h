@@ -24,6 +24,7 @@ struct GemmEpilogue {
 	unsigned char* mask = nullptr;      // relu alive flags, same (i, j) layout as C with ld_aux
 	float* pre = nullptr;               // gelu pre-activation, same (i, j) layout as C with ld_aux
 	long long ld_aux = 0, s_aux_outer = 0, s_aux_inner = 0;
+	long long s_bias_outer = 0;         // floats between the biases of consecutive outer batch entries
 };
 
 // A B operand gathered on the fly from a 4-D tensor [N, C, H, W] into the GEMM's shared-memory stages

@@ -170,6 +170,27 @@ nnb_status nnb_linear_fwd(void* stream, size_t M, size_t K, size_t n, const floa
 	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
 }
 
+nnb_status nnb_linear_multi_fwd(void* stream, size_t count, size_t M, size_t K, size_t n, const float* x, const float* w,
+		size_t w_stride, const float* bias, size_t bias_stride, float* y, size_t y_stride) {
+	if (count == 0 || M == 0 || n == 0) return NNB_OK;
+	if (!x || !w || !bias || !y) return nnb::fail(NNB_ERR_INVALID, "linear_multi_fwd: null pointer");
+	if (K == 0) return nnb::fail(NNB_ERR_SHAPE, "linear_multi_fwd: zero input features");
+	if (count > 1 && (w_stride < n * K || bias_stride < n || y_stride < M * n))
+		return nnb::fail(NNB_ERR_INVALID, "linear_multi_fwd: strides overlap consecutive weights, biases or outputs");
+	if (count > 65535) return nnb::fail(NNB_ERR_UNSUPPORTED, "linear_multi_fwd: more than 65535 weights");
+	// one batched GEMM whose A (x) is shared by every entry, so x is packed once; entry i is the product
+	// nnb_linear_fwd would compute for (x, w_i, b_i), with the same operations for every element
+	nnb::GemmDesc d;
+	d.ta = 0; d.tb = 1;
+	d.m = (long long)M; d.n = (long long)n; d.k = (long long)K;
+	d.a = x; d.lda = (long long)K; d.b = w; d.ldb = (long long)K; d.c = y; d.ldc = (long long)n;
+	d.batch_outer = (long long)count;
+	d.sa_outer = 0; d.sb_outer = (long long)w_stride; d.sc_outer = (long long)y_stride;
+	d.mode = nnb::math_mode();
+	d.epi.bias = bias; d.epi.bias_mode = nnb::kBiasCol; d.epi.s_bias_outer = (long long)bias_stride;
+	return nnb::gemm_run(static_cast<cudaStream_t>(stream), d);
+}
+
 nnb_status nnb_linear_gelu_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
 		const float* bias, float* y, float* pre) {
 	if (M == 0 || n == 0) return NNB_OK;

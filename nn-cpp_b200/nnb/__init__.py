@@ -97,6 +97,7 @@ _SIGS = {
     "nnb_gelu_bwd": ([_p, _sz, _p, _p, _p, _p, _i], _i),
     "nnb_fill": ([_p, _sz, _f, _p], _i),
     "nnb_scale": ([_p, _sz, _f, _p, _p], _i),
+    "nnb_linear_multi_fwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _sz, _p, _sz, _p, _sz], _i),
     "nnb_linear_bwd_grouped": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _sz, _i, _p, _sz, _i], _i),
     "nnb_layernorm_bwd_grouped": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _sz, _i, _p, _sz, _i], _i),
     "nnb_embedding_bwd_grouped": ([_p, _sz, _sz, _sz, _p, _sz, _p, _p, _sz, _i], _i),

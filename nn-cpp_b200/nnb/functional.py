@@ -70,6 +70,46 @@ def linear(x: Value, weight: Value, bias: Value) -> Value:
     return Value.node(y, (x, weight, bias), backward)
 
 
+def linear_multi(x: Value, layers) -> list[Value]:
+    """[linear(x, w_i, b_i) for (w_i, b_i) in layers] (the q, k, v projections of a self-attention,
+    src/nn/attention.cpp:34). When the weights (and the biases) sit at one constant stride in memory --
+    the data-parallel trainer's flat parameter buffer lays each Linear out as weight then bias -- the
+    products run as one launch that packs x once (nnb_linear_multi_fwd); otherwise one linear per
+    layer. Either way every output has linear's bits and linear's backward."""
+    ws = [w for w, _ in layers]
+    bs = [b for _, b in layers]
+    if not ws or any(w.shape != ws[0].shape for w in ws) or any(b.shape != (ws[0].shape[0],) for b in bs):
+        return [linear(x, w, b) for w, b in layers]
+    xs = x.shape
+    if len(xs) < 2 or len(ws[0].shape) != 2 or xs[-1] != ws[0].shape[1]:
+        raise TensorShapeError("linear: shapes do not agree")
+    n, K = ws[0].shape
+    M = x.data.numel() // K
+
+    def stride(ts):
+        if any(not t.data.is_contiguous() for t in ts):
+            return None
+        d = [t.data.data_ptr() - ts[0].data.data_ptr() for t in ts]
+        if len(ts) == 1:
+            return 0
+        if d[1] <= 0 or d[1] % 4 or any(d[i] != i * d[1] for i in range(len(ts))):
+            return None
+        return d[1] // 4
+
+    w_stride, b_stride = stride(ws), stride(bs)
+    if len(layers) == 1 or w_stride is None or b_stride is None or w_stride < n * K or b_stride < n:
+        return [linear(x, w, b) for w, b in layers]
+    y = empty((len(layers),) + xs[:-1] + (n,))
+    check(lib().nnb_linear_multi_fwd(_s(), len(layers), M, K, n, _p(x.data), _p(ws[0].data), w_stride,
+                                     _p(bs[0].data), b_stride, _p(y), M * n))
+    outs = []
+    for i, (w, b) in enumerate(layers):
+        def backward(g, w=w, b=b):
+            _linear_backward(g, x, w, b, M, K, n)
+        outs.append(Value.node(y[i], (x, w, b), backward))
+    return outs
+
+
 def _linear_backward(g, x, weight, bias, M, K, n):
     dx, fx = x.grad_accum() if _need(x) else (None, 0)
     dw, fw = weight.grad_accum() if _need(weight) else (None, 0)

@@ -184,7 +184,10 @@ class MultiHeadAttention(Module):
         qs, cs = query.shape, context.shape
         if len(qs) != 3 or len(cs) != 3 or qs[2] != self.dim or cs[2] != self.dim or qs[0] != cs[0]:
             raise TensorShapeError("MultiHeadAttention: bad input shapes")
-        q, k, v = self.q(query), self.k(context), self.v(context)
+        if query is context:   # self-attention: the three projections share their input
+            q, k, v = F.linear_multi(query, [(m.weight, m.bias) for m in (self.q, self.k, self.v)])
+        else:
+            q, k, v = self.q(query), self.k(context), self.v(context)
         if not self.drop.active():
             return self.o(F.attention(q, k, v, self.heads, key_padding_mask, self.causal))
         return self.o(F.attention_dropout(q, k, v, self.heads, key_padding_mask, self.causal, self.drop.p,

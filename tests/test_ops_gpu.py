@@ -92,6 +92,62 @@ def test_linear(cuda, M, K, n):
     assert nnb.device_error() == 0
 
 
+@pytest.mark.parametrize("M,K,n", [(37, 65, 23), (4096, 512, 512), (300, 96, 200)])
+def test_linear_multi_matches_separate_linears(cuda, M, K, n):
+    """nnb_linear_multi_fwd (one input under three weights, x packed once, one launch) gives each
+    output nnb_linear_fwd's bits; the Python linear_multi takes that path for weights at one stride
+    (a flat buffer laid out weight, bias, weight, bias, ...) and the per-layer path otherwise, with
+    the same outputs and the same gradients either way."""
+    torch = cuda
+    from nnb import functional as F
+    from nnb.autograd import Value
+    x = dev(torch, rnd(11, M, K))
+    per = n * K + n
+    flat = dev(torch, rnd(12, 3 * per))
+    ws = [flat[i * per: i * per + n * K].view(n, K) for i in range(3)]
+    bs = [flat[i * per + n * K: (i + 1) * per] for i in range(3)]
+    want = []
+    for w, b in zip(ws, bs):
+        y = torch.empty(M, n, device="cuda")
+        ok(lib().nnb_linear_fwd(S(torch), M, K, n, x.data_ptr(), w.data_ptr(), b.data_ptr(), y.data_ptr()))
+        want.append(host(y))
+    y3 = torch.full((3, M, n), 7.0, device="cuda")
+    ok(lib().nnb_linear_multi_fwd(S(torch), 3, M, K, n, x.data_ptr(), ws[0].data_ptr(), per, bs[0].data_ptr(), per,
+                                  y3.data_ptr(), M * n))
+    for i in range(3):
+        assert_bits(host(y3[i]), want[i])
+    st = lib().nnb_linear_multi_fwd(S(torch), 3, M, K, n, x.data_ptr(), ws[0].data_ptr(), n * K - 1, bs[0].data_ptr(),
+                                    per, y3.data_ptr(), M * n)
+    assert st == nnb.NNB_ERR_INVALID
+    # the Python op: flat parameters (one launch) and separate tensors (per layer), forward and backward
+    g = [dev(torch, rnd(20 + i, M, n)) for i in range(3)]
+    grads = []
+    # copies at uneven gaps (no single stride): the per-layer path
+    spread = torch.empty(3 * per + 1024, device="cuda")
+    offs = [0, per + 64, 2 * per + 320]
+    ws2 = [spread[o: o + n * K].view(n, K) for o in offs]
+    bs2 = [spread[o + n * K: o + per] for o in offs]
+    for a, b in zip(ws2 + bs2, ws + bs):
+        a.copy_(b)
+    for batched, params in ((True, [(Value.leaf(w, True), Value.leaf(b, True)) for w, b in zip(ws, bs)]),
+                            (False, [(Value.leaf(w, True), Value.leaf(b, True)) for w, b in zip(ws2, bs2)])):
+        X = Value.leaf(x, True)
+        nnb.trace_reset()
+        nnb.trace_enable(True)
+        outs = F.linear_multi(X, params)
+        nnb.trace_enable(False)
+        _, launches = nnb.trace_query(nnb.TRACE_GEMM)
+        assert launches == (1 if batched else 3)
+        for i, o in enumerate(outs):
+            assert_bits(host(o.data), want[i])
+        for i, o in enumerate(outs):
+            o.backward(g[i])
+        grads.append([host(X.grad)] + [host(t.grad) for p in params for t in p])
+    for a, b in zip(grads[0], grads[1]):
+        assert_bits(a, b)
+    assert nnb.device_error() == 0
+
+
 @pytest.mark.parametrize("R,D", [(29, 77), (4096, 512), (3, 1000)])
 def test_layernorm(cuda, R, D):
     torch = cuda
