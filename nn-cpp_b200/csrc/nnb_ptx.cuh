@@ -362,4 +362,34 @@ __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
 	lo = to_tf32(x - hi);
 }
 
+// Packed fp32 pairs (the f32x2 instructions of sm_100: one instruction for two lanes' operations),
+// round to nearest. A multiply whose result feeds an add is not guaranteed to stay two roundings
+// (measured: a packed GELU built from such pairs, or from the __fmul2_rn / __fadd2_rn intrinsics, did
+// not reproduce the separately rounded scalar results bit for bit), so code that needs two roundings
+// does not rely on a mul2_rn -> add2_rn pair: it writes the fused form explicitly or avoids the pattern.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+	float2 d;
+	asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+	    "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+	    : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+	return d;
+}
+
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+	float2 d;
+	asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+	    "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+	    : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+	return d;
+}
+
+// d = a * b + c with one rounding per lane
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+	float2 d;
+	asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+	    "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+	    : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+	return d;
+}
+
 }  // namespace nnb

@@ -97,19 +97,22 @@ __device__ __forceinline__ void prefetch_l2(const void* p) {
 // hi / lo split of an even count of per-tile values (probabilities, score gradients), two at a time
 // with packed fp32 instructions. hi is Veltkamp's splitting (Dekker 1971) with the constant 2^13 + 1:
 // p = 8193 v, hi = (v - p) + p keeps the top 11 significant bits of v rounded to nearest (a TF32
-// value, low 13 bits zero) and lo = v - hi is exact. lo keeps up to 13 significant bits, of which the
-// TF32 MMA reads the top 11 (it ignores an operand's low 13 bits), so lo is not rounded here: the
-// products' error stays near 2^-21 of |v| (against 2^-22 for a rounded lo), and the split costs four
-// fp32 operations per value instead of two conversions. |v| must stay below 2^128 / 8193.
+// value, low 13 bits zero) and lo = v - hi is exact. p is formed as the single fused operation
+// fma(v, 8192, v), which is 8193 v rounded once, so no compiler contraction of a multiply into the
+// following add can change it (the splitting needs p rounded before v - p is taken). lo keeps up to 13
+// significant bits, of which the TF32 MMA reads the top 11 (it ignores an operand's low 13 bits), so
+// lo is not rounded here: the products' error stays near 2^-21 of |v| (against 2^-22 for a rounded
+// lo), and the split costs four fp32 operations per value instead of two conversions. |v| must stay
+// below 2^128 / 8193.
 template <int kN>
 __device__ __forceinline__ void split_pairs(const float (&v)[kN], uint32_t (&hi)[kN], uint32_t (&lo)[kN]) {
-	const float2 sig = make_float2(8193.0f, 8193.0f);
+	const float2 k8192 = make_float2(8192.0f, 8192.0f);
 #pragma unroll
 	for (int c = 0; c < kN; c += 2) {
 		const float2 x = make_float2(v[c], v[c + 1]);
-		const float2 p = __fmul2_rn(x, sig);
-		const float2 h = __fadd2_rn(__fadd2_rn(x, make_float2(-p.x, -p.y)), p);
-		const float2 l = __fadd2_rn(x, make_float2(-h.x, -h.y));
+		const float2 p = fma2_rn(x, k8192, x);
+		const float2 h = add2_rn(add2_rn(x, make_float2(-p.x, -p.y)), p);
+		const float2 l = add2_rn(x, make_float2(-h.x, -h.y));
 		hi[c] = __float_as_uint(h.x);
 		hi[c + 1] = __float_as_uint(h.y);
 		lo[c] = __float_as_uint(l.x);
@@ -538,11 +541,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdPara
 				uint32_t r[kFwdHeadCols];
 				tmem_ld_32x32b_x16(lb + kFColPV + b * 64 + part * kFwdHeadCols, r);
 				tmem_wait_ld();
-				// o * alpha, then + PV (two roundings, as the scalar form), two columns per instruction
+				// o * alpha + PV with one rounding, two columns per instruction
 				const float2 av = make_float2(alpha_prev, alpha_prev);
 #pragma unroll
 				for (int c = 0; c < kFwdHeadCols; c += 2) {
-					const float2 y = __fadd2_rn(__fmul2_rn(make_float2(o[c], o[c + 1]), av),
+					const float2 y = fma2_rn(make_float2(o[c], o[c + 1]), av,
 						make_float2(__uint_as_float(r[c]), __uint_as_float(r[c + 1])));
 					o[c] = y.x;
 					o[c + 1] = y.y;
@@ -600,7 +603,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdPara
 					const float2 c1v = make_float2(c1, c1), mv = make_float2(-mlog, -mlog);
 #pragma unroll
 					for (int c = 0; c < kFwdCols; c += 2) {
-						const float2 x = __ffma2_rn(make_float2(sv[c], sv[c + 1]), c1v, mv);
+						const float2 x = fma2_rn(make_float2(sv[c], sv[c + 1]), c1v, mv);
 						const float e0 = exp2_hw(x.x), e1 = exp2_hw(x.y);
 						sv[c] = e0;
 						sv[c + 1] = e1;
@@ -613,7 +616,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdPara
 					const float2 c1v = make_float2(c1, c1), mv = make_float2(-mlog, -mlog);
 #pragma unroll
 					for (int c = 0; c < kFwdCols; c += 2) {
-						const float2 x = __ffma2_rn(make_float2(sv[c], sv[c + 1]), c1v, mv);
+						const float2 x = fma2_rn(make_float2(sv[c], sv[c + 1]), c1v, mv);
 						const bool lv0 = (live >> c) & 1u, pd0 = (padb >> c) & 1u;
 						const bool lv1 = (live >> (c + 1)) & 1u, pd1 = (padb >> (c + 1)) & 1u;
 						const float e0 = !lv0 ? 0.0f : exp2_hw(pd0 ? xpad : x.x);
@@ -651,8 +654,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) flash_fwd_kernel(const FwdPara
 				const float2 il2 = make_float2(inv_l, inv_l);
 #pragma unroll
 				for (int u = 0; u < kFwdHeadCols / 4; ++u) {
-					const float2 a = __fmul2_rn(make_float2(o[4 * u], o[4 * u + 1]), il2);
-					const float2 b2 = __fmul2_rn(make_float2(o[4 * u + 2], o[4 * u + 3]), il2);
+					const float2 a = mul2_rn(make_float2(o[4 * u], o[4 * u + 1]), il2);
+					const float2 b2 = mul2_rn(make_float2(o[4 * u + 2], o[4 * u + 3]), il2);
 					orow[u] = make_float4(a.x, a.y, b2.x, b2.y);
 				}
 				if (part == 0) {
@@ -943,10 +946,10 @@ __global__ void __launch_bounds__(kDqThreads, 1) flash_bwd_dq_kernel(const BwdPa
 						dv = make_float2(-drow, -drow), sc = make_float2(p.scale, p.scale);
 #pragma unroll
 					for (int c = 0; c < kDqCols; c += 2) {
-						const float2 x = __ffma2_rn(make_float2(__uint_as_float(rsv[c]), __uint_as_float(rsv[c + 1])), c1v, mv);
-						const float2 pr = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), ilv);
-						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])), dv);
-						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pr, t2));
+						const float2 x = fma2_rn(make_float2(__uint_as_float(rsv[c]), __uint_as_float(rsv[c + 1])), c1v, mv);
+						const float2 pr = mul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), ilv);
+						const float2 t2 = add2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])), dv);
+						const float2 d2 = mul2_rn(sc, mul2_rn(pr, t2));
 						ds[c] = d2.x;
 						ds[c + 1] = d2.y;
 					}
@@ -957,10 +960,10 @@ __global__ void __launch_bounds__(kDqThreads, 1) flash_bwd_dq_kernel(const BwdPa
 						dv = make_float2(-drow, -drow), sc = make_float2(p.scale, p.scale);
 #pragma unroll
 					for (int c = 0; c < kDqCols; c += 2) {
-						const float2 x = __ffma2_rn(make_float2(__uint_as_float(rsv[c]), __uint_as_float(rsv[c + 1])), c1v, mv);
-						const float2 pr = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), ilv);
-						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])), dv);
-						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pr, t2));
+						const float2 x = fma2_rn(make_float2(__uint_as_float(rsv[c]), __uint_as_float(rsv[c + 1])), c1v, mv);
+						const float2 pr = mul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), ilv);
+						const float2 t2 = add2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])), dv);
+						const float2 d2 = mul2_rn(sc, mul2_rn(pr, t2));
 						ds[c] = ((use >> c) & 1u) ? d2.x : 0.0f;
 						ds[c + 1] = ((use >> (c + 1)) & 1u) ? d2.y : 0.0f;
 					}
@@ -1199,13 +1202,13 @@ __global__ void __launch_bounds__(kKvThreads, 1) flash_bwd_dkdv_kernel(const Bwd
 					const float2 c1v = make_float2(c1, c1), l2e = make_float2(kLog2e, kLog2e), sc = make_float2(p.scale, p.scale);
 #pragma unroll
 					for (int c = 0; c < kKvCols; c += 2) {
-						const float2 ml = __fmul2_rn(make_float2(m_j[c], m_j[c + 1]), l2e);
-						const float2 x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), c1v,
+						const float2 ml = mul2_rn(make_float2(m_j[c], m_j[c + 1]), l2e);
+						const float2 x = fma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), c1v,
 							make_float2(-ml.x, -ml.y));
-						const float2 pv = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), make_float2(il_j[c], il_j[c + 1]));
-						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
+						const float2 pv = mul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), make_float2(il_j[c], il_j[c + 1]));
+						const float2 t2 = add2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
 							make_float2(-d_j[c], -d_j[c + 1]));
-						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pv, t2));
+						const float2 d2 = mul2_rn(sc, mul2_rn(pv, t2));
 						pr[c] = pv.x;
 						pr[c + 1] = pv.y;
 						ds[c] = d2.x;
@@ -1218,16 +1221,16 @@ __global__ void __launch_bounds__(kKvThreads, 1) flash_bwd_dkdv_kernel(const Bwd
 						const bool live0 = !p.causal || key <= qbeg + c, live1 = !p.causal || key <= qbeg + c + 1;
 						float2 x;
 						if (padded) {
-							x = __fmul2_rn(__fadd2_rn(make_float2(-1e9f, -1e9f), make_float2(-m_j[c], -m_j[c + 1])), l2e);
+							x = mul2_rn(add2_rn(make_float2(-1e9f, -1e9f), make_float2(-m_j[c], -m_j[c + 1])), l2e);
 						} else {
-							const float2 ml = __fmul2_rn(make_float2(m_j[c], m_j[c + 1]), l2e);
-							x = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), c1v,
+							const float2 ml = mul2_rn(make_float2(m_j[c], m_j[c + 1]), l2e);
+							x = fma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), c1v,
 								make_float2(-ml.x, -ml.y));
 						}
-						const float2 pv = __fmul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), make_float2(il_j[c], il_j[c + 1]));
-						const float2 t2 = __fadd2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
+						const float2 pv = mul2_rn(make_float2(exp2_hw(x.x), exp2_hw(x.y)), make_float2(il_j[c], il_j[c + 1]));
+						const float2 t2 = add2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])),
 							make_float2(-d_j[c], -d_j[c + 1]));
-						const float2 d2 = __fmul2_rn(sc, __fmul2_rn(pv, t2));
+						const float2 d2 = mul2_rn(sc, mul2_rn(pv, t2));
 						pr[c] = live0 ? pv.x : 0.0f;
 						pr[c + 1] = live1 ? pv.y : 0.0f;
 						ds[c] = (live0 && !padded) ? d2.x : 0.0f;

@@ -82,6 +82,126 @@ __global__ void layernorm_bwd_dx_kernel(const float* __restrict__ g, const float
 	}
 }
 
+// Four-per-lane forms for 16-byte aligned rows with D % 4 == 0 and D <= 128 kV: one warp per row as
+// above, the row held in registers (read from HBM once) and moved as float4; lane l owns the 16-byte
+// groups l, l + 32, ... and sums its elements in order before the same xor-shuffle tree. The
+// per-element expressions are those of the scalar kernels; the sums' grouping differs from theirs
+// (it is fixed by D, so the results are deterministic).
+template <int kV>
+__global__ void layernorm_fwd_vec_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
+		const float* __restrict__ beta, float eps, long long R, int D, float* __restrict__ y,
+		float* __restrict__ mean, float* __restrict__ inv_std) {
+	const int lane = threadIdx.x & 31;
+	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+	if (r >= R) return;
+	const int D4 = D >> 2;
+	const float4* row = reinterpret_cast<const float4*>(x + r * D);
+	float4 v[kV];
+	float s = 0.0f;
+#pragma unroll
+	for (int u = 0; u < kV; ++u) {
+		const int j = lane + 32 * u;
+		v[u] = j < D4 ? __ldg(row + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+		if (j < D4) {
+			s += v[u].x;
+			s += v[u].y;
+			s += v[u].z;
+			s += v[u].w;
+		}
+	}
+	s = warp_sum(s);
+	const float mu = s / (float)D;
+	float q = 0.0f;
+#pragma unroll
+	for (int u = 0; u < kV; ++u)
+		if (lane + 32 * u < D4) {
+			const float d0 = v[u].x - mu, d1 = v[u].y - mu, d2 = v[u].z - mu, d3 = v[u].w - mu;
+			q += d0 * d0;
+			q += d1 * d1;
+			q += d2 * d2;
+			q += d3 * d3;
+		}
+	q = warp_sum(q);
+	const float inv = 1.0f / sqrtf(q / (float)D + eps);
+	float4* o = reinterpret_cast<float4*>(y + r * D);
+	const float4* g4 = reinterpret_cast<const float4*>(gamma);
+	const float4* b4 = reinterpret_cast<const float4*>(beta);
+#pragma unroll
+	for (int u = 0; u < kV; ++u) {
+		const int j = lane + 32 * u;
+		if (j < D4) {
+			const float4 gm = __ldg(g4 + j), bt = __ldg(b4 + j);
+			o[j] = make_float4((v[u].x - mu) * inv * gm.x + bt.x, (v[u].y - mu) * inv * gm.y + bt.y,
+				(v[u].z - mu) * inv * gm.z + bt.z, (v[u].w - mu) * inv * gm.w + bt.w);
+		}
+	}
+	if (lane == 0) {
+		mean[r] = mu;
+		inv_std[r] = inv;
+	}
+}
+
+template <int kV>
+__global__ void layernorm_bwd_dx_vec_kernel(const float* __restrict__ g, const float* __restrict__ x,
+		const float* __restrict__ gamma, const float* __restrict__ mean, const float* __restrict__ inv_std,
+		long long R, int D, float* __restrict__ dx, int first) {
+	const int lane = threadIdx.x & 31;
+	const long long r = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+	if (r >= R) return;
+	const int D4 = D >> 2;
+	const float mu = mean[r], inv = inv_std[r];
+	const float4* gr = reinterpret_cast<const float4*>(g + r * D);
+	const float4* xr = reinterpret_cast<const float4*>(x + r * D);
+	const float4* g4 = reinterpret_cast<const float4*>(gamma);
+	float4 dh[kV], xh[kV];
+	float a = 0.0f, b = 0.0f;
+#pragma unroll
+	for (int u = 0; u < kV; ++u) {
+		const int j = lane + 32 * u;
+		if (j < D4) {
+			const float4 gv = __ldg(gr + j), xv = __ldg(xr + j), gm = __ldg(g4 + j);
+			dh[u] = make_float4(gv.x * gm.x, gv.y * gm.y, gv.z * gm.z, gv.w * gm.w);
+			xh[u] = make_float4((xv.x - mu) * inv, (xv.y - mu) * inv, (xv.z - mu) * inv, (xv.w - mu) * inv);
+			a += dh[u].x;
+			b += dh[u].x * xh[u].x;
+			a += dh[u].y;
+			b += dh[u].y * xh[u].y;
+			a += dh[u].z;
+			b += dh[u].z * xh[u].z;
+			a += dh[u].w;
+			b += dh[u].w * xh[u].w;
+		}
+	}
+	a = warp_sum(a);
+	b = warp_sum(b);
+	const float k = inv / (float)D, fd = (float)D;
+	float4* o = reinterpret_cast<float4*>(dx + r * D);
+#pragma unroll
+	for (int u = 0; u < kV; ++u) {
+		const int j = lane + 32 * u;
+		if (j < D4) {
+			float4 v = make_float4(k * (fd * dh[u].x - a - xh[u].x * b), k * (fd * dh[u].y - a - xh[u].y * b),
+				k * (fd * dh[u].z - a - xh[u].z * b), k * (fd * dh[u].w - a - xh[u].w * b));
+			if (first) {
+				v = make_float4(v.x + 0.0f, v.y + 0.0f, v.z + 0.0f, v.w + 0.0f);
+			} else {
+				const float4 c = o[j];
+				v = make_float4(c.x + v.x, c.y + v.y, c.z + v.z, c.w + v.w);
+			}
+			o[j] = v;
+		}
+	}
+}
+
+// Chooses the four-per-lane form (its register count kV) for a row length and pointers; 0: scalar.
+inline int layernorm_vec_width(int D, const void* p0, const void* p1, const void* p2, const void* p3) {
+	const uintptr_t m = reinterpret_cast<uintptr_t>(p0) | reinterpret_cast<uintptr_t>(p1) |
+		reinterpret_cast<uintptr_t>(p2) | reinterpret_cast<uintptr_t>(p3);
+	if (D % 4 != 0 || (m & 15) != 0 || D > 1024) return 0;
+	const int d4 = D / 4;
+	return d4 <= 32 ? 1 : d4 <= 64 ? 2 : d4 <= 128 ? 4 : 8;
+}
+
 constexpr int kChunk = 256;
 
 // Chunk partials of sum_r g*xhat (dgamma) and sum_r g (dbeta), serial within the chunk; group z
@@ -355,8 +475,15 @@ nnb_status nnb_layernorm_fwd(void* stream, size_t R, size_t D, const float* x, c
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	const long long threads = (long long)R * 32;
 	nnb::TraceScope ts(s, nnb::kTraceRowwise);
-	nnb::layernorm_fwd_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, gamma, beta, eps, (long long)R,
-		(int)D, y, mean, inv_std);
+	const unsigned blocks = (unsigned)((threads + 255) / 256);
+	switch (nnb::layernorm_vec_width((int)D, x, y, gamma, beta)) {
+	case 1: nnb::layernorm_fwd_vec_kernel<1><<<blocks, 256, 0, s>>>(x, gamma, beta, eps, (long long)R, (int)D, y, mean, inv_std); break;
+	case 2: nnb::layernorm_fwd_vec_kernel<2><<<blocks, 256, 0, s>>>(x, gamma, beta, eps, (long long)R, (int)D, y, mean, inv_std); break;
+	case 4: nnb::layernorm_fwd_vec_kernel<4><<<blocks, 256, 0, s>>>(x, gamma, beta, eps, (long long)R, (int)D, y, mean, inv_std); break;
+	case 8: nnb::layernorm_fwd_vec_kernel<8><<<blocks, 256, 0, s>>>(x, gamma, beta, eps, (long long)R, (int)D, y, mean, inv_std); break;
+	default:
+		nnb::layernorm_fwd_kernel<<<blocks, 256, 0, s>>>(x, gamma, beta, eps, (long long)R, (int)D, y, mean, inv_std);
+	}
 	return nnb::cuda_status(cudaGetLastError(), "layernorm_fwd launch");
 }
 
@@ -370,8 +497,19 @@ nnb_status nnb_layernorm_bwd_grouped(void* stream, size_t R, size_t D, size_t gr
 	if (dx) {
 		const long long threads = (long long)R * 32;
 		nnb::TraceScope ts(s, nnb::kTraceRowwise);
-		nnb::layernorm_bwd_dx_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(g, x, gamma, mean, inv_std,
-			(long long)R, (int)D, dx, dx_first);
+		const unsigned blocks = (unsigned)((threads + 255) / 256);
+		const int vw = nnb::layernorm_vec_width((int)D, g, x, gamma, dx);
+		if (vw == 1)
+			nnb::layernorm_bwd_dx_vec_kernel<1><<<blocks, 256, 0, s>>>(g, x, gamma, mean, inv_std, (long long)R, (int)D, dx, dx_first);
+		else if (vw == 2)
+			nnb::layernorm_bwd_dx_vec_kernel<2><<<blocks, 256, 0, s>>>(g, x, gamma, mean, inv_std, (long long)R, (int)D, dx, dx_first);
+		else if (vw == 4)
+			nnb::layernorm_bwd_dx_vec_kernel<4><<<blocks, 256, 0, s>>>(g, x, gamma, mean, inv_std, (long long)R, (int)D, dx, dx_first);
+		else if (vw == 8)
+			nnb::layernorm_bwd_dx_vec_kernel<8><<<blocks, 256, 0, s>>>(g, x, gamma, mean, inv_std, (long long)R, (int)D, dx, dx_first);
+		else
+			nnb::layernorm_bwd_dx_kernel<<<blocks, 256, 0, s>>>(g, x, gamma, mean, inv_std, (long long)R, (int)D, dx,
+				dx_first);
 		NNB_CUDA_TRY(cudaGetLastError());
 	}
 	if (dgamma || dbeta) {

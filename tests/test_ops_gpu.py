@@ -336,6 +336,54 @@ def test_maxpool_bitwise(cuda, k, stride, shape):
     assert_bits(host(dx), dx_o)
 
 
+GELU_SPECIALS = [np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-40, -1e-40, 1e-30, -3e-39, 4.4, -4.4, 4.6, -4.6, 9.0,
+                 -9.0, 43.6, -43.7, 88.0, 1e30, -1e30, 3.0e38, -3.0e38, 0.5, -0.5]
+
+
+def assert_bits_or_both_nan(got, want):
+    """Bitwise equal, except that a NaN's payload is not compared (the GPU's arithmetic returns its
+    canonical NaN where the host's propagates the operand's)."""
+    got, want = np.asarray(got, np.float32).ravel(), np.asarray(want, np.float32).ravel()
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan)
+    assert got[~nan].tobytes() == want[~nan].tobytes()
+
+
+def test_gelu_vector_paths_bitwise(cuda):
+    """The four-per-thread GELU kernels (packed fp32 pairs) against the reference's loops bit for bit:
+    the backward with the tanh given and recomputed (nnb_gelu_bwd, length a multiple of 4), and the
+    forward after linear_gelu's GEMM (its pre-activation set to special values through the bias and a
+    zero input) against the scalar nnb_gelu_fwd of the same pre-activation. Specials: NaN, infinities,
+    signed zeros, subnormals, values at the tanh clamp and past exp's range."""
+    torch = cuda
+    n = 100000
+    x, g = rnd(41, n, lo=-12, hi=12), rnd(42, n)
+    x[:len(GELU_SPECIALS)] = np.array(GELU_SPECIALS, np.float32)
+    x[-len(GELU_SPECIALS):] = np.array(GELU_SPECIALS[::-1], np.float32)
+    y_o, th_o, dx_o = orc.zeros(n), orc.zeros(n), orc.zeros(n)
+    O.orc_gelu_fwd(n, P(x), P(y_o), P(th_o))
+    O.orc_gelu_bwd(n, P(x), P(th_o), P(g), P(dx_o), 1)
+    tx, tg, tth = dev(torch, x), dev(torch, g), dev(torch, th_o)
+    dx = torch.empty(n, device="cuda")
+    ok(lib().nnb_gelu_bwd(S(torch), n, tx.data_ptr(), tth.data_ptr(), tg.data_ptr(), dx.data_ptr(), 1))
+    assert_bits_or_both_nan(host(dx), dx_o)
+    ok(lib().nnb_gelu_bwd(S(torch), n, tx.data_ptr(), None, tg.data_ptr(), dx.data_ptr(), 1))
+    assert_bits_or_both_nan(host(dx), dx_o)
+    # forward: pre = 0 . w^T + b = b (the epilogue stores acc + 0, then adds the bias)
+    M, K, cols = 3, 8, 1024
+    b = rnd(43, cols, lo=-12, hi=12)
+    b[:len(GELU_SPECIALS)] = np.array(GELU_SPECIALS, np.float32)
+    xz, w, tb = torch.zeros(M, K, device="cuda"), dev(torch, rnd(44, cols, K)), dev(torch, b)
+    y, pre = torch.empty(M, cols, device="cuda"), torch.empty(M, cols, device="cuda")
+    ok(lib().nnb_linear_gelu_fwd(S(torch), M, K, cols, xz.data_ptr(), w.data_ptr(), tb.data_ptr(), y.data_ptr(),
+                                 pre.data_ptr()))
+    ys, ths = torch.empty(M * cols, device="cuda"), torch.empty(M * cols, device="cuda")
+    ok(lib().nnb_gelu_fwd(S(torch), M * cols, pre.data_ptr(), ys.data_ptr(), ths.data_ptr()))
+    assert_bits_or_both_nan(host(y), host(ys))
+    assert np.isnan(host(y)[0, 0]) and np.isinf(host(pre)[0, 1])
+    assert nnb.device_error() == 0
+
+
 def test_gelu_relu_bitwise(cuda):
     torch = cuda
     n = 100003
