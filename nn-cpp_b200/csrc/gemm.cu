@@ -1174,33 +1174,33 @@ __device__ __forceinline__ float depth_zero_fix(float a) { return a + 0.0f; }
 __device__ __forceinline__ float4 depth_zero_fix(float4 a) { return f4_add(a, make_float4(0.0f, 0.0f, 0.0f, 0.0f)); }
 
 // c_e = (accumulate ? c_e : 0) + (((part_e0 + part_e1) + part_e2) + ...), part_ep an m x n slab;
-// entry e = blockIdx.z, c_e = c + e * sc. V = float or float4 (4 consecutive columns, when n, ldc and
-// the pointers allow). Up to 8 pieces' loads are issued before their adds, which stay in piece order.
+// entry e = blockIdx.y, c_e = c + e * sc. V = float or float4 (4 consecutive columns, when n, ldc and
+// the pointers allow). A grid-stride walk over the entry's m x (n / W) vectors, so every thread is busy
+// whatever the width; up to 8 pieces' loads are issued before their adds, which stay in piece order.
 template <typename V>
 __global__ void depth_sum_kernel(const float* __restrict__ part, int pieces, long long m, long long n,
 		float* __restrict__ c, long long ldc, long long sc, int accumulate) {
 	constexpr int W = sizeof(V) / sizeof(float);
-	const long long mn = m * n, nv = n / W;
-	part += (long long)blockIdx.z * pieces * mn;
-	c += (long long)blockIdx.z * sc;
-	for (long long i = blockIdx.y; i < m; i += gridDim.y) {
-		for (long long jv = blockIdx.x * (long long)blockDim.x + threadIdx.x; jv < nv;
-				jv += (long long)gridDim.x * blockDim.x) {
-			const V* src = reinterpret_cast<const V*>(part + i * n) + jv;
-			const long long stride = mn / W;                 // one slab, in V units
-			V acc{};
-			for (int p = 0; p < pieces; p += 8) {
-				V v[8];
+	const long long mn = m * n, nv = n / W, total = m * nv;
+	part += (long long)blockIdx.y * pieces * mn;
+	c += (long long)blockIdx.y * sc;
+	const long long stride = mn / W;                 // one slab, in V units
+	for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+			idx += (long long)gridDim.x * blockDim.x) {
+		const long long i = idx / nv, jv = idx - i * nv;
+		const V* src = reinterpret_cast<const V*>(part + i * n) + jv;
+		V acc{};
+		for (int p = 0; p < pieces; p += 8) {
+			V v[8];
 #pragma unroll
-				for (int u = 0; u < 8; ++u)
-					if (p + u < pieces) v[u] = __ldg(src + (long long)(p + u) * stride);
+			for (int u = 0; u < 8; ++u)
+				if (p + u < pieces) v[u] = __ldg(src + (long long)(p + u) * stride);
 #pragma unroll
-				for (int u = 0; u < 8; ++u)
-					if (p + u < pieces) acc = (p + u == 0) ? depth_v(v[u]) : depth_add(acc, v[u]);
-			}
-			V* dst = reinterpret_cast<V*>(c + i * ldc) + jv;
-			*dst = accumulate ? depth_add(*dst, acc) : depth_zero_fix(acc);
+			for (int u = 0; u < 8; ++u)
+				if (p + u < pieces) acc = (p + u == 0) ? depth_v(v[u]) : depth_add(acc, v[u]);
 		}
+		V* dst = reinterpret_cast<V*>(c + i * ldc) + jv;
+		*dst = accumulate ? depth_add(*dst, acc) : depth_zero_fix(acc);
 	}
 }
 
@@ -1247,16 +1247,17 @@ static nnb_status gemm_depth_cut(cudaStream_t s, const DeviceState* dev, const G
 		const bool vec = d.n % 4 == 0 && d.ldc % 4 == 0 && d.sc_outer % 4 == 0 &&
 			(reinterpret_cast<uintptr_t>(d.c) & 15) == 0;
 		const long long nv = vec ? d.n / 4 : d.n;
-		const unsigned bx = (unsigned)std::min<long long>((nv + 255) / 256, 64);
-		const unsigned by = (unsigned)std::min<long long>(d.m, std::max<long long>(1, (148 * 16) / ((long long)bx * E)));
+		// about 16 blocks per SM over all entries, no more blocks than an entry has vectors
+		const unsigned bx = (unsigned)std::max<long long>(1, std::min<long long>((d.m * nv + 255) / 256,
+			std::max<long long>(1, (148 * 16) / E)));
 		{
 			TraceScope ts(s, kTraceAux);
 			if (vec)
-				depth_sum_kernel<float4><<<dim3(bx, std::max(by, 1u), (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n,
-					d.c, d.ldc, d.sc_outer, d.accumulate);
+				depth_sum_kernel<float4><<<dim3(bx, (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc,
+					d.sc_outer, d.accumulate);
 			else
-				depth_sum_kernel<float><<<dim3(bx, std::max(by, 1u), (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n,
-					d.c, d.ldc, d.sc_outer, d.accumulate);
+				depth_sum_kernel<float><<<dim3(bx, (unsigned)E), 256, 0, s>>>(part, pieces, d.m, d.n, d.c, d.ldc,
+					d.sc_outer, d.accumulate);
 		}
 		st = cuda_status(cudaGetLastError(), "depth sum launch");
 	} while (0);
