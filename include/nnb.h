@@ -394,9 +394,9 @@ NNB_API nnb_status nnb_adamw_step_device(void* stream, size_t n, float* w, const
  * not ours to call. The caller still passes A, B and C; the packed operands and flags go into a
  * fixed 32 MiB device array that every GPU loading this library holds until the process exits.
  *
- * - Limit: (roundup(m,128) + roundup(n,256)) * roundup(k,16) * S * 4 bytes of packed operands plus
- *   a few KB of flags must fit in 32 MiB (S = 2 in NNB_MATH_FP32X3, 1 in NNB_MATH_TF32); e.g.
- *   1024 x 1024 x 1024 in 3xTF32 uses 16 MiB. Larger calls return NNB_ERR_UNSUPPORTED and
+ * - Limit: (roundup(m,128) * roundup(k,32) + roundup(n,256) * roundup(k,16)) * S * 4 bytes of
+ *   packed operands plus a few KB of flags must fit in 32 MiB (S = 2 in NNB_MATH_FP32X3, 1 in
+ *   NNB_MATH_TF32); e.g. 1024 x 1024 x 1024 in 3xTF32 uses 16 MiB. Larger calls return NNB_ERR_UNSUPPORTED and
  *   enqueue nothing.
  * - The first call on a device (with that device current) looks up the array's device address and
  *   sets kernel attributes; make that first call before any stream capture.

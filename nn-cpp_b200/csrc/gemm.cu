@@ -33,6 +33,7 @@ namespace gemm {
 constexpr int kBM = 128;                 // rows of C per tile (MMA M)
 constexpr int kBK = 16;                  // floats of depth per pipeline stage (one 64 B row)
 constexpr int kAPanelRows = 128;         // rows per packed panel of A
+constexpr int kAPanelWidth = 32;         // floats per packed row of A (two 16-deep k-blocks; B rows hold one)
 constexpr int kGroupM = 16;              // tiles of M walked together for L2 reuse of B
 constexpr int kThreads = 192;            // TMA producer, MMA issuer, 4 epilogue warps
 constexpr int kGatherThreads = 128;      // + 4 warps that gather B into the stages (implicit GEMM)
@@ -86,7 +87,7 @@ struct Params {
 	long long ld_aux, s_aux_outer, s_aux_inner;
 	// exact IEEE handling of non-finite inputs
 	const int* any_nonfinite;
-	const int* any_b;                // B's any-flag (the same word unless B came packed)
+	const int* any_b;                // B's any-flag
 	const int* flags_a;              // [a_batches][Mp]
 	const int* flags_b;              // [b_batches][Np]
 	const float* A;
@@ -99,18 +100,24 @@ struct Params {
 	GemmGather g;
 	int* gflags_b;                   // writable view of flags_b
 	int* gany_b;                     // writable view of any_b
+	// operands read MN-major from kept row packs (kernel variant kMn): batch entry bi's depth q is
+	// row r0 + (bi / batch_inner) * r_outer + (bi % batch_inner) * r_inner + q of the packed matrix
+	long long ra0, ra_outer, ra_inner, rb0, rb_outer, rb_inner;
 };
 
 // ---------------------------------------------------------------------------------------------
 // Pack
 // ---------------------------------------------------------------------------------------------
 
+// Panel layout: panels of `panel_rows` rows x `pw` floats (pw = 16 for B, 32 for A), panel (rb, c)
+// holding rows rb*panel_rows .. and depths c*pw .., stored as panel index (rb * KW + c) * S + part
+// (part 0 = hi, 1 = lo); KW = panel columns over the padded depth (zero beyond K).
 // One block: 32 rows x 64 depth of op(X) (X stored rows x K, or K x rows when trans), written
 // as 4 k-blocks of the packed panel layout with `panel_rows`-row panels.
-// grid = (Rp/32, ceil(Kp/64), batch entries); entry e reads X + (e / inner)*s_outer + (e % inner)*s_inner.
+// grid = (Rp/32, ceil(KW*pw/64), batch entries); entry e reads X + (e / inner)*s_outer + (e % inner)*s_inner.
 template <int kSplit>
 __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, long long ldx,
-		long long s_outer, long long s_inner, int inner, int trans, int R, int K, int Rp, int KB,
+		long long s_outer, long long s_inner, int inner, int trans, int R, int K, int Rp, int KW, int pw,
 		int panel_rows, float* __restrict__ out, int* __restrict__ flags, int* __restrict__ any_flag) {
 	constexpr int S = kSplit ? 2 : 1;
 	__shared__ float tile[32][65];
@@ -135,13 +142,14 @@ __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, 
 	__syncthreads();
 	const int q = 2 * t;                 // element pair inside a 32 x 16 k-block slab
 	const int rl = q >> 4, kl = q & 15;
-	const long long batch_off = (long long)e * Rp * KB * 16 * S;
-	const int panel_floats = panel_rows * 16;
+	const long long batch_off = (long long)e * Rp * KW * pw * S;
+	const int panel_floats = panel_rows * pw;
+	const int kbs = KW * pw / 16;        // 16-deep blocks of the padded depth
 	bool bad = false;
 #pragma unroll
 	for (int w = 0; w < 4; ++w) {
 		const int kb = (k0 >> 4) + w;
-		if (kb >= KB) break;
+		if (kb >= kbs) break;
 		const float x0 = tile[rl][w * 16 + kl], x1 = tile[rl][w * 16 + kl + 1];
 		const bool f0 = isfinite(x0), f1 = isfinite(x1);
 		bad |= !(f0 && f1);
@@ -154,8 +162,9 @@ __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, 
 			h1 = to_tf32(f1 ? x1 : 0.0f);
 			l0 = l1 = 0.0f;
 		}
-		const long long panel = ((long long)(r0 / panel_rows) * KB + kb) * S;
-		float* dst = out + batch_off + panel * panel_floats + (r0 % panel_rows) * 16 + q;
+		const int k = kb * 16 + kl;
+		const long long panel = ((long long)(r0 / panel_rows) * KW + k / pw) * S;
+		float* dst = out + batch_off + panel * panel_floats + (r0 % panel_rows + rl) * pw + (k % pw);
 		*reinterpret_cast<float2*>(dst) = make_float2(h0, h1);
 		if (kSplit) *reinterpret_cast<float2*>(dst + panel_floats) = make_float2(l0, l1);
 	}
@@ -170,15 +179,15 @@ __global__ void __launch_bounds__(256) pack_kernel(const float* __restrict__ X, 
 // 16 contiguous bytes in both layouts). grid = (blocks, batch entries), grid-stride over Rp * KB * 4.
 template <int kSplit>
 __global__ void __launch_bounds__(256) pack_rows_vec_kernel(const float* __restrict__ X, long long ldx,
-		long long s_outer, long long s_inner, int inner, int R, int K, int Rp, int KB, int panel_rows,
+		long long s_outer, long long s_inner, int inner, int R, int K, int Rp, int KW, int pw, int panel_rows,
 		float* __restrict__ out, int* __restrict__ flags, int* __restrict__ any_flag) {
 	constexpr int S = kSplit ? 2 : 1;
 	const int e = blockIdx.y;
 	const float* Xb = X + (long long)(e / inner) * s_outer + (long long)(e % inner) * s_inner;
-	// Rp * KB * 4 < 2^31 (checked on the host), so the index arithmetic stays in 32 bits
-	const unsigned K4 = (unsigned)KB * 4u, total = (unsigned)Rp * K4;
-	const long long batch_off = (long long)e * Rp * KB * 16 * S;
-	const int panel_floats = panel_rows * 16;
+	// Rp * KW * pw / 4 < 2^31 (checked on the host), so the index arithmetic stays in 32 bits
+	const unsigned K4 = (unsigned)(KW * pw / 4), total = (unsigned)Rp * K4;
+	const long long batch_off = (long long)e * Rp * KW * pw * S;
+	const int panel_floats = panel_rows * pw;
 	for (unsigned idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
 		const int r = (int)(idx / K4), q = (int)(idx - (unsigned)r * K4), k = q * 4;
 		float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -201,9 +210,8 @@ __global__ void __launch_bounds__(256) pack_rows_vec_kernel(const float* __restr
 		} else {
 			h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
 		}
-		const int kb = q >> 2;
-		const long long panel = ((long long)(r / panel_rows) * KB + kb) * S;
-		float* dst = out + batch_off + panel * panel_floats + (r % panel_rows) * 16 + (q & 3) * 4;
+		const long long panel = ((long long)(r / panel_rows) * KW + k / pw) * S;
+		float* dst = out + batch_off + panel * panel_floats + (r % panel_rows) * pw + (k % pw);
 		*reinterpret_cast<float4*>(dst) = h;
 		if (kSplit) *reinterpret_cast<float4*>(dst + panel_floats) = l;
 	}
@@ -214,7 +222,7 @@ __global__ void __launch_bounds__(256) pack_rows_vec_kernel(const float* __restr
 // and written as float4 groups of 4 consecutive k. grid = (ceil(Rp/64), ceil(Kp/32), batch entries).
 template <int kSplit>
 __global__ void __launch_bounds__(256) pack_cols_vec_kernel(const float* __restrict__ X, long long ldx,
-		long long s_outer, long long s_inner, int inner, int R, int K, int Rp, int KB, int panel_rows,
+		long long s_outer, long long s_inner, int inner, int R, int K, int Rp, int KW, int pw, int panel_rows,
 		float* __restrict__ out, int* __restrict__ flags, int* __restrict__ any_flag) {
 	constexpr int S = kSplit ? 2 : 1;
 	__shared__ float tile[64][33];
@@ -234,14 +242,14 @@ __global__ void __launch_bounds__(256) pack_cols_vec_kernel(const float* __restr
 		tile[r4 + 3][kk] = v.w;
 	}
 	__syncthreads();
-	const long long batch_off = (long long)e * Rp * KB * 16 * S;
-	const int panel_floats = panel_rows * 16;
+	const long long batch_off = (long long)e * Rp * KW * pw * S;
+	const int panel_floats = panel_rows * pw;
 #pragma unroll
 	for (int i = 0; i < 2; ++i) {
 		const int f = t + 256 * i;                // (row, k-quad) pairs: 64 rows x 8 quads
 		const int rl = f >> 3, q = f & 7;
-		const int gr = r0 + rl, k = k0 + q * 4, kb = k >> 4;
-		if (kb >= KB || gr >= Rp) continue;
+		const int gr = r0 + rl, k = k0 + q * 4;
+		if (k >= KW * pw || gr >= Rp) continue;
 		float4 v = make_float4(tile[rl][q * 4], tile[rl][q * 4 + 1], tile[rl][q * 4 + 2], tile[rl][q * 4 + 3]);
 		const bool ok = isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
 		if (!ok) {
@@ -261,8 +269,8 @@ __global__ void __launch_bounds__(256) pack_cols_vec_kernel(const float* __restr
 		} else {
 			h = make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
 		}
-		const long long panel = ((long long)(gr / panel_rows) * KB + kb) * S;
-		float* dst = out + batch_off + panel * panel_floats + (gr % panel_rows) * 16 + (k & 15);
+		const long long panel = ((long long)(gr / panel_rows) * KW + k / pw) * S;
+		float* dst = out + batch_off + panel * panel_floats + (gr % panel_rows) * pw + (k % pw);
 		*reinterpret_cast<float4*>(dst) = h;
 		if (kSplit) *reinterpret_cast<float4*>(dst + panel_floats) = l;
 	}
@@ -498,10 +506,16 @@ __device__ __noinline__ float nonfinite_result(const Params& p, int bi, int i, i
 // four 128 x 256 x 8 MMAs instead of 24 KB for two: a third less operand traffic per MMA, and the
 // 192 KB of stages hold 1.5x the tensor time. The cost: no accumulator double buffering (the next
 // tile's MMAs wait for both halves' epilogues). Each element's arithmetic is the narrow kernel's.
-template <int kSplit, int kBN, int kGather, int kWide = 0>
+// kMn (no gather, no wide tiles): bit 0 -- A is read MN-major from a kept row pack (its 128 rows are
+// 4 chunks of 32 packed depths, each chunk 16 packed rows of 128 bytes, the 128-byte swizzle with
+// 32-byte atoms that TMA writes with CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B); bit 1 -- the same for B.
+// Such an operand has no per-row flags: when its pack saw a non-finite value every element is
+// recomputed by nonfinite_result.
+template <int kSplit, int kBN, int kGather, int kWide = 0, int kMn = 0>
 __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a,
 		const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ Params p) {
 	static_assert(!kWide || (!kGather && kBN == 256), "wide tiles: no gather, 256 columns");
+	static_assert(!kMn || (!kGather && !kWide), "MN-major operands: no gather, no wide tiles");
 	constexpr int kAM = kWide ? 2 : 1;
 	constexpr int kKPS = kblocks_per_stage(kSplit, kGather, kWide);
 	using C = Cfg<kSplit, kBN, kKPS, kAM>;
@@ -541,6 +555,7 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 
 	const int num_tiles = p.batch * (p.tiles_m / kAM) * p.tiles_n;      // work items
 	const int a_panels = p.Mp / kAPanelRows, b_panels = p.Np / C::kBPanelRows;
+	const int kwa = (p.KB + 1) >> 1;          // packed 32-wide columns of A
 
 	if (warp == 0) {
 		if (lane == 0) {
@@ -565,15 +580,35 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 						if (g >= nkb) break;
 						const int kb = kb0 + g;
 						const uint32_t base = smem_u32(smem + stage * C::kStageBytes + g * C::kKBlockBytes);
-#pragma unroll
-						for (int h = 0; h < kAM; ++h) {
-							const int ya = (int)((((long long)ab * a_panels + mt + h) * p.KB + kb) * S * kAPanelRows);
+						if (kMn & 1) {
+							// 4 chunks of 32 depths of the kept pack = this tile's 128 rows, at 16 packed rows
+							const long long r = p.ra0 + (long long)(bi / p.batch_inner) * p.ra_outer +
+								(long long)(bi % p.batch_inner) * p.ra_inner + (long long)kb * kBK;
 #pragma unroll
 							for (int s = 0; s < S; ++s)
-								tma_load_2d(base + (h * S + s) * (kAPanelRows * kBK * 4), &tm_a, fb, 0, ya + s * kAPanelRows);
+								tma_load_5d(base + s * (kAPanelRows * kBK * 4), &tm_a, fb, 0, (int)(r % kAPanelRows), s,
+									mt * (kBM / 32), (int)(r / kAPanelRows));
+						} else {
+#pragma unroll
+							for (int h = 0; h < kAM; ++h) {
+								// 32-wide A rows: k-block kb is the (kb & 1) half of packed column kb / 2
+								const int ya = (int)((((long long)ab * a_panels + mt + h) * kwa + (kb >> 1)) * S * kAPanelRows);
+#pragma unroll
+								for (int s = 0; s < S; ++s)
+									tma_load_2d(base + (h * S + s) * (kAPanelRows * kBK * 4), &tm_a, fb, (kb & 1) * kBK,
+										ya + s * kAPanelRows);
+							}
+						}
+						if (kMn & 2) {
+							const long long r = p.rb0 + (long long)(bi / p.batch_inner) * p.rb_outer +
+								(long long)(bi % p.batch_inner) * p.rb_inner + (long long)kb * kBK;
+#pragma unroll
+							for (int s = 0; s < S; ++s)
+								tma_load_5d(base + C::kABytes + s * C::kBPartBytes, &tm_b, fb, 0, (int)(r % kAPanelRows), s,
+									nt * (kBN / 32), (int)(r / kAPanelRows));
 						}
 #pragma unroll
-						for (int q = 0; q < (kGather ? 0 : C::kBPanels); ++q) {
+						for (int q = 0; q < ((kGather || (kMn & 2)) ? 0 : C::kBPanels); ++q) {
 							const long long panel = (long long)bb * b_panels + (long long)nt * C::kBPanels + q;
 							const int yb = (int)((panel * p.KB + kb) * S * C::kBPanelRows);
 #pragma unroll
@@ -594,7 +629,8 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 		// --------------------- MMA issuer (the whole warp; one elected lane issues) ---------------------
 		// accumulator v (the v-th 128-row tile this CTA hands to the epilogue) lives in buffer v & 1; a
 		// wide work item fills two of them, one per 128-row half
-		constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
+		constexpr uint32_t idesc = idesc_tf32(kBM, kBN) | ((kMn & 1) ? kIdescAMajorMN : 0u) |
+			((kMn & 2) ? kIdescBMajorMN : 0u);
 		int stage = 0;
 		uint32_t phase = 0;
 		int it = 0;
@@ -622,17 +658,25 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 					const uint32_t base = smem_u32(smem + stage * C::kStageBytes + g * C::kKBlockBytes);
 #pragma unroll
 					for (int kk = 0; kk < kBK / 8; ++kk) {
-						const uint32_t off = kk * 32;    // 8 tf32 = 32 bytes along the swizzled row
-						const uint64_t b_hi = smem_desc_k_sw64(base + C::kABytes + off);
+						// K-major: 8 tf32 = 32 bytes along the swizzled row; MN-major: 8 rows of 128 bytes,
+						// the next 32 rows (or columns) of C one 2 KB chunk further on
+						const uint32_t off = kk * 32, off_mn = kk * 1024;
+						const uint64_t b_hi = (kMn & 2) ? smem_desc_mn_sw128b32(base + C::kABytes + off_mn, 2048)
+							: smem_desc_k_sw64(base + C::kABytes + off);
 						const uint32_t first = (kb == 0 && kk == 0) ? 0u : 1u;
 #pragma unroll
 						for (int h = 0; h < kAM; ++h) {
 							const uint32_t d_tmem = tmem_base + ((it + h) & 1) * kBN;
 							const uint32_t abase = base + h * S * (kAPanelRows * kBK * 4);
-							const uint64_t a_hi = smem_desc_k_sw64(abase + off);
+							const uint64_t a_hi = (kMn & 1) ? smem_desc_mn_sw128b32(abase + off_mn, 2048)
+								: smem_desc_k_sw64(abase + off);
 							if (kSplit) {
-								const uint64_t a_lo = smem_desc_k_sw64(abase + kAPanelRows * kBK * 4 + off);
-								const uint64_t b_lo = smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
+								const uint64_t a_lo = (kMn & 1)
+									? smem_desc_mn_sw128b32(abase + kAPanelRows * kBK * 4 + off_mn, 2048)
+									: smem_desc_k_sw64(abase + kAPanelRows * kBK * 4 + off);
+								const uint64_t b_lo = (kMn & 2)
+									? smem_desc_mn_sw128b32(base + C::kABytes + C::kBPartBytes + off_mn, 2048)
+									: smem_desc_k_sw64(base + C::kABytes + C::kBPartBytes + off);
 								mma_tf32_elect(d_tmem, a_lo, b_hi, idesc, first);
 								mma_tf32_elect(d_tmem, a_hi, b_lo, idesc, 1u);
 								mma_tf32_elect(d_tmem, a_hi, b_hi, idesc, 1u);
@@ -772,7 +816,7 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 			};
 			// a gathered B's flags are set during this kernel (by atomics, at L2): read them past L1
 			const bool fix = (*p.any_nonfinite | (kGather ? __ldcg(p.any_b) : *p.any_b)) != 0;
-			const bool row_bad = fix && row_ok && p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0;
+			const bool row_bad = fix && row_ok && ((kMn & 1) || p.flags_a[(long long)(p.a_batched ? bi : 0) * p.Mp + gm] != 0);
 			const int* fcol = p.flags_b + (long long)(p.b_batched ? bi : 0) * p.Np;
 			const float* bias_e = p.bias + (long long)(bi / p.batch_inner) * p.s_bias_outer;
 			const float row_bias = (p.bias_mode == kBiasRow && row_ok) ? bias_e[gm] : 0.0f;
@@ -795,7 +839,7 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 #pragma unroll
 					for (int j = 0; j < 32; ++j) {
 						const int gn = gn0 + j;
-						if (gn < p.N && (row_bad || (kGather ? __ldcg(fcol + gn) : fcol[gn]) != 0))
+						if (gn < p.N && (row_bad || (kMn & 2) || (kGather ? __ldcg(fcol + gn) : fcol[gn]) != 0))
 							v[j] = nonfinite_result(p, bi, gm, gn, v[j]);
 					}
 				}
@@ -928,31 +972,62 @@ static int choose_bn(long long m, long long n, long long entries, int sms) {
 	return best;
 }
 
-static bool g_attr_set[64][2][4][2][2];
+static bool g_attr_set[64][2][4][2][2][4];
 static std::mutex g_attr_mutex;
 
 template <int kSplit, int kBN, int kGather, int kWide>
 using KernelCfg = Cfg<kSplit, kBN, kblocks_per_stage(kSplit, kGather, kWide), kWide ? 2 : 1>;
 
-template <int kSplit, int kBN, int kGather = 0, int kWide = 0>
+template <int kSplit, int kBN, int kGather = 0, int kWide = 0, int kMn = 0>
 static nnb_status set_smem_attr(int dev) {
 	const int bi = kBN == 64 ? 0 : kBN == 128 ? 1 : kBN == 224 ? 3 : 2;
 	std::lock_guard<std::mutex> lock(g_attr_mutex);
-	if (g_attr_set[dev & 63][kSplit][bi][kGather][kWide]) return NNB_OK;
-	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN, kGather, kWide>,
+	if (g_attr_set[dev & 63][kSplit][bi][kGather][kWide][kMn]) return NNB_OK;
+	NNB_CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<kSplit, kBN, kGather, kWide, kMn>,
 		cudaFuncAttributeMaxDynamicSharedMemorySize, KernelCfg<kSplit, kBN, kGather, kWide>::kSmemBytes));
-	g_attr_set[dev & 63][kSplit][bi][kGather][kWide] = true;
+	g_attr_set[dev & 63][kSplit][bi][kGather][kWide][kMn] = true;
 	return NNB_OK;
 }
 
-// Scratch layout of one product: packed A, packed B, then the non-finite flags.
+// Scratch layout of one product: packed A, packed B, then the non-finite flags (A's, B's, then the
+// two any-flags) -- each part only when it lives in the scratch (not in a kept, pre-packed or
+// MN-major-read pack).
 struct Plan {
 	int S, bn, b_panel_rows;
 	int wide;                                 // 256 x 256 TF32 tiles (rows padded to 256)
-	long long Mp, Np, Kp, KB, entries, a_entries, b_entries;
-	long long rows_a, rows_b;                 // packed 16-float rows of each operand
+	int mn;                                   // bit 0: A, bit 1: B read MN-major from kept row packs
+	long long Mp, Np, Kp, KB, KWA, entries, a_entries, b_entries;
+	long long rows_a, rows_b;                 // packed rows of each operand (A: 32 floats, B: 16 floats)
+	long long ra0, ra_outer, ra_inner, rb0, rb_outer, rb_inner;
 	size_t off_b, off_f, flag_ints, total;
 };
+
+// Kept row pack of a rows x cols matrix: panel bytes, then round_up(rows, 256) flags and the any-flag.
+static long long row_pack_rows(long long rows) { return round_up(rows, 2 * kBM); }
+static size_t row_pack_panel_bytes(long long rows, long long cols, int S) {
+	return (size_t)round_up(row_pack_rows(rows) * round_up(cols, kAPanelWidth) * S * 4, 1024);
+}
+static int* row_pack_flags(const void* buf, long long rows, long long cols, int S) {
+	return reinterpret_cast<int*>(static_cast<unsigned char*>(const_cast<void*>(buf)) + row_pack_panel_bytes(rows, cols, S));
+}
+
+// Whether operand X (A through mn_a, stored K x m with ta = 1; B through mn_b, stored K x n with
+// tb = 0) can be read from the kept row pack r: every batch entry X_e = x + o*s_outer + i*s_inner
+// must start in column 0 of the packed matrix on a 16-row boundary, the depth must be whole
+// 16-row blocks (so no k-block reaches past its entry), and the rows and `width` columns it covers
+// must lie inside the pack. Gives the entries' first rows.
+static bool mn_usable(const GemmDesc& d, const GemmRowPack& r, const float* x, long long ld, long long s_outer,
+		long long s_inner, long long width, long long& r0, long long& r_outer, long long& r_inner) {
+	if (!r.buf || !r.base || !x || r.mode != d.mode || ld != r.ld || x < r.base || d.k % kBK != 0) return false;
+	const long long off = x - r.base;
+	if (off % ld != 0 || s_outer % ld != 0 || s_inner % ld != 0 || s_outer < 0 || s_inner < 0) return false;
+	r0 = off / ld;
+	r_outer = s_outer / ld;
+	r_inner = s_inner / ld;
+	if (r0 % kBK != 0 || r_outer % kBK != 0 || r_inner % kBK != 0 || width > r.cols) return false;
+	const long long last = r0 + (d.batch_outer - 1) * r_outer + (d.batch_inner - 1) * r_inner + d.k;
+	return last <= r.rows && r.rows <= INT32_MAX;
+}
 
 static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int sms = 148) {
 	pl.S = d.mode == NNB_MATH_FP32X3 ? 2 : 1;
@@ -963,7 +1038,15 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	pl.KB = round_up(d.k, kBK) / kBK;
 	// Wide tiles in TF32 mode when the width was left to the plan, the 256-wide tiles are chosen, the
 	// 256 x 256 work items still fill the SMs and the depth amortises the unoverlapped epilogue
-	pl.wide = (force_bn == 0 && d.gather.mode == kGatherNone && pl.bn == 256 &&
+	pl.mn = 0;
+	pl.ra0 = pl.ra_outer = pl.ra_inner = pl.rb0 = pl.rb_outer = pl.rb_inner = 0;
+	if (d.gather.mode == kGatherNone && !d.packed_b && !d.keep_a) {
+		if (d.ta && mn_usable(d, d.mn_a, d.a, d.lda, d.sa_outer, d.sa_inner, d.m, pl.ra0, pl.ra_outer, pl.ra_inner))
+			pl.mn |= 1;
+		if (!d.tb && mn_usable(d, d.mn_b, d.b, d.ldb, d.sb_outer, d.sb_inner, d.n, pl.rb0, pl.rb_outer, pl.rb_inner))
+			pl.mn |= 2;
+	}
+	pl.wide = (force_bn == 0 && pl.mn == 0 && d.gather.mode == kGatherNone && pl.bn == 256 &&
 		pl.KB >= 64 && pl.entries * (round_up(d.m, 2 * kBM) / (2 * kBM)) * (round_up(d.n, 256) / 256) >= (sms > 0 ? sms : 148))
 		? 1 : 0;
 	pl.Mp = round_up(d.m, pl.wide ? 2 * kBM : kBM);
@@ -974,7 +1057,8 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	pl.a_entries = (d.sa_outer || d.sa_inner) ? pl.entries : 1;
 	const bool gathered = d.gather.mode != kGatherNone;
 	pl.b_entries = (gathered ? (d.gather.s_outer || d.gather.s_inner) : (d.sb_outer || d.sb_inner)) ? pl.entries : 1;
-	pl.rows_a = pl.a_entries * pl.Mp * pl.KB * pl.S;
+	pl.KWA = (pl.KB + 1) / 2;
+	pl.rows_a = pl.a_entries * pl.Mp * pl.KWA * pl.S;
 	pl.rows_b = pl.b_entries * pl.Np * pl.KB * pl.S;
 	if (pl.rows_a > INT32_MAX || pl.rows_b > INT32_MAX)
 		return fail(NNB_ERR_UNSUPPORTED, "gemm: operands too large for one launch (packed rows %lld, %lld)",
@@ -984,9 +1068,11 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	// a B that arrives packed (GemmDesc::packed_b) has its panels and flags outside the workspace; a
 	// gathered B has no panels at all, only its flags
 	const bool pre_b = d.packed_b != nullptr;
-	const size_t bytes_a = (size_t)pl.rows_a * kBK * 4,
-		bytes_b = (pre_b || gathered) ? 0 : (size_t)pl.rows_b * kBK * 4;
-	pl.flag_ints = (size_t)(pl.a_entries * pl.Mp + (pre_b ? 0 : pl.b_entries * pl.Np) + 1);
+	const bool a_ws = !(pl.mn & 1) && !d.keep_a;            // A's panels and flags in the scratch
+	const bool b_flags_ws = !(pl.mn & 2) && !pre_b;        // B's flags (a gathered B has flags, no panels)
+	const size_t bytes_a = a_ws ? (size_t)pl.rows_a * kAPanelWidth * 4 : 0,
+		bytes_b = (pre_b || gathered || (pl.mn & 2)) ? 0 : (size_t)pl.rows_b * kBK * 4;
+	pl.flag_ints = (size_t)((a_ws ? pl.a_entries * pl.Mp : 0) + (b_flags_ws ? pl.b_entries * pl.Np : 0) + 2);
 	pl.off_b = round_up(bytes_a, 1024);
 	pl.off_f = pl.off_b + round_up(bytes_b, 1024);
 	pl.total = pl.off_f + pl.flag_ints * sizeof(int);
@@ -995,68 +1081,107 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 
 // Packs one operand with the fastest kernel its layout allows (16-byte aligned rows and a multiple of
 // 4 along the contiguous axis: float4 paths; anything else: the scalar tile kernel).
+// Panels are `pw` floats wide (16: B operands; 32: A operands, see kAPanelWidth) and KW = padded depth / pw.
 template <int kSplit>
 static void launch_pack(cudaStream_t s, const float* X, long long ldx, long long s_outer, long long s_inner, int inner,
-		int trans, long long R, long long K, long long Rp, long long KB, int panel_rows, long long entries, float* out,
-		int* flags, int* any) {
+		int trans, long long R, long long K, long long Rp, long long KW, int pw, int panel_rows, long long entries,
+		float* out, int* flags, int* any) {
 	const bool base16 = (reinterpret_cast<uintptr_t>(X) & 15) == 0;
 	const bool strides4 = ldx % 4 == 0 && s_outer % 4 == 0 && s_inner % 4 == 0;
-	if (!trans && base16 && strides4 && K % 4 == 0 && Rp * KB * 4 < (1LL << 31)) {
-		const long long work = Rp * KB * 4;
+	const long long width = KW * pw;
+	if (!trans && base16 && strides4 && K % 4 == 0 && Rp * width / 4 < (1LL << 31)) {
+		const long long work = Rp * width / 4;
 		const unsigned blocks = (unsigned)std::max<long long>(1, std::min<long long>((work + 255) / 256, 148 * 16));
 		pack_rows_vec_kernel<kSplit><<<dim3(blocks, (unsigned)entries), 256, 0, s>>>(X, ldx, s_outer, s_inner, inner,
-			(int)R, (int)K, (int)Rp, (int)KB, panel_rows, out, flags, any);
+			(int)R, (int)K, (int)Rp, (int)KW, pw, panel_rows, out, flags, any);
 	} else if (trans && base16 && strides4 && R % 4 == 0) {
-		dim3 g((unsigned)((Rp + 63) / 64), (unsigned)((KB * 16 + 31) / 32), (unsigned)entries);
-		pack_cols_vec_kernel<kSplit><<<g, 256, 0, s>>>(X, ldx, s_outer, s_inner, inner, (int)R, (int)K, (int)Rp, (int)KB,
-			panel_rows, out, flags, any);
+		dim3 g((unsigned)((Rp + 63) / 64), (unsigned)((width + 31) / 32), (unsigned)entries);
+		pack_cols_vec_kernel<kSplit><<<g, 256, 0, s>>>(X, ldx, s_outer, s_inner, inner, (int)R, (int)K, (int)Rp, (int)KW,
+			pw, panel_rows, out, flags, any);
 	} else {
-		dim3 g((unsigned)(Rp / 32), (unsigned)((KB * 16 + 63) / 64), (unsigned)entries);
-		pack_kernel<kSplit><<<g, 256, 0, s>>>(X, ldx, s_outer, s_inner, inner, trans, (int)R, (int)K, (int)Rp, (int)KB,
-			panel_rows, out, flags, any);
+		dim3 g((unsigned)(Rp / 32), (unsigned)((width + 63) / 64), (unsigned)entries);
+		pack_kernel<kSplit><<<g, 256, 0, s>>>(X, ldx, s_outer, s_inner, inner, trans, (int)R, (int)K, (int)Rp, (int)KW,
+			pw, panel_rows, out, flags, any);
 	}
 }
 
-template <int kSplit, int kBN, int kGather = 0, int kWide = 0>
+// Tensor map of a kept row pack read MN-major: (32 depths, 128 panel rows, part, panel column,
+// 128-row block), boxes of 16 rows x `chunks` panel columns (32 rows or columns of C each).
+static nnb_status encode_row_pack_mn(CUtensorMap* map, const GemmRowPack& r, int chunks) {
+	const int S = r.mode == NNB_MATH_FP32X3 ? 2 : 1;
+	const uint64_t kw = (uint64_t)(round_up(r.cols, kAPanelWidth) / kAPanelWidth);
+	const uint64_t panel = (uint64_t)kAPanelRows * kAPanelWidth * 4;
+	const uint64_t dims[5] = {(uint64_t)kAPanelWidth, (uint64_t)kAPanelRows, (uint64_t)S, kw,
+		(uint64_t)(row_pack_rows(r.rows) / kAPanelRows)};
+	const uint64_t strides[4] = {(uint64_t)kAPanelWidth * 4, panel, S * panel, kw * S * panel};
+	const uint32_t box[5] = {(uint32_t)kAPanelWidth, (uint32_t)kBK, 1, (uint32_t)chunks, 1};
+	return encode_tiled_nd(map, r.buf, 5, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+}
+
+template <int kSplit, int kBN, int kGather = 0, int kWide = 0, int kMn = 0>
 static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
 		unsigned char* ws, bool traced) {
 	using Cf = KernelCfg<kSplit, kBN, kGather, kWide>;   // the kernel's own stage layout
 	const bool pre_b = d.packed_b != nullptr;
-	float* pa = reinterpret_cast<float*>(ws);
-	int* flags_a = reinterpret_cast<int*>(ws + pl.off_f);
-	float* pb;
-	int *flags_b, *any, *any_b;
-	if (pre_b) {                                           // panels, then Np flags, then B's any-flag
+	// the scratch's flags: A's (when packed into the scratch), B's (when not pre-packed or MN-major),
+	// then A's and B's any-flags
+	int* wsf = reinterpret_cast<int*>(ws + pl.off_f);
+	long long nf = 0;
+	float* pa = nullptr;
+	float* pb = reinterpret_cast<float*>(ws + pl.off_b);
+	int *flags_a = nullptr, *flags_b = nullptr;
+	const int *any_a = nullptr, *any_b = nullptr;
+	int *any_a_w = nullptr, *any_b_w = nullptr;          // the words the pack kernels set
+	int* kept_flags = nullptr;
+	if (kMn & 1) {
+		any_a = row_pack_flags(d.mn_a.buf, d.mn_a.rows, d.mn_a.cols, pl.S) + row_pack_rows(d.mn_a.rows);
+	} else if (d.keep_a) {                                 // panels, flags and any-flag in the caller's buffer
+		pa = static_cast<float*>(d.keep_a);
+		kept_flags = flags_a = row_pack_flags(d.keep_a, d.m, d.k, pl.S);
+	} else {
+		pa = reinterpret_cast<float*>(ws);
+		flags_a = wsf;
+		nf += pl.a_entries * pl.Mp;
+	}
+	if (kMn & 2) {
+		any_b = row_pack_flags(d.mn_b.buf, d.mn_b.rows, d.mn_b.cols, pl.S) + row_pack_rows(d.mn_b.rows);
+	} else if (pre_b) {                                    // panels, then Np flags, then B's any-flag
 		unsigned char* buf = static_cast<unsigned char*>(const_cast<void*>(d.packed_b));
 		pb = reinterpret_cast<float*>(buf);
 		flags_b = reinterpret_cast<int*>(buf + round_up((long long)pl.rows_b * kBK * 4, 1024));
 		any_b = flags_b + pl.Np;
-		any = flags_a + pl.a_entries * pl.Mp;
 	} else {
-		pb = reinterpret_cast<float*>(ws + pl.off_b);
-		flags_b = flags_a + pl.a_entries * pl.Mp;
-		any = flags_b + pl.b_entries * pl.Np;
-		any_b = any;
+		flags_b = wsf + nf;
+		nf += pl.b_entries * pl.Np;
 	}
+	if (!(kMn & 1)) any_a = any_a_w = kept_flags ? kept_flags + row_pack_rows(d.m) : wsf + nf;
+	if (!(kMn & 2) && !pre_b) any_b = any_b_w = wsf + nf + 1;
 	const int inner = (int)d.batch_inner;
 
-	NNB_CUDA_TRY(cudaMemsetAsync(flags_a, 0, pl.flag_ints * sizeof(int), s));
-	{
+	NNB_CUDA_TRY(cudaMemsetAsync(wsf, 0, pl.flag_ints * sizeof(int), s));
+	if (kept_flags) NNB_CUDA_TRY(cudaMemsetAsync(kept_flags, 0, (row_pack_rows(d.m) + 1) * sizeof(int), s));
+	if (!(kMn & 1)) {
 		TraceScope ts(s, kTracePack, traced);
-		launch_pack<kSplit>(s, d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, d.m, d.k, pl.Mp, pl.KB, kAPanelRows,
-			pl.a_entries, pa, flags_a, any);
+		launch_pack<kSplit>(s, d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, d.m, d.k, pl.Mp, pl.KWA, kAPanelWidth,
+			kAPanelRows, pl.a_entries, pa, flags_a, any_a_w);
 	}
-	if (!pre_b && !kGather) {
+	if (!pre_b && !kGather && !(kMn & 2)) {
 		TraceScope ts(s, kTracePack, traced);
-		launch_pack<kSplit>(s, d.b, d.ldb, d.sb_outer, d.sb_inner, inner, !d.tb, d.n, d.k, pl.Np, pl.KB,
-			Cf::kBPanelRows, pl.b_entries, pb, flags_b, any);
+		launch_pack<kSplit>(s, d.b, d.ldb, d.sb_outer, d.sb_inner, inner, !d.tb, d.n, d.k, pl.Np, pl.KB, kBK,
+			Cf::kBPanelRows, pl.b_entries, pb, flags_b, any_b_w);
 	}
 	NNB_CUDA_TRY(cudaGetLastError());
 
 	CUtensorMap tma, tmb;
-	NNB_TRY(encode_tiled_2d(&tma, pa, kBK, (uint64_t)pl.rows_a, kBK * 4, kBK, kAPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
+	if (kMn & 1)
+		NNB_TRY(encode_row_pack_mn(&tma, d.mn_a, kBM / 32));
+	else      // 16-deep halves of the 32-wide rows, written to shared memory as today's 64-byte rows
+		NNB_TRY(encode_tiled_2d(&tma, pa, kAPanelWidth, (uint64_t)pl.rows_a, kAPanelWidth * 4, kBK, kAPanelRows,
+			CU_TENSOR_MAP_SWIZZLE_64B));
 	if (kGather)
 		tmb = tma;                               // not read: B is gathered by the kernel
+	else if (kMn & 2)
+		NNB_TRY(encode_row_pack_mn(&tmb, d.mn_b, kBN / 32));
 	else
 		NNB_TRY(encode_tiled_2d(&tmb, pb, kBK, (uint64_t)pl.rows_b, kBK * 4, kBK, Cf::kBPanelRows,
 			CU_TENSOR_MAP_SWIZZLE_64B));
@@ -1071,22 +1196,41 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	p.bias = d.epi.bias; p.s_bias_outer = d.epi.s_bias_outer; p.bias_mode = d.epi.bias_mode; p.act = d.epi.act;
 	p.mask = d.epi.mask; p.pre = d.epi.pre;
 	p.ld_aux = d.epi.ld_aux; p.s_aux_outer = d.epi.s_aux_outer; p.s_aux_inner = d.epi.s_aux_inner;
-	p.any_nonfinite = any; p.any_b = any_b; p.flags_a = flags_a; p.flags_b = flags_b;
+	p.any_nonfinite = any_a; p.any_b = any_b; p.flags_a = flags_a; p.flags_b = flags_b;
+	p.ra0 = pl.ra0; p.ra_outer = pl.ra_outer; p.ra_inner = pl.ra_inner;
+	p.rb0 = pl.rb0; p.rb_outer = pl.rb_outer; p.rb_inner = pl.rb_inner;
 	p.A = d.a; p.lda = d.lda; p.sa_outer = d.sa_outer; p.sa_inner = d.sa_inner;
 	p.B = d.b; p.ldb = d.ldb; p.sb_outer = d.sb_outer; p.sb_inner = d.sb_inner;
 	p.ta = d.ta; p.tb = d.tb; p.err = err;
 	p.g = d.gather;
 	p.gflags_b = flags_b;
-	p.gany_b = any_b;
+	p.gany_b = any_b_w;
 
-	NNB_TRY((set_smem_attr<kSplit, kBN, kGather, kWide>(dev)));
+	NNB_TRY((set_smem_attr<kSplit, kBN, kGather, kWide, kMn>(dev)));
 	const long long tiles = pl.entries * (p.tiles_m / (kWide ? 2 : 1)) * p.tiles_n;     // work items
 	const int grid = (int)std::min<long long>(tiles, sm_count);
 	{
 		TraceScope ts(s, kGather ? kTraceConv : kTraceGemm, traced);
-		gemm_tc_kernel<kSplit, kBN, kGather, kWide><<<grid, threads_for(kGather), Cf::kSmemBytes, s>>>(tma, tmb, p);
+		gemm_tc_kernel<kSplit, kBN, kGather, kWide, kMn><<<grid, threads_for(kGather), Cf::kSmemBytes, s>>>(tma, tmb, p);
 	}
 	return cuda_status(cudaGetLastError(), "gemm launch");
+}
+
+template <int kSplit, int kMn>
+static nnb_status dispatch_mn_bn(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
+		unsigned char* ws, bool traced) {
+	if (pl.bn == 256) return launch_main<kSplit, 256, 0, 0, kMn>(s, dev, sm_count, err, d, pl, ws, traced);
+	if (pl.bn == 224) return launch_main<kSplit, 224, 0, 0, kMn>(s, dev, sm_count, err, d, pl, ws, traced);
+	if (pl.bn == 128) return launch_main<kSplit, 128, 0, 0, kMn>(s, dev, sm_count, err, d, pl, ws, traced);
+	return launch_main<kSplit, 64, 0, 0, kMn>(s, dev, sm_count, err, d, pl, ws, traced);
+}
+
+template <int kSplit>
+static nnb_status dispatch_mn(cudaStream_t s, int dev, int sm_count, int* err, const GemmDesc& d, const Plan& pl,
+		unsigned char* ws, bool traced) {
+	if (pl.mn == 3) return dispatch_mn_bn<kSplit, 3>(s, dev, sm_count, err, d, pl, ws, traced);
+	if (pl.mn == 2) return dispatch_mn_bn<kSplit, 2>(s, dev, sm_count, err, d, pl, ws, traced);
+	return dispatch_mn_bn<kSplit, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 }
 
 template <int kSplit>
@@ -1098,6 +1242,7 @@ static nnb_status dispatch_bn(cudaStream_t s, int dev, int sm_count, int* err, c
 		return launch_main<kSplit, 64, 1>(s, dev, sm_count, err, d, pl, ws, traced);
 	}
 	if (pl.wide) return launch_main<kSplit, 256, 0, 1>(s, dev, sm_count, err, d, pl, ws, traced);
+	if (pl.mn) return dispatch_mn<kSplit>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 256) return launch_main<kSplit, 256>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 224) return launch_main<kSplit, 224>(s, dev, sm_count, err, d, pl, ws, traced);
 	if (pl.bn == 128) return launch_main<kSplit, 128>(s, dev, sm_count, err, d, pl, ws, traced);
@@ -1128,6 +1273,8 @@ static nnb_status validate(const GemmDesc& d) {
 		return fail(NNB_ERR_INVALID, "gemm: tile width %d", d.bn);
 	if (d.packed_b && (d.bn == 0 || d.batch_outer * d.batch_inner != 1))
 		return fail(NNB_ERR_INVALID, "gemm: a packed B needs its tile width and a single batch entry");
+	if (d.keep_a && (d.ta || d.batch_outer * d.batch_inner != 1 || d.packed_b || d.gather.mode != kGatherNone))
+		return fail(NNB_ERR_INVALID, "gemm: a kept A pack needs an untransposed A and one batch entry");
 	if (d.gather.mode != kGatherNone) {
 		const GemmGather& g = d.gather;
 		if (d.packed_b || d.bn == 224 || !g.src || g.kh < 1 || g.kw < 1 || g.stride < 1 || g.dil < 1 || g.pad < 0 ||
@@ -1283,6 +1430,7 @@ nnb_status gemm_run(cudaStream_t s, const GemmDesc& d) {
 	}
 	const int pieces = d.gather.mode != kGatherNone ? 1 : depth_pieces(d);
 	if (pieces > 1 && d.packed_b) return fail(NNB_ERR_INVALID, "gemm: a packed B with a depth cut");
+	if (pieces > 1 && d.keep_a) return fail(NNB_ERR_INVALID, "gemm: a kept A pack with a depth cut");
 	if (pieces > 1) return gemm_depth_cut(s, dev, d, pieces);
 	return gemm_direct(s, dev, d);
 }
@@ -1292,6 +1440,11 @@ int gemm_tile_width(const GemmDesc& d, int sms) {
 }
 
 int gemm_depth_pieces(const GemmDesc& d) { return gemm::depth_pieces(d); }
+
+size_t gemm_row_pack_bytes(long long rows, long long cols, int mode) {
+	const int S = mode == NNB_MATH_FP32X3 ? 2 : 1;
+	return gemm::row_pack_panel_bytes(rows, cols, S) + (size_t)(gemm::row_pack_rows(rows) + 1) * sizeof(int);
+}
 
 size_t gemm_packed_b_bytes(const GemmDesc& d, int bn) {
 	gemm::Plan pl;
@@ -1314,10 +1467,10 @@ nnb_status gemm_pack_b(cudaStream_t s, const GemmDesc& d, int bn, void* buf) {
 	{
 		TraceScope ts(s, kTracePack);
 		if (d.mode == NNB_MATH_FP32X3)
-			launch_pack<1>(s, d.b, d.ldb, 0, 0, 1, !d.tb, d.n, d.k, pl.Np, pl.KB, b_panel_rows(bn), 1, pb, flags,
+			launch_pack<1>(s, d.b, d.ldb, 0, 0, 1, !d.tb, d.n, d.k, pl.Np, pl.KB, kBK, b_panel_rows(bn), 1, pb, flags,
 				flags + pl.Np);
 		else
-			launch_pack<0>(s, d.b, d.ldb, 0, 0, 1, !d.tb, d.n, d.k, pl.Np, pl.KB, b_panel_rows(bn), 1, pb, flags,
+			launch_pack<0>(s, d.b, d.ldb, 0, 0, 1, !d.tb, d.n, d.k, pl.Np, pl.KB, kBK, b_panel_rows(bn), 1, pb, flags,
 				flags + pl.Np);
 	}
 	return cuda_status(cudaGetLastError(), "gemm_pack_b launch");
@@ -1463,7 +1616,7 @@ extern "C" nnb_status nnb_sgemm_noalloc(void* stream, int trans_a, int trans_b, 
 	if (pl.total > kNoAllocScratchBytes)
 		return fail(NNB_ERR_UNSUPPORTED,
 			"sgemm_noalloc: %lld x %lld x %lld needs %zu bytes of scratch; the static buffer holds %zu "
-			"(packed operands take (roundup(m,128) + roundup(n,256)) * roundup(k,16) * %d * 4 bytes)",
+			"(packed operands take (roundup(m,128) * roundup(k,32) + roundup(n,256) * roundup(k,16)) * %d * 4 bytes)",
 			d.m, d.n, d.k, pl.total, kNoAllocScratchBytes, pl.S);
 	if (d.mode == NNB_MATH_FP32X3)
 		return launch_main<1, 256>(s, dev, nd->sm_count, nd->error, d, pl, nd->scratch, false);

@@ -46,6 +46,18 @@ struct GemmGather {
 	int C = 0, H = 0, W = 0, ho = 0, wo = 0, kh = 1, kw = 1, stride = 1, pad = 0, dil = 1, cout = 0;
 };
 
+// A row pack kept by an earlier product (GemmDesc::keep_a): the panels of a row-major matrix X
+// [rows x cols] (leading dimension ld, first element `base`) packed as that product's A operand, in
+// math mode `mode`. Buffer layout (gemm_row_pack_bytes): the panels of round_up(rows, 256) rows x
+// round_up(cols, 32) depths (128-row panels, 32 floats wide, hi[, lo]), then one non-finite flag per
+// padded row, then the any-non-finite flag.
+struct GemmRowPack {
+	const void* buf = nullptr;
+	const float* base = nullptr;
+	long long ld = 0, rows = 0, cols = 0;
+	int mode = NNB_MATH_FP32X3;
+};
+
 // C_e = op(A_e) op(B_e) for batch entries e = (o, i), o < batch_outer, i < batch_inner, where
 // X_e = x + o * sx_outer + i * sx_inner (floats). A zero stride shares the operand.
 struct GemmDesc {
@@ -68,7 +80,20 @@ struct GemmDesc {
 	int bn = 0;                         // tile width: 0 chooses it from the shape; 64, 128 or 256
 	// B gathered by the GEMM kernel itself (b, ldb, sb_*, tb unused); never cut along its depth
 	GemmGather gather;
+	// A (not transposed, one batch entry) packed into this caller buffer of gemm_row_pack_bytes(m, k,
+	// mode) bytes instead of the scratch, and left there for later products (mn_a / mn_b)
+	void* keep_a = nullptr;
+	// Operands read from a kept row pack instead of being packed: A = X^T (ta = 1, a and lda inside
+	// X) through mn_a, B = X (tb = 0, b and ldb inside X) through mn_b. The tensor core reads them
+	// MN-major straight from the 32-wide panels, so a weight gradient G^T X reuses the packs the
+	// forward product (X) and the input-gradient product (G) already wrote. Used only when every
+	// batch entry starts on a 16-row boundary of X and k % 16 == 0 (otherwise packed as usual); the
+	// result has the same bits either way.
+	GemmRowPack mn_a, mn_b;
 };
+
+// Bytes of a kept row pack of a rows x cols matrix in math mode `mode` (GemmDesc::keep_a).
+size_t gemm_row_pack_bytes(long long rows, long long cols, int mode);
 
 // Validates and enqueues the product (pack kernels + one persistent tensor-core kernel).
 nnb_status gemm_run(cudaStream_t s, const GemmDesc& d);

@@ -46,6 +46,10 @@ nnb_status device_state(DeviceState** out);
 nnb_status encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
 		uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
 		CUtensorMapSwizzle swizzle);
+// The same for a float32 tensor of `rank` (2..5) dimensions: dims[0] innermost, strides[i] the byte
+// stride of dimension i + 1, box[i] the box extent along dimension i.
+nnb_status encode_tiled_nd(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+		const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle);
 
 // Stream-ordered scratch from the device's default memory pool (kept cached by the pool).
 nnb_status scratch_alloc(void** p, size_t bytes, cudaStream_t s);

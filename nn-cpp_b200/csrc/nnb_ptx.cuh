@@ -128,6 +128,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const void* tmap,
 		: "memory");
 }
 
+// The same for a 5-D tensor map, coordinates innermost first.
+__device__ __forceinline__ void tma_load_5d(uint32_t smem_dst, const void* tmap, uint32_t bar,
+		int32_t c0, int32_t c1, int32_t c2, int32_t c3, int32_t c4) {
+	asm volatile(
+		"cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+		" [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_dst),
+		"l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar)
+		: "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA, commit, loads, fences
 // ---------------------------------------------------------------------------------------------
@@ -209,6 +219,8 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
 
 // Instruction-descriptor bit selecting an MN-major B operand (N contiguous for each k).
 constexpr uint32_t kIdescBMajorMN = 1u << 16;
+// The same for A (M contiguous for each k).
+constexpr uint32_t kIdescAMajorMN = 1u << 15;
 
 // Shared-memory descriptor for an MN-major 32-bit (tf32) operand. The one layout tcgen05 offers for
 // MN-major 32-bit operands is the 128-byte swizzle with 32-byte atoms (layout type 1): each 128-byte

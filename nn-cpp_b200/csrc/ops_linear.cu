@@ -111,6 +111,43 @@ __global__ void colsum_final_kernel(const float* __restrict__ partial, long long
 
 }  // namespace
 
+// The two GEMMs of a linear backward that read the output gradient G [rows x n]: dX = G W packs G as
+// its A operand; when both run (and dX is not cut along its depth) that pack is kept in a scratch
+// buffer and the weight gradient dW = G^T X reads it MN-major instead of packing G^T again -- one
+// pass over G instead of two, with the same bits. `groups` consecutive row blocks of G and X give
+// one weight gradient each (dw_stride apart).
+nnb_status linear_bwd_gemms(cudaStream_t s, long long rows, long long K, long long n, long long groups, const float* g,
+		const float* x, const float* w, float* dx, int dx_first, float* dw, long long dw_stride, int dw_first) {
+	const int mode = math_mode();
+	const long long rg = rows / groups;
+	GemmDesc dxd;                 // dX = G W: [rows, n] x [n, K]
+	dxd.m = rows; dxd.n = K; dxd.k = n;
+	dxd.a = g; dxd.lda = n; dxd.b = w; dxd.ldb = K; dxd.c = dx; dxd.ldc = K;
+	dxd.accumulate = !dx_first; dxd.mode = mode;
+	GemmDesc dwd;                 // dW_z = G_z^T X_z: [n, rg] x [rg, K] per group z, one batched launch
+	dwd.ta = 1;
+	dwd.m = n; dwd.n = K; dwd.k = rg;
+	dwd.a = g; dwd.lda = n; dwd.b = x; dwd.ldb = K; dwd.c = dw; dwd.ldc = K;
+	dwd.batch_outer = groups;
+	if (groups > 1) {
+		dwd.sa_outer = rg * n; dwd.sb_outer = rg * K;
+		dwd.sc_outer = dw_stride ? dw_stride : n * K;
+	}
+	dwd.accumulate = !dw_first; dwd.mode = mode;
+	void* kept = nullptr;
+	if (dx && dw && rows > 0 && n > 0 && K > 0 && gemm_depth_pieces(dxd) == 1) {
+		NNB_TRY(scratch_alloc(&kept, gemm_row_pack_bytes(rows, n, mode), s));
+		dxd.keep_a = kept;
+		dwd.mn_a.buf = kept; dwd.mn_a.base = g; dwd.mn_a.ld = n; dwd.mn_a.rows = rows; dwd.mn_a.cols = n;
+		dwd.mn_a.mode = mode;
+	}
+	nnb_status st = NNB_OK;
+	if (dx) st = gemm_run(s, dxd);
+	if (st == NNB_OK && dw) st = gemm_run(s, dwd);
+	nnb_status st2 = scratch_free(kept, s);
+	return st != NNB_OK ? st : st2;
+}
+
 nnb_status colsum(cudaStream_t s, const float* g, long long rows, long long cols, float* out, int first) {
 	return colsum_grouped(s, g, rows, cols, 1, out, cols, first);
 }
@@ -220,22 +257,9 @@ nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const floa
 		const float* w, float* dx, int dx_first, float* dw, int dw_first, float* db, int db_first) {
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	if (!g || !x || !w) return nnb::fail(NNB_ERR_INVALID, "linear_bwd: null input");
-	const int mode = nnb::math_mode();
-	if (dx) {   // dX = G W: [M, n] x [n, K]
-		nnb::GemmDesc d;
-		d.m = (long long)M; d.n = (long long)K; d.k = (long long)n;
-		d.a = g; d.lda = (long long)n; d.b = w; d.ldb = (long long)K; d.c = dx; d.ldc = (long long)K;
-		d.accumulate = !dx_first; d.mode = mode;
-		NNB_TRY(nnb::gemm_run(s, d));
-	}
-	if (dw) {   // dW = G^T X: [n, M] x [M, K]
-		nnb::GemmDesc d;
-		d.ta = 1;
-		d.m = (long long)n; d.n = (long long)K; d.k = (long long)M;
-		d.a = g; d.lda = (long long)n; d.b = x; d.ldb = (long long)K; d.c = dw; d.ldc = (long long)K;
-		d.accumulate = !dw_first; d.mode = mode;
-		NNB_TRY(nnb::gemm_run(s, d));
-	}
+	// dX = G W: [M, n] x [n, K]; dW = G^T X: [n, M] x [M, K]
+	NNB_TRY(nnb::linear_bwd_gemms(s, (long long)M, (long long)K, (long long)n, 1, g, x, w, dx, dx_first, dw, 0,
+		dw_first));
 	if (db) NNB_TRY(nnb::colsum(s, g, (long long)M, (long long)n, db, db_first));
 	return NNB_OK;
 }
@@ -246,26 +270,9 @@ nnb_status nnb_linear_bwd_grouped(void* stream, size_t M, size_t K, size_t n, si
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	if (!g || !x || !w) return nnb::fail(NNB_ERR_INVALID, "linear_bwd_grouped: null input");
 	if (groups == 0 || M % groups != 0) return nnb::fail(NNB_ERR_SHAPE, "linear_bwd_grouped: %zu rows in %zu groups", M, groups);
-	const int mode = nnb::math_mode();
-	const long long Mg = (long long)(M / groups);
-	if (dx) {   // dX = G W over all rows
-		nnb::GemmDesc d;
-		d.m = (long long)M; d.n = (long long)K; d.k = (long long)n;
-		d.a = g; d.lda = (long long)n; d.b = w; d.ldb = (long long)K; d.c = dx; d.ldc = (long long)K;
-		d.accumulate = !dx_first; d.mode = mode;
-		NNB_TRY(nnb::gemm_run(s, d));
-	}
-	if (dw) {   // dW_z = G_z^T X_z per group z, one batched launch (depth-cut per group)
-		nnb::GemmDesc d;
-		d.ta = 1;
-		d.m = (long long)n; d.n = (long long)K; d.k = Mg;
-		d.a = g; d.lda = (long long)n; d.b = x; d.ldb = (long long)K; d.c = dw; d.ldc = (long long)K;
-		d.batch_outer = (long long)groups;
-		d.sa_outer = Mg * (long long)n; d.sb_outer = Mg * (long long)K;
-		d.sc_outer = dw_stride ? (long long)dw_stride : (long long)n * K;
-		d.accumulate = !dw_first; d.mode = mode;
-		NNB_TRY(nnb::gemm_run(s, d));
-	}
+	// dX = G W over all rows; dW_z = G_z^T X_z per group z, one batched launch (depth-cut per group)
+	NNB_TRY(nnb::linear_bwd_gemms(s, (long long)M, (long long)K, (long long)n, (long long)groups, g, x, w, dx, dx_first,
+		dw, (long long)dw_stride, dw_first));
 	if (db)
 		NNB_TRY(nnb::colsum_grouped(s, g, (long long)M, (long long)n, (long long)groups, db,
 			db_stride ? (long long)db_stride : (long long)n, db_first));

@@ -86,9 +86,7 @@ nnb_status device_state(DeviceState** out) {
 	return NNB_OK;
 }
 
-nnb_status encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
-		uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
-		CUtensorMapSwizzle swizzle) {
+static nnb_status load_encode() {
 	std::call_once(g_encode_once, [] {
 		void* fn = nullptr;
 		cudaDriverEntryPointQueryResult q;
@@ -97,6 +95,33 @@ nnb_status encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, u
 			g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
 	});
 	if (!g_encode) return fail(NNB_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+	return NNB_OK;
+}
+
+nnb_status encode_tiled_nd(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+		const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+	NNB_TRY(load_encode());
+	if (rank < 2 || rank > 5) return fail(NNB_ERR_INVALID, "tensor map rank %d", rank);
+	cuuint64_t d[5], st[4];
+	cuuint32_t b[5], e[5];
+	for (int i = 0; i < rank; ++i) {
+		d[i] = dims[i];
+		b[i] = box[i];
+		e[i] = 1;
+		if (i + 1 < rank) st[i] = strides[i];
+	}
+	CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, e,
+		CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	if (r != CUDA_SUCCESS)
+		return fail(NNB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): rank %d, dims %llu x %llu", (int)r, rank,
+			(unsigned long long)dims[0], (unsigned long long)dims[1]);
+	return NNB_OK;
+}
+
+nnb_status encode_tiled_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+		uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+		CUtensorMapSwizzle swizzle) {
+	NNB_TRY(load_encode());
 	const cuuint64_t dims[2] = {inner, outer};
 	const cuuint64_t strides[1] = {row_stride_bytes};
 	const cuuint32_t box[2] = {box_inner, box_outer};
