@@ -184,6 +184,28 @@ NNB_API nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, co
 NNB_API nnb_status nnb_linear_bwd_grouped(void* stream, size_t M, size_t K, size_t n, size_t groups, const float* g,
 		const float* x, const float* w, float* dx, int dx_first, float* dw, size_t dw_stride, int dw_first, float* db,
 		size_t db_stride, int db_first);
+/* The linear forward and backward with the input's packed operand kept between them (no reference
+ * counterpart: the reference packs inside each sgemm call, src/kernels/gemm.cpp:372-378, and keeps
+ * nothing). Both linear GEMMs of the backward read the input X and the output gradient G, the
+ * forward GEMM reads X: packing X once in the forward and G once in the backward, and letting the
+ * weight gradient G^T X read both packs as they are, saves two of the four operand passes of a
+ * linear layer's training step. Results are bitwise those of nnb_linear_fwd / nnb_linear_multi_fwd /
+ * nnb_linear_gelu_fwd and nnb_linear_bwd_grouped.
+ * nnb_linear_pack_bytes: bytes of the kept pack of an M x K input in the given math mode.
+ * nnb_linear_fwd_ex: count (>= 1) products y_i = x w_i^T + b_i as nnb_linear_multi_fwd (strides
+ *   as there; ignored when count == 1); with pre non-null (count 1 only) the GELU form of
+ *   nnb_linear_gelu_fwd. x_pack (nullable) receives x's pack in the current math mode.
+ * nnb_linear_bwd_ex: nnb_linear_bwd_grouped (groups 1: nnb_linear_bwd) whose weight gradient
+ *   reads x_pack (nullable) when it holds x's pack written in math mode x_pack_mode by
+ *   nnb_linear_fwd_ex with this same x; a pack of another mode, or a group shape the tensor core
+ *   cannot read from a pack (groups not whole 16-row blocks), is ignored and X is packed as usual. */
+NNB_API size_t nnb_linear_pack_bytes(size_t M, size_t K, int math_mode);
+NNB_API nnb_status nnb_linear_fwd_ex(void* stream, size_t count, size_t M, size_t K, size_t n, const float* x,
+		const float* w, size_t w_stride, const float* bias, size_t bias_stride, float* y, size_t y_stride, float* pre,
+		void* x_pack);
+NNB_API nnb_status nnb_linear_bwd_ex(void* stream, size_t M, size_t K, size_t n, size_t groups, const float* g,
+		const float* x, const void* x_pack, int x_pack_mode, const float* w, float* dx, int dx_first, float* dw,
+		size_t dw_stride, int dw_first, float* db, size_t db_stride, int db_first);
 /* out[j] (+)= sum_r g[r][j] in the order above (Tensor::sum(0), src/tensor.cpp:422-455). */
 NNB_API nnb_status nnb_column_sum(void* stream, size_t rows, size_t cols, const float* g, float* out, int first);
 

@@ -1273,8 +1273,8 @@ static nnb_status validate(const GemmDesc& d) {
 		return fail(NNB_ERR_INVALID, "gemm: tile width %d", d.bn);
 	if (d.packed_b && (d.bn == 0 || d.batch_outer * d.batch_inner != 1))
 		return fail(NNB_ERR_INVALID, "gemm: a packed B needs its tile width and a single batch entry");
-	if (d.keep_a && (d.ta || d.batch_outer * d.batch_inner != 1 || d.packed_b || d.gather.mode != kGatherNone))
-		return fail(NNB_ERR_INVALID, "gemm: a kept A pack needs an untransposed A and one batch entry");
+	if (d.keep_a && (d.ta || d.sa_outer || d.sa_inner || d.packed_b || d.gather.mode != kGatherNone))
+		return fail(NNB_ERR_INVALID, "gemm: a kept A pack needs an untransposed A shared by every batch entry");
 	if (d.gather.mode != kGatherNone) {
 		const GemmGather& g = d.gather;
 		if (d.packed_b || d.bn == 224 || !g.src || g.kh < 1 || g.kw < 1 || g.stride < 1 || g.dil < 1 || g.pad < 0 ||

@@ -80,8 +80,9 @@ struct GemmDesc {
 	int bn = 0;                         // tile width: 0 chooses it from the shape; 64, 128 or 256
 	// B gathered by the GEMM kernel itself (b, ldb, sb_*, tb unused); never cut along its depth
 	GemmGather gather;
-	// A (not transposed, one batch entry) packed into this caller buffer of gemm_row_pack_bytes(m, k,
-	// mode) bytes instead of the scratch, and left there for later products (mn_a / mn_b)
+	// A (not transposed, shared by every batch entry) packed into this caller buffer of
+	// gemm_row_pack_bytes(m, k, mode) bytes instead of the scratch, and left there for later products
+	// (mn_a / mn_b)
 	void* keep_a = nullptr;
 	// Operands read from a kept row pack instead of being packed: A = X^T (ta = 1, a and lda inside
 	// X) through mn_a, B = X (tb = 0, b and ldb inside X) through mn_b. The tensor core reads them

@@ -11,7 +11,8 @@ namespace nnb {
 nnb_status colsum(cudaStream_t s, const float* g, long long rows, long long cols, float* out, int first);
 // dX (+)= G W and dW_z (+)= G_z^T X_z (per group of rows) of a linear backward; either may be null.
 nnb_status linear_bwd_gemms(cudaStream_t s, long long rows, long long K, long long n, long long groups, const float* g,
-		const float* x, const float* w, float* dx, int dx_first, float* dw, long long dw_stride, int dw_first);
+		const float* x, const void* x_pack, int x_pack_mode, const float* w, float* dx, int dx_first, float* dw,
+		long long dw_stride, int dw_first);
 // The same per group of rows/groups consecutive rows: out[z*out_stride + j] (+)= sum over group z's rows.
 nnb_status colsum_grouped(cudaStream_t s, const float* g, long long rows, long long cols, long long groups, float* out,
 		long long out_stride, int first);

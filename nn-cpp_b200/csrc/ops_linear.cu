@@ -114,10 +114,13 @@ __global__ void colsum_final_kernel(const float* __restrict__ partial, long long
 // The two GEMMs of a linear backward that read the output gradient G [rows x n]: dX = G W packs G as
 // its A operand; when both run (and dX is not cut along its depth) that pack is kept in a scratch
 // buffer and the weight gradient dW = G^T X reads it MN-major instead of packing G^T again -- one
-// pass over G instead of two, with the same bits. `groups` consecutive row blocks of G and X give
-// one weight gradient each (dw_stride apart).
+// pass over G instead of two, with the same bits. Likewise X: when the forward kept its pack
+// (x_pack, written in math mode x_pack_mode by nnb_linear_fwd_ex), dW reads X from it instead of
+// packing X^T. `groups` consecutive row blocks of G and X give one weight gradient each (dw_stride
+// apart).
 nnb_status linear_bwd_gemms(cudaStream_t s, long long rows, long long K, long long n, long long groups, const float* g,
-		const float* x, const float* w, float* dx, int dx_first, float* dw, long long dw_stride, int dw_first) {
+		const float* x, const void* x_pack, int x_pack_mode, const float* w, float* dx, int dx_first, float* dw,
+		long long dw_stride, int dw_first) {
 	const int mode = math_mode();
 	const long long rg = rows / groups;
 	GemmDesc dxd;                 // dX = G W: [rows, n] x [n, K]
@@ -140,6 +143,10 @@ nnb_status linear_bwd_gemms(cudaStream_t s, long long rows, long long K, long lo
 		dxd.keep_a = kept;
 		dwd.mn_a.buf = kept; dwd.mn_a.base = g; dwd.mn_a.ld = n; dwd.mn_a.rows = rows; dwd.mn_a.cols = n;
 		dwd.mn_a.mode = mode;
+	}
+	if (x_pack) {
+		dwd.mn_b.buf = x_pack; dwd.mn_b.base = x; dwd.mn_b.ld = K; dwd.mn_b.rows = rows; dwd.mn_b.cols = K;
+		dwd.mn_b.mode = x_pack_mode;
 	}
 	nnb_status st = NNB_OK;
 	if (dx) st = gemm_run(s, dxd);
@@ -258,8 +265,8 @@ nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const floa
 	cudaStream_t s = static_cast<cudaStream_t>(stream);
 	if (!g || !x || !w) return nnb::fail(NNB_ERR_INVALID, "linear_bwd: null input");
 	// dX = G W: [M, n] x [n, K]; dW = G^T X: [n, M] x [M, K]
-	NNB_TRY(nnb::linear_bwd_gemms(s, (long long)M, (long long)K, (long long)n, 1, g, x, w, dx, dx_first, dw, 0,
-		dw_first));
+	NNB_TRY(nnb::linear_bwd_gemms(s, (long long)M, (long long)K, (long long)n, 1, g, x, nullptr, 0, w, dx, dx_first, dw,
+		0, dw_first));
 	if (db) NNB_TRY(nnb::colsum(s, g, (long long)M, (long long)n, db, db_first));
 	return NNB_OK;
 }
@@ -271,11 +278,69 @@ nnb_status nnb_linear_bwd_grouped(void* stream, size_t M, size_t K, size_t n, si
 	if (!g || !x || !w) return nnb::fail(NNB_ERR_INVALID, "linear_bwd_grouped: null input");
 	if (groups == 0 || M % groups != 0) return nnb::fail(NNB_ERR_SHAPE, "linear_bwd_grouped: %zu rows in %zu groups", M, groups);
 	// dX = G W over all rows; dW_z = G_z^T X_z per group z, one batched launch (depth-cut per group)
-	NNB_TRY(nnb::linear_bwd_gemms(s, (long long)M, (long long)K, (long long)n, (long long)groups, g, x, w, dx, dx_first,
-		dw, (long long)dw_stride, dw_first));
+	NNB_TRY(nnb::linear_bwd_gemms(s, (long long)M, (long long)K, (long long)n, (long long)groups, g, x, nullptr, 0, w,
+		dx, dx_first, dw, (long long)dw_stride, dw_first));
 	if (db)
 		NNB_TRY(nnb::colsum_grouped(s, g, (long long)M, (long long)n, (long long)groups, db,
 			db_stride ? (long long)db_stride : (long long)n, db_first));
+	return NNB_OK;
+}
+
+size_t nnb_linear_pack_bytes(size_t M, size_t K, int math_mode) {
+	if (math_mode != NNB_MATH_FP32X3 && math_mode != NNB_MATH_TF32) return 0;
+	return nnb::gemm_row_pack_bytes((long long)M, (long long)K, math_mode);
+}
+
+nnb_status nnb_linear_fwd_ex(void* stream, size_t count, size_t M, size_t K, size_t n, const float* x, const float* w,
+		size_t w_stride, const float* bias, size_t bias_stride, float* y, size_t y_stride, float* pre, void* x_pack) {
+	if (count == 0 || M == 0 || n == 0) return NNB_OK;
+	if (!x || !w || !bias || !y) return nnb::fail(NNB_ERR_INVALID, "linear_fwd_ex: null pointer");
+	if (K == 0) return nnb::fail(NNB_ERR_SHAPE, "linear_fwd_ex: zero input features");
+	if (pre && count != 1) return nnb::fail(NNB_ERR_INVALID, "linear_fwd_ex: the GELU form takes one weight");
+	if (count > 1 && (w_stride < n * K || bias_stride < n || y_stride < M * n))
+		return nnb::fail(NNB_ERR_INVALID, "linear_fwd_ex: strides overlap consecutive weights, biases or outputs");
+	if (count > 65535) return nnb::fail(NNB_ERR_UNSUPPORTED, "linear_fwd_ex: more than 65535 weights");
+	// the products of nnb_linear_fwd / nnb_linear_multi_fwd / nnb_linear_gelu_fwd (same bits); x's pack
+	// (the A operand every entry shares) is written into x_pack and left there for the backward
+	nnb::GemmDesc d;
+	d.ta = 0; d.tb = 1;
+	d.m = (long long)M; d.n = (long long)n; d.k = (long long)K;
+	d.a = x; d.lda = (long long)K; d.b = w; d.ldb = (long long)K; d.c = pre ? pre : y; d.ldc = (long long)n;
+	if (count > 1) {
+		d.batch_outer = (long long)count;
+		d.sb_outer = (long long)w_stride; d.sc_outer = (long long)y_stride;
+		d.epi.s_bias_outer = (long long)bias_stride;
+	}
+	d.mode = nnb::math_mode();
+	d.epi.bias = bias; d.epi.bias_mode = nnb::kBiasCol;
+	d.keep_a = x_pack;
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	NNB_TRY(nnb::gemm_run(s, d));
+	if (!pre) return NNB_OK;
+	const long long total = (long long)M * (long long)n;
+	nnb::TraceScope ts(s, nnb::kTraceRowwise);
+	if (total % 4 == 0 && ((reinterpret_cast<uintptr_t>(pre) | reinterpret_cast<uintptr_t>(y)) & 15) == 0)
+		nnb::gelu_apply_vec_kernel<<<nnb::grid_for(total / 4, 256), 256, 0, s>>>(total / 4, pre, y);
+	else
+		nnb::gelu_apply_kernel<<<nnb::grid_for(total, 256), 256, 0, s>>>(total, pre, y);
+	return nnb::cuda_status(cudaGetLastError(), "linear_fwd_ex gelu launch");
+}
+
+nnb_status nnb_linear_bwd_ex(void* stream, size_t M, size_t K, size_t n, size_t groups, const float* g, const float* x,
+		const void* x_pack, int x_pack_mode, const float* w, float* dx, int dx_first, float* dw, size_t dw_stride,
+		int dw_first, float* db, size_t db_stride, int db_first) {
+	cudaStream_t s = static_cast<cudaStream_t>(stream);
+	if (!g || !x || !w) return nnb::fail(NNB_ERR_INVALID, "linear_bwd_ex: null input");
+	if (groups == 0 || M % groups != 0) return nnb::fail(NNB_ERR_SHAPE, "linear_bwd_ex: %zu rows in %zu groups", M, groups);
+	NNB_TRY(nnb::linear_bwd_gemms(s, (long long)M, (long long)K, (long long)n, (long long)groups, g, x, x_pack,
+		x_pack_mode, w, dx, dx_first, dw, groups > 1 ? (long long)dw_stride : 0, dw_first));
+	if (db) {
+		if (groups > 1)
+			NNB_TRY(nnb::colsum_grouped(s, g, (long long)M, (long long)n, (long long)groups, db,
+				db_stride ? (long long)db_stride : (long long)n, db_first));
+		else
+			NNB_TRY(nnb::colsum(s, g, (long long)M, (long long)n, db, db_first));
+	}
 	return NNB_OK;
 }
 

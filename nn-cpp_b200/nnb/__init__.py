@@ -98,6 +98,9 @@ _SIGS = {
     "nnb_fill": ([_p, _sz, _f, _p], _i),
     "nnb_scale": ([_p, _sz, _f, _p, _p], _i),
     "nnb_linear_multi_fwd": ([_p, _sz, _sz, _sz, _sz, _p, _p, _sz, _p, _sz, _p, _sz], _i),
+    "nnb_linear_pack_bytes": ([_sz, _sz, _i], _sz),
+    "nnb_linear_fwd_ex": ([_p, _sz, _sz, _sz, _sz, _p, _p, _sz, _p, _sz, _p, _sz, _p, _p], _i),
+    "nnb_linear_bwd_ex": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _i, _p, _p, _i, _p, _sz, _i, _p, _sz, _i], _i),
     "nnb_linear_bwd_grouped": ([_p, _sz, _sz, _sz, _sz, _p, _p, _p, _p, _i, _p, _sz, _i, _p, _sz, _i], _i),
     "nnb_layernorm_bwd_grouped": ([_p, _sz, _sz, _sz, _p, _p, _p, _p, _p, _p, _i, _p, _sz, _i, _p, _sz, _i], _i),
     "nnb_embedding_bwd_grouped": ([_p, _sz, _sz, _sz, _p, _sz, _p, _p, _sz, _i], _i),

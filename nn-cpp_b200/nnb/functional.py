@@ -62,12 +62,25 @@ def linear(x: Value, weight: Value, bias: Value) -> Value:
     n, K = ws
     M = x.data.numel() // K
     y = empty(xs[:-1] + (n,))
-    check(lib().nnb_linear_fwd(_s(), M, K, n, _p(x.data), _p(weight.data), _p(bias.data), _p(y)))
+    pack, mode = _input_pack(weight, M, K)
+    check(lib().nnb_linear_fwd_ex(_s(), 1, M, K, n, _p(x.data), _p(weight.data), 0, _p(bias.data), 0, _p(y), 0, None,
+                                  _p(pack)))
 
     def backward(g):
-        _linear_backward(g, x, weight, bias, M, K, n)
+        _linear_backward(g, x, weight, bias, M, K, n, pack, mode)
 
     return Value.node(y, (x, weight, bias), backward)
+
+
+def _input_pack(weight: Value, M: int, K: int):
+    """A buffer that keeps the forward GEMM's packed copy of the input x [M, K] for the weight
+    gradient G^T x (nnb_linear_fwd_ex / nnb_linear_bwd_ex: x is then packed once per step instead of
+    twice, with the same bits), when that gradient will be taken and the tensor core can read the
+    pack for it (every parameter-gradient group a whole number of 16-row blocks); else (None, 0)."""
+    if not _need(weight) or M % _GROUPS or (M // _GROUPS) % 16:
+        return None, 0
+    mode = lib().nnb_get_math_mode()
+    return empty((lib().nnb_linear_pack_bytes(M, K, mode),), dtype=torch.uint8), mode
 
 
 def linear_multi(x: Value, layers) -> list[Value]:
@@ -100,26 +113,25 @@ def linear_multi(x: Value, layers) -> list[Value]:
     if len(layers) == 1 or w_stride is None or b_stride is None or w_stride < n * K or b_stride < n:
         return [linear(x, w, b) for w, b in layers]
     y = empty((len(layers),) + xs[:-1] + (n,))
-    check(lib().nnb_linear_multi_fwd(_s(), len(layers), M, K, n, _p(x.data), _p(ws[0].data), w_stride,
-                                     _p(bs[0].data), b_stride, _p(y), M * n))
+    pack, mode = _input_pack(ws[0], M, K)      # x's pack, shared by every product and its backward
+    check(lib().nnb_linear_fwd_ex(_s(), len(layers), M, K, n, _p(x.data), _p(ws[0].data), w_stride,
+                                  _p(bs[0].data), b_stride, _p(y), M * n, None, _p(pack)))
     outs = []
     for i, (w, b) in enumerate(layers):
         def backward(g, w=w, b=b):
-            _linear_backward(g, x, w, b, M, K, n)
+            _linear_backward(g, x, w, b, M, K, n, pack if _need(w) else None, mode)
         outs.append(Value.node(y[i], (x, w, b), backward))
     return outs
 
 
-def _linear_backward(g, x, weight, bias, M, K, n):
+def _linear_backward(g, x, weight, bias, M, K, n, pack=None, mode=0):
+    """nnb_linear_bwd_ex: nnb_linear_bwd (one group) or nnb_linear_bwd_grouped, the weight gradient
+    reading x's pack from the forward when it was kept."""
     dx, fx = x.grad_accum() if _need(x) else (None, 0)
     dw, fw = weight.grad_accum() if _need(weight) else (None, 0)
     db, fb = bias.grad_accum() if _need(bias) else (None, 0)
-    if _GROUPS > 1:
-        check(lib().nnb_linear_bwd_grouped(_s(), M, K, n, _GROUPS, _p(g), _p(x.data), _p(weight.data), _p(dx), fx,
-                                           _p(dw), _gstride(dw, weight), fw, _p(db), _gstride(db, bias), fb))
-    else:
-        check(lib().nnb_linear_bwd(_s(), M, K, n, _p(g), _p(x.data), _p(weight.data), _p(dx), fx, _p(dw), fw,
-                                   _p(db), fb))
+    check(lib().nnb_linear_bwd_ex(_s(), M, K, n, _GROUPS, _p(g), _p(x.data), _p(pack), mode, _p(weight.data), _p(dx),
+                                  fx, _p(dw), _gstride(dw, weight), fw, _p(db), _gstride(db, bias), fb))
 
 
 def linear_gelu(x: Value, weight: Value, bias: Value) -> Value:
@@ -131,12 +143,14 @@ def linear_gelu(x: Value, weight: Value, bias: Value) -> Value:
     M = x.data.numel() // K
     y = empty(xs[:-1] + (n,))
     pre = empty(xs[:-1] + (n,))
-    check(lib().nnb_linear_gelu_fwd(_s(), M, K, n, _p(x.data), _p(weight.data), _p(bias.data), _p(y), _p(pre)))
+    pack, mode = _input_pack(weight, M, K)
+    check(lib().nnb_linear_fwd_ex(_s(), 1, M, K, n, _p(x.data), _p(weight.data), 0, _p(bias.data), 0, _p(y), 0,
+                                  _p(pre), _p(pack)))
 
     def backward(g):
         dpre = empty(pre.shape)
         check(lib().nnb_gelu_bwd(_s(), pre.numel(), _p(pre), None, _p(g), _p(dpre), 1))
-        _linear_backward(dpre, x, weight, bias, M, K, n)
+        _linear_backward(dpre, x, weight, bias, M, K, n, pack, mode)
 
     return Value.node(y, (x, weight, bias), backward)
 
