@@ -103,6 +103,10 @@ struct Params {
 	// operands read MN-major from kept row packs (kernel variant kMn): batch entry bi's depth q is
 	// row r0 + (bi / batch_inner) * r_outer + (bi % batch_inner) * r_inner + q of the packed matrix
 	long long ra0, ra_outer, ra_inner, rb0, rb_outer, rb_inner;
+	// A's packed columns: a_kw 32-wide columns per 128-row panel; batch entry bi's k-block kb is packed
+	// k-block kb + a_kb0 + (bi / batch_inner) * a_kb_outer + (bi % batch_inner) * a_kb_inner (offsets
+	// nonzero only for an A read from a kept row pack at a column offset, GemmDesc::pre_a)
+	int a_kw, a_kb0, a_kb_outer, a_kb_inner;
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -555,7 +559,7 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 
 	const int num_tiles = p.batch * (p.tiles_m / kAM) * p.tiles_n;      // work items
 	const int a_panels = p.Mp / kAPanelRows, b_panels = p.Np / C::kBPanelRows;
-	const int kwa = (p.KB + 1) >> 1;          // packed 32-wide columns of A
+	const int kwa = p.a_kw;                   // packed 32-wide columns of A
 
 	if (warp == 0) {
 		if (lane == 0) {
@@ -591,11 +595,13 @@ __global__ void __launch_bounds__(threads_for(kGather), 1) gemm_tc_kernel(const 
 						} else {
 #pragma unroll
 							for (int h = 0; h < kAM; ++h) {
-								// 32-wide A rows: k-block kb is the (kb & 1) half of packed column kb / 2
-								const int ya = (int)((((long long)ab * a_panels + mt + h) * kwa + (kb >> 1)) * S * kAPanelRows);
+								// 32-wide A rows: packed k-block akb is the (akb & 1) half of packed column akb / 2
+								const int akb = kb + p.a_kb0 + (bi / p.batch_inner) * p.a_kb_outer +
+									(bi % p.batch_inner) * p.a_kb_inner;
+								const int ya = (int)((((long long)ab * a_panels + mt + h) * kwa + (akb >> 1)) * S * kAPanelRows);
 #pragma unroll
 								for (int s = 0; s < S; ++s)
-									tma_load_2d(base + (h * S + s) * (kAPanelRows * kBK * 4), &tm_a, fb, (kb & 1) * kBK,
+									tma_load_2d(base + (h * S + s) * (kAPanelRows * kBK * 4), &tm_a, fb, (akb & 1) * kBK,
 										ya + s * kAPanelRows);
 							}
 						}
@@ -996,6 +1002,8 @@ struct Plan {
 	int S, bn, b_panel_rows;
 	int wide;                                 // 256 x 256 TF32 tiles (rows padded to 256)
 	int mn;                                   // bit 0: A, bit 1: B read MN-major from kept row packs
+	int pre_a;                                // A read K-major from a kept row pack (GemmDesc::pre_a)
+	long long a_kb0, a_kb_outer, a_kb_inner;  // its packed k-block offsets (Params::a_kb0 ...)
 	long long Mp, Np, Kp, KB, KWA, entries, a_entries, b_entries;
 	long long rows_a, rows_b;                 // packed rows of each operand (A: 32 floats, B: 16 floats)
 	long long ra0, ra_outer, ra_inner, rb0, rb_outer, rb_inner;
@@ -1029,6 +1037,28 @@ static bool mn_usable(const GemmDesc& d, const GemmRowPack& r, const float* x, l
 	return last <= r.rows && r.rows <= INT32_MAX;
 }
 
+// Whether A (ta = 0) can be read K-major from the kept row pack r of the matrix it lies in: every
+// batch entry A_e = a + o*sa_outer + i*sa_inner starts in row 0 of the packed matrix at a column
+// offset that is whole 16-column blocks, and its k columns lie inside (k whole 16-column blocks, or a
+// single entry ending at the last column, where the pack's zero padding completes the block).
+static bool pre_a_usable(const GemmDesc& d, const GemmRowPack& r, long long& kb0, long long& kb_outer,
+		long long& kb_inner) {
+	if (!r.buf || !r.base || !d.a || d.ta || r.mode != d.mode || d.lda != r.ld || d.a < r.base) return false;
+	const long long c0 = d.a - r.base;
+	if (c0 >= r.ld || c0 % kBK != 0 || d.sa_outer % kBK != 0 || d.sa_inner % kBK != 0 || d.sa_outer < 0 ||
+			d.sa_inner < 0 || d.m > r.rows ||
+			row_pack_rows(r.rows) * (round_up(r.cols, kAPanelWidth) / kAPanelWidth) * (r.mode == NNB_MATH_FP32X3 ? 2 : 1) >
+				INT32_MAX)
+		return false;
+	const long long end = c0 + (d.batch_outer - 1) * d.sa_outer + (d.batch_inner - 1) * d.sa_inner + d.k;
+	const bool single = d.batch_outer * d.batch_inner == 1;
+	if (end > r.cols || (d.k % kBK != 0 && !(single && end == r.cols))) return false;
+	kb0 = c0 / kBK;
+	kb_outer = d.sa_outer / kBK;
+	kb_inner = d.sa_inner / kBK;
+	return true;
+}
+
 static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int sms = 148) {
 	pl.S = d.mode == NNB_MATH_FP32X3 ? 2 : 1;
 	pl.bn = force_bn ? force_bn : choose_bn(d.m, d.n, d.batch_outer * d.batch_inner, sms > 0 ? sms : 148);
@@ -1040,8 +1070,10 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	// 256 x 256 work items still fill the SMs and the depth amortises the unoverlapped epilogue
 	pl.mn = 0;
 	pl.ra0 = pl.ra_outer = pl.ra_inner = pl.rb0 = pl.rb_outer = pl.rb_inner = 0;
+	pl.a_kb0 = pl.a_kb_outer = pl.a_kb_inner = 0;
+	pl.pre_a = !d.keep_a && pre_a_usable(d, d.pre_a, pl.a_kb0, pl.a_kb_outer, pl.a_kb_inner) ? 1 : 0;
 	if (d.gather.mode == kGatherNone && !d.packed_b && !d.keep_a) {
-		if (d.ta && mn_usable(d, d.mn_a, d.a, d.lda, d.sa_outer, d.sa_inner, d.m, pl.ra0, pl.ra_outer, pl.ra_inner))
+		if (!pl.pre_a && d.ta && mn_usable(d, d.mn_a, d.a, d.lda, d.sa_outer, d.sa_inner, d.m, pl.ra0, pl.ra_outer, pl.ra_inner))
 			pl.mn |= 1;
 		if (!d.tb && mn_usable(d, d.mn_b, d.b, d.ldb, d.sb_outer, d.sb_inner, d.n, pl.rb0, pl.rb_outer, pl.rb_inner))
 			pl.mn |= 2;
@@ -1054,7 +1086,7 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	pl.Kp = round_up(d.k, kBK);
 	pl.KB = pl.Kp / kBK;
 	pl.entries = d.batch_outer * d.batch_inner;
-	pl.a_entries = (d.sa_outer || d.sa_inner) ? pl.entries : 1;
+	pl.a_entries = (!pl.pre_a && (d.sa_outer || d.sa_inner)) ? pl.entries : 1;
 	const bool gathered = d.gather.mode != kGatherNone;
 	pl.b_entries = (gathered ? (d.gather.s_outer || d.gather.s_inner) : (d.sb_outer || d.sb_inner)) ? pl.entries : 1;
 	pl.KWA = (pl.KB + 1) / 2;
@@ -1068,7 +1100,7 @@ static nnb_status make_plan(const GemmDesc& d, Plan& pl, int force_bn = 0, int s
 	// a B that arrives packed (GemmDesc::packed_b) has its panels and flags outside the workspace; a
 	// gathered B has no panels at all, only its flags
 	const bool pre_b = d.packed_b != nullptr;
-	const bool a_ws = !(pl.mn & 1) && !d.keep_a;            // A's panels and flags in the scratch
+	const bool a_ws = !(pl.mn & 1) && !d.keep_a && !pl.pre_a;   // A's panels and flags in the scratch
 	const bool b_flags_ws = !(pl.mn & 2) && !pre_b;        // B's flags (a gathered B has flags, no panels)
 	const size_t bytes_a = a_ws ? (size_t)pl.rows_a * kAPanelWidth * 4 : 0,
 		bytes_b = (pre_b || gathered || (pl.mn & 2)) ? 0 : (size_t)pl.rows_b * kBK * 4;
@@ -1133,8 +1165,14 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	const int *any_a = nullptr, *any_b = nullptr;
 	int *any_a_w = nullptr, *any_b_w = nullptr;          // the words the pack kernels set
 	int* kept_flags = nullptr;
+	const int* pre_flags = nullptr;
 	if (kMn & 1) {
 		any_a = row_pack_flags(d.mn_a.buf, d.mn_a.rows, d.mn_a.cols, pl.S) + row_pack_rows(d.mn_a.rows);
+	} else if (pl.pre_a) {                                 // panels, flags and any-flag of the kept pack
+		pa = static_cast<float*>(const_cast<void*>(d.pre_a.buf));
+		pre_flags = row_pack_flags(d.pre_a.buf, d.pre_a.rows, d.pre_a.cols, pl.S);
+		flags_a = const_cast<int*>(pre_flags);
+		any_a = pre_flags + row_pack_rows(d.pre_a.rows);
 	} else if (d.keep_a) {                                 // panels, flags and any-flag in the caller's buffer
 		pa = static_cast<float*>(d.keep_a);
 		kept_flags = flags_a = row_pack_flags(d.keep_a, d.m, d.k, pl.S);
@@ -1154,13 +1192,13 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 		flags_b = wsf + nf;
 		nf += pl.b_entries * pl.Np;
 	}
-	if (!(kMn & 1)) any_a = any_a_w = kept_flags ? kept_flags + row_pack_rows(d.m) : wsf + nf;
+	if (!(kMn & 1) && !pl.pre_a) any_a = any_a_w = kept_flags ? kept_flags + row_pack_rows(d.m) : wsf + nf;
 	if (!(kMn & 2) && !pre_b) any_b = any_b_w = wsf + nf + 1;
 	const int inner = (int)d.batch_inner;
 
 	NNB_CUDA_TRY(cudaMemsetAsync(wsf, 0, pl.flag_ints * sizeof(int), s));
 	if (kept_flags) NNB_CUDA_TRY(cudaMemsetAsync(kept_flags, 0, (row_pack_rows(d.m) + 1) * sizeof(int), s));
-	if (!(kMn & 1)) {
+	if (!(kMn & 1) && !pl.pre_a) {
 		TraceScope ts(s, kTracePack, traced);
 		launch_pack<kSplit>(s, d.a, d.lda, d.sa_outer, d.sa_inner, inner, d.ta, d.m, d.k, pl.Mp, pl.KWA, kAPanelWidth,
 			kAPanelRows, pl.a_entries, pa, flags_a, any_a_w);
@@ -1175,6 +1213,10 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	CUtensorMap tma, tmb;
 	if (kMn & 1)
 		NNB_TRY(encode_row_pack_mn(&tma, d.mn_a, kBM / 32));
+	else if (pl.pre_a)
+		NNB_TRY(encode_tiled_2d(&tma, pa, kAPanelWidth,
+			(uint64_t)(row_pack_rows(d.pre_a.rows) * (round_up(d.pre_a.cols, kAPanelWidth) / kAPanelWidth) * pl.S),
+			kAPanelWidth * 4, kBK, kAPanelRows, CU_TENSOR_MAP_SWIZZLE_64B));
 	else      // 16-deep halves of the 32-wide rows, written to shared memory as today's 64-byte rows
 		NNB_TRY(encode_tiled_2d(&tma, pa, kAPanelWidth, (uint64_t)pl.rows_a, kAPanelWidth * 4, kBK, kAPanelRows,
 			CU_TENSOR_MAP_SWIZZLE_64B));
@@ -1198,6 +1240,8 @@ static nnb_status launch_main(cudaStream_t s, int dev, int sm_count, int* err, c
 	p.ld_aux = d.epi.ld_aux; p.s_aux_outer = d.epi.s_aux_outer; p.s_aux_inner = d.epi.s_aux_inner;
 	p.any_nonfinite = any_a; p.any_b = any_b; p.flags_a = flags_a; p.flags_b = flags_b;
 	p.ra0 = pl.ra0; p.ra_outer = pl.ra_outer; p.ra_inner = pl.ra_inner;
+	p.a_kw = (int)(pl.pre_a ? round_up(d.pre_a.cols, kAPanelWidth) / kAPanelWidth : pl.KWA);
+	p.a_kb0 = (int)pl.a_kb0; p.a_kb_outer = (int)pl.a_kb_outer; p.a_kb_inner = (int)pl.a_kb_inner;
 	p.rb0 = pl.rb0; p.rb_outer = pl.rb_outer; p.rb_inner = pl.rb_inner;
 	p.A = d.a; p.lda = d.lda; p.sa_outer = d.sa_outer; p.sa_inner = d.sa_inner;
 	p.B = d.b; p.ldb = d.ldb; p.sb_outer = d.sb_outer; p.sb_inner = d.sb_inner;
@@ -1363,6 +1407,24 @@ static nnb_status gemm_direct(cudaStream_t s, const DeviceState* dev, const Gemm
 	return st != NNB_OK ? st : st2;
 }
 
+// A (ta = 0, one batch entry) packed on its own into d.keep_a, in the kept row-pack layout.
+static nnb_status pack_rows_kept(cudaStream_t s, const GemmDesc& d) {
+	const int S = d.mode == NNB_MATH_FP32X3 ? 2 : 1;
+	const long long rp = row_pack_rows(d.m), kw = round_up(d.k, kAPanelWidth) / kAPanelWidth;
+	if (rp * kw * S > INT32_MAX) return fail(NNB_ERR_UNSUPPORTED, "gemm: operand too large to keep packed");
+	int* flags = row_pack_flags(d.keep_a, d.m, d.k, S);
+	NNB_CUDA_TRY(cudaMemsetAsync(flags, 0, (size_t)(rp + 1) * sizeof(int), s));
+	float* out = static_cast<float*>(d.keep_a);
+	{
+		TraceScope ts(s, kTracePack);
+		if (S == 2)
+			launch_pack<1>(s, d.a, d.lda, 0, 0, 1, 0, d.m, d.k, rp, kw, kAPanelWidth, kAPanelRows, 1, out, flags, flags + rp);
+		else
+			launch_pack<0>(s, d.a, d.lda, 0, 0, 1, 0, d.m, d.k, rp, kw, kAPanelWidth, kAPanelRows, 1, out, flags, flags + rp);
+	}
+	return cuda_status(cudaGetLastError(), "kept pack launch");
+}
+
 static nnb_status gemm_depth_cut(cudaStream_t s, const DeviceState* dev, const GemmDesc& d, int pieces) {
 	const long long kp = round_up((d.k + pieces - 1) / pieces, kBK);
 	pieces = (int)((d.k + kp - 1) / kp);
@@ -1430,7 +1492,15 @@ nnb_status gemm_run(cudaStream_t s, const GemmDesc& d) {
 	}
 	const int pieces = d.gather.mode != kGatherNone ? 1 : depth_pieces(d);
 	if (pieces > 1 && d.packed_b) return fail(NNB_ERR_INVALID, "gemm: a packed B with a depth cut");
-	if (pieces > 1 && d.keep_a) return fail(NNB_ERR_INVALID, "gemm: a kept A pack with a depth cut");
+	if (pieces > 1 && d.keep_a) {
+		// the whole of A packed once into the kept buffer, every depth piece reading its columns from it
+		NNB_TRY(pack_rows_kept(s, d));
+		GemmDesc e = d;
+		e.keep_a = nullptr;
+		e.pre_a.buf = d.keep_a; e.pre_a.base = d.a; e.pre_a.ld = d.lda; e.pre_a.rows = d.m; e.pre_a.cols = d.k;
+		e.pre_a.mode = d.mode;
+		return gemm_depth_cut(s, dev, e, pieces);
+	}
 	if (pieces > 1) return gemm_depth_cut(s, dev, d, pieces);
 	return gemm_direct(s, dev, d);
 }

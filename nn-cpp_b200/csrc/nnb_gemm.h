@@ -91,6 +91,10 @@ struct GemmDesc {
 	// batch entry starts on a 16-row boundary of X and k % 16 == 0 (otherwise packed as usual); the
 	// result has the same bits either way.
 	GemmRowPack mn_a, mn_b;
+	// A (ta = 0) read K-major from a kept row pack of the matrix it lies in, at a column offset of
+	// whole 16-column blocks (a depth piece of a product whose A was kept: gemm_run packs a kept A
+	// once and hands every piece its columns this way). Ignored when A does not lie so.
+	GemmRowPack pre_a;
 };
 
 // Bytes of a kept row pack of a rows x cols matrix in math mode `mode` (GemmDesc::keep_a).

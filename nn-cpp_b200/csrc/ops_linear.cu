@@ -112,7 +112,7 @@ __global__ void colsum_final_kernel(const float* __restrict__ partial, long long
 }  // namespace
 
 // The two GEMMs of a linear backward that read the output gradient G [rows x n]: dX = G W packs G as
-// its A operand; when both run (and dX is not cut along its depth) that pack is kept in a scratch
+// its A operand (once, even when dX is cut along its depth); when both run that pack is kept in a scratch
 // buffer and the weight gradient dW = G^T X reads it MN-major instead of packing G^T again -- one
 // pass over G instead of two, with the same bits. Likewise X: when the forward kept its pack
 // (x_pack, written in math mode x_pack_mode by nnb_linear_fwd_ex), dW reads X from it instead of
@@ -138,7 +138,7 @@ nnb_status linear_bwd_gemms(cudaStream_t s, long long rows, long long K, long lo
 	}
 	dwd.accumulate = !dw_first; dwd.mode = mode;
 	void* kept = nullptr;
-	if (dx && dw && rows > 0 && n > 0 && K > 0 && gemm_depth_pieces(dxd) == 1) {
+	if (dx && dw && rows > 0 && n > 0 && K > 0) {
 		NNB_TRY(scratch_alloc(&kept, gemm_row_pack_bytes(rows, n, mode), s));
 		dxd.keep_a = kept;
 		dwd.mn_a.buf = kept; dwd.mn_a.base = g; dwd.mn_a.ld = n; dwd.mn_a.rows = rows; dwd.mn_a.cols = n;

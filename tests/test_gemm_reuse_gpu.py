@@ -78,14 +78,18 @@ def _fp64_bound(g, x, groups, dw, mode):
 
 # (M, K = input features, n = output features, groups): ragged widths (n not a multiple of 32, so the
 # shared pack's last 32-wide column is half padding), several groups, a group depth long enough for
-# the depth cut (2048 rows >= 2 * max(1024, K)), and groups of 24 rows (not whole 16-row blocks: the
-# weight gradient packs G^T itself)
+# the depth cut (2048 rows >= 2 * max(1024, K)), groups of 24 rows (not whole 16-row blocks: the
+# weight gradient packs G^T itself), and input gradients cut along their depth (n >= 2 * max(1024,
+# K): G is packed once and every depth piece reads its columns from the pack; 4100 = three 1040-wide
+# pieces and a 980-wide last one, which ends inside a 16-column block)
 SHAPES = [
     (256, 96, 80, 1),
     (512, 200, 130, 4),
     (4096, 64, 48, 2),
     (96, 40, 24, 4),
     (1024, 512, 512, 8),
+    (512, 64, 2048, 2),
+    (256, 128, 4100, 1),
 ]
 
 
@@ -206,6 +210,7 @@ def _assert_same(kept, plain):
 # then not readable by the weight gradient and X^T is packed as usual)
 KEPT = [
     (256, 96, 80, 1, 1, False),
+    (512, 64, 2048, 2, 1, False),
     (512, 200, 130, 4, 1, False),
     (4096, 64, 48, 2, 1, False),
     (1024, 256, 128, 8, 3, False),
