@@ -63,3 +63,26 @@ def test_flash_attention_host_checks():
 def test_sgemm_host_release_without_calls():
     """Releasing the host-buffer GEMM's device buffers before any call is a no-op (no CUDA work)."""
     nnb.sgemm_host_release()
+
+
+def test_linear_pack_bytes():
+    """The kept input pack's size (host arithmetic only): panels of round_up(M, 256) rows x
+    round_up(K, 32) depths, hi and lo in 3xTF32 (hi only in TF32), rounded to 1 KB, then one flag per
+    padded row and the any-flag; 0 for an unknown math mode."""
+    lib = nnb.lib()
+    panels = 512 * 96 * 2 * 4                       # M = 300 -> 512 rows, K = 70 -> 96 depths
+    assert lib.nnb_linear_pack_bytes(300, 70, nnb.MATH_FP32X3) == panels + (512 + 1) * 4
+    assert lib.nnb_linear_pack_bytes(300, 70, nnb.MATH_TF32) == panels // 2 + (512 + 1) * 4
+    assert lib.nnb_linear_pack_bytes(32768, 512, nnb.MATH_FP32X3) == 32768 * 512 * 8 + (32768 + 1) * 4
+    assert lib.nnb_linear_pack_bytes(16, 16, 7) == 0
+
+
+def test_linear_ex_host_checks():
+    """nnb_linear_fwd_ex / nnb_linear_bwd_ex reject bad arguments before any device work."""
+    lib = nnb.lib()
+    p = ctypes.c_void_p(16)                          # never dereferenced: the checks come first
+    assert lib.nnb_linear_fwd_ex(None, 1, 4, 0, 4, p, p, 0, p, 0, p, 0, None, None) == 5     # K == 0: shape
+    assert lib.nnb_linear_fwd_ex(None, 2, 4, 4, 4, p, p, 0, p, 0, p, 0, p, None) == 1       # GELU form, 2 weights
+    assert lib.nnb_linear_fwd_ex(None, 2, 4, 4, 4, p, p, 15, p, 4, p, 16, None, None) == 1  # weights overlap
+    assert lib.nnb_linear_fwd_ex(None, 1, 4, 4, 4, None, p, 0, p, 0, p, 0, None, None) == 1  # null input
+    assert lib.nnb_linear_bwd_ex(None, 6, 4, 4, 4, p, p, None, 0, p, *([None, 0] * 2), 0, None, 0, 0) == 5
