@@ -138,7 +138,8 @@ nnb_status linear_bwd_gemms(cudaStream_t s, long long rows, long long K, long lo
 	}
 	dwd.accumulate = !dw_first; dwd.mode = mode;
 	void* kept = nullptr;
-	if (dx && dw && rows > 0 && n > 0 && K > 0) {
+	// the weight gradient can read the pack only when every group is whole 16-row blocks
+	if (dx && dw && rows > 0 && n > 0 && K > 0 && rg % 16 == 0) {
 		NNB_TRY(scratch_alloc(&kept, gemm_row_pack_bytes(rows, n, mode), s));
 		dxd.keep_a = kept;
 		dwd.mn_a.buf = kept; dwd.mn_a.base = g; dwd.mn_a.ld = n; dwd.mn_a.rows = rows; dwd.mn_a.cols = n;
