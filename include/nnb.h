@@ -172,7 +172,9 @@ NNB_API nnb_status nnb_linear_multi_fwd(void* stream, size_t count, size_t M, si
 NNB_API nnb_status nnb_linear_gelu_fwd(void* stream, size_t M, size_t K, size_t n, const float* x, const float* w,
 		const float* bias, float* y, float* pre);
 /* dx (+)= g·w, dw (+)= g^T·x, db (+)= column sums of g (fixed chunked order: serial within 256-row
- * chunks, then over chunks; the reference's serial order whenever M <= 256). */
+ * chunks, then over chunks; the reference's serial order whenever M <= 256). When both dx and dw are
+ * asked for, g is packed once: the dx product's packed copy (M x n x 8 bytes in 3xTF32, scratch from
+ * the memory pool, freed in stream order) is read again by the dw product. */
 NNB_API nnb_status nnb_linear_bwd(void* stream, size_t M, size_t K, size_t n, const float* g, const float* x,
 		const float* w, float* dx, int dx_first, float* dw, int dw_first, float* db, int db_first);
 /* nnb_linear_bwd whose weight and bias gradients are kept per group: the M rows are `groups`
