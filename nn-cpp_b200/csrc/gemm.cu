@@ -2,8 +2,12 @@
 // rebuilt for B200 (sm_100a): a pack kernel plus a persistent tcgen05 tensor-core kernel.
 //
 // Pack (the counterpart of pack_a / pack_b, src/kernels/gemm.cpp:79,126): op(A) and op(B)^T are
-// rewritten, whatever their transpose flag and leading dimension, into K-major "panels" of
-// 128 (or 64) rows x 16 floats, contiguous, zero-padded to whole panels. In 3xTF32 mode each value
+// rewritten, whatever their transpose flag and leading dimension, into K-major "panels",
+// contiguous and zero-padded to whole panels: 128 rows x 32 floats for A (each stage loads the
+// 16-float half that holds its k-block), 128 (or the tile width) rows x 16 floats for B. A pack of
+// A can be kept in a caller's buffer and read again by a later product: K-major at a column offset
+// (the depth pieces of a cut product), or MN-major, as the transposed operand of a weight gradient
+// (32 consecutive packed depths of a row are one 128-byte row of a tcgen05 MN-major tile). In 3xTF32 mode each value
 // x is stored twice, as hi = tf32(x) and lo = tf32(x - hi) (the split-precision method of
 // Ootomo & Yokota, 2022), so C = Ahi*Bhi + Ahi*Blo + Alo*Bhi carries about 21 mantissa bits.
 // Rows holding Inf or NaN are flagged; the epilogue recomputes the IEEE result of those
