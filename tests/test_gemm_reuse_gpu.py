@@ -1,12 +1,16 @@
-"""The linear backward's shared output-gradient pack: dX = G W packs G once (32-wide row panels) and
-the weight gradient dW = G^T X reads that pack MN-major instead of packing G^T again.
+"""Kept operand packs of the linear layer. The backward's shared output-gradient pack: dX = G W packs
+G once (32-wide row panels; once for all depth pieces when dX is cut along its depth) and the weight
+gradient dW = G^T X reads that pack MN-major instead of packing G^T again. The kept input pack:
+nnb_linear_fwd_ex keeps x's pack from the forward and nnb_linear_bwd_ex's weight gradient reads it
+instead of packing X^T.
 
-The shared pack must not change a bit: for every shape (ragged feature counts, several groups, a
-depth-cut weight gradient, shapes that cannot share because a group is not whole 16-row blocks)
-and both math modes, nnb_linear_bwd / nnb_linear_bwd_grouped must give exactly the bits of the
-same products run as separate nnb_sgemm_ex calls (each packing its own operands), and non-finite
-gradients must still come out as the reference's IEEE results. The weight gradients are also held
-to the fp64 bound of the GEMM tests.
+Neither may change a bit: for every shape (ragged feature counts, several groups, depth-cut weight
+and input gradients, shapes that cannot share because a group is not whole 16-row blocks) and both
+math modes, the shared paths must give exactly the bits of the same products run without sharing
+(separate nnb_sgemm_ex calls; nnb_linear_fwd / nnb_linear_multi_fwd / nnb_linear_gelu_fwd and
+nnb_linear_bwd_grouped), non-finite inputs must still come out as the reference's IEEE results, and
+a pack written in another math mode must be ignored. The weight gradients are also held to the fp64
+bound of the GEMM tests.
 """
 import numpy as np
 import pytest
